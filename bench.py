@@ -1,0 +1,436 @@
+"""Benchmark: 8B-shaped Q4_0 greedy decode on the cuda-b200 backend.
+
+Workload (the headline configuration): a Llama-3-8B-shaped model, 32
+layers, hidden 4096, 32 query / 8 KV heads of 128, FFN 14336, vocab
+128256; layer matrices Q4_0, embedding and lm head Q8_0; weights N(0, 0.02)
+from a seed; a 512-token seeded prompt, then greedy decode steps with an
+fp16 KV cache, batch 1 (``--batch 8`` for eight independent sequences).
+A step is one decoded token per sequence through every layer and the lm
+head. ``value`` is decode tokens/s with everything resident in HBM
+(CUDA-graph replays timed by CUDA events); ``e2e`` is the same through
+the C ABI's host-buffer call (``pai_b200_session_step``: token H2D, step,
+next-token D2H each step). The model's 4.5 GB of weights exceed the
+126 MB L2, so no flush is needed between steps.
+
+``--impl reference`` times the reference's own CPU implementation of the
+path instead (see ``reference_arm``).
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CFG_8B = dict(n_layer=32, n_embd=4096, n_head=32, n_head_kv=8, head_dim=128, n_ff=14336,
+              vocab=128256, eps=1e-5, rope_theta=500000.0, wtype=2, etype=8)
+PROMPT = 512
+SEED = 20261201
+METRIC = "Q4_0 8B-shape decode tok/s"
+UNIT = "tokens/s"
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class Clocks:
+    """Sample nvidia-smi clocks and throttle reasons during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.dev), f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+                self.lines = [l for l in out.splitlines() if l.strip()]
+            except Exception:
+                pass
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except (ValueError, IndexError):
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def gemv_roofline(dev, hbm_peak, peak_kind, iters=40):
+    """Time the dominant kernel alone: the Q4_0 GEMV of one layer's fused
+    gate|up matrix (28672 x 4096), rotating over 8 distinct copies
+    (8 x 66 MB > L2) so every launch streams its weights from HBM."""
+    from prosperoai_b200 import _native
+    from prosperoai_b200.api import Buffer
+    L = _native.load()
+    n, k, t = 2 * CFG_8B["n_ff"], CFG_8B["n_embd"], 2
+    rb = L.pai_b200_block_bytes(t, k)
+    copies = 8
+    tmp = dev.alloc(n * k * 4)
+    blk = dev.alloc(n * rb)
+    offs = dev.put(np.arange(n, dtype=np.uint64) * rb)
+    mats = []
+    for c in range(copies):
+        _native.check(L.pai_b200_synth_blocks(dev.ctx, t, n, k, SEED + 1000 + c, 0.02, tmp.ptr,
+                                              blk.ptr), "synth")
+        pk = Buffer(dev, L.pai_b200_packed_bytes(t, n, k))
+        _native.check(L.pai_b200_pack(dev.ctx, t, n, k, blk.ptr, offs.ptr, pk.ptr), "pack")
+        mats.append(pk)
+    tmp.free()
+    blk.free()
+    x = dev.put(np.random.default_rng(1).standard_normal(k).astype(np.float32))
+    y = dev.alloc(n * 4)
+    for i in range(6):
+        _native.check(L.pai_b200_gemv_f32(dev.ctx, t, 1, n, k, mats[i % copies].ptr, x.ptr, None,
+                                          y.ptr), "gemv")
+    e0, e1 = C.c_void_p(), C.c_void_p()
+    L.pai_b200_event_create(dev.ctx, C.byref(e0))
+    L.pai_b200_event_create(dev.ctx, C.byref(e1))
+    L.pai_b200_event_record(dev.ctx, e0)
+    for i in range(iters):
+        L.pai_b200_gemv_f32(dev.ctx, t, 1, n, k, mats[i % copies].ptr, x.ptr, None, y.ptr)
+    L.pai_b200_event_record(dev.ctx, e1)
+    ms = C.c_float()
+    _native.check(L.pai_b200_event_elapsed(e0, e1, C.byref(ms)), "elapsed")
+    dev.sync()
+    per = ms.value / iters
+    alg = n * rb + k * 4 + (n // 2) * 4  # weights + x + the n/2 silu*up outputs
+    achieved = alg / (per * 1e-3) / 1e9
+    for mat in mats:
+        mat.free()
+    return {"kernel": "k_gemv<Q4_0> fused gate|up 28672x4096 (silu*up epilogue off: plain store)",
+            "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+            "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind,
+            "algorithmic_bytes_per_launch": int(alg), "avg_launch_ms": round(per, 5),
+            "traffic": None}
+
+
+def cpu_baseline_port(dev, steps=3, prompt=24):
+    """The CPU restatement (oracle/, bit-identical to the reference ops)
+    on a bounded sample of the same decode: one 8B-shaped layer plus 1/32
+    of the lm-head rows, fed a short prompt, then `steps` timed tokens on
+    all host cores. tokens/s for the full model = 1 / (32 x sample time)."""
+    from oracle import py_oracle as po
+    from prosperoai_b200 import _native
+    L = _native.load()
+    cfg = dict(CFG_8B, n_layer=1, vocab=CFG_8B["vocab"] // 32)
+    E, qd, kd, ff = cfg["n_embd"], 4096, 1024, cfg["n_ff"]
+    shapes = {"wq": (qd, E, 2, 3), "wk": (kd, E, 2, 4), "wv": (kd, E, 2, 5), "wo": (E, qd, 2, 6),
+              "wgate": (ff, E, 2, 7), "wup": (ff, E, 2, 8), "wdown": (E, ff, 2, 9),
+              "tok_embd": (cfg["vocab"], E, 8, 0), "output": (cfg["vocab"], E, 8, 1)}
+    w = {}
+    for name, (rows, cols, t, kind) in shapes.items():
+        tmp = dev.alloc(rows * cols * 4)
+        blk = dev.alloc(rows * L.pai_b200_block_bytes(t, cols))
+        _native.check(L.pai_b200_synth_blocks(dev.ctx, t, rows, cols,
+                                              L.pai_b200_tensor_seed(SEED, kind, 0), 0.02, tmp.ptr,
+                                              blk.ptr), "synth")
+        b = blk.download(np.uint8)
+        w[name] = b if name in ("tok_embd", "output") else [b]
+        tmp.free()
+        blk.free()
+    w["attn_norm"] = [np.ones(E, np.float32)]
+    w["ffn_norm"] = [np.ones(E, np.float32)]
+    w["output_norm"] = np.ones(E, np.float32)
+    threads = os.cpu_count() or 1
+    s = po.Session(cfg, w, prompt + steps + 2, threads=threads)
+    tok = 1
+    for i in range(prompt):
+        tok = s.step(i % cfg["vocab"])
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        tok = s.step(tok)
+    dt = (time.perf_counter() - t0) / steps
+    s.close()
+    return {"value": round(1.0 / (32 * dt), 4), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": (f"oracle C restatement, 1 of 32 layers + 1/32 of lm-head rows at the 8B shape, "
+                       f"positions {prompt}..{prompt + steps - 1}, {steps} tokens timed; "
+                       f"full-model tok/s = 1/(32 x {dt * 1e3:.1f} ms)")}
+
+
+def gpu_arm(args):
+    from prosperoai_b200 import _native
+    from prosperoai_b200.api import Device, Model, Session
+    rank, world, local = dist_env()
+    pg = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("gloo", timeout=__import__("datetime").timedelta(seconds=600))
+        pg = dist
+    L = _native.load()
+    dev = Device(local)
+    cfg = dict(CFG_8B)
+    B, K, W = args.batch, args.steps, args.warmup
+    model = Model(dev, cfg)
+    model.synthesize(SEED)
+    max_ctx = PROMPT + W + 2 * K + 8
+    sess = Session(model, B, max_ctx)
+    prompts = np.random.default_rng(SEED).integers(0, cfg["vocab"], (B, PROMPT)).astype(np.int32)
+    for p in range(PROMPT):  # prompt positions, untimed
+        sess.set_tokens(prompts[:, p])
+        sess.run(1)
+    sess.run(W)  # warm-up greedy steps
+    dev.sync()
+    if pg:
+        pg.barrier()
+    launches0 = dev.launches()
+    e0, e1 = C.c_void_p(), C.c_void_p()
+    L.pai_b200_event_create(dev.ctx, C.byref(e0))
+    L.pai_b200_event_create(dev.ctx, C.byref(e1))
+    pos0 = sess.pos
+    with Clocks(local) as clk:
+        dev.sync()
+        L.pai_b200_event_record(dev.ctx, e0)
+        sess.run(K)
+        L.pai_b200_event_record(dev.ctx, e1)
+        dev.sync()
+    ms = C.c_float()
+    _native.check(L.pai_b200_event_elapsed(e0, e1, C.byref(ms)), "elapsed")
+    launches = dev.launches() - launches0
+    t_dev = ms.value
+    # e2e: the same steps through the host-buffer C ABI call
+    tok = sess.tokens()
+    dev.sync()
+    L.pai_b200_event_record(dev.ctx, e0)
+    w0 = time.perf_counter()
+    for _ in range(K):
+        tok = sess.step(tok)
+    wall = (time.perf_counter() - w0) * 1e3
+    L.pai_b200_event_record(dev.ctx, e1)
+    ms2 = C.c_float()
+    _native.check(L.pai_b200_event_elapsed(e0, e1, C.byref(ms2)), "elapsed")
+    t_e2e = max(ms2.value, wall)
+    if pg:
+        import torch
+        t = torch.tensor([t_dev, t_e2e], dtype=torch.float64)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        t_dev, t_e2e = float(t[0]), float(t[1])
+    hbm, kind = peaks()
+    # bytes one decode step reads: weights + the KV cache up to the mean position
+    mean_pos = pos0 + K / 2.0
+    kv_bytes = cfg["n_layer"] * cfg["n_head_kv"] * cfg["head_dim"] * 2 * 2 * mean_pos * B
+    step_bytes = model.step_weight_bytes() + kv_bytes
+    step_gbs = step_bytes / (t_dev / K * 1e-3) / 1e9
+    result = None
+    if rank == 0:
+        roof = gemv_roofline(dev, hbm, kind)
+        cpu = None if args.no_cpu_baseline else cpu_baseline_port(dev)
+        value = world * B * K / (t_dev * 1e-3)
+        result = {
+            "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
+            "steps": K, "warmup": W, "ms_per_step": round(t_dev / K, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "q4_0 weights, f32 accumulate",
+            "data": "synthetic (seeded N(0,0.02) weights, seeded prompt ids)",
+            "config": {"workload": "Llama-3-8B-shaped Q4_0 decode (config 5)", "batch": B,
+                       "prompt": PROMPT, "positions_timed": [pos0, pos0 + K - 1],
+                       "layers": cfg["n_layer"], "hidden": cfg["n_embd"], "vocab": cfg["vocab"],
+                       "kv_cache": "fp16",
+                       "parallelism": "single GPU" if world == 1 else f"{world} independent replicas",
+                       "l2": "no flush: 4.5 GB of weights per step exceed the 126 MB L2"},
+            "e2e": {"value": round(world * B * K / (t_e2e * 1e-3), 3), "unit": UNIT,
+                    "h2d_bytes_per_step": 4 * B, "d2h_bytes_per_step": 4 * B},
+            "gpu_launches": int(launches),
+            "roofline": roof,
+            "step_roofline": {"bytes_per_step": int(step_bytes), "achieved": round(step_gbs, 1),
+                              "peak": hbm, "unit": "GB/s", "frac": round(step_gbs / hbm, 4),
+                              "peak_kind": kind},
+            "clocks": clk.summary(),
+            "cpu_baseline": cpu,
+        }
+    sess.close()
+    model.close()
+    dev.close()
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+    return result
+
+
+def reference_arm(args):
+    """The reference's own CPU code for one decode token, on a bounded sample.
+
+    oracle/_ref/libpai_ref.so is the reference's cpu/reference, cpu/optimized
+    and adapters/llama sources compiled unmodified. Its session keeps
+    weights as f32 after dequantising them once (models/model.c:246-290),
+    so the sample does that with the reference's dequant_block and then
+    runs one 8B-shaped layer per token with the reference's fastest GEMV
+    (pai_opt_gemv_f32, AVX2+FMA) on disjoint row slices over all host
+    threads, the reference's rmsnorm/rope/silu/vecmul/vecadd, and decode
+    attention over 512 cached positions (the last-row loop of
+    pai_ref_attention_f32, restated in oracle/ because the reference only
+    offers the full-sequence form), plus 1/32 of the lm head.
+    tok/s = 1 / (32 x sample time).
+    """
+    from concurrent.futures import ThreadPoolExecutor
+
+    from oracle import py_oracle as po
+    R = po.ref()
+    kind = "reference"
+    if R is None:
+        kind = "port"
+    E, ff, qd, kd, hd = 4096, 14336, 4096, 1024, 128
+    vocab_s = CFG_8B["vocab"] // 32
+    rng = np.random.default_rng(SEED)
+    threads = os.cpu_count() or 1
+
+    def dq(t, rows, cols):
+        w = (rng.standard_normal(rows * cols, dtype=np.float32) * np.float32(0.02))
+        blocks = po.quantize(t, w)
+        out = np.empty(rows * cols, np.float32)
+        if R is not None:
+            assert R.pai_refshim_dequant(t, blocks, out, out.size) == 0
+        else:
+            out[:] = po.dequant(t, blocks, out.size)
+        return out.reshape(rows, cols)
+
+    mats = {"q": dq(2, qd, E), "k": dq(2, kd, E), "v": dq(2, kd, E), "o": dq(2, E, qd),
+            "gate": dq(2, ff, E), "up": dq(2, ff, E), "down": dq(2, E, ff), "lm": dq(8, vocab_s, E)}
+    pool = ThreadPoolExecutor(threads)
+    gemv_fn = R.pai_opt_gemv_f32 if R is not None else po.lib().po_gemv_f32
+
+    def gemv(W, x):
+        n, k = W.shape
+        y = np.empty(n, np.float32)
+        bounds = np.linspace(0, n, threads + 1).astype(int)
+
+        def part(i):
+            a, b = bounds[i], bounds[i + 1]
+            if b > a:
+                yv = y[a:b]
+                gemv_fn(b - a, k, np.ascontiguousarray(W[a:b]), x, yv)
+        list(pool.map(part, range(threads)))
+        return y
+
+    P = PROMPT
+    kc = rng.standard_normal((8, P + 1, hd)).astype(np.float16).view(np.uint16)
+    vc = rng.standard_normal((8, P + 1, hd)).astype(np.float16).view(np.uint16)
+    cos_t, sin_t = po.rope_tables(P + 1, hd // 2, 500000.0)
+    ones = np.ones(E, np.float32)
+    x = rng.standard_normal(E).astype(np.float32)
+
+    def ref_call(fn, *a):
+        if R is not None:
+            getattr(R, "pai_ref_" + fn)(*a)
+        else:
+            getattr(po.lib(), "po_" + fn)(*a)
+
+    def one_token(x):
+        xn = np.empty(E, np.float32)
+        ref_call("rmsnorm_gamma_f32", x, xn, E, ones, 1e-5)
+        q, k, v = gemv(mats["q"], xn), gemv(mats["k"], xn), gemv(mats["v"], xn)
+        qr, kr = np.empty_like(q), np.empty_like(k)
+        po.lib().po_rope_at_f32(q, 32, hd, P, cos_t, sin_t, hd // 2, qr)
+        po.lib().po_rope_at_f32(k, 8, hd, P, cos_t, sin_t, hd // 2, kr)
+        kc[:, P] = kr.reshape(8, hd).astype(np.float16).view(np.uint16)
+        vc[:, P] = v.reshape(8, hd).astype(np.float16).view(np.uint16)
+        att = po.attention_decode_f16(32, 8, hd, P + 1, P + 1, qr, kc, vc)
+        o = gemv(mats["o"], att)
+        x1 = np.empty(E, np.float32)
+        ref_call("vecadd_f32", x, o, x1, E)
+        ref_call("rmsnorm_gamma_f32", x1, xn, E, ones, 1e-5)
+        g, u = gemv(mats["gate"], xn), gemv(mats["up"], xn)
+        sg, h = np.empty_like(g), np.empty_like(g)
+        ref_call("silu_f32", g, sg, ff)
+        ref_call("vecmul_f32", sg, u, h, ff)
+        d = gemv(mats["down"], h)
+        x2 = np.empty(E, np.float32)
+        ref_call("vecadd_f32", x1, d, x2, E)
+        gemv(mats["lm"], x2)
+        return x2
+
+    for _ in range(args.warmup):
+        one_token(x)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        one_token(x)
+    dt = (time.perf_counter() - t0) / args.steps
+    value = 1.0 / (32 * dt)
+    sample = (f"reference cpu/optimized pai_opt_gemv_f32 (AVX2) on row slices x {threads} threads + "
+              f"cpu/reference elementwise ops, 1 of 32 layers + 1/32 of the lm head per step, "
+              f"f32 weights dequantised by the reference's dequant_block, attention over {P + 1} "
+              f"cached positions; tok/s = 1/(32 x {dt * 1e3:.1f} ms)")
+    return {"metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": 0,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(32 * dt * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32 (weights dequantised from Q4_0/Q8_0)", "data": "synthetic",
+            "config": {"workload": "Llama-3-8B-shaped Q4_0 decode (config 5)", "batch": 1,
+                       "prompt": PROMPT},
+            "impl": "reference",
+            "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": kind,
+                             "sample": sample},
+            "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--batch", type=int, default=1, choices=[1, 2, 4, 8])
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank, world, _ = dist_env()
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        args.steps = min(args.steps, 8)
+        print(json.dumps(reference_arm(args)), flush=True)
+        return
+    res = gpu_arm(args)
+    if res is not None:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

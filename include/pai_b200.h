@@ -1,0 +1,342 @@
+/*
+ * pai_b200.h — the `cuda-b200` backend of the ProsperoAI runtime: a C ABI
+ * over hand-written sm_100a kernels for the quantized-weights hot path.
+ *
+ * Everything here is plain C: integers, floats and pointers. Device
+ * pointers are returned by pai_b200_alloc and passed back unchanged;
+ * nothing in the signatures is a CUDA or PyTorch type. All calls return
+ * a ProsperoAI status code (pai/error.h:13-23): PAI_ERR_INVALID_ARG for a
+ * NULL or ill-shaped argument, PAI_ERR_MISMATCH for inconsistent shapes,
+ * PAI_ERR_UNSUPPORTED for a block type or size the backend does not run,
+ * PAI_ERR_NOMEM when device memory is exhausted, PAI_ERR_TIMEOUT when a
+ * bounded device wait ran out, and PAI_ERR_INTERNAL for a CUDA or NCCL
+ * failure (the message is kept for pai_b200_last_error).
+ *
+ * Operations are asynchronous on the context's stream, like kernel
+ * launches; pai_b200_sync() waits. The reference executor is synchronous
+ * (scheduler/scheduler.c:346-632 returns when every step is done), so
+ * the integration shim syncs at the same boundaries.
+ */
+#ifndef PAI_B200_H
+#define PAI_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- types shared with the reference ABI --------------------------------
+ * When the reference headers are included first, theirs are used; the
+ * definitions below are layout-identical restatements of them.          */
+
+#ifndef PAI_ERROR_H
+typedef int32_t pai_status_t; /* pai/error.h:11 */
+#define PAI_OK 0
+#define PAI_ERR_INVALID_ARG -1
+#define PAI_ERR_NOMEM -2
+#define PAI_ERR_UNSUPPORTED -3
+#define PAI_ERR_CAPABILITY -4
+#define PAI_ERR_TIMEOUT -5
+#define PAI_ERR_MISMATCH -6
+#define PAI_ERR_IO -7
+#define PAI_ERR_INIT -8
+#define PAI_ERR_INTERNAL -9
+#endif
+
+#ifndef PAI_OP_H
+typedef int32_t pai_kernel_id_t;               /* pai/op.h:28 */
+typedef pai_status_t (*pai_op_ref_fn)(void);   /* pai/op.h:69 */
+typedef struct pai_op_descriptor {             /* pai/op.h:71-84 */
+  const char *name;
+  uint32_t version;
+  uint32_t num_inputs;
+  uint32_t num_outputs;
+  int32_t in_dtype;  /* pai_dtype_t (pai/dtype.h:13-24), an int-sized enum */
+  int32_t out_dtype;
+  uint32_t caps;
+  pai_op_ref_fn ref_fn;
+  pai_kernel_id_t kernel_id;
+  uint32_t reserved[2];
+} pai_op_descriptor_t;
+#define PAI_OP_REGISTRY_MAX_OPS 64u            /* pai/op.h:88 */
+typedef struct pai_op_registry {               /* pai/op.h:90-94 */
+  uint32_t version;
+  uint32_t count;
+  const pai_op_descriptor_t *ops[PAI_OP_REGISTRY_MAX_OPS];
+} pai_op_registry_t;
+#endif
+
+/* Capability bit of this backend: the next free bit after
+ * PAI_OP_CAP_HOST_REF (pai/op.h:59-61). */
+#define PAI_OP_CAP_CUDA_B200 (1u << 3)
+
+/* Kernel ids of this backend, after the reference's 1..13 (pai/op.h:37-51). */
+enum {
+  PAI_KERNEL_B200_GEMV_Q8_0 = 14,
+  PAI_KERNEL_B200_GEMV_Q4_0 = 15,
+  PAI_KERNEL_B200_GEMV_Q4_K = 16,
+  PAI_KERNEL_B200_GEMM_Q4_0 = 17,
+  PAI_KERNEL_B200_RMSNORM = 18,
+  PAI_KERNEL_B200_ROPE = 19,
+  PAI_KERNEL_B200_ATTN_DECODE = 20,
+  PAI_KERNEL_B200_ATTENTION = 21,
+  PAI_KERNEL_B200_SILU_MUL = 22,
+  PAI_KERNEL_B200_VECADD = 23,
+  PAI_KERNEL_B200_DEQUANT = 24,
+  PAI_KERNEL_B200_ARGMAX = 25
+};
+
+/* ggml block types, numbered as adapters/llama/gguf.h:36-51. */
+#define PAI_B200_Q4_0 2u  /* 32 weights: fp16 d, 16 B of nibbles       (18 B) */
+#define PAI_B200_Q8_0 8u  /* 32 weights: fp16 d, 32 int8                (34 B) */
+#define PAI_B200_Q4_K 12u /* 256 weights: fp16 d, fp16 dmin, 12 B packed
+                             6-bit scales/mins, 128 B of nibbles      (144 B) */
+
+typedef struct pai_b200_ctx pai_b200_ctx_t;
+
+/* ---- runtime ---------------------------------------------------------------- */
+
+/* Open device `device` and create a context with its own stream and
+ * scratch memory. Replaces the PS5 HAL's device bring-up
+ * (runtime/runtime.c:18-80, gpu/hal/hal.h:45-61). */
+pai_status_t pai_b200_init(int device, pai_b200_ctx_t **out);
+pai_status_t pai_b200_shutdown(pai_b200_ctx_t *ctx);
+pai_status_t pai_b200_device_count(int *out);
+/* Text of the last failure on this thread ("" when none). */
+const char *pai_b200_last_error(void);
+/* Library build string (kernels, arch). */
+const char *pai_b200_version(void);
+
+/* Device memory (the planner region of models/model.c:236 moves here). */
+pai_status_t pai_b200_alloc(pai_b200_ctx_t *ctx, uint64_t bytes, void **out);
+pai_status_t pai_b200_free(pai_b200_ctx_t *ctx, void *p);
+/* Page-locked host memory for copies that overlap compute. */
+pai_status_t pai_b200_host_alloc(pai_b200_ctx_t *ctx, uint64_t bytes, void **out);
+pai_status_t pai_b200_host_free(pai_b200_ctx_t *ctx, void *p);
+pai_status_t pai_b200_memcpy_h2d(pai_b200_ctx_t *ctx, void *dst, const void *src,
+                                 uint64_t bytes);
+pai_status_t pai_b200_memcpy_d2h(pai_b200_ctx_t *ctx, void *dst, const void *src,
+                                 uint64_t bytes);
+pai_status_t pai_b200_memcpy_d2d(pai_b200_ctx_t *ctx, void *dst, const void *src,
+                                 uint64_t bytes);
+pai_status_t pai_b200_memset(pai_b200_ctx_t *ctx, void *dst, int value,
+                             uint64_t bytes);
+/* Wait for all work queued on the context; reports any device error. */
+pai_status_t pai_b200_sync(pai_b200_ctx_t *ctx);
+
+/* Stream-ordered timing: event_record places a marker, event_elapsed
+ * waits for both markers and returns milliseconds between them. */
+pai_status_t pai_b200_event_create(pai_b200_ctx_t *ctx, void **ev);
+pai_status_t pai_b200_event_destroy(pai_b200_ctx_t *ctx, void *ev);
+pai_status_t pai_b200_event_record(pai_b200_ctx_t *ctx, void *ev);
+pai_status_t pai_b200_event_elapsed(void *start, void *stop, float *ms);
+
+/* Number of this library's kernels launched on the context so far
+ * (graph replays count every kernel node they run). */
+uint64_t pai_b200_launch_count(pai_b200_ctx_t *ctx);
+
+/* ---- weight blocks ------------------------------------------------------------- */
+
+/* ggml byte size of numel elements (adapters/llama/gguf.c:563-599);
+ * 0 when numel is not a whole number of blocks. */
+uint64_t pai_b200_block_bytes(uint32_t type, uint64_t numel);
+/* Host block quantiser: numel fp32 values -> ggml blocks.
+ *   Q8_0: d = max|w|/127, q = lrintf(w/d) in [-127,127]
+ *   Q4_0: d = m/-8 (m the first element of largest |w|),
+ *         q = clamp(lrintf(w/d)+8, 0, 15)
+ *   Q4_K: per 32-sub-block scale (max-min)/15 and offset -min, 6-bit
+ *         codes against fp16 d/dmin = their maxima/63.
+ * Dequantising the result with gguf.c:651-967 gives w back to within the
+ * block's step. The reference has no ggml quantiser (it dequantises at
+ * import, adapters/llama/llama.c:408-457), so these formulas are the
+ * benchmark specification's. */
+pai_status_t pai_b200_quantize(uint32_t type, const float *src, uint64_t numel,
+                               void *dst_blocks);
+
+/* Weights live on the device in a packed layout built once at load from
+ * ggml blocks: rows in groups of 32, each (group, block) stored as 16-byte
+ * chunks interleaved across the 32 rows, with the fp16 scales in a
+ * separate plane. Byte count of an n x k matrix in that layout: */
+uint64_t pai_b200_packed_bytes(uint32_t type, uint64_t n, uint64_t k);
+/* Pack rows of ggml blocks already on the device. Packed row r is taken
+ * from src + row_offsets[r] (a device array of n byte offsets; ~0 gives
+ * a zero row, ~0-1 leaves the row untouched), reading k/block_elems
+ * blocks starting there. Concatenation,
+ * interleaving and tensor-parallel slicing are all row-offset tables. */
+pai_status_t pai_b200_pack(pai_b200_ctx_t *ctx, uint32_t type, uint64_t n,
+                           uint64_t k, const void *src,
+                           const uint64_t *row_offsets, void *dst_packed);
+/* Upload an n x k ggml matrix from host memory and pack it (convenience
+ * over pai_b200_pack with contiguous rows). */
+pai_status_t pai_b200_upload_matrix(pai_b200_ctx_t *ctx, uint32_t type, uint64_t n,
+                                    uint64_t k, const void *host_blocks,
+                                    void *dst_packed);
+/* Device dequantisation of a packed n x k matrix to fp32 [n][k],
+ * bit-identical to dequant_block (adapters/llama/gguf.c:680-693,
+ * 750-761, 852-882). */
+pai_status_t pai_b200_dequant(pai_b200_ctx_t *ctx, uint32_t type, uint64_t n,
+                              uint64_t k, const void *packed, float *out);
+
+/* ---- hot-path ops (device pointers; asynchronous) ----------------------------- */
+
+/* y[n] = W[n,k] . x[k] with the dequantisation fused into the dot product,
+ * fp32 accumulation. Replaces the GEMM/GEMV step of the executor
+ * (scheduler/scheduler.c:413-428 -> run_gemm :285-343 -> pai_ref_gemm_f32,
+ * ref_ops.c:428-444) for a quantized B operand; the reference result is
+ * pai_gguf_dequant + pai_ref_gemv_f32 (ref_ops.c:92-106). */
+pai_status_t pai_b200_gemv_q8_0_f32(pai_b200_ctx_t *ctx, uint64_t n, uint64_t k,
+                                    const void *w, const float *x, float *y);
+pai_status_t pai_b200_gemv_q4_0_f32(pai_b200_ctx_t *ctx, uint64_t n, uint64_t k,
+                                    const void *w, const float *x, float *y);
+pai_status_t pai_b200_gemv_q4_k_f32(pai_b200_ctx_t *ctx, uint64_t n, uint64_t k,
+                                    const void *w, const float *x, float *y);
+/* Batched form with optional fused residual: for each of `batch` rows,
+ * y[b][n] = (residual ? residual[b][n] : 0) + W . x[b]. The residual add
+ * is the executor's following PAI_OP_ADD (scheduler.c:396-403,
+ * adapters/llama/llama.c:747-749,793-795), fused. residual may equal y. */
+pai_status_t pai_b200_gemv_f32(pai_b200_ctx_t *ctx, uint32_t type, uint64_t batch,
+                               uint64_t n, uint64_t k, const void *w,
+                               const float *x, const float *residual, float *y);
+
+/* c = a * gamma * (1/sqrtf(mean(a^2) + eps)) per row of n
+ * (pai_ref_rmsnorm_gamma_f32, ref_ops.c:196-216; eps 0 selects 1e-5). */
+pai_status_t pai_b200_rmsnorm_gamma_f32(pai_b200_ctx_t *ctx, uint64_t rows,
+                                        uint64_t n, const float *a,
+                                        const float *gamma, float eps, float *c);
+/* out = silu(gate) * up (pai_ref_silu_f32 + pai_ref_vecmul_f32,
+ * ref_ops.c:219-228, 124-133). */
+pai_status_t pai_b200_silu_mul_f32(pai_b200_ctx_t *ctx, const float *gate,
+                                   const float *up, float *out, uint64_t n);
+/* c = a + b (pai_ref_vecadd_f32, ref_ops.c:8-17). */
+pai_status_t pai_b200_vecadd_f32(pai_b200_ctx_t *ctx, const float *a,
+                                 const float *b, float *c, uint64_t n);
+/* Rotary embedding, same arguments as pai_ref_rope_f32 (ref_ops.c:231-257;
+ * ref_ops.h:96-99): half-split pairs (i, i+r2), row = p*heads + h. */
+pai_status_t pai_b200_rope_f32(pai_b200_ctx_t *ctx, const float *x, uint64_t rows,
+                               uint64_t hd, uint64_t seq, uint64_t heads,
+                               const float *cos_t, const float *sin_t, uint64_t r2,
+                               float *out);
+/* Host: RoPE tables as pai_ref_rope_cossin_f32 (ref_ops.c:260-279). */
+pai_status_t pai_b200_rope_cossin_f32(uint64_t ctx_len, uint64_t r2, float base,
+                                      float *cos_t, float *sin_t);
+/* Causal GQA attention over position-major fp32 q/k/v
+ * (pai_ref_attention_f32, ref_ops.c:287-354). */
+pai_status_t pai_b200_attention_f32(pai_b200_ctx_t *ctx, uint64_t h, uint64_t hk,
+                                    uint64_t seq, uint64_t hd, const float *q,
+                                    const float *k, const float *v, float *out);
+/* Decode attention of one query position over an fp16 KV cache laid out
+ * [hk][cap][hd]: out[h][hd] for positions 0..npos-1. This is the last row
+ * of pai_ref_attention_f32 on the cache contents. */
+pai_status_t pai_b200_attn_decode_f16kv(pai_b200_ctx_t *ctx, uint64_t h,
+                                        uint64_t hk, uint64_t hd, uint64_t npos,
+                                        uint64_t cap, const float *q,
+                                        const uint16_t *kcache,
+                                        const uint16_t *vcache, float *out);
+/* First index of the strict maximum of each row of logits[rows][n]
+ * (models/sampler.c:89-99 greedy). out is device int32[rows]. */
+pai_status_t pai_b200_argmax_f32(pai_b200_ctx_t *ctx, uint64_t rows, uint64_t n,
+                                 const float *logits, int32_t *out);
+
+/* ---- registry ------------------------------------------------------------------- */
+
+/* Register this backend's op descriptors (caps PAI_OP_CAP_CUDA_B200,
+ * ref_fn NULL: the CPU twin stays the builtin op of the same meaning) into
+ * a registry filled by pai_op_registry_builtin (runtime/op_registry.c:
+ * 367-397). Descriptors are static and outlive any registry (pai/op.h:
+ * 98-100). Returns PAI_ERR_NOMEM when the 64-op table is full. */
+pai_status_t pai_b200_register_ops(pai_op_registry_t *reg);
+/* Number of descriptors pai_b200_register_ops adds, and access to them. */
+uint32_t pai_b200_op_count(void);
+const pai_op_descriptor_t *pai_b200_op(uint32_t i);
+
+/* ---- decoder model and session ---------------------------------------------- */
+
+/* A LLaMA-shaped decoder in the op order of adapters/llama/llama.c:669-797
+ * (rmsnorm, q/k/v, rope(q,k), attention, o, add, rmsnorm, gate/up,
+ * silu*up, down, add; then final rmsnorm, lm head, greedy). */
+typedef struct pai_b200_model_cfg {
+  uint32_t n_layer, n_embd, n_head, n_head_kv, head_dim, n_ff, vocab;
+  float eps, rope_theta;
+  uint32_t wtype; /* block type of the layer matrices (Q4_0/Q8_0/Q4_K) */
+  uint32_t etype; /* block type of token embedding and lm head        */
+} pai_b200_model_cfg_t;
+
+typedef struct pai_b200_model pai_b200_model_t;
+typedef struct pai_b200_session pai_b200_session_t;
+
+/* Tensor kinds for pai_b200_model_set_tensor. */
+enum {
+  PAI_B200_T_TOK_EMBD = 0, /* [vocab][n_embd] etype blocks  */
+  PAI_B200_T_OUTPUT = 1,   /* [vocab][n_embd] etype blocks  */
+  PAI_B200_T_OUTPUT_NORM = 2, /* [n_embd] f32               */
+  PAI_B200_T_WQ = 3, PAI_B200_T_WK = 4, PAI_B200_T_WV = 5, PAI_B200_T_WO = 6,
+  PAI_B200_T_WGATE = 7, PAI_B200_T_WUP = 8, PAI_B200_T_WDOWN = 9,
+  PAI_B200_T_ATTN_NORM = 10, PAI_B200_T_FFN_NORM = 11
+};
+
+/* Create the model for tensor-parallel rank tp_rank of tp_size (1 for a
+ * single GPU). Column-parallel q/k/v/gate/up and vocab-sharded lm head are
+ * split by output rows, row-parallel o/down by input columns. */
+pai_status_t pai_b200_model_create(pai_b200_ctx_t *ctx,
+                                   const pai_b200_model_cfg_t *cfg,
+                                   uint32_t tp_rank, uint32_t tp_size,
+                                   pai_b200_model_t **out);
+pai_status_t pai_b200_model_destroy(pai_b200_model_t *m);
+/* Load one whole (unsharded) tensor from host memory: ggml blocks
+ * [out][in] for matrices, fp32 for norms. The model keeps its shard. */
+pai_status_t pai_b200_model_set_tensor(pai_b200_model_t *m, uint32_t kind,
+                                       uint32_t layer, const void *host);
+/* Fill every tensor with the seeded synthetic model: weights N(0, 0.02)
+ * quantised to the configured block types, norm gains 1.0. */
+pai_status_t pai_b200_model_synthesize(pai_b200_model_t *m, uint64_t seed);
+/* Seed of one synthetic tensor (kind, layer) of the model seeded `seed`. */
+uint64_t pai_b200_tensor_seed(uint64_t seed, uint32_t kind, uint32_t layer);
+/* Device generator behind pai_b200_model_synthesize: rows x cols values
+ * N(0, stddev) into tmp_f32 (row r is the splitmix64 stream from
+ * mix64(seed + r), Box-Muller in double), then ggml blocks of `type`
+ * into dst_blocks. Exposed so tests can hand the same blocks to a CPU
+ * checker. */
+pai_status_t pai_b200_synth_blocks(pai_b200_ctx_t *ctx, uint32_t type, uint64_t rows,
+                                   uint64_t cols, uint64_t seed, float stddev,
+                                   float *tmp_f32, void *dst_blocks);
+/* Device bytes held by the model's weights on this rank. */
+uint64_t pai_b200_model_weight_bytes(const pai_b200_model_t *m);
+/* Bytes of weights one decode step reads on this rank (all layers plus
+ * the lm-head shard plus one embedding row). */
+uint64_t pai_b200_model_step_weight_bytes(const pai_b200_model_t *m);
+
+/* A decode session of `batch` independent sequences with an fp16 KV cache
+ * of max_ctx positions per sequence ([layer][kv_head][pos][head_dim],
+ * split by KV head across tensor-parallel ranks). */
+pai_status_t pai_b200_session_create(pai_b200_model_t *m, uint32_t batch,
+                                     uint32_t max_ctx, pai_b200_session_t **out);
+pai_status_t pai_b200_session_destroy(pai_b200_session_t *s);
+/* Position of the next token (equal for all sequences). */
+uint32_t pai_b200_session_pos(const pai_b200_session_t *s);
+/* Reset to position 0 (the cache contents are left; positions >= pos
+ * are never read). */
+pai_status_t pai_b200_session_reset(pai_b200_session_t *s);
+/* One decode step from host memory: feed tokens[batch], run every layer
+ * and the lm head, and write the greedy next tokens to next[batch]
+ * (host). logits (host, [batch][vocab]) may be NULL. Synchronous: the
+ * call returns when `next` is written, like pai_sched_execute. */
+pai_status_t pai_b200_session_step(pai_b200_session_t *s, const int32_t *tokens,
+                                   int32_t *next, float *logits);
+/* Device-resident decode: run `steps` greedy steps, each feeding back the
+ * previous step's token, without host round trips (CUDA-graph replays).
+ * The first step reads the device token buffer set by the last
+ * session_step or session_set_tokens. Asynchronous. */
+pai_status_t pai_b200_session_run(pai_b200_session_t *s, uint32_t steps);
+pai_status_t pai_b200_session_set_tokens(pai_b200_session_t *s,
+                                         const int32_t *tokens);
+pai_status_t pai_b200_session_get_tokens(pai_b200_session_t *s, int32_t *tokens);
+/* Hidden state after the last step (device pointer, [batch][n_embd]). */
+const float *pai_b200_session_hidden(const pai_b200_session_t *s);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PAI_B200_H */

@@ -1,0 +1,240 @@
+"""Host-side API over the C ABI, shaped like the reference's op interface.
+
+Each op takes the arguments of its ``pai_ref_*`` twin (cpu/reference/ref_ops.h)
+with device buffers in place of host arrays, and raises ``PaiError`` carrying
+the reference status code (pai/error.h) when the C call fails.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from ._native import (Q4_0, Q4_K, Q8_0, ModelCfg, OpRegistry, PaiError, check, load)
+
+__all__ = ["Device", "Buffer", "PackedMatrix", "Model", "Session", "PaiError",
+           "Q4_0", "Q8_0", "Q4_K", "block_bytes", "quantize", "rope_tables"]
+
+BLOCK_ELEMS = {Q4_0: 32, Q8_0: 32, Q4_K: 256}
+
+
+def block_bytes(wtype: int, numel: int) -> int:
+    return int(load().pai_b200_block_bytes(wtype, numel))
+
+
+def quantize(wtype: int, w: np.ndarray) -> np.ndarray:
+    """Host ggml block quantiser (pai_b200_quantize)."""
+    w = np.ascontiguousarray(w, np.float32).ravel()
+    out = np.empty(block_bytes(wtype, w.size), np.uint8)
+    check(load().pai_b200_quantize(wtype, w.ctypes.data, w.size, out.ctypes.data), "quantize")
+    return out
+
+
+def rope_tables(ctx_len: int, r2: int, base: float):
+    c = np.empty(ctx_len * r2, np.float32)
+    s = np.empty(ctx_len * r2, np.float32)
+    check(load().pai_b200_rope_cossin_f32(ctx_len, r2, base, c.ctypes.data, s.ctypes.data),
+          "rope_cossin")
+    return c, s
+
+
+class Buffer:
+    """Device allocation owned by a Device."""
+
+    def __init__(self, dev: "Device", nbytes: int):
+        self.dev = dev
+        self.nbytes = int(nbytes)
+        p = C.c_void_p()
+        check(load().pai_b200_alloc(dev.ctx, max(self.nbytes, 1), C.byref(p)), "alloc")
+        self.ptr = p.value
+
+    def upload(self, arr: np.ndarray) -> "Buffer":
+        a = np.ascontiguousarray(arr)
+        assert a.nbytes <= self.nbytes
+        check(load().pai_b200_memcpy_h2d(self.dev.ctx, self.ptr, a.ctypes.data, a.nbytes), "h2d")
+        return self
+
+    def download(self, dtype, count: int | None = None) -> np.ndarray:
+        dtype = np.dtype(dtype)
+        n = self.nbytes // dtype.itemsize if count is None else count
+        out = np.empty(n, dtype)
+        check(load().pai_b200_memcpy_d2h(self.dev.ctx, out.ctypes.data, self.ptr, out.nbytes), "d2h")
+        self.dev.sync()
+        return out
+
+    def free(self):
+        if self.ptr and self.dev.ctx:
+            load().pai_b200_free(self.dev.ctx, self.ptr)
+        self.ptr = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class PackedMatrix:
+    """An n x k matrix of ggml blocks in the device GEMV layout."""
+
+    def __init__(self, dev: "Device", wtype: int, n: int, k: int, blocks: np.ndarray):
+        self.dev, self.wtype, self.n, self.k = dev, wtype, n, k
+        self.buf = dev.alloc(int(load().pai_b200_packed_bytes(wtype, n, k)))
+        b = np.ascontiguousarray(blocks, np.uint8)
+        assert b.nbytes == block_bytes(wtype, n * k)
+        check(load().pai_b200_upload_matrix(dev.ctx, wtype, n, k, b.ctypes.data, self.buf.ptr),
+              "upload_matrix")
+
+    @property
+    def ptr(self):
+        return self.buf.ptr
+
+
+class Device:
+    """One CUDA device context (pai_b200_init)."""
+
+    def __init__(self, device: int = 0):
+        L = load()
+        ctx = C.c_void_p()
+        check(L.pai_b200_init(device, C.byref(ctx)), "init")
+        self.ctx = ctx.value
+        self.device = device
+
+    def close(self):
+        if self.ctx:
+            load().pai_b200_shutdown(self.ctx)
+            self.ctx = None
+
+    def sync(self):
+        check(load().pai_b200_sync(self.ctx), "sync")
+
+    def alloc(self, nbytes: int) -> Buffer:
+        return Buffer(self, nbytes)
+
+    def put(self, arr: np.ndarray) -> Buffer:
+        a = np.ascontiguousarray(arr)
+        return Buffer(self, a.nbytes).upload(a)
+
+    def launches(self) -> int:
+        return int(load().pai_b200_launch_count(self.ctx))
+
+    # --- ops ------------------------------------------------------------------------------
+    def gemv(self, w: PackedMatrix, x: Buffer, y: Buffer, batch: int = 1,
+             residual: Buffer | None = None):
+        check(load().pai_b200_gemv_f32(self.ctx, w.wtype, batch, w.n, w.k, w.ptr, x.ptr,
+                                       residual.ptr if residual else None, y.ptr), "gemv")
+
+    def dequant(self, w: PackedMatrix, out: Buffer):
+        check(load().pai_b200_dequant(self.ctx, w.wtype, w.n, w.k, w.ptr, out.ptr), "dequant")
+
+    def rmsnorm_gamma(self, rows: int, n: int, a: Buffer, gamma: Buffer, eps: float, c: Buffer):
+        check(load().pai_b200_rmsnorm_gamma_f32(self.ctx, rows, n, a.ptr, gamma.ptr, eps, c.ptr),
+              "rmsnorm_gamma")
+
+    def silu_mul(self, gate: Buffer, up: Buffer, out: Buffer, n: int):
+        check(load().pai_b200_silu_mul_f32(self.ctx, gate.ptr, up.ptr, out.ptr, n), "silu_mul")
+
+    def vecadd(self, a: Buffer, b: Buffer, c: Buffer, n: int):
+        check(load().pai_b200_vecadd_f32(self.ctx, a.ptr, b.ptr, c.ptr, n), "vecadd")
+
+    def rope(self, x: Buffer, rows, hd, seq, heads, cos_t: Buffer, sin_t: Buffer, r2, out: Buffer):
+        check(load().pai_b200_rope_f32(self.ctx, x.ptr, rows, hd, seq, heads, cos_t.ptr, sin_t.ptr,
+                                       r2, out.ptr), "rope")
+
+    def attention(self, h, hk, seq, hd, q: Buffer, k: Buffer, v: Buffer, out: Buffer):
+        check(load().pai_b200_attention_f32(self.ctx, h, hk, seq, hd, q.ptr, k.ptr, v.ptr, out.ptr),
+              "attention")
+
+    def attn_decode_f16kv(self, h, hk, hd, npos, cap, q: Buffer, kc: Buffer, vc: Buffer,
+                          out: Buffer):
+        check(load().pai_b200_attn_decode_f16kv(self.ctx, h, hk, hd, npos, cap, q.ptr, kc.ptr,
+                                                vc.ptr, out.ptr), "attn_decode_f16kv")
+
+    def argmax(self, rows: int, n: int, logits: Buffer, out: Buffer):
+        check(load().pai_b200_argmax_f32(self.ctx, rows, n, logits.ptr, out.ptr), "argmax")
+
+    def register_ops(self, registry: OpRegistry):
+        check(load().pai_b200_register_ops(C.byref(registry)), "register_ops")
+
+
+class Model:
+    """LLaMA-shaped decoder resident on one device (one tensor-parallel rank)."""
+
+    def __init__(self, dev: Device, cfg: dict, tp_rank: int = 0, tp_size: int = 1):
+        self.dev = dev
+        self.cfg = dict(cfg)
+        c = ModelCfg(cfg["n_layer"], cfg["n_embd"], cfg["n_head"], cfg["n_head_kv"],
+                     cfg["head_dim"], cfg["n_ff"], cfg["vocab"], cfg["eps"], cfg["rope_theta"],
+                     cfg["wtype"], cfg["etype"])
+        h = C.c_void_p()
+        check(load().pai_b200_model_create(dev.ctx, C.byref(c), tp_rank, tp_size, C.byref(h)),
+              "model_create")
+        self.h = h.value
+
+    def set_tensor(self, kind: int, layer: int, host: np.ndarray):
+        a = np.ascontiguousarray(host)
+        check(load().pai_b200_model_set_tensor(self.h, kind, layer, a.ctypes.data), "set_tensor")
+
+    def synthesize(self, seed: int):
+        check(load().pai_b200_model_synthesize(self.h, seed), "synthesize")
+
+    def step_weight_bytes(self) -> int:
+        return int(load().pai_b200_model_step_weight_bytes(self.h))
+
+    def close(self):
+        if self.h:
+            load().pai_b200_model_destroy(self.h)
+            self.h = None
+
+
+class Session:
+    """Greedy decode session (pai_b200_session_*)."""
+
+    def __init__(self, model: Model, batch: int, max_ctx: int):
+        self.model, self.batch = model, batch
+        h = C.c_void_p()
+        check(load().pai_b200_session_create(model.h, batch, max_ctx, C.byref(h)),
+              "session_create")
+        self.h = h.value
+
+    def step(self, tokens, want_logits: bool = False):
+        t = np.ascontiguousarray(tokens, np.int32)
+        nxt = np.empty(self.batch, np.int32)
+        logits = (np.empty(self.batch * self.model.cfg["vocab"], np.float32)
+                  if want_logits else None)
+        check(load().pai_b200_session_step(self.h, t.ctypes.data, nxt.ctypes.data,
+                                           logits.ctypes.data if want_logits else None),
+              "session_step")
+        return (nxt, logits) if want_logits else nxt
+
+    def run(self, steps: int):
+        check(load().pai_b200_session_run(self.h, steps), "session_run")
+
+    def set_tokens(self, tokens):
+        t = np.ascontiguousarray(tokens, np.int32)
+        check(load().pai_b200_session_set_tokens(self.h, t.ctypes.data), "set_tokens")
+
+    def tokens(self) -> np.ndarray:
+        out = np.empty(self.batch, np.int32)
+        check(load().pai_b200_session_get_tokens(self.h, out.ctypes.data), "get_tokens")
+        return out
+
+    @property
+    def pos(self) -> int:
+        return int(load().pai_b200_session_pos(self.h))
+
+    def reset(self):
+        check(load().pai_b200_session_reset(self.h), "session_reset")
+
+    def hidden(self) -> np.ndarray:
+        p = load().pai_b200_session_hidden(self.h)
+        n = self.batch * self.model.cfg["n_embd"]
+        out = np.empty(n, np.float32)
+        check(load().pai_b200_memcpy_d2h(self.model.dev.ctx, out.ctypes.data, p, out.nbytes), "d2h")
+        self.model.dev.sync()
+        return out
+
+    def close(self):
+        if self.h:
+            load().pai_b200_session_destroy(self.h)
+            self.h = None

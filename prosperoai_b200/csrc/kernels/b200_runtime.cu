@@ -1,0 +1,269 @@
+// Runtime shim: device context, memory, copies, events, CUDA graphs and
+// error reporting behind the C ABI of include/pai_b200.h. The PS5 backend
+// this replaces kept the same duties in gpu/hal (hal.h:45-61: device
+// open, allocation, submit/wait); here a context owns one CUDA stream and
+// the split-K scratch the kernels share.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <new>
+
+#include "../b200_internal.h"
+
+struct pai_b200_ctx {
+  int device;
+  cudaStream_t stream;
+  float *partial;         // split-K partial sums
+  uint64_t partial_floats;
+  uint32_t *counters;     // split-K arrival counters, left at zero
+  uint32_t ncounters;
+  uint64_t launches;
+  int capturing;
+};
+
+static thread_local char g_err[512];
+
+extern "C" pai_status_t b200_fail(pai_status_t st, const char *fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return st;
+}
+
+extern "C" pai_status_t b200_cuda(int err, const char *what) {
+  if (err == cudaSuccess) return PAI_OK;
+  cudaError_t e = (cudaError_t)err;
+  if (e == cudaErrorMemoryAllocation)
+    return b200_fail(PAI_ERR_NOMEM, "%s: %s", what, cudaGetErrorString(e));
+  return b200_fail(PAI_ERR_INTERNAL, "%s: %s", what, cudaGetErrorString(e));
+}
+
+extern "C" const char *pai_b200_last_error(void) { return g_err; }
+
+extern "C" const char *pai_b200_version(void) {
+  return "pai_b200 0.1 (sm_100a; packed Q4_0/Q8_0/Q4_K GEMV, fp16-KV decode)";
+}
+
+extern "C" pai_status_t pai_b200_device_count(int *out) {
+  if (!out) return b200_fail(PAI_ERR_INVALID_ARG, "device_count: NULL");
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    *out = 0;
+    return PAI_OK;
+  }
+  *out = n;
+  return PAI_OK;
+}
+
+extern "C" pai_status_t pai_b200_init(int device, pai_b200_ctx_t **out) {
+  if (!out) return b200_fail(PAI_ERR_INVALID_ARG, "init: NULL out");
+  *out = nullptr;
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess || n == 0) {
+    cudaGetLastError();
+    return b200_fail(PAI_ERR_INIT, "init: no CUDA device (%s)", cudaGetErrorString(e));
+  }
+  if (device < 0 || device >= n) return b200_fail(PAI_ERR_INVALID_ARG, "init: device %d of %d", device, n);
+  pai_status_t st = b200_cuda(cudaSetDevice(device), "cudaSetDevice");
+  if (st) return st;
+  cudaDeviceProp prop;
+  st = b200_cuda(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+  if (st) return st;
+  if (prop.major != 10) {
+    return b200_fail(PAI_ERR_UNSUPPORTED, "init: device %d is sm_%d%d; this library is built for sm_100a only",
+                     device, prop.major, prop.minor);
+  }
+  pai_b200_ctx *c = new (std::nothrow) pai_b200_ctx();
+  if (!c) return b200_fail(PAI_ERR_NOMEM, "init: host allocation");
+  c->device = device;
+  st = b200_cuda(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "cudaStreamCreate");
+  if (st) {
+    delete c;
+    return st;
+  }
+  *out = c;
+  return PAI_OK;
+}
+
+extern "C" pai_status_t pai_b200_shutdown(pai_b200_ctx_t *c) {
+  if (!c) return PAI_OK;
+  cudaSetDevice(c->device);
+  cudaStreamSynchronize(c->stream);
+  if (c->partial) cudaFree(c->partial);
+  if (c->counters) cudaFree(c->counters);
+  cudaStreamDestroy(c->stream);
+  delete c;
+  return PAI_OK;
+}
+
+extern "C" void *b200_ctx_stream(pai_b200_ctx_t *c) { return c->stream; }
+extern "C" int b200_ctx_device(pai_b200_ctx_t *c) { return c->device; }
+extern "C" void b200_ctx_count_launch(pai_b200_ctx_t *c, uint32_t k) {
+  if (!c->capturing) c->launches += k;
+}
+extern "C" uint64_t pai_b200_launch_count(pai_b200_ctx_t *c) { return c ? c->launches : 0; }
+
+extern "C" pai_status_t b200_ctx_scratch(pai_b200_ctx_t *c, uint64_t partial_floats,
+                                         uint32_t counters, float **partial,
+                                         uint32_t **counter) {
+  if (partial_floats > c->partial_floats) {
+    if (c->capturing) return b200_fail(PAI_ERR_INTERNAL, "scratch growth during graph capture");
+    if (c->partial) {
+      cudaStreamSynchronize(c->stream);
+      cudaFree(c->partial);
+      c->partial = nullptr;
+    }
+    uint64_t want = partial_floats < (1u << 20) ? (1u << 20) : partial_floats;
+    pai_status_t st = b200_cuda(cudaMalloc(&c->partial, want * sizeof(float)), "scratch alloc");
+    if (st) {
+      c->partial_floats = 0;
+      return st;
+    }
+    c->partial_floats = want;
+  }
+  if (counters > c->ncounters) {
+    if (c->capturing) return b200_fail(PAI_ERR_INTERNAL, "scratch growth during graph capture");
+    if (c->counters) {
+      cudaStreamSynchronize(c->stream);
+      cudaFree(c->counters);
+      c->counters = nullptr;
+    }
+    uint32_t want = counters < 16384u ? 16384u : counters;
+    pai_status_t st = b200_cuda(cudaMalloc(&c->counters, want * sizeof(uint32_t)), "counter alloc");
+    if (st) {
+      c->ncounters = 0;
+      return st;
+    }
+    st = b200_cuda(cudaMemsetAsync(c->counters, 0, want * sizeof(uint32_t), c->stream), "counter clear");
+    if (st) return st;
+    c->ncounters = want;
+  }
+  *partial = c->partial;
+  *counter = c->counters;
+  return PAI_OK;
+}
+
+// ---- memory -------------------------------------------------------------------------------
+
+extern "C" pai_status_t pai_b200_alloc(pai_b200_ctx_t *c, uint64_t bytes, void **out) {
+  if (!c || !out) return b200_fail(PAI_ERR_INVALID_ARG, "alloc: NULL");
+  *out = nullptr;
+  if (bytes == 0) bytes = 256;
+  cudaSetDevice(c->device);
+  return b200_cuda(cudaMalloc(out, bytes), "cudaMalloc");
+}
+
+extern "C" pai_status_t pai_b200_free(pai_b200_ctx_t *c, void *p) {
+  if (!c) return b200_fail(PAI_ERR_INVALID_ARG, "free: NULL ctx");
+  if (!p) return PAI_OK;
+  cudaSetDevice(c->device);
+  cudaStreamSynchronize(c->stream);
+  return b200_cuda(cudaFree(p), "cudaFree");
+}
+
+extern "C" pai_status_t pai_b200_host_alloc(pai_b200_ctx_t *c, uint64_t bytes, void **out) {
+  if (!c || !out) return b200_fail(PAI_ERR_INVALID_ARG, "host_alloc: NULL");
+  return b200_cuda(cudaMallocHost(out, bytes ? bytes : 64), "cudaMallocHost");
+}
+
+extern "C" pai_status_t pai_b200_host_free(pai_b200_ctx_t *c, void *p) {
+  if (!c) return b200_fail(PAI_ERR_INVALID_ARG, "host_free: NULL ctx");
+  return p ? b200_cuda(cudaFreeHost(p), "cudaFreeHost") : PAI_OK;
+}
+
+static pai_status_t copy(pai_b200_ctx_t *c, void *dst, const void *src, uint64_t bytes,
+                         cudaMemcpyKind kind, const char *what) {
+  if (!c || ((!dst || !src) && bytes)) return b200_fail(PAI_ERR_INVALID_ARG, "%s: NULL", what);
+  if (!bytes) return PAI_OK;
+  return b200_cuda(cudaMemcpyAsync(dst, src, bytes, kind, c->stream), what);
+}
+
+extern "C" pai_status_t pai_b200_memcpy_h2d(pai_b200_ctx_t *c, void *d, const void *s, uint64_t n) {
+  return copy(c, d, s, n, cudaMemcpyHostToDevice, "memcpy_h2d");
+}
+extern "C" pai_status_t pai_b200_memcpy_d2h(pai_b200_ctx_t *c, void *d, const void *s, uint64_t n) {
+  return copy(c, d, s, n, cudaMemcpyDeviceToHost, "memcpy_d2h");
+}
+extern "C" pai_status_t pai_b200_memcpy_d2d(pai_b200_ctx_t *c, void *d, const void *s, uint64_t n) {
+  return copy(c, d, s, n, cudaMemcpyDeviceToDevice, "memcpy_d2d");
+}
+
+extern "C" pai_status_t pai_b200_memset(pai_b200_ctx_t *c, void *dst, int v, uint64_t n) {
+  if (!c || (!dst && n)) return b200_fail(PAI_ERR_INVALID_ARG, "memset: NULL");
+  return n ? b200_cuda(cudaMemsetAsync(dst, v, n, c->stream), "memset") : PAI_OK;
+}
+
+extern "C" pai_status_t pai_b200_sync(pai_b200_ctx_t *c) {
+  if (!c) return b200_fail(PAI_ERR_INVALID_ARG, "sync: NULL ctx");
+  pai_status_t st = b200_cuda(cudaStreamSynchronize(c->stream), "stream sync");
+  if (st) return st;
+  return b200_cuda(cudaGetLastError(), "kernel launch");
+}
+
+// ---- events -------------------------------------------------------------------------------
+
+extern "C" pai_status_t pai_b200_event_create(pai_b200_ctx_t *c, void **ev) {
+  if (!c || !ev) return b200_fail(PAI_ERR_INVALID_ARG, "event_create: NULL");
+  return b200_cuda(cudaEventCreate((cudaEvent_t *)ev), "cudaEventCreate");
+}
+extern "C" pai_status_t pai_b200_event_destroy(pai_b200_ctx_t *c, void *ev) {
+  (void)c;
+  return ev ? b200_cuda(cudaEventDestroy((cudaEvent_t)ev), "cudaEventDestroy") : PAI_OK;
+}
+extern "C" pai_status_t pai_b200_event_record(pai_b200_ctx_t *c, void *ev) {
+  if (!c || !ev) return b200_fail(PAI_ERR_INVALID_ARG, "event_record: NULL");
+  return b200_cuda(cudaEventRecord((cudaEvent_t)ev, c->stream), "cudaEventRecord");
+}
+extern "C" pai_status_t pai_b200_event_elapsed(void *a, void *b, float *ms) {
+  if (!a || !b || !ms) return b200_fail(PAI_ERR_INVALID_ARG, "event_elapsed: NULL");
+  pai_status_t st = b200_cuda(cudaEventSynchronize((cudaEvent_t)b), "cudaEventSynchronize");
+  if (st) return st;
+  return b200_cuda(cudaEventElapsedTime(ms, (cudaEvent_t)a, (cudaEvent_t)b), "cudaEventElapsedTime");
+}
+
+// ---- graphs -------------------------------------------------------------------------------
+
+static thread_local uint64_t g_capture_start;
+
+extern "C" pai_status_t b200_graph_begin(pai_b200_ctx_t *c) {
+  pai_status_t st = b200_cuda(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal),
+                              "cudaStreamBeginCapture");
+  if (st) return st;
+  c->capturing = 1;
+  g_capture_start = c->launches;
+  return PAI_OK;
+}
+
+extern "C" pai_status_t b200_graph_end(pai_b200_ctx_t *c, void **exec, uint32_t *kernels) {
+  cudaGraph_t g = nullptr;
+  c->capturing = 0;
+  pai_status_t st = b200_cuda(cudaStreamEndCapture(c->stream, &g), "cudaStreamEndCapture");
+  if (st) return st;
+  size_t nodes = 0;
+  cudaGraphGetNodes(g, nullptr, &nodes);
+  cudaGraphExec_t ge = nullptr;
+  st = b200_cuda(cudaGraphInstantiate(&ge, g, 0), "cudaGraphInstantiate");
+  cudaGraphDestroy(g);
+  if (st) return st;
+  *exec = ge;
+  // Count kernel nodes: every node this library captures is a kernel,
+  // except memset/memcpy nodes which the launchers never issue in steps.
+  *kernels = (uint32_t)nodes;
+  return PAI_OK;
+}
+
+extern "C" pai_status_t b200_graph_launch(pai_b200_ctx_t *c, void *exec, uint32_t kernels) {
+  pai_status_t st = b200_cuda(cudaGraphLaunch((cudaGraphExec_t)exec, c->stream), "cudaGraphLaunch");
+  if (!st) c->launches += kernels;
+  return st;
+}
+
+extern "C" void b200_graph_destroy(void *exec) {
+  if (exec) cudaGraphExecDestroy((cudaGraphExec_t)exec);
+}

@@ -1,0 +1,283 @@
+// GQA attention.
+//
+// Decode (one new query position over the fp16 KV cache) is split over
+// positions, flash-decoding style: CTA (kv head, chunk, sequence) scores
+// the chunk for all G = H/HK query heads that share the KV head (K rows
+// are read once for the G heads), takes the chunk's max and exp-sum,
+// and accumulates exp-weighted V rows; a second kernel merges the chunks
+// with the usual max-rescaling. Reference: the last-row iteration of
+// pai_ref_attention_f32 (cpu/reference/ref_ops.c:307-349) on the cache
+// contents: scores scaled by 1/sqrtf(hd) after the dot, softmax with the
+// max subtracted, then sum_i p_i v_i.
+//
+// Prefill (pai_b200_attention_f32) keeps the reference's loop structure
+// per (position, head) -- sequential dots, sequential max and sum, then
+// p_i = e_i/sum and a sequential weighted sum per dimension -- with
+// explicitly rounded operations, so only expf's last bit can differ.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "../b200_internal.h"
+#include "b200_device.cuh"
+
+namespace {
+
+constexpr int HD = 128;
+
+struct AttnParams {
+  const float *q;  // [B][H][HD]
+  const __half *kc, *vc;
+  float *opart;  // [B][H][nsplit][HD]
+  float *ml;     // [B][H][nsplit][2]
+  float *out;    // [B][H][HD]
+  const int32_t *pos;
+  uint32_t npos_host;
+  uint32_t h, hk, chunk, nsplit;
+  uint64_t cap, seq_stride;
+  float inv_scale;
+};
+
+__device__ __forceinline__ uint32_t npos_of(const AttnParams &p) {
+  return p.pos ? (uint32_t)(*p.pos) + 1u : p.npos_host;
+}
+
+template <int G>
+__global__ void __launch_bounds__(128) k_attn_split(AttnParams p) {
+  const uint32_t kvh = blockIdx.x, split = blockIdx.y, bi = blockIdx.z;
+  const uint32_t npos = npos_of(p);
+  const uint32_t start = split * p.chunk;
+  if (start >= npos) return;
+  const uint32_t len = min(p.chunk, npos - start);
+  extern __shared__ __align__(16) float sm[];
+  float *qs = sm;               // [G][HD]
+  float *sc = sm + G * HD;      // [G][chunk]
+  __shared__ float red[2][G][HD];
+  __shared__ float mls[G][2];
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const uint32_t h0 = kvh * G;
+  for (int i = t; i < G * HD; i += 128) qs[i] = p.q[((size_t)bi * p.h + h0) * HD + i];
+  __syncthreads();
+
+  float qr[G][4];
+#pragma unroll
+  for (int g = 0; g < G; g++)
+#pragma unroll
+    for (int e = 0; e < 4; e++) qr[g][e] = qs[g * HD + 4 * lane + e];
+
+  const size_t kvoff = (size_t)bi * p.seq_stride + ((size_t)kvh * p.cap + start) * HD;
+  const __half *kb = p.kc + kvoff;
+  const __half *vb = p.vc + kvoff;
+
+  // Scores: warp w takes positions w, w+4, ...; lane l holds dims 4l..4l+3.
+  for (uint32_t i = warp; i < len; i += 4) {
+    uint2 raw = *reinterpret_cast<const uint2 *>(kb + (size_t)i * HD + 4 * lane);
+    float2 k01 = __half22float2(*reinterpret_cast<__half2 *>(&raw.x));
+    float2 k23 = __half22float2(*reinterpret_cast<__half2 *>(&raw.y));
+    float part[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+      float s = qr[g][0] * k01.x;
+      s = fmaf(qr[g][1], k01.y, s);
+      s = fmaf(qr[g][2], k23.x, s);
+      s = fmaf(qr[g][3], k23.y, s);
+      part[g] = warp_sum(s);
+    }
+    if (lane == 0) {
+#pragma unroll
+      for (int g = 0; g < G; g++) sc[g * p.chunk + i] = part[g] * p.inv_scale;
+    }
+  }
+  __syncthreads();
+
+  // Chunk softmax statistics; warp w handles heads w, w+4, ...
+  for (int g = warp; g < G; g += 4) {
+    float *s = sc + g * p.chunk;
+    float m = -INFINITY;
+    for (uint32_t i = lane; i < len; i += 32) m = fmaxf(m, s[i]);
+    m = warp_max(m);
+    float l = 0.f;
+    for (uint32_t i = lane; i < len; i += 32) {
+      float e = expf(s[i] - m);
+      s[i] = e;
+      l += e;
+    }
+    l = warp_sum(l);
+    if (lane == 0) {
+      mls[g][0] = m;
+      mls[g][1] = l;
+    }
+  }
+  __syncthreads();
+
+  // Exp-weighted V: thread t covers dims 2*(t&63), +1 over every other position.
+  const int dp = t & 63, sub = t >> 6;
+  float acc[G][2];
+#pragma unroll
+  for (int g = 0; g < G; g++) acc[g][0] = acc[g][1] = 0.f;
+  for (uint32_t i = sub; i < len; i += 2) {
+    float2 v = __half22float2(*reinterpret_cast<const __half2 *>(vb + (size_t)i * HD + 2 * dp));
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+      float e = sc[g * p.chunk + i];
+      acc[g][0] = fmaf(e, v.x, acc[g][0]);
+      acc[g][1] = fmaf(e, v.y, acc[g][1]);
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < G; g++) {
+    red[sub][g][2 * dp] = acc[g][0];
+    red[sub][g][2 * dp + 1] = acc[g][1];
+  }
+  __syncthreads();
+  for (int i = t; i < G * HD; i += 128) {
+    int g = i / HD, d = i % HD;
+    size_t slot = ((size_t)bi * p.h + h0 + g) * p.nsplit + split;
+    p.opart[slot * HD + d] = red[0][g][d] + red[1][g][d];
+    if (d == 0) {
+      p.ml[slot * 2] = mls[g][0];
+      p.ml[slot * 2 + 1] = mls[g][1];
+    }
+  }
+}
+
+__global__ void __launch_bounds__(128) k_attn_combine(AttnParams p) {
+  const uint32_t h = blockIdx.x, bi = blockIdx.y, d = threadIdx.x;
+  const uint32_t npos = npos_of(p);
+  const uint32_t ns = (npos + p.chunk - 1) / p.chunk;
+  const size_t base = ((size_t)bi * p.h + h) * p.nsplit;
+  float M = -INFINITY;
+  for (uint32_t s = 0; s < ns; s++) M = fmaxf(M, p.ml[(base + s) * 2]);
+  float L = 0.f, o = 0.f;
+  for (uint32_t s = 0; s < ns; s++) {
+    float w = expf(p.ml[(base + s) * 2] - M);
+    L = fmaf(p.ml[(base + s) * 2 + 1], w, L);
+    o = fmaf(p.opart[(base + s) * HD + d], w, o);
+  }
+  p.out[((size_t)bi * p.h + h) * HD + d] = o / L;
+}
+
+// Prefill: one CTA per (position, head).
+__global__ void __launch_bounds__(128) k_attention_f32(uint32_t h, uint32_t hk, uint32_t hd,
+                                                       const float *__restrict__ q, const float *__restrict__ k,
+                                                       const float *__restrict__ v, float *__restrict__ out) {
+  extern __shared__ float sc[];  // [p+1]
+  const uint32_t pos = blockIdx.x, hh = blockIdx.y;
+  const uint32_t kvh = (hh * hk) / h;
+  const uint32_t np = pos + 1;
+  const float *qp = q + ((size_t)pos * h + hh) * hd;
+  const float inv_scale = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
+  for (uint32_t i = threadIdx.x; i < np; i += blockDim.x) {
+    const float *kp = k + ((size_t)i * hk + kvh) * hd;
+    float dot = 0.0f;
+    for (uint32_t d = 0; d < hd; d++) dot = __fadd_rn(dot, __fmul_rn(qp[d], kp[d]));
+    sc[i] = __fmul_rn(dot, inv_scale);
+  }
+  __syncthreads();
+  __shared__ float mx, sum;
+  if (threadIdx.x == 0) {
+    float m = sc[0];
+    for (uint32_t i = 1; i < np; i++) m = sc[i] > m ? sc[i] : m;
+    mx = m;
+  }
+  __syncthreads();
+  for (uint32_t i = threadIdx.x; i < np; i += blockDim.x) sc[i] = expf(__fsub_rn(sc[i], mx));
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float s = 0.0f;
+    for (uint32_t i = 0; i < np; i++) s = __fadd_rn(s, sc[i]);
+    sum = s;
+  }
+  __syncthreads();
+  for (uint32_t i = threadIdx.x; i < np; i += blockDim.x) sc[i] = __fdiv_rn(sc[i], sum);
+  __syncthreads();
+  for (uint32_t d = threadIdx.x; d < hd; d += blockDim.x) {
+    float acc = 0.0f;
+    for (uint32_t i = 0; i < np; i++) acc = __fadd_rn(acc, __fmul_rn(sc[i], v[((size_t)i * hk + kvh) * hd + d]));
+    out[((size_t)pos * h + hh) * hd + d] = acc;
+  }
+}
+
+template <int G>
+void launch_split(const AttnParams &p, uint32_t batch, cudaStream_t s) {
+  size_t smem = (size_t)(G * HD + G * p.chunk) * sizeof(float);
+  if (smem > 48 * 1024) cudaFuncSetAttribute(k_attn_split<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  k_attn_split<G><<<dim3(p.hk, p.nsplit, batch), 128, smem, s>>>(p);
+}
+
+}  // namespace
+
+extern "C" pai_status_t b200_launch_attn_decode(pai_b200_ctx_t *ctx, uint32_t batch, uint32_t h, uint32_t hk,
+                                                uint32_t hd, const int32_t *pos, uint64_t npos_host,
+                                                uint64_t max_npos, uint64_t cap, uint64_t seq_stride,
+                                                const float *q, const uint16_t *kc, const uint16_t *vc,
+                                                float *out) {
+  if (hd != HD) return b200_fail(PAI_ERR_UNSUPPORTED, "attn_decode: head_dim %u (this kernel takes 128)", hd);
+  if (hk == 0 || h % hk) return b200_fail(PAI_ERR_INVALID_ARG, "attn_decode: heads %u / kv heads %u", h, hk);
+  uint32_t G = h / hk;
+  if (G != 1 && G != 2 && G != 4 && G != 8)
+    return b200_fail(PAI_ERR_UNSUPPORTED, "attn_decode: %u query heads per kv head", G);
+  if (max_npos == 0 || max_npos > cap) return b200_fail(PAI_ERR_INVALID_ARG, "attn_decode: positions > cache");
+  // Chunk so that about two CTAs per SM are busy at the longest context.
+  uint64_t want = (max_npos * hk * batch + 295) / 296;
+  uint32_t chunk = (uint32_t)(((want + 31) / 32) * 32);
+  if (chunk < 32) chunk = 32;
+  if (chunk > 4096) chunk = 4096;
+  uint32_t nsplit = (uint32_t)((max_npos + chunk - 1) / chunk);
+  AttnParams p{};
+  p.q = q;
+  p.kc = (const __half *)kc;
+  p.vc = (const __half *)vc;
+  p.out = out;
+  p.pos = pos;
+  p.npos_host = (uint32_t)npos_host;
+  p.h = h;
+  p.hk = hk;
+  p.chunk = chunk;
+  p.nsplit = nsplit;
+  p.cap = cap;
+  p.seq_stride = seq_stride;
+  p.inv_scale = 1.0f / sqrtf((float)hd);
+  uint64_t slots = (uint64_t)batch * h * nsplit;
+  float *scratch;
+  uint32_t *counters;
+  pai_status_t st = b200_ctx_scratch(ctx, slots * (HD + 2), 0, &scratch, &counters);
+  if (st) return st;
+  p.opart = scratch;
+  p.ml = scratch + slots * HD;
+  cudaStream_t s = (cudaStream_t)b200_ctx_stream(ctx);
+  switch (G) {
+    case 1: launch_split<1>(p, batch, s); break;
+    case 2: launch_split<2>(p, batch, s); break;
+    case 4: launch_split<4>(p, batch, s); break;
+    default: launch_split<8>(p, batch, s); break;
+  }
+  k_attn_combine<<<dim3(h, batch), HD, 0, s>>>(p);
+  b200_ctx_count_launch(ctx, 2);
+  return b200_cuda(cudaGetLastError(), "k_attn_decode");
+}
+
+extern "C" pai_status_t pai_b200_attn_decode_f16kv(pai_b200_ctx_t *ctx, uint64_t h, uint64_t hk, uint64_t hd,
+                                                   uint64_t npos, uint64_t cap, const float *q,
+                                                   const uint16_t *kcache, const uint16_t *vcache, float *out) {
+  if (!ctx || !q || !kcache || !vcache || !out) return b200_fail(PAI_ERR_INVALID_ARG, "attn_decode: NULL");
+  if (h == 0 || hk == 0 || npos == 0 || npos > cap || h > 4096 || cap > 0x7FFFFFFFull)
+    return b200_fail(PAI_ERR_INVALID_ARG, "attn_decode: shape");
+  return b200_launch_attn_decode(ctx, 1, (uint32_t)h, (uint32_t)hk, (uint32_t)hd, nullptr, npos, npos, cap, 0,
+                                 q, kcache, vcache, out);
+}
+
+extern "C" pai_status_t pai_b200_attention_f32(pai_b200_ctx_t *ctx, uint64_t h, uint64_t hk, uint64_t seq,
+                                               uint64_t hd, const float *q, const float *k, const float *v,
+                                               float *out) {
+  // Argument rules of pai_ref_attention_f32 (ref_ops.c:298-301).
+  if (!ctx || h == 0 || hk == 0 || seq == 0 || hd == 0 || h % hk != 0 || !q || !k || !v || !out)
+    return b200_fail(PAI_ERR_INVALID_ARG, "attention: invalid arguments");
+  size_t smem = seq * sizeof(float);
+  if (smem > 200 * 1024 || h > 65535 || seq > 0x7FFFFFFFull)
+    return b200_fail(PAI_ERR_UNSUPPORTED, "attention: seq %llu beyond the prefill kernel", (unsigned long long)seq);
+  if (smem > 48 * 1024) cudaFuncSetAttribute(k_attention_f32, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  k_attention_f32<<<dim3((unsigned)seq, (unsigned)h), 128, smem, (cudaStream_t)b200_ctx_stream(ctx)>>>(
+      (uint32_t)h, (uint32_t)hk, (uint32_t)hd, q, k, v, out);
+  b200_ctx_count_launch(ctx, 1);
+  return b200_cuda(cudaGetLastError(), "k_attention_f32");
+}

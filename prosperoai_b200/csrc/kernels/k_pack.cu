@@ -1,0 +1,263 @@
+// Weight-format kernels: packing ggml blocks into the GEMV layout,
+// bit-exact device dequantisation, the device block quantiser and the
+// seeded synthetic-weight generator. All of these run once per model
+// load; the per-token path only reads the packed layout.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "../b200_internal.h"
+#include "b200_device.cuh"
+
+namespace {
+
+__global__ void k_pack(uint32_t type, uint64_t n, uint64_t npad, uint32_t nb,
+                       const uint8_t *__restrict__ src, const uint64_t *__restrict__ row_off,
+                       uint8_t *__restrict__ qs, uint8_t *__restrict__ sc) {
+  uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  uint64_t r = idx / nb;
+  uint32_t b = (uint32_t)(idx % nb);
+  if (r >= npad) return;
+  const uint32_t bb = b200_blk_bytes(type), chunks = b200_chunks(type), hdr = b200_hdr_bytes(type);
+  const uint32_t qoff = type == PAI_B200_Q4_K ? 16u : 2u;
+  uint64_t off = r < n ? row_off[r] : ~0ull;
+  if (off == ~0ull - 1ull) return;  // row owned by another source tensor
+  const uint8_t *s = off == ~0ull ? nullptr : src + off + (uint64_t)b * bb;
+  uint64_t g = r / B200_RG, lr = r % B200_RG;
+  uint64_t tile = g * nb + b;
+  uint8_t *h = sc + (tile * B200_RG + lr) * hdr;
+  for (uint32_t i = 0; i < hdr; i++) h[i] = s ? s[i] : 0;
+  for (uint32_t c = 0; c < chunks; c++) {
+    uint8_t *d = qs + ((tile * chunks + c) * B200_RG + lr) * 16u;
+    for (uint32_t i = 0; i < 16; i++) d[i] = s ? s[qoff + 16u * c + i] : 0;
+  }
+}
+
+// Bit-exact dequantisation (adapters/llama/gguf.c:680-693, 750-761,
+// 852-882). Products of an fp16 scale and a small integer are exact in
+// fp32; the Q4_K form keeps gguf.c's rounding steps (d*sc, dmin*m, then
+// (d*sc)*q - dmin*m) with explicitly rounded operations.
+__global__ void k_dequant(uint32_t type, uint64_t n, uint32_t nb, const uint8_t *__restrict__ qs,
+                          const uint8_t *__restrict__ sc, float *__restrict__ out) {
+  uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  uint64_t r = idx / nb;
+  uint32_t b = (uint32_t)(idx % nb);
+  if (r >= n) return;
+  const uint32_t chunks = b200_chunks(type), hdr = b200_hdr_bytes(type);
+  const uint32_t el = b200_blk_elems(type);
+  uint64_t g = r / B200_RG, lr = r % B200_RG;
+  uint64_t tile = g * nb + b;
+  const uint8_t *h = sc + (tile * B200_RG + lr) * hdr;
+  float *o = out + r * (uint64_t)nb * el + (uint64_t)b * el;
+  auto q = [&](uint32_t byte) -> uint8_t {
+    return qs[((tile * chunks + byte / 16u) * B200_RG + lr) * 16u + byte % 16u];
+  };
+  float d = f16_bits_to_f32((uint16_t)(h[0] | (h[1] << 8)));
+  if (type == PAI_B200_Q4_0) {
+    for (int j = 0; j < 16; j++) {
+      uint8_t v = q(j);
+      o[j] = __fmul_rn((float)((int)(v & 15) - 8), d);
+      o[j + 16] = __fmul_rn((float)((int)(v >> 4) - 8), d);
+    }
+  } else if (type == PAI_B200_Q8_0) {
+    for (int j = 0; j < 32; j++) o[j] = __fmul_rn((float)(int8_t)q(j), d);
+  } else {
+    float dmin = f16_bits_to_f32((uint16_t)(h[2] | (h[3] << 8)));
+    const uint8_t *s12 = h + 4;
+    for (int c = 0; c < 4; c++) {
+      uint8_t s0, m0, s1, m1;
+      k4_scale_min(2 * c, s12, &s0, &m0);
+      k4_scale_min(2 * c + 1, s12, &s1, &m1);
+      float d1 = __fmul_rn(d, (float)s0), mm1 = __fmul_rn(dmin, (float)m0);
+      float d2 = __fmul_rn(d, (float)s1), mm2 = __fmul_rn(dmin, (float)m1);
+      for (int l = 0; l < 32; l++) {
+        uint8_t v = q(32 * c + l);
+        o[64 * c + l] = __fsub_rn(__fmul_rn(d1, (float)(v & 15)), mm1);
+        o[64 * c + 32 + l] = __fsub_rn(__fmul_rn(d2, (float)(v >> 4)), mm2);
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ int clampi(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); }
+
+__device__ __forceinline__ void put_f16(uint8_t *p, float f) {
+  uint16_t h = __half_as_ushort(__float2half_rn(f));
+  p[0] = (uint8_t)(h & 0xFF);
+  p[1] = (uint8_t)(h >> 8);
+}
+
+// Device block quantiser: the same formulas and rounding steps as the
+// host quantiser (csrc/host/b200_quant.c), with IEEE division and
+// round-half-even conversion (lrintf) so both produce identical bytes.
+__global__ void k_quantize(uint32_t type, uint64_t nblocks, const float *__restrict__ src,
+                           uint8_t *__restrict__ dst) {
+  uint64_t b = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= nblocks) return;
+  if (type == PAI_B200_Q8_0) {
+    const float *s = src + b * 32;
+    uint8_t *o = dst + b * 34;
+    float amax = 0.0f;
+    for (int j = 0; j < 32; j++) amax = fmaxf(amax, fabsf(s[j]));
+    float d = __fdiv_rn(amax, 127.0f);
+    put_f16(o, d);
+    for (int j = 0; j < 32; j++) {
+      int q = d > 0.0f ? clampi(__float2int_rn(__fdiv_rn(s[j], d)), -127, 127) : 0;
+      o[2 + j] = (uint8_t)(int8_t)q;
+    }
+  } else if (type == PAI_B200_Q4_0) {
+    const float *s = src + b * 32;
+    uint8_t *o = dst + b * 18;
+    float amax = 0.0f, m = 0.0f;
+    for (int j = 0; j < 32; j++) {
+      float a = fabsf(s[j]);
+      if (a > amax) {
+        amax = a;
+        m = s[j];
+      }
+    }
+    float d = __fdiv_rn(m, -8.0f);
+    put_f16(o, d);
+    int q[32];
+    for (int j = 0; j < 32; j++) q[j] = d != 0.0f ? clampi(__float2int_rn(__fdiv_rn(s[j], d)) + 8, 0, 15) : 8;
+    for (int j = 0; j < 16; j++) o[2 + j] = (uint8_t)(q[j] | (q[j + 16] << 4));
+  } else {
+    const float *s = src + b * 256;
+    uint8_t *o = dst + b * 144;
+    float S[8], M[8], maxS = 0.0f, maxM = 0.0f;
+    for (int t = 0; t < 8; t++) {
+      float lo = 0.0f, hi = 0.0f;
+      for (int l = 0; l < 32; l++) {
+        float v = s[32 * t + l];
+        lo = v < lo ? v : lo;
+        hi = v > hi ? v : hi;
+      }
+      S[t] = __fdiv_rn(__fsub_rn(hi, lo), 15.0f);
+      M[t] = -lo;
+      maxS = S[t] > maxS ? S[t] : maxS;
+      maxM = M[t] > maxM ? M[t] : maxM;
+    }
+    __half d16 = __float2half_rn(__fdiv_rn(maxS, 63.0f));
+    __half dm16 = __float2half_rn(__fdiv_rn(maxM, 63.0f));
+    float df = __half2float(d16), dmf = __half2float(dm16);
+    uint16_t db = __half_as_ushort(d16), dmb = __half_as_ushort(dm16);
+    o[0] = db & 0xFF; o[1] = db >> 8; o[2] = dmb & 0xFF; o[3] = dmb >> 8;
+    int sc[8], mn[8];
+    for (int t = 0; t < 8; t++) {
+      sc[t] = df > 0.0f ? clampi(__float2int_rn(__fdiv_rn(S[t], df)), 0, 63) : 0;
+      mn[t] = dmf > 0.0f ? clampi(__float2int_rn(__fdiv_rn(M[t], dmf)), 0, 63) : 0;
+    }
+    for (int j = 0; j < 4; j++) {
+      o[4 + j] = (uint8_t)((sc[j] & 63) | ((sc[j + 4] >> 4) << 6));
+      o[8 + j] = (uint8_t)((mn[j] & 63) | ((mn[j + 4] >> 4) << 6));
+      o[12 + j] = (uint8_t)((sc[j + 4] & 15) | ((mn[j + 4] & 15) << 4));
+    }
+    for (int c = 0; c < 4; c++) {
+      int t0 = 2 * c, t1 = 2 * c + 1;
+      float sc0 = __fmul_rn(df, (float)sc[t0]), of0 = __fmul_rn(dmf, (float)mn[t0]);
+      float sc1 = __fmul_rn(df, (float)sc[t1]), of1 = __fmul_rn(dmf, (float)mn[t1]);
+      for (int l = 0; l < 32; l++) {
+        float v0 = s[64 * c + l], v1 = s[64 * c + 32 + l];
+        int q0 = sc0 > 0.0f ? clampi(__float2int_rn(__fdiv_rn(__fadd_rn(v0, of0), sc0)), 0, 15) : 0;
+        int q1 = sc1 > 0.0f ? clampi(__float2int_rn(__fdiv_rn(__fadd_rn(v1, of1), sc1)), 0, 15) : 0;
+        o[16 + 32 * c + l] = (uint8_t)(q0 | (q1 << 4));
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+// Seeded N(0, std) rows: row r is the splitmix64 stream started at
+// mix64(seed + r); pair j draws outputs 2j and 2j+1 of that stream and
+// turns them into two normals by Box-Muller in double precision.
+__global__ void k_synth_normal(float *__restrict__ dst, uint64_t rows, uint64_t cols, uint64_t seed,
+                               double stddev) {
+  const uint64_t pairs = (cols + 1) / 2;
+  uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= rows * pairs) return;
+  uint64_t r = idx / pairs, j = idx % pairs;
+  const uint64_t gamma = 0x9E3779B97F4A7C15ull;
+  uint64_t st = mix64(seed + r);
+  uint64_t x1 = mix64(st + (2 * j + 1) * gamma);
+  uint64_t x2 = mix64(st + (2 * j + 2) * gamma);
+  double u1 = __dmul_rn((double)((x1 >> 11) + 1), 0x1.0p-53);
+  double u2 = __dmul_rn((double)(x2 >> 11), 0x1.0p-53);
+  double rad = sqrt(__dmul_rn(-2.0, log(u1)));
+  double t = __dmul_rn(6.283185307179586, u2);
+  double sr = __dmul_rn(stddev, rad);
+  float *o = dst + r * cols + 2 * j;
+  o[0] = (float)__dmul_rn(sr, cos(t));
+  if (2 * j + 1 < cols) o[1] = (float)__dmul_rn(sr, sin(t));
+}
+
+__global__ void k_fill(float *dst, uint64_t n, float v) {
+  uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) dst[i] = v;
+}
+
+inline unsigned nblk(uint64_t work, unsigned t) { return (unsigned)((work + t - 1) / t); }
+
+}  // namespace
+
+extern "C" uint64_t pai_b200_packed_bytes(uint32_t type, uint64_t n, uint64_t k) {
+  if (!b200_type_ok(type) || n == 0 || k == 0 || k % b200_blk_elems(type)) return 0;
+  uint64_t nb = k / b200_blk_elems(type);
+  return b200_sc_offset(type, n, k) + b200_align256(b200_ngroups(n) * nb * B200_RG * b200_hdr_bytes(type));
+}
+
+extern "C" pai_status_t pai_b200_pack(pai_b200_ctx_t *ctx, uint32_t type, uint64_t n, uint64_t k,
+                                      const void *src, const uint64_t *row_off, void *dst) {
+  if (!ctx || !src || !row_off || !dst) return b200_fail(PAI_ERR_INVALID_ARG, "pack: NULL");
+  if (!b200_type_ok(type)) return b200_fail(PAI_ERR_UNSUPPORTED, "pack: block type %u", type);
+  if (n == 0 || k == 0 || k % b200_blk_elems(type))
+    return b200_fail(PAI_ERR_MISMATCH, "pack: k=%llu not a multiple of %u", (unsigned long long)k,
+                     b200_blk_elems(type));
+  uint32_t nb = (uint32_t)(k / b200_blk_elems(type));
+  uint64_t npad = b200_ngroups(n) * B200_RG;
+  uint8_t *qs = (uint8_t *)dst;
+  uint8_t *sc = qs + b200_sc_offset(type, n, k);
+  cudaStream_t s = (cudaStream_t)b200_ctx_stream(ctx);
+  k_pack<<<nblk(npad * nb, 256), 256, 0, s>>>(type, n, npad, nb, (const uint8_t *)src, row_off, qs, sc);
+  b200_ctx_count_launch(ctx, 1);
+  return b200_cuda(cudaGetLastError(), "k_pack");
+}
+
+extern "C" pai_status_t pai_b200_dequant(pai_b200_ctx_t *ctx, uint32_t type, uint64_t n, uint64_t k,
+                                         const void *packed, float *out) {
+  if (!ctx || !packed || !out) return b200_fail(PAI_ERR_INVALID_ARG, "dequant: NULL");
+  if (!b200_type_ok(type)) return b200_fail(PAI_ERR_UNSUPPORTED, "dequant: block type %u", type);
+  if (n == 0 || k == 0 || k % b200_blk_elems(type)) return b200_fail(PAI_ERR_MISMATCH, "dequant: shape");
+  uint32_t nb = (uint32_t)(k / b200_blk_elems(type));
+  const uint8_t *qs = (const uint8_t *)packed;
+  const uint8_t *sc = qs + b200_sc_offset(type, n, k);
+  k_dequant<<<nblk(n * nb, 128), 128, 0, (cudaStream_t)b200_ctx_stream(ctx)>>>(type, n, nb, qs, sc, out);
+  b200_ctx_count_launch(ctx, 1);
+  return b200_cuda(cudaGetLastError(), "k_dequant");
+}
+
+extern "C" pai_status_t b200_launch_quantize(pai_b200_ctx_t *ctx, uint32_t type, const float *src,
+                                             uint64_t numel, void *dst) {
+  uint64_t nb = numel / b200_blk_elems(type);
+  k_quantize<<<nblk(nb, 128), 128, 0, (cudaStream_t)b200_ctx_stream(ctx)>>>(type, nb, src, (uint8_t *)dst);
+  b200_ctx_count_launch(ctx, 1);
+  return b200_cuda(cudaGetLastError(), "k_quantize");
+}
+
+extern "C" pai_status_t b200_launch_synth_normal(pai_b200_ctx_t *ctx, float *dst, uint64_t rows,
+                                                 uint64_t cols, uint64_t seed, float stddev) {
+  uint64_t work = rows * ((cols + 1) / 2);
+  k_synth_normal<<<nblk(work, 256), 256, 0, (cudaStream_t)b200_ctx_stream(ctx)>>>(dst, rows, cols, seed,
+                                                                                     (double)stddev);
+  b200_ctx_count_launch(ctx, 1);
+  return b200_cuda(cudaGetLastError(), "k_synth_normal");
+}
+
+extern "C" pai_status_t b200_launch_fill(pai_b200_ctx_t *ctx, float *dst, uint64_t n, float v) {
+  k_fill<<<nblk(n, 256), 256, 0, (cudaStream_t)b200_ctx_stream(ctx)>>>(dst, n, v);
+  b200_ctx_count_launch(ctx, 1);
+  return b200_cuda(cudaGetLastError(), "k_fill");
+}

@@ -1,0 +1,131 @@
+"""Host-side checks of libpai_b200.so that need no GPU.
+
+The library must load and export every function include/pai_b200.h
+declares; the host quantiser must produce the same ggml bytes as the CPU
+restatement of the quantisation formulas; the op descriptors must be
+layout-compatible with the reference's pai_op_descriptor_t.
+"""
+import ctypes as C
+import os
+import re
+import subprocess
+
+import numpy as np
+import pytest
+
+from oracle import py_oracle as po
+from prosperoai_b200 import _native
+from prosperoai_b200.api import quantize, rope_tables
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "pai_b200.h")
+REF = "/root/reference"
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(pai_b200_\w+)\s*\(", text)))
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    L = _native.load()
+    missing = [n for n in declared_functions() if not hasattr(L, n)]
+    assert not missing, missing
+    assert set(declared_functions()) <= set(_native.SIGNATURES), "ctypes signature table incomplete"
+    assert b"sm_100a" in L.pai_b200_version()
+
+
+def test_host_quantiser_matches_restated_formulas():
+    rng = np.random.default_rng(11)
+    for t in (po.Q4_0, po.Q8_0, po.Q4_K):
+        el = po.BLOCK[t][0]
+        w = (rng.standard_normal(el * 300) * 0.02).astype(np.float32)
+        w[:el] = 0.0                    # an all-zero block
+        w[el:2 * el] = np.abs(w[el:2 * el])  # all-positive block
+        w[2 * el:3 * el] = -np.abs(w[2 * el:3 * el])
+        assert np.array_equal(quantize(t, w), po.quantize(t, w)), t
+
+
+# Q8_0: half a step plus the fp16 rounding of d (127 * 2^-11 steps);
+# Q4_0: the extreme of the opposite sign clamps at +7, up to one step.
+@pytest.mark.parametrize("t,step", [(po.Q8_0, 0.6 / 127), (po.Q4_0, 1.01 / 8), (po.Q4_K, 1.0)])
+def test_quantise_round_trip_error_bound(t, step):
+    rng = np.random.default_rng(3)
+    el = po.BLOCK[t][0]
+    w = (rng.standard_normal(el * 200) * 0.02).astype(np.float32)
+    back = po.dequant(t, quantize(t, w), w.size)
+    err = np.abs(back - w).reshape(-1, el)
+    amax = np.abs(w).reshape(-1, el).max(axis=1)
+    if t == po.Q4_K:
+        bound = (w.reshape(-1, 32).max(1) - np.minimum(0, w.reshape(-1, 32).min(1)))
+        assert (np.abs(back - w).reshape(-1, 32).max(1) <= bound / 15 * 1.3 + 1e-6).all()
+    else:
+        assert (err.max(axis=1) <= amax * step + 1e-7).all()
+
+
+def test_quantise_rejects_ragged_input():
+    with pytest.raises(_native.PaiError) as e:
+        quantize(po.Q4_0, np.zeros(33, np.float32))
+    assert e.value.status == -6  # PAI_ERR_MISMATCH
+
+
+def test_rope_tables_match_reference_formula():
+    c1, s1 = rope_tables(100, 64, 500000.0)
+    c2, s2 = po.rope_tables(100, 64, 500000.0)
+    assert np.array_equal(c1, c2) and np.array_equal(s1, s2)
+
+
+def test_registry_registration():
+    reg = _native.OpRegistry()
+    reg.version, reg.count = 1, 28  # a registry already holding the 28 builtin ops
+    L = _native.load()
+    _native.check(L.pai_b200_register_ops(C.byref(reg)), "register_ops")
+    n = L.pai_b200_op_count()
+    assert reg.count == 28 + n
+    names = {reg.ops[28 + i].contents.name.decode() for i in range(n)}
+    assert {"gemv_q4_0_f32", "gemv_q8_0_f32", "gemv_q4_k_f32", "attention_decode_f16kv"} <= names
+    for i in range(n):
+        d = reg.ops[28 + i].contents
+        assert d.caps == 1 << 3 and 14 <= d.kernel_id <= 25
+    full = _native.OpRegistry()
+    full.count = 60
+    assert L.pai_b200_register_ops(C.byref(full)) == -2  # PAI_ERR_NOMEM: 64-op cap
+
+
+def test_init_without_gpu_reports_error():
+    L = _native.load()
+    n = C.c_int(-1)
+    assert L.pai_b200_device_count(C.byref(n)) == 0
+    if n.value > 0:
+        pytest.skip("a GPU is present")
+    ctx = C.c_void_p()
+    assert L.pai_b200_init(0, C.byref(ctx)) == -8  # PAI_ERR_INIT
+    assert b"no CUDA device" in L.pai_b200_last_error()
+
+
+@pytest.mark.skipif(not os.path.exists(f"{REF}/sdk/include/pai/op.h"),
+                    reason="reference headers not present")
+def test_descriptor_layout_matches_reference(tmp_path):
+    """Compile the reference's pai/op.h and this header separately and
+    compare sizes and field offsets."""
+    probe = r"""
+#include <stdio.h>
+#include <stddef.h>
+#include HDR
+int main(void) {
+  printf("%zu %zu %zu %zu %zu %zu %zu\n", sizeof(pai_op_descriptor_t),
+         offsetof(pai_op_descriptor_t, caps), offsetof(pai_op_descriptor_t, ref_fn),
+         offsetof(pai_op_descriptor_t, kernel_id), offsetof(pai_op_descriptor_t, reserved),
+         sizeof(pai_op_registry_t), offsetof(pai_op_registry_t, ops));
+  return 0;
+}
+"""
+    src = tmp_path / "probe.c"
+    src.write_text(probe)
+    outs = []
+    for hdr, inc in (("<pai/op.h>", f"-I{REF}/sdk/include"), ('"pai_b200.h"', f"-I{ROOT}/include")):
+        exe = tmp_path / f"probe{len(outs)}"
+        subprocess.run(["gcc", "-std=c11", inc, f"-DHDR={hdr}", str(src), "-o", str(exe)], check=True)
+        outs.append(subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout)
+    assert outs[0] == outs[1], outs
