@@ -210,10 +210,11 @@ def gpu_arm(args):
     B, K, W = args.batch, args.steps, args.warmup
     model = Model(dev, cfg)
     model.synthesize(SEED)
-    max_ctx = PROMPT + W + 2 * K + 8
+    P = args.prompt
+    max_ctx = P + W + 2 * K + 8
     sess = Session(model, B, max_ctx)
-    prompts = np.random.default_rng(SEED).integers(0, cfg["vocab"], (B, PROMPT)).astype(np.int32)
-    for p in range(PROMPT):  # prompt positions, untimed
+    prompts = np.random.default_rng(SEED).integers(0, cfg["vocab"], (B, P)).astype(np.int32)
+    for p in range(P):  # prompt positions, untimed
         sess.set_tokens(prompts[:, p])
         sess.run(1)
     sess.run(W)  # warm-up greedy steps
@@ -260,7 +261,7 @@ def gpu_arm(args):
     step_gbs = step_bytes / (t_dev / K * 1e-3) / 1e9
     result = None
     if rank == 0:
-        roof = gemv_roofline(dev, hbm, kind)
+        roof = None if args.no_roofline else gemv_roofline(dev, hbm, kind)
         cpu = None if args.no_cpu_baseline else cpu_baseline_port(dev)
         value = world * B * K / (t_dev * 1e-3)
         result = {
@@ -269,7 +270,7 @@ def gpu_arm(args):
             "scaling": "weak", "vs_baseline": None, "dtype": "q4_0 weights, f32 accumulate",
             "data": "synthetic (seeded N(0,0.02) weights, seeded prompt ids)",
             "config": {"workload": "Llama-3-8B-shaped Q4_0 decode (config 5)", "batch": B,
-                       "prompt": PROMPT, "positions_timed": [pos0, pos0 + K - 1],
+                       "prompt": P, "positions_timed": [pos0, pos0 + K - 1],
                        "layers": cfg["n_layer"], "hidden": cfg["n_embd"], "vocab": cfg["vocab"],
                        "kv_cache": "fp16",
                        "parallelism": "single GPU" if world == 1 else f"{world} independent replicas",
@@ -417,6 +418,10 @@ def main():
     ap.add_argument("--batch", type=int, default=1, choices=[1, 2, 4, 8])
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-roofline", action="store_true",
+                    help="skip the standalone GEMV timing (profiling runs)")
+    ap.add_argument("--prompt", type=int, default=PROMPT,
+                    help="prompt length fed before timing (profiling runs use a short one)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

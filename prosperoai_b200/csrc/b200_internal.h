@@ -66,6 +66,11 @@ pai_status_t b200_cuda(int err, const char *what);
 void *b200_ctx_stream(pai_b200_ctx_t *ctx);
 int b200_ctx_device(pai_b200_ctx_t *ctx);
 void b200_ctx_count_launch(pai_b200_ctx_t *ctx, uint32_t kernels);
+/* Count `kernels` launches and report a launch error under `name`. With
+ * PAI_B200_SYNC_CHECK=1 in the environment (and outside graph capture)
+ * it also waits for the kernels and reports their execution errors,
+ * which localises a failing kernel. */
+pai_status_t b200_launched(pai_b200_ctx_t *ctx, uint32_t kernels, const char *name);
 /* Per-context split-K scratch: float partial sums and zeroed counters
  * (each kernel that uses the counters leaves them at zero). */
 pai_status_t b200_ctx_scratch(pai_b200_ctx_t *ctx, uint64_t partial_floats,

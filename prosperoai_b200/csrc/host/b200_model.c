@@ -487,7 +487,7 @@ pai_status_t pai_b200_session_create(pai_b200_model_t *m, uint32_t batch, uint32
   SALLOC(s->logits, (uint64_t)batch * m->vl * 4);
   SALLOC(s->cos_t, (uint64_t)max_ctx * c->head_dim / 2 * 4);
   SALLOC(s->sin_t, (uint64_t)max_ctx * c->head_dim / 2 * 4);
-  SALLOC(s->kc, kv);
+  SALLOC(s->kc, kv * 2); /* kv counts fp16 elements (K and V) */
   if (!st) s->vc = s->kc + s->layer_stride * c->n_layer;
   if (!st) st = pai_b200_host_alloc(ctx, 64, (void **)&s->htok);
   if (!st) st = pai_b200_memset(ctx, s->kc, 0, kv * 2);

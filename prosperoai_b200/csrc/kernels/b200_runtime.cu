@@ -7,6 +7,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 
@@ -109,6 +110,24 @@ extern "C" void b200_ctx_count_launch(pai_b200_ctx_t *c, uint32_t k) {
 }
 extern "C" uint64_t pai_b200_launch_count(pai_b200_ctx_t *c) { return c ? c->launches : 0; }
 
+static int sync_check_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char *e = getenv("PAI_B200_SYNC_CHECK");
+    v = (e && e[0] == '1') ? 1 : 0;
+  }
+  return v;
+}
+
+extern "C" pai_status_t b200_launched(pai_b200_ctx_t *c, uint32_t k, const char *name) {
+  b200_ctx_count_launch(c, k);
+  pai_status_t st = b200_cuda(cudaGetLastError(), name);
+  if (st || c->capturing || !sync_check_enabled()) return st;
+  st = b200_cuda(cudaStreamSynchronize(c->stream), name);
+  if (st) return st;
+  return b200_cuda(cudaGetLastError(), name);
+}
+
 extern "C" pai_status_t b200_ctx_scratch(pai_b200_ctx_t *c, uint64_t partial_floats,
                                          uint32_t counters, float **partial,
                                          uint32_t **counter) {
@@ -201,9 +220,14 @@ extern "C" pai_status_t pai_b200_memset(pai_b200_ctx_t *c, void *dst, int v, uin
 
 extern "C" pai_status_t pai_b200_sync(pai_b200_ctx_t *c) {
   if (!c) return b200_fail(PAI_ERR_INVALID_ARG, "sync: NULL ctx");
-  pai_status_t st = b200_cuda(cudaStreamSynchronize(c->stream), "stream sync");
+  pai_status_t st = b200_cuda(cudaPeekAtLastError(), "earlier unchecked CUDA call");
+  if (st) {
+    cudaGetLastError();
+    return st;
+  }
+  st = b200_cuda(cudaStreamSynchronize(c->stream), "stream sync");
   if (st) return st;
-  return b200_cuda(cudaGetLastError(), "kernel launch");
+  return b200_cuda(cudaGetLastError(), "kernel execution");
 }
 
 // ---- events -------------------------------------------------------------------------------

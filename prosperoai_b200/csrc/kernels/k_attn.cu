@@ -198,10 +198,16 @@ __global__ void __launch_bounds__(128) k_attention_f32(uint32_t h, uint32_t hk, 
 }
 
 template <int G>
-void launch_split(const AttnParams &p, uint32_t batch, cudaStream_t s) {
+pai_status_t launch_split(const AttnParams &p, uint32_t batch, cudaStream_t s) {
   size_t smem = (size_t)(G * HD + G * p.chunk) * sizeof(float);
-  if (smem > 48 * 1024) cudaFuncSetAttribute(k_attn_split<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (smem > 48 * 1024) {
+    pai_status_t st = b200_cuda(
+        cudaFuncSetAttribute(k_attn_split<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+        "k_attn_split smem attribute");
+    if (st) return st;
+  }
   k_attn_split<G><<<dim3(p.hk, p.nsplit, batch), 128, smem, s>>>(p);
+  return PAI_OK;
 }
 
 }  // namespace
@@ -246,14 +252,14 @@ extern "C" pai_status_t b200_launch_attn_decode(pai_b200_ctx_t *ctx, uint32_t ba
   p.ml = scratch + slots * HD;
   cudaStream_t s = (cudaStream_t)b200_ctx_stream(ctx);
   switch (G) {
-    case 1: launch_split<1>(p, batch, s); break;
-    case 2: launch_split<2>(p, batch, s); break;
-    case 4: launch_split<4>(p, batch, s); break;
-    default: launch_split<8>(p, batch, s); break;
+    case 1: st = launch_split<1>(p, batch, s); break;
+    case 2: st = launch_split<2>(p, batch, s); break;
+    case 4: st = launch_split<4>(p, batch, s); break;
+    default: st = launch_split<8>(p, batch, s); break;
   }
+  if (st) return st;
   k_attn_combine<<<dim3(h, batch), HD, 0, s>>>(p);
-  b200_ctx_count_launch(ctx, 2);
-  return b200_cuda(cudaGetLastError(), "k_attn_decode");
+  return b200_launched(ctx, 2, "k_attn_decode");
 }
 
 extern "C" pai_status_t pai_b200_attn_decode_f16kv(pai_b200_ctx_t *ctx, uint64_t h, uint64_t hk, uint64_t hd,
@@ -275,9 +281,13 @@ extern "C" pai_status_t pai_b200_attention_f32(pai_b200_ctx_t *ctx, uint64_t h, 
   size_t smem = seq * sizeof(float);
   if (smem > 200 * 1024 || h > 65535 || seq > 0x7FFFFFFFull)
     return b200_fail(PAI_ERR_UNSUPPORTED, "attention: seq %llu beyond the prefill kernel", (unsigned long long)seq);
-  if (smem > 48 * 1024) cudaFuncSetAttribute(k_attention_f32, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (smem > 48 * 1024) {
+    pai_status_t st = b200_cuda(
+        cudaFuncSetAttribute(k_attention_f32, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+        "k_attention_f32 smem attribute");
+    if (st) return st;
+  }
   k_attention_f32<<<dim3((unsigned)seq, (unsigned)h), 128, smem, (cudaStream_t)b200_ctx_stream(ctx)>>>(
       (uint32_t)h, (uint32_t)hk, (uint32_t)hd, q, k, v, out);
-  b200_ctx_count_launch(ctx, 1);
-  return b200_cuda(cudaGetLastError(), "k_attention_f32");
+  return b200_launched(ctx, 1, "k_attention_f32");
 }

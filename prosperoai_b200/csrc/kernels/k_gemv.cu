@@ -376,13 +376,14 @@ pai_status_t launch_t(pai_b200_ctx_t *ctx, GemvParams p, int num_sms) {
   }
   static bool attr_set = false;
   if (!attr_set) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
+    pai_status_t st = b200_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024),
+                                "k_gemv smem attribute");
+    if (st) return st;
     attr_set = true;
   }
   dim3 grid(p.ngroups, kcta);
   kern<<<grid, kThreads, smem, (cudaStream_t)b200_ctx_stream(ctx)>>>(p);
-  b200_ctx_count_launch(ctx, 1);
-  return b200_cuda(cudaGetLastError(), "k_gemv");
+  return b200_launched(ctx, 1, "k_gemv");
 }
 
 template <uint32_t T>

@@ -225,8 +225,7 @@ extern "C" pai_status_t b200_launch_rmsnorm(pai_b200_ctx_t *ctx, uint64_t rows, 
                                             const float *gamma, float eps, float *c) {
   if (eps == 0.0f) eps = 1e-5f;
   k_rmsnorm<<<(unsigned)rows, 256, 0, (cudaStream_t)b200_ctx_stream(ctx)>>>(n, a, gamma, eps, c);
-  b200_ctx_count_launch(ctx, 1);
-  return b200_cuda(cudaGetLastError(), "k_rmsnorm");
+  return b200_launched(ctx, 1, "k_rmsnorm");
 }
 
 extern "C" pai_status_t pai_b200_rmsnorm_gamma_f32(pai_b200_ctx_t *ctx, uint64_t rows, uint64_t n,
@@ -241,8 +240,7 @@ extern "C" pai_status_t pai_b200_silu_mul_f32(pai_b200_ctx_t *ctx, const float *
   if (!ctx || ((!gate || !up || !out) && n)) return b200_fail(PAI_ERR_INVALID_ARG, "silu_mul: NULL");
   if (!n) return PAI_OK;
   k_silu_mul<<<nblk(n, 256), 256, 0, (cudaStream_t)b200_ctx_stream(ctx)>>>(gate, up, out, n);
-  b200_ctx_count_launch(ctx, 1);
-  return b200_cuda(cudaGetLastError(), "k_silu_mul");
+  return b200_launched(ctx, 1, "k_silu_mul");
 }
 
 extern "C" pai_status_t pai_b200_vecadd_f32(pai_b200_ctx_t *ctx, const float *a, const float *b, float *c,
@@ -250,8 +248,7 @@ extern "C" pai_status_t pai_b200_vecadd_f32(pai_b200_ctx_t *ctx, const float *a,
   if (!ctx || ((!a || !b || !c) && n)) return b200_fail(PAI_ERR_INVALID_ARG, "vecadd: NULL");
   if (!n) return PAI_OK;
   k_vecadd<<<nblk(n, 256), 256, 0, (cudaStream_t)b200_ctx_stream(ctx)>>>(a, b, c, n);
-  b200_ctx_count_launch(ctx, 1);
-  return b200_cuda(cudaGetLastError(), "k_vecadd");
+  return b200_launched(ctx, 1, "k_vecadd");
 }
 
 extern "C" pai_status_t pai_b200_rope_f32(pai_b200_ctx_t *ctx, const float *x, uint64_t rows, uint64_t hd,
@@ -263,8 +260,7 @@ extern "C" pai_status_t pai_b200_rope_f32(pai_b200_ctx_t *ctx, const float *x, u
     return b200_fail(PAI_ERR_INVALID_ARG, "rope: invalid arguments");
   k_rope<<<nblk(rows * hd, 256), 256, 0, (cudaStream_t)b200_ctx_stream(ctx)>>>(x, rows, hd, heads, cos_t, sin_t,
                                                                                r2, out);
-  b200_ctx_count_launch(ctx, 1);
-  return b200_cuda(cudaGetLastError(), "k_rope");
+  return b200_launched(ctx, 1, "k_rope");
 }
 
 extern "C" pai_status_t b200_launch_rope_kv(pai_b200_ctx_t *ctx, uint32_t batch, uint32_t h, uint32_t hk,
@@ -273,8 +269,7 @@ extern "C" pai_status_t b200_launch_rope_kv(pai_b200_ctx_t *ctx, uint32_t batch,
                                             uint16_t *vc, uint64_t cap, uint64_t seq_stride) {
   k_rope_kv<<<batch, 256, 0, (cudaStream_t)b200_ctx_stream(ctx)>>>(h, hk, hd, qkv, pos, cos_t, sin_t, q,
                                                                     (__half *)kc, (__half *)vc, cap, seq_stride);
-  b200_ctx_count_launch(ctx, 1);
-  return b200_cuda(cudaGetLastError(), "k_rope_kv");
+  return b200_launched(ctx, 1, "k_rope_kv");
 }
 
 extern "C" pai_status_t b200_launch_embed(pai_b200_ctx_t *ctx, uint32_t type, uint32_t batch, uint64_t rows,
@@ -283,15 +278,13 @@ extern "C" pai_status_t b200_launch_embed(pai_b200_ctx_t *ctx, uint32_t type, ui
   const uint8_t *qs = (const uint8_t *)w;
   const uint8_t *sc = qs + b200_sc_offset(type, rows, k);
   k_embed<<<batch, 128, 0, (cudaStream_t)b200_ctx_stream(ctx)>>>(type, nb, qs, sc, tokens, x);
-  b200_ctx_count_launch(ctx, 1);
-  return b200_cuda(cudaGetLastError(), "k_embed");
+  return b200_launched(ctx, 1, "k_embed");
 }
 
 extern "C" pai_status_t b200_launch_argmax(pai_b200_ctx_t *ctx, uint64_t rows, uint64_t n, const float *logits,
                                            int32_t *out) {
   k_argmax<<<(unsigned)rows, 1024, 0, (cudaStream_t)b200_ctx_stream(ctx)>>>(n, logits, out);
-  b200_ctx_count_launch(ctx, 1);
-  return b200_cuda(cudaGetLastError(), "k_argmax");
+  return b200_launched(ctx, 1, "k_argmax");
 }
 
 extern "C" pai_status_t pai_b200_argmax_f32(pai_b200_ctx_t *ctx, uint64_t rows, uint64_t n, const float *logits,
@@ -305,6 +298,5 @@ extern "C" pai_status_t pai_b200_argmax_f32(pai_b200_ctx_t *ctx, uint64_t rows, 
 extern "C" pai_status_t b200_launch_step_tail(pai_b200_ctx_t *ctx, uint32_t batch, int32_t *tok_out,
                                               int32_t *tok_in, int32_t *pos) {
   k_step_tail<<<1, 32, 0, (cudaStream_t)b200_ctx_stream(ctx)>>>(batch, tok_out, tok_in, pos);
-  b200_ctx_count_launch(ctx, 1);
-  return b200_cuda(cudaGetLastError(), "k_step_tail");
+  return b200_launched(ctx, 1, "k_step_tail");
 }

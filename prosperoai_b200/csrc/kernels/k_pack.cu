@@ -222,8 +222,7 @@ extern "C" pai_status_t pai_b200_pack(pai_b200_ctx_t *ctx, uint32_t type, uint64
   uint8_t *sc = qs + b200_sc_offset(type, n, k);
   cudaStream_t s = (cudaStream_t)b200_ctx_stream(ctx);
   k_pack<<<nblk(npad * nb, 256), 256, 0, s>>>(type, n, npad, nb, (const uint8_t *)src, row_off, qs, sc);
-  b200_ctx_count_launch(ctx, 1);
-  return b200_cuda(cudaGetLastError(), "k_pack");
+  return b200_launched(ctx, 1, "k_pack");
 }
 
 extern "C" pai_status_t pai_b200_dequant(pai_b200_ctx_t *ctx, uint32_t type, uint64_t n, uint64_t k,
@@ -235,16 +234,14 @@ extern "C" pai_status_t pai_b200_dequant(pai_b200_ctx_t *ctx, uint32_t type, uin
   const uint8_t *qs = (const uint8_t *)packed;
   const uint8_t *sc = qs + b200_sc_offset(type, n, k);
   k_dequant<<<nblk(n * nb, 128), 128, 0, (cudaStream_t)b200_ctx_stream(ctx)>>>(type, n, nb, qs, sc, out);
-  b200_ctx_count_launch(ctx, 1);
-  return b200_cuda(cudaGetLastError(), "k_dequant");
+  return b200_launched(ctx, 1, "k_dequant");
 }
 
 extern "C" pai_status_t b200_launch_quantize(pai_b200_ctx_t *ctx, uint32_t type, const float *src,
                                              uint64_t numel, void *dst) {
   uint64_t nb = numel / b200_blk_elems(type);
   k_quantize<<<nblk(nb, 128), 128, 0, (cudaStream_t)b200_ctx_stream(ctx)>>>(type, nb, src, (uint8_t *)dst);
-  b200_ctx_count_launch(ctx, 1);
-  return b200_cuda(cudaGetLastError(), "k_quantize");
+  return b200_launched(ctx, 1, "k_quantize");
 }
 
 extern "C" pai_status_t b200_launch_synth_normal(pai_b200_ctx_t *ctx, float *dst, uint64_t rows,
@@ -252,12 +249,10 @@ extern "C" pai_status_t b200_launch_synth_normal(pai_b200_ctx_t *ctx, float *dst
   uint64_t work = rows * ((cols + 1) / 2);
   k_synth_normal<<<nblk(work, 256), 256, 0, (cudaStream_t)b200_ctx_stream(ctx)>>>(dst, rows, cols, seed,
                                                                                      (double)stddev);
-  b200_ctx_count_launch(ctx, 1);
-  return b200_cuda(cudaGetLastError(), "k_synth_normal");
+  return b200_launched(ctx, 1, "k_synth_normal");
 }
 
 extern "C" pai_status_t b200_launch_fill(pai_b200_ctx_t *ctx, float *dst, uint64_t n, float v) {
   k_fill<<<nblk(n, 256), 256, 0, (cudaStream_t)b200_ctx_stream(ctx)>>>(dst, n, v);
-  b200_ctx_count_launch(ctx, 1);
-  return b200_cuda(cudaGetLastError(), "k_fill");
+  return b200_launched(ctx, 1, "k_fill");
 }
