@@ -234,6 +234,24 @@ pai_status_t pai_b200_attn_decode_f16kv(pai_b200_ctx_t *ctx, uint64_t h,
                                         uint64_t cap, const float *q,
                                         const uint16_t *kcache,
                                         const uint16_t *vcache, float *out);
+/* Allocation-free form of pai_b200_attn_decode_f16kv, for callers that
+ * cannot allocate device memory when they run attention (a runtime that
+ * reserved the whole GPU for its own arena, code running inside CUDA-graph
+ * capture, a latency-critical loop). No counterpart in the reference: its
+ * attention is CPU-only. Same arguments and result; the chunk partials go
+ * to a fixed 4 MiB device array that the library holds on every GPU it is
+ * loaded on, so h x ceil(npos/chunk) x 130 floats must fit in 2^20 (about
+ * 8000 head-chunks), else PAI_ERR_UNSUPPORTED. The first call on a device
+ * looks the array up on that device; make it before any stream capture.
+ * Calls share the array: two calls that overlap on the GPU (different
+ * streams or contexts of one device) race. Allocates nothing. */
+pai_status_t pai_b200_attn_decode_f16kv_noalloc(pai_b200_ctx_t *ctx, uint64_t h,
+                                                uint64_t hk, uint64_t hd,
+                                                uint64_t npos, uint64_t cap,
+                                                const float *q,
+                                                const uint16_t *kcache,
+                                                const uint16_t *vcache,
+                                                float *out);
 /* First index of the strict maximum of each row of logits[rows][n]
  * (models/sampler.c:89-99 greedy). out is device int32[rows]. */
 pai_status_t pai_b200_argmax_f32(pai_b200_ctx_t *ctx, uint64_t rows, uint64_t n,

@@ -92,6 +92,7 @@ SIGNATURES = {
     "pai_b200_rope_cossin_f32": (I32, [U64, U64, F32, P, P]),
     "pai_b200_attention_f32": (I32, [P, U64, U64, U64, U64, P, P, P, P]),
     "pai_b200_attn_decode_f16kv": (I32, [P, U64, U64, U64, U64, U64, P, P, P, P]),
+    "pai_b200_attn_decode_f16kv_noalloc": (I32, [P, U64, U64, U64, U64, U64, P, P, P, P]),
     "pai_b200_argmax_f32": (I32, [P, U64, U64, P, P]),
     "pai_b200_register_ops": (I32, [P]),
     "pai_b200_op_count": (U32, []),

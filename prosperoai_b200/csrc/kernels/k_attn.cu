@@ -17,6 +17,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <mutex>
+
 #include "../b200_internal.h"
 #include "b200_device.cuh"
 
@@ -290,4 +292,104 @@ extern "C" pai_status_t pai_b200_attention_f32(pai_b200_ctx_t *ctx, uint64_t h, 
   k_attention_f32<<<dim3((unsigned)seq, (unsigned)h), 128, smem, (cudaStream_t)b200_ctx_stream(ctx)>>>(
       (uint32_t)h, (uint32_t)hk, (uint32_t)hd, q, k, v, out);
   return b200_launched(ctx, 1, "k_attention_f32");
+}
+
+// ---- allocation-free decode attention ------------------------------------------------------
+//
+// pai_b200_attn_decode_f16kv keeps its chunk partials in the context's
+// scratch buffer, which grows with cudaMalloc on first use. Callers that
+// must not allocate device memory where they call attention -- a host
+// runtime that reserved all of the GPU's memory up front for its own
+// arena, code that runs while a CUDA graph is being captured, or a
+// latency-critical loop where an allocation would synchronise the device
+// -- use pai_b200_attn_decode_f16kv_noalloc instead. Its partials live in
+// the fixed array below (4 MiB of device memory that every GPU loading
+// this library holds until the process exits).
+constexpr size_t kNoAllocScratchFloats = size_t(1) << 20;
+static __device__ __align__(256) float g_attn_noalloc_scratch[kNoAllocScratchFloats];
+
+namespace {
+
+// Device address of the array for `device`, looked up once per device with
+// that device current (the host-side symbol is only a stand-in, not a
+// device address).
+pai_status_t noalloc_scratch(int device, float **out) {
+  static std::mutex mu;
+  static float *addr[64];
+  if (device < 0 || device >= 64) return b200_fail(PAI_ERR_UNSUPPORTED, "attn_decode_noalloc: device %d", device);
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[device]) {
+    int prev = 0;
+    pai_status_t st = b200_cuda(cudaGetDevice(&prev), "cudaGetDevice");
+    if (st) return st;
+    st = b200_cuda(cudaSetDevice(device), "cudaSetDevice");
+    if (st) return st;
+    void *p = nullptr;
+    st = b200_cuda(cudaGetSymbolAddress(&p, g_attn_noalloc_scratch), "cudaGetSymbolAddress");
+    cudaSetDevice(prev);
+    if (st) return st;
+    addr[device] = (float *)p;
+  }
+  *out = addr[device];
+  return PAI_OK;
+}
+
+}  // namespace
+
+extern "C" pai_status_t pai_b200_attn_decode_f16kv_noalloc(pai_b200_ctx_t *ctx, uint64_t h, uint64_t hk,
+                                                           uint64_t hd, uint64_t npos, uint64_t cap,
+                                                           const float *q, const uint16_t *kcache,
+                                                           const uint16_t *vcache, float *out) {
+  if (!ctx || !q || !kcache || !vcache || !out) return b200_fail(PAI_ERR_INVALID_ARG, "attn_decode_noalloc: NULL");
+  if (h == 0 || hk == 0 || npos == 0 || npos > cap || h > 4096 || cap > 0x7FFFFFFFull)
+    return b200_fail(PAI_ERR_INVALID_ARG, "attn_decode_noalloc: shape");
+  if (hd != HD) return b200_fail(PAI_ERR_UNSUPPORTED, "attn_decode_noalloc: head_dim %llu (this kernel takes 128)",
+                                 (unsigned long long)hd);
+  if (h % hk) return b200_fail(PAI_ERR_INVALID_ARG, "attn_decode_noalloc: heads %llu / kv heads %llu",
+                               (unsigned long long)h, (unsigned long long)hk);
+  const uint64_t G = h / hk;
+  if (G != 1 && G != 2 && G != 4 && G != 8)
+    return b200_fail(PAI_ERR_UNSUPPORTED, "attn_decode_noalloc: %llu query heads per kv head", (unsigned long long)G);
+  // Same position chunking as pai_b200_attn_decode_f16kv for one sequence.
+  uint64_t want = (npos * hk + 295) / 296;
+  uint32_t chunk = (uint32_t)(((want + 31) / 32) * 32);
+  if (chunk < 32) chunk = 32;
+  if (chunk > 4096) chunk = 4096;
+  const uint32_t nsplit = (uint32_t)((npos + chunk - 1) / chunk);
+  const uint64_t need = h * nsplit * (uint64_t)(HD + 2);
+  if (need > kNoAllocScratchFloats)
+    return b200_fail(PAI_ERR_UNSUPPORTED,
+                     "attn_decode_noalloc: %llu heads x %u position chunks need %llu scratch floats; the fixed "
+                     "array holds %llu (use pai_b200_attn_decode_f16kv)",
+                     (unsigned long long)h, nsplit, (unsigned long long)need,
+                     (unsigned long long)kNoAllocScratchFloats);
+  float *scratch = nullptr;
+  pai_status_t st = noalloc_scratch(b200_ctx_device(ctx), &scratch);
+  if (st) return st;
+  AttnParams p{};
+  p.q = q;
+  p.kc = (const __half *)kcache;
+  p.vc = (const __half *)vcache;
+  p.out = out;
+  p.pos = nullptr;
+  p.npos_host = (uint32_t)npos;
+  p.h = (uint32_t)h;
+  p.hk = (uint32_t)hk;
+  p.chunk = chunk;
+  p.nsplit = nsplit;
+  p.cap = cap;
+  p.seq_stride = 0;
+  p.inv_scale = 1.0f / sqrtf((float)hd);
+  p.opart = scratch;
+  p.ml = scratch + h * nsplit * HD;
+  cudaStream_t s = (cudaStream_t)b200_ctx_stream(ctx);
+  switch (G) {
+    case 1: st = launch_split<1>(p, 1, s); break;
+    case 2: st = launch_split<2>(p, 1, s); break;
+    case 4: st = launch_split<4>(p, 1, s); break;
+    default: st = launch_split<8>(p, 1, s); break;
+  }
+  if (st) return st;
+  k_attn_combine<<<dim3((unsigned)h, 1), HD, 0, s>>>(p);
+  return b200_launched(ctx, 2, "k_attn_decode_noalloc");
 }
