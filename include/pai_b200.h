@@ -156,9 +156,11 @@ pai_status_t pai_b200_quantize(uint32_t type, const float *src, uint64_t numel,
                                void *dst_blocks);
 
 /* Weights live on the device in a packed layout built once at load from
- * ggml blocks: rows in groups of 32, each (group, block) stored as 16-byte
- * chunks interleaved across the 32 rows, with the fp16 scales in a
- * separate plane. Byte count of an n x k matrix in that layout: */
+ * ggml blocks: rows in tiles of 16 and K in units of 128 weights (one
+ * super-block for Q4_K), each (tile, unit) piece holding the quant bytes
+ * in the operand order of the int8 tensor-core MMA and the block headers
+ * in a separate plane; pieces are stored unit-major. Bytes are moved,
+ * never re-encoded. Byte count of an n x k matrix in that layout: */
 uint64_t pai_b200_packed_bytes(uint32_t type, uint64_t n, uint64_t k);
 /* Pack rows of ggml blocks already on the device. Packed row r is taken
  * from src + row_offsets[r] (a device array of n byte offsets; ~0 gives
@@ -199,6 +201,30 @@ pai_status_t pai_b200_gemv_q4_k_f32(pai_b200_ctx_t *ctx, uint64_t n, uint64_t k,
 pai_status_t pai_b200_gemv_f32(pai_b200_ctx_t *ctx, uint32_t type, uint64_t batch,
                                uint64_t n, uint64_t k, const void *w,
                                const float *x, const float *residual, float *y);
+/* The same GEMV with the activations prepared once for several matrices
+ * (the q, k and v projections of one x, for instance). pai_b200_prepare_x_f32
+ * writes x[batch][k] into a device buffer of pai_b200_xq_bytes(batch, k)
+ * bytes (256-byte aligned) in the GEMV kernels' operand format (24-bit
+ * fixed point per 32-element block); pai_b200_gemv_prepared_f32 then
+ * multiplies without re-reading x in fp32. Results equal pai_b200_gemv_f32's
+ * bit for bit. No counterpart in the reference, whose GEMVs take f32 x
+ * each time. */
+uint64_t pai_b200_xq_bytes(uint64_t batch, uint64_t k);
+pai_status_t pai_b200_prepare_x_f32(pai_b200_ctx_t *ctx, uint64_t batch, uint64_t k,
+                                    const float *x, void *xq);
+pai_status_t pai_b200_gemv_prepared_f32(pai_b200_ctx_t *ctx, uint32_t type, uint64_t batch,
+                                        uint64_t n, uint64_t k, const void *w,
+                                        const void *xq, const float *residual, float *y);
+/* y[b] = (residual ? residual[b] : 0) + W . rmsnorm_gamma(x[b], gamma, eps):
+ * pai_ref_rmsnorm_gamma_f32 (ref_ops.c:196-216) followed by the GEMV, the
+ * executor's PAI_OP_RMSNORM -> PAI_OP_GEMM pair (llama.c:674-697), with the
+ * norm computed inside the GEMV kernel. PAI_ERR_UNSUPPORTED when x is too
+ * long to stay in one CTA's shared memory (k above about 4096 at batch 8,
+ * 16384 at batch 1). */
+pai_status_t pai_b200_gemv_rmsnorm_f32(pai_b200_ctx_t *ctx, uint32_t type, uint64_t batch,
+                                       uint64_t n, uint64_t k, const void *w, const float *x,
+                                       const float *gamma, float eps, const float *residual,
+                                       float *y);
 
 /* c = a * gamma * (1/sqrtf(mean(a^2) + eps)) per row of n
  * (pai_ref_rmsnorm_gamma_f32, ref_ops.c:196-216; eps 0 selects 1e-5). */

@@ -124,6 +124,24 @@ class Device:
         check(load().pai_b200_gemv_f32(self.ctx, w.wtype, batch, w.n, w.k, w.ptr, x.ptr,
                                        residual.ptr if residual else None, y.ptr), "gemv")
 
+    def prepare_x(self, x: Buffer, k: int, batch: int = 1) -> Buffer:
+        """x[batch][k] in the GEMV operand format, for several gemv_prepared calls."""
+        xq = Buffer(self, int(load().pai_b200_xq_bytes(batch, k)))
+        check(load().pai_b200_prepare_x_f32(self.ctx, batch, k, x.ptr, xq.ptr), "prepare_x")
+        return xq
+
+    def gemv_prepared(self, w: PackedMatrix, xq: Buffer, y: Buffer, batch: int = 1,
+                      residual: Buffer | None = None):
+        check(load().pai_b200_gemv_prepared_f32(self.ctx, w.wtype, batch, w.n, w.k, w.ptr, xq.ptr,
+                                                residual.ptr if residual else None, y.ptr),
+              "gemv_prepared")
+
+    def gemv_rmsnorm(self, w: PackedMatrix, x: Buffer, gamma: Buffer, eps: float, y: Buffer,
+                     batch: int = 1, residual: Buffer | None = None):
+        check(load().pai_b200_gemv_rmsnorm_f32(self.ctx, w.wtype, batch, w.n, w.k, w.ptr, x.ptr,
+                                               gamma.ptr, eps, residual.ptr if residual else None,
+                                               y.ptr), "gemv_rmsnorm")
+
     def dequant(self, w: PackedMatrix, out: Buffer):
         check(load().pai_b200_dequant(self.ctx, w.wtype, w.n, w.k, w.ptr, out.ptr), "dequant")
 

@@ -14,20 +14,27 @@
 extern "C" {
 #endif
 
-/* ---- packed weight layout -------------------------------------------------------
- * Rows are grouped by B200_RG = 32. For row group g and block b, the
- * block's quant bytes are split into 16-byte chunks and chunk c of all
- * 32 rows is stored contiguously (512 B), so a warp with one lane per row
- * reads a chunk with a single fully coalesced 128-bit load per lane:
- *     qs plane: [ngroups][nb][chunks][32 rows][16 B]
- * The per-row block header (the fp16 d of Q4_0/Q8_0; d, dmin and the 12
- * packed scale bytes of Q4_K) goes to a second plane:
- *     sc plane: [ngroups][nb][32 rows][hdr bytes]
- * starting at the 256-byte aligned end of the qs plane. The bytes are
- * those of the ggml block (adapters/llama/gguf.c:680-693, 750-761,
- * 852-882) moved, never re-encoded, so the total equals the ggml size up
- * to alignment and zero rows that pad n to a multiple of 32. */
-#define B200_RG 32u
+/* ---- packed weight layout ------------------------------------------------------
+ * Built once at load from ggml blocks; bytes are moved, never re-encoded.
+ * Rows are taken 16 at a time (a "tile": the M of one m16n8k32 int8 MMA)
+ * and K in "units": 4 blocks (128 weights) for Q4_0/Q8_0, one 256-weight
+ * super-block for Q4_K. Each (tile, unit) holds
+ *   qs plane: CH chunks x 32 lanes x 16 B, in the order the MMA A-fragment
+ *             wants them: lane l (row r = l/4, column group c = l%4) finds in
+ *             one 16-byte load the 4-byte words it needs of 4 blocks (or of
+ *             the 4 64-weight groups of a Q4_K super-block):
+ *     Q4_0 (CH 2):  chunk h      = word c of qs[16] of row r+8h, blocks 0..3
+ *     Q8_0 (CH 4):  chunk 2h+p   = bytes 16p+4c..+3 of row r+8h, blocks 0..3
+ *     Q4_K (CH 4):  chunk 2h+p   = bytes 32g+16p+4c..+3 of row r+8h, g 0..3
+ *   sc plane: the block headers, [16 rows][4 blocks] fp16 d (Q4_0/Q8_0) or
+ *             [16 rows][16 B] {d, dmin, scales[12]} (Q4_K), at the 256-byte
+ *             aligned end of the qs plane.
+ * The (tile, unit) pieces are stored unit-major (all tiles of unit 0, then
+ * unit 1, ...), so the pieces of consecutive tiles for one unit are one
+ * contiguous run: a GEMV CTA that owns a group of tiles fetches a unit of
+ * all of them with one bulk copy per plane.
+ * Rows beyond n and blocks beyond k (to a whole unit) are zero. */
+#define B200_TILE 16u
 
 #ifdef __CUDACC__
 #define B200_HD __host__ __device__
@@ -39,20 +46,66 @@ static inline B200_HD uint32_t b200_blk_elems(uint32_t t) { return t == PAI_B200
 static inline B200_HD uint32_t b200_blk_bytes(uint32_t t) {
   return t == PAI_B200_Q4_0 ? 18u : (t == PAI_B200_Q8_0 ? 34u : 144u);
 }
-static inline B200_HD uint32_t b200_chunks(uint32_t t) {
-  return t == PAI_B200_Q4_0 ? 1u : (t == PAI_B200_Q8_0 ? 2u : 8u);
-}
-static inline B200_HD uint32_t b200_hdr_bytes(uint32_t t) { return t == PAI_B200_Q4_K ? 16u : 2u; }
 static inline B200_HD int b200_type_ok(uint32_t t) {
   return t == PAI_B200_Q4_0 || t == PAI_B200_Q8_0 || t == PAI_B200_Q4_K;
 }
 static inline B200_HD uint64_t b200_align256(uint64_t v) { return (v + 255u) & ~(uint64_t)255u; }
-static inline B200_HD uint64_t b200_ngroups(uint64_t n) { return (n + B200_RG - 1) / B200_RG; }
-static inline B200_HD uint64_t b200_qs_bytes(uint32_t t, uint64_t n, uint64_t k) {
-  return b200_ngroups(n) * (k / b200_blk_elems(t)) * b200_chunks(t) * B200_RG * 16u;
+static inline B200_HD uint64_t b200_ntiles(uint64_t n) { return (n + B200_TILE - 1) / B200_TILE; }
+/* Blocks per unit, units per row of k elements. */
+static inline B200_HD uint32_t b200_unit_blocks(uint32_t t) { return t == PAI_B200_Q4_K ? 1u : 4u; }
+static inline B200_HD uint64_t b200_units(uint32_t t, uint64_t k) {
+  uint64_t nb = k / b200_blk_elems(t);
+  return (nb + b200_unit_blocks(t) - 1) / b200_unit_blocks(t);
 }
+static inline B200_HD uint32_t b200_unit_qs_bytes(uint32_t t) { return t == PAI_B200_Q4_0 ? 1024u : 2048u; }
+static inline B200_HD uint32_t b200_unit_sc_bytes(uint32_t t) { return t == PAI_B200_Q4_K ? 256u : 128u; }
 static inline B200_HD uint64_t b200_sc_offset(uint32_t t, uint64_t n, uint64_t k) {
-  return b200_align256(b200_qs_bytes(t, n, k));
+  return b200_align256(b200_ntiles(n) * b200_units(t, k) * b200_unit_qs_bytes(t));
+}
+
+/* ---- quantised activations ("xq") ----------------------------------------------
+ * A GEMV reads x as 24-bit fixed point per 32-element block: x_j ~ s_b * X_j
+ * with X_j = L2*65536 + L1*256 + L0 in balanced base-256 digits (each an
+ * int8), s_b = max|x_b| / 8355711. The digits are stored in the order of
+ * the MMA B-fragment: vectors go in pairs (a pair fills the 8 columns of
+ * one MMA: columns 0..3 = L2, L1, L0, 0 of the even vector, 4..7 of the
+ * odd one), and for pair t, x-quad q (4 blocks), part p (elements 16p..):
+ *   limbs: [pair][quad][2][32 lanes][16 B]; lane l = column*4 + c holds
+ *          bytes 4c..4c+3 of elements 16p.. of blocks 0..3 of its column
+ *   sb:    [vec][quad*4] f32 block scales s_b
+ *   sx:    [vec][quad*4] f32 s_b * sum_j X_j (for the Q4_0 -8 offset and
+ *          the Q4_K mins)
+ * Writers fill every byte of a block, zero column included; the bytes of
+ * an absent odd vector are never weighted (its scales read as 0). */
+#define B200_XQ_MAX 8355711
+static inline B200_HD uint64_t b200_xq_quads(uint64_t k) { return (k / 32u + 3u) / 4u; }
+static inline B200_HD uint64_t b200_xq_limb_bytes(uint32_t batch, uint64_t k) {
+  return (uint64_t)((batch + 1u) / 2u) * b200_xq_quads(k) * 1024u;
+}
+static inline B200_HD uint64_t b200_xq_bytes(uint32_t batch, uint64_t k) {
+  return b200_align256(b200_xq_limb_bytes(batch, k)) + 2u * b200_align256((uint64_t)batch * b200_xq_quads(k) * 16u);
+}
+
+typedef struct b200_xq {
+  uint8_t *limbs;
+  float *sb, *sx;
+  uint32_t batch;
+  uint64_t k, quads;
+} b200_xq_t;
+
+/* Carve an xq view out of `base` (b200_xq_bytes(batch, k) bytes). */
+static inline B200_HD b200_xq_t b200_xq_view(void *base, uint32_t batch, uint64_t k) {
+  b200_xq_t v;
+  uint8_t *p = (uint8_t *)base;
+  v.batch = batch;
+  v.k = k;
+  v.quads = b200_xq_quads(k);
+  v.limbs = p;
+  p += b200_align256(b200_xq_limb_bytes(batch, k));
+  v.sb = (float *)p;
+  p += b200_align256((uint64_t)batch * v.quads * 16u);
+  v.sx = (float *)p;
+  return v;
 }
 
 /* ---- errors ------------------------------------------------------------------------- */
@@ -71,11 +124,27 @@ void b200_ctx_count_launch(pai_b200_ctx_t *ctx, uint32_t kernels);
  * it also waits for the kernels and reports their execution errors,
  * which localises a failing kernel. */
 pai_status_t b200_launched(pai_b200_ctx_t *ctx, uint32_t kernels, const char *name);
-/* Per-context split-K scratch: float partial sums and zeroed counters
- * (each kernel that uses the counters leaves them at zero). */
+/* Per-context scratch: float partial sums and zeroed counters (each
+ * kernel that uses the counters leaves them at zero). Kernels on the
+ * context stream use it one after another. */
 pai_status_t b200_ctx_scratch(pai_b200_ctx_t *ctx, uint64_t partial_floats,
                               uint32_t counters, float **partial,
                               uint32_t **counter);
+/* Activation scratch of the public GEMV entry points (grown on demand). */
+pai_status_t b200_ctx_xq(pai_b200_ctx_t *ctx, uint64_t bytes, void **buf);
+/* Device address of the context's error word: kernels whose bounded waits
+ * run out set it, and pai_b200_sync then reports PAI_ERR_TIMEOUT. */
+uint32_t *b200_ctx_errflag(pai_b200_ctx_t *ctx);
+/* Programmatic dependent launch for the kernels of the model's decode
+ * step: while on, those kernels are launched so that each may become
+ * resident before its predecessor in the stream finishes; each waits
+ * (griddepcontrol.wait) before it touches memory the predecessor writes,
+ * and only the GEMV does work before that wait: it prefetches weights,
+ * which nothing in the step writes. Off for the public single-op entry
+ * points, whose inputs a preceding kernel may just have written.
+ * PAI_B200_PDL=0 in the environment keeps it off. */
+int b200_ctx_pdl(pai_b200_ctx_t *ctx);
+void b200_ctx_set_pdl(pai_b200_ctx_t *ctx, int on);
 
 /* CUDA graph capture of everything launched on the context stream. */
 pai_status_t b200_graph_begin(pai_b200_ctx_t *ctx);
@@ -87,36 +156,56 @@ void b200_graph_destroy(void *exec);
 
 enum { B200_EPI_STORE = 0, B200_EPI_RESIDUAL = 1, B200_EPI_SILU_GLU = 2 };
 
-/* GEMV over a packed matrix. For B200_EPI_SILU_GLU the packed rows come
- * in groups of 16 gate rows followed by the 16 matching up rows, n counts
- * both, and y receives n/2 values silu(gate)*up per batch row. */
+/* GEMV over a packed matrix with x given as xq (batch vectors of k).
+ * B200_EPI_SILU_GLU: each 16-row tile holds 8 gate rows then the 8 matching
+ * up rows, n counts both, y receives n/2 values silu(gate)*up per vector,
+ * and when xq_out is non-NULL they are also quantised into it (the next
+ * GEMV's input). */
 pai_status_t b200_launch_gemv(pai_b200_ctx_t *ctx, uint32_t type, uint32_t batch,
-                              uint64_t n, uint64_t k, const void *w, const float *x,
-                              const float *residual, float *y, int epi);
+                              uint64_t n, uint64_t k, const void *w, const b200_xq_t *xq,
+                              const float *residual, float *y, int epi,
+                              const b200_xq_t *xq_out);
+/* The same GEMV with x = rmsnorm_gamma(x_f32, gamma, eps) computed by
+ * every CTA in its prologue (pai_ref_rmsnorm_gamma_f32's arithmetic) and
+ * quantised into shared memory: no norm kernel, no xq round trip.
+ * PAI_ERR_UNSUPPORTED, before any launch, when the quantised x does not
+ * fit in a CTA's shared memory: use rmsnorm_xq + gemv then. */
+pai_status_t b200_launch_gemv_norm(pai_b200_ctx_t *ctx, uint32_t type, uint32_t batch,
+                                   uint64_t n, uint64_t k, const void *w, const float *x,
+                                   const float *gamma, float eps, const float *residual,
+                                   float *y, int epi, const b200_xq_t *xq_out);
+/* Quantise x[batch][k] (fp32) into xq. */
+pai_status_t b200_launch_xprep(pai_b200_ctx_t *ctx, uint32_t batch, uint64_t k,
+                               const float *x, const b200_xq_t *xq);
+/* rmsnorm_gamma of each of `rows` rows of n; writes c (fp32) when non-NULL
+ * and the quantised result into xq when non-NULL. */
+pai_status_t b200_launch_rmsnorm_xq(pai_b200_ctx_t *ctx, uint64_t rows, uint64_t n,
+                                    const float *a, const float *gamma, float eps,
+                                    float *c, const b200_xq_t *xq);
 /* x[b] = dequantised row tokens[b] of a packed rows x k table. */
 pai_status_t b200_launch_embed(pai_b200_ctx_t *ctx, uint32_t type, uint32_t batch,
                                uint64_t rows, uint64_t k, const void *w,
                                const int32_t *tokens, float *x);
-/* q/k/v from the fused projection ([batch][(H+2HK)*hd]), rotate q and k
- * at position *pos, write q (fp32) and the new k/v rows into the fp16
- * caches [hk][cap][hd] of each sequence (cache stride per sequence
- * seq_stride elements). */
-pai_status_t b200_launch_rope_kv(pai_b200_ctx_t *ctx, uint32_t batch, uint32_t h,
-                                 uint32_t hk, uint32_t hd, const float *qkv,
-                                 const int32_t *pos, const float *cos_t,
-                                 const float *sin_t, float *q, uint16_t *kc,
-                                 uint16_t *vc, uint64_t cap, uint64_t seq_stride);
 /* Decode attention at position *pos (npos = *pos + 1) when pos is a
- * device pointer; max_npos bounds the launch. */
+ * device pointer; max_npos bounds the launch. q is already rotated. */
 pai_status_t b200_launch_attn_decode(pai_b200_ctx_t *ctx, uint32_t batch, uint32_t h,
                                      uint32_t hk, uint32_t hd, const int32_t *pos,
                                      uint64_t npos_host, uint64_t max_npos,
                                      uint64_t cap, uint64_t seq_stride,
                                      const float *q, const uint16_t *kc,
-                                     const uint16_t *vc, float *out);
-pai_status_t b200_launch_rmsnorm(pai_b200_ctx_t *ctx, uint64_t rows, uint64_t n,
-                                 const float *a, const float *gamma, float eps,
-                                 float *c);
+                                     const uint16_t *vc, float *out,
+                                     const b200_xq_t *xq_out);
+/* Decode-step attention straight from the fused projection rows qkv
+ * [batch][(h + 2 hk) hd]: rotates q and k at *pos (tables cos_t/sin_t),
+ * appends k and v (fp16) at *pos of each sequence's cache ([hk][cap][hd],
+ * seq_stride elements apart), attends over positions 0..*pos and merges
+ * the position chunks in the same kernel; out (and xq_out when non-NULL)
+ * receive the attention output. */
+pai_status_t b200_launch_attn_step(pai_b200_ctx_t *ctx, uint32_t batch, uint32_t h, uint32_t hk,
+                                   uint32_t hd, const int32_t *pos, uint64_t max_npos, uint64_t cap,
+                                   uint64_t seq_stride, const float *qkv, const float *cos_t,
+                                   const float *sin_t, uint16_t *kc, uint16_t *vc, float *out,
+                                   const b200_xq_t *xq_out);
 pai_status_t b200_launch_argmax(pai_b200_ctx_t *ctx, uint64_t rows, uint64_t n,
                                 const float *logits, int32_t *out);
 pai_status_t b200_launch_step_tail(pai_b200_ctx_t *ctx, uint32_t batch,

@@ -15,6 +15,12 @@
  *     x   = x + h.Wdown              (residual fused)    :782-795
  *   logits = rmsnorm(x, output_norm).Wout; token = argmax :884-895
  *
+ * Kernels per layer: the norms run inside the prologue of the GEMV that
+ * consumes them; RoPE, the cache append, attention and the chunk merge
+ * are one kernel that also writes the o projection's quantised input; the
+ * gate/up GEMV applies SiLU*up and quantises h for the down projection.
+ * So a layer is 5 kernels: qkv, attention, o (+x), gate/up, down (+x).
+ *
  * Host code only: every device step is a launcher from csrc/kernels.
  */
 #include <stdlib.h>
@@ -66,7 +72,7 @@ pai_status_t pai_b200_model_create(pai_b200_ctx_t *ctx, const pai_b200_model_cfg
       c->n_ff == 0 || c->vocab == 0 || c->n_head % c->n_head_kv) {
     return b200_fail(PAI_ERR_UNSUPPORTED, "model_create: shape (head_dim must be 128, heads a multiple of kv heads)");
   }
-  if (c->n_head_kv % tp_size || c->n_ff % (16u * tp_size) || c->vocab % tp_size) {
+  if (c->n_head_kv % tp_size || c->n_ff % (32u * tp_size) || c->vocab % tp_size) {
     return b200_fail(PAI_ERR_MISMATCH, "model_create: kv heads, ffn and vocab must split over %u ranks", tp_size);
   }
   E = c->n_embd;
@@ -242,7 +248,7 @@ static pai_status_t pack_tensor(pai_b200_model_t *m, uint32_t kind, uint32_t lay
   for (uint64_t r = 0; r < n_dst; r++) {
     uint64_t o = ROW_SKIP;
     uint64_t qrows = (uint64_t)m->hl * hd, krows = (uint64_t)m->hkl * hd;
-    uint64_t g = r / 32, w = r % 32, i = g * 16 + (w % 16);
+    uint64_t g = r / 16, w = r % 16, i = g * 8 + (w % 8); /* gate/up tile: 8 gate then 8 up rows */
     switch (kind) {
       case PAI_B200_T_WQ:
         if (r < qrows) o = ((uint64_t)m->rank * qrows + r) * rb;
@@ -258,10 +264,10 @@ static pai_status_t pack_tensor(pai_b200_model_t *m, uint32_t kind, uint32_t lay
         o = r * rb + pai_b200_block_bytes(type, (uint64_t)m->rank * k_dst);
         break;
       case PAI_B200_T_WGATE:
-        if (w < 16) o = ((uint64_t)m->rank * m->ffl + i) * rb;
+        if (w < 8) o = ((uint64_t)m->rank * m->ffl + i) * rb;
         break;
       case PAI_B200_T_WUP:
-        if (w >= 16) o = ((uint64_t)m->rank * m->ffl + i) * rb;
+        if (w >= 8) o = ((uint64_t)m->rank * m->ffl + i) * rb;
         break;
       case PAI_B200_T_TOK_EMBD: o = r * rb; break;
       default: o = ((uint64_t)m->v0 + r) * rb; break;
@@ -388,7 +394,9 @@ struct pai_b200_session {
   uint32_t batch, max_ctx, pos;
   int32_t *tok_in, *tok_out, *dpos; /* device */
   int32_t *htok;                    /* pinned host staging, 2*batch */
-  float *x, *xn, *qkv, *q, *att, *ox, *h, *logits, *cos_t, *sin_t;
+  float *x, *qkv, *att, *ox, *h, *logits, *cos_t, *sin_t;
+  void *xq_buf;                   /* GEMV operands: */
+  b200_xq_t xq_e, xq_o, xq_h;     /* normed x (fallback path), attention output, silu*up */
   uint16_t *kc, *vc; /* [layer][batch][hkl][max_ctx][hd] */
   uint64_t seq_stride, layer_stride;
   void *graph;
@@ -401,46 +409,58 @@ pai_status_t b200_tp_allreduce(void *tp, pai_b200_ctx_t *ctx, float *buf, uint64
 pai_status_t b200_tp_argmax(void *tp, pai_b200_ctx_t *ctx, uint32_t batch, uint32_t vl, uint32_t v0,
                             const float *logits, int32_t *tok_out);
 
+/* y = W . rmsnorm_gamma(x): the norm fused into the GEMV's prologue when
+ * the quantised x fits in a CTA's shared memory, else the norm kernel
+ * writes xq_e and the GEMV reads it. */
+static pai_status_t norm_gemv(pai_b200_session_t *s, uint32_t type, uint64_t n, const void *w, const float *gamma,
+                              float *y, int epi, const b200_xq_t *xq_out) {
+  pai_b200_model_t *m = s->m;
+  const uint32_t B = s->batch, E = m->cfg.n_embd;
+  pai_status_t st = b200_launch_gemv_norm(m->ctx, type, B, n, E, w, s->x, gamma, m->cfg.eps, NULL, y, epi, xq_out);
+  if (st != PAI_ERR_UNSUPPORTED) return st;
+  st = b200_launch_rmsnorm_xq(m->ctx, B, E, s->x, gamma, m->cfg.eps, NULL, &s->xq_e);
+  if (!st) st = b200_launch_gemv(m->ctx, type, B, n, E, w, &s->xq_e, NULL, y, epi, xq_out);
+  return st;
+}
+
 static pai_status_t enqueue_step(pai_b200_session_t *s) {
   pai_b200_model_t *m = s->m;
   const pai_b200_model_cfg_t *c = &m->cfg;
   pai_b200_ctx_t *ctx = m->ctx;
   const uint32_t B = s->batch, E = c->n_embd, hd = c->head_dim;
+  b200_ctx_set_pdl(ctx, 1); /* every kernel of the step waits for its predecessor's writes */
   pai_status_t st = b200_launch_embed(ctx, c->etype, B, c->vocab, E, m->tok_embd, s->tok_in, s->x);
   for (uint32_t l = 0; !st && l < c->n_layer; l++) {
     uint16_t *kc = s->kc + (uint64_t)l * s->layer_stride, *vc = s->vc + (uint64_t)l * s->layer_stride;
-    st = b200_launch_rmsnorm(ctx, B, E, s->x, m->attn_norm[l], c->eps, s->xn);
-    if (!st) st = b200_launch_gemv(ctx, c->wtype, B, m->n_qkv, E, m->wqkv[l], s->xn, NULL, s->qkv, B200_EPI_STORE);
+    st = norm_gemv(s, c->wtype, m->n_qkv, m->wqkv[l], m->attn_norm[l], s->qkv, B200_EPI_STORE, NULL);
     if (!st)
-      st = b200_launch_rope_kv(ctx, B, m->hl, m->hkl, hd, s->qkv, s->dpos, s->cos_t, s->sin_t, s->q, kc, vc,
-                               s->max_ctx, s->seq_stride);
-    if (!st)
-      st = b200_launch_attn_decode(ctx, B, m->hl, m->hkl, hd, s->dpos, 0, s->max_ctx, s->max_ctx, s->seq_stride,
-                                   s->q, kc, vc, s->att);
+      st = b200_launch_attn_step(ctx, B, m->hl, m->hkl, hd, s->dpos, s->max_ctx, s->max_ctx, s->seq_stride, s->qkv,
+                                 s->cos_t, s->sin_t, kc, vc, s->att, &s->xq_o);
     if (m->tp == 1) {
-      if (!st) st = b200_launch_gemv(ctx, c->wtype, B, E, m->k_o, m->wo[l], s->att, s->x, s->x, B200_EPI_RESIDUAL);
+      if (!st)
+        st = b200_launch_gemv(ctx, c->wtype, B, E, m->k_o, m->wo[l], &s->xq_o, s->x, s->x, B200_EPI_RESIDUAL, NULL);
     } else {
-      if (!st) st = b200_launch_gemv(ctx, c->wtype, B, E, m->k_o, m->wo[l], s->att, NULL, s->ox, B200_EPI_STORE);
+      if (!st) st = b200_launch_gemv(ctx, c->wtype, B, E, m->k_o, m->wo[l], &s->xq_o, NULL, s->ox, B200_EPI_STORE, NULL);
       if (!st) st = b200_tp_allreduce(s->tp, ctx, s->ox, (uint64_t)B * E);
       if (!st) st = pai_b200_vecadd_f32(ctx, s->x, s->ox, s->x, (uint64_t)B * E);
     }
-    if (!st) st = b200_launch_rmsnorm(ctx, B, E, s->x, m->ffn_norm[l], c->eps, s->xn);
-    if (!st) st = b200_launch_gemv(ctx, c->wtype, B, 2ull * m->ffl, E, m->wgu[l], s->xn, NULL, s->h, B200_EPI_SILU_GLU);
+    if (!st) st = norm_gemv(s, c->wtype, 2ull * m->ffl, m->wgu[l], m->ffn_norm[l], s->h, B200_EPI_SILU_GLU, &s->xq_h);
     if (m->tp == 1) {
-      if (!st) st = b200_launch_gemv(ctx, c->wtype, B, E, m->ffl, m->wdown[l], s->h, s->x, s->x, B200_EPI_RESIDUAL);
+      if (!st)
+        st = b200_launch_gemv(ctx, c->wtype, B, E, m->ffl, m->wdown[l], &s->xq_h, s->x, s->x, B200_EPI_RESIDUAL, NULL);
     } else {
-      if (!st) st = b200_launch_gemv(ctx, c->wtype, B, E, m->ffl, m->wdown[l], s->h, NULL, s->ox, B200_EPI_STORE);
+      if (!st) st = b200_launch_gemv(ctx, c->wtype, B, E, m->ffl, m->wdown[l], &s->xq_h, NULL, s->ox, B200_EPI_STORE, NULL);
       if (!st) st = b200_tp_allreduce(s->tp, ctx, s->ox, (uint64_t)B * E);
       if (!st) st = pai_b200_vecadd_f32(ctx, s->x, s->ox, s->x, (uint64_t)B * E);
     }
   }
-  if (!st) st = b200_launch_rmsnorm(ctx, B, E, s->x, m->output_norm, c->eps, s->xn);
-  if (!st) st = b200_launch_gemv(ctx, c->etype, B, m->vl, E, m->output, s->xn, NULL, s->logits, B200_EPI_STORE);
+  if (!st) st = norm_gemv(s, c->etype, m->vl, m->output, m->output_norm, s->logits, B200_EPI_STORE, NULL);
   if (!st) {
     st = m->tp == 1 ? b200_launch_argmax(ctx, B, m->vl, s->logits, s->tok_out)
                     : b200_tp_argmax(s->tp, ctx, B, m->vl, m->v0, s->logits, s->tok_out);
   }
   if (!st) st = b200_launch_step_tail(ctx, B, s->tok_out, s->tok_in, s->dpos);
+  b200_ctx_set_pdl(ctx, 0);
   return st;
 }
 
@@ -478,11 +498,20 @@ pai_status_t pai_b200_session_create(pai_b200_model_t *m, uint32_t batch, uint32
   SALLOC(s->tok_out, 64);
   SALLOC(s->dpos, 64);
   SALLOC(s->x, (uint64_t)batch * c->n_embd * 4);
-  SALLOC(s->xn, (uint64_t)batch * c->n_embd * 4);
   SALLOC(s->ox, (uint64_t)batch * c->n_embd * 4);
   SALLOC(s->qkv, (uint64_t)batch * m->n_qkv * 4);
-  SALLOC(s->q, (uint64_t)batch * m->k_o * 4);
   SALLOC(s->att, (uint64_t)batch * m->k_o * 4);
+  {
+    const uint64_t be = b200_xq_bytes(batch, c->n_embd), bo = b200_xq_bytes(batch, m->k_o);
+    const uint64_t bh = b200_xq_bytes(batch, m->ffl);
+    SALLOC(s->xq_buf, be + bo + bh);
+    if (!st) st = pai_b200_memset(ctx, s->xq_buf, 0, be + bo + bh);
+    if (!st) {
+      s->xq_e = b200_xq_view(s->xq_buf, batch, c->n_embd);
+      s->xq_o = b200_xq_view((uint8_t *)s->xq_buf + be, batch, m->k_o);
+      s->xq_h = b200_xq_view((uint8_t *)s->xq_buf + be + bo, batch, m->ffl);
+    }
+  }
   SALLOC(s->h, (uint64_t)batch * m->ffl * 4);
   SALLOC(s->logits, (uint64_t)batch * m->vl * 4);
   SALLOC(s->cos_t, (uint64_t)max_ctx * c->head_dim / 2 * 4);
@@ -536,11 +565,10 @@ pai_status_t pai_b200_session_destroy(pai_b200_session_t *s) {
   pai_b200_free(ctx, s->tok_out);
   pai_b200_free(ctx, s->dpos);
   pai_b200_free(ctx, s->x);
-  pai_b200_free(ctx, s->xn);
   pai_b200_free(ctx, s->ox);
   pai_b200_free(ctx, s->qkv);
-  pai_b200_free(ctx, s->q);
   pai_b200_free(ctx, s->att);
+  pai_b200_free(ctx, s->xq_buf);
   pai_b200_free(ctx, s->h);
   pai_b200_free(ctx, s->logits);
   pai_b200_free(ctx, s->cos_t);

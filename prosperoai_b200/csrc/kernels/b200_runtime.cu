@@ -20,8 +20,14 @@ struct pai_b200_ctx {
   uint64_t partial_floats;
   uint32_t *counters;     // split-K arrival counters, left at zero
   uint32_t ncounters;
+  uint32_t *err_host;     // host-mapped error word (bounded device waits)
+  uint32_t *err_dev;
+  void *xq;               // activation scratch of the public GEMV entry points
+  uint64_t xq_bytes;
   uint64_t launches;
   int capturing;
+  int pdl;          // launch the decode-step kernels with programmatic dependent launch
+  int pdl_allowed;  // PAI_B200_PDL=0 in the environment turns it off
 };
 
 static thread_local char g_err[512];
@@ -83,11 +89,24 @@ extern "C" pai_status_t pai_b200_init(int device, pai_b200_ctx_t **out) {
   pai_b200_ctx *c = new (std::nothrow) pai_b200_ctx();
   if (!c) return b200_fail(PAI_ERR_NOMEM, "init: host allocation");
   c->device = device;
+  {
+    const char *e = getenv("PAI_B200_PDL");
+    c->pdl_allowed = !(e && e[0] == '0');
+  }
   st = b200_cuda(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "cudaStreamCreate");
   if (st) {
     delete c;
     return st;
   }
+  st = b200_cuda(cudaHostAlloc((void **)&c->err_host, sizeof(uint32_t), cudaHostAllocMapped), "error word");
+  if (!st) st = b200_cuda(cudaHostGetDevicePointer((void **)&c->err_dev, c->err_host, 0), "error word mapping");
+  if (st) {
+    if (c->err_host) cudaFreeHost(c->err_host);
+    cudaStreamDestroy(c->stream);
+    delete c;
+    return st;
+  }
+  *c->err_host = 0;
   *out = c;
   return PAI_OK;
 }
@@ -98,6 +117,8 @@ extern "C" pai_status_t pai_b200_shutdown(pai_b200_ctx_t *c) {
   cudaStreamSynchronize(c->stream);
   if (c->partial) cudaFree(c->partial);
   if (c->counters) cudaFree(c->counters);
+  if (c->xq) cudaFree(c->xq);
+  if (c->err_host) cudaFreeHost(c->err_host);
   cudaStreamDestroy(c->stream);
   delete c;
   return PAI_OK;
@@ -105,6 +126,27 @@ extern "C" pai_status_t pai_b200_shutdown(pai_b200_ctx_t *c) {
 
 extern "C" void *b200_ctx_stream(pai_b200_ctx_t *c) { return c->stream; }
 extern "C" int b200_ctx_device(pai_b200_ctx_t *c) { return c->device; }
+extern "C" int b200_ctx_pdl(pai_b200_ctx_t *c) { return c->pdl; }
+extern "C" void b200_ctx_set_pdl(pai_b200_ctx_t *c, int on) { c->pdl = on && c->pdl_allowed; }
+extern "C" uint32_t *b200_ctx_errflag(pai_b200_ctx_t *c) { return c->err_dev; }
+
+extern "C" pai_status_t b200_ctx_xq(pai_b200_ctx_t *c, uint64_t bytes, void **buf) {
+  if (bytes > c->xq_bytes) {
+    if (c->capturing) return b200_fail(PAI_ERR_INTERNAL, "activation scratch growth during graph capture");
+    if (c->xq) {
+      cudaStreamSynchronize(c->stream);
+      cudaFree(c->xq);
+      c->xq = nullptr;
+      c->xq_bytes = 0;
+    }
+    const uint64_t want = bytes < (1u << 20) ? (1u << 20) : bytes;
+    pai_status_t st = b200_cuda(cudaMalloc(&c->xq, want), "activation scratch alloc");
+    if (st) return st;
+    c->xq_bytes = want;
+  }
+  *buf = c->xq;
+  return PAI_OK;
+}
 extern "C" void b200_ctx_count_launch(pai_b200_ctx_t *c, uint32_t k) {
   if (!c->capturing) c->launches += k;
 }
@@ -227,7 +269,13 @@ extern "C" pai_status_t pai_b200_sync(pai_b200_ctx_t *c) {
   }
   st = b200_cuda(cudaStreamSynchronize(c->stream), "stream sync");
   if (st) return st;
-  return b200_cuda(cudaGetLastError(), "kernel execution");
+  st = b200_cuda(cudaGetLastError(), "kernel execution");
+  if (st) return st;
+  if (*(volatile uint32_t *)c->err_host) {
+    *(volatile uint32_t *)c->err_host = 0;
+    return b200_fail(PAI_ERR_TIMEOUT, "a bounded device wait ran out (a bulk copy or peer never completed)");
+  }
+  return PAI_OK;
 }
 
 // ---- events -------------------------------------------------------------------------------

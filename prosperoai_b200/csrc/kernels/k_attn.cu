@@ -5,7 +5,10 @@
 // the chunk for all G = H/HK query heads that share the KV head (K rows
 // are read once for the G heads), takes the chunk's max and exp-sum,
 // and accumulates exp-weighted V rows; a second kernel merges the chunks
-// with the usual max-rescaling. Reference: the last-row iteration of
+// with the usual max-rescaling. In the decode step the same kernel also
+// rotates q and k at the position, appends k and v to the cache, and the
+// last chunk of each kv head to finish merges the chunks (no separate
+// RoPE or merge kernel). Reference: the last-row iteration of
 // pai_ref_attention_f32 (cpu/reference/ref_ops.c:307-349) on the cache
 // contents: scores scaled by 1/sqrtf(hd) after the dot, softmax with the
 // max subtracted, then sum_i p_i v_i.
@@ -17,6 +20,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "../b200_internal.h"
@@ -37,27 +41,90 @@ struct AttnParams {
   uint32_t h, hk, chunk, nsplit;
   uint64_t cap, seq_stride;
   float inv_scale;
+  b200_xq_t xo;  // when xo.limbs is set, the merged output is also quantised for the o projection
+  // decode-step form: q, k, v come unrotated from the fused projection row
+  // qkv [B][(H + 2 HK) HD]; the kernel rotates q and k at the position, the
+  // CTA holding the position appends k and v to the cache, and the last
+  // CTA of each (sequence, kv head) merges the chunks (ticket in cnt)
+  const float *qkv, *cos_t, *sin_t;
+  __half *kw, *vw;
+  uint32_t *cnt;
 };
 
 __device__ __forceinline__ uint32_t npos_of(const AttnParams &p) {
   return p.pos ? (uint32_t)(*p.pos) + 1u : p.npos_host;
 }
+// Positions per chunk: fixed by the host when it knows the length; when the
+// position lives on the device, the nsplit chunks cover it evenly (a
+// multiple of 32, at most the host's p.chunk, which sized shared memory).
+__device__ __forceinline__ uint32_t chunk_of(const AttnParams &p, uint32_t npos) {
+  if (!p.pos) return p.chunk;
+  const uint32_t c = ((npos + p.nsplit - 1) / p.nsplit + 31) / 32 * 32;
+  return c < 32 ? 32 : c;
+}
 
-template <int G>
+// Merge the chunk partials of query head hh (one thread per dimension d);
+// returns the output value of dimension d.
+__device__ __forceinline__ float merge_chunks(const AttnParams &p, uint32_t bi, uint32_t hh, uint32_t ns,
+                                              uint32_t d) {
+  const size_t base = ((size_t)bi * p.h + hh) * p.nsplit;
+  float M = -INFINITY;
+  for (uint32_t s = 0; s < ns; s++) M = fmaxf(M, __ldcg(&p.ml[(base + s) * 2]));
+  float L = 0.f, o = 0.f;
+  for (uint32_t s = 0; s < ns; s++) {
+    const float w = expf(__ldcg(&p.ml[(base + s) * 2]) - M);
+    L = fmaf(__ldcg(&p.ml[(base + s) * 2 + 1]), w, L);
+    o = fmaf(__ldcg(&p.opart[(base + s) * HD + d]), w, o);
+  }
+  return o / L;
+}
+
+template <int G, bool STEP>
 __global__ void __launch_bounds__(128) k_attn_split(AttnParams p) {
+  pdl_trigger();
+  pdl_wait();
   const uint32_t kvh = blockIdx.x, split = blockIdx.y, bi = blockIdx.z;
   const uint32_t npos = npos_of(p);
-  const uint32_t start = split * p.chunk;
+  const uint32_t chunk = chunk_of(p, npos);
+  const uint32_t start = split * chunk;
   if (start >= npos) return;
-  const uint32_t len = min(p.chunk, npos - start);
+  const uint32_t len = min(chunk, npos - start);
   extern __shared__ __align__(16) float sm[];
   float *qs = sm;               // [G][HD]
   float *sc = sm + G * HD;      // [G][chunk]
   __shared__ float red[2][G][HD];
   __shared__ float mls[G][2];
+  __shared__ uint32_t ticket;
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const uint32_t h0 = kvh * G;
-  for (int i = t; i < G * HD; i += 128) qs[i] = p.q[((size_t)bi * p.h + h0) * HD + i];
+  if (STEP) {
+    // rotate this CTA's G query heads at the position (pai_ref_rope_f32 on
+    // the q part of the projection row, adapters/llama/llama.c:713-724)
+    const uint32_t pos = npos - 1, r2 = HD / 2;
+    const float *row = p.qkv + (size_t)bi * (p.h + 2 * p.hk) * HD;
+    for (int i = t; i < G * (int)r2; i += 128) {
+      const uint32_t g = i / r2, j = i % r2;
+      const float *xr = row + (size_t)(h0 + g) * HD;
+      float o0, o1;
+      rope_pair(xr[j], xr[j + r2], p.cos_t[(size_t)pos * r2 + j], p.sin_t[(size_t)pos * r2 + j], o0, o1);
+      qs[g * HD + j] = o0;
+      qs[g * HD + j + r2] = o1;
+    }
+    if (start + len == npos) {
+      // this chunk holds the position: append the rotated k and v (fp16)
+      const size_t at = (size_t)bi * p.seq_stride + ((size_t)kvh * p.cap + pos) * HD;
+      const float *kr = row + (size_t)(p.h + kvh) * HD, *vr = row + (size_t)(p.h + p.hk + kvh) * HD;
+      if (t < (int)r2) {
+        float o0, o1;
+        rope_pair(kr[t], kr[t + r2], p.cos_t[(size_t)pos * r2 + t], p.sin_t[(size_t)pos * r2 + t], o0, o1);
+        p.kw[at + t] = __float2half_rn(o0);
+        p.kw[at + t + r2] = __float2half_rn(o1);
+      }
+      p.vw[at + t] = __float2half_rn(vr[t]);
+    }
+  } else {
+    for (int i = t; i < G * HD; i += 128) qs[i] = p.q[((size_t)bi * p.h + h0) * HD + i];
+  }
   __syncthreads();
 
   float qr[G][4];
@@ -86,14 +153,14 @@ __global__ void __launch_bounds__(128) k_attn_split(AttnParams p) {
     }
     if (lane == 0) {
 #pragma unroll
-      for (int g = 0; g < G; g++) sc[g * p.chunk + i] = part[g] * p.inv_scale;
+      for (int g = 0; g < G; g++) sc[g * chunk + i] = part[g] * p.inv_scale;
     }
   }
   __syncthreads();
 
   // Chunk softmax statistics; warp w handles heads w, w+4, ...
   for (int g = warp; g < G; g += 4) {
-    float *s = sc + g * p.chunk;
+    float *s = sc + g * chunk;
     float m = -INFINITY;
     for (uint32_t i = lane; i < len; i += 32) m = fmaxf(m, s[i]);
     m = warp_max(m);
@@ -120,7 +187,7 @@ __global__ void __launch_bounds__(128) k_attn_split(AttnParams p) {
     float2 v = __half22float2(*reinterpret_cast<const __half2 *>(vb + (size_t)i * HD + 2 * dp));
 #pragma unroll
     for (int g = 0; g < G; g++) {
-      float e = sc[g * p.chunk + i];
+      float e = sc[g * chunk + i];
       acc[g][0] = fmaf(e, v.x, acc[g][0]);
       acc[g][1] = fmaf(e, v.y, acc[g][1]);
     }
@@ -140,22 +207,36 @@ __global__ void __launch_bounds__(128) k_attn_split(AttnParams p) {
       p.ml[slot * 2 + 1] = mls[g][1];
     }
   }
+  if (!STEP) return;
+  // the last chunk of this (sequence, kv head) to finish merges all chunks
+  __threadfence();
+  __syncthreads();
+  const uint32_t ns = (npos + chunk - 1) / chunk;
+  if (t == 0) ticket = atomicAdd(&p.cnt[bi * p.hk + kvh], 1u);
+  __syncthreads();
+  if (ticket != ns - 1) return;
+  __threadfence();
+  for (int g = 0; g < G; g++) {
+    const float v = merge_chunks(p, bi, h0 + g, ns, (uint32_t)t);
+    p.out[((size_t)bi * p.h + h0 + g) * HD + t] = v;
+    // head h0+g covers elements 128(h0+g).. of the attention output: warp w holds block 4(h0+g)+w
+    if (p.xo.limbs) xq_store_block(p.xo, bi, (h0 + g) * 4 + warp, v);
+  }
+  if (t == 0) p.cnt[bi * p.hk + kvh] = 0;
 }
 
 __global__ void __launch_bounds__(128) k_attn_combine(AttnParams p) {
+  pdl_trigger();
+  pdl_wait();
   const uint32_t h = blockIdx.x, bi = blockIdx.y, d = threadIdx.x;
   const uint32_t npos = npos_of(p);
-  const uint32_t ns = (npos + p.chunk - 1) / p.chunk;
-  const size_t base = ((size_t)bi * p.h + h) * p.nsplit;
-  float M = -INFINITY;
-  for (uint32_t s = 0; s < ns; s++) M = fmaxf(M, p.ml[(base + s) * 2]);
-  float L = 0.f, o = 0.f;
-  for (uint32_t s = 0; s < ns; s++) {
-    float w = expf(p.ml[(base + s) * 2] - M);
-    L = fmaf(p.ml[(base + s) * 2 + 1], w, L);
-    o = fmaf(p.opart[(base + s) * HD + d], w, o);
-  }
-  p.out[((size_t)bi * p.h + h) * HD + d] = o / L;
+  const uint32_t chunk = chunk_of(p, npos);
+  const uint32_t ns = (npos + chunk - 1) / chunk;
+  const float v = merge_chunks(p, bi, h, ns, d);
+  p.out[((size_t)bi * p.h + h) * HD + d] = v;
+  // head h covers elements 128h..128h+127 of the attention output: warp w
+  // holds block 4h+w
+  if (p.xo.limbs) xq_store_block(p.xo, bi, h * 4 + (d >> 5), v);
 }
 
 // Prefill: one CTA per (position, head).
@@ -199,42 +280,44 @@ __global__ void __launch_bounds__(128) k_attention_f32(uint32_t h, uint32_t hk, 
   }
 }
 
-template <int G>
-pai_status_t launch_split(const AttnParams &p, uint32_t batch, cudaStream_t s) {
-  size_t smem = (size_t)(G * HD + G * p.chunk) * sizeof(float);
+template <int G, bool STEP = false>
+pai_status_t launch_split(pai_b200_ctx_t *ctx, const AttnParams &p, uint32_t batch) {
+  const size_t smem = (size_t)(G * HD + G * p.chunk) * sizeof(float);
+  if (smem > 200 * 1024) return b200_fail(PAI_ERR_UNSUPPORTED, "attn_decode: chunk of %u positions", p.chunk);
   if (smem > 48 * 1024) {
     pai_status_t st = b200_cuda(
-        cudaFuncSetAttribute(k_attn_split<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+        cudaFuncSetAttribute(k_attn_split<G, STEP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
         "k_attn_split smem attribute");
     if (st) return st;
   }
-  k_attn_split<G><<<dim3(p.hk, p.nsplit, batch), 128, smem, s>>>(p);
+  b200_launch(ctx, k_attn_split<G, STEP>, dim3(p.hk, p.nsplit, batch), dim3(128), smem, p);
   return PAI_OK;
 }
 
-}  // namespace
-
-extern "C" pai_status_t b200_launch_attn_decode(pai_b200_ctx_t *ctx, uint32_t batch, uint32_t h, uint32_t hk,
-                                                uint32_t hd, const int32_t *pos, uint64_t npos_host,
-                                                uint64_t max_npos, uint64_t cap, uint64_t seq_stride,
-                                                const float *q, const uint16_t *kc, const uint16_t *vc,
-                                                float *out) {
+// Common set-up. With a device position (pos), nsplit is fixed here so that
+// about two CTAs per SM work at the longest context and the kernels cut
+// the current length into nsplit even chunks; with a host length, chunks
+// are sized from it directly.
+pai_status_t attn_setup(pai_b200_ctx_t *ctx, uint32_t batch, uint32_t h, uint32_t hk, uint32_t hd,
+                        const int32_t *pos, uint64_t npos_host, uint64_t max_npos, uint64_t cap, uint64_t seq_stride,
+                        float *out, const b200_xq_t *xq_out, AttnParams &p, uint32_t &G) {
   if (hd != HD) return b200_fail(PAI_ERR_UNSUPPORTED, "attn_decode: head_dim %u (this kernel takes 128)", hd);
   if (hk == 0 || h % hk) return b200_fail(PAI_ERR_INVALID_ARG, "attn_decode: heads %u / kv heads %u", h, hk);
-  uint32_t G = h / hk;
+  G = h / hk;
   if (G != 1 && G != 2 && G != 4 && G != 8)
     return b200_fail(PAI_ERR_UNSUPPORTED, "attn_decode: %u query heads per kv head", G);
   if (max_npos == 0 || max_npos > cap) return b200_fail(PAI_ERR_INVALID_ARG, "attn_decode: positions > cache");
-  // Chunk so that about two CTAs per SM are busy at the longest context.
-  uint64_t want = (max_npos * hk * batch + 295) / 296;
-  uint32_t chunk = (uint32_t)(((want + 31) / 32) * 32);
-  if (chunk < 32) chunk = 32;
-  if (chunk > 4096) chunk = 4096;
-  uint32_t nsplit = (uint32_t)((max_npos + chunk - 1) / chunk);
-  AttnParams p{};
-  p.q = q;
-  p.kc = (const __half *)kc;
-  p.vc = (const __half *)vc;
+  uint32_t chunk, nsplit;
+  if (pos) {
+    const uint64_t by_sms = (296 + (uint64_t)hk * batch - 1) / ((uint64_t)hk * batch);
+    nsplit = (uint32_t)std::max<uint64_t>(1, std::min<uint64_t>((max_npos + 31) / 32, by_sms));
+    chunk = (uint32_t)std::max<uint64_t>(32, ((max_npos + nsplit - 1) / nsplit + 31) / 32 * 32);
+  } else {
+    const uint64_t want = (max_npos * hk * batch + 295) / 296;
+    chunk = (uint32_t)std::min<uint64_t>(4096, std::max<uint64_t>(32, (want + 31) / 32 * 32));
+    nsplit = (uint32_t)((max_npos + chunk - 1) / chunk);
+  }
+  p = AttnParams{};
   p.out = out;
   p.pos = pos;
   p.npos_host = (uint32_t)npos_host;
@@ -245,23 +328,69 @@ extern "C" pai_status_t b200_launch_attn_decode(pai_b200_ctx_t *ctx, uint32_t ba
   p.cap = cap;
   p.seq_stride = seq_stride;
   p.inv_scale = 1.0f / sqrtf((float)hd);
-  uint64_t slots = (uint64_t)batch * h * nsplit;
+  if (xq_out) p.xo = *xq_out;
+  const uint64_t slots = (uint64_t)batch * h * nsplit;
   float *scratch;
   uint32_t *counters;
-  pai_status_t st = b200_ctx_scratch(ctx, slots * (HD + 2), 0, &scratch, &counters);
+  pai_status_t st = b200_ctx_scratch(ctx, slots * (HD + 2), batch * hk, &scratch, &counters);
   if (st) return st;
   p.opart = scratch;
   p.ml = scratch + slots * HD;
-  cudaStream_t s = (cudaStream_t)b200_ctx_stream(ctx);
+  p.cnt = counters;
+  return PAI_OK;
+}
+
+}  // namespace
+
+extern "C" pai_status_t b200_launch_attn_decode(pai_b200_ctx_t *ctx, uint32_t batch, uint32_t h, uint32_t hk,
+                                                uint32_t hd, const int32_t *pos, uint64_t npos_host,
+                                                uint64_t max_npos, uint64_t cap, uint64_t seq_stride,
+                                                const float *q, const uint16_t *kc, const uint16_t *vc,
+                                                float *out, const b200_xq_t *xq_out) {
+  AttnParams p;
+  uint32_t G;
+  pai_status_t st = attn_setup(ctx, batch, h, hk, hd, pos, npos_host, max_npos, cap, seq_stride, out, xq_out, p, G);
+  if (st) return st;
+  p.q = q;
+  p.kc = (const __half *)kc;
+  p.vc = (const __half *)vc;
   switch (G) {
-    case 1: st = launch_split<1>(p, batch, s); break;
-    case 2: st = launch_split<2>(p, batch, s); break;
-    case 4: st = launch_split<4>(p, batch, s); break;
-    default: st = launch_split<8>(p, batch, s); break;
+    case 1: st = launch_split<1>(ctx, p, batch); break;
+    case 2: st = launch_split<2>(ctx, p, batch); break;
+    case 4: st = launch_split<4>(ctx, p, batch); break;
+    default: st = launch_split<8>(ctx, p, batch); break;
   }
   if (st) return st;
-  k_attn_combine<<<dim3(h, batch), HD, 0, s>>>(p);
+  b200_launch(ctx, k_attn_combine, dim3(h, batch), dim3(HD), 0, p);
   return b200_launched(ctx, 2, "k_attn_decode");
+}
+
+extern "C" pai_status_t b200_launch_attn_step(pai_b200_ctx_t *ctx, uint32_t batch, uint32_t h, uint32_t hk,
+                                              uint32_t hd, const int32_t *pos, uint64_t max_npos, uint64_t cap,
+                                              uint64_t seq_stride, const float *qkv, const float *cos_t,
+                                              const float *sin_t, uint16_t *kc, uint16_t *vc, float *out,
+                                              const b200_xq_t *xq_out) {
+  if (!pos || !qkv || !cos_t || !sin_t || !kc || !vc || !out)
+    return b200_fail(PAI_ERR_INVALID_ARG, "attn_step: NULL pointer");
+  AttnParams p;
+  uint32_t G;
+  pai_status_t st = attn_setup(ctx, batch, h, hk, hd, pos, 0, max_npos, cap, seq_stride, out, xq_out, p, G);
+  if (st) return st;
+  p.qkv = qkv;
+  p.cos_t = cos_t;
+  p.sin_t = sin_t;
+  p.kc = (const __half *)kc;
+  p.vc = (const __half *)vc;
+  p.kw = (__half *)kc;
+  p.vw = (__half *)vc;
+  switch (G) {
+    case 1: st = launch_split<1, true>(ctx, p, batch); break;
+    case 2: st = launch_split<2, true>(ctx, p, batch); break;
+    case 4: st = launch_split<4, true>(ctx, p, batch); break;
+    default: st = launch_split<8, true>(ctx, p, batch); break;
+  }
+  if (st) return st;
+  return b200_launched(ctx, 1, "k_attn_split(step)");
 }
 
 extern "C" pai_status_t pai_b200_attn_decode_f16kv(pai_b200_ctx_t *ctx, uint64_t h, uint64_t hk, uint64_t hd,
@@ -271,7 +400,7 @@ extern "C" pai_status_t pai_b200_attn_decode_f16kv(pai_b200_ctx_t *ctx, uint64_t
   if (h == 0 || hk == 0 || npos == 0 || npos > cap || h > 4096 || cap > 0x7FFFFFFFull)
     return b200_fail(PAI_ERR_INVALID_ARG, "attn_decode: shape");
   return b200_launch_attn_decode(ctx, 1, (uint32_t)h, (uint32_t)hk, (uint32_t)hd, nullptr, npos, npos, cap, 0,
-                                 q, kcache, vcache, out);
+                                 q, kcache, vcache, out, nullptr);
 }
 
 extern "C" pai_status_t pai_b200_attention_f32(pai_b200_ctx_t *ctx, uint64_t h, uint64_t hk, uint64_t seq,
@@ -382,14 +511,13 @@ extern "C" pai_status_t pai_b200_attn_decode_f16kv_noalloc(pai_b200_ctx_t *ctx, 
   p.inv_scale = 1.0f / sqrtf((float)hd);
   p.opart = scratch;
   p.ml = scratch + h * nsplit * HD;
-  cudaStream_t s = (cudaStream_t)b200_ctx_stream(ctx);
   switch (G) {
-    case 1: st = launch_split<1>(p, 1, s); break;
-    case 2: st = launch_split<2>(p, 1, s); break;
-    case 4: st = launch_split<4>(p, 1, s); break;
-    default: st = launch_split<8>(p, 1, s); break;
+    case 1: st = launch_split<1>(ctx, p, 1); break;
+    case 2: st = launch_split<2>(ctx, p, 1); break;
+    case 4: st = launch_split<4>(ctx, p, 1); break;
+    default: st = launch_split<8>(ctx, p, 1); break;
   }
   if (st) return st;
-  k_attn_combine<<<dim3((unsigned)h, 1), HD, 0, s>>>(p);
+  b200_launch(ctx, k_attn_combine, dim3((unsigned)h, 1), dim3(HD), 0, p);
   return b200_launched(ctx, 2, "k_attn_decode_noalloc");
 }

@@ -1,24 +1,47 @@
-// Fused dequantise-and-dot GEMV over the packed Q4_0 / Q8_0 / Q4_K layout.
+// Fused dequantise-and-dot GEMV on the int8 tensor cores.
 //
-// Mapping: one CTA = one group of 32 output rows x a contiguous range of
-// K blocks; lane l of every warp owns row l of the group, the 8 warps
-// stride over the CTA's blocks. Each lane reads its row's block with
-// 128-bit loads that are coalesced across the warp (the packed layout
-// puts chunk c of the 32 rows of a group side by side), unpacks nibbles
-// or bytes to exact fp32 in registers, and accumulates sum_j q_j * x_j
-// per block before applying the block scale once. x for the CTA's
-// K-range is staged in shared memory and read as warp-wide broadcasts.
-// Warps are reduced through shared memory in a fixed order; when K is
-// split across several CTAs, each writes its partial row sums to scratch
-// and the last CTA to arrive (an atomic ticket per row group) adds them
-// in split order and applies the epilogue, so results do not depend on
-// scheduling.
+// Each consumer warp owns one 16-row tile of W and walks K in units (4
+// blocks of Q4_0/Q8_0, one Q4_K super-block). For every 32-weight block it
+// issues one m16n8k32 int8 MMA: A = the tile's 16 x 32 quant codes,
+// unpacked from the packed bytes with two LOP3s per word (Q4_0/Q4_K
+// nibbles) or used as-is (Q8_0); B = x in 24-bit fixed point, three int8
+// digit columns per vector (two vectors per MMA). The integer products are
+// exact; each lane folds its two accumulator columns into one integer,
+// converts it once, and applies the block's scales in fp32:
+//   sum_j w_j x_j = d * (s_b * sum_j q_j X_j  - 8 s_b sum_j X_j)   (Q4_0)
+//                 = d * s_b * sum_j q_j X_j                         (Q8_0)
+//                 = d sc_s * s_b sum q X - dmin m_s * s_b sum X     (Q4_K)
+// so the per-weight work is the unpack plus 1/16 of an MMA, instead of an
+// unpack, convert and FMA per weight on the CUDA cores.
 //
-// Reference semantics: y = W.x with W = dequant_block(...) rows
-// (adapters/llama/gguf.c:680-693, 750-761, 852-882) and the dot of
-// pai_ref_gemv_f32 (cpu/reference/ref_ops.c:92-106); the epilogues fuse
-// the executor's residual PAI_OP_ADD and the SILU -> MUL pair of the
-// LLaMA MLP (adapters/llama/llama.c:747-749, 774-795).
+// Memory pipeline (warp-specialised): the CTA's 8 consumer warps own the 8
+// tiles of a 128-row group, and in the unit-major packed layout the group's
+// tiles of one K unit are one contiguous run of bytes. One producer thread
+// streams those runs (two bulk asynchronous copies per unit: codes and
+// headers; cp.async.bulk, completion on an mbarrier per stage, no
+// multicast) into a 4-stage ring shared by the consumers, which only
+// unpack, multiply and accumulate from shared memory. Work is split
+// stream-K style: the (group, unit) pairs are numbered group-major and CTA
+// i takes the i-th contiguous share, so every CTA streams the same number
+// of bytes. x (digits and scales) is staged in shared memory: all of it
+// once per CTA when the CTA reuses it across groups, else per sub-item in
+// three rotating slots filled one sub-item ahead. Under programmatic
+// dependent launch the producer fills the ring before it waits for the
+// previous kernel: weights never depend on it.
+//
+// Split-K is deterministic: a CTA that holds part of a group parks its
+// partial row sums in scratch, and at the end of its range the last part
+// of a tile to arrive (atomic ticket per tile) adds them in CTA order.
+// Epilogues: plain store, residual add (the executor's following
+// PAI_OP_ADD, adapters/llama/llama.c:747-749,793-795), and SiLU(gate)*up
+// (llama.c:774-781); for the latter the last tile of each 64-row group
+// (ticket per group) also re-quantises the group's 32 outputs for the down
+// projection. Every mbarrier wait is bounded; on timeout the kernel raises
+// the context's error flag (reported as PAI_ERR_TIMEOUT), waits (bounded)
+// for its copies in flight and stops.
+// Reference result: dequant_block rows (adapters/llama/gguf.c:680-693,
+// 750-761, 852-882) dotted as in pai_ref_gemv_f32 (cpu/reference/ref_ops.c:92-106).
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -28,436 +51,863 @@
 
 namespace {
 
-constexpr int kWarps = 8;
-constexpr int kThreads = kWarps * 32;
+constexpr int kCons = 8;                     // consumer warps per CTA, one 16-row tile each
+constexpr int kThreads = (kCons + 1) * 32;  // + one producer warp
+constexpr int kStages = 4;                   // depth of the CTA's weight ring
+constexpr int kXSlots = 3;                   // staged-x slots (current, next, one being released)
+// One CTA per SM, two for batch <= 2 (whose consumers need few registers)
+// so twice the warps hide the unpack-MMA-scale latency.
+template <int NT>
+constexpr int kCtasPerSm = NT == 1 ? 2 : 1;
+template <int NT>
+constexpr size_t kSmemCap = NT == 1 ? 110 * 1024 : 220 * 1024;  // dynamic shared memory per CTA
+constexpr uint32_t M4 = 0x0F0F0F0Fu;
+constexpr uint64_t kWaitLimit = 2000000000ull;  // ns before a wait gives up (2 s)
 
-struct GemvParams {
-  const uint8_t *qs;
-  const uint8_t *sc;
-  const float *x;    // [batch][k]
-  const float *res;  // [batch][n] or null
+struct GemvP {
+  const uint8_t *qs, *sc;
+  b200_xq_t xq;  // input activations (xnorm: only batch, k and quads are used)
+  const float *res;
   float *y;
-  float *partial;    // [kcta][batch][npad]
-  uint32_t *counters;
-  uint32_t n, k, nb, ngroups, kcta, bpc, npad;
+  float *partial;        // [segment][batch][npad] split-K partial sums
+  uint32_t *tile_cnt;    // split-K tickets, one per tile, left at zero
+  uint32_t *grp_cnt;     // SILU_GLU re-quantisation tickets, one per 64-row group
+  uint32_t *err;         // host-mapped error word (timeouts)
+  b200_xq_t xo;          // SILU_GLU: re-quantised output (limbs == nullptr: none)
+  uint32_t n, nout, units, ntiles, ngroups, upc, batch, npad;
+  uint32_t resident;     // 1: all of x staged once per CTA (slot 0)
+  uint32_t xslot_bytes;  // bytes of one staged-x slot
   int epi;
+  // xnorm: x arrives in fp32 and each CTA applies RMSNorm (gamma, eps) and
+  // quantises it into its resident x slot itself (no xq input, no norm kernel)
+  int xnorm;
+  const float *xf, *gamma;
+  float eps;
 };
 
-// Magic constants: a 0..255 field OR'ed into the mantissa of 2^23 gives
-// the exact float 2^23 + v; subtracting 2^23 + bias leaves v - bias.
-constexpr float kM = 8388608.0f;
-
-// byte i of w (i = 0..3) placed in bits 0..7 of 0x4B000000
-__device__ __forceinline__ float byte_f(uint32_t w, int i, float bias) {
-  return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540u + (uint32_t)i)) - bias;
+__device__ __forceinline__ uint32_t comp(const uint4 &v, int i) {
+  return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
+}
+__device__ __forceinline__ float comp(const float4 &v, int i) {
+  return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
+}
+__device__ __forceinline__ float half_at(const uint2 &v, int i) {
+  uint32_t w = (i < 2) ? v.x : v.y;
+  return __half2float(__ushort_as_half((uint16_t)((i & 1) ? (w >> 16) : (w & 0xFFFFu))));
 }
 
+// Activation operand: the CTA's staged copy of the xq digits and block
+// scales for the K range of the current sub-item: digits [pair][quad][1024 B],
+// then sb and sx, each [vec][quad*4] floats.
+struct XS {
+  const uint8_t *limbs;
+  const float *sb, *sx;
+  uint32_t quads, batch;
+};
+
+struct XOp {
+  uint4 lo, hi;
+  float4 sb, sx;
+};
+
+__device__ __forceinline__ void load_x(const XS &xs, uint32_t nt, uint32_t qq, int lane, XOp &o) {
+  const uint8_t *l = xs.limbs + ((size_t)nt * xs.quads + qq) * 1024 + lane * 16;
+  o.lo = *reinterpret_cast<const uint4 *>(l);
+  o.hi = *reinterpret_cast<const uint4 *>(l + 512);
+  const uint32_t vec = 2 * nt + ((lane & 3) >> 1);
+  if (vec < xs.batch) {
+    o.sb = *reinterpret_cast<const float4 *>(xs.sb + ((size_t)vec * xs.quads + qq) * 4);
+    o.sx = *reinterpret_cast<const float4 *>(xs.sx + ((size_t)vec * xs.quads + qq) * 4);
+  } else {
+    o.sb = make_float4(0.f, 0.f, 0.f, 0.f);
+    o.sx = o.sb;
+  }
+}
+
+// Fold a lane's two accumulator columns: even lanes hold (L2, L1) sums,
+// odd lanes (L0, 0); 256*c_even + c_odd/256 over the lane pair is
+// sum_j q_j X_j. |c| < 2^16, so the folded integer (< 2^24) converts exactly.
+__device__ __forceinline__ float fold(int c_a, int c_b) { return (float)(c_a * 256 + c_b); }
+
 template <uint32_t T>
-struct Block;
+struct Unit;
 
-// Q4_0: 16 bytes of nibbles; byte j holds element j (low) and j+16 (high).
+// Q4_0: unit = 4 blocks; qs: chunk h = word c of row r+8h for blocks 0..3;
+// sc: [16 rows][4 blocks] fp16.
 template <>
-struct Block<PAI_B200_Q4_0> {
-  static constexpr uint32_t EL = 32, CH = 1, U = 4;
-  struct Raw {
-    uint4 q;
-    uint16_t d;
-  };
-  __device__ static void load(const GemvParams &p, uint32_t g, uint32_t b, int lane, Raw &r) {
-    size_t tile = (size_t)g * p.nb + b;
-    r.q = ldg_stream(p.qs + (tile * 32 + lane) * 16);
-    r.d = ldg_u16(p.sc + (tile * 32 + lane) * 2);
-  }
-  template <int B>
-  __device__ static void dot(const Raw &r, const float *xb, uint32_t xstride, float (&acc)[B]) {
-    float w[32];
-    const uint32_t q[4] = {r.q.x, r.q.y, r.q.z, r.q.w};
+struct Unit<PAI_B200_Q4_0> {
+  static constexpr int U = 2;  // units per pipeline stage
+  static constexpr uint32_t QB = 1024, SB = 128;
+  static constexpr int XPU = 1;  // x-quads per unit
+  template <int NT>
+  __device__ static void compute(const uint8_t *qs, const uint8_t *sc, const XS &xs, uint32_t qq, int lane,
+                                 float (&yr)[NT], float (&yr8)[NT]) {
+    XOp x[NT];
 #pragma unroll
-    for (int wi = 0; wi < 4; wi++) {
-      uint32_t lo = q[wi] & 0x0F0F0F0Fu;
-      uint32_t hi = (q[wi] >> 4) & 0x0F0F0F0Fu;
-#pragma unroll
-      for (int i = 0; i < 4; i++) {
-        w[4 * wi + i] = byte_f(lo, i, kM + 8.0f);
-        w[16 + 4 * wi + i] = byte_f(hi, i, kM + 8.0f);
-      }
-    }
-    float d = __half2float(__ushort_as_half(r.d));
-#pragma unroll
-    for (int bi = 0; bi < B; bi++) {
-      const float4 *x4 = reinterpret_cast<const float4 *>(xb + bi * xstride);
-      float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-      for (int j = 0; j < 8; j += 2) {
-        float4 a = x4[j], c = x4[j + 1];
-        s0 = fmaf(w[4 * j + 0], a.x, s0);
-        s0 = fmaf(w[4 * j + 1], a.y, s0);
-        s0 = fmaf(w[4 * j + 2], a.z, s0);
-        s0 = fmaf(w[4 * j + 3], a.w, s0);
-        s1 = fmaf(w[4 * j + 4], c.x, s1);
-        s1 = fmaf(w[4 * j + 5], c.y, s1);
-        s1 = fmaf(w[4 * j + 6], c.z, s1);
-        s1 = fmaf(w[4 * j + 7], c.w, s1);
-      }
-      acc[bi] = fmaf(d, s0 + s1, acc[bi]);
-    }
-  }
-};
-
-// Q8_0: 32 signed bytes in two chunks.
-template <>
-struct Block<PAI_B200_Q8_0> {
-  static constexpr uint32_t EL = 32, CH = 2, U = 2;
-  struct Raw {
-    uint4 q[2];
-    uint16_t d;
-  };
-  __device__ static void load(const GemvParams &p, uint32_t g, uint32_t b, int lane, Raw &r) {
-    size_t tile = (size_t)g * p.nb + b;
-    r.q[0] = ldg_stream(p.qs + ((tile * 2 + 0) * 32 + lane) * 16);
-    r.q[1] = ldg_stream(p.qs + ((tile * 2 + 1) * 32 + lane) * 16);
-    r.d = ldg_u16(p.sc + (tile * 32 + lane) * 2);
-  }
-  template <int B>
-  __device__ static void dot(const Raw &r, const float *xb, uint32_t xstride, float (&acc)[B]) {
-    float w[32];
-#pragma unroll
-    for (int c = 0; c < 2; c++) {
-      const uint32_t q[4] = {r.q[c].x ^ 0x80808080u, r.q[c].y ^ 0x80808080u, r.q[c].z ^ 0x80808080u,
-                             r.q[c].w ^ 0x80808080u};
-#pragma unroll
-      for (int wi = 0; wi < 4; wi++)
-#pragma unroll
-        for (int i = 0; i < 4; i++) w[16 * c + 4 * wi + i] = byte_f(q[wi], i, kM + 128.0f);
-    }
-    float d = __half2float(__ushort_as_half(r.d));
-#pragma unroll
-    for (int bi = 0; bi < B; bi++) {
-      const float4 *x4 = reinterpret_cast<const float4 *>(xb + bi * xstride);
-      float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-      for (int j = 0; j < 8; j += 2) {
-        float4 a = x4[j], c = x4[j + 1];
-        s0 = fmaf(w[4 * j + 0], a.x, s0);
-        s0 = fmaf(w[4 * j + 1], a.y, s0);
-        s0 = fmaf(w[4 * j + 2], a.z, s0);
-        s0 = fmaf(w[4 * j + 3], a.w, s0);
-        s1 = fmaf(w[4 * j + 4], c.x, s1);
-        s1 = fmaf(w[4 * j + 5], c.y, s1);
-        s1 = fmaf(w[4 * j + 6], c.z, s1);
-        s1 = fmaf(w[4 * j + 7], c.w, s1);
-      }
-      acc[bi] = fmaf(d, s0 + s1, acc[bi]);
-    }
-  }
-};
-
-// Q4_K: 128 bytes of nibbles in 8 chunks plus a 16-byte header
-// {d, dmin, scales[12]}. Chunk t holds bytes 16t..16t+15 of qs; byte l
-// of 64-group c = t/2 holds element 64c+l (sub-block 2c, low nibble) and
-// 64c+32+l (sub-block 2c+1, high nibble). Per sub-block s the weight is
-// (d*sc_s)*q - dmin*m_s, so W.x = sum_s d*sc_s * (q.x)_s - dmin*m_s * (sum x)_s,
-// with the sub-block sums of x precomputed when x is staged.
-template <>
-struct Block<PAI_B200_Q4_K> {
-  static constexpr uint32_t EL = 256, CH = 8, U = 1;
-  struct Raw {
-    uint4 q[8];
-    uint4 h;
-  };
-  __device__ static void load(const GemvParams &p, uint32_t g, uint32_t b, int lane, Raw &r) {
-    size_t tile = (size_t)g * p.nb + b;
-#pragma unroll
-    for (int c = 0; c < 8; c++) r.q[c] = ldg_stream(p.qs + ((tile * 8 + c) * 32 + lane) * 16);
-    r.h = ldg_stream(p.sc + (tile * 32 + lane) * 16);
-  }
-  template <int B>
-  __device__ static void dot(const Raw &r, const float *xb, uint32_t xstride, const float *xsum,
-                             uint32_t sstride, float (&acc)[B]) {
-    float d = __half2float(__ushort_as_half((uint16_t)(r.h.x & 0xFFFFu)));
-    float dmin = __half2float(__ushort_as_half((uint16_t)(r.h.x >> 16)));
-    uint8_t s12[12];
+    for (int nt = 0; nt < NT; nt++) load_x(xs, nt, qq, lane, x[nt]);
+    const uint4 a0 = *reinterpret_cast<const uint4 *>(qs + lane * 16);
+    const uint4 a1 = *reinterpret_cast<const uint4 *>(qs + 512 + lane * 16);
+    const uint2 d0 = *reinterpret_cast<const uint2 *>(sc + (lane >> 2) * 8);
+    const uint2 d1 = *reinterpret_cast<const uint2 *>(sc + 64 + (lane >> 2) * 8);
+    const float lscale = (lane & 1) ? (1.0f / 256.0f) : 256.0f;
+    const float cmul = (lane & 1) ? 0.0f : 8.0f;  // the -8 offset of Q4_0 codes, once per lane pair
 #pragma unroll
     for (int i = 0; i < 4; i++) {
-      s12[i] = (uint8_t)(r.h.y >> (8 * i));
-      s12[4 + i] = (uint8_t)(r.h.z >> (8 * i));
-      s12[8 + i] = (uint8_t)(r.h.w >> (8 * i));
-    }
-    float dsc[8], dmm[8];
+      const uint32_t wr = comp(a0, i), wr8 = comp(a1, i);
+      const uint32_t A0 = wr & M4, A1 = wr8 & M4, A2 = (wr >> 4) & M4, A3 = (wr8 >> 4) & M4;
+      const float dr = half_at(d0, i), dr8 = half_at(d1, i);
 #pragma unroll
-    for (int j = 0; j < 8; j++) {
-      uint8_t s, m;
-      k4_scale_min(j, s12, &s, &m);
-      dsc[j] = d * (float)s;
-      dmm[j] = dmin * (float)m;
-    }
-#pragma unroll
-    for (int bi = 0; bi < B; bi++) {
-      const float *xr = xb + bi * xstride;
-      float tot = 0.f;
-#pragma unroll
-      for (int c = 0; c < 4; c++) {
-        float slo = 0.f, shi = 0.f;
-#pragma unroll
-        for (int half = 0; half < 2; half++) {
-          const uint4 qq = r.q[2 * c + half];
-          const uint32_t q[4] = {qq.x, qq.y, qq.z, qq.w};
-          const float4 *xl = reinterpret_cast<const float4 *>(xr + 64 * c + 16 * half);
-          const float4 *xh = reinterpret_cast<const float4 *>(xr + 64 * c + 32 + 16 * half);
-#pragma unroll
-          for (int wi = 0; wi < 4; wi++) {
-            uint32_t lo = q[wi] & 0x0F0F0F0Fu, hi = (q[wi] >> 4) & 0x0F0F0F0Fu;
-            float4 a = xl[wi], e = xh[wi];
-            slo = fmaf(byte_f(lo, 0, kM), a.x, slo);
-            slo = fmaf(byte_f(lo, 1, kM), a.y, slo);
-            slo = fmaf(byte_f(lo, 2, kM), a.z, slo);
-            slo = fmaf(byte_f(lo, 3, kM), a.w, slo);
-            shi = fmaf(byte_f(hi, 0, kM), e.x, shi);
-            shi = fmaf(byte_f(hi, 1, kM), e.y, shi);
-            shi = fmaf(byte_f(hi, 2, kM), e.z, shi);
-            shi = fmaf(byte_f(hi, 3, kM), e.w, shi);
-          }
-        }
-        const float *xs8 = xsum + bi * sstride;
-        tot = fmaf(dsc[2 * c], slo, tot);
-        tot = fmaf(dsc[2 * c + 1], shi, tot);
-        tot = fmaf(-dmm[2 * c], xs8[2 * c], tot);
-        tot = fmaf(-dmm[2 * c + 1], xs8[2 * c + 1], tot);
+      for (int nt = 0; nt < NT; nt++) {
+        int acc[4];
+        mma_u8s8(acc, A0, A1, A2, A3, comp(x[nt].lo, i), comp(x[nt].hi, i));
+        const float sl = comp(x[nt].sb, i) * lscale;
+        const float cr = comp(x[nt].sx, i) * cmul;
+        yr[nt] = fmaf(dr, fmaf(sl, fold(acc[0], acc[1]), -cr), yr[nt]);
+        yr8[nt] = fmaf(dr8, fmaf(sl, fold(acc[2], acc[3]), -cr), yr8[nt]);
       }
-      acc[bi] += tot;
     }
   }
 };
 
-template <uint32_t T, int B>
-__global__ void __launch_bounds__(kThreads, 2) k_gemv(GemvParams p) {
-  using Blk = Block<T>;
-  constexpr uint32_t EL = Blk::EL, U = Blk::U;
-  extern __shared__ __align__(16) float xs[];
-  __shared__ float red[kWarps][B][32];
-  __shared__ int is_last;
-
-  const uint32_t g = blockIdx.x, ks = blockIdx.y;
-  const uint32_t b0 = ks * p.bpc;
-  const uint32_t b1 = min(p.nb, b0 + p.bpc);
-  const uint32_t nblk = b1 - b0;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const uint32_t xstride = p.bpc * EL;
-  float *xsum = xs + B * xstride;  // Q4_K: [B][bpc*8] sub-block sums
-
-  // Stage this CTA's K-range of x (all batch rows).
-  for (int bi = 0; bi < B; bi++) {
-    const float4 *src = reinterpret_cast<const float4 *>(p.x + (size_t)bi * p.k + (size_t)b0 * EL);
-    float4 *dst = reinterpret_cast<float4 *>(xs + bi * xstride);
-    for (uint32_t i = threadIdx.x; i < nblk * EL / 4; i += kThreads) dst[i] = src[i];
-  }
-  if constexpr (T == PAI_B200_Q4_K) {
-    __syncthreads();
-    for (uint32_t i = threadIdx.x; i < B * nblk * 8; i += kThreads) {
-      uint32_t bi = i / (nblk * 8), j = i % (nblk * 8);
-      const float *v = xs + bi * xstride + j * 32;
-      float s = 0.f;
+// Q8_0: unit = 4 blocks; qs: chunk 2h+p = bytes 16p+4c.. of row r+8h.
+template <>
+struct Unit<PAI_B200_Q8_0> {
+  static constexpr int U = 1;
+  static constexpr uint32_t QB = 2048, SB = 128;
+  static constexpr int XPU = 1;
+  template <int NT>
+  __device__ static void compute(const uint8_t *qs, const uint8_t *sc, const XS &xs, uint32_t qq, int lane,
+                                 float (&yr)[NT], float (&yr8)[NT]) {
+    XOp x[NT];
 #pragma unroll
-      for (int e = 0; e < 32; e++) s += v[e];
-      xsum[bi * p.bpc * 8 + j] = s;
-    }
-  }
-  __syncthreads();
-
-  float acc[B];
+    for (int nt = 0; nt < NT; nt++) load_x(xs, nt, qq, lane, x[nt]);
+    uint4 a[4];
 #pragma unroll
-  for (int bi = 0; bi < B; bi++) acc[bi] = 0.f;
-
-  for (uint32_t base = b0 + warp; base < b1; base += kWarps * U) {
-    typename Blk::Raw raw[U];
+    for (int j = 0; j < 4; j++) a[j] = *reinterpret_cast<const uint4 *>(qs + j * 512 + lane * 16);
+    const uint2 d0 = *reinterpret_cast<const uint2 *>(sc + (lane >> 2) * 8);
+    const uint2 d1 = *reinterpret_cast<const uint2 *>(sc + 64 + (lane >> 2) * 8);
+    const float lscale = (lane & 1) ? (1.0f / 256.0f) : 256.0f;
 #pragma unroll
-    for (uint32_t u = 0; u < U; u++) {
-      uint32_t b = base + u * kWarps;
-      if (b < b1) Blk::load(p, g, b, lane, raw[u]);
-    }
+    for (int i = 0; i < 4; i++) {
+      const uint32_t A0 = comp(a[0], i), A2 = comp(a[1], i), A1 = comp(a[2], i), A3 = comp(a[3], i);
+      const float dr = half_at(d0, i), dr8 = half_at(d1, i);
 #pragma unroll
-    for (uint32_t u = 0; u < U; u++) {
-      uint32_t b = base + u * kWarps;
-      if (b < b1) {
-        const float *xb = xs + (b - b0) * EL;
-        if constexpr (T == PAI_B200_Q4_K)
-          Blk::template dot<B>(raw[u], xb, xstride, xsum + (b - b0) * 8, p.bpc * 8, acc);
-        else
-          Blk::template dot<B>(raw[u], xb, xstride, acc);
+      for (int nt = 0; nt < NT; nt++) {
+        int acc[4];
+        mma_s8s8(acc, A0, A1, A2, A3, comp(x[nt].lo, i), comp(x[nt].hi, i));
+        const float sl = comp(x[nt].sb, i) * lscale;
+        yr[nt] = fmaf(dr * sl, fold(acc[0], acc[1]), yr[nt]);
+        yr8[nt] = fmaf(dr8 * sl, fold(acc[2], acc[3]), yr8[nt]);
       }
     }
   }
+};
 
-#pragma unroll
-  for (int bi = 0; bi < B; bi++) red[warp][bi][lane] = acc[bi];
-  __syncthreads();
-  if (warp != 0) {
-    if (p.kcta == 1) return;
+// Q4_K: unit = one super-block (8 sub-blocks of 32 = 2 x-quads). qs: chunk
+// 2h+p holds, for each 64-group g, bytes 32g+16p+4c.. of row r+8h (low
+// nibbles = sub-block 2g, high = 2g+1); sc: [16 rows][16 B] headers.
+template <>
+struct Unit<PAI_B200_Q4_K> {
+  static constexpr int U = 1;
+  static constexpr uint32_t QB = 2048, SB = 256;
+  static constexpr int XPU = 2;
+  // scale and min of sub-block s from the 12 packed bytes (gguf.c:640-648)
+  __device__ static void scale_min(const uint4 &h, int s, float &dsc, float &dmm) {
+    const float d = __half2float(__ushort_as_half((uint16_t)(h.x & 0xFFFFu)));
+    const float dmin = __half2float(__ushort_as_half((uint16_t)(h.x >> 16)));
+    auto byte = [&](int i) -> uint32_t { return (comp(h, 1 + i / 4) >> (8 * (i % 4))) & 0xFFu; };
+    uint32_t sc, m;
+    if (s < 4) {
+      sc = byte(s) & 63;
+      m = byte(s + 4) & 63;
+    } else {
+      sc = (byte(s + 4) & 0x0F) | ((byte(s - 4) >> 6) << 4);
+      m = (byte(s + 4) >> 4) | ((byte(s) >> 6) << 4);
+    }
+    dsc = d * (float)sc;
+    dmm = dmin * (float)m;
   }
-  float vals[B];
-  if (warp == 0) {
+  template <int NT>
+  __device__ static void compute(const uint8_t *qs, const uint8_t *sc, const XS &xs, uint32_t qq, int lane,
+                                 float (&yr)[NT], float (&yr8)[NT]) {
+    uint4 a[4];
 #pragma unroll
-    for (int bi = 0; bi < B; bi++) {
-      float v = 0.f;
+    for (int j = 0; j < 4; j++) a[j] = *reinterpret_cast<const uint4 *>(qs + j * 512 + lane * 16);
+    const uint4 h0 = *reinterpret_cast<const uint4 *>(sc + (lane >> 2) * 16);
+    const uint4 h1 = *reinterpret_cast<const uint4 *>(sc + 128 + (lane >> 2) * 16);
+    const float lscale = (lane & 1) ? (1.0f / 256.0f) : 256.0f;
+    const float cmul = (lane & 1) ? 0.0f : 1.0f;
 #pragma unroll
-      for (int w = 0; w < kWarps; w++) v += red[w][bi][lane];
-      vals[bi] = v;
+    for (int half = 0; half < 2; half++) {  // x-quads 2u, 2u+1 = sub-blocks 0..3, 4..7
+      XOp x[NT];
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++) load_x(xs, nt, qq + half, lane, x[nt]);
+#pragma unroll
+      for (int gg = 0; gg < 2; gg++) {
+        const int g = 2 * half + gg;
+        const uint32_t w0 = comp(a[0], g), w1 = comp(a[1], g), w2 = comp(a[2], g), w3 = comp(a[3], g);
+#pragma unroll
+        for (int nib = 0; nib < 2; nib++) {
+          const int s = 2 * g + nib;  // sub-block
+          const int i = s & 3;        // block within the x-quad
+          const uint32_t A0 = (w0 >> (4 * nib)) & M4, A2 = (w1 >> (4 * nib)) & M4;
+          const uint32_t A1 = (w2 >> (4 * nib)) & M4, A3 = (w3 >> (4 * nib)) & M4;
+          float dsc, dmm, dsc8, dmm8;
+          scale_min(h0, s, dsc, dmm);
+          scale_min(h1, s, dsc8, dmm8);
+#pragma unroll
+          for (int nt = 0; nt < NT; nt++) {
+            int acc[4];
+            mma_u8s8(acc, A0, A1, A2, A3, comp(x[nt].lo, i), comp(x[nt].hi, i));
+            const float sl = comp(x[nt].sb, i) * lscale;
+            const float sx = comp(x[nt].sx, i) * cmul;
+            yr[nt] = fmaf(dsc, sl * fold(acc[0], acc[1]), fmaf(-dmm, sx, yr[nt]));
+            yr8[nt] = fmaf(dsc8, sl * fold(acc[2], acc[3]), fmaf(-dmm8, sx, yr8[nt]));
+          }
+        }
+      }
     }
   }
-  if (p.kcta > 1) {
-    if (warp == 0) {
-#pragma unroll
-      for (int bi = 0; bi < B; bi++)
-        p.partial[((size_t)ks * B + bi) * p.npad + (size_t)g * 32 + lane] = vals[bi];
-      __threadfence();
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      uint32_t prev = atomicAdd(&p.counters[g], 1u);
-      is_last = (prev == p.kcta - 1);
-    }
-    __syncthreads();
-    if (!is_last || warp != 0) return;
+};
+
+// Work walk shared by the producer and the consumers of a CTA. The flat
+// index pos = group * units + unit runs over all (8-tile group, K unit)
+// pairs; CTA i owns [i*T/G, (i+1)*T/G) (stream-K), cut into sub-items that
+// stay inside one group and hold at most `upc` units (one staged-x slot).
+struct Sub {
+  uint32_t g, u0, u1;
+  bool first, last;  // starts / ends this CTA's segment of group g
+};
+
+// The CTA whose share holds flat position x: the largest i with
+// floor(i*total/grid) <= x.
+__device__ __forceinline__ uint32_t cta_of(uint64_t x, uint64_t total, uint32_t grid) {
+  return (uint32_t)(((x + 1) * grid - 1) / total);
+}
+
+__device__ __forceinline__ Sub sub_at(const GemvP &p, uint64_t pos, uint64_t r0, uint64_t r1) {
+  Sub s;
+  s.g = (uint32_t)(pos / p.units);
+  s.u0 = (uint32_t)(pos - (uint64_t)s.g * p.units);
+  const uint64_t seg_end = min(r1, (uint64_t)(s.g + 1) * p.units);
+  s.u1 = (uint32_t)min((uint64_t)s.u0 + p.upc, seg_end - (uint64_t)s.g * p.units);
+  s.first = (pos == r0) || s.u0 == 0;
+  s.last = (uint64_t)s.g * p.units + s.u1 == seg_end;
+  return s;
+}
+
+// SiLU*up outputs wait for re-quantisation until all 4 tiles of their
+// 64-row group are written (ticket per group); tickets are batched so one
+// fence covers several.
+struct Requant {
+  uint32_t q[4];
+  int n = 0;
+  __device__ void flush(const GemvP &p, int lane) {
+    if (n == 0) return;
     __threadfence();
-#pragma unroll
-    for (int bi = 0; bi < B; bi++) {
-      float v = 0.f;
-      for (uint32_t s = 0; s < p.kcta; s++) v += __ldcg(&p.partial[((size_t)s * B + bi) * p.npad + (size_t)g * 32 + lane]);
-      vals[bi] = v;
-    }
-    if (lane == 0) p.counters[g] = 0;
-  }
-
-  // Epilogue (warp 0 of the finishing CTA).
-  const uint32_t row = g * 32 + lane;
-  if (p.epi == B200_EPI_SILU_GLU) {
-    const uint32_t nout = p.n / 2;
-#pragma unroll
-    for (int bi = 0; bi < B; bi++) {
-      float up = __shfl_down_sync(0xffffffffu, vals[bi], 16);
-      uint32_t orow = g * 16 + lane;
-      if (lane < 16 && orow < nout) {
-        float gate = vals[bi];
-        float sg = __fdiv_rn(gate, __fadd_rn(1.0f, expf(-gate)));
-        p.y[(size_t)bi * nout + orow] = __fmul_rn(sg, up);
+    __syncwarp();
+    for (int i = 0; i < n; i++) {
+      uint32_t ticket = 0;
+      if (lane == 0) ticket = atomicAdd(&p.grp_cnt[q[i]], 1u);
+      ticket = __shfl_sync(0xffffffffu, ticket, 0);
+      if (ticket == 3) {  // the last of the group's 4 tiles quantises outputs 32q..32q+31
+        __threadfence();
+        for (uint32_t vec = 0; vec < p.batch; vec++)
+          xq_store_block(p.xo, vec, q[i], __ldcg(&p.y[(size_t)vec * p.nout + q[i] * 32 + lane]));
+        if (lane == 0) p.grp_cnt[q[i]] = 0;
       }
     }
-  } else if (row < p.n) {
+    n = 0;
+  }
+  __device__ void add(const GemvP &p, int lane, uint32_t group) {
+    if (n == 4) flush(p, lane);
+    q[n++] = group;
+  }
+};
+
+// Final row sums of a tile (holder lanes: rows r and r+8 of vector
+// 2nt + vsel) -> y through the epilogue.
+template <int NT>
+__device__ void finish_tile(const GemvP &p, uint32_t tile, int lane, const float (&ya)[NT], const float (&yb)[NT],
+                            Requant &pend) {
+  const uint32_t r = lane >> 2, vsel = (lane & 3) >> 1;
+  const bool holder = (lane & 1) == 0;
+  if (p.epi == B200_EPI_SILU_GLU) {
+    // rows r (gate) and r+8 (up) of the tile are in the same lane
+    const uint32_t o = tile * 8 + r;
+    if (holder) {
 #pragma unroll
-    for (int bi = 0; bi < B; bi++) {
-      float v = vals[bi];
-      if (p.epi == B200_EPI_RESIDUAL) v = __fadd_rn(p.res[(size_t)bi * p.n + row], v);
-      p.y[(size_t)bi * p.n + row] = v;
+      for (int nt = 0; nt < NT; nt++) {
+        const uint32_t vec = 2 * nt + vsel;
+        if (vec < p.batch && o < p.nout) {
+          const float gate = ya[nt], up = yb[nt];
+          p.y[(size_t)vec * p.nout + o] = __fmul_rn(__fdiv_rn(gate, __fadd_rn(1.0f, expf(-gate))), up);
+        }
+      }
+    }
+    if (p.xo.limbs) pend.add(p, lane, tile / 4);
+    return;
+  }
+  if (!holder) return;
+#pragma unroll
+  for (int nt = 0; nt < NT; nt++) {
+    const uint32_t vec = 2 * nt + vsel;
+    if (vec >= p.batch) continue;
+    const uint32_t row = tile * 16 + r;
+    float a = ya[nt], b = yb[nt];
+    if (p.epi == B200_EPI_RESIDUAL) {
+      if (row < p.n) a = __fadd_rn(p.res[(size_t)vec * p.n + row], a);
+      if (row + 8 < p.n) b = __fadd_rn(p.res[(size_t)vec * p.n + row + 8], b);
+    }
+    if (row < p.n) p.y[(size_t)vec * p.n + row] = a;
+    if (row + 8 < p.n) p.y[(size_t)vec * p.n + row + 8] = b;
+  }
+}
+
+// Take the split-K tickets of this warp's parked tiles; the last part of
+// a tile to arrive adds all parts in CTA order and finishes the tile.
+template <int NT>
+__device__ void settle_splits(const GemvP &p, uint32_t (&tiles)[2], uint32_t (&nsegs)[2], int &n, int lane,
+                              Requant &pend) {
+  if (n == 0) return;
+  const uint32_t r = lane >> 2, vsel = (lane & 3) >> 1;
+  const bool holder = (lane & 1) == 0;
+  __threadfence();
+  __syncwarp();
+  for (int i = 0; i < n; i++) {
+    const uint32_t tile = tiles[i], nseg = nsegs[i];
+    uint32_t ticket = 0;
+    if (lane == 0) ticket = atomicAdd(&p.tile_cnt[tile], 1u);
+    ticket = __shfl_sync(0xffffffffu, ticket, 0);
+    if (ticket != nseg - 1) continue;  // another part finishes this tile
+    __threadfence();
+    float ya[NT], yb[NT];
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++) {
+      const uint32_t vec = 2 * nt + vsel;
+      float a = 0.f, b = 0.f;
+      if (holder && vec < p.batch) {
+        for (uint32_t q = 0; q < nseg; q++) {
+          const float *pp = p.partial + ((size_t)q * p.batch + vec) * p.npad + (size_t)tile * 16 + r;
+          a += __ldcg(pp);
+          b += __ldcg(pp + 8);
+        }
+      }
+      ya[nt] = a;
+      yb[nt] = b;
+    }
+    if (lane == 0) p.tile_cnt[tile] = 0;
+    finish_tile<NT>(p, tile, lane, ya, yb, pend);
+  }
+  n = 0;
+}
+
+// RMSNorm of x[batch][k] (pai_ref_rmsnorm_gamma_f32, ref_ops.c:196-216:
+// the sum of squares in double, scale = 1/sqrtf(mean + eps), then
+// (x*gamma)*scale with single roundings) computed by the 8 consumer warps
+// of a CTA, quantised straight into the CTA's resident x slot.
+template <int NT>
+__device__ void norm_prologue(const GemvP &p, const XS &slot, int c, int lane, double (&red)[kCons][8]) {
+  const uint32_t tid = (uint32_t)(c * 32 + lane), nthr = kCons * 32;
+  for (uint32_t vec = 0; vec < p.batch; vec++) {
+    const float *xr = p.xf + (size_t)vec * p.xq.k;
+    double acc = 0.0;
+    for (uint32_t i = tid; i < p.xq.k; i += nthr) {
+      const double v = (double)xr[i];
+      acc = __dadd_rn(acc, __dmul_rn(v, v));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) red[c][vec] = acc;
+  }
+  asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
+  b200_xq_t v;
+  v.limbs = const_cast<uint8_t *>(slot.limbs);
+  v.sb = const_cast<float *>(slot.sb);
+  v.sx = const_cast<float *>(slot.sx);
+  v.batch = p.batch;
+  v.k = p.xq.k;
+  v.quads = slot.quads;
+  for (uint32_t vec = 0; vec < p.batch; vec++) {
+    double t = 0.0;
+    for (int w = 0; w < kCons; w++) t += red[w][vec];
+    const float ms = (float)__ddiv_rn(t, (double)p.xq.k);
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, p.eps)));
+    const float *xr = p.xf + (size_t)vec * p.xq.k;
+    for (uint32_t b = (uint32_t)c; b < slot.quads * 4; b += kCons) {
+      const uint32_t i = b * 32 + lane;
+      const float x = i < p.xq.k ? __fmul_rn(__fmul_rn(xr[i], p.gamma[i]), scale) : 0.0f;
+      xq_store_block(v, vec, b, x);
     }
   }
+  asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
 }
 
-template <uint32_t T, int B>
-pai_status_t launch_t(pai_b200_ctx_t *ctx, GemvParams p, int num_sms) {
-  constexpr uint32_t EL = Block<T>::EL;
-  auto kern = k_gemv<T, B>;
-  // K split: aim for ~3 resident CTAs per SM, with at least 2 blocks per
-  // warp (Q4_K: 1) and x staging within 96 KB of shared memory.
-  const uint32_t min_bpc = (T == PAI_B200_Q4_K) ? kWarps : 2 * kWarps;
-  const uint32_t per_blk_smem = B * EL * 4 + (T == PAI_B200_Q4_K ? B * 8 * 4 : 0);
-  const uint32_t max_bpc = std::max<uint32_t>(1, (96u * 1024u) / per_blk_smem);
-  uint32_t target = (uint32_t)num_sms * 3;
-  uint32_t kcta = (target + p.ngroups - 1) / p.ngroups;
-  kcta = std::min<uint32_t>(kcta, std::max<uint32_t>(1, p.nb / min_bpc));
-  uint32_t bpc = (p.nb + kcta - 1) / kcta;
-  if (bpc > max_bpc) bpc = max_bpc;
-  kcta = (p.nb + bpc - 1) / bpc;
-  p.bpc = bpc;
-  p.kcta = kcta;
-  size_t smem = (size_t)bpc * per_blk_smem;
-  if (kcta > 1) {
-    pai_status_t st = b200_ctx_scratch(ctx, (uint64_t)kcta * B * p.npad, p.ngroups, &p.partial, &p.counters);
-    if (st) return st;
-  }
-  static bool attr_set = false;
-  if (!attr_set) {
-    pai_status_t st = b200_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024),
-                                "k_gemv smem attribute");
-    if (st) return st;
-    attr_set = true;
-  }
-  dim3 grid(p.ngroups, kcta);
-  kern<<<grid, kThreads, smem, (cudaStream_t)b200_ctx_stream(ctx)>>>(p);
-  return b200_launched(ctx, 1, "k_gemv");
-}
+template <uint32_t T, int NT>
+__global__ void __launch_bounds__(kThreads, kCtasPerSm<NT>) k_gemv(GemvP p) {
+  using Un = Unit<T>;
+  constexpr int U = Un::U, XPU = Un::XPU;
+  constexpr uint32_t GQ = kCons * Un::QB, GS = kCons * Un::SB;  // bytes of one unit of a group
+  constexpr uint32_t STAGE = U * (GQ + GS);
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) uint64_t full[kStages], empty[kStages];
+  __shared__ __align__(8) uint64_t xfull[kXSlots], xempty[kXSlots];
+  __shared__ double red[kCons][8];  // xnorm: per-warp sums of squares per vector
 
-template <uint32_t T>
-pai_status_t launch_b(pai_b200_ctx_t *ctx, GemvParams p, uint32_t batch, int sms) {
-  switch (batch) {
-    case 1: return launch_t<T, 1>(ctx, p, sms);
-    case 2: return launch_t<T, 2>(ctx, p, sms);
-    case 4: return launch_t<T, 4>(ctx, p, sms);
-    case 8: return launch_t<T, 8>(ctx, p, sms);
-    default: return b200_fail(PAI_ERR_UNSUPPORTED, "gemv: batch %u (1, 2, 4 or 8)", batch);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint64_t total = (uint64_t)p.ngroups * p.units;
+  const uint64_t r0 = (uint64_t)blockIdx.x * total / gridDim.x;
+  const uint64_t r1 = (uint64_t)(blockIdx.x + 1) * total / gridDim.x;
+  uint8_t *ring = smem;                            // [kStages][STAGE]
+  uint8_t *xbuf = smem + (size_t)kStages * STAGE;  // [kXSlots][xslot_bytes]
+  const uint32_t xq_slot = p.upc * XPU;            // x-quads one slot holds
+  auto slot_view = [&](int xs) {
+    XS v;
+    uint8_t *b = xbuf + (size_t)xs * p.xslot_bytes;
+    v.limbs = b;
+    v.sb = reinterpret_cast<const float *>(b + (size_t)NT * xq_slot * 1024);
+    v.sx = v.sb + (size_t)p.batch * xq_slot * 4;
+    v.quads = xq_slot;
+    v.batch = p.batch;
+    return v;
+  };
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kCons);
+    }
+    for (int x = 0; x < kXSlots; x++) {
+      mbar_init(&xfull[x], 1);
+      mbar_init(&xempty[x], kCons);
+    }
+    fence_mbar_init();
+    pdl_trigger();
   }
+  __syncthreads();
+
+  if (warp == 0) {
+    // ---- producer (one thread): stage x, stream the weights of each sub-item ----
+    if (lane != 0) return;
+    bool ok = true;
+    uint32_t xuse[kXSlots];
+    for (int x = 0; x < kXSlots; x++) xuse[x] = 0;
+    // x of quads [u0*XPU, u1*XPU) into slot xs, after the consumers released it
+    auto stage_x = [&](int xs, uint32_t u0, uint32_t u1) {
+      if (xuse[xs] > 0 && !mbar_wait(&xempty[xs], (xuse[xs] - 1) & 1u, kWaitLimit)) {
+        ok = false;
+        return;
+      }
+      xuse[xs]++;
+      XS v = slot_view(xs);
+      const uint32_t qx0 = u0 * XPU, nq = (u1 - u0) * XPU;
+      fence_proxy_async();
+      mbar_expect_tx(&xfull[xs], NT * nq * 1024 + 2 * p.batch * nq * 16);
+      for (int nt = 0; nt < NT; nt++)
+        bulk_g2s(const_cast<uint8_t *>(v.limbs) + (size_t)nt * xq_slot * 1024,
+                 p.xq.limbs + ((size_t)nt * p.xq.quads + qx0) * 1024, nq * 1024, &xfull[xs]);
+      for (uint32_t vec = 0; vec < p.batch; vec++) {
+        bulk_g2s(const_cast<float *>(v.sb) + (size_t)vec * xq_slot * 4, p.xq.sb + ((size_t)vec * p.xq.quads + qx0) * 4,
+                 nq * 16, &xfull[xs]);
+        bulk_g2s(const_cast<float *>(v.sx) + (size_t)vec * xq_slot * 4, p.xq.sx + ((size_t)vec * p.xq.quads + qx0) * 4,
+                 nq * 16, &xfull[xs]);
+      }
+    };
+    // Weight walker: sub-item wi (w, at flat position wpos), next unit wu.
+    uint32_t fill = 0, wi = 0;
+    uint64_t wpos = r0;
+    Sub w = sub_at(p, r0, r0, r1);
+    uint32_t wu = w.u0;
+    // Fill one ring stage at the weight walker; false once all are issued.
+    auto fill_stage = [&]() -> bool {
+      if (wpos >= r1) return false;
+      const uint32_t ua = wu, ub = min(w.u1, ua + U), slot = fill % kStages;
+      if (fill >= (uint32_t)kStages && !mbar_wait(&empty[slot], ((fill / kStages) - 1) & 1u, kWaitLimit)) {
+        ok = false;
+        return false;
+      }
+      const uint32_t nv = min((uint32_t)kCons, p.ntiles - w.g * kCons);  // tiles present in the group
+      const size_t tile0 = (size_t)w.g * kCons;
+      uint8_t *dst = ring + (size_t)slot * STAGE;
+      mbar_expect_tx(&full[slot], (ub - ua) * nv * (Un::QB + Un::SB));
+      for (uint32_t u = ua; u < ub; u++) {  // unit-major: the group's tiles of one unit are contiguous
+        const size_t t0 = (size_t)u * p.ntiles + tile0;
+        bulk_g2s(dst + (u - ua) * GQ, p.qs + t0 * Un::QB, nv * Un::QB, &full[slot]);
+        bulk_g2s(dst + U * GQ + (u - ua) * GS, p.sc + t0 * Un::SB, nv * Un::SB, &full[slot]);
+      }
+      fill++;
+      wu = ub;
+      if (wu >= w.u1) {
+        wpos += w.u1 - w.u0;
+        wi++;
+        if (wpos < r1) {
+          w = sub_at(p, wpos, r0, r1);
+          wu = w.u0;
+        }
+      }
+      return true;
+    };
+    // The weights do not depend on the previous kernel: fill the ring
+    // before waiting for it.
+    for (int i = 0; i < kStages && fill_stage(); i++) {
+    }
+    pdl_wait();
+    if (p.resident && !p.xnorm && ok) stage_x(0, 0, p.units);
+    uint64_t xpos = r0;  // x walker: next sub-item whose x is staged (index xi)
+    uint32_t xi = 0;
+    while (ok) {
+      // x stays one sub-item ahead of the weights
+      while (!p.resident && ok && xpos < r1 && xi <= wi + 1) {
+        const Sub sx = sub_at(p, xpos, r0, r1);
+        stage_x((int)(xi % kXSlots), sx.u0, sx.u1);
+        xpos += sx.u1 - sx.u0;
+        xi++;
+      }
+      if (!ok || !fill_stage()) break;
+    }
+    if (!ok) {
+      // A wait ran out: raise the error, let this CTA's copies land
+      // (bounded), and stop; the consumers time out on their own waits.
+      atomicExch(p.err, 1u);
+      for (uint32_t f = fill > (uint32_t)kStages ? fill - kStages : 0; f < fill; f++)
+        mbar_wait(&full[f % kStages], (f / kStages) & 1u, kWaitLimit);
+      for (int x = 0; x < kXSlots; x++)
+        if (xuse[x]) mbar_wait(&xfull[x], (xuse[x] - 1) & 1u, kWaitLimit);
+    }
+    return;
+  }
+
+  // ---- consumers: warp c owns tile c of every group ----
+  pdl_wait();  // before the prologue reads x and the epilogue writes y and scratch
+  const int c = warp - 1;
+  const uint32_t r = lane >> 2;
+  const bool holder = (lane & 1) == 0;  // c = 0 (even vector of the pair) or c = 2 (odd)
+  const uint32_t vsel = (lane & 3) >> 1;
+  uint32_t seq = 0, xuse = 0;
+  int xs = 0;
+  float yr[NT], yr8[NT];
+  uint32_t split_tile[2], split_n[2];
+  int nsplit = 0;
+  Requant pend;
+  if (p.xnorm) {
+    norm_prologue<NT>(p, slot_view(0), c, lane, red);
+  } else if (p.resident && !mbar_wait(&xfull[0], 0, kWaitLimit)) {
+    if (lane == 0) atomicExch(p.err, 1u);
+    return;
+  }
+  for (uint64_t pos = r0; pos < r1;) {
+    const Sub s = sub_at(p, pos, r0, r1);
+    pos += s.u1 - s.u0;
+    if (!p.resident && !mbar_wait(&xfull[xs], (xuse / kXSlots) & 1u, kWaitLimit)) {
+      if (lane == 0) atomicExch(p.err, 1u);
+      return;
+    }
+    const XS v = slot_view(p.resident ? 0 : xs);
+    const uint32_t xu0 = p.resident ? 0 : s.u0;  // unit held at the slot's start
+    const uint32_t tile = s.g * kCons + c;
+    const bool active = tile < p.ntiles;
+    if (s.first) {
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++) yr[nt] = yr8[nt] = 0.f;
+    }
+    for (uint32_t ua = s.u0; ua < s.u1; ua += U) {
+      const uint32_t slot = seq % kStages, par = (seq / kStages) & 1u;
+      if (!mbar_wait(&full[slot], par, kWaitLimit)) {
+        if (lane == 0) atomicExch(p.err, 1u);
+        return;
+      }
+      if (active) {
+        const uint8_t *st = ring + (size_t)slot * STAGE;
+#pragma unroll
+        for (int uu = 0; uu < U; uu++) {
+          const uint32_t u = ua + uu;
+          if (u < s.u1)
+            Un::template compute<NT>(st + uu * GQ + c * Un::QB, st + U * GQ + uu * GS + c * Un::SB, v,
+                                     (u - xu0) * XPU, lane, yr, yr8);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+      seq++;
+    }
+    if (!p.resident) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&xempty[xs]);  // this warp is done with the x slot
+      xs = (xs + 1) % kXSlots;
+      xuse++;
+    }
+    if (!s.last || !active) continue;
+
+    // ---- segment finished ----
+    const uint32_t cta_lo = cta_of((uint64_t)s.g * p.units, total, gridDim.x);
+    const uint32_t nseg = cta_of((uint64_t)(s.g + 1) * p.units - 1, total, gridDim.x) - cta_lo + 1;
+    float ya[NT], yb[NT];
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++) {  // lane pairs (c, c^1) hold the two halves of one sum
+      ya[nt] = yr[nt] + __shfl_xor_sync(0xffffffffu, yr[nt], 1);
+      yb[nt] = yr8[nt] + __shfl_xor_sync(0xffffffffu, yr8[nt], 1);
+    }
+    if (nseg == 1) {
+      finish_tile<NT>(p, tile, lane, ya, yb, pend);
+      continue;
+    }
+    // part of a split tile: park the partial sums; the ticket is taken at
+    // the end, so the fence it needs does not stall the ring
+    const uint32_t split = blockIdx.x - cta_lo;
+    if (holder) {
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++) {
+        const uint32_t vec = 2 * nt + vsel;
+        if (vec < p.batch) {
+          float *pp = p.partial + ((size_t)split * p.batch + vec) * p.npad + (size_t)tile * 16 + r;
+          pp[0] = ya[nt];
+          pp[8] = yb[nt];
+        }
+      }
+    }
+    if (nsplit == 2) settle_splits<NT>(p, split_tile, split_n, nsplit, lane, pend);  // only first and last split
+    split_tile[nsplit] = tile;
+    split_n[nsplit++] = nseg;
+  }
+  settle_splits<NT>(p, split_tile, split_n, nsplit, lane, pend);
+  pend.flush(p, lane);
 }
 
 int sm_count(pai_b200_ctx_t *ctx) {
   static int cached[64];
   int dev = b200_ctx_device(ctx);
-  if (dev < 64 && cached[dev]) return cached[dev];
+  if (dev >= 0 && dev < 64 && cached[dev]) return cached[dev];
   int v = 148;
   cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
-  if (dev < 64) cached[dev] = v;
+  if (dev >= 0 && dev < 64) cached[dev] = v;
   return v;
 }
 
-}  // namespace
+template <uint32_t T, int NT>
+pai_status_t launch_t(pai_b200_ctx_t *ctx, GemvP p) {
+  auto kern = k_gemv<T, NT>;
+  using Un = Unit<T>;
+  const size_t ring = (size_t)kStages * Un::U * kCons * (Un::QB + Un::SB);
+  p.ngroups = (p.ntiles + kCons - 1) / kCons;
+  const uint64_t total = (uint64_t)p.ngroups * p.units;
+  const uint32_t grid = (uint32_t)std::min<uint64_t>(total, (uint64_t)kCtasPerSm<NT> * sm_count(ctx));
+  // x staging: all of x once per CTA when the CTA's share spans at least
+  // two groups' K ranges (so x is reused), or for the fused norm, and it
+  // fits beside the ring; else three slots of up to `upc` units, refilled
+  // one sub-item ahead, so a CTA with a short share stages only the x its
+  // units use.
+  const size_t per_unit_x = (size_t)Un::XPU * (NT * 1024 + 2 * p.batch * 16);
+  const size_t room = kSmemCap<NT> - ring;
+  const bool fits = p.units * per_unit_x + 256 <= room;
+  if (p.xnorm && !fits)
+    return b200_fail(PAI_ERR_UNSUPPORTED, "gemv: x of %u units does not fit for the fused norm", p.units);
+  if ((p.xnorm || total / grid >= 2ull * p.units) && fits) {
+    p.resident = 1;
+    p.upc = p.units;
+  } else {
+    p.resident = 0;
+    p.upc = (uint32_t)std::max<size_t>(Un::U, (room / kXSlots - 256) / per_unit_x);
+  }
+  const size_t xq_slot = (size_t)p.upc * Un::XPU;
+  p.xslot_bytes = (uint32_t)b200_align256(NT * xq_slot * 1024 + 2 * (size_t)p.batch * xq_slot * 16);
+  const size_t smem = ring + (p.resident ? 1 : kXSlots) * (size_t)p.xslot_bytes;
+  if (smem > kSmemCap<NT>) return b200_fail(PAI_ERR_UNSUPPORTED, "gemv: %zu B of shared memory", smem);
+  // Function attributes are set once per device (the largest size seen),
+  // not per launch: they cost host time on the decode path.
+  static size_t smem_set[64];
+  const int dev = b200_ctx_device(ctx);
+  pai_status_t st = PAI_OK;
+  if (dev < 0 || dev >= 64 || smem > smem_set[dev]) {
+    st = b200_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                   "k_gemv smem attribute");
+    if (!st)
+      st = b200_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100),
+                     "k_gemv carveout attribute");
+    if (st) return st;
+    if (dev >= 0 && dev < 64) smem_set[dev] = smem;
+  }
+  // Most segments a group can be cut into: a CTA's share is at least
+  // floor(total / grid) units, so a group of `units` meets at most
+  // ceil(units / share) + 1 CTAs.
+  const uint64_t share = total / grid;
+  const uint32_t maxseg = (uint32_t)std::min<uint64_t>(grid, (p.units + share - 1) / share + 1);
+  const uint32_t ngroups4 = (p.ntiles + 3) / 4;
+  float *partial = nullptr;
+  uint32_t *cnt = nullptr;
+  st = b200_ctx_scratch(ctx, maxseg > 1 ? (uint64_t)maxseg * p.batch * p.npad : 0, p.ntiles + ngroups4, &partial,
+                        &cnt);
+  if (st) return st;
+  p.partial = partial;
+  p.tile_cnt = cnt;
+  p.grp_cnt = cnt + p.ntiles;
+  p.err = b200_ctx_errflag(ctx);
+  b200_launch(ctx, kern, dim3(grid), dim3(kThreads), smem, p);
+  return b200_launched(ctx, 1, "k_gemv");
+}
 
-extern "C" pai_status_t b200_launch_gemv(pai_b200_ctx_t *ctx, uint32_t type, uint32_t batch, uint64_t n,
-                                         uint64_t k, const void *w, const float *x, const float *residual,
-                                         float *y, int epi) {
-  if (!ctx || !w || !x || !y) return b200_fail(PAI_ERR_INVALID_ARG, "gemv: NULL pointer");
+template <uint32_t T>
+pai_status_t launch_b(pai_b200_ctx_t *ctx, const GemvP &p) {
+  switch ((p.batch + 1) / 2) {
+    case 1: return launch_t<T, 1>(ctx, p);
+    case 2: return launch_t<T, 2>(ctx, p);
+    case 3: return launch_t<T, 3>(ctx, p);
+    default: return launch_t<T, 4>(ctx, p);
+  }
+}
+
+// Quantise x[batch][k] into xq: one warp per 32-element block, including
+// the zero padding blocks of the last x-quad (whose scales must read 0).
+__global__ void __launch_bounds__(256) k_xprep(const float *__restrict__ x, uint64_t k, b200_xq_t xq) {
+  const uint32_t vec = blockIdx.y;
+  const uint64_t b = (uint64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (b >= xq.quads * 4) return;
+  const float v = b * 32 < k ? x[(size_t)vec * k + b * 32 + (threadIdx.x & 31)] : 0.0f;
+  xq_store_block(xq, vec, (uint32_t)b, v);
+}
+
+// Shared argument checks and parameter set-up of both GEMV launchers; x is
+// either xq (staged by the producer) or fp32 x with RMSNorm applied in the
+// kernel (xf != nullptr).
+pai_status_t gemv_launch(pai_b200_ctx_t *ctx, uint32_t type, uint32_t batch, uint64_t n, uint64_t k, const void *w,
+                         const b200_xq_t *xq, const float *xf, const float *gamma, float eps, const float *residual,
+                         float *y, int epi, const b200_xq_t *xq_out) {
+  if (!ctx || !w || (!xq && !(xf && gamma)) || !y) return b200_fail(PAI_ERR_INVALID_ARG, "gemv: NULL pointer");
   if (!b200_type_ok(type)) return b200_fail(PAI_ERR_UNSUPPORTED, "gemv: block type %u", type);
   if (n == 0 || k == 0 || k % b200_blk_elems(type))
     return b200_fail(PAI_ERR_MISMATCH, "gemv: k=%llu is not a whole number of %u-element blocks",
                      (unsigned long long)k, b200_blk_elems(type));
-  if (n > 0xFFFFFFFFull || k > 0x7FFFFFFFull) return b200_fail(PAI_ERR_UNSUPPORTED, "gemv: shape too large");
+  if (batch == 0 || batch > 8) return b200_fail(PAI_ERR_UNSUPPORTED, "gemv: batch %u (1..8)", batch);
+  if (n > 0x7FFFFFF0ull || k > 0x7FFFFFFFull) return b200_fail(PAI_ERR_UNSUPPORTED, "gemv: shape too large");
+  if (xq && (xq->batch < batch || xq->k < k)) return b200_fail(PAI_ERR_MISMATCH, "gemv: activation buffer too small");
   if (epi == B200_EPI_RESIDUAL && !residual) return b200_fail(PAI_ERR_INVALID_ARG, "gemv: NULL residual");
-  if (epi == B200_EPI_SILU_GLU && n % 32) return b200_fail(PAI_ERR_MISMATCH, "gemv: gate/up rows must be 32-aligned");
-  if (((uintptr_t)x & 15) || ((uintptr_t)w & 255)) return b200_fail(PAI_ERR_INVALID_ARG, "gemv: misaligned x or w");
-  GemvParams p{};
+  if (epi == B200_EPI_SILU_GLU && (n % 64 || (xq_out && (xq_out->batch < batch || xq_out->k < n / 2))))
+    return b200_fail(PAI_ERR_MISMATCH, "gemv: gate/up rows must come in 64-row groups");
+  if ((uintptr_t)w & 255) return b200_fail(PAI_ERR_INVALID_ARG, "gemv: weights not 256-byte aligned");
+  GemvP p{};
   p.qs = (const uint8_t *)w;
   p.sc = p.qs + b200_sc_offset(type, n, k);
-  p.x = x;
+  if (xq) {
+    p.xq = *xq;
+  } else {
+    p.xnorm = 1;
+    p.xf = xf;
+    p.gamma = gamma;
+    p.eps = eps == 0.0f ? 1e-5f : eps;
+    p.xq.batch = batch;
+    p.xq.k = k;
+    p.xq.quads = b200_xq_quads(k);
+  }
   p.res = residual;
   p.y = y;
+  if (epi == B200_EPI_SILU_GLU && xq_out) p.xo = *xq_out;
   p.n = (uint32_t)n;
-  p.k = (uint32_t)k;
-  p.nb = (uint32_t)(k / b200_blk_elems(type));
-  p.ngroups = (uint32_t)b200_ngroups(n);
-  p.npad = p.ngroups * 32;
+  p.nout = (uint32_t)(n / 2);
+  p.units = (uint32_t)b200_units(type, k);
+  p.ntiles = (uint32_t)b200_ntiles(n);
+  p.npad = p.ntiles * 16;
+  p.batch = batch;
   p.epi = epi;
-  int sms = sm_count(ctx);
   switch (type) {
-    case PAI_B200_Q4_0: return launch_b<PAI_B200_Q4_0>(ctx, p, batch, sms);
-    case PAI_B200_Q8_0: return launch_b<PAI_B200_Q8_0>(ctx, p, batch, sms);
-    default: return launch_b<PAI_B200_Q4_K>(ctx, p, batch, sms);
+    case PAI_B200_Q4_0: return launch_b<PAI_B200_Q4_0>(ctx, p);
+    case PAI_B200_Q8_0: return launch_b<PAI_B200_Q8_0>(ctx, p);
+    default: return launch_b<PAI_B200_Q4_K>(ctx, p);
   }
+}
+
+}  // namespace
+
+extern "C" pai_status_t b200_launch_xprep(pai_b200_ctx_t *ctx, uint32_t batch, uint64_t k, const float *x,
+                                          const b200_xq_t *xq) {
+  const uint64_t nb = xq->quads * 4;
+  k_xprep<<<dim3((unsigned)((nb + 7) / 8), batch), 256, 0, (cudaStream_t)b200_ctx_stream(ctx)>>>(x, k, *xq);
+  return b200_launched(ctx, 1, "k_xprep");
+}
+
+extern "C" pai_status_t b200_launch_gemv(pai_b200_ctx_t *ctx, uint32_t type, uint32_t batch, uint64_t n,
+                                         uint64_t k, const void *w, const b200_xq_t *xq, const float *residual,
+                                         float *y, int epi, const b200_xq_t *xq_out) {
+  if (!xq) return b200_fail(PAI_ERR_INVALID_ARG, "gemv: NULL activations");
+  return gemv_launch(ctx, type, batch, n, k, w, xq, nullptr, nullptr, 0.0f, residual, y, epi, xq_out);
+}
+
+extern "C" pai_status_t b200_launch_gemv_norm(pai_b200_ctx_t *ctx, uint32_t type, uint32_t batch, uint64_t n,
+                                              uint64_t k, const void *w, const float *x, const float *gamma,
+                                              float eps, const float *residual, float *y, int epi,
+                                              const b200_xq_t *xq_out) {
+  return gemv_launch(ctx, type, batch, n, k, w, nullptr, x, gamma, eps, residual, y, epi, xq_out);
+}
+
+// Public GEMV: x arrives in fp32, is quantised into the context's
+// activation scratch, then multiplied.
+static pai_status_t gemv_public(pai_b200_ctx_t *ctx, uint32_t type, uint64_t batch, uint64_t n, uint64_t k,
+                                const void *w, const float *x, const float *residual, float *y) {
+  if (!ctx || !x) return b200_fail(PAI_ERR_INVALID_ARG, "gemv: NULL pointer");
+  if (batch == 0 || batch > 8)
+    return b200_fail(PAI_ERR_UNSUPPORTED, "gemv: batch %llu (1..8)", (unsigned long long)batch);
+  if (!b200_type_ok(type) || k == 0 || k % b200_blk_elems(type))
+    return b200_fail(b200_type_ok(type) ? PAI_ERR_MISMATCH : PAI_ERR_UNSUPPORTED, "gemv: type %u with k=%llu", type,
+                     (unsigned long long)k);
+  void *buf = nullptr;
+  pai_status_t st = b200_ctx_xq(ctx, b200_xq_bytes((uint32_t)batch, k), &buf);
+  if (st) return st;
+  b200_xq_t xq = b200_xq_view(buf, (uint32_t)batch, k);
+  st = b200_launch_xprep(ctx, (uint32_t)batch, k, x, &xq);
+  if (st) return st;
+  return b200_launch_gemv(ctx, type, (uint32_t)batch, n, k, w, &xq, residual, y,
+                          residual ? B200_EPI_RESIDUAL : B200_EPI_STORE, nullptr);
 }
 
 extern "C" pai_status_t pai_b200_gemv_f32(pai_b200_ctx_t *ctx, uint32_t type, uint64_t batch, uint64_t n,
                                           uint64_t k, const void *w, const float *x, const float *residual,
                                           float *y) {
-  if (batch == 0 || batch > 0xFFFFFFFFull) return b200_fail(PAI_ERR_INVALID_ARG, "gemv: batch");
-  return b200_launch_gemv(ctx, type, (uint32_t)batch, n, k, w, x, residual, y,
-                          residual ? B200_EPI_RESIDUAL : B200_EPI_STORE);
+  return gemv_public(ctx, type, batch, n, k, w, x, residual, y);
 }
-
 extern "C" pai_status_t pai_b200_gemv_q8_0_f32(pai_b200_ctx_t *ctx, uint64_t n, uint64_t k, const void *w,
                                                const float *x, float *y) {
-  return b200_launch_gemv(ctx, PAI_B200_Q8_0, 1, n, k, w, x, nullptr, y, B200_EPI_STORE);
+  return gemv_public(ctx, PAI_B200_Q8_0, 1, n, k, w, x, nullptr, y);
 }
 extern "C" pai_status_t pai_b200_gemv_q4_0_f32(pai_b200_ctx_t *ctx, uint64_t n, uint64_t k, const void *w,
                                                const float *x, float *y) {
-  return b200_launch_gemv(ctx, PAI_B200_Q4_0, 1, n, k, w, x, nullptr, y, B200_EPI_STORE);
+  return gemv_public(ctx, PAI_B200_Q4_0, 1, n, k, w, x, nullptr, y);
 }
 extern "C" pai_status_t pai_b200_gemv_q4_k_f32(pai_b200_ctx_t *ctx, uint64_t n, uint64_t k, const void *w,
                                                const float *x, float *y) {
-  return b200_launch_gemv(ctx, PAI_B200_Q4_K, 1, n, k, w, x, nullptr, y, B200_EPI_STORE);
+  return gemv_public(ctx, PAI_B200_Q4_K, 1, n, k, w, x, nullptr, y);
+}
+
+extern "C" uint64_t pai_b200_xq_bytes(uint64_t batch, uint64_t k) {
+  return (batch == 0 || batch > 8 || k == 0) ? 0 : b200_xq_bytes((uint32_t)batch, k);
+}
+
+extern "C" pai_status_t pai_b200_prepare_x_f32(pai_b200_ctx_t *ctx, uint64_t batch, uint64_t k, const float *x,
+                                               void *xq) {
+  if (!ctx || !x || !xq) return b200_fail(PAI_ERR_INVALID_ARG, "prepare_x: NULL pointer");
+  if (batch == 0 || batch > 8)
+    return b200_fail(PAI_ERR_UNSUPPORTED, "prepare_x: batch %llu (1..8)", (unsigned long long)batch);
+  if (k == 0 || k % 32)
+    return b200_fail(PAI_ERR_MISMATCH, "prepare_x: k=%llu is not a multiple of 32", (unsigned long long)k);
+  if ((uintptr_t)xq & 255) return b200_fail(PAI_ERR_INVALID_ARG, "prepare_x: buffer not 256-byte aligned");
+  const b200_xq_t v = b200_xq_view(xq, (uint32_t)batch, k);
+  return b200_launch_xprep(ctx, (uint32_t)batch, k, x, &v);
+}
+
+extern "C" pai_status_t pai_b200_gemv_prepared_f32(pai_b200_ctx_t *ctx, uint32_t type, uint64_t batch, uint64_t n,
+                                                   uint64_t k, const void *w, const void *xq, const float *residual,
+                                                   float *y) {
+  if (!ctx || !xq) return b200_fail(PAI_ERR_INVALID_ARG, "gemv_prepared: NULL pointer");
+  if (batch == 0 || batch > 8)
+    return b200_fail(PAI_ERR_UNSUPPORTED, "gemv_prepared: batch %llu (1..8)", (unsigned long long)batch);
+  if (!b200_type_ok(type) || k == 0 || k % b200_blk_elems(type))
+    return b200_fail(b200_type_ok(type) ? PAI_ERR_MISMATCH : PAI_ERR_UNSUPPORTED, "gemv_prepared: type %u with k=%llu",
+                     type, (unsigned long long)k);
+  const b200_xq_t v = b200_xq_view(const_cast<void *>(xq), (uint32_t)batch, k);
+  return b200_launch_gemv(ctx, type, (uint32_t)batch, n, k, w, &v, residual, y,
+                          residual ? B200_EPI_RESIDUAL : B200_EPI_STORE, nullptr);
+}
+
+extern "C" pai_status_t pai_b200_gemv_rmsnorm_f32(pai_b200_ctx_t *ctx, uint32_t type, uint64_t batch, uint64_t n,
+                                                  uint64_t k, const void *w, const float *x, const float *gamma,
+                                                  float eps, const float *residual, float *y) {
+  if (!ctx || !x || !gamma) return b200_fail(PAI_ERR_INVALID_ARG, "gemv_rmsnorm: NULL pointer");
+  return b200_launch_gemv_norm(ctx, type, (uint32_t)batch, n, k, w, x, gamma, eps, residual, y,
+                               residual ? B200_EPI_RESIDUAL : B200_EPI_STORE, nullptr);
 }

@@ -1,6 +1,7 @@
-// Row and elementwise kernels around the GEMVs: RMSNorm, RoPE (op form
-// and the decode form that also appends the new K/V rows to the fp16
-// cache), SiLU-gate, residual add, embedding lookup and greedy argmax.
+// Row and elementwise kernels around the GEMVs: RMSNorm (optionally
+// writing the GEMV operand format), RoPE, SiLU-gate, residual add,
+// embedding lookup and greedy argmax. The decode form of RoPE (with the
+// K/V append) lives in the attention kernel (k_attn.cu).
 // Where the reference's result is a fixed sequence of IEEE operations
 // (rmsnorm scale, rope, residual add, embedding) the kernels issue the
 // same operations with explicit rounding (__fmul_rn, __fadd_rn, ...) so
@@ -18,31 +19,51 @@ inline unsigned nblk(uint64_t work, unsigned t) { return (unsigned)((work + t - 
 // pai_ref_rmsnorm_gamma_f32 (cpu/reference/ref_ops.c:196-216): the sum of
 // squares is taken in double like the reference (products of floats are
 // exact in double); scale = 1/sqrtf((float)(acc/n) + eps) and
-// c = (a*gamma)*scale with single roundings.
-__global__ void k_rmsnorm(uint64_t n, const float *__restrict__ a, const float *__restrict__ gamma,
-                          float eps, float *__restrict__ c) {
-  const float *ar = a + blockIdx.x * n;
-  float *cr = c + blockIdx.x * n;
+// c = (a*gamma)*scale with single roundings. One 1024-thread CTA per row;
+// the loads of the first pass are independent, so they overlap. When xq
+// is given, each warp also quantises whole 32-element blocks of the result
+// for the GEMV that consumes it.
+__global__ void __launch_bounds__(1024) k_rmsnorm(uint32_t n, const float *__restrict__ a,
+                                                  const float *__restrict__ gamma, float eps, float *__restrict__ c,
+                                                  b200_xq_t xq) {
+  pdl_trigger();
+  pdl_wait();
+  const float *ar = a + (size_t)blockIdx.x * n;
   double acc = 0.0;
-  for (uint64_t i = threadIdx.x; i < n; i += blockDim.x) {
-    double v = (double)ar[i];
+#pragma unroll 4
+  for (uint32_t i = threadIdx.x; i < n; i += 1024) {
+    const double v = (double)ar[i];
     acc = __dadd_rn(acc, __dmul_rn(v, v));
   }
   __shared__ double red[32];
+  __shared__ float scale;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
   __syncthreads();
-  __shared__ float scale;
-  if (threadIdx.x == 0) {
-    double t = 0.0;
-    for (unsigned w = 0; w < (blockDim.x + 31) / 32; w++) t += red[w];
-    float ms = (float)__ddiv_rn(t, (double)n);
-    scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
+  if (threadIdx.x < 32) {
+    double t = threadIdx.x < (blockDim.x + 31) / 32 ? red[threadIdx.x] : 0.0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (threadIdx.x == 0) {
+      const float ms = (float)__ddiv_rn(t, (double)n);
+      scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
+    }
   }
   __syncthreads();
-  float s = scale;
-  for (uint64_t i = threadIdx.x; i < n; i += blockDim.x) cr[i] = __fmul_rn(__fmul_rn(ar[i], gamma[i]), s);
+  const float s = scale;
+  float *cr = c ? c + (size_t)blockIdx.x * n : nullptr;
+  if (xq.limbs) {
+    const uint32_t lane = threadIdx.x & 31;
+    for (uint32_t b = threadIdx.x >> 5; b < xq.quads * 4; b += 32) {
+      const uint32_t i = b * 32 + lane;
+      const float v = i < n ? __fmul_rn(__fmul_rn(ar[i], gamma[i]), s) : 0.0f;
+      if (cr && i < n) cr[i] = v;
+      xq_store_block(xq, blockIdx.x, b, v);
+    }
+  } else {
+    for (uint32_t i = threadIdx.x; i < n; i += 1024) cr[i] = __fmul_rn(__fmul_rn(ar[i], gamma[i]), s);
+  }
 }
 
 // pai_ref_silu_f32 then pai_ref_vecmul_f32 (ref_ops.c:219-228, 124-133).
@@ -59,11 +80,6 @@ __global__ void k_vecadd(const float *__restrict__ a, const float *__restrict__ 
                          uint64_t n) {
   uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) c[i] = __fadd_rn(a[i], b[i]);
-}
-
-__device__ __forceinline__ void rope_pair(float x0, float x1, float c, float s, float &o0, float &o1) {
-  o0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
-  o1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
 }
 
 // pai_ref_rope_f32 (ref_ops.c:231-257): one thread per (row, i) with
@@ -87,85 +103,18 @@ __global__ void k_rope(const float *__restrict__ x, uint64_t rows, uint64_t hd, 
   }
 }
 
-// Decode form: the fused q|k|v projection row of each sequence is split,
-// q and k are rotated at position *pos, k and v are rounded to fp16 and
-// written at *pos of the sequence's cache ([hk][cap][hd]).
-__global__ void k_rope_kv(uint32_t h, uint32_t hk, uint32_t hd, const float *__restrict__ qkv,
-                          const int32_t *__restrict__ pos, const float *__restrict__ cos_t,
-                          const float *__restrict__ sin_t, float *__restrict__ q, __half *__restrict__ kc,
-                          __half *__restrict__ vc, uint64_t cap, uint64_t seq_stride) {
-  const uint32_t bi = blockIdx.x;
-  const uint32_t p = (uint32_t)*pos;
-  const uint32_t r2 = hd / 2;
-  const uint32_t width = (h + 2 * hk) * hd;
-  const float *row = qkv + (size_t)bi * width;
-  float *qo = q + (size_t)bi * h * hd;
-  __half *kcs = kc + (size_t)bi * seq_stride;
-  __half *vcs = vc + (size_t)bi * seq_stride;
-  for (uint32_t idx = threadIdx.x; idx < (h + hk) * r2; idx += blockDim.x) {
-    uint32_t head = idx / r2, i = idx % r2;
-    float c = cos_t[(size_t)p * r2 + i], s = sin_t[(size_t)p * r2 + i];
-    const float *xr = row + (size_t)head * hd;
-    float o0, o1;
-    rope_pair(xr[i], xr[i + r2], c, s, o0, o1);
-    if (head < h) {
-      qo[(size_t)head * hd + i] = o0;
-      qo[(size_t)head * hd + i + r2] = o1;
-    } else {
-      __half *kr = kcs + ((size_t)(head - h) * cap + p) * hd;
-      kr[i] = __float2half_rn(o0);
-      kr[i + r2] = __float2half_rn(o1);
-    }
-  }
-  for (uint32_t idx = threadIdx.x; idx < hk * hd; idx += blockDim.x) {
-    uint32_t head = idx / hd, d = idx % hd;
-    vcs[((size_t)head * cap + p) * hd + d] = __float2half_rn(row[(size_t)(h + hk) * hd + idx]);
-  }
-}
-
 // Embedding lookup: the reference multiplies a one-hot row by the
 // dequantised table (adapters/llama/llama.c:490, 510-522), which yields
 // the dequantised table row exactly. One thread per block of the row.
-__global__ void k_embed(uint32_t type, uint32_t nb, const uint8_t *__restrict__ qs,
-                        const uint8_t *__restrict__ sc, const int32_t *__restrict__ tokens,
-                        float *__restrict__ x) {
+__global__ void k_embed(uint32_t type, uint32_t nb, uint64_t ntiles, const uint8_t *__restrict__ qs,
+                        const uint8_t *__restrict__ sc, const int32_t *__restrict__ tokens, float *__restrict__ x) {
+  pdl_trigger();
+  pdl_wait();
   const uint32_t bi = blockIdx.x;
-  const uint32_t r = (uint32_t)tokens[bi];
-  const uint32_t chunks = b200_chunks(type), hdr = b200_hdr_bytes(type), el = b200_blk_elems(type);
-  const uint64_t g = r / B200_RG, lr = r % B200_RG;
-  float *xr = x + (size_t)bi * nb * el;
-  for (uint32_t b = threadIdx.x; b < nb; b += blockDim.x) {
-    uint64_t tile = g * nb + b;
-    const uint8_t *h = sc + (tile * B200_RG + lr) * hdr;
-    float d = f16_bits_to_f32((uint16_t)(h[0] | (h[1] << 8)));
-    float *o = xr + (size_t)b * el;
-    auto q = [&](uint32_t byte) -> uint8_t {
-      return qs[((tile * chunks + byte / 16u) * B200_RG + lr) * 16u + byte % 16u];
-    };
-    if (type == PAI_B200_Q8_0) {
-      for (int j = 0; j < 32; j++) o[j] = __fmul_rn((float)(int8_t)q(j), d);
-    } else if (type == PAI_B200_Q4_0) {
-      for (int j = 0; j < 16; j++) {
-        uint8_t v = q(j);
-        o[j] = __fmul_rn((float)((int)(v & 15) - 8), d);
-        o[j + 16] = __fmul_rn((float)((int)(v >> 4) - 8), d);
-      }
-    } else {
-      float dmin = f16_bits_to_f32((uint16_t)(h[2] | (h[3] << 8)));
-      for (int c = 0; c < 4; c++) {
-        uint8_t s0, m0, s1, m1;
-        k4_scale_min(2 * c, h + 4, &s0, &m0);
-        k4_scale_min(2 * c + 1, h + 4, &s1, &m1);
-        float d1 = __fmul_rn(d, (float)s0), mm1 = __fmul_rn(dmin, (float)m0);
-        float d2 = __fmul_rn(d, (float)s1), mm2 = __fmul_rn(dmin, (float)m1);
-        for (int l = 0; l < 32; l++) {
-          uint8_t v = q(32 * c + l);
-          o[64 * c + l] = __fsub_rn(__fmul_rn(d1, (float)(v & 15)), mm1);
-          o[64 * c + 32 + l] = __fsub_rn(__fmul_rn(d2, (float)(v >> 4)), mm2);
-        }
-      }
-    }
-  }
+  const uint64_t r = (uint32_t)tokens[bi];
+  const uint32_t el = b200_blk_elems(type);
+  for (uint32_t b = threadIdx.x; b < nb; b += blockDim.x)
+    dequant_block_dev(type, ntiles, qs, sc, r, b, x + ((size_t)bi * nb + b) * el);
 }
 
 // Greedy pick (models/sampler.c:89-99): first index of the strict
@@ -173,6 +122,8 @@ __global__ void k_embed(uint32_t type, uint32_t nb, const uint8_t *__restrict__ 
 // reduction prefers the larger value and, on equal values, the smaller
 // index, which is the sequential scan's answer.
 __global__ void k_argmax(uint64_t n, const float *__restrict__ logits, int32_t *__restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const float *row = logits + (size_t)blockIdx.x * n;
   float best = -INFINITY;
   uint32_t bidx = 0xFFFFFFFFu;
@@ -214,6 +165,8 @@ __global__ void k_argmax(uint64_t n, const float *__restrict__ logits, int32_t *
 // the chosen tokens back as the next step's input.
 __global__ void k_step_tail(uint32_t batch, const int32_t *__restrict__ tok_out, int32_t *__restrict__ tok_in,
                             int32_t *__restrict__ pos) {
+  pdl_trigger();
+  pdl_wait();
   uint32_t i = threadIdx.x;
   if (i < batch) tok_in[i] = tok_out[i];
   if (i == 0) *pos += 1;
@@ -221,18 +174,21 @@ __global__ void k_step_tail(uint32_t batch, const int32_t *__restrict__ tok_out,
 
 }  // namespace
 
-extern "C" pai_status_t b200_launch_rmsnorm(pai_b200_ctx_t *ctx, uint64_t rows, uint64_t n, const float *a,
-                                            const float *gamma, float eps, float *c) {
+extern "C" pai_status_t b200_launch_rmsnorm_xq(pai_b200_ctx_t *ctx, uint64_t rows, uint64_t n, const float *a,
+                                               const float *gamma, float eps, float *c, const b200_xq_t *xq) {
   if (eps == 0.0f) eps = 1e-5f;
-  k_rmsnorm<<<(unsigned)rows, 256, 0, (cudaStream_t)b200_ctx_stream(ctx)>>>(n, a, gamma, eps, c);
+  b200_xq_t q{};
+  if (xq) q = *xq;
+  b200_launch(ctx, k_rmsnorm, dim3((unsigned)rows), dim3(1024), 0, (uint32_t)n, a, gamma, eps, c, q);
   return b200_launched(ctx, 1, "k_rmsnorm");
 }
 
 extern "C" pai_status_t pai_b200_rmsnorm_gamma_f32(pai_b200_ctx_t *ctx, uint64_t rows, uint64_t n,
                                                    const float *a, const float *gamma, float eps, float *c) {
   if (!ctx || !a || !gamma || !c) return b200_fail(PAI_ERR_INVALID_ARG, "rmsnorm: NULL");
-  if (rows == 0 || n == 0 || rows > 0x7FFFFFFFull) return b200_fail(PAI_ERR_INVALID_ARG, "rmsnorm: shape");
-  return b200_launch_rmsnorm(ctx, rows, n, a, gamma, eps, c);
+  if (rows == 0 || n == 0 || rows > 0x7FFFFFFFull || n > 0x7FFFFFFFull)
+    return b200_fail(PAI_ERR_INVALID_ARG, "rmsnorm: shape");
+  return b200_launch_rmsnorm_xq(ctx, rows, n, a, gamma, eps, c, nullptr);
 }
 
 extern "C" pai_status_t pai_b200_silu_mul_f32(pai_b200_ctx_t *ctx, const float *gate, const float *up,
@@ -263,27 +219,18 @@ extern "C" pai_status_t pai_b200_rope_f32(pai_b200_ctx_t *ctx, const float *x, u
   return b200_launched(ctx, 1, "k_rope");
 }
 
-extern "C" pai_status_t b200_launch_rope_kv(pai_b200_ctx_t *ctx, uint32_t batch, uint32_t h, uint32_t hk,
-                                            uint32_t hd, const float *qkv, const int32_t *pos,
-                                            const float *cos_t, const float *sin_t, float *q, uint16_t *kc,
-                                            uint16_t *vc, uint64_t cap, uint64_t seq_stride) {
-  k_rope_kv<<<batch, 256, 0, (cudaStream_t)b200_ctx_stream(ctx)>>>(h, hk, hd, qkv, pos, cos_t, sin_t, q,
-                                                                    (__half *)kc, (__half *)vc, cap, seq_stride);
-  return b200_launched(ctx, 1, "k_rope_kv");
-}
-
 extern "C" pai_status_t b200_launch_embed(pai_b200_ctx_t *ctx, uint32_t type, uint32_t batch, uint64_t rows,
                                           uint64_t k, const void *w, const int32_t *tokens, float *x) {
-  uint32_t nb = (uint32_t)(k / b200_blk_elems(type));
+  const uint32_t nb = (uint32_t)(k / b200_blk_elems(type));
   const uint8_t *qs = (const uint8_t *)w;
   const uint8_t *sc = qs + b200_sc_offset(type, rows, k);
-  k_embed<<<batch, 128, 0, (cudaStream_t)b200_ctx_stream(ctx)>>>(type, nb, qs, sc, tokens, x);
+  b200_launch(ctx, k_embed, dim3(batch), dim3(128), 0, type, nb, (uint64_t)b200_ntiles(rows), qs, sc, tokens, x);
   return b200_launched(ctx, 1, "k_embed");
 }
 
 extern "C" pai_status_t b200_launch_argmax(pai_b200_ctx_t *ctx, uint64_t rows, uint64_t n, const float *logits,
                                            int32_t *out) {
-  k_argmax<<<(unsigned)rows, 1024, 0, (cudaStream_t)b200_ctx_stream(ctx)>>>(n, logits, out);
+  b200_launch(ctx, k_argmax, dim3((unsigned)rows), dim3(1024), 0, n, logits, out);
   return b200_launched(ctx, 1, "k_argmax");
 }
 
@@ -297,6 +244,6 @@ extern "C" pai_status_t pai_b200_argmax_f32(pai_b200_ctx_t *ctx, uint64_t rows, 
 
 extern "C" pai_status_t b200_launch_step_tail(pai_b200_ctx_t *ctx, uint32_t batch, int32_t *tok_out,
                                               int32_t *tok_in, int32_t *pos) {
-  k_step_tail<<<1, 32, 0, (cudaStream_t)b200_ctx_stream(ctx)>>>(batch, tok_out, tok_in, pos);
+  b200_launch(ctx, k_step_tail, dim3(1), dim3(32), 0, batch, tok_out, tok_in, pos);
   return b200_launched(ctx, 1, "k_step_tail");
 }

@@ -10,72 +10,35 @@
 
 namespace {
 
-__global__ void k_pack(uint32_t type, uint64_t n, uint64_t npad, uint32_t nb,
+// One thread per (padded row, padded block): moves the block's header and
+// quant bytes to their places in the packed layout (b200_internal.h), or
+// writes zeros for padding rows, padding blocks and ROW_ZERO rows; rows
+// marked ROW_SKIP belong to another source tensor and are left alone.
+__global__ void k_pack(uint32_t type, uint64_t n, uint64_t npad, uint32_t nb, uint32_t nbpad, uint64_t ntiles,
                        const uint8_t *__restrict__ src, const uint64_t *__restrict__ row_off,
                        uint8_t *__restrict__ qs, uint8_t *__restrict__ sc) {
-  uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  uint64_t r = idx / nb;
-  uint32_t b = (uint32_t)(idx % nb);
+  const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const uint64_t r = idx / nbpad;
+  const uint32_t b = (uint32_t)(idx % nbpad);
   if (r >= npad) return;
-  const uint32_t bb = b200_blk_bytes(type), chunks = b200_chunks(type), hdr = b200_hdr_bytes(type);
-  const uint32_t qoff = type == PAI_B200_Q4_K ? 16u : 2u;
-  uint64_t off = r < n ? row_off[r] : ~0ull;
+  const uint64_t off = r < n ? row_off[r] : ~0ull;
   if (off == ~0ull - 1ull) return;  // row owned by another source tensor
-  const uint8_t *s = off == ~0ull ? nullptr : src + off + (uint64_t)b * bb;
-  uint64_t g = r / B200_RG, lr = r % B200_RG;
-  uint64_t tile = g * nb + b;
-  uint8_t *h = sc + (tile * B200_RG + lr) * hdr;
+  const uint32_t bb = b200_blk_bytes(type);
+  const uint8_t *s = (off == ~0ull || b >= nb) ? nullptr : src + off + (uint64_t)b * bb;
+  const uint32_t hdr = type == PAI_B200_Q4_K ? 16u : 2u, nq = bb - hdr;
+  uint8_t *h = sc + pk_hdr_off(type, ntiles, r, b);
   for (uint32_t i = 0; i < hdr; i++) h[i] = s ? s[i] : 0;
-  for (uint32_t c = 0; c < chunks; c++) {
-    uint8_t *d = qs + ((tile * chunks + c) * B200_RG + lr) * 16u;
-    for (uint32_t i = 0; i < 16; i++) d[i] = s ? s[qoff + 16u * c + i] : 0;
-  }
+  for (uint32_t j = 0; j < nq; j++) qs[pk_qs_off(type, ntiles, r, b, j)] = s ? s[hdr + j] : 0;
 }
 
-// Bit-exact dequantisation (adapters/llama/gguf.c:680-693, 750-761,
-// 852-882). Products of an fp16 scale and a small integer are exact in
-// fp32; the Q4_K form keeps gguf.c's rounding steps (d*sc, dmin*m, then
-// (d*sc)*q - dmin*m) with explicitly rounded operations.
-__global__ void k_dequant(uint32_t type, uint64_t n, uint32_t nb, const uint8_t *__restrict__ qs,
+__global__ void k_dequant(uint32_t type, uint64_t n, uint32_t nb, uint64_t ntiles, const uint8_t *__restrict__ qs,
                           const uint8_t *__restrict__ sc, float *__restrict__ out) {
-  uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  uint64_t r = idx / nb;
-  uint32_t b = (uint32_t)(idx % nb);
+  const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const uint64_t r = idx / nb;
+  const uint32_t b = (uint32_t)(idx % nb);
   if (r >= n) return;
-  const uint32_t chunks = b200_chunks(type), hdr = b200_hdr_bytes(type);
   const uint32_t el = b200_blk_elems(type);
-  uint64_t g = r / B200_RG, lr = r % B200_RG;
-  uint64_t tile = g * nb + b;
-  const uint8_t *h = sc + (tile * B200_RG + lr) * hdr;
-  float *o = out + r * (uint64_t)nb * el + (uint64_t)b * el;
-  auto q = [&](uint32_t byte) -> uint8_t {
-    return qs[((tile * chunks + byte / 16u) * B200_RG + lr) * 16u + byte % 16u];
-  };
-  float d = f16_bits_to_f32((uint16_t)(h[0] | (h[1] << 8)));
-  if (type == PAI_B200_Q4_0) {
-    for (int j = 0; j < 16; j++) {
-      uint8_t v = q(j);
-      o[j] = __fmul_rn((float)((int)(v & 15) - 8), d);
-      o[j + 16] = __fmul_rn((float)((int)(v >> 4) - 8), d);
-    }
-  } else if (type == PAI_B200_Q8_0) {
-    for (int j = 0; j < 32; j++) o[j] = __fmul_rn((float)(int8_t)q(j), d);
-  } else {
-    float dmin = f16_bits_to_f32((uint16_t)(h[2] | (h[3] << 8)));
-    const uint8_t *s12 = h + 4;
-    for (int c = 0; c < 4; c++) {
-      uint8_t s0, m0, s1, m1;
-      k4_scale_min(2 * c, s12, &s0, &m0);
-      k4_scale_min(2 * c + 1, s12, &s1, &m1);
-      float d1 = __fmul_rn(d, (float)s0), mm1 = __fmul_rn(dmin, (float)m0);
-      float d2 = __fmul_rn(d, (float)s1), mm2 = __fmul_rn(dmin, (float)m1);
-      for (int l = 0; l < 32; l++) {
-        uint8_t v = q(32 * c + l);
-        o[64 * c + l] = __fsub_rn(__fmul_rn(d1, (float)(v & 15)), mm1);
-        o[64 * c + 32 + l] = __fsub_rn(__fmul_rn(d2, (float)(v >> 4)), mm2);
-      }
-    }
-  }
+  dequant_block_dev(type, ntiles, qs, sc, r, b, out + r * (uint64_t)nb * el + (uint64_t)b * el);
 }
 
 __device__ __forceinline__ int clampi(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); }
@@ -205,8 +168,7 @@ inline unsigned nblk(uint64_t work, unsigned t) { return (unsigned)((work + t - 
 
 extern "C" uint64_t pai_b200_packed_bytes(uint32_t type, uint64_t n, uint64_t k) {
   if (!b200_type_ok(type) || n == 0 || k == 0 || k % b200_blk_elems(type)) return 0;
-  uint64_t nb = k / b200_blk_elems(type);
-  return b200_sc_offset(type, n, k) + b200_align256(b200_ngroups(n) * nb * B200_RG * b200_hdr_bytes(type));
+  return b200_sc_offset(type, n, k) + b200_align256(b200_ntiles(n) * b200_units(type, k) * b200_unit_sc_bytes(type));
 }
 
 extern "C" pai_status_t pai_b200_pack(pai_b200_ctx_t *ctx, uint32_t type, uint64_t n, uint64_t k,
@@ -216,12 +178,15 @@ extern "C" pai_status_t pai_b200_pack(pai_b200_ctx_t *ctx, uint32_t type, uint64
   if (n == 0 || k == 0 || k % b200_blk_elems(type))
     return b200_fail(PAI_ERR_MISMATCH, "pack: k=%llu not a multiple of %u", (unsigned long long)k,
                      b200_blk_elems(type));
-  uint32_t nb = (uint32_t)(k / b200_blk_elems(type));
-  uint64_t npad = b200_ngroups(n) * B200_RG;
+  if ((uintptr_t)dst & 255) return b200_fail(PAI_ERR_INVALID_ARG, "pack: destination not 256-byte aligned");
+  const uint32_t nb = (uint32_t)(k / b200_blk_elems(type));
+  const uint32_t nbpad = (uint32_t)(b200_units(type, k) * b200_unit_blocks(type));
+  const uint64_t ntiles = b200_ntiles(n), npad = ntiles * B200_TILE;
   uint8_t *qs = (uint8_t *)dst;
   uint8_t *sc = qs + b200_sc_offset(type, n, k);
   cudaStream_t s = (cudaStream_t)b200_ctx_stream(ctx);
-  k_pack<<<nblk(npad * nb, 256), 256, 0, s>>>(type, n, npad, nb, (const uint8_t *)src, row_off, qs, sc);
+  k_pack<<<nblk(npad * nbpad, 256), 256, 0, s>>>(type, n, npad, nb, nbpad, ntiles, (const uint8_t *)src, row_off,
+                                                 qs, sc);
   return b200_launched(ctx, 1, "k_pack");
 }
 
@@ -230,10 +195,11 @@ extern "C" pai_status_t pai_b200_dequant(pai_b200_ctx_t *ctx, uint32_t type, uin
   if (!ctx || !packed || !out) return b200_fail(PAI_ERR_INVALID_ARG, "dequant: NULL");
   if (!b200_type_ok(type)) return b200_fail(PAI_ERR_UNSUPPORTED, "dequant: block type %u", type);
   if (n == 0 || k == 0 || k % b200_blk_elems(type)) return b200_fail(PAI_ERR_MISMATCH, "dequant: shape");
-  uint32_t nb = (uint32_t)(k / b200_blk_elems(type));
+  const uint32_t nb = (uint32_t)(k / b200_blk_elems(type));
   const uint8_t *qs = (const uint8_t *)packed;
   const uint8_t *sc = qs + b200_sc_offset(type, n, k);
-  k_dequant<<<nblk(n * nb, 128), 128, 0, (cudaStream_t)b200_ctx_stream(ctx)>>>(type, n, nb, qs, sc, out);
+  k_dequant<<<nblk(n * nb, 128), 128, 0, (cudaStream_t)b200_ctx_stream(ctx)>>>(type, n, nb, b200_ntiles(n), qs,
+                                                                                 sc, out);
   return b200_launched(ctx, 1, "k_dequant");
 }
 

@@ -108,6 +108,44 @@ def test_gemv_batched_with_residual(dev, t, batch):
         assert maxrel(got[b], ref) <= TOL
 
 
+@pytest.mark.parametrize("t", [po.Q4_0, po.Q8_0, po.Q4_K])
+@pytest.mark.parametrize("batch", [1, 3])
+def test_gemv_prepared_equals_gemv(dev, t, batch):
+    """x prepared once and reused by several matrices gives gemv's bits."""
+    rng = np.random.default_rng(40 + batch)
+    k = 4096
+    x = dev.put(rng.standard_normal((batch, k)).astype(np.float32))
+    xq = dev.prepare_x(x, k, batch)
+    for n in (4096, 1040):
+        blocks = quantize(t, (rng.standard_normal(n * k) * 0.02).astype(np.float32))
+        w = PackedMatrix(dev, t, n, k, blocks)
+        res = dev.put(rng.standard_normal((batch, n)).astype(np.float32))
+        y0, y1 = dev.alloc(batch * n * 4), dev.alloc(batch * n * 4)
+        dev.gemv(w, x, y0, batch=batch, residual=res)
+        dev.gemv_prepared(w, xq, y1, batch=batch, residual=res)
+        assert np.array_equal(bits(y0.download(np.float32)), bits(y1.download(np.float32)))
+
+
+@pytest.mark.parametrize("t", [po.Q4_0, po.Q8_0, po.Q4_K])
+@pytest.mark.parametrize("batch,k", [(1, 4096), (3, 2048), (8, 4096)])
+def test_gemv_rmsnorm_against_oracle(dev, t, batch, k):
+    """RMSNorm computed inside the GEMV: the oracle's rmsnorm_gamma then gemv."""
+    rng = np.random.default_rng(7 * batch + k)
+    n = 1552  # not a multiple of the 128-row group
+    blocks = quantize(t, (rng.standard_normal(n * k) * 0.02).astype(np.float32))
+    x = (rng.standard_normal((batch, k)) * 3.0).astype(np.float32)
+    gamma = (1.0 + 0.1 * rng.standard_normal(k)).astype(np.float32)
+    res = rng.standard_normal((batch, n)).astype(np.float32)
+    w = PackedMatrix(dev, t, n, k, blocks)
+    y = dev.alloc(batch * n * 4)
+    dev.gemv_rmsnorm(w, dev.put(x), dev.put(gamma), 1e-5, y, batch=batch, residual=dev.put(res))
+    got = y.download(np.float32).reshape(batch, n)
+    for b in range(batch):
+        xn = po.rmsnorm_gamma(x[b][None, :], gamma, 1e-5).reshape(k)
+        ref = res[b] + po.gemv_q(t, n, k, blocks, xn)
+        assert maxrel(got[b], ref) <= TOL
+
+
 def test_gemv_rejects_bad_shapes(dev):
     from prosperoai_b200 import PaiError
     blocks = quantize(po.Q4_K, np.zeros(256 * 4, np.float32))
