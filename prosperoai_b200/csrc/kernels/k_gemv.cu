@@ -405,16 +405,26 @@ __device__ void settle_splits(const GemvP &p, uint32_t (&tiles)[2], uint32_t (&n
 // RMSNorm of x[batch][k] (pai_ref_rmsnorm_gamma_f32, ref_ops.c:196-216:
 // the sum of squares in double, scale = 1/sqrtf(mean + eps), then
 // (x*gamma)*scale with single roundings) computed by the 8 consumer warps
-// of a CTA, quantised straight into the CTA's resident x slot.
+// of a CTA, quantised straight into the CTA's resident x slot. Warp c owns
+// blocks c, c+8, c+16, ... (lane = element); each pass loads kPB of them at
+// once and quantises them unrolled, so loads and warp reductions overlap
+// instead of paying one L2 round trip per block.
+constexpr int kPB = 16;
 template <int NT>
 __device__ void norm_prologue(const GemvP &p, const XS &slot, int c, int lane, double (&red)[kCons][8]) {
-  const uint32_t tid = (uint32_t)(c * 32 + lane), nthr = kCons * 32;
+  const uint32_t nthr = kCons * 32, nblk = slot.quads * 4, kk = (uint32_t)p.xq.k;
   for (uint32_t vec = 0; vec < p.batch; vec++) {
-    const float *xr = p.xf + (size_t)vec * p.xq.k;
+    const float *xr = p.xf + (size_t)vec * kk;
     double acc = 0.0;
-    for (uint32_t i = tid; i < p.xq.k; i += nthr) {
-      const double v = (double)xr[i];
-      acc = __dadd_rn(acc, __dmul_rn(v, v));
+    for (uint32_t b0 = 0; b0 < nblk; b0 += kPB * kCons) {
+      float xv[kPB];
+#pragma unroll
+      for (int m = 0; m < kPB; m++) {
+        const uint32_t i = (b0 + m * kCons + c) * 32 + lane;
+        xv[m] = i < kk ? xr[i] : 0.0f;
+      }
+#pragma unroll
+      for (int m = 0; m < kPB; m++) acc = __dadd_rn(acc, __dmul_rn((double)xv[m], (double)xv[m]));
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
@@ -426,18 +436,26 @@ __device__ void norm_prologue(const GemvP &p, const XS &slot, int c, int lane, d
   v.sb = const_cast<float *>(slot.sb);
   v.sx = const_cast<float *>(slot.sx);
   v.batch = p.batch;
-  v.k = p.xq.k;
+  v.k = kk;
   v.quads = slot.quads;
   for (uint32_t vec = 0; vec < p.batch; vec++) {
     double t = 0.0;
     for (int w = 0; w < kCons; w++) t += red[w][vec];
-    const float ms = (float)__ddiv_rn(t, (double)p.xq.k);
+    const float ms = (float)__ddiv_rn(t, (double)kk);
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, p.eps)));
-    const float *xr = p.xf + (size_t)vec * p.xq.k;
-    for (uint32_t b = (uint32_t)c; b < slot.quads * 4; b += kCons) {
-      const uint32_t i = b * 32 + lane;
-      const float x = i < p.xq.k ? __fmul_rn(__fmul_rn(xr[i], p.gamma[i]), scale) : 0.0f;
-      xq_store_block(v, vec, b, x);
+    const float *xr = p.xf + (size_t)vec * kk;
+    for (uint32_t b0 = 0; b0 < nblk; b0 += kPB * kCons) {
+      float xv[kPB];
+#pragma unroll
+      for (int m = 0; m < kPB; m++) {
+        const uint32_t i = (b0 + m * kCons + c) * 32 + lane;
+        xv[m] = i < kk ? __fmul_rn(__fmul_rn(xr[i], p.gamma[i]), scale) : 0.0f;
+      }
+#pragma unroll
+      for (int m = 0; m < kPB; m++) {
+        const uint32_t b = b0 + m * kCons + c;
+        if (b < nblk) xq_store_block(v, vec, b, xv[m]);
+      }
     }
   }
   asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");

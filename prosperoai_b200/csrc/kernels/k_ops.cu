@@ -9,6 +9,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "../b200_internal.h"
 #include "b200_device.cuh"
 
@@ -118,30 +120,23 @@ __global__ void k_embed(uint32_t type, uint32_t nb, uint64_t ntiles, const uint8
 }
 
 // Greedy pick (models/sampler.c:89-99): first index of the strict
-// maximum. Each thread keeps the first maximum of its strided slice; the
-// reduction prefers the larger value and, on equal values, the smaller
-// index, which is the sequential scan's answer.
-__global__ void k_argmax(uint64_t n, const float *__restrict__ logits, int32_t *__restrict__ out) {
-  pdl_trigger();
-  pdl_wait();
-  const float *row = logits + (size_t)blockIdx.x * n;
-  float best = -INFINITY;
-  uint32_t bidx = 0xFFFFFFFFu;
-  for (uint64_t i = threadIdx.x; i < n; i += blockDim.x) {
-    float v = row[i];
-    if (bidx == 0xFFFFFFFFu || v > best) {
-      best = v;
-      bidx = (uint32_t)i;
-    }
+// maximum. CTA (slice, row) scans a contiguous slice; each thread keeps the
+// first maximum of its strided part, and merges prefer the larger value
+// and, on equal values, the smaller index, which is the sequential scan's
+// answer. The last slice of a row to finish (ticket) merges the slices.
+__device__ __forceinline__ void amax_merge(float &best, uint32_t &bidx, float ov, uint32_t oi) {
+  if (oi != 0xFFFFFFFFu && (bidx == 0xFFFFFFFFu || ov > best || (ov == best && oi < bidx))) {
+    best = ov;
+    bidx = oi;
   }
+}
+
+__device__ __forceinline__ void amax_block(float &best, uint32_t &bidx) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
-    float ov = __shfl_xor_sync(0xffffffffu, best, o);
-    uint32_t oi = __shfl_xor_sync(0xffffffffu, bidx, o);
-    if (oi != 0xFFFFFFFFu && (bidx == 0xFFFFFFFFu || ov > best || (ov == best && oi < bidx))) {
-      best = ov;
-      bidx = oi;
-    }
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const uint32_t oi = __shfl_xor_sync(0xffffffffu, bidx, o);
+    amax_merge(best, bidx, ov, oi);
   }
   __shared__ float sv[32];
   __shared__ uint32_t si[32];
@@ -150,14 +145,48 @@ __global__ void k_argmax(uint64_t n, const float *__restrict__ logits, int32_t *
     si[threadIdx.x >> 5] = bidx;
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    for (unsigned w = 1; w < blockDim.x / 32; w++) {
-      if (si[w] != 0xFFFFFFFFu && (bidx == 0xFFFFFFFFu || sv[w] > best || (sv[w] == best && si[w] < bidx))) {
-        best = sv[w];
-        bidx = si[w];
-      }
+  if (threadIdx.x == 0)
+    for (unsigned w = 1; w < blockDim.x / 32; w++) amax_merge(best, bidx, sv[w], si[w]);
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(256) k_argmax(uint64_t n, uint64_t per, const float *__restrict__ logits,
+                                                int32_t *__restrict__ out, float *__restrict__ part,
+                                                uint32_t *__restrict__ cnt) {
+  pdl_trigger();
+  pdl_wait();
+  const uint32_t row = blockIdx.y, slice = blockIdx.x, nsl = gridDim.x;
+  const float *lr = logits + (size_t)row * n;
+  const uint64_t lo = (uint64_t)slice * per, hi = min(n, lo + per);
+  float best = -INFINITY;
+  uint32_t bidx = 0xFFFFFFFFu;
+  for (uint64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+    const float v = lr[i];
+    if (bidx == 0xFFFFFFFFu || v > best) {
+      best = v;
+      bidx = (uint32_t)i;
     }
-    out[blockIdx.x] = (int32_t)bidx;
+  }
+  amax_block(best, bidx);
+  __shared__ uint32_t ticket;
+  if (threadIdx.x == 0) {
+    part[((size_t)row * nsl + slice) * 2] = best;
+    part[((size_t)row * nsl + slice) * 2 + 1] = __uint_as_float(bidx);
+    __threadfence();
+    ticket = atomicAdd(&cnt[row], 1u);
+  }
+  __syncthreads();
+  if (ticket != nsl - 1) return;
+  __threadfence();
+  best = -INFINITY;
+  bidx = 0xFFFFFFFFu;
+  for (uint32_t s = threadIdx.x; s < nsl; s += blockDim.x)
+    amax_merge(best, bidx, __ldcg(&part[((size_t)row * nsl + s) * 2]),
+               __float_as_uint(__ldcg(&part[((size_t)row * nsl + s) * 2 + 1])));
+  amax_block(best, bidx);
+  if (threadIdx.x == 0) {
+    out[row] = (int32_t)bidx;
+    cnt[row] = 0;
   }
 }
 
@@ -230,15 +259,21 @@ extern "C" pai_status_t b200_launch_embed(pai_b200_ctx_t *ctx, uint32_t type, ui
 
 extern "C" pai_status_t b200_launch_argmax(pai_b200_ctx_t *ctx, uint64_t rows, uint64_t n, const float *logits,
                                            int32_t *out) {
-  b200_launch(ctx, k_argmax, dim3((unsigned)rows), dim3(1024), 0, n, logits, out);
+  // slices of at least 2048 logits, at most one per SM
+  const uint64_t nsl = std::min<uint64_t>(148, (n + 2047) / 2048), per = (n + nsl - 1) / nsl;
+  float *part = nullptr;
+  uint32_t *cnt = nullptr;
+  pai_status_t st = b200_ctx_scratch(ctx, rows * nsl * 2, (uint32_t)rows, &part, &cnt);
+  if (st) return st;
+  b200_launch(ctx, k_argmax, dim3((unsigned)nsl, (unsigned)rows), dim3(256), 0, n, per, logits, out, part, cnt);
   return b200_launched(ctx, 1, "k_argmax");
 }
 
 extern "C" pai_status_t pai_b200_argmax_f32(pai_b200_ctx_t *ctx, uint64_t rows, uint64_t n, const float *logits,
                                             int32_t *out) {
   if (!ctx || !logits || !out) return b200_fail(PAI_ERR_INVALID_ARG, "argmax: NULL");
-  if (rows == 0 || n == 0 || n > 0xFFFFFFFEull || rows > 0x7FFFFFFFull)
-    return b200_fail(PAI_ERR_INVALID_ARG, "argmax: shape");
+  if (rows == 0 || n == 0 || n > 0xFFFFFFFEull) return b200_fail(PAI_ERR_INVALID_ARG, "argmax: shape");
+  if (rows > 65535) return b200_fail(PAI_ERR_UNSUPPORTED, "argmax: %llu rows (at most 65535)", (unsigned long long)rows);
   return b200_launch_argmax(ctx, rows, n, logits, out);
 }
 

@@ -228,3 +228,12 @@ def test_argmax_first_of_ties(dev):
     out = dev.alloc(4)
     dev.argmax(1, big.size, dev.put(big), out)
     assert out.download(np.int32)[0] == po.argmax(big)
+    # equal maxima in different slices of the multi-CTA scan: the first wins,
+    # and a repeat call (counters left at zero) agrees
+    tie = big.copy()
+    tie[[70001, 3003, 128255]] = 9.0
+    out = dev.alloc(8)
+    rows2 = np.stack([tie, tie[::-1].copy()])
+    for _ in range(2):
+        dev.argmax(2, tie.size, dev.put(rows2), out)
+        assert list(out.download(np.int32)) == [3003, po.argmax(tie[::-1].copy())]
