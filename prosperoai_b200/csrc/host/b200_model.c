@@ -15,11 +15,11 @@
  *     x   = x + h.Wdown              (residual fused)    :782-795
  *   logits = rmsnorm(x, output_norm).Wout; token = argmax :884-895
  *
- * Kernels per layer: the norms run inside the prologue of the GEMV that
- * consumes them; RoPE, the cache append, attention and the chunk merge
- * are one kernel that also writes the o projection's quantised input; the
- * gate/up GEMV applies SiLU*up and quantises h for the down projection.
- * So a layer is 5 kernels: qkv, attention, o (+x), gate/up, down (+x).
+ * Kernels per layer: each norm quantises x for the GEMV that consumes it;
+ * RoPE, the cache append, attention and the chunk merge are one kernel
+ * that also writes the o projection's quantised input; the gate/up GEMV
+ * applies SiLU*up and quantises h for the down projection. So a layer is
+ * 7 kernels: norm, qkv, attention, o (+x), norm, gate/up, down (+x).
  *
  * Host code only: every device step is a launcher from csrc/kernels.
  */
@@ -409,16 +409,16 @@ pai_status_t b200_tp_allreduce(void *tp, pai_b200_ctx_t *ctx, float *buf, uint64
 pai_status_t b200_tp_argmax(void *tp, pai_b200_ctx_t *ctx, uint32_t batch, uint32_t vl, uint32_t v0,
                             const float *logits, int32_t *tok_out);
 
-/* y = W . rmsnorm_gamma(x): the norm fused into the GEMV's prologue when
- * the quantised x fits in a CTA's shared memory, else the norm kernel
- * writes xq_e and the GEMV reads it. */
+/* y = W . rmsnorm_gamma(x): a many-CTA norm kernel quantises x once into
+ * xq_e (it overlaps the GEMV's weight prefetch under programmatic
+ * dependent launch), then the GEMV stages xq_e. The GEMV can also apply
+ * the norm itself (b200_launch_gemv_norm), but then every CTA quantises
+ * all of x, which costs more than this kernel at 4096-wide rows. */
 static pai_status_t norm_gemv(pai_b200_session_t *s, uint32_t type, uint64_t n, const void *w, const float *gamma,
                               float *y, int epi, const b200_xq_t *xq_out) {
   pai_b200_model_t *m = s->m;
   const uint32_t B = s->batch, E = m->cfg.n_embd;
-  pai_status_t st = b200_launch_gemv_norm(m->ctx, type, B, n, E, w, s->x, gamma, m->cfg.eps, NULL, y, epi, xq_out);
-  if (st != PAI_ERR_UNSUPPORTED) return st;
-  st = b200_launch_rmsnorm_xq(m->ctx, B, E, s->x, gamma, m->cfg.eps, NULL, &s->xq_e);
+  pai_status_t st = b200_launch_rmsnorm_xq(m->ctx, B, E, s->x, gamma, m->cfg.eps, NULL, &s->xq_e);
   if (!st) st = b200_launch_gemv(m->ctx, type, B, n, E, w, &s->xq_e, NULL, y, epi, xq_out);
   return st;
 }

@@ -21,50 +21,43 @@ inline unsigned nblk(uint64_t work, unsigned t) { return (unsigned)((work + t - 
 // pai_ref_rmsnorm_gamma_f32 (cpu/reference/ref_ops.c:196-216): the sum of
 // squares is taken in double like the reference (products of floats are
 // exact in double); scale = 1/sqrtf((float)(acc/n) + eps) and
-// c = (a*gamma)*scale with single roundings. One 1024-thread CTA per row;
-// the loads of the first pass are independent, so they overlap. When xq
-// is given, each warp also quantises whole 32-element blocks of the result
-// for the GEMV that consumes it.
-__global__ void __launch_bounds__(1024) k_rmsnorm(uint32_t n, const float *__restrict__ a,
-                                                  const float *__restrict__ gamma, float eps, float *__restrict__ c,
-                                                  b200_xq_t xq) {
+// c = (a*gamma)*scale with single roundings. CTA (slice, row): every CTA
+// of a row sums the whole row (16 KB at n = 4096, in one round of loads)
+// in the same order, so all get the same scale, then writes only its
+// slice of 32-element blocks -- as fp32 into c and/or quantised into xq
+// for the GEMV that consumes it, one block per warp.
+constexpr int kNormThreads = 128;
+__global__ void __launch_bounds__(kNormThreads) k_rmsnorm(uint32_t n, uint32_t bps, const float *__restrict__ a,
+                                                          const float *__restrict__ gamma, float eps,
+                                                          float *__restrict__ c, b200_xq_t xq) {
   pdl_trigger();
   pdl_wait();
-  const float *ar = a + (size_t)blockIdx.x * n;
+  const uint32_t row = blockIdx.y;
+  const float *ar = a + (size_t)row * n;
   double acc = 0.0;
-#pragma unroll 4
-  for (uint32_t i = threadIdx.x; i < n; i += 1024) {
+#pragma unroll 8
+  for (uint32_t i = threadIdx.x; i < n; i += kNormThreads) {
     const double v = (double)ar[i];
     acc = __dadd_rn(acc, __dmul_rn(v, v));
   }
-  __shared__ double red[32];
-  __shared__ float scale;
+  __shared__ double red[kNormThreads / 32];
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
   __syncthreads();
-  if (threadIdx.x < 32) {
-    double t = threadIdx.x < (blockDim.x + 31) / 32 ? red[threadIdx.x] : 0.0;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-    if (threadIdx.x == 0) {
-      const float ms = (float)__ddiv_rn(t, (double)n);
-      scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
-    }
-  }
-  __syncthreads();
-  const float s = scale;
-  float *cr = c ? c + (size_t)blockIdx.x * n : nullptr;
-  if (xq.limbs) {
-    const uint32_t lane = threadIdx.x & 31;
-    for (uint32_t b = threadIdx.x >> 5; b < xq.quads * 4; b += 32) {
-      const uint32_t i = b * 32 + lane;
-      const float v = i < n ? __fmul_rn(__fmul_rn(ar[i], gamma[i]), s) : 0.0f;
-      if (cr && i < n) cr[i] = v;
-      xq_store_block(xq, blockIdx.x, b, v);
-    }
-  } else {
-    for (uint32_t i = threadIdx.x; i < n; i += 1024) cr[i] = __fmul_rn(__fmul_rn(ar[i], gamma[i]), s);
+  double t = 0.0;
+  for (int w = 0; w < kNormThreads / 32; w++) t += red[w];
+  const float ms = (float)__ddiv_rn(t, (double)n);
+  const float s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
+  float *cr = c ? c + (size_t)row * n : nullptr;
+  const uint32_t lane = threadIdx.x & 31;
+  const uint32_t nblk = xq.limbs ? (uint32_t)(xq.quads * 4) : (n + 31) / 32;
+  const uint32_t b1 = min(nblk, (blockIdx.x + 1) * bps);
+  for (uint32_t b = blockIdx.x * bps + (threadIdx.x >> 5); b < b1; b += kNormThreads / 32) {
+    const uint32_t i = b * 32 + lane;
+    const float v = i < n ? __fmul_rn(__fmul_rn(ar[i], gamma[i]), s) : 0.0f;
+    if (cr && i < n) cr[i] = v;
+    if (xq.limbs) xq_store_block(xq, row, b, v);
   }
 }
 
@@ -206,9 +199,15 @@ __global__ void k_step_tail(uint32_t batch, const int32_t *__restrict__ tok_out,
 extern "C" pai_status_t b200_launch_rmsnorm_xq(pai_b200_ctx_t *ctx, uint64_t rows, uint64_t n, const float *a,
                                                const float *gamma, float eps, float *c, const b200_xq_t *xq) {
   if (eps == 0.0f) eps = 1e-5f;
+  if (rows > 65535) return b200_fail(PAI_ERR_UNSUPPORTED, "rmsnorm: %llu rows (at most 65535)", (unsigned long long)rows);
   b200_xq_t q{};
   if (xq) q = *xq;
-  b200_launch(ctx, k_rmsnorm, dim3((unsigned)rows), dim3(1024), 0, (uint32_t)n, a, gamma, eps, c, q);
+  // one 32-element block per warp, up to 256 CTAs per row
+  const uint64_t nblk = xq ? xq->quads * 4 : (n + 31) / 32;
+  const uint64_t nsl = std::max<uint64_t>(1, std::min<uint64_t>(256, (nblk + 3) / 4));
+  const uint32_t bps = (uint32_t)((nblk + nsl - 1) / nsl);
+  b200_launch(ctx, k_rmsnorm, dim3((unsigned)nsl, (unsigned)rows), dim3(kNormThreads), 0, (uint32_t)n, bps, a, gamma,
+              eps, c, q);
   return b200_launched(ctx, 1, "k_rmsnorm");
 }
 
