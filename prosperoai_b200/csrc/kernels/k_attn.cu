@@ -63,18 +63,39 @@ __device__ __forceinline__ uint32_t chunk_of(const AttnParams &p, uint32_t npos)
   return c < 32 ? 32 : c;
 }
 
-// Merge the chunk partials of query head hh (one thread per dimension d);
-// returns the output value of dimension d.
-__device__ __forceinline__ float merge_chunks(const AttnParams &p, uint32_t bi, uint32_t hh, uint32_t ns,
-                                              uint32_t d) {
+// Merge the chunk partials of query head hh; every thread of the CTA
+// calls it (block-wide max), thread d gets output dimension d. The sums
+// run over chunks in order, eight loads in flight at a time.
+__device__ __forceinline__ float merge_chunks(const AttnParams &p, uint32_t bi, uint32_t hh, uint32_t ns, uint32_t d,
+                                              float *sred) {
   const size_t base = ((size_t)bi * p.h + hh) * p.nsplit;
   float M = -INFINITY;
-  for (uint32_t s = 0; s < ns; s++) M = fmaxf(M, __ldcg(&p.ml[(base + s) * 2]));
+  for (uint32_t s = threadIdx.x; s < ns; s += blockDim.x) M = fmaxf(M, __ldcg(&p.ml[(base + s) * 2]));
+  M = warp_max(M);
+  if ((threadIdx.x & 31) == 0) sred[threadIdx.x >> 5] = M;
+  __syncthreads();
+  M = sred[0];
+  for (uint32_t w = 1; w < blockDim.x / 32; w++) M = fmaxf(M, sred[w]);
+  __syncthreads();
   float L = 0.f, o = 0.f;
-  for (uint32_t s = 0; s < ns; s++) {
-    const float w = expf(__ldcg(&p.ml[(base + s) * 2]) - M);
-    L = fmaf(__ldcg(&p.ml[(base + s) * 2 + 1]), w, L);
-    o = fmaf(__ldcg(&p.opart[(base + s) * HD + d]), w, o);
+  for (uint32_t s0 = 0; s0 < ns; s0 += 8) {
+    float mv[8], lv[8], ov[8];
+#pragma unroll
+    for (int m = 0; m < 8; m++) {
+      if (s0 + m < ns) {
+        mv[m] = __ldcg(&p.ml[(base + s0 + m) * 2]);
+        lv[m] = __ldcg(&p.ml[(base + s0 + m) * 2 + 1]);
+        ov[m] = __ldcg(&p.opart[(base + s0 + m) * HD + d]);
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < 8; m++) {
+      if (s0 + m < ns) {
+        const float w = expf(mv[m] - M);
+        L = fmaf(lv[m], w, L);
+        o = fmaf(ov[m], w, o);
+      }
+    }
   }
   return o / L;
 }
@@ -216,8 +237,9 @@ __global__ void __launch_bounds__(128) k_attn_split(AttnParams p) {
   __syncthreads();
   if (ticket != ns - 1) return;
   __threadfence();
+  __shared__ float sred[4];
   for (int g = 0; g < G; g++) {
-    const float v = merge_chunks(p, bi, h0 + g, ns, (uint32_t)t);
+    const float v = merge_chunks(p, bi, h0 + g, ns, (uint32_t)t, sred);
     p.out[((size_t)bi * p.h + h0 + g) * HD + t] = v;
     // head h0+g covers elements 128(h0+g).. of the attention output: warp w holds block 4(h0+g)+w
     if (p.xo.limbs) xq_store_block(p.xo, bi, (h0 + g) * 4 + warp, v);
@@ -232,7 +254,8 @@ __global__ void __launch_bounds__(128) k_attn_combine(AttnParams p) {
   const uint32_t npos = npos_of(p);
   const uint32_t chunk = chunk_of(p, npos);
   const uint32_t ns = (npos + chunk - 1) / chunk;
-  const float v = merge_chunks(p, bi, h, ns, d);
+  __shared__ float sred[HD / 32];
+  const float v = merge_chunks(p, bi, h, ns, d, sred);
   p.out[((size_t)bi * p.h + h) * HD + d] = v;
   // head h covers elements 128h..128h+127 of the attention output: warp w
   // holds block 4h+w

@@ -387,10 +387,25 @@ __device__ void settle_splits(const GemvP &p, uint32_t (&tiles)[2], uint32_t (&n
       const uint32_t vec = 2 * nt + vsel;
       float a = 0.f, b = 0.f;
       if (holder && vec < p.batch) {
-        for (uint32_t q = 0; q < nseg; q++) {
-          const float *pp = p.partial + ((size_t)q * p.batch + vec) * p.npad + (size_t)tile * 16 + r;
-          a += __ldcg(pp);
-          b += __ldcg(pp + 8);
+        // parts in CTA order, eight loads in flight at a time
+        const float *pp = p.partial + (size_t)vec * p.npad + (size_t)tile * 16 + r;
+        const size_t stride = (size_t)p.batch * p.npad;
+        for (uint32_t q0 = 0; q0 < nseg; q0 += 8) {
+          float ta[8], tb[8];
+#pragma unroll
+          for (int m = 0; m < 8; m++) {
+            if (q0 + m < nseg) {
+              ta[m] = __ldcg(pp + (q0 + m) * stride);
+              tb[m] = __ldcg(pp + (q0 + m) * stride + 8);
+            }
+          }
+#pragma unroll
+          for (int m = 0; m < 8; m++) {
+            if (q0 + m < nseg) {
+              a += ta[m];
+              b += tb[m];
+            }
+          }
         }
       }
       ya[nt] = a;
