@@ -29,6 +29,8 @@
 namespace {
 
 constexpr int HD = 128;
+constexpr int kSub = 64;           // K/V positions staged in shared memory per round (the step chunk)
+constexpr int kMaxStepSplit = 64;  // most position chunks per kv head in the decode step
 
 struct AttnParams {
   const float *q;  // [B][H][HD]
@@ -116,6 +118,7 @@ __global__ void __launch_bounds__(128) k_attn_split(AttnParams p) {
   __shared__ float red[2][G][HD];
   __shared__ float mls[G][2];
   __shared__ uint32_t ticket;
+  __shared__ __align__(16) __half kvs[2][kSub][HD];  // staged K and V rows
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const uint32_t h0 = kvh * G;
   if (STEP) {
@@ -158,23 +161,46 @@ __global__ void __launch_bounds__(128) k_attn_split(AttnParams p) {
   const __half *kb = p.kc + kvoff;
   const __half *vb = p.vc + kvoff;
 
-  // Scores: warp w takes positions w, w+4, ...; lane l holds dims 4l..4l+3.
-  for (uint32_t i = warp; i < len; i += 4) {
-    uint2 raw = *reinterpret_cast<const uint2 *>(kb + (size_t)i * HD + 4 * lane);
-    float2 k01 = __half22float2(*reinterpret_cast<__half2 *>(&raw.x));
-    float2 k23 = __half22float2(*reinterpret_cast<__half2 *>(&raw.y));
-    float part[G];
-#pragma unroll
-    for (int g = 0; g < G; g++) {
-      float s = qr[g][0] * k01.x;
-      s = fmaf(qr[g][1], k01.y, s);
-      s = fmaf(qr[g][2], k23.x, s);
-      s = fmaf(qr[g][3], k23.y, s);
-      part[g] = warp_sum(s);
+  // K and V rows are staged in shared memory kSub positions at a time with
+  // all loads of a round in flight (a chunk of <= kSub positions, the usual
+  // case, needs one round for both); the loops below read shared memory
+  // only, so no global load waits on the previous position's reductions.
+  auto stage = [&](const __half *src, __half (*dst)[HD], uint32_t s0, uint32_t cnt) {
+    for (uint32_t i = t; i < cnt * (HD / 8); i += 128) {
+      const uint32_t r = i / (HD / 8), c = i % (HD / 8);
+      reinterpret_cast<uint4 *>(dst[r])[c] = *reinterpret_cast<const uint4 *>(src + (size_t)(s0 + r) * HD + c * 8);
     }
-    if (lane == 0) {
+  };
+  const bool one = len <= kSub;
+  if (one) {
+    stage(kb, kvs[0], 0, len);
+    stage(vb, kvs[1], 0, len);
+  }
+  // Scores: warp w takes positions w, w+4, ...; lane l holds dims 4l..4l+3.
+  for (uint32_t s0 = 0; s0 < len; s0 += kSub) {
+    const uint32_t cnt = min((uint32_t)kSub, len - s0);
+    if (!one) {
+      __syncthreads();
+      stage(kb, kvs[0], s0, cnt);
+    }
+    __syncthreads();
+    for (uint32_t i = warp; i < cnt; i += 4) {
+      uint2 raw = *reinterpret_cast<const uint2 *>(&kvs[0][i][4 * lane]);
+      float2 k01 = __half22float2(*reinterpret_cast<__half2 *>(&raw.x));
+      float2 k23 = __half22float2(*reinterpret_cast<__half2 *>(&raw.y));
+      float part[G];
 #pragma unroll
-      for (int g = 0; g < G; g++) sc[g * chunk + i] = part[g] * p.inv_scale;
+      for (int g = 0; g < G; g++) {
+        float s = qr[g][0] * k01.x;
+        s = fmaf(qr[g][1], k01.y, s);
+        s = fmaf(qr[g][2], k23.x, s);
+        s = fmaf(qr[g][3], k23.y, s);
+        part[g] = warp_sum(s);
+      }
+      if (lane == 0) {
+#pragma unroll
+        for (int g = 0; g < G; g++) sc[g * chunk + s0 + i] = part[g] * p.inv_scale;
+      }
     }
   }
   __syncthreads();
@@ -204,14 +230,22 @@ __global__ void __launch_bounds__(128) k_attn_split(AttnParams p) {
   float acc[G][2];
 #pragma unroll
   for (int g = 0; g < G; g++) acc[g][0] = acc[g][1] = 0.f;
-  for (uint32_t i = sub; i < len; i += 2) {
-    float2 v = __half22float2(*reinterpret_cast<const __half2 *>(vb + (size_t)i * HD + 2 * dp));
-#pragma unroll
-    for (int g = 0; g < G; g++) {
-      float e = sc[g * chunk + i];
-      acc[g][0] = fmaf(e, v.x, acc[g][0]);
-      acc[g][1] = fmaf(e, v.y, acc[g][1]);
+  for (uint32_t s0 = 0; s0 < len; s0 += kSub) {
+    const uint32_t cnt = min((uint32_t)kSub, len - s0);
+    if (!one) {
+      stage(vb, kvs[1], s0, cnt);
+      __syncthreads();
     }
+    for (uint32_t i = sub; i < cnt; i += 2) {
+      float2 v = __half22float2(*reinterpret_cast<const __half2 *>(&kvs[1][i][2 * dp]));
+#pragma unroll
+      for (int g = 0; g < G; g++) {
+        float e = sc[g * chunk + s0 + i];
+        acc[g][0] = fmaf(e, v.x, acc[g][0]);
+        acc[g][1] = fmaf(e, v.y, acc[g][1]);
+      }
+    }
+    if (!one) __syncthreads();
   }
 #pragma unroll
   for (int g = 0; g < G; g++) {
@@ -237,9 +271,55 @@ __global__ void __launch_bounds__(128) k_attn_split(AttnParams p) {
   __syncthreads();
   if (ticket != ns - 1) return;
   __threadfence();
-  __shared__ float sred[4];
+  // Statistics of all G heads at once (warp w: heads w, w+4): the chunk
+  // maxima, weights exp(m_s - M) and sums, then every thread (dimension t)
+  // accumulates all heads with the loads of eight chunks in flight. Same
+  // operations in the same order as merge_chunks, so the same bits.
+  __shared__ float wsm[G][kMaxStepSplit], lsm[G][kMaxStepSplit], Ls[G];
+  // the first eight chunks' outputs do not depend on the statistics: load them first
+  float ov[G][8];
+#pragma unroll
+  for (int g = 0; g < G; g++)
+#pragma unroll
+    for (int m = 0; m < 8; m++)
+      if (m < (int)ns) ov[g][m] = __ldcg(&p.opart[(((size_t)bi * p.h + h0 + g) * p.nsplit + m) * HD + t]);
+  for (int g = warp; g < G; g += 4) {
+    const size_t base = ((size_t)bi * p.h + h0 + g) * p.nsplit;
+    float M = -INFINITY;
+    for (uint32_t s2 = lane; s2 < ns; s2 += 32) M = fmaxf(M, __ldcg(&p.ml[(base + s2) * 2]));
+    M = warp_max(M);
+    for (uint32_t s2 = lane; s2 < ns; s2 += 32) {
+      wsm[g][s2] = expf(__ldcg(&p.ml[(base + s2) * 2]) - M);
+      lsm[g][s2] = __ldcg(&p.ml[(base + s2) * 2 + 1]);
+    }
+    __syncwarp();
+    if (lane == 0) {
+      float L = 0.f;
+      for (uint32_t s2 = 0; s2 < ns; s2++) L = fmaf(lsm[g][s2], wsm[g][s2], L);
+      Ls[g] = L;
+    }
+  }
+  __syncthreads();
+  float o[G];
+#pragma unroll
+  for (int g = 0; g < G; g++) o[g] = 0.f;
+  for (uint32_t s0 = 0; s0 < ns; s0 += 8) {
+    if (s0 > 0) {
+#pragma unroll
+      for (int g = 0; g < G; g++)
+#pragma unroll
+        for (int m = 0; m < 8; m++)
+          if (s0 + m < ns) ov[g][m] = __ldcg(&p.opart[(((size_t)bi * p.h + h0 + g) * p.nsplit + s0 + m) * HD + t]);
+    }
+#pragma unroll
+    for (int g = 0; g < G; g++)
+#pragma unroll
+      for (int m = 0; m < 8; m++)
+        if (s0 + m < ns) o[g] = fmaf(ov[g][m], wsm[g][s0 + m], o[g]);
+  }
+#pragma unroll
   for (int g = 0; g < G; g++) {
-    const float v = merge_chunks(p, bi, h0 + g, ns, (uint32_t)t, sred);
+    const float v = o[g] / Ls[g];
     p.out[((size_t)bi * p.h + h0 + g) * HD + t] = v;
     // head h0+g covers elements 128(h0+g).. of the attention output: warp w holds block 4(h0+g)+w
     if (p.xo.limbs) xq_store_block(p.xo, bi, (h0 + g) * 4 + warp, v);
@@ -306,8 +386,10 @@ __global__ void __launch_bounds__(128) k_attention_f32(uint32_t h, uint32_t hk, 
 template <int G, bool STEP = false>
 pai_status_t launch_split(pai_b200_ctx_t *ctx, const AttnParams &p, uint32_t batch) {
   const size_t smem = (size_t)(G * HD + G * p.chunk) * sizeof(float);
-  if (smem > 200 * 1024) return b200_fail(PAI_ERR_UNSUPPORTED, "attn_decode: chunk of %u positions", p.chunk);
-  if (smem > 48 * 1024) {
+  const size_t stat = (size_t)(2 * G * HD + 2 * G + (STEP ? 2 * G * kMaxStepSplit + G : 0)) * sizeof(float) +
+                      2 * kSub * HD * sizeof(__half) + 64;
+  if (smem + stat > 200 * 1024) return b200_fail(PAI_ERR_UNSUPPORTED, "attn_decode: chunk of %u positions", p.chunk);
+  if (smem + stat > 48 * 1024) {
     pai_status_t st = b200_cuda(
         cudaFuncSetAttribute(k_attn_split<G, STEP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
         "k_attn_split smem attribute");
@@ -332,8 +414,11 @@ pai_status_t attn_setup(pai_b200_ctx_t *ctx, uint32_t batch, uint32_t h, uint32_
   if (max_npos == 0 || max_npos > cap) return b200_fail(PAI_ERR_INVALID_ARG, "attn_decode: positions > cache");
   uint32_t chunk, nsplit;
   if (pos) {
-    const uint64_t by_sms = (296 + (uint64_t)hk * batch - 1) / ((uint64_t)hk * batch);
-    nsplit = (uint32_t)std::max<uint64_t>(1, std::min<uint64_t>((max_npos + 31) / 32, by_sms));
+    // chunks of at least 64 positions, about one CTA per SM at the longest
+    // context: the fewer the chunks, the shorter the merge
+    const uint64_t by_sms = (148 + (uint64_t)hk * batch - 1) / ((uint64_t)hk * batch);
+    nsplit = (uint32_t)std::max<uint64_t>(
+        1, std::min<uint64_t>(std::min<uint64_t>((max_npos + 63) / 64, by_sms), kMaxStepSplit));
     chunk = (uint32_t)std::max<uint64_t>(32, ((max_npos + nsplit - 1) / nsplit + 31) / 32 * 32);
   } else {
     const uint64_t want = (max_npos * hk * batch + 295) / 296;
