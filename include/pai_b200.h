@@ -225,6 +225,15 @@ pai_status_t pai_b200_gemv_rmsnorm_f32(pai_b200_ctx_t *ctx, uint32_t type, uint6
                                        uint64_t n, uint64_t k, const void *w, const float *x,
                                        const float *gamma, float eps, const float *residual,
                                        float *y);
+/* Prefill GEMM with Q4_0 weights: Y[m][n] = X[m][k] . W^T (W packed n x k,
+ * X and Y fp32, row-major). pai_ref_gemm_f32 (cpu/reference/ref_ops.c:428-444)
+ * on the dequantised weights -- the executor's GEMM for a prompt of m tokens
+ * (scheduler/scheduler.c:285-343). Runs on the tcgen05 tensor cores with the
+ * weights dequantised to bf16 tiles in shared memory and X rounded to bf16,
+ * fp32 accumulation: results match the fp32 reference to about 2^-8
+ * relative (the benchmark's bar is max-abs-rel 2e-2). */
+pai_status_t pai_b200_gemm_q4_0_f32(pai_b200_ctx_t *ctx, uint64_t m, uint64_t n, uint64_t k,
+                                    const float *x, const void *w, float *y);
 
 /* c = a * gamma * (1/sqrtf(mean(a^2) + eps)) per row of n
  * (pai_ref_rmsnorm_gamma_f32, ref_ops.c:196-216; eps 0 selects 1e-5). */

@@ -142,6 +142,10 @@ class Device:
                                                gamma.ptr, eps, residual.ptr if residual else None,
                                                y.ptr), "gemv_rmsnorm")
 
+    def gemm_q4_0(self, w: PackedMatrix, x: Buffer, y: Buffer, m: int):
+        """Y[m][n] = X[m][k] . W^T on the tensor cores (bf16 tiles, fp32 accumulate)."""
+        check(load().pai_b200_gemm_q4_0_f32(self.ctx, m, w.n, w.k, x.ptr, w.ptr, y.ptr), "gemm_q4_0")
+
     def dequant(self, w: PackedMatrix, out: Buffer):
         check(load().pai_b200_dequant(self.ctx, w.wtype, w.n, w.k, w.ptr, out.ptr), "dequant")
 

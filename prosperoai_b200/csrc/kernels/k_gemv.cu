@@ -51,16 +51,25 @@
 
 namespace {
 
-constexpr int kCons = 8;                     // consumer warps per CTA, one 16-row tile each
-constexpr int kThreads = (kCons + 1) * 32;  // + one producer warp
 constexpr int kStages = 4;                   // depth of the CTA's weight ring
 constexpr int kXSlots = 3;                   // staged-x slots (current, next, one being released)
-// One CTA per SM, two for batch <= 2 (whose consumers need few registers)
-// so twice the warps hide the unpack-MMA-scale latency.
+// CTA shape: consumer warps (one 16-row tile each; a group is kConsT
+// tiles) + one producer warp, one CTA per SM. Batch <= 2 needs few
+// registers, so its CTA has 16 consumers (twice the warps to hide the
+// unpack-MMA-scale latency) sharing one ring. Two CTAs of 8 per SM do the
+// same work but the second CTA's warps lose issue priority to the first's
+// and finish about 10% later.
+#ifndef B200_GEMV_WIDE
+#define B200_GEMV_WIDE 1
+#endif
 template <int NT>
-constexpr int kCtasPerSm = NT == 1 ? 2 : 1;
+constexpr int kConsT = (NT == 1 && B200_GEMV_WIDE) ? 16 : 8;
 template <int NT>
-constexpr size_t kSmemCap = NT == 1 ? 110 * 1024 : 220 * 1024;  // dynamic shared memory per CTA
+constexpr int kThreadsT = (kConsT<NT> + 1) * 32;
+template <int NT>
+constexpr int kCtasPerSm = (NT == 1 && !B200_GEMV_WIDE) ? 2 : 1;
+template <int NT>
+constexpr size_t kSmemCap = kCtasPerSm<NT> == 2 ? 110 * 1024 : 220 * 1024;  // dynamic shared memory per CTA
 constexpr uint32_t M4 = 0x0F0F0F0Fu;
 constexpr uint64_t kWaitLimit = 2000000000ull;  // ns before a wait gives up (2 s)
 
@@ -426,7 +435,8 @@ __device__ void settle_splits(const GemvP &p, uint32_t (&tiles)[2], uint32_t (&n
 // instead of paying one L2 round trip per block.
 constexpr int kPB = 16;
 template <int NT>
-__device__ void norm_prologue(const GemvP &p, const XS &slot, int c, int lane, double (&red)[kCons][8]) {
+__device__ void norm_prologue(const GemvP &p, const XS &slot, int c, int lane, double (&red)[kConsT<NT>][8]) {
+  constexpr int kCons = kConsT<NT>;
   const uint32_t nthr = kCons * 32, nblk = slot.quads * 4, kk = (uint32_t)p.xq.k;
   for (uint32_t vec = 0; vec < p.batch; vec++) {
     const float *xr = p.xf + (size_t)vec * kk;
@@ -477,7 +487,8 @@ __device__ void norm_prologue(const GemvP &p, const XS &slot, int c, int lane, d
 }
 
 template <uint32_t T, int NT>
-__global__ void __launch_bounds__(kThreads, kCtasPerSm<NT>) k_gemv(GemvP p) {
+__global__ void __launch_bounds__(kThreadsT<NT>, kCtasPerSm<NT>) k_gemv(GemvP p) {
+  constexpr int kCons = kConsT<NT>;
   using Un = Unit<T>;
   constexpr int U = Un::U, XPU = Un::XPU;
   constexpr uint32_t GQ = kCons * Un::QB, GS = kCons * Un::SB;  // bytes of one unit of a group
@@ -719,6 +730,7 @@ template <uint32_t T, int NT>
 pai_status_t launch_t(pai_b200_ctx_t *ctx, GemvP p) {
   auto kern = k_gemv<T, NT>;
   using Un = Unit<T>;
+  constexpr int kCons = kConsT<NT>;
   const size_t ring = (size_t)kStages * Un::U * kCons * (Un::QB + Un::SB);
   p.ngroups = (p.ntiles + kCons - 1) / kCons;
   const uint64_t total = (uint64_t)p.ngroups * p.units;
@@ -773,7 +785,7 @@ pai_status_t launch_t(pai_b200_ctx_t *ctx, GemvP p) {
   p.tile_cnt = cnt;
   p.grp_cnt = cnt + p.ntiles;
   p.err = b200_ctx_errflag(ctx);
-  b200_launch(ctx, kern, dim3(grid), dim3(kThreads), smem, p);
+  b200_launch(ctx, kern, dim3(grid), dim3(kThreadsT<NT>), smem, p);
   return b200_launched(ctx, 1, "k_gemv");
 }
 
