@@ -34,8 +34,6 @@ namespace {
 
 constexpr int kFT = 256;          // output features per CTA (two M=128 MMAs)
 constexpr int kBK = 64;           // K per stage: one 128-byte row of bf16
-constexpr int kGStages = 4;       // ring depth
-constexpr int kGThreads = 256;    // 8 warps
 constexpr int kAStage = kFT * kBK * 2;  // 32 KB of bf16 weights per stage
 constexpr uint64_t kGWaitLimit = 2000000000ull;
 
@@ -92,19 +90,21 @@ struct GemmP {
   const uint8_t *qs, *sc;  // packed Q4_0 weights
   const uint8_t *xp;       // activations, bf16, swizzled, [token tile][K chunk][BN][128 B]
   float *y;                // [M][N]
+  float *partial;          // split-K: [split][M][N]
+  uint32_t *cnt;           // split-K tickets, one per output tile, left at zero
   uint32_t *err;
-  uint32_t m, n, ntiles, nkc;  // tokens, features, weight tiles, K chunks of 64
+  uint32_t m, n, ntiles, nunits, ksplit;  // tokens, features, weight tiles, K units of 128, K splits
 };
 
-// Dequantise half a unit (2 blocks, 64 weights) of one 16-row tile from the
-// registers of its packed piece into the swizzled bf16 stage.
-__device__ __forceinline__ void dequant_half(uint8_t *a_stage, uint32_t tile_row0, const uint4 &q0, const uint4 &q1,
-                                             const uint2 &d0, const uint2 &d1, int half, int lane) {
+// Dequantise half a unit (2 blocks, 64 weights) of one 16-row tile from its
+// packed piece in shared memory into the swizzled bf16 stage.
+__device__ __forceinline__ void dequant_half(uint8_t *a_stage, uint32_t tile_row0, const uint8_t *piece_qs,
+                                             const uint8_t *piece_sc, int half, int lane) {
   const uint32_t rl = lane >> 2, c = lane & 3;
 #pragma unroll
   for (int h = 0; h < 2; h++) {
-    const uint4 &q = h ? q1 : q0;
-    const uint2 &dd = h ? d1 : d0;
+    const uint4 q = *reinterpret_cast<const uint4 *>(piece_qs + h * 512 + lane * 16);
+    const uint2 dd = *reinterpret_cast<const uint2 *>(piece_sc + h * 64 + rl * 8);
     const uint32_t fr = tile_row0 + rl + 8 * h;  // feature row within the CTA's 256
     uint8_t *blk = a_stage + (fr >> 7) * (128 * 128);
     const uint32_t r = fr & 127;
@@ -134,34 +134,51 @@ __device__ __forceinline__ void dequant_half(uint8_t *a_stage, uint32_t tile_row
   }
 }
 
+constexpr int kWorkers = 8;                       // dequantising warps
+constexpr int kGThreadsWS = (kWorkers + 3) * 32;  // + raw-W producer, X producer, MMA issuer
+constexpr int kRawStages = 3;                     // packed-weight units in flight
+constexpr uint32_t kRawStage = 16 * 1024 + 16 * 128;  // one unit of the CTA's 16 tiles: codes, then headers
 template <int BN>
-__global__ void __launch_bounds__(kGThreads, 1) k_gemm_q4_0(GemmP p) {
-  constexpr uint32_t kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;  // power of two for BN in {16, 64, 128}
+constexpr int kAStages = BN == 256 ? 2 : 3;       // bf16 stages (shared memory bound)
+
+template <int BN>
+__global__ void __launch_bounds__(kGThreadsWS, 1) k_gemm_q4_0(GemmP p) {
+  constexpr uint32_t kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;  // power of two for BN in {16, 64, 128, 256}
   constexpr uint32_t kBStage = BN * 128;
   constexpr uint32_t kIdesc = idesc_bf16(BN);
+  constexpr int SA = kAStages<BN>;
   extern __shared__ __align__(1024) uint8_t gsm_raw[];
   // 1024-byte alignment of the swizzled stages
   uint8_t *gsm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~(uintptr_t)1023);
-  uint8_t *a_st = gsm;                                 // [stage][2 acc][128 rows][128 B]
-  uint8_t *b_st = gsm + (size_t)kGStages * kAStage;    // [stage][BN rows][128 B]
-  __shared__ __align__(8) uint64_t full[kGStages], wready[kGStages], empty[kGStages];
-  __shared__ uint32_t tmem_base_s;
+  uint8_t *a_st = gsm;                                // [SA][2 acc][128 rows][128 B]
+  uint8_t *b_st = a_st + (size_t)SA * kAStage;        // [SA][BN rows][128 B]
+  uint8_t *r_st = b_st + (size_t)SA * kBStage;        // [kRawStages][16 KB codes | 2 KB headers]
+  __shared__ __align__(8) uint64_t rfull[kRawStages], rempty[kRawStages];
+  __shared__ __align__(8) uint64_t afull[SA], bfull[SA], aempty[SA];
+  __shared__ uint32_t tmem_base_s, ticket_s;
   __shared__ int abort_s;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const uint32_t f0 = blockIdx.x * kFT;                 // first feature of the CTA
-  const uint32_t tt = blockIdx.y, m0 = tt * BN;         // token tile
-  const uint32_t tile0 = f0 / 16;
+  const uint32_t f0 = blockIdx.x * kFT, tile0 = f0 / 16;        // first feature and weight tile
+  const uint32_t tt = blockIdx.y, m0 = tt * BN;                  // token tile
+  const uint32_t z = blockIdx.z;                                 // K split
+  const uint32_t u0 = z * p.nunits / p.ksplit, u1 = (z + 1) * p.nunits / p.ksplit;
+  const uint32_t nu = u1 - u0, nkt = 2 * nu;                    // units and 64-wide K chunks of this CTA
+  const uint32_t nv = min(16u, p.ntiles - min(p.ntiles, tile0));  // weight tiles present
   if (tid == 0) {
-    for (int s = 0; s < kGStages; s++) {
-      mbar_init(&full[s], 1);
-      mbar_init(&wready[s], kGThreads);
-      mbar_init(&empty[s], 1);
+    for (int s = 0; s < kRawStages; s++) {
+      mbar_init(&rfull[s], 1);
+      mbar_init(&rempty[s], kWorkers * 32);
+    }
+    for (int s = 0; s < SA; s++) {
+      mbar_init(&afull[s], kWorkers * 32);
+      mbar_init(&bfull[s], 1);
+      mbar_init(&aempty[s], 1);
     }
     abort_s = 0;
     fence_mbar_init();
   }
-  if (warp == 0) {
+  if (warp == kWorkers + 2) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_s)),
                  "r"(kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -170,102 +187,146 @@ __global__ void __launch_bounds__(kGThreads, 1) k_gemm_q4_0(GemmP p) {
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_base_s;
-
-  // this warp's two weight tiles: registers of the current unit (c*) and of
-  // the next one (n*), loaded while the current unit is dequantised
-  const uint32_t tA = tile0 + 2 * warp, tB = tA + 1, nunits = p.nkc / 2;
-  struct Piece {
-    uint4 a0, a1, b0, b1;
-    uint2 da0, da1, db0, db1;
-  };
-  auto load_unit = [&](uint32_t u, Piece &pc) {
-    pc = Piece{};
-    if (tA < p.ntiles) {
-      const uint8_t *pq = p.qs + ((size_t)u * p.ntiles + tA) * 1024, *ps = p.sc + ((size_t)u * p.ntiles + tA) * 128;
-      pc.a0 = *reinterpret_cast<const uint4 *>(pq + lane * 16);
-      pc.a1 = *reinterpret_cast<const uint4 *>(pq + 512 + lane * 16);
-      pc.da0 = *reinterpret_cast<const uint2 *>(ps + (lane >> 2) * 8);
-      pc.da1 = *reinterpret_cast<const uint2 *>(ps + 64 + (lane >> 2) * 8);
-    }
-    if (tB < p.ntiles) {
-      const uint8_t *pq = p.qs + ((size_t)u * p.ntiles + tB) * 1024, *ps = p.sc + ((size_t)u * p.ntiles + tB) * 128;
-      pc.b0 = *reinterpret_cast<const uint4 *>(pq + lane * 16);
-      pc.b1 = *reinterpret_cast<const uint4 *>(pq + 512 + lane * 16);
-      pc.db0 = *reinterpret_cast<const uint2 *>(ps + (lane >> 2) * 8);
-      pc.db1 = *reinterpret_cast<const uint2 *>(ps + 64 + (lane >> 2) * 8);
-    }
-  };
-  Piece cur, nxt;
-  load_unit(0, cur);
   bool ok = true;
-  for (uint32_t kt = 0; kt < p.nkc && ok; kt++) {
-    const uint32_t s = kt % kGStages, ph = (kt / kGStages) & 1u;
-    if (kt >= (uint32_t)kGStages && !mbar_wait(&empty[s], ph ^ 1u, kGWaitLimit)) {
-      ok = false;
-      break;
+
+  if (warp == kWorkers) {
+    // ---- packed weights: one unit of the CTA's tiles per raw stage ----
+    if (lane == 0) {
+      for (uint32_t i = 0; i < nu && ok; i++) {
+        const uint32_t rs = i % kRawStages;
+        if (i >= (uint32_t)kRawStages && !mbar_wait(&rempty[rs], ((i / kRawStages) - 1) & 1u, kGWaitLimit)) {
+          ok = false;
+          break;
+        }
+        uint8_t *dst = r_st + (size_t)rs * kRawStage;
+        const size_t piece = (size_t)(u0 + i) * p.ntiles + tile0;
+        if (nv) {
+          mbar_expect_tx(&rfull[rs], nv * (1024 + 128));
+          bulk_g2s(dst, p.qs + piece * 1024, nv * 1024, &rfull[rs]);
+          bulk_g2s(dst + 16 * 1024, p.sc + piece * 128, nv * 128, &rfull[rs]);
+        } else {
+          mbar_arrive(&rfull[rs]);
+        }
+      }
     }
-    if (tid == 0) {
-      mbar_expect_tx(&full[s], kBStage);
-      bulk_g2s(b_st + (size_t)s * kBStage, p.xp + ((size_t)tt * p.nkc + kt) * kBStage, kBStage, &full[s]);
+  } else if (warp == kWorkers + 1) {
+    // ---- activations: one 64-wide K chunk per stage ----
+    if (lane == 0) {
+      for (uint32_t j = 0; j < nkt && ok; j++) {
+        const uint32_t s = j % SA;
+        if (j >= (uint32_t)SA && !mbar_wait(&aempty[s], ((j / SA) - 1) & 1u, kGWaitLimit)) {
+          ok = false;
+          break;
+        }
+        mbar_expect_tx(&bfull[s], kBStage);
+        bulk_g2s(b_st + (size_t)s * kBStage, p.xp + ((size_t)tt * (2 * p.nunits) + 2 * u0 + j) * kBStage, kBStage,
+                 &bfull[s]);
+      }
     }
-    const int half = kt & 1;
-    if (half == 0 && kt / 2 + 1 < nunits) load_unit(kt / 2 + 1, nxt);
-    uint8_t *as = a_st + (size_t)s * kAStage;
-    dequant_half(as, 32 * warp, cur.a0, cur.a1, cur.da0, cur.da1, half, lane);
-    dequant_half(as, 32 * warp + 16, cur.b0, cur.b1, cur.db0, cur.db1, half, lane);
-    if (half == 1) cur = nxt;
-    fence_proxy_async();  // generic-proxy stores -> visible to the tensor core
-    mbar_arrive(&wready[s]);
-    if (tid == 0) {
-      if (!mbar_wait(&wready[s], ph, kGWaitLimit) || !mbar_wait(&full[s], ph, kGWaitLimit)) {
+  } else if (warp == kWorkers + 2) {
+    // ---- MMA issue ----
+    if (lane == 0) {
+      for (uint32_t j = 0; j < nkt && ok; j++) {
+        const uint32_t s = j % SA, ph = (j / SA) & 1u;
+        if (!mbar_wait(&afull[s], ph, kGWaitLimit) || !mbar_wait(&bfull[s], ph, kGWaitLimit)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t abase = smem_u32(a_st + (size_t)s * kAStage), bbase = smem_u32(b_st + (size_t)s * kBStage);
+#pragma unroll
+        for (int acc = 0; acc < 2; acc++)
+#pragma unroll
+          for (int k = 0; k < kBK / 16; k++)
+            mma_bf16(tmem + acc * BN, sdesc(abase + acc * (128 * 128) + k * 32), sdesc(bbase + k * 32), kIdesc,
+                     (j > 0 || k > 0) ? 1u : 0u);
+        mma_commit(&aempty[s]);
+      }
+    }
+  } else {
+    // ---- dequantising warps: warp w owns tiles 2w, 2w+1 of the CTA ----
+    for (uint32_t i = 0; i < nu && ok; i++) {
+      const uint32_t rs = i % kRawStages;
+      if (!mbar_wait(&rfull[rs], (i / kRawStages) & 1u, kGWaitLimit)) {
         ok = false;
         break;
       }
-      tc_fence_after();
-      const uint32_t abase = smem_u32(as), bbase = smem_u32(b_st + (size_t)s * kBStage);
-#pragma unroll
-      for (int acc = 0; acc < 2; acc++)
-#pragma unroll
-        for (int j = 0; j < kBK / 16; j++)
-          mma_bf16(tmem + acc * BN, sdesc(abase + acc * (128 * 128) + j * 32), sdesc(bbase + j * 32), kIdesc,
-                   (kt > 0 || j > 0) ? 1u : 0u);
-      mma_commit(&empty[s]);
+      const uint8_t *raw = r_st + (size_t)rs * kRawStage;
+      for (int half = 0; half < 2 && ok; half++) {
+        const uint32_t j = 2 * i + half, s = j % SA;
+        if (j >= (uint32_t)SA && !mbar_wait(&aempty[s], ((j / SA) - 1) & 1u, kGWaitLimit)) {
+          ok = false;
+          break;
+        }
+        uint8_t *as = a_st + (size_t)s * kAStage;
+        for (int tl = 0; tl < 2; tl++) {
+          const uint32_t lt = 2 * warp + tl;  // tile within the CTA
+          if (lt < nv) dequant_half(as, 16 * lt, raw + lt * 1024, raw + 16 * 1024 + lt * 128, half, lane);
+        }
+        fence_proxy_async();  // generic-proxy stores -> visible to the tensor core
+        mbar_arrive(&afull[s]);
+      }
+      mbar_arrive(&rempty[rs]);
     }
   }
   if (!ok) {
     atomicExch(p.err, 1u);
     abort_s = 1;
   }
-  // all MMAs done: the last stage's commit
-  const uint32_t kl = p.nkc - 1;
-  if (ok && !mbar_wait(&empty[kl % kGStages], (kl / kGStages) & 1u, kGWaitLimit)) {
+  // all MMAs done: the commit of the last stage
+  if (nkt && !mbar_wait(&aempty[(nkt - 1) % SA], ((nkt - 1) / SA) & 1u, kGWaitLimit)) {
     atomicExch(p.err, 1u);
     abort_s = 1;
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (!abort_s) {
+  const bool split = p.ksplit > 1;
+  if (!abort_s && warp < kWorkers) {
     // epilogue: warp w reads TMEM lanes 32(w%4).. of accumulator w/4
     const uint32_t g = warp & 3, acc = warp >> 2;
     const uint32_t feat = f0 + acc * 128 + g * 32 + lane;
-#pragma unroll
+    float *dst = split ? p.partial + (size_t)z * p.m * p.n : p.y;
+#pragma unroll 1
     for (int c0 = 0; c0 < BN; c0 += 16) {
       uint32_t v[16];
       tmem_ld16(tmem + ((g * 32u) << 16) + acc * BN + c0, v);
       tmem_ld_wait();
       if (feat < p.n) {
 #pragma unroll
-        for (int j = 0; j < 16; j++) {
-          const uint32_t m = m0 + c0 + j;
-          if (m < p.m) p.y[(size_t)m * p.n + feat] = __uint_as_float(v[j]);
+        for (int jj = 0; jj < 16; jj++) {
+          const uint32_t m = m0 + c0 + jj;
+          if (m < p.m) dst[(size_t)m * p.n + feat] = __uint_as_float(v[jj]);
         }
       }
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  if (warp == kWorkers + 2) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  if (!split || abort_s) return;
+  // split K: the last split of this output tile to finish adds the parts in order
+  __threadfence();
+  __syncthreads();
+  const uint32_t tile_id = blockIdx.y * gridDim.x + blockIdx.x;
+  if (tid == 0) ticket_s = atomicAdd(&p.cnt[tile_id], 1u);
+  __syncthreads();
+  if (ticket_s != p.ksplit - 1) return;
+  __threadfence();
+  for (uint32_t e = tid; e < kFT * BN; e += blockDim.x) {
+    const uint32_t f = f0 + e % kFT, m = m0 + e / kFT;
+    if (f >= p.n || m >= p.m) continue;
+    float part[8];  // ksplit <= 8: all loads in flight, then the sum in split order
+#pragma unroll
+    for (uint32_t q = 0; q < 8; q++)
+      if (q < p.ksplit) part[q] = __ldcg(&p.partial[((size_t)q * p.m + m) * p.n + f]);
+    float a = 0.f;
+#pragma unroll
+    for (uint32_t q = 0; q < 8; q++)
+      if (q < p.ksplit) a += part[q];
+    p.y[(size_t)m * p.n + f] = a;
+  }
+  if (tid == 0) p.cnt[tile_id] = 0;
 }
 
 // X fp32 [M][K] -> bf16 in the GEMM's operand layout: [token tile][K chunk of
@@ -298,11 +359,21 @@ __global__ void __launch_bounds__(256) k_gemm_xprep(const float *__restrict__ x,
 template <int BN>
 pai_status_t gemm_launch(pai_b200_ctx_t *ctx, uint32_t m, uint32_t n, uint32_t k, const float *x, const void *w,
                          float *y) {
-  const uint32_t nkc = (uint32_t)(b200_units(PAI_B200_Q4_0, k) * 2);  // K chunks of 64 (whole units)
-  const uint32_t mtiles = (m + BN - 1) / BN;
+  const uint32_t nunits = (uint32_t)b200_units(PAI_B200_Q4_0, k), nkc = 2 * nunits;  // K chunks of 64
+  const uint32_t mtiles = (m + BN - 1) / BN, ftiles = (n + kFT - 1) / kFT;
+  // K split when the output tiles alone leave SMs idle (small prompts)
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, b200_ctx_device(ctx));
+  uint32_t ksplit = 1;
+  while (ksplit < 8 && (uint64_t)ftiles * mtiles * ksplit * 2 <= (uint64_t)sms && nunits / (ksplit * 2) >= 4)
+    ksplit *= 2;
   const uint64_t xp_bytes = (uint64_t)mtiles * nkc * BN * 128;
   void *xp = nullptr;
   pai_status_t st = b200_ctx_xq(ctx, xp_bytes, &xp);
+  if (st) return st;
+  float *partial = nullptr;
+  uint32_t *cnt = nullptr;
+  st = b200_ctx_scratch(ctx, ksplit > 1 ? (uint64_t)ksplit * m * n : 0, ftiles * mtiles, &partial, &cnt);
   if (st) return st;
   cudaStream_t s = (cudaStream_t)b200_ctx_stream(ctx);
   const uint64_t nchunks = (uint64_t)mtiles * BN * nkc * 8;
@@ -314,12 +385,15 @@ pai_status_t gemm_launch(pai_b200_ctx_t *ctx, uint32_t m, uint32_t n, uint32_t k
   p.sc = p.qs + b200_sc_offset(PAI_B200_Q4_0, n, k);
   p.xp = (const uint8_t *)xp;
   p.y = y;
+  p.partial = partial;
+  p.cnt = cnt;
   p.err = b200_ctx_errflag(ctx);
   p.m = m;
   p.n = n;
   p.ntiles = (uint32_t)b200_ntiles(n);
-  p.nkc = nkc;
-  const size_t smem = 1024 + (size_t)kGStages * (kAStage + BN * 128);
+  p.nunits = nunits;
+  p.ksplit = ksplit;
+  const size_t smem = 1024 + (size_t)kAStages<BN> * (kAStage + BN * 128) + (size_t)kRawStages * kRawStage;
   static bool attr_set[64];
   const int dev = b200_ctx_device(ctx);
   if (dev < 0 || dev >= 64 || !attr_set[dev]) {
@@ -328,8 +402,8 @@ pai_status_t gemm_launch(pai_b200_ctx_t *ctx, uint32_t m, uint32_t n, uint32_t k
     if (st) return st;
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
-  const dim3 grid((n + kFT - 1) / kFT, mtiles);
-  k_gemm_q4_0<BN><<<grid, kGThreads, smem, s>>>(p);
+  const dim3 grid(ftiles, mtiles, ksplit);
+  k_gemm_q4_0<BN><<<grid, kGThreadsWS, smem, s>>>(p);
   return b200_launched(ctx, 1, "k_gemm_q4_0");
 }
 
@@ -341,10 +415,11 @@ extern "C" pai_status_t pai_b200_gemm_q4_0_f32(pai_b200_ctx_t *ctx, uint64_t m, 
   if (m == 0 || n == 0 || k == 0 || k % 32)
     return b200_fail(PAI_ERR_MISMATCH, "gemm: k=%llu is not a whole number of Q4_0 blocks", (unsigned long long)k);
   if (m > 0x7FFFFFFFull || n > 0x7FFFFFF0ull || k > 0x7FFFFFFFull || (n + kFT - 1) / kFT > 0x7FFFFFFFull ||
-      (m + 15) / 16 > 65535)
+      (m + 15) / 16 > 65535 || m * n > (1ull << 40))
     return b200_fail(PAI_ERR_UNSUPPORTED, "gemm: shape too large");
   if ((uintptr_t)w & 255) return b200_fail(PAI_ERR_INVALID_ARG, "gemm: weights not 256-byte aligned");
   if (m <= 16) return gemm_launch<16>(ctx, (uint32_t)m, (uint32_t)n, (uint32_t)k, x, w, y);
   if (m <= 64) return gemm_launch<64>(ctx, (uint32_t)m, (uint32_t)n, (uint32_t)k, x, w, y);
-  return gemm_launch<128>(ctx, (uint32_t)m, (uint32_t)n, (uint32_t)k, x, w, y);
+  if (m <= 128) return gemm_launch<128>(ctx, (uint32_t)m, (uint32_t)n, (uint32_t)k, x, w, y);
+  return gemm_launch<256>(ctx, (uint32_t)m, (uint32_t)n, (uint32_t)k, x, w, y);
 }

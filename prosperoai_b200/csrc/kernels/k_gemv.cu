@@ -54,13 +54,14 @@ namespace {
 constexpr int kStages = 4;                   // depth of the CTA's weight ring
 constexpr int kXSlots = 3;                   // staged-x slots (current, next, one being released)
 // CTA shape: consumer warps (one 16-row tile each; a group is kConsT
-// tiles) + one producer warp, one CTA per SM. Batch <= 2 needs few
-// registers, so its CTA has 16 consumers (twice the warps to hide the
-// unpack-MMA-scale latency) sharing one ring. Two CTAs of 8 per SM do the
-// same work but the second CTA's warps lose issue priority to the first's
-// and finish about 10% later.
+// tiles) + one producer warp. Batch <= 2 needs few registers and runs two
+// CTAs of 8 consumers per SM, the rest one CTA of 8. With B200_GEMV_WIDE=1
+// batch <= 2 runs one CTA of 16 consumers per SM instead: the 66 MB
+// gate/up matrix is 7% faster that way (two CTAs on one SM do not share
+// issue slots evenly), the 0.5 GB lm head 3% slower and the decode step as
+// a whole 0.5% slower, so it is off.
 #ifndef B200_GEMV_WIDE
-#define B200_GEMV_WIDE 1
+#define B200_GEMV_WIDE 0
 #endif
 template <int NT>
 constexpr int kConsT = (NT == 1 && B200_GEMV_WIDE) ? 16 : 8;
