@@ -48,6 +48,74 @@ def peaks():
         return 6650.0, "fallback"
 
 
+def tensor_peak():
+    """bf16 dense TFLOP/s: the measured burst figure (a kernel timed alone)."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def prefill_gemm(dev, iters=12):
+    """Config 2: the Q4_0 prefill GEMM Y[M,14336] = X[M,4096] . W^T on the
+    tcgen05 tensor cores (X f32 -> bf16 tiles, W dequantised to bf16 in
+    shared memory, fp32 accumulate in TMEM), for M in 16/128/512/2048.
+    Rotates over 4 distinct weight copies (4 x 33 MB > L2) so every launch
+    streams its weights from HBM, as successive layers of a prefill do.
+    Timed with CUDA events; the time covers the X conversion kernel and
+    the GEMM (the whole call)."""
+    from prosperoai_b200 import _native
+    from prosperoai_b200.api import Buffer
+    L = _native.load()
+    n, k, t = CFG_8B["n_ff"], CFG_8B["n_embd"], 2
+    rb = L.pai_b200_block_bytes(t, k)
+    copies = 4
+    tmp = dev.alloc(n * k * 4)
+    blk = dev.alloc(n * rb)
+    offs = dev.put(np.arange(n, dtype=np.uint64) * rb)
+    mats = []
+    for c in range(copies):
+        _native.check(L.pai_b200_synth_blocks(dev.ctx, t, n, k, SEED + 2000 + c, 0.02, tmp.ptr,
+                                              blk.ptr), "synth")
+        w = Buffer(dev, L.pai_b200_packed_bytes(t, n, k))
+        _native.check(L.pai_b200_pack(dev.ctx, t, n, k, blk.ptr, offs.ptr, w.ptr), "pack")
+        mats.append(w)
+    tmp.free()
+    blk.free()
+    peak, kind = tensor_peak()
+    out = {"workload": "Q4_0 GEMM N=14336 K=4096 (config 2), bf16 tiles, fp32 accumulate",
+           "kernel": "k_gemm (tcgen05.mma kind::f16, TMEM accumulators) + k_gemm_xprep",
+           "peak_tflops": peak, "peak_kind": kind, "l2": "4 rotating weight copies (132 MB)",
+           "by_m": {}}
+    e0, e1 = C.c_void_p(), C.c_void_p()
+    L.pai_b200_event_create(dev.ctx, C.byref(e0))
+    L.pai_b200_event_create(dev.ctx, C.byref(e1))
+    for m in (16, 128, 512, 2048):
+        x = dev.put(np.random.default_rng(m).standard_normal((m, k)).astype(np.float32))
+        y = dev.alloc(m * n * 4)
+        for i in range(4):
+            _native.check(L.pai_b200_gemm_q4_0_f32(dev.ctx, m, n, k, x.ptr, mats[i % copies].ptr,
+                                                   y.ptr), "gemm")
+        dev.sync()
+        L.pai_b200_event_record(dev.ctx, e0)
+        for i in range(iters):
+            L.pai_b200_gemm_q4_0_f32(dev.ctx, m, n, k, x.ptr, mats[i % copies].ptr, y.ptr)
+        L.pai_b200_event_record(dev.ctx, e1)
+        ms = C.c_float()
+        _native.check(L.pai_b200_event_elapsed(e0, e1, C.byref(ms)), "elapsed")
+        dev.sync()
+        per = ms.value / iters
+        tf = 2.0 * m * n * k / (per * 1e-3) / 1e12
+        out["by_m"][str(m)] = {"us": round(per * 1e3, 2), "tflops": round(tf, 1),
+                               "frac": round(tf / peak, 4)}
+        x.free()
+        y.free()
+    for w in mats:
+        w.free()
+    return out
+
+
 class Clocks:
     """Sample nvidia-smi clocks and throttle reasons during the timed region."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -272,6 +340,7 @@ def gpu_arm(args):
     result = None
     if rank == 0:
         roof = None if args.no_roofline else gemv_roofline(dev, hbm, kind)
+        gemm = None if args.no_roofline else prefill_gemm(dev)
         cpu = None if args.no_cpu_baseline else cpu_baseline_port(dev)
         value = world * B * K / (t_dev * 1e-3)
         result = {
@@ -289,6 +358,7 @@ def gpu_arm(args):
                     "h2d_bytes_per_step": 4 * B, "d2h_bytes_per_step": 4 * B},
             "gpu_launches": int(launches),
             "roofline": roof,
+            "prefill_gemm": gemm,
             "step_roofline": {"bytes_per_step": int(step_bytes), "achieved": round(step_gbs, 1),
                               "peak": hbm, "unit": "GB/s", "frac": round(step_gbs / hbm, 4),
                               "peak_kind": kind},
@@ -434,10 +504,18 @@ def main():
                     help="prompt length fed before timing (profiling runs use a short one)")
     ap.add_argument("--kernel-only", action="store_true",
                     help="time only the dominant GEMV (28672x4096 Q4_0) and print its roofline line")
+    ap.add_argument("--gemm-only", action="store_true",
+                    help="time only the config-2 prefill GEMM and print its line")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     rank, world, local = dist_env()
+    if args.gemm_only:
+        from prosperoai_b200.api import Device
+        dev = Device(local)
+        print(json.dumps(prefill_gemm(dev)), flush=True)
+        dev.close()
+        return
     if args.kernel_only:
         from prosperoai_b200.api import Device
         dev = Device(local)

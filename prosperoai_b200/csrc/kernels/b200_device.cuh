@@ -243,6 +243,53 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint64
       return false;
   }
 }
+// As mbar_wait, but each probe lets the thread sleep until the phase
+// completes or `hint_ns` passes (mbarrier.try_wait's suspend-time hint), so
+// warps waiting in a warp-specialised pipeline take no issue slots from the
+// warps doing the work.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity, uint64_t limit_ns,
+                                                uint32_t hint_ns = 100000u) {
+  const uint32_t a = smem_u32(bar);
+  uint64_t t0 = 0;
+  for (uint32_t it = 0;; it++) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(a), "r"(parity), "r"(hint_ns)
+        : "memory");
+    if (done) return true;
+    const uint64_t now = globaltimer_ns();
+    if (it == 0)
+      t0 = now;
+    else if (now - t0 > limit_ns)
+      return false;
+  }
+}
+// As mbar_wait, but polls with the non-blocking mbarrier.test_wait, so the
+// thread sees the phase complete without a suspend/wake-up round trip: for
+// the single threads (copy producers, MMA issuer) on a pipeline's critical
+// path. Reads the clock only every 256 polls.
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t *bar, uint32_t parity, uint64_t limit_ns) {
+  const uint32_t a = smem_u32(bar);
+  uint64_t t0 = 0;
+  for (uint32_t it = 0;; it++) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if ((it & 255u) == 0) {
+      const uint64_t now = globaltimer_ns();
+      if (it == 0)
+        t0 = now;
+      else if (now - t0 > limit_ns)
+        return false;
+    }
+  }
+}
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }

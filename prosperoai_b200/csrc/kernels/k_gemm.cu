@@ -6,12 +6,14 @@
 //
 // Tiling ("swap AB"): a CTA owns 256 output features x BN tokens. The
 // weights are the MMA's A operand (two M=128 MMAs, one TMEM accumulator
-// each) and the activations its B operand (N = BN = 16, 64 or 128), so a
-// 16-token prefill wastes no MMA rows. K advances 64 at a time through a
-// 4-stage shared-memory ring:
-//   - W: the 8 warps dequantise the packed Q4_0 pieces of the stage (2
-//     tiles of 16 rows each, loaded into registers one unit ahead) to bf16
-//     and store them in the canonical K-major 128-byte-swizzle layout;
+// each) and the activations its B operand (N = BN = 16, 64, 128 or 256), so
+// a 16-token prefill wastes no MMA rows. K advances 64 at a time through a
+// 2- to 4-stage shared-memory ring:
+//   - W: one thread streams the packed Q4_0 pieces of the CTA's 16 tiles,
+//     one 128-wide K unit at a time, into a 3-deep raw ring (bulk copies);
+//     16 warps, one per tile, dequantise them to bf16 (each weight rounded
+//     once from the reference's fp32 value, see dq_pair) and store them in
+//     the canonical K-major 128-byte-swizzle layout;
 //   - X: converted to bf16 once per call by k_gemm_xprep into the same
 //     swizzled layout, tile by tile, so one bulk copy (cp.async.bulk, no
 //     multicast) moves a stage's activations;
@@ -19,13 +21,15 @@
 //     halves are in place and commits them to the stage's mbarrier, which
 //     frees the stage for refilling.
 // The epilogue reads each accumulator from TMEM (tcgen05.ld, 32 lanes per
-// warp) and writes fp32 Y. Every mbarrier wait is bounded (2 s); on timeout
+// warp) and writes fp32 Y; with a K split, each split writes its part and
+// the last to finish adds all parts in split order (bit-reproducible). Every mbarrier wait is bounded (2 s); on timeout
 // the CTA raises the context's error flag, still frees its TMEM and exits.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <type_traits>
 
 #include "../b200_internal.h"
 #include "b200_device.cuh"
@@ -37,11 +41,8 @@ constexpr int kBK = 64;           // K per stage: one 128-byte row of bf16
 constexpr int kAStage = kFT * kBK * 2;  // 32 KB of bf16 weights per stage
 constexpr uint64_t kGWaitLimit = 2000000000ull;
 
-// Byte offset of element (row, k) of a [rows][64] bf16 block in the 128-byte
-// swizzle layout: 16-byte chunk c of row r sits at chunk c ^ (r % 8).
-__device__ __forceinline__ uint32_t sw128(uint32_t row, uint32_t k) {
-  return row * 128u + ((((k >> 3) ^ row) & 7u) << 4) + (k & 7u) * 2u;
-}
+// Stages are [rows][64] bf16 in the 128-byte swizzle layout: 16-byte chunk c
+// of row r sits at chunk position c ^ (r % 8).
 
 // Shared-memory matrix descriptor (tcgen05): K-major, 128-byte swizzle,
 // 8-row groups 1024 bytes apart (stride byte offset), leading byte offset
@@ -90,92 +91,174 @@ struct GemmP {
   const uint8_t *qs, *sc;  // packed Q4_0 weights
   const uint8_t *xp;       // activations, bf16, swizzled, [token tile][K chunk][BN][128 B]
   float *y;                // [M][N]
-  float *partial;          // split-K: [split][M][N]
-  uint32_t *cnt;           // split-K tickets, one per output tile, left at zero
+  float *partial;          // split output tiles: [2 slots per CTA][BN][256] fp32
+  uint32_t *cnt;           // tickets, one per (output tile, epilogue warp), left at zero
   uint32_t *err;
-  uint32_t m, n, ntiles, nunits, ksplit;  // tokens, features, weight tiles, K units of 128, K splits
+  uint32_t m, n, ntiles, nunits;  // tokens, features, weight tiles, K units of 128
+  uint32_t mtiles;                // token tiles; output tile t = (feature tile t / mtiles, token tile t % mtiles)
+  uint64_t work;                  // output tiles x K units: the stream every CTA takes an equal run of
 };
 
-// Dequantise half a unit (2 blocks, 64 weights) of one 16-row tile from its
-// packed piece in shared memory into the swizzled bf16 stage.
-__device__ __forceinline__ void dequant_half(uint8_t *a_stage, uint32_t tile_row0, const uint8_t *piece_qs,
-                                             const uint8_t *piece_sc, int half, int lane) {
-  const uint32_t rl = lane >> 2, c = lane & 3;
+// Stream-K partition: CTA c of G processes work units [c W / G, (c + 1) W / G)
+// of the (output tile, K unit) stream, tile-major.
+__host__ __device__ __forceinline__ uint64_t sk_begin(uint64_t c, uint64_t work, uint64_t g) { return c * work / g; }
+// the CTA whose run holds unit w: the largest c with floor(c W / G) <= w
+__host__ __device__ __forceinline__ uint64_t sk_owner(uint64_t w, uint64_t work, uint64_t g) {
+  return ((w + 1) * g - 1) / work;
+}
+
+// K order inside each 64-wide stage. Both operands use it, so the
+// contraction is unchanged: 16-byte chunk 2c + b (b = which of the stage's
+// two Q4_0 blocks, c = the packed 32-bit word of the block row) holds
+// elements e(c, 0..7) of block b,
+//   e(c, j) = 4c + {0, 2, 1, 3}[j]            j < 4  (low nibbles)
+//           = 16 + 4c + {0, 2, 1, 3}[j - 4]   j >= 4 (high nibbles),
+// which is the order in which masking a packed word at bits 0/16, 8/24,
+// 4/20 and 12/28 yields the nibbles (Q4_0 byte i: low nibble element i, high
+// nibble element i + 16). Chunks 2c + b keep the 8 rows x 4 words a quarter
+// warp stores in distinct banks after the 128-byte swizzle.
+__host__ __device__ constexpr uint32_t kperm(uint32_t c, uint32_t j) {
+  return (j < 4 ? 0u : 16u) + 4u * c + ((j & 1u) << 1) + ((j >> 1) & 1u);
+}
+
+// fp16 block scale d -> bf16x2 pairs (dh, dh) and (dl, dl) with dh + dl == d
+// exactly: dh is d truncated to 8 significant bits, dl the remaining 3 bits.
+__device__ __forceinline__ void split_scale(uint32_t hbits, uint32_t &dh2, uint32_t &dl2) {
+  const float d = __half2float(__ushort_as_half((uint16_t)hbits));
+  const uint32_t hb = __float_as_uint(d) & 0xFFFF0000u;
+  const uint32_t lb = __float_as_uint(d - __uint_as_float(hb));  // exact, low 16 bits zero
+  dh2 = hb | (hb >> 16);
+  dl2 = (lb & 0xFFFF0000u) | (lb >> 16);
+}
+
+__device__ __forceinline__ uint32_t bf2_fma(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t r;
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+  return r;
+}
+
+// Two nibbles q (at bits 0-3 and 16-19 of v) -> bf16x2 of (q - 8) * d rounded
+// once to bf16, the reference's fp32 dequantised weight (q - 8) * d (exact in
+// fp32) rounded to nearest. Three bf16x2 fused multiply-adds: 0x4300 | q is
+// the bf16 128 + q, times 1 minus 136 gives q - 8 exactly; (q - 8) * dl is
+// exact (at most 7 significant bits; the -0 addend keeps it a product); the
+// last one rounds (q - 8) * dh + (q - 8) * dl once.
+__device__ __forceinline__ uint32_t dq_pair(uint32_t v, uint32_t dh2, uint32_t dl2) {
+  const uint32_t t = bf2_fma((v & 0x000F000Fu) | 0x43004300u, 0x3F803F80u, 0xC308C308u);  // x 1 + (-136)
+  return bf2_fma(t, dh2, bf2_fma(t, dl2, 0x80008000u));
+}
+
+// Dequantise half a unit (2 blocks, 64 weights) of one 16-row tile into the
+// swizzled bf16 stage: lane (rl, c) converts word c of both blocks of rows
+// rl and rl + 8 (q[h] = the lane's 16 packed bytes of row rl + 8h: word c of
+// blocks 0..3), one 16-byte store each at stage + soff[h][b]. `sclp` points
+// at the lane's row in the tile's split scales ([16 rows][2 block pairs] x
+// {dh2, dl2, dh2', dl2'}).
+template <int HALF>
+__device__ __forceinline__ void dequant_half(uint8_t *stage, const uint32_t (&soff)[2][2], const uint4 (&q)[2],
+                                             const uint4 *sclp) {
 #pragma unroll
   for (int h = 0; h < 2; h++) {
-    const uint4 q = *reinterpret_cast<const uint4 *>(piece_qs + h * 512 + lane * 16);
-    const uint2 dd = *reinterpret_cast<const uint2 *>(piece_sc + h * 64 + rl * 8);
-    const uint32_t fr = tile_row0 + rl + 8 * h;  // feature row within the CTA's 256
-    uint8_t *blk = a_stage + (fr >> 7) * (128 * 128);
-    const uint32_t r = fr & 127;
+    const uint4 sp = sclp[h * 16 + HALF];  // {dh2, dl2} of blocks 2 HALF and 2 HALF + 1
 #pragma unroll
-    for (int ii = 0; ii < 2; ii++) {
-      const int i = 2 * half + ii;  // block within the unit
-      const uint32_t w = i == 0 ? q.x : (i == 1 ? q.y : (i == 2 ? q.z : q.w));
-      const uint32_t dw = i < 2 ? dd.x : dd.y;
-      const float d = __half2float(__ushort_as_half((uint16_t)((i & 1) ? (dw >> 16) : (dw & 0xFFFFu))));
-      __nv_bfloat162 lo0 = __floats2bfloat162_rn((float)((int)(w & 15) - 8) * d, (float)((int)((w >> 8) & 15) - 8) * d);
-      __nv_bfloat162 lo1 =
-          __floats2bfloat162_rn((float)((int)((w >> 16) & 15) - 8) * d, (float)((int)((w >> 24) & 15) - 8) * d);
-      __nv_bfloat162 hi0 =
-          __floats2bfloat162_rn((float)((int)((w >> 4) & 15) - 8) * d, (float)((int)((w >> 12) & 15) - 8) * d);
-      __nv_bfloat162 hi1 =
-          __floats2bfloat162_rn((float)((int)((w >> 20) & 15) - 8) * d, (float)((int)((w >> 28) & 15) - 8) * d);
-      // low nibbles: elements 4c..4c+3 of the block; high: 16+4c..
-      const uint32_t k_lo = ii * 32 + 4 * c, k_hi = ii * 32 + 16 + 4 * c;
-      uint2 vlo, vhi;
-      vlo.x = *reinterpret_cast<uint32_t *>(&lo0);
-      vlo.y = *reinterpret_cast<uint32_t *>(&lo1);
-      vhi.x = *reinterpret_cast<uint32_t *>(&hi0);
-      vhi.y = *reinterpret_cast<uint32_t *>(&hi1);
-      *reinterpret_cast<uint2 *>(blk + sw128(r, k_lo)) = vlo;
-      *reinterpret_cast<uint2 *>(blk + sw128(r, k_hi)) = vhi;
+    for (int b = 0; b < 2; b++) {
+      const uint32_t w = HALF ? (b ? q[h].w : q[h].z) : (b ? q[h].y : q[h].x);
+      const uint32_t dh2 = b ? sp.z : sp.x, dl2 = b ? sp.w : sp.y;
+      uint4 o;
+      o.x = dq_pair(w, dh2, dl2);
+      o.y = dq_pair(w >> 8, dh2, dl2);
+      o.z = dq_pair(w >> 4, dh2, dl2);
+      o.w = dq_pair(w >> 12, dh2, dl2);
+      *reinterpret_cast<uint4 *>(stage + soff[h][b]) = o;
     }
   }
 }
 
-constexpr int kWorkers = 8;                       // dequantising warps
+// tcgen05.ld of 8 or 32 consecutive accumulator columns for the warp's 32 lanes
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&v)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+               : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+}
+// N consecutive accumulator columns of the warp's 32 lanes
+template <uint32_t N>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&v)[N]) {
+  static_assert(N == 8 || N == 16 || N == 32, "8, 16 or 32 columns");
+  if constexpr (N == 8) {
+    tmem_ld8(taddr, v);
+  } else if constexpr (N == 16) {
+    tmem_ld16(taddr, v);
+  } else {
+    tmem_ld32(taddr, v);
+  }
+}
+
+constexpr int kWorkers = 16;                      // dequantising warps, one weight tile each
 constexpr int kGThreadsWS = (kWorkers + 3) * 32;  // + raw-W producer, X producer, MMA issuer
 constexpr int kRawStages = 3;                     // packed-weight units in flight
 constexpr uint32_t kRawStage = 16 * 1024 + 16 * 128;  // one unit of the CTA's 16 tiles: codes, then headers
+constexpr uint32_t kSclBytes = kWorkers * 16 * 4 * 8;  // split scales of the current unit, per warp
 template <int BN>
-constexpr int kAStages = BN == 256 ? 2 : 3;       // bf16 stages (shared memory bound)
+constexpr int kAStages = BN == 256 ? 2 : (BN == 128 ? 3 : 4);  // bf16 weight stages (shared memory bound)
+template <int BN>
+constexpr int kBStages = BN == 256 ? 3 : 4;  // bf16 activation stages
+template <int BN>
+constexpr size_t gemm_smem_bytes() {
+  return 1024 + (size_t)kAStages<BN> * kAStage + (size_t)kBStages<BN> * BN * 128 + (size_t)kRawStages * kRawStage +
+         kSclBytes;
+}
 
 template <int BN>
 __global__ void __launch_bounds__(kGThreadsWS, 1) k_gemm_q4_0(GemmP p) {
   constexpr uint32_t kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;  // power of two for BN in {16, 64, 128, 256}
   constexpr uint32_t kBStage = BN * 128;
   constexpr uint32_t kIdesc = idesc_bf16(BN);
-  constexpr int SA = kAStages<BN>;
+  constexpr int SA = kAStages<BN>, SB = kBStages<BN>;
+  constexpr uint32_t kECols = BN / 2;                      // epilogue columns (tokens) per warp
+  constexpr uint32_t kEChunk = kECols < 16 ? kECols : 16;  // columns per TMEM load round
+  constexpr uint32_t kFChunk = kECols < 16 ? kECols : 16;  // columns per round of the split-tile sum
   extern __shared__ __align__(1024) uint8_t gsm_raw[];
   // 1024-byte alignment of the swizzled stages
   uint8_t *gsm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~(uintptr_t)1023);
   uint8_t *a_st = gsm;                                // [SA][2 acc][128 rows][128 B]
-  uint8_t *b_st = a_st + (size_t)SA * kAStage;        // [SA][BN rows][128 B]
-  uint8_t *r_st = b_st + (size_t)SA * kBStage;        // [kRawStages][16 KB codes | 2 KB headers]
+  uint8_t *b_st = a_st + (size_t)SA * kAStage;        // [SB][BN rows][128 B]
+  uint8_t *r_st = b_st + (size_t)SB * kBStage;        // [kRawStages][16 KB codes | 2 KB headers]
+  uint4 *scl_all = reinterpret_cast<uint4 *>(r_st + (size_t)kRawStages * kRawStage);
   __shared__ __align__(8) uint64_t rfull[kRawStages], rempty[kRawStages];
-  __shared__ __align__(8) uint64_t afull[SA], bfull[SA], aempty[SA];
-  __shared__ uint32_t tmem_base_s, ticket_s;
-  __shared__ int abort_s;
+  __shared__ __align__(8) uint64_t afull[SA], aempty[SA], bfull[SB], bempty[SB];
+  __shared__ __align__(8) uint64_t accfull, accempty;
+  __shared__ uint32_t tmem_base_s;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const uint32_t f0 = blockIdx.x * kFT, tile0 = f0 / 16;        // first feature and weight tile
-  const uint32_t tt = blockIdx.y, m0 = tt * BN;                  // token tile
-  const uint32_t z = blockIdx.z;                                 // K split
-  const uint32_t u0 = z * p.nunits / p.ksplit, u1 = (z + 1) * p.nunits / p.ksplit;
-  const uint32_t nu = u1 - u0, nkt = 2 * nu;                    // units and 64-wide K chunks of this CTA
-  const uint32_t nv = min(16u, p.ntiles - min(p.ntiles, tile0));  // weight tiles present
+  const uint64_t G = gridDim.x, cta = blockIdx.x, U = p.nunits;
+  const uint64_t w_begin = sk_begin(cta, p.work, G), w_end = sk_begin(cta + 1, p.work, G);
+  const uint32_t first_tile = (uint32_t)(w_begin / U);
   if (tid == 0) {
     for (int s = 0; s < kRawStages; s++) {
       mbar_init(&rfull[s], 1);
-      mbar_init(&rempty[s], kWorkers * 32);
+      mbar_init(&rempty[s], kWorkers);
     }
     for (int s = 0; s < SA; s++) {
-      mbar_init(&afull[s], kWorkers * 32);
-      mbar_init(&bfull[s], 1);
+      mbar_init(&afull[s], kWorkers);
       mbar_init(&aempty[s], 1);
     }
-    abort_s = 0;
+    for (int s = 0; s < SB; s++) {
+      mbar_init(&bfull[s], 1);
+      mbar_init(&bempty[s], 1);
+    }
+    mbar_init(&accfull, 1);
+    mbar_init(&accempty, kWorkers);
     fence_mbar_init();
   }
   if (warp == kWorkers + 2) {
@@ -190,143 +273,265 @@ __global__ void __launch_bounds__(kGThreadsWS, 1) k_gemm_q4_0(GemmP p) {
   bool ok = true;
 
   if (warp == kWorkers) {
-    // ---- packed weights: one unit of the CTA's tiles per raw stage ----
+    // ---- packed weights: one K unit of the output tile's 16 weight tiles per raw stage ----
     if (lane == 0) {
-      for (uint32_t i = 0; i < nu && ok; i++) {
+      uint32_t i = 0, u = (uint32_t)(w_begin % U), tile0 = (first_tile / p.mtiles) * 16, mt = first_tile % p.mtiles;
+      for (uint64_t w = w_begin; w < w_end && ok; w++, i++) {
+        const uint32_t nv = min(16u, p.ntiles - tile0);
         const uint32_t rs = i % kRawStages;
-        if (i >= (uint32_t)kRawStages && !mbar_wait(&rempty[rs], ((i / kRawStages) - 1) & 1u, kGWaitLimit)) {
+        if (i >= (uint32_t)kRawStages && !mbar_wait_spin(&rempty[rs], ((i / kRawStages) - 1) & 1u, kGWaitLimit)) {
           ok = false;
           break;
         }
         uint8_t *dst = r_st + (size_t)rs * kRawStage;
-        const size_t piece = (size_t)(u0 + i) * p.ntiles + tile0;
-        if (nv) {
-          mbar_expect_tx(&rfull[rs], nv * (1024 + 128));
-          bulk_g2s(dst, p.qs + piece * 1024, nv * 1024, &rfull[rs]);
-          bulk_g2s(dst + 16 * 1024, p.sc + piece * 128, nv * 128, &rfull[rs]);
-        } else {
-          mbar_arrive(&rfull[rs]);
+        const size_t piece = (size_t)u * p.ntiles + tile0;
+        mbar_expect_tx(&rfull[rs], nv * (1024 + 128));
+        bulk_g2s(dst, p.qs + piece * 1024, nv * 1024, &rfull[rs]);
+        bulk_g2s(dst + 16 * 1024, p.sc + piece * 128, nv * 128, &rfull[rs]);
+        if (++u == U) {  // next output tile: token tile fastest
+          u = 0;
+          if (++mt == p.mtiles) {
+            mt = 0;
+            tile0 += 16;
+          }
         }
       }
     }
   } else if (warp == kWorkers + 1) {
     // ---- activations: one 64-wide K chunk per stage ----
     if (lane == 0) {
-      for (uint32_t j = 0; j < nkt && ok; j++) {
-        const uint32_t s = j % SA;
-        if (j >= (uint32_t)SA && !mbar_wait(&aempty[s], ((j / SA) - 1) & 1u, kGWaitLimit)) {
-          ok = false;
-          break;
+      uint32_t j = 0, u = (uint32_t)(w_begin % U), mt = first_tile % p.mtiles;
+      for (uint64_t w = w_begin; w < w_end && ok; w++) {
+        for (uint32_t half = 0; half < 2; half++, j++) {
+          const uint32_t s = j % SB;
+          if (j >= (uint32_t)SB && !mbar_wait_spin(&bempty[s], ((j / SB) - 1) & 1u, kGWaitLimit)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&bfull[s], kBStage);
+          bulk_g2s(b_st + (size_t)s * kBStage, p.xp + ((size_t)mt * (2 * U) + 2 * u + half) * kBStage, kBStage,
+                   &bfull[s]);
         }
-        mbar_expect_tx(&bfull[s], kBStage);
-        bulk_g2s(b_st + (size_t)s * kBStage, p.xp + ((size_t)tt * (2 * p.nunits) + 2 * u0 + j) * kBStage, kBStage,
-                 &bfull[s]);
+        if (++u == U) {
+          u = 0;
+          if (++mt == p.mtiles) mt = 0;
+        }
       }
     }
   } else if (warp == kWorkers + 2) {
-    // ---- MMA issue ----
+    // ---- MMA issue: each segment (the run's part of one output tile) into the TMEM accumulators ----
     if (lane == 0) {
-      for (uint32_t j = 0; j < nkt && ok; j++) {
-        const uint32_t s = j % SA, ph = (j / SA) & 1u;
-        if (!mbar_wait(&afull[s], ph, kGWaitLimit) || !mbar_wait(&bfull[s], ph, kGWaitLimit)) {
-          ok = false;
-          break;
+      const uint64_t a_desc0 = sdesc(smem_u32(a_st)), b_desc0 = sdesc(smem_u32(b_st));
+      uint32_t j = 0, e = 0, u = (uint32_t)(w_begin % U);
+      for (uint64_t w = w_begin; w < w_end && ok; w++, u = (u + 1 == U) ? 0 : u + 1) {
+        const bool seg_first = w == w_begin || u == 0, seg_last = w + 1 == w_end || u == U - 1;
+        if (seg_first && e > 0) {  // the previous segment's epilogue has read the accumulators
+          if (!mbar_wait_spin(&accempty, (e - 1) & 1u, kGWaitLimit)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
         }
-        tc_fence_after();
-        const uint32_t abase = smem_u32(a_st + (size_t)s * kAStage), bbase = smem_u32(b_st + (size_t)s * kBStage);
-#pragma unroll
-        for (int acc = 0; acc < 2; acc++)
+        for (uint32_t half = 0; half < 2; half++, j++) {
+          const uint32_t s = j % SA, sb = j % SB;
+          if (!mbar_wait_spin(&afull[s], (j / SA) & 1u, kGWaitLimit) ||
+              !mbar_wait_spin(&bfull[sb], (j / SB) & 1u, kGWaitLimit)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          // descriptors are linear in the start address (bits 0-13 = address / 16):
+          // build the stage's two once, then step 32 bytes per K slice and 16 KB
+          // to the second accumulator's rows
+          const uint64_t ad = a_desc0 + (uint64_t)(s * (kAStage >> 4)), bd = b_desc0 + (uint64_t)(sb * (kBStage >> 4));
+          const bool fresh = seg_first && half == 0;
+          // alternate the two accumulators so consecutive MMAs are independent
 #pragma unroll
           for (int k = 0; k < kBK / 16; k++)
-            mma_bf16(tmem + acc * BN, sdesc(abase + acc * (128 * 128) + k * 32), sdesc(bbase + k * 32), kIdesc,
-                     (j > 0 || k > 0) ? 1u : 0u);
-        mma_commit(&aempty[s]);
+#pragma unroll
+            for (int acc = 0; acc < 2; acc++)
+              mma_bf16(tmem + acc * BN, ad + (uint64_t)(acc * (128 * 128 >> 4) + k * 2), bd + (uint64_t)(k * 2), kIdesc,
+                       (!fresh || k > 0) ? 1u : 0u);
+          mma_commit(&aempty[s]);
+          mma_commit(&bempty[sb]);
+        }
+        if (!ok) break;
+        if (seg_last) {
+          mma_commit(&accfull);
+          e++;
+        }
       }
     }
   } else {
-    // ---- dequantising warps: warp w owns tiles 2w, 2w+1 of the CTA ----
-    for (uint32_t i = 0; i < nu && ok; i++) {
+    // ---- dequantising warps: warp w owns weight tile w of the output tile; then its epilogue slice ----
+    const uint4 *scl = scl_all + warp * (16 * 2);
+    uint32_t soff[2][2];  // the lane's store offsets within a stage: rows rl, rl + 8; blocks 0, 1
+#pragma unroll
+    for (int h = 0; h < 2; h++)
+#pragma unroll
+      for (int b = 0; b < 2; b++) {
+        const uint32_t fr = 16u * warp + (lane >> 2) + 8u * h, c = lane & 3;
+        soff[h][b] = (fr >> 7) * (128 * 128) + (fr & 127) * 128 + ((((2u * c + b) ^ fr) & 7u) << 4);
+      }
+    const uint4 *sclp = scl + (lane >> 2) * 2;
+    uint4 q[2];
+    bool mine = false;
+    // one stage (half a unit): wait for its slot, dequantise, publish
+    auto stage_half = [&](uint32_t j, auto half_tag) -> bool {
+      constexpr int HALF = decltype(half_tag)::value;
+      const uint32_t s = j % SA;
+      if (j >= (uint32_t)SA && !mbar_wait_sleep(&aempty[s], ((j / SA) - 1) & 1u, kGWaitLimit)) return false;
+      if (mine) dequant_half<HALF>(a_st + (size_t)s * kAStage, soff, q, sclp);
+      fence_proxy_async();  // each lane's generic-proxy stores -> visible to the tensor core
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&afull[s]);  // one arrival per warp
+      return true;
+    };
+    // epilogue slice of this warp: TMEM lanes 32 (w % 4).. of accumulator (w / 4) % 2 (features),
+    // columns [w / 8 * BN / 2, + BN / 2) (tokens)
+    const uint32_t g = warp & 3, acc = (warp >> 2) & 1, cbase = (warp >> 3) * kECols;
+    const uint32_t fin = acc * 128 + g * 32 + lane;  // feature within the output tile
+    const uint32_t taddr = tmem + ((g * 32u) << 16) + acc * BN + cbase;
+    uint32_t i = 0, e = 0, tile = first_tile, u = (uint32_t)(w_begin % U);
+    uint32_t ft = first_tile / p.mtiles, mt = first_tile % p.mtiles;
+    bool seg_full_start = u == 0;  // the current segment starts at the tile's first K unit
+    for (uint64_t w = w_begin; w < w_end && ok; w++, i++) {
+      mine = (uint32_t)warp < min(16u, p.ntiles - ft * 16);
       const uint32_t rs = i % kRawStages;
-      if (!mbar_wait(&rfull[rs], (i / kRawStages) & 1u, kGWaitLimit)) {
+      if (!mbar_wait_sleep(&rfull[rs], (i / kRawStages) & 1u, kGWaitLimit)) {
         ok = false;
         break;
       }
       const uint8_t *raw = r_st + (size_t)rs * kRawStage;
-      for (int half = 0; half < 2 && ok; half++) {
-        const uint32_t j = 2 * i + half, s = j % SA;
-        if (j >= (uint32_t)SA && !mbar_wait(&aempty[s], ((j / SA) - 1) & 1u, kGWaitLimit)) {
-          ok = false;
-          break;
-        }
-        uint8_t *as = a_st + (size_t)s * kAStage;
-        for (int tl = 0; tl < 2; tl++) {
-          const uint32_t lt = 2 * warp + tl;  // tile within the CTA
-          if (lt < nv) dequant_half(as, 16 * lt, raw + lt * 1024, raw + 16 * 1024 + lt * 128, half, lane);
-        }
-        fence_proxy_async();  // generic-proxy stores -> visible to the tensor core
-        mbar_arrive(&afull[s]);
+      if (mine) {
+        // split the tile's 64 block scales once: lane l takes row l / 2, blocks 2 (l % 2) + {0, 1}
+        const uint32_t dd = *reinterpret_cast<const uint32_t *>(raw + 16 * 1024 + warp * 128 + lane * 4);
+        uint4 sp;
+        split_scale(dd & 0xFFFFu, sp.x, sp.y);
+        split_scale(dd >> 16, sp.z, sp.w);
+        __syncwarp();  // the previous unit's scales are no longer read
+        scl_all[warp * (16 * 2) + lane] = sp;
+        __syncwarp();
+        const uint8_t *pq = raw + warp * 1024 + lane * 16;
+        q[0] = *reinterpret_cast<const uint4 *>(pq);
+        q[1] = *reinterpret_cast<const uint4 *>(pq + 512);
       }
-      mbar_arrive(&rempty[rs]);
-    }
-  }
-  if (!ok) {
-    atomicExch(p.err, 1u);
-    abort_s = 1;
-  }
-  // all MMAs done: the commit of the last stage
-  if (nkt && !mbar_wait(&aempty[(nkt - 1) % SA], ((nkt - 1) / SA) & 1u, kGWaitLimit)) {
-    atomicExch(p.err, 1u);
-    abort_s = 1;
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const bool split = p.ksplit > 1;
-  if (!abort_s && warp < kWorkers) {
-    // epilogue: warp w reads TMEM lanes 32(w%4).. of accumulator w/4
-    const uint32_t g = warp & 3, acc = warp >> 2;
-    const uint32_t feat = f0 + acc * 128 + g * 32 + lane;
-    float *dst = split ? p.partial + (size_t)z * p.m * p.n : p.y;
+      ok = stage_half(2 * i, std::integral_constant<int, 0>{}) && stage_half(2 * i + 1, std::integral_constant<int, 1>{});
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&rempty[rs]);
+      if (!ok) break;
+      if (!(w + 1 == w_end || u == U - 1)) {
+        u++;
+        continue;
+      }
+
+      // ---- segment end: epilogue of this warp's slice ----
+      if (!mbar_wait_sleep(&accfull, e & 1u, kGWaitLimit)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t f0 = ft * kFT, m0 = mt * BN;
+      const uint32_t feat = f0 + fin;
+      const bool whole = seg_full_start && u == U - 1;
+      if (whole) {
 #pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 16) {
-      uint32_t v[16];
-      tmem_ld16(tmem + ((g * 32u) << 16) + acc * BN + c0, v);
-      tmem_ld_wait();
-      if (feat < p.n) {
+        for (uint32_t c0 = 0; c0 < kECols; c0 += kEChunk) {
+          uint32_t v[kEChunk];
+          tmem_ld_cols(taddr + c0, v);
+          tmem_ld_wait();
+          if (feat < p.n) {
 #pragma unroll
-        for (int jj = 0; jj < 16; jj++) {
-          const uint32_t m = m0 + c0 + jj;
-          if (m < p.m) dst[(size_t)m * p.n + feat] = __uint_as_float(v[jj]);
+            for (uint32_t jj = 0; jj < kEChunk; jj++) {
+              const uint32_t m = m0 + cbase + c0 + jj;
+              if (m < p.m) p.y[(size_t)m * p.n + feat] = __uint_as_float(v[jj]);
+            }
+          }
         }
+      } else {
+        // part of a tile shared with neighbouring runs: park it in this CTA's
+        // slot, and the last of the tile's contributors to finish adds all
+        // parts in K order, its own straight from TMEM. Slot layout per warp:
+        // [column / 4][lane][4 columns], so a warp's float4 access is 512
+        // contiguous bytes.
+        const uint32_t slot = 2u * (uint32_t)cta + (tile == first_tile ? 0u : 1u);
+        float4 *part = reinterpret_cast<float4 *>(p.partial + (size_t)slot * (BN * kFT)) +
+                       (size_t)warp * (kECols / 4) * 32 + lane;
+#pragma unroll 1
+        for (uint32_t c0 = 0; c0 < kECols; c0 += kEChunk) {
+          uint32_t v[kEChunk];
+          tmem_ld_cols(taddr + c0, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (uint32_t jj = 0; jj < kEChunk; jj += 4)
+            part[(size_t)((c0 + jj) / 4) * 32] = make_float4(__uint_as_float(v[jj]), __uint_as_float(v[jj + 1]),
+                                                             __uint_as_float(v[jj + 2]), __uint_as_float(v[jj + 3]));
+        }
+        __threadfence();
+        __syncwarp();
+        uint32_t ticket = 0;
+        if (lane == 0) ticket = atomicAdd(&p.cnt[(size_t)tile * kWorkers + warp], 1u);
+        ticket = __shfl_sync(0xFFFFFFFFu, ticket, 0);
+        const uint64_t tw0 = (uint64_t)tile * U;
+        const uint32_t c_lo = (uint32_t)sk_owner(tw0, p.work, G), c_hi = (uint32_t)sk_owner(tw0 + U - 1, p.work, G);
+        if (ticket == c_hi - c_lo) {
+          __threadfence();
+#pragma unroll 1
+          for (uint32_t c0 = 0; c0 < kECols; c0 += kFChunk) {
+            float a[kFChunk];
+#pragma unroll 1
+            for (uint32_t cc = c_lo; cc <= c_hi; cc++) {
+              uint32_t v[kFChunk];
+              if (cc == (uint32_t)cta) {
+                tmem_ld_cols(taddr + c0, v);
+                tmem_ld_wait();
+              } else {
+                const uint32_t ccf = (uint32_t)(sk_begin(cc, p.work, G) / U);
+                const float4 *pp = reinterpret_cast<const float4 *>(
+                                       p.partial + (size_t)(2u * cc + (tile == ccf ? 0u : 1u)) * (BN * kFT)) +
+                                   ((size_t)warp * (kECols / 4) + c0 / 4) * 32 + lane;
+#pragma unroll
+                for (uint32_t jj = 0; jj < kFChunk; jj += 4) {
+                  const float4 f = __ldcg(pp + (size_t)(jj / 4) * 32);
+                  v[jj] = __float_as_uint(f.x);
+                  v[jj + 1] = __float_as_uint(f.y);
+                  v[jj + 2] = __float_as_uint(f.z);
+                  v[jj + 3] = __float_as_uint(f.w);
+                }
+              }
+#pragma unroll
+              for (uint32_t jj = 0; jj < kFChunk; jj++)
+                a[jj] = cc == c_lo ? __uint_as_float(v[jj]) : a[jj] + __uint_as_float(v[jj]);
+            }
+            if (feat < p.n) {
+#pragma unroll
+              for (uint32_t jj = 0; jj < kFChunk; jj++) {
+                const uint32_t m = m0 + cbase + c0 + jj;
+                if (m < p.m) p.y[(size_t)m * p.n + feat] = a[jj];
+              }
+            }
+          }
+          if (lane == 0) p.cnt[(size_t)tile * kWorkers + warp] = 0;
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&accempty);  // this warp is done with the accumulators
+      e++;
+      // next output tile: token tile fastest
+      u = 0;
+      seg_full_start = true;
+      tile++;
+      if (++mt == p.mtiles) {
+        mt = 0;
+        ft++;
       }
     }
   }
+  if (!ok) atomicExch(p.err, 1u);
   tc_fence_before();
   __syncthreads();
   if (warp == kWorkers + 2) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
-  if (!split || abort_s) return;
-  // split K: the last split of this output tile to finish adds the parts in order
-  __threadfence();
-  __syncthreads();
-  const uint32_t tile_id = blockIdx.y * gridDim.x + blockIdx.x;
-  if (tid == 0) ticket_s = atomicAdd(&p.cnt[tile_id], 1u);
-  __syncthreads();
-  if (ticket_s != p.ksplit - 1) return;
-  __threadfence();
-  for (uint32_t e = tid; e < kFT * BN; e += blockDim.x) {
-    const uint32_t f = f0 + e % kFT, m = m0 + e / kFT;
-    if (f >= p.n || m >= p.m) continue;
-    float part[8];  // ksplit <= 8: all loads in flight, then the sum in split order
-#pragma unroll
-    for (uint32_t q = 0; q < 8; q++)
-      if (q < p.ksplit) part[q] = __ldcg(&p.partial[((size_t)q * p.m + m) * p.n + f]);
-    float a = 0.f;
-#pragma unroll
-    for (uint32_t q = 0; q < 8; q++)
-      if (q < p.ksplit) a += part[q];
-    p.y[(size_t)m * p.n + f] = a;
-  }
-  if (tid == 0) p.cnt[tile_id] = 0;
 }
 
 // X fp32 [M][K] -> bf16 in the GEMM's operand layout: [token tile][K chunk of
@@ -340,10 +545,15 @@ __global__ void __launch_bounds__(256) k_gemm_xprep(const float *__restrict__ x,
   const uint32_t ch = (uint32_t)(idx % chunks_per_row);
   const uint32_t mtiles = (m + BN - 1) / BN;
   if (row >= (uint64_t)mtiles * BN) return;
-  const uint32_t kt = ch / 8, c = ch % 8, k0 = ch * 8;
+  const uint32_t kt = ch / 8, c = ch % 8;
+  // chunk c of the stage: block c & 1, packed word c >> 1, in kperm order
+  const uint32_t kb = kt * 64 + (c & 1u) * 32;
   float v[8];
 #pragma unroll
-  for (int j = 0; j < 8; j++) v[j] = (row < m && k0 + j < k) ? x[row * k + k0 + j] : 0.0f;
+  for (int j = 0; j < 8; j++) {
+    const uint32_t kk = kb + kperm(c >> 1, j);
+    v[j] = (row < m && kk < k) ? x[row * k + kk] : 0.0f;
+  }
   uint4 o;
   __nv_bfloat162 b0 = __floats2bfloat162_rn(v[0], v[1]), b1 = __floats2bfloat162_rn(v[2], v[3]);
   __nv_bfloat162 b2 = __floats2bfloat162_rn(v[4], v[5]), b3 = __floats2bfloat162_rn(v[6], v[7]);
@@ -361,19 +571,22 @@ pai_status_t gemm_launch(pai_b200_ctx_t *ctx, uint32_t m, uint32_t n, uint32_t k
                          float *y) {
   const uint32_t nunits = (uint32_t)b200_units(PAI_B200_Q4_0, k), nkc = 2 * nunits;  // K chunks of 64
   const uint32_t mtiles = (m + BN - 1) / BN, ftiles = (n + kFT - 1) / kFT;
-  // K split when the output tiles alone leave SMs idle (small prompts)
+  const uint64_t tiles = (uint64_t)ftiles * mtiles, work = tiles * nunits;
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, b200_ctx_device(ctx));
-  uint32_t ksplit = 1;
-  while (ksplit < 8 && (uint64_t)ftiles * mtiles * ksplit * 2 <= (uint64_t)sms && nunits / (ksplit * 2) >= 4)
-    ksplit *= 2;
+  // Grid: with at least as many output tiles as SMs, one persistent CTA per
+  // SM over the whole stream (tiles split only where runs meet). With fewer,
+  // each tile is split evenly over floor(SMs / tiles) CTAs, so no tile has
+  // more contributors than it needs. Runs are at least 4 K units long.
+  const uint64_t g_want = tiles >= (uint64_t)sms ? (uint64_t)sms : tiles * ((uint64_t)sms / tiles);
+  const uint32_t grid = (uint32_t)std::max<uint64_t>(1, std::min<uint64_t>(g_want, work / 4));
   const uint64_t xp_bytes = (uint64_t)mtiles * nkc * BN * 128;
   void *xp = nullptr;
   pai_status_t st = b200_ctx_xq(ctx, xp_bytes, &xp);
   if (st) return st;
   float *partial = nullptr;
   uint32_t *cnt = nullptr;
-  st = b200_ctx_scratch(ctx, ksplit > 1 ? (uint64_t)ksplit * m * n : 0, ftiles * mtiles, &partial, &cnt);
+  st = b200_ctx_scratch(ctx, (uint64_t)2 * grid * BN * kFT, (uint32_t)(tiles * kWorkers), &partial, &cnt);
   if (st) return st;
   cudaStream_t s = (cudaStream_t)b200_ctx_stream(ctx);
   const uint64_t nchunks = (uint64_t)mtiles * BN * nkc * 8;
@@ -392,8 +605,9 @@ pai_status_t gemm_launch(pai_b200_ctx_t *ctx, uint32_t m, uint32_t n, uint32_t k
   p.n = n;
   p.ntiles = (uint32_t)b200_ntiles(n);
   p.nunits = nunits;
-  p.ksplit = ksplit;
-  const size_t smem = 1024 + (size_t)kAStages<BN> * (kAStage + BN * 128) + (size_t)kRawStages * kRawStage;
+  p.mtiles = mtiles;
+  p.work = work;
+  const size_t smem = gemm_smem_bytes<BN>();
   static bool attr_set[64];
   const int dev = b200_ctx_device(ctx);
   if (dev < 0 || dev >= 64 || !attr_set[dev]) {
@@ -402,7 +616,6 @@ pai_status_t gemm_launch(pai_b200_ctx_t *ctx, uint32_t m, uint32_t n, uint32_t k
     if (st) return st;
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
-  const dim3 grid(ftiles, mtiles, ksplit);
   k_gemm_q4_0<BN><<<grid, kGThreadsWS, smem, s>>>(p);
   return b200_launched(ctx, 1, "k_gemm_q4_0");
 }
