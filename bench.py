@@ -57,7 +57,7 @@ def tensor_peak():
         return 1590.0, "fallback"
 
 
-def prefill_gemm(dev, iters=12):
+def prefill_gemm(dev, iters=12, ms=(16, 128, 512, 2048)):
     """Config 2: the Q4_0 prefill GEMM Y[M,14336] = X[M,4096] . W^T on the
     tcgen05 tensor cores (X f32 -> bf16 tiles, W dequantised to bf16 in
     shared memory, fp32 accumulate in TMEM), for M in 16/128/512/2048.
@@ -91,7 +91,7 @@ def prefill_gemm(dev, iters=12):
     e0, e1 = C.c_void_p(), C.c_void_p()
     L.pai_b200_event_create(dev.ctx, C.byref(e0))
     L.pai_b200_event_create(dev.ctx, C.byref(e1))
-    for m in (16, 128, 512, 2048):
+    for m in ms:
         x = dev.put(np.random.default_rng(m).standard_normal((m, k)).astype(np.float32))
         y = dev.alloc(m * n * 4)
         for i in range(4):
@@ -305,10 +305,15 @@ def gpu_arm(args):
     L.pai_b200_event_create(dev.ctx, C.byref(e1))
     pos0 = sess.pos
     dev.sync()
+    if args.nvtx:  # lets a profiler select the timed steps (ncu --nvtx --nvtx-include decode_timed/)
+        import torch.cuda.nvtx as nvtx
+        nvtx.range_push("decode_timed")
     L.pai_b200_event_record(dev.ctx, e0)
     sess.run(K)
     L.pai_b200_event_record(dev.ctx, e1)
     dev.sync()
+    if args.nvtx:
+        nvtx.range_pop()
     clk.__exit__(None, None, None)
     ms = C.c_float()
     _native.check(L.pai_b200_event_elapsed(e0, e1, C.byref(ms)), "elapsed")
@@ -506,6 +511,10 @@ def main():
                     help="time only the dominant GEMV (28672x4096 Q4_0) and print its roofline line")
     ap.add_argument("--gemm-only", action="store_true",
                     help="time only the config-2 prefill GEMM and print its line")
+    ap.add_argument("--gemm-m", type=int, action="append",
+                    help="with --gemm-only: token counts to time (repeatable; default 16 128 512 2048)")
+    ap.add_argument("--nvtx", action="store_true",
+                    help="wrap the timed decode steps in the NVTX range decode_timed")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -513,7 +522,7 @@ def main():
     if args.gemm_only:
         from prosperoai_b200.api import Device
         dev = Device(local)
-        print(json.dumps(prefill_gemm(dev)), flush=True)
+        print(json.dumps(prefill_gemm(dev, ms=tuple(args.gemm_m or (16, 128, 512, 2048)))), flush=True)
         dev.close()
         return
     if args.kernel_only:

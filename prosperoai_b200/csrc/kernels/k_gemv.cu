@@ -54,12 +54,13 @@ namespace {
 constexpr int kStages = 4;                   // depth of the CTA's weight ring
 constexpr int kXSlots = 3;                   // staged-x slots (current, next, one being released)
 // CTA shape: consumer warps (one 16-row tile each; a group is kConsT
-// tiles) + one producer warp. Batch <= 2 needs few registers and runs two
-// CTAs of 8 consumers per SM, the rest one CTA of 8. With B200_GEMV_WIDE=1
-// batch <= 2 runs one CTA of 16 consumers per SM instead: the 66 MB
-// gate/up matrix is 7% faster that way (two CTAs on one SM do not share
-// issue slots evenly), the 0.5 GB lm head 3% slower and the decode step as
-// a whole 0.5% slower, so it is off.
+// tiles) + one producer warp, one CTA per SM. Batch <= 2 keeps its shared
+// memory to 110 KB so that, under programmatic dependent launch, the next
+// kernel's CTA fits beside it and its producer prefills that kernel's
+// weights while this one streams: in the decode step that is 2.6% faster
+// than two GEMV CTAs per SM (which is faster for a GEMV timed alone). With
+// B200_GEMV_WIDE=1 batch <= 2 runs 16 consumers per CTA instead (the 66 MB
+// gate/up matrix alone is 7% faster; the decode step is not).
 #ifndef B200_GEMV_WIDE
 #define B200_GEMV_WIDE 0
 #endif
@@ -68,9 +69,9 @@ constexpr int kConsT = (NT == 1 && B200_GEMV_WIDE) ? 16 : 8;
 template <int NT>
 constexpr int kThreadsT = (kConsT<NT> + 1) * 32;
 template <int NT>
-constexpr int kCtasPerSm = (NT == 1 && !B200_GEMV_WIDE) ? 2 : 1;
+constexpr int kCtasPerSm = 1;
 template <int NT>
-constexpr size_t kSmemCap = kCtasPerSm<NT> == 2 ? 110 * 1024 : 220 * 1024;  // dynamic shared memory per CTA
+constexpr size_t kSmemCap = (NT == 1 && !B200_GEMV_WIDE) ? 110 * 1024 : 220 * 1024;  // dynamic shared memory per CTA
 constexpr uint32_t M4 = 0x0F0F0F0Fu;
 constexpr uint64_t kWaitLimit = 2000000000ull;  // ns before a wait gives up (2 s)
 
