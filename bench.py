@@ -271,19 +271,31 @@ def cpu_baseline_port(dev, steps=3, prompt=24):
 
 def gpu_arm(args):
     from prosperoai_b200 import _native
-    from prosperoai_b200.api import Device, Model, Session
+    from prosperoai_b200.api import Device, Model, Session, TPComm
     rank, world, local = dist_env()
     pg = None
     if world > 1:
         import torch.distributed as dist
-        dist.init_process_group("gloo", timeout=__import__("datetime").timedelta(seconds=600))
+        # host-side plumbing only (barriers, timing max, the communicator id)
+        dist.init_process_group("gloo", timeout=__import__("datetime").timedelta(seconds=180))
         pg = dist
+    tp = world > 1 and not args.replicas
+    if tp:
+        # the exchanges are 16 KB per sequence: no NVLink multicast (NVLS) objects
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     L = _native.load()
     dev = Device(local)
     cfg = dict(CFG_8B)
     B, K, W = args.batch, args.steps, args.warmup
-    model = Model(dev, cfg)
+    # tensor parallel: rank r holds 1/world of every matrix (column-parallel
+    # q/k/v/gate/up, row-parallel o/down, vocab-sharded lm head) and the
+    # exchange steps run on an NCCL communicator inside the step's graph
+    model = Model(dev, cfg, tp_rank=rank if tp else 0, tp_size=world if tp else 1)
     model.synthesize(SEED)
+    comm = None
+    if tp:
+        comm = TPComm.over_group(dev, rank, world)
+        model.set_tp(comm)
     P = args.prompt
     max_ctx = P + W + 2 * K + 8
     sess = Session(model, B, max_ctx)
@@ -340,37 +352,48 @@ def gpu_arm(args):
     # bytes one decode step reads: weights + the KV cache up to the mean position
     mean_pos = pos0 + K / 2.0
     kv_bytes = cfg["n_layer"] * cfg["n_head_kv"] * cfg["head_dim"] * 2 * 2 * mean_pos * B
-    step_bytes = model.step_weight_bytes() + kv_bytes
+    # whole job: every rank reads its shard (equal shards), the KV heads split
+    step_bytes = model.step_weight_bytes() * (world if tp else 1) + kv_bytes
     step_gbs = step_bytes / (t_dev / K * 1e-3) / 1e9
+    step_peak_gpus = world if tp else 1
     result = None
     if rank == 0:
         roof = None if args.no_roofline else gemv_roofline(dev, hbm, kind)
         gemm = None if args.no_roofline else prefill_gemm(dev)
         cpu = None if args.no_cpu_baseline else cpu_baseline_port(dev)
-        value = world * B * K / (t_dev * 1e-3)
+        jobs = 1 if tp else world  # sequences advanced per step: TP ranks share one job
+        value = jobs * B * K / (t_dev * 1e-3)
         result = {
             "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
             "steps": K, "warmup": W, "ms_per_step": round(t_dev / K, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "q4_0 weights, f32 accumulate",
+            "scaling": "strong" if tp else "weak", "vs_baseline": None,
+            "dtype": "q4_0 weights, f32 accumulate",
             "data": "synthetic (seeded N(0,0.02) weights, seeded prompt ids)",
             "config": {"workload": "Llama-3-8B-shaped Q4_0 decode (config 5)", "batch": B,
                        "prompt": P, "positions_timed": [pos0, pos0 + K - 1],
                        "layers": cfg["n_layer"], "hidden": cfg["n_embd"], "vocab": cfg["vocab"],
                        "kv_cache": "fp16",
-                       "parallelism": "single GPU" if world == 1 else f"{world} independent replicas",
+                       "parallelism": ("single GPU" if world == 1 else
+                                       f"tp{world} (NCCL all-reduce after o/down, vocab-sharded argmax)"
+                                       if tp else f"{world} independent replicas"),
                        "l2": "no flush: 4.5 GB of weights per step exceed the 126 MB L2"},
-            "e2e": {"value": round(world * B * K / (t_e2e * 1e-3), 3), "unit": UNIT,
+            "e2e": {"value": round(jobs * B * K / (t_e2e * 1e-3), 3), "unit": UNIT,
                     "h2d_bytes_per_step": 4 * B, "d2h_bytes_per_step": 4 * B},
             "gpu_launches": int(launches),
             "roofline": roof,
             "prefill_gemm": gemm,
             "step_roofline": {"bytes_per_step": int(step_bytes), "achieved": round(step_gbs, 1),
-                              "peak": hbm, "unit": "GB/s", "frac": round(step_gbs / hbm, 4),
-                              "peak_kind": kind},
+                              "peak": round(hbm * step_peak_gpus, 1), "unit": "GB/s",
+                              "frac": round(step_gbs / (hbm * step_peak_gpus), 4), "peak_kind": kind,
+                              "gpus": step_peak_gpus},
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
         }
-    sess.close()
+    if pg:
+        pg.barrier()  # no rank leaves while another may still run collectives
+    sess.close()  # releases the graph that holds the NCCL calls first
+    if comm:
+        comm.close()
     model.close()
     dev.close()
     if pg:
@@ -501,6 +524,8 @@ def main():
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--batch", type=int, default=1, choices=[1, 2, 4, 8])
+    ap.add_argument("--replicas", action="store_true",
+                    help="with several GPUs: independent replicas instead of tensor parallelism")
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-roofline", action="store_true",

@@ -360,6 +360,29 @@ uint64_t pai_b200_model_weight_bytes(const pai_b200_model_t *m);
  * the lm-head shard plus one embedding row). */
 uint64_t pai_b200_model_step_weight_bytes(const pai_b200_model_t *m);
 
+/* ---- tensor parallelism (NCCL over NVLink, one process per GPU) ----------- */
+
+/* No reference counterpart: the reference runs on one device. Ranks of
+ * one node share a communicator; the exchange steps of a tensor-parallel
+ * decode (all-reduce of the o/down partial sums, argmax across lm-head
+ * vocabulary shards) run on it, captured into the session's CUDA graph. */
+typedef struct pai_b200_tp pai_b200_tp_t;
+#define PAI_B200_TP_ID_BYTES 128
+/* Make a communicator id on one rank; hand it to every rank out of band. */
+pai_status_t pai_b200_tp_unique_id(uint8_t id[PAI_B200_TP_ID_BYTES]);
+/* Join the communicator as `rank` of `size` on ctx's device. Collective:
+ * every rank calls it with the same id. */
+pai_status_t pai_b200_tp_create(pai_b200_ctx_t *ctx, const uint8_t id[PAI_B200_TP_ID_BYTES],
+                                uint32_t rank, uint32_t size, pai_b200_tp_t **out);
+pai_status_t pai_b200_tp_destroy(pai_b200_tp_t *tp);
+uint32_t pai_b200_tp_rank(const pai_b200_tp_t *tp);
+uint32_t pai_b200_tp_size(const pai_b200_tp_t *tp);
+/* In-place sum over all ranks of n fp32 values, on the context's stream. */
+pai_status_t pai_b200_tp_allreduce_f32(pai_b200_tp_t *tp, float *buf, uint64_t n);
+/* Attach the communicator to a model created for the same rank and size
+ * (before pai_b200_session_create; the model does not own it). */
+pai_status_t pai_b200_model_set_tp(pai_b200_model_t *m, pai_b200_tp_t *tp);
+
 /* A decode session of `batch` independent sequences with an fp16 KV cache
  * of max_ctx positions per sequence ([layer][kv_head][pos][head_dim],
  * split by KV head across tensor-parallel ranks). */

@@ -103,6 +103,13 @@ SIGNATURES = {
     "pai_b200_op_count": (U32, []),
     "pai_b200_op": (C.POINTER(OpDescriptor), [U32]),
     "pai_b200_model_create": (I32, [P, C.POINTER(ModelCfg), U32, U32, PP]),
+    "pai_b200_model_set_tp": (I32, [P, P]),
+    "pai_b200_tp_unique_id": (I32, [P]),
+    "pai_b200_tp_create": (I32, [P, P, U32, U32, PP]),
+    "pai_b200_tp_destroy": (I32, [P]),
+    "pai_b200_tp_rank": (U32, [P]),
+    "pai_b200_tp_size": (U32, [P]),
+    "pai_b200_tp_allreduce_f32": (I32, [P, P, U64]),
     "pai_b200_model_destroy": (I32, [P]),
     "pai_b200_model_set_tensor": (I32, [P, U32, U32, P]),
     "pai_b200_model_synthesize": (I32, [P, U64]),

@@ -179,6 +179,54 @@ class Device:
         check(load().pai_b200_register_ops(C.byref(registry)), "register_ops")
 
 
+TP_ID_BYTES = 128
+
+
+def share_tp_id(rank: int, make_id, group=None) -> bytes:
+    """Rank 0 makes a communicator id with `make_id()`, every rank of the
+    torch.distributed `group` (gloo is enough) receives the same bytes."""
+    import torch
+    import torch.distributed as dist
+    t = torch.zeros(TP_ID_BYTES, dtype=torch.uint8)
+    if rank == 0:
+        t[:] = torch.frombuffer(bytearray(make_id()), dtype=torch.uint8)
+    dist.broadcast(t, src=0, group=group)
+    return bytes(t.tolist())
+
+
+class TPComm:
+    """Tensor-parallel communicator of one rank (pai_b200_tp_*: NCCL over
+    NVLink). Every rank of the group constructs it with the same id."""
+
+    def __init__(self, dev: Device, rank: int, size: int, uid: bytes):
+        if len(uid) != TP_ID_BYTES:
+            raise ValueError(f"communicator id must be {TP_ID_BYTES} bytes")
+        self.dev, self.rank, self.size = dev, rank, size
+        buf = (C.c_uint8 * TP_ID_BYTES).from_buffer_copy(uid)
+        h = C.c_void_p()
+        check(load().pai_b200_tp_create(dev.ctx, buf, rank, size, C.byref(h)), "tp_create")
+        self.h = h.value
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = (C.c_uint8 * TP_ID_BYTES)()
+        check(load().pai_b200_tp_unique_id(buf), "tp_unique_id")
+        return bytes(buf)
+
+    @classmethod
+    def over_group(cls, dev: Device, rank: int, size: int, group=None) -> "TPComm":
+        """Create the communicator of a torch.distributed group (id from rank 0)."""
+        return cls(dev, rank, size, share_tp_id(rank, cls.unique_id, group))
+
+    def allreduce(self, buf: Buffer, n: int):
+        check(load().pai_b200_tp_allreduce_f32(self.h, buf.ptr, n), "tp_allreduce")
+
+    def close(self):
+        if self.h:
+            load().pai_b200_tp_destroy(self.h)
+            self.h = None
+
+
 class Model:
     """LLaMA-shaped decoder resident on one device (one tensor-parallel rank)."""
 
@@ -202,6 +250,10 @@ class Model:
 
     def step_weight_bytes(self) -> int:
         return int(load().pai_b200_model_step_weight_bytes(self.h))
+
+    def set_tp(self, comm: "TPComm | None"):
+        """Attach the rank's communicator (needed before a tensor-parallel session)."""
+        check(load().pai_b200_model_set_tp(self.h, comm.h if comm else None), "model_set_tp")
 
     def close(self):
         if self.h:

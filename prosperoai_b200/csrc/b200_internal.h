@@ -118,6 +118,8 @@ pai_status_t b200_cuda(int err, const char *what);
 
 void *b200_ctx_stream(pai_b200_ctx_t *ctx);
 int b200_ctx_device(pai_b200_ctx_t *ctx);
+/* Make ctx's device current on the calling thread. */
+pai_status_t b200_ctx_use_device(pai_b200_ctx_t *ctx);
 void b200_ctx_count_launch(pai_b200_ctx_t *ctx, uint32_t kernels);
 /* Count `kernels` launches and report a launch error under `name`. With
  * PAI_B200_SYNC_CHECK=1 in the environment (and outside graph capture)
@@ -208,6 +210,12 @@ pai_status_t b200_launch_attn_step(pai_b200_ctx_t *ctx, uint32_t batch, uint32_t
                                    const b200_xq_t *xq_out);
 pai_status_t b200_launch_argmax(pai_b200_ctx_t *ctx, uint64_t rows, uint64_t n,
                                 const float *logits, int32_t *out);
+/* Tensor-parallel argmax: this shard's (maximum, index + v0) per row into
+ * pair[row][2]; then the merge of all ranks' pairs, pairs[rank][row][2]. */
+pai_status_t b200_launch_argmax_pair(pai_b200_ctx_t *ctx, uint64_t rows, uint64_t n, uint32_t v0,
+                                     const float *logits, float *pair);
+pai_status_t b200_launch_argmax_ranks(pai_b200_ctx_t *ctx, uint32_t rows, uint32_t nranks, const float *pairs,
+                                      int32_t *out);
 pai_status_t b200_launch_step_tail(pai_b200_ctx_t *ctx, uint32_t batch,
                                    int32_t *tok_out, int32_t *tok_in, int32_t *pos);
 pai_status_t b200_launch_synth_normal(pai_b200_ctx_t *ctx, float *dst, uint64_t rows,

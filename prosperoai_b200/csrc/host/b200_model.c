@@ -469,6 +469,15 @@ static pai_status_t enqueue_step(pai_b200_session_t *s) {
     if (!st) st = pai_b200_alloc(ctx, (bytes), (void **)&(ptr)); \
   } while (0)
 
+pai_status_t pai_b200_model_set_tp(pai_b200_model_t *m, pai_b200_tp_t *tp) {
+  if (!m) return b200_fail(PAI_ERR_INVALID_ARG, "model_set_tp: NULL model");
+  if (tp && (pai_b200_tp_size(tp) != m->tp || pai_b200_tp_rank(tp) != m->rank))
+    return b200_fail(PAI_ERR_MISMATCH, "model_set_tp: communicator rank %u of %u, model rank %u of %u",
+                     pai_b200_tp_rank(tp), pai_b200_tp_size(tp), m->rank, m->tp);
+  m->tp_comm = tp;
+  return PAI_OK;
+}
+
 pai_status_t pai_b200_session_create(pai_b200_model_t *m, uint32_t batch, uint32_t max_ctx,
                                      pai_b200_session_t **out) {
   pai_b200_session_t *s;

@@ -25,6 +25,7 @@ struct pai_b200_ctx {
   void *xq;               // activation scratch of the public GEMV entry points
   uint64_t xq_bytes;
   uint64_t launches;
+  uint32_t captured;  // this library's launches recorded into the graph being captured
   int capturing;
   int pdl;          // launch the decode-step kernels with programmatic dependent launch
   int pdl_allowed;  // PAI_B200_PDL=0 in the environment turns it off
@@ -126,6 +127,9 @@ extern "C" pai_status_t pai_b200_shutdown(pai_b200_ctx_t *c) {
 
 extern "C" void *b200_ctx_stream(pai_b200_ctx_t *c) { return c->stream; }
 extern "C" int b200_ctx_device(pai_b200_ctx_t *c) { return c->device; }
+extern "C" pai_status_t b200_ctx_use_device(pai_b200_ctx_t *c) {
+  return b200_cuda(cudaSetDevice(c->device), "cudaSetDevice");
+}
 extern "C" int b200_ctx_pdl(pai_b200_ctx_t *c) { return c->pdl; }
 extern "C" void b200_ctx_set_pdl(pai_b200_ctx_t *c, int on) { c->pdl = on && c->pdl_allowed; }
 extern "C" uint32_t *b200_ctx_errflag(pai_b200_ctx_t *c) { return c->err_dev; }
@@ -148,7 +152,10 @@ extern "C" pai_status_t b200_ctx_xq(pai_b200_ctx_t *c, uint64_t bytes, void **bu
   return PAI_OK;
 }
 extern "C" void b200_ctx_count_launch(pai_b200_ctx_t *c, uint32_t k) {
-  if (!c->capturing) c->launches += k;
+  if (c->capturing)
+    c->captured += k;
+  else
+    c->launches += k;
 }
 extern "C" uint64_t pai_b200_launch_count(pai_b200_ctx_t *c) { return c ? c->launches : 0; }
 
@@ -301,14 +308,12 @@ extern "C" pai_status_t pai_b200_event_elapsed(void *a, void *b, float *ms) {
 
 // ---- graphs -------------------------------------------------------------------------------
 
-static thread_local uint64_t g_capture_start;
-
 extern "C" pai_status_t b200_graph_begin(pai_b200_ctx_t *c) {
   pai_status_t st = b200_cuda(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal),
                               "cudaStreamBeginCapture");
   if (st) return st;
   c->capturing = 1;
-  g_capture_start = c->launches;
+  c->captured = 0;
   return PAI_OK;
 }
 
@@ -317,16 +322,14 @@ extern "C" pai_status_t b200_graph_end(pai_b200_ctx_t *c, void **exec, uint32_t 
   c->capturing = 0;
   pai_status_t st = b200_cuda(cudaStreamEndCapture(c->stream, &g), "cudaStreamEndCapture");
   if (st) return st;
-  size_t nodes = 0;
-  cudaGraphGetNodes(g, nullptr, &nodes);
   cudaGraphExec_t ge = nullptr;
   st = b200_cuda(cudaGraphInstantiate(&ge, g, 0), "cudaGraphInstantiate");
   cudaGraphDestroy(g);
   if (st) return st;
   *exec = ge;
-  // Count kernel nodes: every node this library captures is a kernel,
-  // except memset/memcpy nodes which the launchers never issue in steps.
-  *kernels = (uint32_t)nodes;
+  // This library's kernels in the graph (collective kernels of NCCL, when
+  // the step holds tensor-parallel exchanges, are not counted).
+  *kernels = c->captured;
   return PAI_OK;
 }
 

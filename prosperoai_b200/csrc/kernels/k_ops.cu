@@ -143,9 +143,13 @@ __device__ __forceinline__ void amax_block(float &best, uint32_t &bidx) {
   __syncthreads();
 }
 
+// Greedy argmax of each logit row: slices per CTA, the last slice to finish
+// merges them (first index of the maximum, as models/sampler.c:89-99). With
+// `pair` set, the row's result is written as (maximum, index + v0) for a
+// merge across tensor-parallel vocabulary shards instead of to `out`.
 __global__ void __launch_bounds__(256) k_argmax(uint64_t n, uint64_t per, const float *__restrict__ logits,
                                                 int32_t *__restrict__ out, float *__restrict__ part,
-                                                uint32_t *__restrict__ cnt) {
+                                                uint32_t *__restrict__ cnt, float *__restrict__ pair, uint32_t v0) {
   pdl_trigger();
   pdl_wait();
   const uint32_t row = blockIdx.y, slice = blockIdx.x, nsl = gridDim.x;
@@ -178,9 +182,30 @@ __global__ void __launch_bounds__(256) k_argmax(uint64_t n, uint64_t per, const 
                __float_as_uint(__ldcg(&part[((size_t)row * nsl + s) * 2 + 1])));
   amax_block(best, bidx);
   if (threadIdx.x == 0) {
-    out[row] = (int32_t)bidx;
+    if (pair) {
+      pair[(size_t)row * 2] = best;
+      pair[(size_t)row * 2 + 1] = __uint_as_float(bidx == 0xFFFFFFFFu ? bidx : bidx + v0);
+    } else {
+      out[row] = (int32_t)bidx;
+    }
     cnt[row] = 0;
   }
+}
+
+// Merge the (maximum, index) pairs of `nranks` vocabulary shards, ranks in
+// order: pairs[rank][row][2]. Shard r holds the indices [r vl, (r + 1) vl),
+// so the first index of the maximum over the whole vocabulary wins ties.
+__global__ void k_argmax_ranks(uint32_t rows, uint32_t nranks, const float *__restrict__ pairs,
+                               int32_t *__restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
+  const uint32_t row = blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= rows) return;
+  float best = -INFINITY;
+  uint32_t bidx = 0xFFFFFFFFu;
+  for (uint32_t r = 0; r < nranks; r++)
+    amax_merge(best, bidx, pairs[((size_t)r * rows + row) * 2], __float_as_uint(pairs[((size_t)r * rows + row) * 2 + 1]));
+  out[row] = (int32_t)bidx;
 }
 
 // End of a device-resident decode step: advance the position and feed
@@ -264,8 +289,27 @@ extern "C" pai_status_t b200_launch_argmax(pai_b200_ctx_t *ctx, uint64_t rows, u
   uint32_t *cnt = nullptr;
   pai_status_t st = b200_ctx_scratch(ctx, rows * nsl * 2, (uint32_t)rows, &part, &cnt);
   if (st) return st;
-  b200_launch(ctx, k_argmax, dim3((unsigned)nsl, (unsigned)rows), dim3(256), 0, n, per, logits, out, part, cnt);
+  b200_launch(ctx, k_argmax, dim3((unsigned)nsl, (unsigned)rows), dim3(256), 0, n, per, logits, out, part, cnt,
+              (float *)nullptr, 0u);
   return b200_launched(ctx, 1, "k_argmax");
+}
+
+extern "C" pai_status_t b200_launch_argmax_pair(pai_b200_ctx_t *ctx, uint64_t rows, uint64_t n, uint32_t v0,
+                                                const float *logits, float *pair) {
+  const uint64_t nsl = std::min<uint64_t>(148, (n + 2047) / 2048), per = (n + nsl - 1) / nsl;
+  float *part = nullptr;
+  uint32_t *cnt = nullptr;
+  pai_status_t st = b200_ctx_scratch(ctx, rows * nsl * 2, (uint32_t)rows, &part, &cnt);
+  if (st) return st;
+  b200_launch(ctx, k_argmax, dim3((unsigned)nsl, (unsigned)rows), dim3(256), 0, n, per, logits, (int32_t *)nullptr,
+              part, cnt, pair, v0);
+  return b200_launched(ctx, 1, "k_argmax");
+}
+
+extern "C" pai_status_t b200_launch_argmax_ranks(pai_b200_ctx_t *ctx, uint32_t rows, uint32_t nranks,
+                                                 const float *pairs, int32_t *out) {
+  b200_launch(ctx, k_argmax_ranks, dim3((rows + 31) / 32), dim3(32), 0, rows, nranks, pairs, out);
+  return b200_launched(ctx, 1, "k_argmax_ranks");
 }
 
 extern "C" pai_status_t pai_b200_argmax_f32(pai_b200_ctx_t *ctx, uint64_t rows, uint64_t n, const float *logits,

@@ -1,0 +1,113 @@
+"""Tensor parallelism on 2 GPUs (one process per GPU, NCCL over NVLink).
+
+- the communicator's all-reduce sums exactly (small integers in fp32);
+- a 2-rank tensor-parallel decode (column-parallel q/k/v/gate/up,
+  row-parallel o/down with the all-reduce, vocabulary-sharded lm head with
+  the cross-rank argmax) gives the same 64 greedy tokens on both ranks as
+  the oracle's unsharded decode of the same synthetic weights.
+
+Skipped on a box with fewer than 2 GPUs. Children bind one GPU each and
+run with NVLink SHARP (NVLS) off, so no rank binds memory to an NVLink
+multicast object; the parent bounds every wait and kills its own children
+if one stalls.
+"""
+import datetime
+import multiprocessing as mp
+import os
+import socket
+
+import numpy as np
+import pytest
+
+from oracle import py_oracle as po
+
+pytestmark = pytest.mark.gpu
+
+TP_CFG = dict(n_layer=2, n_embd=512, n_head=4, n_head_kv=2, head_dim=128, n_ff=1024,
+              vocab=2048, eps=1e-5, rope_theta=500000.0, wtype=po.Q4_0, etype=po.Q8_0)
+SEED = 20261203
+STEPS = 64
+
+
+def _gpu_count():
+    import torch
+    return torch.cuda.device_count()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, cfg, prompt, steps, max_ctx, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    out = {"rank": rank}
+    try:
+        import torch.distributed as dist
+        from prosperoai_b200.api import Device, Model, Session, TPComm
+        from test_gpu_model import gpu_generate
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60))
+        dev = Device(rank)
+        comm = TPComm.over_group(dev, rank, world)
+        n = 4096
+        buf = dev.put(np.arange(n, dtype=np.float32) * (rank + 1))
+        comm.allreduce(buf, n)
+        dev.sync()
+        out["allreduce"] = buf.download(np.float32)
+        model = Model(dev, cfg, tp_rank=rank, tp_size=world)
+        model.synthesize(SEED)
+        model.set_tp(comm)
+        sess = Session(model, 1, max_ctx)
+        out["tokens"] = gpu_generate(sess, prompt, steps)
+        dist.barrier()
+        sess.close()
+        comm.close()
+        model.close()
+        dev.close()
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:  # reported to the parent, which fails the test
+        out["error"] = repr(e)
+    q.put(out)
+
+
+def _run_ranks(world, cfg, prompt, steps, max_ctx):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, cfg, prompt, steps, max_ctx, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    try:
+        for _ in range(world):
+            r = q.get(timeout=600)
+            results[r["rank"]] = r
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+                p.join()
+    return results
+
+
+def test_tp2_decode_matches_oracle(dev):
+    if _gpu_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from test_gpu_model import oracle_generate, synth_weights
+    cfg = dict(TP_CFG)
+    prompt = list(np.random.default_rng(7).integers(0, cfg["vocab"], 5))
+    max_ctx = len(prompt) + STEPS + 4
+    w = synth_weights(dev, cfg, SEED)
+    want, _ = oracle_generate(cfg, w, prompt, STEPS, max_ctx)
+    res = _run_ranks(2, cfg, prompt, STEPS, max_ctx)
+    for r in range(2):
+        assert "error" not in res[r], res[r]["error"]
+        np.testing.assert_array_equal(res[r]["allreduce"], np.arange(4096, dtype=np.float32) * 3)
+        assert res[r]["tokens"] == [int(t) for t in want], f"rank {r}"
