@@ -216,6 +216,21 @@ pai_status_t b200_launch_argmax_pair(pai_b200_ctx_t *ctx, uint64_t rows, uint64_
                                      const float *logits, float *pair);
 pai_status_t b200_launch_argmax_ranks(pai_b200_ctx_t *ctx, uint32_t rows, uint32_t nranks, const float *pairs,
                                       int32_t *out);
+
+/* Tensor-parallel exchange over NVLink peer memory (kernels/k_tp.cu). */
+#define B200_TP_MAX_RANKS 8
+#define B200_TP_HANDLE_BYTES 64
+/* This rank's exchange buffer (header + 2 slots of `cap` floats), zeroed,
+ * and its IPC handle for the other ranks. */
+pai_status_t b200_tp_xbuf_alloc(pai_b200_ctx_t *ctx, uint64_t cap, void **buf, uint8_t handle[B200_TP_HANDLE_BYTES]);
+pai_status_t b200_tp_xbuf_open(pai_b200_ctx_t *ctx, const uint8_t handle[B200_TP_HANDLE_BYTES], void **buf);
+void b200_tp_xbuf_close(void *buf);
+void b200_tp_xbuf_free(void *buf);
+float *b200_tp_xbuf_slot(void *buf, uint32_t slot, uint64_t cap);
+/* x[0..n) += sum over ranks (in rank order) of slot `slot` of every rank's
+ * buffer; bufs[r] = rank r's buffer as mapped in this process. */
+pai_status_t b200_launch_tp_allreduce_add(pai_b200_ctx_t *ctx, void *const *bufs, uint32_t rank, uint32_t nranks,
+                                          uint32_t slot, uint64_t cap, float *x, uint64_t n);
 pai_status_t b200_launch_step_tail(pai_b200_ctx_t *ctx, uint32_t batch,
                                    int32_t *tok_out, int32_t *tok_in, int32_t *pos);
 pai_status_t b200_launch_synth_normal(pai_b200_ctx_t *ctx, float *dst, uint64_t rows,

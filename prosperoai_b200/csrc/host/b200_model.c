@@ -401,11 +401,13 @@ struct pai_b200_session {
   uint64_t seq_stride, layer_stride;
   void *graph;
   uint32_t graph_kernels;
-  void *tp; /* tensor-parallel communicator, NULL on one GPU */
+  pai_b200_tp_t *tp; /* tensor-parallel communicator, NULL on one GPU */
 };
 
 /* Tensor-parallel hooks (csrc/host/b200_tp.c). */
-pai_status_t b200_tp_allreduce(void *tp, pai_b200_ctx_t *ctx, float *buf, uint64_t n);
+pai_status_t b200_tp_reserve(pai_b200_tp_t *tp, uint64_t cap);
+float *b200_tp_slot(pai_b200_tp_t *tp, uint32_t slot);
+pai_status_t b200_tp_allreduce_add(pai_b200_tp_t *tp, pai_b200_ctx_t *ctx, uint32_t slot, float *x, uint64_t n);
 pai_status_t b200_tp_argmax(void *tp, pai_b200_ctx_t *ctx, uint32_t batch, uint32_t vl, uint32_t v0,
                             const float *logits, int32_t *tok_out);
 
@@ -440,18 +442,21 @@ static pai_status_t enqueue_step(pai_b200_session_t *s) {
       if (!st)
         st = b200_launch_gemv(ctx, c->wtype, B, E, m->k_o, m->wo[l], &s->xq_o, s->x, s->x, B200_EPI_RESIDUAL, NULL);
     } else {
-      if (!st) st = b200_launch_gemv(ctx, c->wtype, B, E, m->k_o, m->wo[l], &s->xq_o, NULL, s->ox, B200_EPI_STORE, NULL);
-      if (!st) st = b200_tp_allreduce(s->tp, ctx, s->ox, (uint64_t)B * E);
-      if (!st) st = pai_b200_vecadd_f32(ctx, s->x, s->ox, s->x, (uint64_t)B * E);
+      /* partial o output into exchange slot 0, then x += sum over ranks */
+      if (!st)
+        st = b200_launch_gemv(ctx, c->wtype, B, E, m->k_o, m->wo[l], &s->xq_o, NULL, b200_tp_slot(s->tp, 0),
+                              B200_EPI_STORE, NULL);
+      if (!st) st = b200_tp_allreduce_add(s->tp, ctx, 0, s->x, (uint64_t)B * E);
     }
     if (!st) st = norm_gemv(s, c->wtype, 2ull * m->ffl, m->wgu[l], m->ffn_norm[l], s->h, B200_EPI_SILU_GLU, &s->xq_h);
     if (m->tp == 1) {
       if (!st)
         st = b200_launch_gemv(ctx, c->wtype, B, E, m->ffl, m->wdown[l], &s->xq_h, s->x, s->x, B200_EPI_RESIDUAL, NULL);
     } else {
-      if (!st) st = b200_launch_gemv(ctx, c->wtype, B, E, m->ffl, m->wdown[l], &s->xq_h, NULL, s->ox, B200_EPI_STORE, NULL);
-      if (!st) st = b200_tp_allreduce(s->tp, ctx, s->ox, (uint64_t)B * E);
-      if (!st) st = pai_b200_vecadd_f32(ctx, s->x, s->ox, s->x, (uint64_t)B * E);
+      if (!st)
+        st = b200_launch_gemv(ctx, c->wtype, B, E, m->ffl, m->wdown[l], &s->xq_h, NULL, b200_tp_slot(s->tp, 1),
+                              B200_EPI_STORE, NULL);
+      if (!st) st = b200_tp_allreduce_add(s->tp, ctx, 1, s->x, (uint64_t)B * E);
     }
   }
   if (!st) st = norm_gemv(s, c->etype, m->vl, m->output, m->output_norm, s->logits, B200_EPI_STORE, NULL);
@@ -498,6 +503,7 @@ pai_status_t pai_b200_session_create(pai_b200_model_t *m, uint32_t batch, uint32
   if (!s) return b200_fail(PAI_ERR_NOMEM, "session_create: host allocation");
   s->m = m;
   s->tp = m->tp_comm;
+  if (s->tp) st = b200_tp_reserve(s->tp, (uint64_t)batch * c->n_embd); /* collective */
   s->batch = batch;
   s->max_ctx = max_ctx;
   s->seq_stride = (uint64_t)m->hkl * max_ctx * c->head_dim;

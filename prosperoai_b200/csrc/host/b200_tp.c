@@ -10,8 +10,14 @@
  * torch.distributed) shares that copy. Only the handful of entry points
  * and constants used here are declared, with the types of NCCL's public
  * API: ncclUniqueId is 128 opaque bytes passed by value, ncclComm_t an
- * opaque pointer, ncclResult_t 0 on success; data type 2 = int32,
+ * opaque pointer, ncclResult_t 0 on success; data type 1 = uint8,
  * 7 = float32; reduction 0 = sum.
+ *
+ * The all-reduce of the o/down partial outputs does not use NCCL: it runs
+ * over NVLink peer memory, fused with the residual add (kernels/k_tp.cu),
+ * on exchange buffers mapped between the ranks with CUDA IPC (handles
+ * exchanged with an NCCL all-gather). NCCL carries the lm-head argmax
+ * pairs and the public pai_b200_tp_allreduce_f32.
  */
 #include <dlfcn.h>
 #include <pthread.h>
@@ -25,7 +31,7 @@ typedef struct {
   char internal[PAI_B200_TP_ID_BYTES];
 } nccl_uid_t;
 typedef void *nccl_comm_t;
-enum { NCCL_SUCCESS = 0, NCCL_FLOAT32 = 7, NCCL_SUM = 0 };
+enum { NCCL_SUCCESS = 0, NCCL_UINT8 = 1, NCCL_FLOAT32 = 7, NCCL_SUM = 0 };
 
 static struct {
   void *lib;
@@ -80,8 +86,63 @@ struct pai_b200_tp {
   pai_b200_ctx_t *ctx;
   nccl_comm_t comm;
   uint32_t rank, size;
-  float *pairs; /* argmax exchange: [rank][row][2] for up to 8 rows */
+  float *pairs;                     /* argmax exchange: [rank][row][2] for up to 8 rows */
+  void *xbuf[B200_TP_MAX_RANKS];    /* exchange buffers: own (allocated), peers (IPC-mapped) */
+  uint64_t cap;                     /* floats per exchange slot */
 };
+
+static void xbufs_release(pai_b200_tp_t *tp) {
+  for (uint32_t r = 0; r < tp->size; r++) {
+    if (!tp->xbuf[r]) continue;
+    if (r == tp->rank)
+      b200_tp_xbuf_free(tp->xbuf[r]);
+    else
+      b200_tp_xbuf_close(tp->xbuf[r]);
+    tp->xbuf[r] = NULL;
+  }
+  tp->cap = 0;
+}
+
+/* Make every rank's exchange buffer hold `cap` floats per slot and map all
+ * of them here. Collective: every rank calls it with the same cap. */
+pai_status_t b200_tp_reserve(pai_b200_tp_t *tp, uint64_t cap) {
+  uint8_t *dev_h = NULL, *host_h = NULL, mine[B200_TP_HANDLE_BYTES];
+  pai_status_t st;
+  if (cap <= tp->cap) return PAI_OK;
+  st = pai_b200_sync(tp->ctx);
+  if (st) return st;
+  xbufs_release(tp);
+  st = b200_tp_xbuf_alloc(tp->ctx, cap, &tp->xbuf[tp->rank], mine);
+  if (!st) st = pai_b200_alloc(tp->ctx, (uint64_t)tp->size * B200_TP_HANDLE_BYTES, (void **)&dev_h);
+  if (!st) {
+    host_h = (uint8_t *)malloc((size_t)tp->size * B200_TP_HANDLE_BYTES);
+    if (!host_h) st = b200_fail(PAI_ERR_NOMEM, "tp_reserve: host allocation");
+  }
+  if (!st) st = pai_b200_memcpy_h2d(tp->ctx, dev_h + (uint64_t)tp->rank * B200_TP_HANDLE_BYTES, mine, sizeof mine);
+  if (!st)
+    st = nccl_check(g_nccl.all_gather(dev_h + (uint64_t)tp->rank * B200_TP_HANDLE_BYTES, dev_h, B200_TP_HANDLE_BYTES,
+                                      NCCL_UINT8, tp->comm, b200_ctx_stream(tp->ctx)),
+                    "ncclAllGather (exchange handles)");
+  if (!st) st = pai_b200_memcpy_d2h(tp->ctx, host_h, dev_h, (uint64_t)tp->size * B200_TP_HANDLE_BYTES);
+  if (!st) st = pai_b200_sync(tp->ctx);
+  for (uint32_t r = 0; !st && r < tp->size; r++)
+    if (r != tp->rank) st = b200_tp_xbuf_open(tp->ctx, host_h + (uint64_t)r * B200_TP_HANDLE_BYTES, &tp->xbuf[r]);
+  free(host_h);
+  pai_b200_free(tp->ctx, dev_h);
+  if (st) {
+    xbufs_release(tp);
+    return st;
+  }
+  tp->cap = cap;
+  return PAI_OK;
+}
+
+float *b200_tp_slot(pai_b200_tp_t *tp, uint32_t slot) { return b200_tp_xbuf_slot(tp->xbuf[tp->rank], slot, tp->cap); }
+
+pai_status_t b200_tp_allreduce_add(pai_b200_tp_t *tp, pai_b200_ctx_t *ctx, uint32_t slot, float *x, uint64_t n) {
+  if (!tp) return b200_fail(PAI_ERR_INIT, "tp_allreduce_add: no communicator");
+  return b200_launch_tp_allreduce_add(ctx, tp->xbuf, tp->rank, tp->size, slot, tp->cap, x, n);
+}
 
 pai_status_t pai_b200_tp_unique_id(uint8_t id[PAI_B200_TP_ID_BYTES]) {
   nccl_uid_t u;
@@ -101,7 +162,8 @@ pai_status_t pai_b200_tp_create(pai_b200_ctx_t *ctx, const uint8_t id[PAI_B200_T
   pai_status_t st;
   if (!ctx || !id || !out) return b200_fail(PAI_ERR_INVALID_ARG, "tp_create: NULL");
   *out = NULL;
-  if (size == 0 || size > 64 || rank >= size) return b200_fail(PAI_ERR_INVALID_ARG, "tp_create: rank %u of %u", rank, size);
+  if (size == 0 || size > B200_TP_MAX_RANKS || rank >= size)
+    return b200_fail(PAI_ERR_INVALID_ARG, "tp_create: rank %u of %u (at most %u ranks)", rank, size, B200_TP_MAX_RANKS);
   st = nccl_ready();
   if (st) return st;
   st = b200_ctx_use_device(ctx);
@@ -127,6 +189,7 @@ pai_status_t pai_b200_tp_destroy(pai_b200_tp_t *tp) {
   pai_status_t st = PAI_OK;
   if (!tp) return PAI_OK;
   pai_b200_sync(tp->ctx);
+  xbufs_release(tp);
   pai_b200_free(tp->ctx, tp->pairs);
   if (tp->comm) st = nccl_check(g_nccl.comm_destroy(tp->comm), "ncclCommDestroy");
   free(tp);
