@@ -125,6 +125,13 @@ pai_status_t pai_b200_memset(pai_b200_ctx_t *ctx, void *dst, int value,
                              uint64_t bytes);
 /* Wait for all work queued on the context; reports any device error. */
 pai_status_t pai_b200_sync(pai_b200_ctx_t *ctx);
+/* Launch this context's kernels with programmatic dependent launch (1) or
+ * plainly (0, the default outside a decode step): each kernel then starts
+ * its prologue (weight prefetch) while its predecessor on the stream
+ * finishes, and waits for the predecessor before it reads dependent data.
+ * No reference counterpart. The environment variable PAI_B200_PDL=0
+ * disables it for the process. */
+pai_status_t pai_b200_set_pdl(pai_b200_ctx_t *ctx, int on);
 
 /* Stream-ordered timing: event_record places a marker, event_elapsed
  * waits for both markers and returns milliseconds between them. */

@@ -70,6 +70,7 @@ SIGNATURES = {
     "pai_b200_memcpy_d2d": (I32, [P, P, P, U64]),
     "pai_b200_memset": (I32, [P, P, C.c_int, U64]),
     "pai_b200_sync": (I32, [P]),
+    "pai_b200_set_pdl": (I32, [P, I32]),
     "pai_b200_event_create": (I32, [P, PP]),
     "pai_b200_event_destroy": (I32, [P, P]),
     "pai_b200_event_record": (I32, [P, P]),

@@ -132,6 +132,11 @@ extern "C" pai_status_t b200_ctx_use_device(pai_b200_ctx_t *c) {
 }
 extern "C" int b200_ctx_pdl(pai_b200_ctx_t *c) { return c->pdl; }
 extern "C" void b200_ctx_set_pdl(pai_b200_ctx_t *c, int on) { c->pdl = on && c->pdl_allowed; }
+extern "C" pai_status_t pai_b200_set_pdl(pai_b200_ctx_t *c, int on) {
+  if (!c) return b200_fail(PAI_ERR_INVALID_ARG, "set_pdl: NULL context");
+  b200_ctx_set_pdl(c, on);
+  return PAI_OK;
+}
 extern "C" uint32_t *b200_ctx_errflag(pai_b200_ctx_t *c) { return c->err_dev; }
 
 extern "C" pai_status_t b200_ctx_xq(pai_b200_ctx_t *c, uint64_t bytes, void **buf) {

@@ -53,25 +53,20 @@ namespace {
 
 constexpr int kStages = 4;                   // depth of the CTA's weight ring
 constexpr int kXSlots = 3;                   // staged-x slots (current, next, one being released)
-// CTA shape: consumer warps (one 16-row tile each; a group is kConsT
-// tiles) + one producer warp, one CTA per SM. Batch <= 2 keeps its shared
-// memory to 110 KB so that, under programmatic dependent launch, the next
-// kernel's CTA fits beside it and its producer prefills that kernel's
-// weights while this one streams: in the decode step that is 2.6% faster
-// than two GEMV CTAs per SM (which is faster for a GEMV timed alone). With
-// B200_GEMV_WIDE=1 batch <= 2 runs 16 consumers per CTA instead (the 66 MB
-// gate/up matrix alone is 7% faster; the decode step is not).
-#ifndef B200_GEMV_WIDE
-#define B200_GEMV_WIDE 0
-#endif
-template <int NT>
-constexpr int kConsT = (NT == 1 && B200_GEMV_WIDE) ? 16 : 8;
-template <int NT>
-constexpr int kThreadsT = (kConsT<NT> + 1) * 32;
-template <int NT>
-constexpr int kCtasPerSm = 1;
-template <int NT>
-constexpr size_t kSmemCap = (NT == 1 && !B200_GEMV_WIDE) ? 110 * 1024 : 220 * 1024;  // dynamic shared memory per CTA
+// CTA shape: CONS consumer warps (one 16-row tile each; a group is CONS
+// tiles) + one producer warp, one CTA per SM. Batch <= 2 with 8 consumers
+// keeps its shared memory to 110 KB so that, under programmatic dependent
+// launch, the next kernel's CTA fits beside it and its producer prefills
+// that kernel's weights while this one streams. Large batch-1/2 matrices
+// (>= kWideRows rows) run 16 consumers: the consumers bound the stream
+// there (about 0.7 us of issue per 18 KB stage with 8 of them), and twice
+// the warps hide their latencies (the 66 MB gate/up matrix: 23.7 -> 18.4
+// us per launch under programmatic dependent launch).
+constexpr uint32_t kWideRows = 16384;
+template <int NT, int CONS>
+constexpr int kThreadsT = (CONS + 1) * 32;
+template <int NT, int CONS>
+constexpr size_t kSmemCap = (NT == 1 && CONS == 8) ? 110 * 1024 : 220 * 1024;  // dynamic shared memory per CTA
 constexpr uint32_t M4 = 0x0F0F0F0Fu;
 constexpr uint64_t kWaitLimit = 2000000000ull;  // ns before a wait gives up (2 s)
 
@@ -436,9 +431,9 @@ __device__ void settle_splits(const GemvP &p, uint32_t (&tiles)[2], uint32_t (&n
 // once and quantises them unrolled, so loads and warp reductions overlap
 // instead of paying one L2 round trip per block.
 constexpr int kPB = 16;
-template <int NT>
-__device__ void norm_prologue(const GemvP &p, const XS &slot, int c, int lane, double (&red)[kConsT<NT>][8]) {
-  constexpr int kCons = kConsT<NT>;
+template <int NT, int CONS>
+__device__ void norm_prologue(const GemvP &p, const XS &slot, int c, int lane, double (&red)[CONS][8]) {
+  constexpr int kCons = CONS;
   const uint32_t nthr = kCons * 32, nblk = slot.quads * 4, kk = (uint32_t)p.xq.k;
   for (uint32_t vec = 0; vec < p.batch; vec++) {
     const float *xr = p.xf + (size_t)vec * kk;
@@ -488,9 +483,9 @@ __device__ void norm_prologue(const GemvP &p, const XS &slot, int c, int lane, d
   asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
 }
 
-template <uint32_t T, int NT>
-__global__ void __launch_bounds__(kThreadsT<NT>, kCtasPerSm<NT>) k_gemv(GemvP p) {
-  constexpr int kCons = kConsT<NT>;
+template <uint32_t T, int NT, int CONS>
+__global__ void __launch_bounds__(kThreadsT<NT, CONS>, 1) k_gemv(GemvP p) {
+  constexpr int kCons = CONS;
   using Un = Unit<T>;
   constexpr int U = Un::U, XPU = Un::XPU;
   constexpr uint32_t GQ = kCons * Un::QB, GS = kCons * Un::SB;  // bytes of one unit of a group
@@ -635,7 +630,7 @@ __global__ void __launch_bounds__(kThreadsT<NT>, kCtasPerSm<NT>) k_gemv(GemvP p)
   int nsplit = 0;
   Requant pend;
   if (p.xnorm) {
-    norm_prologue<NT>(p, slot_view(0), c, lane, red);
+    norm_prologue<NT, CONS>(p, slot_view(0), c, lane, red);
   } else if (p.resident && !mbar_wait(&xfull[0], 0, kWaitLimit)) {
     if (lane == 0) atomicExch(p.err, 1u);
     return;
@@ -728,26 +723,26 @@ int sm_count(pai_b200_ctx_t *ctx) {
   return v;
 }
 
-template <uint32_t T, int NT>
+template <uint32_t T, int NT, int CONS>
 pai_status_t launch_t(pai_b200_ctx_t *ctx, GemvP p) {
-  auto kern = k_gemv<T, NT>;
+  auto kern = k_gemv<T, NT, CONS>;
   using Un = Unit<T>;
-  constexpr int kCons = kConsT<NT>;
+  constexpr int kCons = CONS;
   const size_t ring = (size_t)kStages * Un::U * kCons * (Un::QB + Un::SB);
   p.ngroups = (p.ntiles + kCons - 1) / kCons;
   const uint64_t total = (uint64_t)p.ngroups * p.units;
-  const uint32_t grid = (uint32_t)std::min<uint64_t>(total, (uint64_t)kCtasPerSm<NT> * sm_count(ctx));
-  // x staging: all of x once per CTA when the CTA's share spans at least
-  // two groups' K ranges (so x is reused), or for the fused norm, and it
-  // fits beside the ring; else three slots of up to `upc` units, refilled
-  // one sub-item ahead, so a CTA with a short share stages only the x its
-  // units use.
+  const uint32_t grid = (uint32_t)std::min<uint64_t>(total, (uint64_t)sm_count(ctx));
+  // x staging: all of x once per CTA when it fits beside the ring (one
+  // bulk copy up front keeps the producer free to stream weights; staging
+  // x per sub-item made the producer wait on x slots: the 66 MB gate/up
+  // matrix went from 23.7 to 21.3 us per launch this way); else three
+  // slots of up to `upc` units, refilled one sub-item ahead.
   const size_t per_unit_x = (size_t)Un::XPU * (NT * 1024 + 2 * p.batch * 16);
-  const size_t room = kSmemCap<NT> - ring;
+  const size_t room = kSmemCap<NT, CONS> - ring;
   const bool fits = p.units * per_unit_x + 256 <= room;
   if (p.xnorm && !fits)
     return b200_fail(PAI_ERR_UNSUPPORTED, "gemv: x of %u units does not fit for the fused norm", p.units);
-  if ((p.xnorm || total / grid >= 2ull * p.units) && fits) {
+  if (fits) {
     p.resident = 1;
     p.upc = p.units;
   } else {
@@ -757,7 +752,7 @@ pai_status_t launch_t(pai_b200_ctx_t *ctx, GemvP p) {
   const size_t xq_slot = (size_t)p.upc * Un::XPU;
   p.xslot_bytes = (uint32_t)b200_align256(NT * xq_slot * 1024 + 2 * (size_t)p.batch * xq_slot * 16);
   const size_t smem = ring + (p.resident ? 1 : kXSlots) * (size_t)p.xslot_bytes;
-  if (smem > kSmemCap<NT>) return b200_fail(PAI_ERR_UNSUPPORTED, "gemv: %zu B of shared memory", smem);
+  if (smem > kSmemCap<NT, CONS>) return b200_fail(PAI_ERR_UNSUPPORTED, "gemv: %zu B of shared memory", smem);
   // Function attributes are set once per device (the largest size seen),
   // not per launch: they cost host time on the decode path.
   static size_t smem_set[64];
@@ -787,17 +782,17 @@ pai_status_t launch_t(pai_b200_ctx_t *ctx, GemvP p) {
   p.tile_cnt = cnt;
   p.grp_cnt = cnt + p.ntiles;
   p.err = b200_ctx_errflag(ctx);
-  b200_launch(ctx, kern, dim3(grid), dim3(kThreadsT<NT>), smem, p);
+  b200_launch(ctx, kern, dim3(grid), dim3(kThreadsT<NT, CONS>), smem, p);
   return b200_launched(ctx, 1, "k_gemv");
 }
 
 template <uint32_t T>
 pai_status_t launch_b(pai_b200_ctx_t *ctx, const GemvP &p) {
   switch ((p.batch + 1) / 2) {
-    case 1: return launch_t<T, 1>(ctx, p);
-    case 2: return launch_t<T, 2>(ctx, p);
-    case 3: return launch_t<T, 3>(ctx, p);
-    default: return launch_t<T, 4>(ctx, p);
+    case 1: return p.n >= kWideRows ? launch_t<T, 1, 16>(ctx, p) : launch_t<T, 1, 8>(ctx, p);
+    case 2: return launch_t<T, 2, 8>(ctx, p);
+    case 3: return launch_t<T, 3, 8>(ctx, p);
+    default: return launch_t<T, 4, 8>(ctx, p);
   }
 }
 
