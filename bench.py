@@ -57,7 +57,7 @@ def tensor_peak():
         return 1590.0, "fallback"
 
 
-def prefill_gemm(dev, iters=12, ms=(16, 128, 512, 2048)):
+def prefill_gemm(dev, iters=12, ms=(16, 128, 512, 2048), shards=1):
     """Config 2: the Q4_0 prefill GEMM Y[M,14336] = X[M,4096] . W^T on the
     tcgen05 tensor cores (X f32 -> bf16 tiles, W dequantised to bf16 in
     shared memory, fp32 accumulate in TMEM), for M in 16/128/512/2048.
@@ -68,9 +68,10 @@ def prefill_gemm(dev, iters=12, ms=(16, 128, 512, 2048)):
     from prosperoai_b200 import _native
     from prosperoai_b200.api import Buffer
     L = _native.load()
-    n, k, t = CFG_8B["n_ff"], CFG_8B["n_embd"], 2
+    # with shards > 1 this rank holds a column shard (N / shards output rows)
+    n, k, t = CFG_8B["n_ff"] // shards, CFG_8B["n_embd"], 2
     rb = L.pai_b200_block_bytes(t, k)
-    copies = 4
+    copies = 4 * shards
     tmp = dev.alloc(n * k * 4)
     blk = dev.alloc(n * rb)
     offs = dev.put(np.arange(n, dtype=np.uint64) * rb)
@@ -84,9 +85,11 @@ def prefill_gemm(dev, iters=12, ms=(16, 128, 512, 2048)):
     tmp.free()
     blk.free()
     peak, kind = tensor_peak()
-    out = {"workload": "Q4_0 GEMM N=14336 K=4096 (config 2), bf16 tiles, fp32 accumulate",
+    out = {"workload": f"Q4_0 GEMM N={n} K=4096 (config 2{', column shard' if shards > 1 else ''}), "
+                       "bf16 tiles, fp32 accumulate",
            "kernel": "k_gemm (tcgen05.mma kind::f16, TMEM accumulators) + k_gemm_xprep",
-           "peak_tflops": peak, "peak_kind": kind, "l2": "4 rotating weight copies (132 MB)",
+           "peak_tflops": peak, "peak_kind": kind,
+           "l2": f"{copies} rotating weight copies ({copies * n * rb / 1e6:.0f} MB)",
            "by_m": {}}
     e0, e1 = C.c_void_p(), C.c_void_p()
     L.pai_b200_event_create(dev.ctx, C.byref(e0))
@@ -237,6 +240,74 @@ def gemv_roofline(dev, hbm_peak, peak_kind, iters=40):
             "traffic": 66847744, "traffic_source": "ncu --set full, one launch"}
 
 
+def gemv_sweep(dev, hbm_peak, peak_kind, iters=30):
+    """Configs 1 and 3: the Q8_0 4096x4096 GEMV and the Q4_K GEMV shapes,
+    batch 1, x prepared once; each shape rotates over enough distinct
+    copies to exceed 2x the L2 (every launch streams from HBM). Timed with
+    CUDA events over back-to-back launches under programmatic dependent
+    launch (as in the decode step) and plainly."""
+    from prosperoai_b200 import _native
+    from prosperoai_b200.api import Buffer
+    L = _native.load()
+    shapes = [("config 1", 8, 4096, 4096)] + [("config 3", 12, n_, k_) for n_, k_ in
+                                             ((4096, 4096), (1024, 4096), (14336, 4096), (4096, 14336),
+                                              (128256, 4096))]
+    out = []
+    e0, e1 = C.c_void_p(), C.c_void_p()
+    L.pai_b200_event_create(dev.ctx, C.byref(e0))
+    L.pai_b200_event_create(dev.ctx, C.byref(e1))
+    for cfg_name, t, n, k in shapes:
+        rb = L.pai_b200_block_bytes(t, k)
+        copies = max(2, int(2 * 126e6 // (n * rb)) + 1)
+        tmp = dev.alloc(n * k * 4)
+        blk = dev.alloc(n * rb)
+        offs = dev.put(np.arange(n, dtype=np.uint64) * rb)
+        mats = []
+        for c in range(copies):
+            _native.check(L.pai_b200_synth_blocks(dev.ctx, t, n, k, SEED + 3000 + c, 0.02, tmp.ptr, blk.ptr),
+                          "synth")
+            pk = Buffer(dev, L.pai_b200_packed_bytes(t, n, k))
+            _native.check(L.pai_b200_pack(dev.ctx, t, n, k, blk.ptr, offs.ptr, pk.ptr), "pack")
+            mats.append(pk)
+        tmp.free()
+        blk.free()
+        offs.free()
+        x = dev.put(np.random.default_rng(2).standard_normal(k).astype(np.float32))
+        xq = C.c_void_p()
+        _native.check(L.pai_b200_alloc(dev.ctx, L.pai_b200_xq_bytes(1, k), C.byref(xq)), "alloc xq")
+        _native.check(L.pai_b200_prepare_x_f32(dev.ctx, 1, k, x.ptr, xq), "prepare_x")
+        y = dev.alloc(n * 4)
+        per = {}
+        for mode in (0, 1):
+            _native.check(L.pai_b200_set_pdl(dev.ctx, mode), "set_pdl")
+            for i in range(4):
+                _native.check(L.pai_b200_gemv_prepared_f32(dev.ctx, t, 1, n, k, mats[i % copies].ptr, xq,
+                                                           None, y.ptr), "gemv")
+            dev.sync()
+            L.pai_b200_event_record(dev.ctx, e0)
+            for i in range(iters):
+                L.pai_b200_gemv_prepared_f32(dev.ctx, t, 1, n, k, mats[i % copies].ptr, xq, None, y.ptr)
+            L.pai_b200_event_record(dev.ctx, e1)
+            ms = C.c_float()
+            _native.check(L.pai_b200_event_elapsed(e0, e1, C.byref(ms)), "elapsed")
+            dev.sync()
+            per[mode] = ms.value / iters
+        _native.check(L.pai_b200_set_pdl(dev.ctx, 0), "set_pdl")
+        alg = n * (k // (256 if t == 12 else 32)) * (144 if t == 12 else 34) + 4 * k + 4 * n
+        gbs = alg / (per[1] * 1e-3) / 1e9
+        out.append({"config": cfg_name, "type": "Q4_K" if t == 12 else "Q8_0", "n": n, "k": k,
+                    "algorithmic_bytes": int(alg), "us": round(per[1] * 1e3, 2), "gbs": round(gbs, 1),
+                    "frac": round(gbs / hbm_peak, 4), "plain_us": round(per[0] * 1e3, 2)})
+        for m_ in mats:
+            m_.free()
+        y.free()
+        x.free()
+        L.pai_b200_free(dev.ctx, xq)
+    return {"peak": hbm_peak, "peak_kind": peak_kind, "unit": "GB/s",
+            "launch_mode": "back-to-back, programmatic dependent launch; plain_us: plain launches",
+            "shapes": out}
+
+
 def cpu_baseline_port(dev, steps=3, prompt=24):
     """The CPU restatement (oracle/, bit-identical to the reference ops)
     on a bounded sample of the same decode: one 8B-shaped layer plus 1/32
@@ -368,9 +439,29 @@ def gpu_arm(args):
     step_gbs = step_bytes / (t_dev / K * 1e-3) / 1e9
     step_peak_gpus = world if tp else 1
     result = None
+    gemm = None
+    if tp and not args.no_roofline:
+        # config 2 column-sharded over the ranks: every rank times its shard,
+        # the job's time per M is the maximum over ranks
+        import torch
+        part = prefill_gemm(dev, shards=world)
+        ms_list = sorted(int(m) for m in part["by_m"])
+        t = torch.tensor([part["by_m"][str(m)]["us"] for m in ms_list], dtype=torch.float64)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        peak_tf = part["peak_tflops"]
+        gemm = {"workload": f"Q4_0 GEMM N=14336 K=4096 (config 2), column-sharded over {world} GPUs "
+                            f"({CFG_8B['n_ff'] // world} rows each), bf16 tiles, fp32 accumulate",
+                "kernel": part["kernel"], "peak_tflops": peak_tf * world, "peak_kind": part["peak_kind"],
+                "timing": "max over ranks of each rank's CUDA-event time", "by_m": {}}
+        for i, m in enumerate(ms_list):
+            tf = 2.0 * m * CFG_8B["n_ff"] * CFG_8B["n_embd"] / (float(t[i]) * 1e-6) / 1e12
+            gemm["by_m"][str(m)] = {"us": round(float(t[i]), 2), "tflops": round(tf, 1),
+                                    "frac": round(tf / (peak_tf * world), 4)}
     if rank == 0:
         roof = None if args.no_roofline else gemv_roofline(dev, hbm, kind)
-        gemm = None if args.no_roofline else prefill_gemm(dev)
+        if gemm is None and not args.no_roofline:
+            gemm = prefill_gemm(dev)
+        sweep = None if args.no_roofline else gemv_sweep(dev, hbm, kind)
         cpu = None if args.no_cpu_baseline else cpu_baseline_port(dev)
         jobs = 1 if tp else world  # sequences advanced per step: TP ranks share one job
         value = jobs * B * K / (t_dev * 1e-3)
@@ -393,6 +484,7 @@ def gpu_arm(args):
             "gpu_launches": int(launches),
             "roofline": roof,
             "prefill_gemm": gemm,
+            "gemv_configs": sweep,
             "step_roofline": {"bytes_per_step": int(step_bytes), "achieved": round(step_gbs, 1),
                               "peak": round(hbm * step_peak_gpus, 1), "unit": "GB/s",
                               "frac": round(step_gbs / (hbm * step_peak_gpus), 4), "peak_kind": kind,
