@@ -51,6 +51,7 @@ struct AttnParams {
   const float *qkv, *cos_t, *sin_t;
   __half *kw, *vw;
   uint32_t *cnt;
+  uint32_t *err;  // the context's error word (a bounded wait ran out)
 };
 
 __device__ __forceinline__ uint32_t npos_of(const AttnParams &p) {
@@ -119,8 +120,16 @@ __global__ void __launch_bounds__(128) k_attn_split(AttnParams p) {
   __shared__ float mls[G][2];
   __shared__ uint32_t ticket;
   __shared__ __align__(16) __half kvs[2][kSub][HD];  // staged K and V rows
+  __shared__ __align__(8) uint64_t kvbar;             // the bulk copies of a one-round chunk
+  __shared__ int kvfail;
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const uint32_t h0 = kvh * G;
+  const bool one = len <= kSub;
+  if (t == 0) {
+    mbar_init(&kvbar, 1);
+    fence_mbar_init();
+    kvfail = 0;
+  }
   if (STEP) {
     // rotate this CTA's G query heads at the position (pai_ref_rope_f32 on
     // the q part of the projection row, adapters/llama/llama.c:713-724)
@@ -149,6 +158,8 @@ __global__ void __launch_bounds__(128) k_attn_split(AttnParams p) {
   } else {
     for (int i = t; i < G * HD; i += 128) qs[i] = p.q[((size_t)bi * p.h + h0) * HD + i];
   }
+  // the appended k/v (generic stores) are read below by bulk copies (async proxy)
+  asm volatile("fence.proxy.async;" ::: "memory");
   __syncthreads();
 
   float qr[G][4];
@@ -171,10 +182,19 @@ __global__ void __launch_bounds__(128) k_attn_split(AttnParams p) {
       reinterpret_cast<uint4 *>(dst[r])[c] = *reinterpret_cast<const uint4 *>(src + (size_t)(s0 + r) * HD + c * 8);
     }
   };
-  const bool one = len <= kSub;
   if (one) {
-    stage(kb, kvs[0], 0, len);
-    stage(vb, kvs[1], 0, len);
+    // the chunk's K rows and V rows are each one contiguous run: two bulk copies
+    if (t == 0) {
+      mbar_expect_tx(&kvbar, 2 * len * HD * 2);
+      bulk_g2s(kvs[0], kb, len * HD * 2, &kvbar);
+      bulk_g2s(kvs[1], vb, len * HD * 2, &kvbar);
+    }
+    if (!mbar_wait(&kvbar, 0, 2000000000ull)) kvfail = 1;
+    __syncthreads();
+    if (kvfail) {
+      if (t == 0) atomicExch(p.err, 1u);
+      return;
+    }
   }
   // Scores: warp w takes positions w, w+4, ...; lane l holds dims 4l..4l+3.
   for (uint32_t s0 = 0; s0 < len; s0 += kSub) {
@@ -184,22 +204,41 @@ __global__ void __launch_bounds__(128) k_attn_split(AttnParams p) {
       stage(kb, kvs[0], s0, cnt);
     }
     __syncthreads();
-    for (uint32_t i = warp; i < cnt; i += 4) {
-      uint2 raw = *reinterpret_cast<const uint2 *>(&kvs[0][i][4 * lane]);
-      float2 k01 = __half22float2(*reinterpret_cast<__half2 *>(&raw.x));
-      float2 k23 = __half22float2(*reinterpret_cast<__half2 *>(&raw.y));
-      float part[G];
+    // positions i0, i0 + 4, i0 + 8, i0 + 12 per warp iteration: four
+    // independent shuffle reductions per head in flight
+    for (uint32_t i0 = warp; i0 < cnt; i0 += 16) {
+      float part[4][G];
 #pragma unroll
-      for (int g = 0; g < G; g++) {
-        float s = qr[g][0] * k01.x;
-        s = fmaf(qr[g][1], k01.y, s);
-        s = fmaf(qr[g][2], k23.x, s);
-        s = fmaf(qr[g][3], k23.y, s);
-        part[g] = warp_sum(s);
+      for (int u = 0; u < 4; u++) {
+        const uint32_t i = i0 + 4 * u;
+        float2 k01 = make_float2(0.f, 0.f), k23 = k01;
+        if (i < cnt) {
+          uint2 raw = *reinterpret_cast<const uint2 *>(&kvs[0][i][4 * lane]);
+          k01 = __half22float2(*reinterpret_cast<__half2 *>(&raw.x));
+          k23 = __half22float2(*reinterpret_cast<__half2 *>(&raw.y));
+        }
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+          float s = qr[g][0] * k01.x;
+          s = fmaf(qr[g][1], k01.y, s);
+          s = fmaf(qr[g][2], k23.x, s);
+          s = fmaf(qr[g][3], k23.y, s);
+          part[u][g] = s;
+        }
       }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int u = 0; u < 4; u++)
+#pragma unroll
+          for (int g = 0; g < G; g++) part[u][g] += __shfl_xor_sync(0xffffffffu, part[u][g], o);
       if (lane == 0) {
 #pragma unroll
-        for (int g = 0; g < G; g++) sc[g * chunk + s0 + i] = part[g] * p.inv_scale;
+        for (int u = 0; u < 4; u++)
+          if (i0 + 4 * u < cnt) {
+#pragma unroll
+            for (int g = 0; g < G; g++) sc[g * chunk + s0 + i0 + 4 * u] = part[u][g] * p.inv_scale;
+          }
       }
     }
   }
@@ -437,6 +476,7 @@ pai_status_t attn_setup(pai_b200_ctx_t *ctx, uint32_t batch, uint32_t h, uint32_
   p.seq_stride = seq_stride;
   p.inv_scale = 1.0f / sqrtf((float)hd);
   if (xq_out) p.xo = *xq_out;
+  p.err = b200_ctx_errflag(ctx);
   const uint64_t slots = (uint64_t)batch * h * nsplit;
   float *scratch;
   uint32_t *counters;
@@ -505,6 +545,8 @@ extern "C" pai_status_t pai_b200_attn_decode_f16kv(pai_b200_ctx_t *ctx, uint64_t
                                                    uint64_t npos, uint64_t cap, const float *q,
                                                    const uint16_t *kcache, const uint16_t *vcache, float *out) {
   if (!ctx || !q || !kcache || !vcache || !out) return b200_fail(PAI_ERR_INVALID_ARG, "attn_decode: NULL");
+  if (((uintptr_t)kcache | (uintptr_t)vcache) & 15)
+    return b200_fail(PAI_ERR_INVALID_ARG, "attn_decode: K/V caches must be 16-byte aligned");
   if (h == 0 || hk == 0 || npos == 0 || npos > cap || h > 4096 || cap > 0x7FFFFFFFull)
     return b200_fail(PAI_ERR_INVALID_ARG, "attn_decode: shape");
   return b200_launch_attn_decode(ctx, 1, (uint32_t)h, (uint32_t)hk, (uint32_t)hd, nullptr, npos, npos, cap, 0,
@@ -578,6 +620,8 @@ extern "C" pai_status_t pai_b200_attn_decode_f16kv_noalloc(pai_b200_ctx_t *ctx, 
                                                            const float *q, const uint16_t *kcache,
                                                            const uint16_t *vcache, float *out) {
   if (!ctx || !q || !kcache || !vcache || !out) return b200_fail(PAI_ERR_INVALID_ARG, "attn_decode_noalloc: NULL");
+  if (((uintptr_t)kcache | (uintptr_t)vcache) & 15)
+    return b200_fail(PAI_ERR_INVALID_ARG, "attn_decode_noalloc: K/V caches must be 16-byte aligned");
   if (h == 0 || hk == 0 || npos == 0 || npos > cap || h > 4096 || cap > 0x7FFFFFFFull)
     return b200_fail(PAI_ERR_INVALID_ARG, "attn_decode_noalloc: shape");
   if (hd != HD) return b200_fail(PAI_ERR_UNSUPPORTED, "attn_decode_noalloc: head_dim %llu (this kernel takes 128)",
@@ -619,6 +663,7 @@ extern "C" pai_status_t pai_b200_attn_decode_f16kv_noalloc(pai_b200_ctx_t *ctx, 
   p.inv_scale = 1.0f / sqrtf((float)hd);
   p.opart = scratch;
   p.ml = scratch + h * nsplit * HD;
+  p.err = b200_ctx_errflag(ctx);
   switch (G) {
     case 1: st = launch_split<1>(ctx, p, 1); break;
     case 2: st = launch_split<2>(ctx, p, 1); break;
