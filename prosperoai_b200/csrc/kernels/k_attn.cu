@@ -29,7 +29,7 @@
 namespace {
 
 constexpr int HD = 128;
-constexpr int kSub = 64;           // K/V positions staged in shared memory per round (the step chunk)
+constexpr uint32_t kMaxStage = 256;  // most K/V positions staged in shared memory per round
 constexpr int kMaxStepSplit = 64;  // most position chunks per kv head in the decode step
 
 struct AttnParams {
@@ -51,7 +51,8 @@ struct AttnParams {
   const float *qkv, *cos_t, *sin_t;
   __half *kw, *vw;
   uint32_t *cnt;
-  uint32_t *err;  // the context's error word (a bounded wait ran out)
+  uint32_t *err;   // the context's error word (a bounded wait ran out)
+  uint32_t stage;  // positions of K (and of V) staged in shared memory per round
 };
 
 __device__ __forceinline__ uint32_t npos_of(const AttnParams &p) {
@@ -116,15 +117,18 @@ __global__ void __launch_bounds__(128) k_attn_split(AttnParams p) {
   extern __shared__ __align__(16) float sm[];
   float *qs = sm;               // [G][HD]
   float *sc = sm + G * HD;      // [G][chunk]
+  // staged K and V rows, p.stage positions each (16-byte aligned: the
+  // float parts above are multiples of 4 floats)
+  __half (*kst)[HD] = reinterpret_cast<__half (*)[HD]>(sc + (size_t)G * p.chunk);
+  __half (*vst)[HD] = kst + p.stage;
   __shared__ float red[2][G][HD];
   __shared__ float mls[G][2];
   __shared__ uint32_t ticket;
-  __shared__ __align__(16) __half kvs[2][kSub][HD];  // staged K and V rows
-  __shared__ __align__(8) uint64_t kvbar;             // the bulk copies of a one-round chunk
+  __shared__ __align__(8) uint64_t kvbar;  // completion of the K/V bulk copies
   __shared__ int kvfail;
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const uint32_t h0 = kvh * G;
-  const bool one = len <= kSub;
+  const bool one = len <= p.stage;
   if (t == 0) {
     mbar_init(&kvbar, 1);
     fence_mbar_init();
@@ -172,24 +176,33 @@ __global__ void __launch_bounds__(128) k_attn_split(AttnParams p) {
   const __half *kb = p.kc + kvoff;
   const __half *vb = p.vc + kvoff;
 
-  // K and V rows are staged in shared memory kSub positions at a time with
-  // all loads of a round in flight (a chunk of <= kSub positions, the usual
-  // case, needs one round for both); the loops below read shared memory
-  // only, so no global load waits on the previous position's reductions.
-  auto stage = [&](const __half *src, __half (*dst)[HD], uint32_t s0, uint32_t cnt) {
-    for (uint32_t i = t; i < cnt * (HD / 8); i += 128) {
-      const uint32_t r = i / (HD / 8), c = i % (HD / 8);
-      reinterpret_cast<uint4 *>(dst[r])[c] = *reinterpret_cast<const uint4 *>(src + (size_t)(s0 + r) * HD + c * 8);
+  // K and V rows are staged in shared memory by bulk copies (a chunk's rows
+  // of one kv head are contiguous): the whole chunk at once when it fits in
+  // p.stage positions, else p.stage positions per round. The loops below
+  // read shared memory only, so no global load waits on the previous
+  // position's reductions. Every wait is bounded.
+  uint32_t kv_phase = 0;
+  auto stage_rows = [&](__half (*dst)[HD], const __half *src, uint32_t cnt) -> bool {
+    __syncthreads();  // the previous round's rows are no longer read
+    if (t == 0) {
+      mbar_expect_tx(&kvbar, cnt * HD * 2);
+      bulk_g2s(dst, src, cnt * HD * 2, &kvbar);
     }
+    if (!mbar_wait(&kvbar, kv_phase & 1u, 2000000000ull)) kvfail = 1;
+    kv_phase++;
+    __syncthreads();
+    if (kvfail && t == 0) atomicExch(p.err, 1u);
+    return !kvfail;
   };
   if (one) {
-    // the chunk's K rows and V rows are each one contiguous run: two bulk copies
+    // K and V of the whole chunk: two bulk copies on one barrier phase
     if (t == 0) {
       mbar_expect_tx(&kvbar, 2 * len * HD * 2);
-      bulk_g2s(kvs[0], kb, len * HD * 2, &kvbar);
-      bulk_g2s(kvs[1], vb, len * HD * 2, &kvbar);
+      bulk_g2s(kst, kb, len * HD * 2, &kvbar);
+      bulk_g2s(vst, vb, len * HD * 2, &kvbar);
     }
     if (!mbar_wait(&kvbar, 0, 2000000000ull)) kvfail = 1;
+    kv_phase = 1;
     __syncthreads();
     if (kvfail) {
       if (t == 0) atomicExch(p.err, 1u);
@@ -197,11 +210,10 @@ __global__ void __launch_bounds__(128) k_attn_split(AttnParams p) {
     }
   }
   // Scores: warp w takes positions w, w+4, ...; lane l holds dims 4l..4l+3.
-  for (uint32_t s0 = 0; s0 < len; s0 += kSub) {
-    const uint32_t cnt = min((uint32_t)kSub, len - s0);
+  for (uint32_t s0 = 0; s0 < len; s0 += p.stage) {
+    const uint32_t cnt = min(p.stage, len - s0);
     if (!one) {
-      __syncthreads();
-      stage(kb, kvs[0], s0, cnt);
+      if (!stage_rows(kst, kb + (size_t)s0 * HD, cnt)) return;
     }
     __syncthreads();
     // positions i0, i0 + 4, i0 + 8, i0 + 12 per warp iteration: four
@@ -213,7 +225,7 @@ __global__ void __launch_bounds__(128) k_attn_split(AttnParams p) {
         const uint32_t i = i0 + 4 * u;
         float2 k01 = make_float2(0.f, 0.f), k23 = k01;
         if (i < cnt) {
-          uint2 raw = *reinterpret_cast<const uint2 *>(&kvs[0][i][4 * lane]);
+          uint2 raw = *reinterpret_cast<const uint2 *>(&kst[i][4 * lane]);
           k01 = __half22float2(*reinterpret_cast<__half2 *>(&raw.x));
           k23 = __half22float2(*reinterpret_cast<__half2 *>(&raw.y));
         }
@@ -269,14 +281,13 @@ __global__ void __launch_bounds__(128) k_attn_split(AttnParams p) {
   float acc[G][2];
 #pragma unroll
   for (int g = 0; g < G; g++) acc[g][0] = acc[g][1] = 0.f;
-  for (uint32_t s0 = 0; s0 < len; s0 += kSub) {
-    const uint32_t cnt = min((uint32_t)kSub, len - s0);
+  for (uint32_t s0 = 0; s0 < len; s0 += p.stage) {
+    const uint32_t cnt = min(p.stage, len - s0);
     if (!one) {
-      stage(vb, kvs[1], s0, cnt);
-      __syncthreads();
+      if (!stage_rows(vst, vb + (size_t)s0 * HD, cnt)) return;
     }
     for (uint32_t i = sub; i < cnt; i += 2) {
-      float2 v = __half22float2(*reinterpret_cast<const __half2 *>(&kvs[1][i][2 * dp]));
+      float2 v = __half22float2(*reinterpret_cast<const __half2 *>(&vst[i][2 * dp]));
 #pragma unroll
       for (int g = 0; g < G; g++) {
         float e = sc[g * chunk + s0 + i];
@@ -423,11 +434,19 @@ __global__ void __launch_bounds__(128) k_attention_f32(uint32_t h, uint32_t hk, 
 }
 
 template <int G, bool STEP = false>
-pai_status_t launch_split(pai_b200_ctx_t *ctx, const AttnParams &p, uint32_t batch) {
-  const size_t smem = (size_t)(G * HD + G * p.chunk) * sizeof(float);
-  const size_t stat = (size_t)(2 * G * HD + 2 * G + (STEP ? 2 * G * kMaxStepSplit + G : 0)) * sizeof(float) +
-                      2 * kSub * HD * sizeof(__half) + 64;
-  if (smem + stat > 200 * 1024) return b200_fail(PAI_ERR_UNSUPPORTED, "attn_decode: chunk of %u positions", p.chunk);
+pai_status_t launch_split(pai_b200_ctx_t *ctx, const AttnParams &p0, uint32_t batch) {
+  AttnParams p = p0;
+  // dynamic shared memory: q [G][HD] and scores [G][chunk] in fp32, then the
+  // staged K and V rows; the whole chunk is staged at once when it fits
+  // (up to kMaxStage positions), else kMaxStage-or-fewer positions per round
+  const size_t base = (size_t)(G * HD + G * p.chunk) * sizeof(float);
+  const size_t stat = (size_t)(2 * G * HD + 2 * G + (STEP ? 2 * G * kMaxStepSplit + G : 0)) * sizeof(float) + 64;
+  const size_t cap = 200 * 1024, row2 = 2 * HD * sizeof(__half);  // K and V bytes per position
+  if (base + stat + 32 * row2 > cap) return b200_fail(PAI_ERR_UNSUPPORTED, "attn_decode: chunk of %u positions", p.chunk);
+  uint32_t stage = std::min<uint32_t>(p.chunk, kMaxStage);
+  while (stage > 32 && base + stat + stage * row2 > cap) stage -= 32;
+  p.stage = stage;
+  const size_t smem = base + stage * row2;
   if (smem + stat > 48 * 1024) {
     pai_status_t st = b200_cuda(
         cudaFuncSetAttribute(k_attn_split<G, STEP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
