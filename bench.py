@@ -351,6 +351,35 @@ def cpu_baseline_port(dev, steps=3, prompt=24):
                        f"full-model tok/s = 1/(32 x {dt * 1e3:.1f} ms)")}
 
 
+def decode_variant(dev, model, batch, prompt, steps=20, warmup=3):
+    """Decode tok/s of one more session of the same model: `batch`
+    independent sequences after a `prompt`-token seeded prompt, CUDA-graph
+    steps timed with CUDA events (as the headline line)."""
+    from prosperoai_b200 import _native
+    from prosperoai_b200.api import Session
+    L = _native.load()
+    sess = Session(model, batch, prompt + warmup + steps + 8)
+    ids = np.random.default_rng(SEED + batch).integers(0, CFG_8B["vocab"], (batch, prompt)).astype(np.int32)
+    for p in range(prompt):
+        sess.set_tokens(ids[:, p])
+        sess.run(1)
+    sess.run(warmup)
+    dev.sync()
+    e0, e1 = C.c_void_p(), C.c_void_p()
+    L.pai_b200_event_create(dev.ctx, C.byref(e0))
+    L.pai_b200_event_create(dev.ctx, C.byref(e1))
+    pos0 = sess.pos
+    L.pai_b200_event_record(dev.ctx, e0)
+    sess.run(steps)
+    L.pai_b200_event_record(dev.ctx, e1)
+    ms = C.c_float()
+    _native.check(L.pai_b200_event_elapsed(e0, e1, C.byref(ms)), "elapsed")
+    sess.close()
+    return {"batch": batch, "prompt": prompt, "positions_timed": [pos0, pos0 + steps - 1],
+            "ms_per_step": round(ms.value / steps, 4), "value": round(batch * steps / (ms.value * 1e-3), 3),
+            "unit": UNIT}
+
+
 def gpu_arm(args):
     from prosperoai_b200 import _native
     from prosperoai_b200.api import Device, Model, Session, TPComm
@@ -463,6 +492,10 @@ def gpu_arm(args):
             gemm = prefill_gemm(dev)
         sweep = None if args.no_roofline else gemv_sweep(dev, hbm, kind)
         cpu = None if args.no_cpu_baseline else cpu_baseline_port(dev)
+        variants = None
+        if world == 1 and not args.no_roofline:
+            # configs 4-5 also name 8 independent sequences and a 4096-position cache
+            variants = [decode_variant(dev, model, 8, P), decode_variant(dev, model, 1, 4096)]
         jobs = 1 if tp else world  # sequences advanced per step: TP ranks share one job
         value = jobs * B * K / (t_dev * 1e-3)
         result = {
@@ -484,6 +517,7 @@ def gpu_arm(args):
             "gpu_launches": int(launches),
             "roofline": roof,
             "prefill_gemm": gemm,
+            "decode_variants": variants,
             "gemv_configs": sweep,
             "step_roofline": {"bytes_per_step": int(step_bytes), "achieved": round(step_gbs, 1),
                               "peak": round(hbm * step_peak_gpus, 1), "unit": "GB/s",
