@@ -308,6 +308,66 @@ def gemv_sweep(dev, hbm_peak, peak_kind, iters=30):
             "shapes": out}
 
 
+def v0_sweep(dev, hbm_peak, peak_kind, iters=40):
+    """The v0 grouped-scale GEMMs at the config-1 shape (4096x4096, one
+    activation row): the registered w8/w4 ops (scales per (k-group,
+    column)) and .pai blobs (scales per 32 flat elements), each rotating
+    over enough distinct weight copies to exceed 2x the L2. Plain launches,
+    CUDA events around the timed loop."""
+    from prosperoai_b200 import _native
+    L = _native.load()
+    n = k = 4096
+    g = 32
+    rng = np.random.default_rng(SEED + 77)
+    a = dev.put(rng.standard_normal(k).astype(np.float32))
+    c = dev.alloc(n * 4)
+    e0, e1 = C.c_void_p(), C.c_void_p()
+    L.pai_b200_event_create(dev.ctx, C.byref(e0))
+    L.pai_b200_event_create(dev.ctx, C.byref(e1))
+    out = []
+    for name, bits, form in (("gemm_w8_f32", 8, "op"), ("gemm_w4_f32", 4, "op"),
+                             ("gemm_v0_f32 q8", 8, "pai"), ("gemm_v0_f32 q4", 4, "pai")):
+        vbytes = n * k if bits == 8 else n * k // 2
+        sbytes = 4 * (n * k // g)
+        copies = int(2 * 126e6 // (vbytes + sbytes)) + 1
+        bufs = []
+        for _ in range(copies):
+            v = rng.integers(-128, 128, vbytes, dtype=np.int8).view(np.uint8)
+            sc = (rng.uniform(0.5, 1.5, n * k // g) / 127).astype(np.float32).view(np.uint8)
+            bufs.append((dev.put(v), dev.put(sc)) if form == "op" else (dev.put(np.concatenate([v, sc])),))
+
+        def call(i):
+            b = bufs[i % copies]
+            if form == "op":
+                fn = L.pai_b200_gemm_w8_f32 if bits == 8 else L.pai_b200_gemm_w4_f32
+                return fn(dev.ctx, 1, n, k, a.ptr, b[0].ptr, b[1].ptr, g, c.ptr)
+            return L.pai_b200_gemm_v0_f32(dev.ctx, bits, g, 1, n, k, a.ptr, b[0].ptr, c.ptr)
+
+        for i in range(4):
+            _native.check(call(i), name)
+        dev.sync()
+        L.pai_b200_event_record(dev.ctx, e0)
+        for i in range(iters):
+            call(i)
+        L.pai_b200_event_record(dev.ctx, e1)
+        ms = C.c_float()
+        _native.check(L.pai_b200_event_elapsed(e0, e1, C.byref(ms)), "elapsed")
+        dev.sync()
+        us = ms.value / iters * 1e3
+        alg = vbytes + sbytes + 4 * k + 4 * n
+        gbs = alg / (us * 1e-6) / 1e9
+        out.append({"op": name, "scales": "per (32-row group, column)" if form == "op"
+                    else "per 32 flat elements (.pai blob)", "n": n, "k": k, "rows": 1,
+                    "algorithmic_bytes": int(alg), "us": round(us, 2), "gbs": round(gbs, 1),
+                    "frac": round(gbs / hbm_peak, 4), "copies": copies})
+        for b in bufs:
+            for x in b:
+                x.free()
+    a.free()
+    c.free()
+    return {"peak": hbm_peak, "peak_kind": peak_kind, "unit": "GB/s", "shapes": out}
+
+
 def cpu_baseline_port(dev, steps=3, prompt=24):
     """The CPU restatement (oracle/, bit-identical to the reference ops)
     on a bounded sample of the same decode: one 8B-shaped layer plus 1/32
@@ -491,6 +551,7 @@ def gpu_arm(args):
         if gemm is None and not args.no_roofline:
             gemm = prefill_gemm(dev)
         sweep = None if args.no_roofline else gemv_sweep(dev, hbm, kind)
+        v0 = None if args.no_roofline else v0_sweep(dev, hbm, kind)
         cpu = None if args.no_cpu_baseline else cpu_baseline_port(dev)
         variants = None
         if world == 1 and not args.no_roofline:
@@ -519,6 +580,7 @@ def gpu_arm(args):
             "prefill_gemm": gemm,
             "decode_variants": variants,
             "gemv_configs": sweep,
+            "v0_gemm": v0,
             "step_roofline": {"bytes_per_step": int(step_bytes), "achieved": round(step_gbs, 1),
                               "peak": round(hbm * step_peak_gpus, 1), "unit": "GB/s",
                               "frac": round(step_gbs / (hbm * step_peak_gpus), 4), "peak_kind": kind,
@@ -675,6 +737,8 @@ def main():
                     help="time only the config-2 prefill GEMM and print its line")
     ap.add_argument("--gemm-m", type=int, action="append",
                     help="with --gemm-only: token counts to time (repeatable; default 16 128 512 2048)")
+    ap.add_argument("--v0-only", action="store_true",
+                    help="time only the v0 grouped-scale GEMMs (w8/w4 ops and .pai blobs)")
     ap.add_argument("--nvtx", action="store_true",
                     help="wrap the timed decode steps in the NVTX range decode_timed")
     args = ap.parse_args()
@@ -685,6 +749,13 @@ def main():
         from prosperoai_b200.api import Device
         dev = Device(local)
         print(json.dumps(prefill_gemm(dev, ms=tuple(args.gemm_m or (16, 128, 512, 2048)))), flush=True)
+        dev.close()
+        return
+    if args.v0_only:
+        from prosperoai_b200.api import Device
+        dev = Device(local)
+        hbm, kind = peaks()
+        print(json.dumps(v0_sweep(dev, hbm, kind)), flush=True)
         dev.close()
         return
     if args.kernel_only:

@@ -85,7 +85,10 @@ enum {
   PAI_KERNEL_B200_SILU_MUL = 22,
   PAI_KERNEL_B200_VECADD = 23,
   PAI_KERNEL_B200_DEQUANT = 24,
-  PAI_KERNEL_B200_ARGMAX = 25
+  PAI_KERNEL_B200_ARGMAX = 25,
+  PAI_KERNEL_B200_GEMM_W8 = 26,
+  PAI_KERNEL_B200_GEMM_W4 = 27,
+  PAI_KERNEL_B200_GEMM_V0 = 28
 };
 
 /* ggml block types, numbered as adapters/llama/gguf.h:36-51. */
@@ -241,6 +244,36 @@ pai_status_t pai_b200_gemv_rmsnorm_f32(pai_b200_ctx_t *ctx, uint32_t type, uint6
  * relative (the benchmark's bar is max-abs-rel 2e-2). */
 pai_status_t pai_b200_gemm_q4_0_f32(pai_b200_ctx_t *ctx, uint64_t m, uint64_t n, uint64_t k,
                                     const float *x, const void *w, float *y);
+
+/* v0 grouped-scale integer weights (models/quantize.h), read in place.
+ * The weight is a [k][n] GEMM B operand (n contiguous), c[m][n] = a[m][k] x W.
+ *
+ * pai_b200_gemm_w8_f32 / pai_b200_gemm_w4_f32: the registered quantized
+ * GEMMs pai_ref_gemm_w8_f32 / pai_ref_gemm_w4_f32 (cpu/reference/ref_ops.c:
+ * 447-499, ref_ops.h:164-180) with device pointers and the same arguments:
+ * W(t, j) = q(t, j) * b_scales[(t / g) * n + j], q the int8 w_q[t*n + j] or
+ * the signed nibble at flat index t*n + j of w_q4 (even index: low nibble),
+ * g = group_size (0 or > k: k). Same status codes (PAI_ERR_INVALID_ARG for
+ * a zero dimension or a NULL pointer). */
+pai_status_t pai_b200_gemm_w8_f32(pai_b200_ctx_t *ctx, uint64_t m, uint64_t n, uint64_t k,
+                                  const float *a, const int8_t *w_q, const float *b_scales,
+                                  uint64_t group_size, float *c);
+pai_status_t pai_b200_gemm_w4_f32(pai_b200_ctx_t *ctx, uint64_t m, uint64_t n, uint64_t k,
+                                  const float *a, const int8_t *w_q4, const float *b_scales,
+                                  uint64_t group_size, float *c);
+/* A quantized tensor of a v0 .pai container as stored: blob = [values]
+ * [f32 scales] (pai_quant_weights_bytes bytes, models/quantize.c:53-72;
+ * manifest size_bytes, models/container.c:176-182), one scale per
+ * group_size consecutive flat elements (0: the whole tensor). c is what the
+ * reference computes with pai_dequantize_f32 (models/model.c:259-290) then
+ * pai_ref_gemm_f32 (ref_ops.c:428-444), to fp32 accumulation noise, without
+ * dequantising. bit_width other than 8 or 4: PAI_ERR_UNSUPPORTED
+ * (models/model.c:264-267). */
+pai_status_t pai_b200_gemm_v0_f32(pai_b200_ctx_t *ctx, uint32_t bit_width, uint32_t group_size,
+                                  uint64_t m, uint64_t n, uint64_t k, const float *a,
+                                  const void *blob, float *c);
+/* Bytes of such a blob for numel elements; 0 for an unsupported width. */
+uint64_t pai_b200_v0_blob_bytes(uint32_t bit_width, uint32_t group_size, uint64_t numel);
 
 /* c = a * gamma * (1/sqrtf(mean(a^2) + eps)) per row of n
  * (pai_ref_rmsnorm_gamma_f32, ref_ops.c:196-216; eps 0 selects 1e-5). */

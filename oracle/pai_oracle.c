@@ -308,6 +308,107 @@ void po_gemv_f32(uint64_t m, uint64_t k, const float *a, const float *x,
   }
 }
 
+void po_gemm_f32(uint64_t m, uint64_t n, uint64_t k, const float *a,
+                 const float *b, float *c) {
+  for (uint64_t i = 0; i < m; i++) {
+    for (uint64_t j = 0; j < n; j++) {
+      float acc = 0.0f;
+      for (uint64_t l = 0; l < k; l++) {
+        acc += a[i * k + l] * b[l * n + j];
+      }
+      c[i * n + j] = acc;
+    }
+  }
+}
+
+/* ---- v0 grouped-scale formats ----------------------------------------------- */
+
+/* Signed value of element i of a v0 blob: int8, or the nibble of byte i/2
+ * selected by the parity of i, sign-extended (models/quantize.c:165-172). */
+static int32_t v0_value(uint32_t bits, const int8_t *q, uint64_t i) {
+  if (bits == 8) {
+    return q[i];
+  }
+  const uint8_t byte = (uint8_t)q[i / 2];
+  const int32_t nib = (i & 1) ? (byte >> 4) & 0x0F : byte & 0x0F;
+  return (nib & 0x08) ? nib - 16 : nib;
+}
+
+uint64_t po_quant_v0(uint32_t bits, uint64_t gs, const float *src, uint64_t n,
+                     int8_t *q, float *scales) {
+  if ((bits != 8 && bits != 4) || n == 0) {
+    return 0;
+  }
+  if (gs == 0) {
+    gs = n;
+  }
+  const int32_t qmax = bits == 8 ? 127 : 7;
+  memset(q, 0, bits == 8 ? n : (n + 1) / 2);
+  uint64_t g = 0;
+  for (uint64_t t = 0; t < n; t += gs, g++) {
+    const uint64_t t1 = t + gs < n ? t + gs : n;
+    float amax = 0.0f;
+    for (uint64_t i = t; i < t1; i++) {
+      const float v = fabsf(src[i]);
+      if (v > amax) {
+        amax = v;
+      }
+    }
+    const float scale = amax > 0.0f ? amax / (float)qmax : 0.0f;
+    scales[g] = scale;
+    for (uint64_t i = t; i < t1; i++) {
+      int32_t v = 0;
+      if (scale > 0.0f) {
+        v = (int32_t)lrintf(src[i] / scale);
+        v = v > qmax ? qmax : (v < -qmax ? -qmax : v);
+      }
+      if (bits == 8) {
+        q[i] = (int8_t)v;
+      } else {
+        uint8_t *b = (uint8_t *)q + i / 2;
+        *b = (i & 1) ? (uint8_t)((*b & 0x0F) | ((v & 0x0F) << 4)) : (uint8_t)((*b & 0xF0) | (v & 0x0F));
+      }
+    }
+  }
+  return g;
+}
+
+int po_dequant_v0(uint32_t bits, uint64_t gs, const int8_t *q,
+                  const float *scales, uint64_t n, float *out) {
+  if (bits != 8 && bits != 4) {
+    return -1;
+  }
+  if (gs == 0) {
+    gs = n;
+  }
+  for (uint64_t i = 0; i < n; i++) {
+    out[i] = scales[i / gs] * (float)v0_value(bits, q, i);
+  }
+  return 0;
+}
+
+int po_gemm_wq_f32(uint32_t bits, uint64_t m, uint64_t n, uint64_t k,
+                   const float *a, const int8_t *w_q, const float *s,
+                   uint64_t g, float *c) {
+  if ((bits != 8 && bits != 4) || m == 0 || n == 0 || k == 0) {
+    return -1;
+  }
+  if (g == 0 || g > k) {
+    g = k;
+  }
+  for (uint64_t i = 0; i < m; i++) {
+    for (uint64_t j = 0; j < n; j++) {
+      float acc = 0.0f;
+      for (uint64_t t = 0; t < k; t++) {
+        const float prod = a[i * k + t] * (float)v0_value(bits, w_q, t * n + j);
+        acc += prod * s[(t / g) * n + j];
+      }
+      c[i * n + j] = acc;
+    }
+  }
+  return 0;
+}
+
 typedef struct {
   uint32_t type;
   uint64_t r0, r1, k, row_bytes;

@@ -73,6 +73,31 @@ void po_gemv_f32(uint64_t m, uint64_t k, const float *a, const float *x,
  * per-row operation order does not change. */
 int po_gemv_q(uint32_t type, uint64_t n, uint64_t k, const uint8_t *w,
               const float *x, float *y, int threads);
+/* ref_ops.c:428-444: c[m,n] = sum over l ascending of a[m,l] * b[l,n]. */
+void po_gemm_f32(uint64_t m, uint64_t n, uint64_t k, const float *a,
+                 const float *b, float *c);
+
+/* v0 grouped-scale formats (models/quantize.c, cpu/reference/ref_ops.c) -- */
+
+/* models/quantize.c:74-143 (pai_quantize_f32): signed symmetric, one f32
+ * scale max|w|/qmax per `gs` consecutive elements (gs 0: all n), q =
+ * lrintf(w/scale) clamped to [-qmax, qmax], qmax 127 (bits 8) or 7 (bits
+ * 4, two per byte: even index low nibble). Returns the number of groups,
+ * or 0 for an unsupported width. q must hold value_bytes(n) bytes. */
+uint64_t po_quant_v0(uint32_t bits, uint64_t gs, const float *src, uint64_t n,
+                     int8_t *q, float *scales);
+/* models/quantize.c:146-181 (pai_dequantize_f32): out[i] =
+ * scales[i / gs] * (float)q(i), nibbles sign-extended. */
+int po_dequant_v0(uint32_t bits, uint64_t gs, const int8_t *q,
+                  const float *scales, uint64_t n, float *out);
+/* ref_ops.c:447-499 (pai_ref_gemm_w8_f32 / pai_ref_gemm_w4_f32):
+ * c[i,j] = sum over t ascending of (a[i,t] * (float)q(t,j)) * s[(t/g)*n + j],
+ * q(t,j) the int8 w_q[t*n+j] (bits 8) or the signed nibble at flat index
+ * t*n+j (bits 4); g 0 or > k selects k. */
+int po_gemm_wq_f32(uint32_t bits, uint64_t m, uint64_t n, uint64_t k,
+                   const float *a, const int8_t *w_q, const float *s,
+                   uint64_t g, float *c);
+
 /* ref_ops.c:196-216 (eps == 0 selects 1e-5) */
 void po_rmsnorm_gamma_f32(const float *a, float *c, uint64_t n,
                           const float *gamma, float eps);

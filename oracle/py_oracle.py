@@ -52,6 +52,11 @@ def lib():
         _sig(L.po_quantize, C.c_int, C.c_uint32, f32p, u8p, U64)
         _sig(L.po_gemv_f32, None, U64, U64, f32p, f32p, f32p)
         _sig(L.po_gemv_q, C.c_int, C.c_uint32, U64, U64, u8p, f32p, f32p, C.c_int)
+        _sig(L.po_gemm_f32, None, U64, U64, U64, f32p, f32p, f32p)
+        _sig(L.po_quant_v0, U64, C.c_uint32, U64, f32p, U64, i8p, f32p)
+        _sig(L.po_dequant_v0, C.c_int, C.c_uint32, U64, i8p, f32p, U64, f32p)
+        _sig(L.po_gemm_wq_f32, C.c_int, C.c_uint32, U64, U64, U64, f32p, i8p, f32p, U64,
+             f32p)
         _sig(L.po_rmsnorm_gamma_f32, None, f32p, f32p, U64, f32p, C.c_float)
         _sig(L.po_silu_f32, None, f32p, f32p, U64)
         _sig(L.po_vecmul_f32, None, f32p, f32p, f32p, U64)
@@ -71,6 +76,11 @@ def lib():
         _sig(L.po_session_hidden, C.POINTER(C.c_float), C.c_void_p)
         _lib = L
     return _lib
+
+
+class QuantScheme(C.Structure):
+    """pai_quant_scheme_t (models/quantize.h:35-39)."""
+    _fields_ = [("bit_width", C.c_uint8), ("is_signed", C.c_uint8), ("group_size", C.c_uint16)]
 
 
 def ref():
@@ -99,6 +109,9 @@ def ref():
         _sig(R.pai_ref_gemm_w4_f32, C.c_int32, U64, U64, U64, f32p, i8p, f32p, U64,
              f32p)
         _sig(R.pai_opt_gemv_f32, C.c_int32, U64, U64, f32p, f32p, f32p)
+        _sig(R.pai_quantize_f32, C.c_int32, f32p, U64, C.POINTER(QuantScheme), i8p, f32p,
+             C.POINTER(U64))
+        _sig(R.pai_dequantize_f32, C.c_int32, i8p, f32p, U64, C.POINTER(QuantScheme), f32p)
         _sig(R.pai_opt_gemm_f32, C.c_int32, U64, U64, U64, f32p, f32p, f32p)
         _sig(R.pai_opt_gemm_w8_f32, C.c_int32, U64, U64, U64, f32p, i8p, f32p, U64,
              f32p)
@@ -139,6 +152,47 @@ def gemv_q(wtype: int, n: int, k: int, blocks: np.ndarray, x: np.ndarray,
                          np.ascontiguousarray(x, np.float32), y, threads)
     assert rc == 0
     return y
+
+
+def gemm_f32(m: int, n: int, k: int, a, b) -> np.ndarray:
+    c = np.empty(m * n, np.float32)
+    lib().po_gemm_f32(m, n, k, np.ascontiguousarray(a, np.float32).ravel(),
+                      np.ascontiguousarray(b, np.float32).ravel(), c)
+    return c.reshape(m, n)
+
+
+def v0_value_bytes(bits: int, n: int) -> int:
+    return n if bits == 8 else (n + 1) // 2
+
+
+def v0_groups(n: int, gs: int) -> int:
+    gs = gs or n
+    return (n + gs - 1) // gs
+
+
+def quant_v0(bits: int, gs: int, w) -> tuple[np.ndarray, np.ndarray]:
+    """models/quantize.c:74-143 restated: (packed values, f32 scales)."""
+    w = np.ascontiguousarray(w, np.float32).ravel()
+    q = np.empty(v0_value_bytes(bits, w.size), np.int8)
+    s = np.empty(v0_groups(w.size, gs), np.float32)
+    assert lib().po_quant_v0(bits, gs, w, w.size, q, s) == s.size
+    return q, s
+
+
+def dequant_v0(bits: int, gs: int, q, scales, n: int) -> np.ndarray:
+    out = np.empty(n, np.float32)
+    assert lib().po_dequant_v0(bits, gs, np.ascontiguousarray(q, np.int8),
+                               np.ascontiguousarray(scales, np.float32), n, out) == 0
+    return out
+
+
+def gemm_wq(bits: int, m: int, n: int, k: int, a, w_q, scales, g: int) -> np.ndarray:
+    """ref_ops.c:447-499 restated (pai_ref_gemm_w8_f32 / _w4_f32)."""
+    c = np.empty(m * n, np.float32)
+    assert lib().po_gemm_wq_f32(bits, m, n, k, np.ascontiguousarray(a, np.float32).ravel(),
+                                np.ascontiguousarray(w_q, np.int8).ravel(),
+                                np.ascontiguousarray(scales, np.float32).ravel(), g, c) == 0
+    return c.reshape(m, n)
 
 
 def rmsnorm_gamma(a, gamma, eps=1e-5):

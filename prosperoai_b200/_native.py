@@ -91,6 +91,10 @@ SIGNATURES = {
     "pai_b200_gemv_prepared_f32": (I32, [P, U32, U64, U64, U64, P, P, P, P]),
     "pai_b200_gemv_rmsnorm_f32": (I32, [P, U32, U64, U64, U64, P, P, P, F32, P, P]),
     "pai_b200_gemm_q4_0_f32": (I32, [P, U64, U64, U64, P, P, P]),
+    "pai_b200_gemm_w8_f32": (I32, [P, U64, U64, U64, P, P, P, U64, P]),
+    "pai_b200_gemm_w4_f32": (I32, [P, U64, U64, U64, P, P, P, U64, P]),
+    "pai_b200_gemm_v0_f32": (I32, [P, U32, U32, U64, U64, U64, P, P, P]),
+    "pai_b200_v0_blob_bytes": (U64, [U32, U32, U64]),
     "pai_b200_rmsnorm_gamma_f32": (I32, [P, U64, U64, P, P, F32, P]),
     "pai_b200_silu_mul_f32": (I32, [P, P, P, P, U64]),
     "pai_b200_vecadd_f32": (I32, [P, P, P, P, U64]),

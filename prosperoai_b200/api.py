@@ -146,6 +146,18 @@ class Device:
         """Y[m][n] = X[m][k] . W^T on the tensor cores (bf16 tiles, fp32 accumulate)."""
         check(load().pai_b200_gemm_q4_0_f32(self.ctx, m, w.n, w.k, x.ptr, w.ptr, y.ptr), "gemm_q4_0")
 
+    def gemm_wq(self, bits: int, m: int, n: int, k: int, a: Buffer, w_q: Buffer, scales: Buffer,
+                group_size: int, c: Buffer):
+        """pai_ref_gemm_w8_f32 / _w4_f32 semantics on the GPU ([k][n] int8 or nibbles)."""
+        fn = load().pai_b200_gemm_w8_f32 if bits == 8 else load().pai_b200_gemm_w4_f32
+        check(fn(self.ctx, m, n, k, a.ptr, w_q.ptr, scales.ptr, group_size, c.ptr), f"gemm_w{bits}")
+
+    def gemm_v0(self, bits: int, group_size: int, m: int, n: int, k: int, a: Buffer, blob: Buffer,
+                c: Buffer, blob_offset: int = 0):
+        """A v0 .pai quantized [k][n] tensor ([values][f32 scales]) read in place."""
+        check(load().pai_b200_gemm_v0_f32(self.ctx, bits, group_size, m, n, k, a.ptr,
+                                          blob.ptr + blob_offset, c.ptr), "gemm_v0")
+
     def dequant(self, w: PackedMatrix, out: Buffer):
         check(load().pai_b200_dequant(self.ctx, w.wtype, w.n, w.k, w.ptr, out.ptr), "dequant")
 

@@ -31,6 +31,9 @@ static const pai_op_descriptor_t s_ops[] = {
     B200_DESC("vecadd_f32_b200", 2, PAI_KERNEL_B200_VECADD),
     B200_DESC("dequant_block_f32", 1, PAI_KERNEL_B200_DEQUANT),
     B200_DESC("argmax_f32", 1, PAI_KERNEL_B200_ARGMAX),
+    B200_DESC("gemm_w8_f32_b200", 3, PAI_KERNEL_B200_GEMM_W8),    /* a, w_q, b_scales */
+    B200_DESC("gemm_w4_f32_b200", 3, PAI_KERNEL_B200_GEMM_W4),    /* a, w_q4, b_scales */
+    B200_DESC("gemm_v0_f32", 2, PAI_KERNEL_B200_GEMM_V0),         /* a, .pai blob    */
 };
 
 #define B200_NOPS (sizeof(s_ops) / sizeof(s_ops[0]))

@@ -1,0 +1,376 @@
+// GEMM over weights in ProsperoAI's v0 grouped-scale integer formats,
+// read in place, with m <= 8 activation rows per launch.
+//
+// The weight is the executor's GEMM B operand [k][n] (n contiguous,
+// scheduler/scheduler.c:285-343), stored as signed int8 values or as signed
+// nibbles packed two per byte over the flat index (even index in the low
+// nibble), with f32 scales in one of two layouts:
+//   kOpScales   s[(t / g) * n + j]: one scale per (k-group, column), the
+//               registered w8/w4 GEMMs (cpu/reference/ref_ops.c:447-499);
+//   kFlatScales s[(t * n + j) / g]: one scale per g consecutive flat
+//               elements, the blob a v0 .pai container holds for a
+//               quantized tensor ([values][scales], models/quantize.c:74-181,
+//               models/container.c:176-229).
+// c[r][j] = sum over t of a[r][t] * q(t, j) * scale(t, j), accumulated in
+// fp32. The reference rounds each product as (a*q)*s (w8/w4) or a*(s*q)
+// (dequantise, then pai_ref_gemm_f32); here the scale is applied with the
+// same two roundings in a different order and the sum is split over k, so
+// the result agrees with the reference to fp32 accumulation noise.
+//
+// HBM-bound (1 or 0.5 B of values per weight plus the scales), so the
+// design is about moving bytes: a CTA owns a strip of 256 columns and a
+// range of k; each lane holds 8 consecutive columns (8 B of int8 or 4 B of
+// nibbles per row), its warp takes every 8th row of the range, and 4-8
+// rows are loaded before any is used. Values become floats without the
+// integer-conversion pipe: the biased byte or nibble is placed in the low
+// mantissa bits of 2^23 by one byte permute and the bias subtracted in one
+// exact fp32 add. Partial sums of the warps are added in warp order in
+// shared memory; k-splits write partials that the last CTA of the strip to
+// finish adds in split order, so results do not depend on timing.
+//
+// Shapes the vector path does not take (n not a multiple of 8, unaligned
+// pointers, flat groups that are not a multiple of 8) run an element-wise
+// kernel with the same split and reduction order.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <type_traits>
+
+#include "../b200_internal.h"
+#include "b200_device.cuh"
+
+namespace {
+
+enum { kOpScales = 0, kFlatScales = 1 };
+
+constexpr int kCols = 8;                 // columns per lane
+constexpr int kWarps = 8;                // warps per CTA; warp w takes rows t0 + w + 8i
+constexpr int kThreads = kWarps * 32;    // 256
+constexpr int kStrip = 32 * kCols;       // 256 columns per CTA
+constexpr int kMaxRows = 8;              // activation rows per launch
+constexpr uint64_t kMaxPer = 1024;       // rows of k per split (activation staging)
+
+struct V0Args {
+  uint64_t m, n, k;   // m <= kMaxRows
+  const float *a;     // [m][k]
+  const uint8_t *w;   // values
+  const uint8_t *s;   // f32 scales (4-byte aligned on the vector path)
+  uint64_t g;         // group size: rows (kOpScales) or flat elements (kFlatScales)
+  float *c;           // [m][n]
+  uint64_t per;       // rows of k per split, a multiple of kWarps
+  float *part;        // [split][m][n] when gridDim.y > 1
+  uint32_t *cnt;      // [strip] arrival counters, left at zero
+};
+
+// Signed value of flat element f (models/quantize.c:165-172).
+template <int BITS>
+__device__ __forceinline__ int32_t v0_value(const uint8_t *w, uint64_t f) {
+  if (BITS == 8) return (int8_t)w[f];
+  const uint32_t b = w[f >> 1];
+  const int32_t nib = (f & 1) ? (b >> 4) & 0xF : b & 0xF;
+  return (nib ^ 8) - 8;
+}
+
+__device__ __forceinline__ float ld_scale_any(const uint8_t *s, uint64_t i) {
+  const uint8_t *p = s + 4 * i;
+  return __uint_as_float((uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24));
+}
+
+// Float of the biased unsigned byte `sel` of word x: 2^23 + byte, exact.
+__device__ __forceinline__ float biased_byte(uint32_t x, uint32_t sel) {
+  return __uint_as_float(__byte_perm(x, 0x4B000000u, 0x7540u | sel));
+}
+
+// After every thread has written its columns' results (to c when the grid
+// has one split, else to its split's partials): the last CTA of the strip
+// adds the splits in order.
+__device__ __forceinline__ void finish_strip(const V0Args &p) {
+  if (gridDim.y == 1) return;
+  __shared__ uint32_t ticket;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) ticket = atomicAdd(&p.cnt[blockIdx.x], 1u);
+  __syncthreads();
+  if (ticket != gridDim.y - 1) return;
+  __threadfence();
+  const uint64_t j = (uint64_t)blockIdx.x * kStrip + threadIdx.x;
+  if (j < p.n) {
+    for (uint64_t r = 0; r < p.m; r++) {
+      float v = 0.0f;
+      for (uint32_t y = 0; y < gridDim.y; y++) v += __ldcg(&p.part[((uint64_t)y * p.m + r) * p.n + j]);
+      p.c[r * p.n + j] = v;
+    }
+  }
+  if (threadIdx.x == 0) p.cnt[blockIdx.x] = 0;
+}
+
+__device__ __forceinline__ void put_result(const V0Args &p, uint64_t r, uint64_t j, float v) {
+  if (gridDim.y == 1)
+    p.c[r * p.n + j] = v;
+  else
+    p.part[((uint64_t)blockIdx.y * p.m + r) * p.n + j] = v;
+}
+
+// Vector path: n % 8 == 0, values 8-byte (int8) or 4-byte (nibbles)
+// aligned, scales 16-byte (kOpScales) or 4-byte aligned with g % 8 == 0
+// (kFlatScales, so a lane's 8 columns of a row share one scale).
+template <int BITS, int LAYOUT, int MB>
+__global__ void __launch_bounds__(kThreads) k_gemm_v0(V0Args p) {
+  extern __shared__ float sa[];  // [MB][per] activations of this split
+  __shared__ float red[kWarps][kStrip];
+  constexpr int U = BITS == 8 ? 4 : 8;  // rows in flight per lane
+  using Raw = typename std::conditional<BITS == 8, uint2, uint32_t>::type;
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint64_t j0 = (uint64_t)blockIdx.x * kStrip + lane * kCols;
+  const uint64_t t0 = (uint64_t)blockIdx.y * p.per, t1 = min(p.k, t0 + p.per);
+  const bool live = j0 < p.n;
+  pdl_wait();  // a no-op unless launched as a programmatic dependent
+  for (uint32_t i = threadIdx.x; i < MB * p.per; i += kThreads) {
+    const uint32_t r = i / (uint32_t)p.per, tt = i - r * (uint32_t)p.per;
+    sa[i] = (r < p.m && t0 + tt < t1) ? __ldg(p.a + r * p.k + t0 + tt) : 0.0f;
+  }
+  __syncthreads();
+
+  float acc[MB][kCols];
+#pragma unroll
+  for (int r = 0; r < MB; r++)
+#pragma unroll
+    for (int e = 0; e < kCols; e++) acc[r][e] = 0.0f;
+
+  // scale cursor: kOpScales keeps the 8 scales of the current k-group;
+  // kFlatScales keeps (f / g, f % g) of this lane's first column f of the row
+  const float *sf = reinterpret_cast<const float *>(p.s);
+  float sc[kCols];
+  uint64_t gnext = 0, qg = 0, rg = 0, dq = 0, dr = 0;
+  const uint64_t tf = t0 + warp;
+  if (LAYOUT == kFlatScales) {
+    const uint64_t f = tf * p.n + j0, step = (uint64_t)kWarps * p.n;
+    qg = f / p.g;
+    rg = f - qg * p.g;
+    dq = step / p.g;
+    dr = step - dq * p.g;
+  }
+
+  for (uint64_t t = tf; t < t1; t += (uint64_t)kWarps * U) {
+    Raw raw[U];
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const uint64_t tu = t + (uint64_t)kWarps * u;
+      if (live && tu < t1) {
+        raw[u] = __ldcs(reinterpret_cast<const Raw *>(p.w + (BITS == 8 ? tu * p.n + j0 : (tu * p.n + j0) >> 1)));
+      } else {
+        raw[u] = Raw{};  // decodes to zeros
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const uint64_t tu = t + (uint64_t)kWarps * u;
+      if (tu >= t1) break;
+      float v[kCols];
+      if constexpr (BITS == 8) {
+        const uint32_t x0 = raw[u].x ^ 0x80808080u, x1 = raw[u].y ^ 0x80808080u;
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          v[e] = biased_byte(x0, e) - 8388736.0f;  // 2^23 + 128
+          v[e + 4] = biased_byte(x1, e) - 8388736.0f;
+        }
+      } else {
+        const uint32_t x = raw[u] ^ 0x88888888u;
+        const uint32_t lo = x & 0x0F0F0F0Fu, hi = (x >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          v[2 * e] = biased_byte(lo, e) - 8388616.0f;  // 2^23 + 8
+          v[2 * e + 1] = biased_byte(hi, e) - 8388616.0f;
+        }
+      }
+      const uint32_t tl = (uint32_t)(tu - t0);
+      if constexpr (LAYOUT == kOpScales) {
+        if (tu >= gnext) {  // uniform across the warp
+          const uint64_t gi = tu / p.g;
+          gnext = (gi + 1) * p.g;
+          if (live) {
+            const float4 s0 = __ldg(reinterpret_cast<const float4 *>(sf + gi * p.n + j0));
+            const float4 s1 = __ldg(reinterpret_cast<const float4 *>(sf + gi * p.n + j0 + 4));
+            sc[0] = s0.x, sc[1] = s0.y, sc[2] = s0.z, sc[3] = s0.w;
+            sc[4] = s1.x, sc[5] = s1.y, sc[6] = s1.z, sc[7] = s1.w;
+          } else {
+#pragma unroll
+            for (int e = 0; e < kCols; e++) sc[e] = 0.0f;
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < kCols; e++) {
+          const float we = v[e] * sc[e];
+#pragma unroll
+          for (int r = 0; r < MB; r++) acc[r][e] = fmaf(sa[r * p.per + tl], we, acc[r][e]);
+        }
+      } else {
+        const float srow = live ? __ldg(sf + qg) : 0.0f;
+        rg += dr;
+        qg += dq;
+        if (rg >= p.g) {
+          rg -= p.g;
+          qg++;
+        }
+#pragma unroll
+        for (int r = 0; r < MB; r++) {
+          const float as = sa[r * p.per + tl] * srow;
+#pragma unroll
+          for (int e = 0; e < kCols; e++) acc[r][e] = fmaf(as, v[e], acc[r][e]);
+        }
+      }
+    }
+  }
+
+  // warps' partial sums, added in warp order
+#pragma unroll
+  for (int r = 0; r < MB; r++) {
+    if (r >= (int)p.m) break;
+    float4 *dst = reinterpret_cast<float4 *>(&red[warp][lane * kCols]);
+    dst[0] = make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+    dst[1] = make_float4(acc[r][4], acc[r][5], acc[r][6], acc[r][7]);
+    __syncthreads();
+    float s = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kWarps; w++) s += red[w][threadIdx.x];
+    const uint64_t j = (uint64_t)blockIdx.x * kStrip + threadIdx.x;
+    if (j < p.n) put_result(p, r, j, s);
+    __syncthreads();
+  }
+  finish_strip(p);
+}
+
+// Element-wise path for every other shape: thread per column, all rows of
+// the split in order.
+template <int BITS, int LAYOUT>
+__global__ void __launch_bounds__(kThreads) k_gemm_v0_any(V0Args p) {
+  const uint64_t j = (uint64_t)blockIdx.x * kStrip + threadIdx.x;
+  const uint64_t t0 = (uint64_t)blockIdx.y * p.per, t1 = min(p.k, t0 + p.per);
+  pdl_wait();
+  float acc[kMaxRows];
+#pragma unroll
+  for (int r = 0; r < kMaxRows; r++) acc[r] = 0.0f;
+  if (j < p.n) {
+    for (uint64_t t = t0; t < t1; t++) {
+      const uint64_t f = t * p.n + j;
+      const float sv = ld_scale_any(p.s, LAYOUT == kOpScales ? (t / p.g) * p.n + j : f / p.g);
+      const float we = (float)v0_value<BITS>(p.w, f) * sv;
+#pragma unroll
+      for (int r = 0; r < kMaxRows; r++)
+        if (r < (int)p.m) acc[r] = fmaf(__ldg(p.a + r * p.k + t), we, acc[r]);
+    }
+#pragma unroll
+    for (int r = 0; r < kMaxRows; r++)
+      if (r < (int)p.m) put_result(p, r, j, acc[r]);
+  }
+  finish_strip(p);
+}
+
+template <int BITS, int LAYOUT>
+cudaError_t launch_vec(pai_b200_ctx_t *ctx, dim3 grid, uint32_t mb, const V0Args &a) {
+  const size_t smem = (size_t)mb * a.per * sizeof(float);
+  switch (mb) {
+    case 1: return b200_launch(ctx, k_gemm_v0<BITS, LAYOUT, 1>, grid, dim3(kThreads), smem, a);
+    case 2: return b200_launch(ctx, k_gemm_v0<BITS, LAYOUT, 2>, grid, dim3(kThreads), smem, a);
+    case 4: return b200_launch(ctx, k_gemm_v0<BITS, LAYOUT, 4>, grid, dim3(kThreads), smem, a);
+    default: return b200_launch(ctx, k_gemm_v0<BITS, LAYOUT, 8>, grid, dim3(kThreads), smem, a);
+  }
+}
+
+pai_status_t gemm_v0(pai_b200_ctx_t *ctx, uint32_t bits, int layout, uint64_t m, uint64_t n, uint64_t k,
+                     const float *a, const void *w, const void *s, uint64_t g, float *c, const char *what) {
+  const uintptr_t wa = (uintptr_t)w, sa = (uintptr_t)s;
+  const bool vec = n % kCols == 0 && wa % (bits == 8 ? 8 : 4) == 0 &&
+                   (layout == kOpScales ? sa % 16 == 0 : (sa % 4 == 0 && g % kCols == 0));
+  const uint64_t strips = (n + kStrip - 1) / kStrip;
+  // about 4 CTAs per SM, at least 64 rows per split, at most kMaxPer
+  uint64_t splits = std::max<uint64_t>(1, (4 * 148 + strips - 1) / strips);
+  splits = std::min<uint64_t>(splits, std::max<uint64_t>(1, k / 64));
+  splits = std::max<uint64_t>(splits, (k + kMaxPer - 1) / kMaxPer);
+  uint64_t per = (k + splits - 1) / splits;
+  per = (per + kWarps - 1) / kWarps * kWarps;
+  splits = (k + per - 1) / per;
+  if (strips > 0xFFFFFFFFull || splits > 65535)
+    return b200_fail(PAI_ERR_INVALID_ARG, "%s: n %llu x k %llu is beyond the launch grid", what,
+                     (unsigned long long)n, (unsigned long long)k);
+  for (uint64_t r0 = 0; r0 < m; r0 += kMaxRows) {
+    const uint64_t mm = std::min<uint64_t>(kMaxRows, m - r0);
+    V0Args p{};
+    p.m = mm;
+    p.n = n;
+    p.k = k;
+    p.a = a + r0 * k;
+    p.w = static_cast<const uint8_t *>(w);
+    p.s = static_cast<const uint8_t *>(s);
+    p.g = g;
+    p.c = c + r0 * n;
+    p.per = per;
+    if (splits > 1) {
+      pai_status_t st = b200_ctx_scratch(ctx, splits * mm * n, (uint32_t)strips, &p.part, &p.cnt);
+      if (st) return st;
+    }
+    const dim3 grid((uint32_t)strips, (uint32_t)splits);
+    cudaError_t e;
+    if (vec) {
+      const uint32_t mb = mm == 1 ? 1 : mm == 2 ? 2 : mm <= 4 ? 4 : 8;
+      if (bits == 8)
+        e = layout == kOpScales ? launch_vec<8, kOpScales>(ctx, grid, mb, p) : launch_vec<8, kFlatScales>(ctx, grid, mb, p);
+      else
+        e = layout == kOpScales ? launch_vec<4, kOpScales>(ctx, grid, mb, p) : launch_vec<4, kFlatScales>(ctx, grid, mb, p);
+    } else {
+      if (bits == 8)
+        e = layout == kOpScales ? b200_launch(ctx, k_gemm_v0_any<8, kOpScales>, grid, dim3(kThreads), 0, p)
+                                : b200_launch(ctx, k_gemm_v0_any<8, kFlatScales>, grid, dim3(kThreads), 0, p);
+      else
+        e = layout == kOpScales ? b200_launch(ctx, k_gemm_v0_any<4, kOpScales>, grid, dim3(kThreads), 0, p)
+                                : b200_launch(ctx, k_gemm_v0_any<4, kFlatScales>, grid, dim3(kThreads), 0, p);
+    }
+    if (e != cudaSuccess) return b200_cuda(e, what);
+    pai_status_t st = b200_launched(ctx, 1, vec ? "k_gemm_v0" : "k_gemm_v0_any");
+    if (st) return st;
+  }
+  return PAI_OK;
+}
+
+pai_status_t gemm_wq(pai_b200_ctx_t *ctx, uint32_t bits, uint64_t m, uint64_t n, uint64_t k, const float *a,
+                     const int8_t *w_q, const float *b_scales, uint64_t group_size, float *c, const char *what) {
+  // argument rules of ref_ops.c:450-455 / 474-479
+  if (!ctx || m == 0 || n == 0 || k == 0 || !a || !w_q || !b_scales || !c)
+    return b200_fail(PAI_ERR_INVALID_ARG, "%s: invalid arguments", what);
+  if (group_size == 0 || group_size > k) group_size = k;
+  return gemm_v0(ctx, bits, kOpScales, m, n, k, a, w_q, b_scales, group_size, c, what);
+}
+
+}  // namespace
+
+extern "C" pai_status_t pai_b200_gemm_w8_f32(pai_b200_ctx_t *ctx, uint64_t m, uint64_t n, uint64_t k, const float *a,
+                                             const int8_t *w_q, const float *b_scales, uint64_t group_size,
+                                             float *c) {
+  return gemm_wq(ctx, 8, m, n, k, a, w_q, b_scales, group_size, c, "gemm_w8_f32");
+}
+
+extern "C" pai_status_t pai_b200_gemm_w4_f32(pai_b200_ctx_t *ctx, uint64_t m, uint64_t n, uint64_t k, const float *a,
+                                             const int8_t *w_q4, const float *b_scales, uint64_t group_size,
+                                             float *c) {
+  return gemm_wq(ctx, 4, m, n, k, a, w_q4, b_scales, group_size, c, "gemm_w4_f32");
+}
+
+extern "C" uint64_t pai_b200_v0_blob_bytes(uint32_t bit_width, uint32_t group_size, uint64_t numel) {
+  // pai_quant_weights_bytes (models/quantize.c:53-72)
+  if ((bit_width != 8 && bit_width != 4) || numel == 0) return 0;
+  const uint64_t gs = group_size ? group_size : numel;
+  return (bit_width == 8 ? numel : (numel + 1) / 2) + (numel + gs - 1) / gs * sizeof(float);
+}
+
+extern "C" pai_status_t pai_b200_gemm_v0_f32(pai_b200_ctx_t *ctx, uint32_t bit_width, uint32_t group_size, uint64_t m,
+                                             uint64_t n, uint64_t k, const float *a, const void *blob, float *c) {
+  if (!ctx || m == 0 || n == 0 || k == 0 || !a || !blob || !c)
+    return b200_fail(PAI_ERR_INVALID_ARG, "gemm_v0: invalid arguments");
+  // v0 executes signed q8/q4 only (models/quantize.c:14-19, models/model.c:264-267)
+  if (bit_width != 8 && bit_width != 4)
+    return b200_fail(PAI_ERR_UNSUPPORTED, "gemm_v0: bit width %u (v0 runs 8 and 4)", bit_width);
+  const uint64_t numel = n * k, gs = group_size ? group_size : numel;
+  const uint64_t vbytes = bit_width == 8 ? numel : (numel + 1) / 2;
+  return gemm_v0(ctx, bit_width, kFlatScales, m, n, k, a, blob, static_cast<const uint8_t *>(blob) + vbytes, gs, c,
+                 "gemm_v0");
+}

@@ -171,6 +171,89 @@ def main():
     np.savez_compressed(path, **g)
     print(f"wrote {path}: {len(g)} arrays, {os.path.getsize(path)} bytes")
 
+    v0 = v0_cases(R)
+    path = os.path.join(OUT, "golden_v0.npz")
+    np.savez_compressed(path, **v0)
+    print(f"wrote {path}: {len(v0)} arrays, {os.path.getsize(path)} bytes")
+
+
+def ref_quant_v0(R, bits, gs, w):
+    """pai_quantize_f32 (models/quantize.c:74-143) on w: (values, scales)."""
+    w = np.ascontiguousarray(w, np.float32).ravel()
+    sch = po.QuantScheme(bits, 1, gs)
+    q = np.empty(po.v0_value_bytes(bits, w.size), np.int8)
+    s = np.empty(po.v0_groups(w.size, gs), np.float32)
+    ng = po.U64()
+    assert R.pai_quantize_f32(w, w.size, C.byref(sch), q, s, C.byref(ng)) == 0
+    assert ng.value == s.size
+    return q, s
+
+
+def per_column_quant(R, bits, gs, w, k, n):
+    """The reference test's per-column quantisation of a [k][n] weight with
+    the scales scattered to [k/g][n] (tests/test_quantize.c:155-180,
+    201-230): what pai_ref_gemm_w8_f32 / _w4_f32 take."""
+    g = k if gs == 0 else gs
+    ng = (k + g - 1) // g
+    vals = np.zeros((k, n), np.int32)
+    scales = np.empty((ng, n), np.float32)
+    for j in range(n):
+        q, sc = ref_quant_v0(R, bits, gs, w[:, j])
+        if bits == 8:
+            vals[:, j] = q
+        else:
+            b = q.view(np.uint8).astype(np.int32)
+            nib = np.stack([b & 15, b >> 4], 1).ravel()[:k]
+            vals[:, j] = np.where(nib & 8, nib - 16, nib)
+        scales[:, j] = sc
+    flat = vals.ravel()
+    if bits == 8:
+        packed = flat.astype(np.int8)
+    else:
+        nib = (flat & 15).astype(np.uint8)
+        if nib.size % 2:
+            nib = np.append(nib, 0)
+        packed = (nib[0::2] | (nib[1::2] << 4)).astype(np.uint8).view(np.int8)
+    return packed, scales
+
+
+def v0_cases(R):
+    """v0 grouped-scale formats. (a) the registered w8/w4 GEMMs on the
+    reference test's shapes (tests/test_quantize.c:135-271: m 3, n 5, k 8,
+    group 4 and per-tensor) and on a larger ragged shape; (b) .pai blobs
+    ([values][scales] of pai_quantize_f32 over the flat [k][n] tensor) with
+    the reference's dequantise-then-GEMM result (models/model.c:259-290,
+    ref_ops.c:428-444), including an odd element count whose scales start
+    at an unaligned offset."""
+    rng = np.random.default_rng(20261202)
+    g = {}
+    for name, bits, (m, n, k), gs in (("w8_g4", 8, (3, 5, 8), 4), ("w4_g4", 4, (3, 5, 8), 4),
+                                      ("w8_g0", 8, (3, 5, 8), 0), ("w8_g32", 8, (4, 37, 96), 32),
+                                      ("w4_g32", 4, (4, 37, 96), 32), ("w4_g0", 4, (2, 24, 40), 0)):
+        a = rng.standard_normal((m, k)).astype(np.float32)
+        w = rng.standard_normal((k, n)).astype(np.float32)
+        wq, sc = per_column_quant(R, bits, gs, w, k, n)
+        c = np.empty(m * n, np.float32)
+        fn = R.pai_ref_gemm_w8_f32 if bits == 8 else R.pai_ref_gemm_w4_f32
+        assert fn(m, n, k, a, wq, sc, gs, c) == 0
+        g[f"{name}_shape"] = np.array([m, n, k, gs], np.int64)
+        g[f"{name}_a"], g[f"{name}_wq"], g[f"{name}_scales"], g[f"{name}_ref"] = a, wq, sc.ravel(), c
+    for name, bits, (m, n, k), gs in (("pai8_g32", 8, (1, 48, 64), 32), ("pai4_g32", 4, (2, 48, 64), 32),
+                                      ("pai8_g0", 8, (3, 40, 24), 0), ("pai4_g12", 4, (1, 20, 30), 12),
+                                      ("pai4_odd", 4, (2, 5, 7), 3)):
+        a = rng.standard_normal((m, k)).astype(np.float32)
+        w = (rng.standard_normal((k, n)) * 0.05).astype(np.float32)
+        q, sc = ref_quant_v0(R, bits, gs, w)
+        deq = np.empty(k * n, np.float32)
+        assert R.pai_dequantize_f32(q, sc, k * n, C.byref(po.QuantScheme(bits, 1, gs)), deq) == 0
+        c = np.empty(m * n, np.float32)
+        assert R.pai_ref_gemm_f32(m, n, k, a, deq, c) == 0
+        g[f"{name}_shape"] = np.array([m, n, k, gs, bits], np.int64)
+        g[f"{name}_a"], g[f"{name}_w"] = a, w
+        g[f"{name}_blob"] = np.concatenate([q.view(np.uint8), sc.view(np.uint8)])
+        g[f"{name}_deq"], g[f"{name}_ref"] = deq, c
+    return g
+
 
 if __name__ == "__main__":
     main()

@@ -87,7 +87,7 @@ def test_registry_registration():
     assert {"gemv_q4_0_f32", "gemv_q8_0_f32", "gemv_q4_k_f32", "attention_decode_f16kv"} <= names
     for i in range(n):
         d = reg.ops[28 + i].contents
-        assert d.caps == 1 << 3 and 14 <= d.kernel_id <= 25
+        assert d.caps == 1 << 3 and 14 <= d.kernel_id <= 28
     full = _native.OpRegistry()
     full.count = 60
     assert L.pai_b200_register_ops(C.byref(full)) == -2  # PAI_ERR_NOMEM: 64-op cap

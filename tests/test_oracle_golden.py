@@ -145,3 +145,72 @@ def test_live_q8_0_maps_onto_reference_w8_gemm():
     c = np.empty(n, np.float32)
     assert ref.pai_ref_gemm_w8_f32(1, n, k, x, wq, sc, 32, c) == 0
     np.testing.assert_allclose(c, po.gemv_q(po.Q8_0, n, k, blocks, x), rtol=1e-5, atol=1e-6)
+
+
+# ---- v0 grouped-scale formats (models/quantize.c, ref_ops.c:447-499) ------------------
+
+V0 = np.load(os.path.join(os.path.dirname(__file__), "golden", "golden_v0.npz"))
+WQ_CASES = ["w8_g4", "w4_g4", "w8_g0", "w8_g32", "w4_g32", "w4_g0"]
+PAI_CASES = ["pai8_g32", "pai4_g32", "pai8_g0", "pai4_g12", "pai4_odd"]
+
+
+@pytest.mark.parametrize("name", WQ_CASES)
+def test_gemm_wq_matches_reference(name):
+    m, n, k, gs = (int(v) for v in V0[f"{name}_shape"])
+    bits = 8 if name.startswith("w8") else 4
+    got = po.gemm_wq(bits, m, n, k, V0[f"{name}_a"], V0[f"{name}_wq"], V0[f"{name}_scales"], gs)
+    assert same_bits(got.ravel(), V0[f"{name}_ref"])
+
+
+@pytest.mark.parametrize("name", PAI_CASES)
+def test_v0_blob_quantise_dequantise_gemm_match_reference(name):
+    m, n, k, gs, bits = (int(v) for v in V0[f"{name}_shape"])
+    q, s = po.quant_v0(bits, gs, V0[f"{name}_w"])
+    blob = V0[f"{name}_blob"]
+    assert np.array_equal(np.concatenate([q.view(np.uint8), s.view(np.uint8)]), blob)
+    deq = po.dequant_v0(bits, gs, q, s, n * k)
+    assert same_bits(deq, V0[f"{name}_deq"])
+    assert same_bits(po.gemm_f32(m, n, k, V0[f"{name}_a"], deq).ravel(), V0[f"{name}_ref"])
+
+
+def test_v0_known_answers():
+    """The reference's own round-trip cases (tests/test_quantize.c:62-116)."""
+    rng = np.random.default_rng(5)
+    src = rng.uniform(-1, 1, 256).astype(np.float32)
+    q, s = po.quant_v0(8, 64, src)
+    assert s.size == 4 and np.abs(po.dequant_v0(8, 64, q, s, 256) - src).max() < 0.02
+    exact = np.array([0, 100, -100, 100], np.float32)
+    q, s = po.quant_v0(8, 0, exact)
+    assert np.abs(po.dequant_v0(8, 0, q, s, 4) - exact).max() < 1e-4
+    exact = np.array([0, 2, -2, 1], np.float32)
+    q, s = po.quant_v0(4, 0, exact)
+    d = po.dequant_v0(4, 0, q, s, 4)
+    assert q.size == 2 and np.abs(d[:3] - exact[:3]).max() < 1e-4 and abs(d[3] - 1) < 0.2
+    odd = np.array([4, -4, 4], np.float32)
+    q, s = po.quant_v0(4, 0, odd)
+    assert q.size == 2 and np.abs(po.dequant_v0(4, 0, q, s, 3) - odd).max() < 1e-4
+    assert q.view(np.uint8)[1] >> 4 == 0  # the padding nibble stays zero
+
+
+@pytest.mark.skipif(po.ref() is None, reason="reference build (oracle/_ref) not present")
+@pytest.mark.parametrize("bits,gs", [(8, 0), (8, 7), (4, 32), (4, 5)])
+def test_v0_live_against_reference(bits, gs):
+    import ctypes as C
+    R = po.ref()
+    rng = np.random.default_rng(bits * 100 + gs)
+    w = (rng.standard_normal(777) * 0.1).astype(np.float32)
+    q, s = po.quant_v0(bits, gs, w)
+    q2, s2 = np.empty_like(q), np.empty_like(s)
+    ng = po.U64()
+    sch = po.QuantScheme(bits, 1, gs)
+    assert R.pai_quantize_f32(w, w.size, C.byref(sch), q2, s2, C.byref(ng)) == 0
+    assert np.array_equal(q, q2) and same_bits(s, s2)
+    m, n, k = 2, 21, 37
+    a = rng.standard_normal(m * k).astype(np.float32)
+    g = gs or k
+    wq = rng.integers(-128, 128, n * k if bits == 8 else (n * k + 1) // 2).astype(np.int8)
+    sc = rng.standard_normal((k + g - 1) // g * n).astype(np.float32)
+    c2 = np.empty(m * n, np.float32)
+    fn = R.pai_ref_gemm_w8_f32 if bits == 8 else R.pai_ref_gemm_w4_f32
+    assert fn(m, n, k, a, wq, sc, gs, c2) == 0
+    assert same_bits(po.gemm_wq(bits, m, n, k, a, wq, sc, gs).ravel(), c2)
