@@ -43,6 +43,7 @@ typedef int32_t pai_status_t; /* pai/error.h:11 */
 #define PAI_ERR_IO -7
 #define PAI_ERR_INIT -8
 #define PAI_ERR_INTERNAL -9
+#define PAI_ERR_PROTOCOL -10
 #endif
 
 #ifndef PAI_OP_H
@@ -377,6 +378,37 @@ pai_status_t pai_b200_model_create(pai_b200_ctx_t *ctx,
                                    uint32_t tp_rank, uint32_t tp_size,
                                    pai_b200_model_t **out);
 pai_status_t pai_b200_model_destroy(pai_b200_model_t *m);
+
+/* ---- GGUF import ------------------------------------------------------------------ */
+
+/* What a LLaMA-family GGUF file describes (adapters/llama/llama.c:304-375
+ * reads the same keys): the model configuration (eps is the executor's
+ * default 1e-5; wtype/etype the ggml types of the layer matrices and of
+ * the embedding/lm head), the container version, context length, rotary
+ * dims, whether output.weight is absent (the lm head is then the
+ * embedding, llama.c:445-470) and the bytes of the tensors the model uses. */
+typedef struct pai_b200_gguf_info {
+  pai_b200_model_cfg_t cfg;
+  uint32_t version, context_length, n_rot, tied_output;
+  uint64_t tensor_count, weight_bytes;
+  char architecture[64];
+} pai_b200_gguf_info_t;
+
+/* Parse and validate a GGUF file without a GPU (the file is mapped, not
+ * read into memory; no size cap). PAI_ERR_IO: the file cannot be opened;
+ * PAI_ERR_PROTOCOL: malformed container or tensor bytes outside the file;
+ * PAI_ERR_UNSUPPORTED: version, architecture, tensor count over 1024, or
+ * a shape/type the backend does not run (head_dim 128 fully rotated, one
+ * of Q4_0/Q8_0/Q4_K for all matrices, f32 norms); PAI_ERR_MISMATCH: an
+ * absent key or tensor, or inconsistent shapes. */
+pai_status_t pai_b200_gguf_inspect(const char *path, pai_b200_gguf_info_t *info);
+/* Create the model (pai_b200_model_create for tp_rank of tp_size) and load
+ * every tensor's ggml blocks from the file as stored: no f32 dequantisation
+ * at import (the reference dequantises and transposes, llama.c:402-470).
+ * info, when non-NULL, receives what pai_b200_gguf_inspect reports. */
+pai_status_t pai_b200_model_load_gguf(pai_b200_ctx_t *ctx, const char *path, uint32_t tp_rank,
+                                      uint32_t tp_size, pai_b200_model_t **out,
+                                      pai_b200_gguf_info_t *info);
 /* Load one whole (unsharded) tensor from host memory: ggml blocks
  * [out][in] for matrices, fp32 for norms. The model keeps its shard. */
 pai_status_t pai_b200_model_set_tensor(pai_b200_model_t *m, uint32_t kind,

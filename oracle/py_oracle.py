@@ -78,6 +78,20 @@ def lib():
     return _lib
 
 
+class GgufTensor(C.Structure):
+    """pai_gguf_tensor_t (adapters/llama/gguf.h:55-61)."""
+    _fields_ = [("name", C.c_char * 128), ("n_dims", C.c_uint32), ("dims", C.c_uint64 * 4),
+                ("type", C.c_uint32), ("offset", C.c_uint64)]
+
+
+class Gguf(C.Structure):
+    """pai_gguf_t (adapters/llama/gguf.h:64-74)."""
+    _fields_ = [("data", C.c_void_p), ("size", C.c_uint64), ("version", C.c_uint32),
+                ("tensor_count", C.c_uint64), ("kv_count", C.c_uint64), ("alignment", C.c_uint64),
+                ("kv_start", C.c_void_p), ("data_start", C.c_void_p),
+                ("tensors", C.POINTER(GgufTensor))]
+
+
 class QuantScheme(C.Structure):
     """pai_quant_scheme_t (models/quantize.h:35-39)."""
     _fields_ = [("bit_width", C.c_uint8), ("is_signed", C.c_uint8), ("group_size", C.c_uint16)]
@@ -109,6 +123,16 @@ def ref():
         _sig(R.pai_ref_gemm_w4_f32, C.c_int32, U64, U64, U64, f32p, i8p, f32p, U64,
              f32p)
         _sig(R.pai_opt_gemv_f32, C.c_int32, U64, U64, f32p, f32p, f32p)
+        _sig(R.pai_gguf_open, C.c_int32, C.c_char_p, U64, C.POINTER(Gguf))
+        _sig(R.pai_gguf_close, None, C.POINTER(Gguf))
+        _sig(R.pai_gguf_get_u32, C.c_int32, C.POINTER(Gguf), C.c_char_p, C.POINTER(C.c_uint32))
+        _sig(R.pai_gguf_get_f32, C.c_int32, C.POINTER(Gguf), C.c_char_p, C.POINTER(C.c_float))
+        _sig(R.pai_gguf_get_string, C.c_int32, C.POINTER(Gguf), C.c_char_p, C.c_char_p, U64)
+        _sig(R.pai_gguf_get_string_array, C.c_int32, C.POINTER(Gguf), C.c_char_p,
+             C.POINTER(C.POINTER(C.c_char_p)), C.POINTER(U64))
+        _sig(R.pai_gguf_find_tensor, C.POINTER(GgufTensor), C.POINTER(Gguf), C.c_char_p)
+        _sig(R.pai_gguf_dequant, C.c_int32, C.POINTER(Gguf), C.POINTER(GgufTensor),
+             C.POINTER(C.POINTER(C.c_float)), C.POINTER(U64))
         _sig(R.pai_quantize_f32, C.c_int32, f32p, U64, C.POINTER(QuantScheme), i8p, f32p,
              C.POINTER(U64))
         _sig(R.pai_dequantize_f32, C.c_int32, i8p, f32p, U64, C.POINTER(QuantScheme), f32p)

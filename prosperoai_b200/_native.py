@@ -38,6 +38,13 @@ class ModelCfg(C.Structure):
                 ("wtype", C.c_uint32), ("etype", C.c_uint32)]
 
 
+class GgufInfo(C.Structure):
+    """pai_b200_gguf_info_t."""
+    _fields_ = [("cfg", ModelCfg), ("version", C.c_uint32), ("context_length", C.c_uint32),
+                ("n_rot", C.c_uint32), ("tied_output", C.c_uint32), ("tensor_count", C.c_uint64),
+                ("weight_bytes", C.c_uint64), ("architecture", C.c_char * 64)]
+
+
 class OpDescriptor(C.Structure):
     _fields_ = [("name", C.c_char_p), ("version", C.c_uint32), ("num_inputs", C.c_uint32),
                 ("num_outputs", C.c_uint32), ("in_dtype", C.c_int32), ("out_dtype", C.c_int32),
@@ -116,6 +123,8 @@ SIGNATURES = {
     "pai_b200_tp_size": (U32, [P]),
     "pai_b200_tp_allreduce_f32": (I32, [P, P, U64]),
     "pai_b200_model_destroy": (I32, [P]),
+    "pai_b200_gguf_inspect": (I32, [C.c_char_p, C.POINTER(GgufInfo)]),
+    "pai_b200_model_load_gguf": (I32, [P, C.c_char_p, U32, U32, PP, C.POINTER(GgufInfo)]),
     "pai_b200_model_set_tensor": (I32, [P, U32, U32, P]),
     "pai_b200_model_synthesize": (I32, [P, U64]),
     "pai_b200_tensor_seed": (U64, [U64, U32, U32]),

@@ -7,13 +7,14 @@ the reference status code (pai/error.h) when the C call fails.
 from __future__ import annotations
 
 import ctypes as C
+import os
 
 import numpy as np
 
-from ._native import (Q4_0, Q4_K, Q8_0, ModelCfg, OpRegistry, PaiError, check, load)
+from ._native import (Q4_0, Q4_K, Q8_0, GgufInfo, ModelCfg, OpRegistry, PaiError, check, load)
 
 __all__ = ["Device", "Buffer", "PackedMatrix", "Model", "Session", "PaiError",
-           "Q4_0", "Q8_0", "Q4_K", "block_bytes", "quantize", "rope_tables"]
+           "Q4_0", "Q8_0", "Q4_K", "block_bytes", "quantize", "rope_tables", "gguf_inspect"]
 
 BLOCK_ELEMS = {Q4_0: 32, Q8_0: 32, Q4_K: 256}
 
@@ -239,6 +240,22 @@ class TPComm:
             self.h = None
 
 
+def _info_dict(info: "GgufInfo") -> dict:
+    c = info.cfg
+    cfg = {f: getattr(c, f) for f, _ in ModelCfg._fields_}
+    return {"cfg": cfg, "version": info.version, "context_length": info.context_length,
+            "n_rot": info.n_rot, "tied_output": bool(info.tied_output),
+            "tensor_count": info.tensor_count, "weight_bytes": info.weight_bytes,
+            "architecture": info.architecture.decode()}
+
+
+def gguf_inspect(path: str) -> dict:
+    """Parse a GGUF file's header, metadata and tensor table (no GPU needed)."""
+    info = GgufInfo()
+    check(load().pai_b200_gguf_inspect(os.fsencode(path), C.byref(info)), "gguf_inspect")
+    return _info_dict(info)
+
+
 class Model:
     """LLaMA-shaped decoder resident on one device (one tensor-parallel rank)."""
 
@@ -252,6 +269,19 @@ class Model:
         check(load().pai_b200_model_create(dev.ctx, C.byref(c), tp_rank, tp_size, C.byref(h)),
               "model_create")
         self.h = h.value
+
+    @classmethod
+    def from_gguf(cls, dev: Device, path: str, tp_rank: int = 0, tp_size: int = 1) -> "Model":
+        """Load a LLaMA-family GGUF file's blocks as stored (pai_b200_model_load_gguf)."""
+        info = GgufInfo()
+        h = C.c_void_p()
+        check(load().pai_b200_model_load_gguf(dev.ctx, os.fsencode(path), tp_rank, tp_size, C.byref(h),
+                                              C.byref(info)), "model_load_gguf")
+        self = cls.__new__(cls)
+        self.dev = dev
+        self.cfg = _info_dict(info)["cfg"]
+        self.h = h.value
+        return self
 
     def set_tensor(self, kind: int, layer: int, host: np.ndarray):
         a = np.ascontiguousarray(host)
