@@ -117,7 +117,7 @@ __device__ __forceinline__ void put_result(const V0Args &p, uint64_t r, uint64_t
 template <int BITS, int LAYOUT, int MB>
 __global__ void __launch_bounds__(kThreads) k_gemm_v0(V0Args p) {
   extern __shared__ float sa[];  // [MB][per] activations of this split
-  __shared__ float red[kWarps][kStrip];
+  __shared__ __align__(16) float red[kWarps][kStrip];  // written as float4
   constexpr int U = BITS == 8 ? 4 : 8;  // rows in flight per lane
   using Raw = typename std::conditional<BITS == 8, uint2, uint32_t>::type;
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
