@@ -312,8 +312,10 @@ def v0_sweep(dev, hbm_peak, peak_kind, iters=40):
     """The v0 grouped-scale GEMMs at the config-1 shape (4096x4096, one
     activation row): the registered w8/w4 ops (scales per (k-group,
     column)) and .pai blobs (scales per 32 flat elements), each rotating
-    over enough distinct weight copies to exceed 2x the L2. Plain launches,
-    CUDA events around the timed loop."""
+    over enough distinct weight copies to exceed 2x the L2. Device time:
+    CUDA events around graph replays of the calls (one graph of `iters`
+    calls, so host launch cost is not in the device time); plain_us: the
+    same calls launched one by one from Python."""
     from prosperoai_b200 import _native
     L = _native.load()
     n = k = 4096
@@ -346,6 +348,7 @@ def v0_sweep(dev, hbm_peak, peak_kind, iters=40):
         for i in range(4):
             _native.check(call(i), name)
         dev.sync()
+        # plain launches: one ctypes call each, host-bound at this size
         L.pai_b200_event_record(dev.ctx, e0)
         for i in range(iters):
             call(i)
@@ -353,13 +356,31 @@ def v0_sweep(dev, hbm_peak, peak_kind, iters=40):
         ms = C.c_float()
         _native.check(L.pai_b200_event_elapsed(e0, e1, C.byref(ms)), "elapsed")
         dev.sync()
-        us = ms.value / iters * 1e3
+        plain_us = ms.value / iters * 1e3
+        # device time: the same calls captured in one CUDA graph and replayed
+        graph = C.c_void_p()
+        _native.check(L.pai_b200_graph_begin(dev.ctx), "graph_begin")
+        for i in range(iters):
+            _native.check(call(i), name)
+        _native.check(L.pai_b200_graph_end(dev.ctx, C.byref(graph)), "graph_end")
+        for _ in range(3):
+            _native.check(L.pai_b200_graph_launch(dev.ctx, graph), "graph_launch")
+        dev.sync()
+        reps = 5
+        L.pai_b200_event_record(dev.ctx, e0)
+        for _ in range(reps):
+            L.pai_b200_graph_launch(dev.ctx, graph)
+        L.pai_b200_event_record(dev.ctx, e1)
+        _native.check(L.pai_b200_event_elapsed(e0, e1, C.byref(ms)), "elapsed")
+        dev.sync()
+        L.pai_b200_graph_destroy(graph)
+        us = ms.value / (reps * iters) * 1e3
         alg = vbytes + sbytes + 4 * k + 4 * n
         gbs = alg / (us * 1e-6) / 1e9
         out.append({"op": name, "scales": "per (32-row group, column)" if form == "op"
                     else "per 32 flat elements (.pai blob)", "n": n, "k": k, "rows": 1,
                     "algorithmic_bytes": int(alg), "us": round(us, 2), "gbs": round(gbs, 1),
-                    "frac": round(gbs / hbm_peak, 4), "copies": copies})
+                    "frac": round(gbs / hbm_peak, 4), "plain_us": round(plain_us, 2), "copies": copies})
         for b in bufs:
             for x in b:
                 x.free()

@@ -148,6 +148,17 @@ pai_status_t pai_b200_event_elapsed(void *start, void *stop, float *ms);
  * (graph replays count every kernel node they run). */
 uint64_t pai_b200_launch_count(pai_b200_ctx_t *ctx);
 
+/* CUDA graph capture of the ops enqueued on the context's stream between
+ * begin and end (for sequences of small ops whose host launch cost
+ * exceeds their device time). Ops that would grow the context's scratch
+ * fail during a capture: run each op once before capturing it.
+ * pai_b200_graph_launch replays the graph on the context's stream. */
+typedef struct pai_b200_graph pai_b200_graph_t;
+pai_status_t pai_b200_graph_begin(pai_b200_ctx_t *ctx);
+pai_status_t pai_b200_graph_end(pai_b200_ctx_t *ctx, pai_b200_graph_t **graph);
+pai_status_t pai_b200_graph_launch(pai_b200_ctx_t *ctx, pai_b200_graph_t *graph);
+pai_status_t pai_b200_graph_destroy(pai_b200_graph_t *graph);
+
 /* ---- weight blocks ------------------------------------------------------------- */
 
 /* ggml byte size of numel elements (adapters/llama/gguf.c:563-599);

@@ -83,6 +83,10 @@ SIGNATURES = {
     "pai_b200_event_record": (I32, [P, P]),
     "pai_b200_event_elapsed": (I32, [P, P, C.POINTER(C.c_float)]),
     "pai_b200_launch_count": (U64, [P]),
+    "pai_b200_graph_begin": (I32, [P]),
+    "pai_b200_graph_end": (I32, [P, PP]),
+    "pai_b200_graph_launch": (I32, [P, P]),
+    "pai_b200_graph_destroy": (I32, [P]),
     "pai_b200_block_bytes": (U64, [U32, U64]),
     "pai_b200_quantize": (I32, [U32, P, U64, P]),
     "pai_b200_packed_bytes": (U64, [U32, U64, U64]),

@@ -347,3 +347,48 @@ extern "C" pai_status_t b200_graph_launch(pai_b200_ctx_t *c, void *exec, uint32_
 extern "C" void b200_graph_destroy(void *exec) {
   if (exec) cudaGraphExecDestroy((cudaGraphExec_t)exec);
 }
+
+// ---- public graph capture -------------------------------------------------------------------
+
+struct pai_b200_graph {
+  void *exec;
+  uint32_t kernels;  // this library's kernels per replay
+};
+
+extern "C" pai_status_t pai_b200_graph_begin(pai_b200_ctx_t *c) {
+  if (!c) return b200_fail(PAI_ERR_INVALID_ARG, "graph_begin: NULL");
+  if (c->capturing) return b200_fail(PAI_ERR_INVALID_ARG, "graph_begin: a capture is already open");
+  pai_status_t st = b200_ctx_use_device(c);
+  return st ? st : b200_graph_begin(c);
+}
+
+extern "C" pai_status_t pai_b200_graph_end(pai_b200_ctx_t *c, pai_b200_graph_t **out) {
+  if (!c || !out) return b200_fail(PAI_ERR_INVALID_ARG, "graph_end: NULL");
+  if (!c->capturing) return b200_fail(PAI_ERR_INVALID_ARG, "graph_end: no capture open");
+  pai_b200_graph_t *g = (pai_b200_graph_t *)calloc(1, sizeof(*g));
+  void *exec = nullptr;
+  uint32_t kernels = 0;
+  pai_status_t st = b200_graph_end(c, &exec, &kernels);
+  if (st || !g) {
+    b200_graph_destroy(exec);
+    free(g);
+    return st ? st : b200_fail(PAI_ERR_NOMEM, "graph_end: host allocation");
+  }
+  g->exec = exec;
+  g->kernels = kernels;
+  *out = g;
+  return PAI_OK;
+}
+
+extern "C" pai_status_t pai_b200_graph_launch(pai_b200_ctx_t *c, pai_b200_graph_t *g) {
+  if (!c || !g) return b200_fail(PAI_ERR_INVALID_ARG, "graph_launch: NULL");
+  return b200_graph_launch(c, g->exec, g->kernels);
+}
+
+extern "C" pai_status_t pai_b200_graph_destroy(pai_b200_graph_t *g) {
+  if (g) {
+    b200_graph_destroy(g->exec);
+    free(g);
+  }
+  return PAI_OK;
+}

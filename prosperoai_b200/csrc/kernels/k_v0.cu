@@ -49,6 +49,9 @@ constexpr int kThreads = kWarps * 32;    // 256
 constexpr int kStrip = 32 * kCols;       // 256 columns per CTA
 constexpr int kMaxRows = 8;              // activation rows per launch
 constexpr uint64_t kMaxPer = 1024;       // rows of k per split (activation staging)
+constexpr int kU8 = 8, kU4 = 16;         // rows per lane and batch: 64 B of int8, 64 B of nibbles
+constexpr int kCtasPerSm = 2;            // grid target: about this many CTAs per SM
+constexpr int kSplitLoads = 8;           // partials loaded at once by the split reduction
 
 struct V0Args {
   uint64_t m, n, k;   // m <= kMaxRows
@@ -95,9 +98,19 @@ __device__ __forceinline__ void finish_strip(const V0Args &p) {
   __threadfence();
   const uint64_t j = (uint64_t)blockIdx.x * kStrip + threadIdx.x;
   if (j < p.n) {
+    const uint64_t ys = p.m * p.n;  // stride between splits
     for (uint64_t r = 0; r < p.m; r++) {
+      const float *src = p.part + r * p.n + j;
       float v = 0.0f;
-      for (uint32_t y = 0; y < gridDim.y; y++) v += __ldcg(&p.part[((uint64_t)y * p.m + r) * p.n + j]);
+      uint32_t y = 0;
+      for (; y + kSplitLoads <= gridDim.y; y += kSplitLoads) {  // loads in flight together, added in order
+        float b[kSplitLoads];
+#pragma unroll
+        for (int u = 0; u < kSplitLoads; u++) b[u] = __ldcg(src + (uint64_t)(y + u) * ys);
+#pragma unroll
+        for (int u = 0; u < kSplitLoads; u++) v += b[u];
+      }
+      for (; y < gridDim.y; y++) v += __ldcg(src + (uint64_t)y * ys);
       p.c[r * p.n + j] = v;
     }
   }
@@ -118,13 +131,28 @@ template <int BITS, int LAYOUT, int MB>
 __global__ void __launch_bounds__(kThreads) k_gemm_v0(V0Args p) {
   extern __shared__ float sa[];  // [MB][per] activations of this split
   __shared__ __align__(16) float red[kWarps][kStrip];  // written as float4
-  constexpr int U = BITS == 8 ? 4 : 8;  // rows in flight per lane
+  constexpr int U = BITS == 8 ? kU8 : kU4;
   using Raw = typename std::conditional<BITS == 8, uint2, uint32_t>::type;
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint64_t j0 = (uint64_t)blockIdx.x * kStrip + lane * kCols;
   const uint64_t t0 = (uint64_t)blockIdx.y * p.per, t1 = min(p.k, t0 + p.per);
+  const uint64_t tf = t0 + warp;
   const bool live = j0 < p.n;
+  // U rows of this lane's 8 columns starting at row t (rows t, t+8, ...)
+  auto load_batch = [&](Raw *raw, uint64_t t) {
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const uint64_t tu = t + (uint64_t)kWarps * u;
+      if (live && tu < t1)
+        raw[u] = __ldcs(reinterpret_cast<const Raw *>(p.w + (BITS == 8 ? tu * p.n + j0 : (tu * p.n + j0) >> 1)));
+      else
+        raw[u] = Raw{};  // decodes to zeros
+    }
+  };
   pdl_wait();  // a no-op unless launched as a programmatic dependent
+  // the first weight batch is in flight while the activations are staged
+  Raw nxt[U];
+  load_batch(nxt, tf);
   for (uint32_t i = threadIdx.x; i < MB * p.per; i += kThreads) {
     const uint32_t r = i / (uint32_t)p.per, tt = i - r * (uint32_t)p.per;
     sa[i] = (r < p.m && t0 + tt < t1) ? __ldg(p.a + r * p.k + t0 + tt) : 0.0f;
@@ -142,7 +170,6 @@ __global__ void __launch_bounds__(kThreads) k_gemm_v0(V0Args p) {
   const float *sf = reinterpret_cast<const float *>(p.s);
   float sc[kCols];
   uint64_t gnext = 0, qg = 0, rg = 0, dq = 0, dr = 0;
-  const uint64_t tf = t0 + warp;
   if (LAYOUT == kFlatScales) {
     const uint64_t f = tf * p.n + j0, step = (uint64_t)kWarps * p.n;
     qg = f / p.g;
@@ -154,14 +181,8 @@ __global__ void __launch_bounds__(kThreads) k_gemm_v0(V0Args p) {
   for (uint64_t t = tf; t < t1; t += (uint64_t)kWarps * U) {
     Raw raw[U];
 #pragma unroll
-    for (int u = 0; u < U; u++) {
-      const uint64_t tu = t + (uint64_t)kWarps * u;
-      if (live && tu < t1) {
-        raw[u] = __ldcs(reinterpret_cast<const Raw *>(p.w + (BITS == 8 ? tu * p.n + j0 : (tu * p.n + j0) >> 1)));
-      } else {
-        raw[u] = Raw{};  // decodes to zeros
-      }
-    }
+    for (int u = 0; u < U; u++) raw[u] = nxt[u];
+    if (t + (uint64_t)kWarps * U < t1) load_batch(nxt, t + (uint64_t)kWarps * U);  // next batch in flight
 #pragma unroll
     for (int u = 0; u < U; u++) {
       const uint64_t tu = t + (uint64_t)kWarps * u;
@@ -283,8 +304,8 @@ pai_status_t gemm_v0(pai_b200_ctx_t *ctx, uint32_t bits, int layout, uint64_t m,
   const bool vec = n % kCols == 0 && wa % (bits == 8 ? 8 : 4) == 0 &&
                    (layout == kOpScales ? sa % 16 == 0 : (sa % 4 == 0 && g % kCols == 0));
   const uint64_t strips = (n + kStrip - 1) / kStrip;
-  // about 4 CTAs per SM, at least 64 rows per split, at most kMaxPer
-  uint64_t splits = std::max<uint64_t>(1, (4 * 148 + strips - 1) / strips);
+  // about kCtasPerSm CTAs per SM, at least 64 rows per split, at most kMaxPer
+  uint64_t splits = std::max<uint64_t>(1, (kCtasPerSm * 148 + strips - 1) / strips);
   splits = std::min<uint64_t>(splits, std::max<uint64_t>(1, k / 64));
   splits = std::max<uint64_t>(splits, (k + kMaxPer - 1) / kMaxPer);
   uint64_t per = (k + splits - 1) / splits;

@@ -122,3 +122,31 @@ def test_v0_argument_errors(dev):
         dev.gemm_v0(2, 0, 1, 8, 8, a, w, c)
     assert e.value.status == -3  # PAI_ERR_UNSUPPORTED: v0 runs q8 and q4 only
     assert _native.load().pai_b200_v0_blob_bytes(2, 0, 64) == 0
+
+
+def test_graph_capture_replays_the_op(dev):
+    """pai_b200_graph_begin/end/launch: two ops captured once, replayed,
+    give the bits of the direct calls."""
+    import ctypes as C
+    L = _native.load()
+    rng = np.random.default_rng(9)
+    m, n, k = 2, 1024, 512
+    a = dev.put(rng.standard_normal((m, k)).astype(np.float32))
+    wq, sc = random_wq(rng, 8, n, k, 32)
+    w, s = dev.put(wq), dev.put(sc)
+    c1, c2 = dev.alloc(m * n * 4), dev.alloc(m * n * 4)
+    dev.gemm_wq(8, m, n, k, a, w, s, 32, c1)
+    direct = c1.download(np.float32)
+    g = C.c_void_p()
+    _native.check(L.pai_b200_graph_begin(dev.ctx), "graph_begin")
+    dev.gemm_wq(8, m, n, k, a, w, s, 32, c2)
+    dev.gemm_wq(8, m, n, k, a, w, s, 32, c1)
+    _native.check(L.pai_b200_graph_end(dev.ctx, C.byref(g)), "graph_end")
+    before = L.pai_b200_launch_count(dev.ctx)
+    for _ in range(3):
+        _native.check(L.pai_b200_graph_launch(dev.ctx, g), "graph_launch")
+    dev.sync()
+    assert L.pai_b200_launch_count(dev.ctx) - before == 3 * 2
+    L.pai_b200_graph_destroy(g)
+    assert np.array_equal(c2.download(np.float32).view(np.uint32), direct.view(np.uint32))
+    assert np.array_equal(c1.download(np.float32).view(np.uint32), direct.view(np.uint32))
