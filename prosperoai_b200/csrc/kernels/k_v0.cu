@@ -48,7 +48,8 @@ constexpr int kWarps = 8;                // warps per CTA; warp w takes rows t0 
 constexpr int kThreads = kWarps * 32;    // 256
 constexpr int kStrip = 32 * kCols;       // 256 columns per CTA
 constexpr int kMaxRows = 8;              // activation rows per launch
-constexpr uint64_t kMaxPer = 1024;       // rows of k per split (activation staging)
+constexpr uint64_t kMaxPer = 512;        // rows of k per split (activation staging)
+constexpr uint64_t kMaxScaleGroups = 16; // k-groups of scales one split stages (kOpScales)
 constexpr int kU8 = 8, kU4 = 16;         // rows per lane and batch: 64 B of int8, 64 B of nibbles
 constexpr int kCtasPerSm = 2;            // grid target: about this many CTAs per SM
 constexpr int kSplitLoads = 8;           // partials loaded at once by the split reduction
@@ -125,37 +126,80 @@ __device__ __forceinline__ void put_result(const V0Args &p, uint64_t r, uint64_t
 }
 
 // Vector path: n % 8 == 0, values 8-byte (int8) or 4-byte (nibbles)
-// aligned, scales 16-byte (kOpScales) or 4-byte aligned with g % 8 == 0
-// (kFlatScales, so a lane's 8 columns of a row share one scale).
+// aligned, and g a multiple of 8 (kFlatScales: a lane's 8 columns of a row
+// share one scale) or at least 8 (kOpScales: a warp's row step of 8 crosses
+// at most one group boundary), scales 16-byte (kOpScales) or 4-byte
+// aligned. No scale load waits on the critical path: kOpScales stages the
+// split's (group, column) scales in shared memory with the activations;
+// kFlatScales loads each row's scale together with the row's weights.
 template <int BITS, int LAYOUT, int MB>
 __global__ void __launch_bounds__(kThreads) k_gemm_v0(V0Args p) {
-  extern __shared__ float sa[];  // [MB][per] activations of this split
+  extern __shared__ __align__(16) float dyn[];  // [MB][per] activations, then [ngr][kStrip] scales (kOpScales)
   __shared__ __align__(16) float red[kWarps][kStrip];  // written as float4
   constexpr int U = BITS == 8 ? kU8 : kU4;
   using Raw = typename std::conditional<BITS == 8, uint2, uint32_t>::type;
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const uint64_t j0 = (uint64_t)blockIdx.x * kStrip + lane * kCols;
+  const uint64_t c0 = (uint64_t)blockIdx.x * kStrip, j0 = c0 + lane * kCols;
   const uint64_t t0 = (uint64_t)blockIdx.y * p.per, t1 = min(p.k, t0 + p.per);
   const uint64_t tf = t0 + warp;
   const bool live = j0 < p.n;
-  // U rows of this lane's 8 columns starting at row t (rows t, t+8, ...)
-  auto load_batch = [&](Raw *raw, uint64_t t) {
+  const float *sf = reinterpret_cast<const float *>(p.s);
+  float *sa = dyn;
+  float *ss = dyn + MB * p.per;
+
+  // kFlatScales cursor: (f / g, f % g) of this lane's first column f of the
+  // next row to load; rows advance by kWarps
+  uint64_t qg = 0, rg = 0, dq = 0, dr = 0;
+  if (LAYOUT == kFlatScales) {
+    const uint64_t f = tf * p.n + j0, step = (uint64_t)kWarps * p.n;
+    qg = f / p.g;
+    rg = f - qg * p.g;
+    dq = step / p.g;
+    dr = step - dq * p.g;
+  }
+  // U rows of this lane's 8 columns from row t (rows t, t+8, ...), and for
+  // kFlatScales each row's scale
+  auto load_batch = [&](Raw *raw, float *rs, uint64_t t) {
 #pragma unroll
     for (int u = 0; u < U; u++) {
       const uint64_t tu = t + (uint64_t)kWarps * u;
-      if (live && tu < t1)
-        raw[u] = __ldcs(reinterpret_cast<const Raw *>(p.w + (BITS == 8 ? tu * p.n + j0 : (tu * p.n + j0) >> 1)));
-      else
-        raw[u] = Raw{};  // decodes to zeros
+      const bool in = tu < t1;
+      raw[u] = (live && in) ? __ldcs(reinterpret_cast<const Raw *>(
+                                  p.w + (BITS == 8 ? tu * p.n + j0 : (tu * p.n + j0) >> 1)))
+                            : Raw{};  // decodes to zeros
+      if (LAYOUT == kFlatScales) {
+        rs[u] = (live && in) ? __ldg(sf + qg) : 0.0f;
+        if (in) {
+          rg += dr;
+          qg += dq;
+          if (rg >= p.g) {
+            rg -= p.g;
+            qg++;
+          }
+        }
+      }
     }
   };
   pdl_wait();  // a no-op unless launched as a programmatic dependent
-  // the first weight batch is in flight while the activations are staged
+  // the first weight batch is in flight while activations (and scales) are staged
   Raw nxt[U];
-  load_batch(nxt, tf);
+  float nsc[U];
+  load_batch(nxt, nsc, tf);
   for (uint32_t i = threadIdx.x; i < MB * p.per; i += kThreads) {
     const uint32_t r = i / (uint32_t)p.per, tt = i - r * (uint32_t)p.per;
     sa[i] = (r < p.m && t0 + tt < t1) ? __ldg(p.a + r * p.k + t0 + tt) : 0.0f;
+  }
+  uint64_t gnext = 0;
+  uint32_t gl = 0;
+  if (LAYOUT == kOpScales) {
+    const uint64_t gfirst = t0 / p.g, ngr = (t1 - 1) / p.g - gfirst + 1, ngroups = (p.k + p.g - 1) / p.g;
+    for (uint32_t i = threadIdx.x; i < ngr * kStrip; i += kThreads) {
+      const uint64_t gi = gfirst + i / kStrip, col = c0 + i % kStrip;
+      ss[i] = (col < p.n && gi < ngroups) ? __ldg(sf + gi * p.n + col) : 0.0f;
+    }
+    const uint64_t gi = tf / p.g;
+    gl = (uint32_t)(gi - gfirst);
+    gnext = (gi + 1) * p.g;
   }
   __syncthreads();
 
@@ -164,25 +208,23 @@ __global__ void __launch_bounds__(kThreads) k_gemm_v0(V0Args p) {
   for (int r = 0; r < MB; r++)
 #pragma unroll
     for (int e = 0; e < kCols; e++) acc[r][e] = 0.0f;
-
-  // scale cursor: kOpScales keeps the 8 scales of the current k-group;
-  // kFlatScales keeps (f / g, f % g) of this lane's first column f of the row
-  const float *sf = reinterpret_cast<const float *>(p.s);
   float sc[kCols];
-  uint64_t gnext = 0, qg = 0, rg = 0, dq = 0, dr = 0;
-  if (LAYOUT == kFlatScales) {
-    const uint64_t f = tf * p.n + j0, step = (uint64_t)kWarps * p.n;
-    qg = f / p.g;
-    rg = f - qg * p.g;
-    dq = step / p.g;
-    dr = step - dq * p.g;
+  if (LAYOUT == kOpScales) {
+    const float4 s0 = *reinterpret_cast<const float4 *>(ss + gl * kStrip + lane * kCols);
+    const float4 s1 = *reinterpret_cast<const float4 *>(ss + gl * kStrip + lane * kCols + 4);
+    sc[0] = s0.x, sc[1] = s0.y, sc[2] = s0.z, sc[3] = s0.w;
+    sc[4] = s1.x, sc[5] = s1.y, sc[6] = s1.z, sc[7] = s1.w;
   }
 
   for (uint64_t t = tf; t < t1; t += (uint64_t)kWarps * U) {
     Raw raw[U];
+    float rsc[U];
 #pragma unroll
-    for (int u = 0; u < U; u++) raw[u] = nxt[u];
-    if (t + (uint64_t)kWarps * U < t1) load_batch(nxt, t + (uint64_t)kWarps * U);  // next batch in flight
+    for (int u = 0; u < U; u++) {
+      raw[u] = nxt[u];
+      rsc[u] = nsc[u];
+    }
+    if (t + (uint64_t)kWarps * U < t1) load_batch(nxt, nsc, t + (uint64_t)kWarps * U);  // next batch in flight
 #pragma unroll
     for (int u = 0; u < U; u++) {
       const uint64_t tu = t + (uint64_t)kWarps * u;
@@ -206,18 +248,13 @@ __global__ void __launch_bounds__(kThreads) k_gemm_v0(V0Args p) {
       }
       const uint32_t tl = (uint32_t)(tu - t0);
       if constexpr (LAYOUT == kOpScales) {
-        if (tu >= gnext) {  // uniform across the warp
-          const uint64_t gi = tu / p.g;
-          gnext = (gi + 1) * p.g;
-          if (live) {
-            const float4 s0 = __ldg(reinterpret_cast<const float4 *>(sf + gi * p.n + j0));
-            const float4 s1 = __ldg(reinterpret_cast<const float4 *>(sf + gi * p.n + j0 + 4));
-            sc[0] = s0.x, sc[1] = s0.y, sc[2] = s0.z, sc[3] = s0.w;
-            sc[4] = s1.x, sc[5] = s1.y, sc[6] = s1.z, sc[7] = s1.w;
-          } else {
-#pragma unroll
-            for (int e = 0; e < kCols; e++) sc[e] = 0.0f;
-          }
+        if (tu >= gnext) {  // uniform across the warp; g >= 8, so one group at most
+          gl++;
+          gnext += p.g;
+          const float4 s0 = *reinterpret_cast<const float4 *>(ss + gl * kStrip + lane * kCols);
+          const float4 s1 = *reinterpret_cast<const float4 *>(ss + gl * kStrip + lane * kCols + 4);
+          sc[0] = s0.x, sc[1] = s0.y, sc[2] = s0.z, sc[3] = s0.w;
+          sc[4] = s1.x, sc[5] = s1.y, sc[6] = s1.z, sc[7] = s1.w;
         }
 #pragma unroll
         for (int e = 0; e < kCols; e++) {
@@ -226,16 +263,9 @@ __global__ void __launch_bounds__(kThreads) k_gemm_v0(V0Args p) {
           for (int r = 0; r < MB; r++) acc[r][e] = fmaf(sa[r * p.per + tl], we, acc[r][e]);
         }
       } else {
-        const float srow = live ? __ldg(sf + qg) : 0.0f;
-        rg += dr;
-        qg += dq;
-        if (rg >= p.g) {
-          rg -= p.g;
-          qg++;
-        }
 #pragma unroll
         for (int r = 0; r < MB; r++) {
-          const float as = sa[r * p.per + tl] * srow;
+          const float as = sa[r * p.per + tl] * rsc[u];
 #pragma unroll
           for (int e = 0; e < kCols; e++) acc[r][e] = fmaf(as, v[e], acc[r][e]);
         }
@@ -254,7 +284,7 @@ __global__ void __launch_bounds__(kThreads) k_gemm_v0(V0Args p) {
     float s = 0.0f;
 #pragma unroll
     for (int w = 0; w < kWarps; w++) s += red[w][threadIdx.x];
-    const uint64_t j = (uint64_t)blockIdx.x * kStrip + threadIdx.x;
+    const uint64_t j = c0 + threadIdx.x;
     if (j < p.n) put_result(p, r, j, s);
     __syncthreads();
   }
@@ -287,9 +317,14 @@ __global__ void __launch_bounds__(kThreads) k_gemm_v0_any(V0Args p) {
   finish_strip(p);
 }
 
+// Groups of k one split of `per` rows can touch (its first row need not
+// start a group).
+inline uint64_t split_groups(uint64_t per, uint64_t g) { return (per + g - 1) / g + 1; }
+
 template <int BITS, int LAYOUT>
 cudaError_t launch_vec(pai_b200_ctx_t *ctx, dim3 grid, uint32_t mb, const V0Args &a) {
-  const size_t smem = (size_t)mb * a.per * sizeof(float);
+  size_t smem = (size_t)mb * a.per * sizeof(float);
+  if (LAYOUT == kOpScales) smem += split_groups(a.per, a.g) * kStrip * sizeof(float);
   switch (mb) {
     case 1: return b200_launch(ctx, k_gemm_v0<BITS, LAYOUT, 1>, grid, dim3(kThreads), smem, a);
     case 2: return b200_launch(ctx, k_gemm_v0<BITS, LAYOUT, 2>, grid, dim3(kThreads), smem, a);
@@ -302,12 +337,16 @@ pai_status_t gemm_v0(pai_b200_ctx_t *ctx, uint32_t bits, int layout, uint64_t m,
                      const float *a, const void *w, const void *s, uint64_t g, float *c, const char *what) {
   const uintptr_t wa = (uintptr_t)w, sa = (uintptr_t)s;
   const bool vec = n % kCols == 0 && wa % (bits == 8 ? 8 : 4) == 0 &&
-                   (layout == kOpScales ? sa % 16 == 0 : (sa % 4 == 0 && g % kCols == 0));
+                   (layout == kOpScales ? (sa % 16 == 0 && g >= kCols) : (sa % 4 == 0 && g % kCols == 0));
   const uint64_t strips = (n + kStrip - 1) / kStrip;
-  // about kCtasPerSm CTAs per SM, at least 64 rows per split, at most kMaxPer
+  // about kCtasPerSm CTAs per SM, at least 64 rows per split, at most
+  // kMaxPer (and, with staged scales, at most kMaxScaleGroups groups)
+  const uint64_t max_per = vec && layout == kOpScales
+                               ? std::min<uint64_t>(kMaxPer, (kMaxScaleGroups - 2) * g / kWarps * kWarps)
+                               : kMaxPer;
   uint64_t splits = std::max<uint64_t>(1, (kCtasPerSm * 148 + strips - 1) / strips);
   splits = std::min<uint64_t>(splits, std::max<uint64_t>(1, k / 64));
-  splits = std::max<uint64_t>(splits, (k + kMaxPer - 1) / kMaxPer);
+  splits = std::max<uint64_t>(splits, (k + max_per - 1) / max_per);
   uint64_t per = (k + splits - 1) / splits;
   per = (per + kWarps - 1) / kWarps * kWarps;
   splits = (k + per - 1) / per;
