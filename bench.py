@@ -389,6 +389,34 @@ def v0_sweep(dev, hbm_peak, peak_kind, iters=40):
     return {"peak": hbm_peak, "peak_kind": peak_kind, "unit": "GB/s", "shapes": out}
 
 
+def prefill_timing(dev, sess, prompts, reps=3):
+    """Time-to-first-token of the config-5 prompt through
+    pai_b200_session_prefill (tokens from host memory, the next token read
+    back), against stepping the prompt one decode step per position.
+    CUDA events around each call; the best of `reps` after one warm-up."""
+    from prosperoai_b200 import _native
+    L = _native.load()
+    e0, e1 = C.c_void_p(), C.c_void_p()
+    L.pai_b200_event_create(dev.ctx, C.byref(e0))
+    L.pai_b200_event_create(dev.ctx, C.byref(e1))
+    times = []
+    for i in range(reps + 1):
+        sess.reset()
+        dev.sync()
+        L.pai_b200_event_record(dev.ctx, e0)
+        sess.prefill(prompts)
+        L.pai_b200_event_record(dev.ctx, e1)
+        ms = C.c_float()
+        _native.check(L.pai_b200_event_elapsed(e0, e1, C.byref(ms)), "elapsed")
+        if i:
+            times.append(ms.value)
+    best = min(times)
+    B, P = prompts.shape
+    return {"api": "pai_b200_session_prefill", "sequences": B, "positions": P, "ms": round(best, 3),
+            "tokens_per_s": round(B * P / (best * 1e-3), 1),
+            "path": "Q4_0 layers: tcgen05 GEMM over all prompt rows; attention over the fp16 cache"}
+
+
 def cpu_baseline_port(dev, steps=3, prompt=24):
     """The CPU restatement (oracle/, bit-identical to the reference ops)
     on a bounded sample of the same decode: one 8B-shaped layer plus 1/32
@@ -496,6 +524,10 @@ def gpu_arm(args):
     # take a fraction of one, so sampling spans the prompt, warm-up and
     # timed steps (the same kernels throughout)
     clk = Clocks(local).__enter__()
+    prefill = None
+    if not tp and not args.no_roofline:
+        prefill = prefill_timing(dev, sess, prompts)
+        sess.reset()  # the stepped prompt below overwrites the cache from position 0
     for p in range(P):  # prompt positions, untimed
         sess.set_tokens(prompts[:, p])
         sess.run(1)
@@ -599,6 +631,7 @@ def gpu_arm(args):
             "gpu_launches": int(launches),
             "roofline": roof,
             "prefill_gemm": gemm,
+            "prompt_prefill": prefill,
             "decode_variants": variants,
             "gemv_configs": sweep,
             "v0_gemm": v0,

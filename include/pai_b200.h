@@ -488,6 +488,19 @@ pai_status_t pai_b200_session_step(pai_b200_session_t *s, const int32_t *tokens,
  * The first step reads the device token buffer set by the last
  * session_step or session_set_tokens. Asynchronous. */
 pai_status_t pai_b200_session_run(pai_b200_session_t *s, uint32_t steps);
+/* Prompt prefill: n positions of every sequence (tokens[batch][n], host)
+ * appended in one pass per layer instead of n decode steps -- RMSNorm over
+ * all rows, the layer matrices as GEMMs over all rows (the tcgen05 GEMM
+ * for Q4_0 layers, bf16 tiles with fp32 accumulation; the batched GEMV for
+ * Q8_0/Q4_K), RoPE and the fp16 K/V append for every position, causal
+ * attention over the cache, SiLU*up, residual adds. next[batch] receives
+ * the greedy token after the last position, which is also the input of the
+ * next pai_b200_session_run step. Equivalent to stepping the prompt; with
+ * Q4_0 layers the bf16 GEMM tiles put the hidden state within about 1e-2
+ * (max-abs-rel) of the stepped result. Single GPU: tensor-parallel
+ * sessions return PAI_ERR_UNSUPPORTED and step the prompt. */
+pai_status_t pai_b200_session_prefill(pai_b200_session_t *s, const int32_t *tokens, uint32_t n,
+                                      int32_t *next);
 pai_status_t pai_b200_session_set_tokens(pai_b200_session_t *s,
                                          const int32_t *tokens);
 pai_status_t pai_b200_session_get_tokens(pai_b200_session_t *s, int32_t *tokens);

@@ -141,6 +141,7 @@ SIGNATURES = {
     "pai_b200_session_reset": (I32, [P]),
     "pai_b200_session_step": (I32, [P, P, P, P]),
     "pai_b200_session_run": (I32, [P, U32]),
+    "pai_b200_session_prefill": (I32, [P, P, U32, P]),
     "pai_b200_session_set_tokens": (I32, [P, P]),
     "pai_b200_session_get_tokens": (I32, [P, P]),
     "pai_b200_session_hidden": (P, [P]),

@@ -326,6 +326,15 @@ class Session:
     def run(self, steps: int):
         check(load().pai_b200_session_run(self.h, steps), "session_run")
 
+    def prefill(self, tokens) -> np.ndarray:
+        """Append a prompt ([batch][n] token ids) in one pass per layer; returns
+        the greedy next token of every sequence (pai_b200_session_prefill)."""
+        t = np.ascontiguousarray(tokens, np.int32).reshape(self.batch, -1)
+        nxt = np.empty(self.batch, np.int32)
+        check(load().pai_b200_session_prefill(self.h, t.ctypes.data, t.shape[1], nxt.ctypes.data),
+              "session_prefill")
+        return nxt
+
     def set_tokens(self, tokens):
         t = np.ascontiguousarray(tokens, np.int32)
         check(load().pai_b200_session_set_tokens(self.h, t.ctypes.data), "set_tokens")

@@ -231,6 +231,17 @@ float *b200_tp_xbuf_slot(void *buf, uint32_t slot, uint64_t cap);
  * buffer; bufs[r] = rank r's buffer as mapped in this process. */
 pai_status_t b200_launch_tp_allreduce_add(pai_b200_ctx_t *ctx, void *const *bufs, uint32_t rank, uint32_t nranks,
                                           uint32_t slot, uint64_t cap, float *x, uint64_t n);
+/* Prompt prefill (kernels/k_prefill.cu). Row r = b * rows_per_seq + i is
+ * position p0 + i of sequence b; qkv rows are [(h + 2 hk) hd]. */
+pai_status_t b200_launch_prefill_rope_append(pai_b200_ctx_t *ctx, uint32_t rows, uint32_t rows_per_seq,
+                                             uint32_t p0, uint32_t h, uint32_t hk, uint32_t hd, float *qkv,
+                                             const float *cos_t, const float *sin_t, uint16_t *kc, uint16_t *vc,
+                                             uint64_t cap, uint64_t seq_stride);
+pai_status_t b200_launch_attn_prefill(pai_b200_ctx_t *ctx, uint32_t rows, uint32_t rows_per_seq, uint32_t p0,
+                                      uint32_t h, uint32_t hk, uint32_t hd, const float *qkv, const uint16_t *kc,
+                                      const uint16_t *vc, uint64_t cap, uint64_t seq_stride, float *out);
+pai_status_t b200_launch_silu_glu_rows(pai_b200_ctx_t *ctx, uint64_t rows, uint32_t ff, const float *gu,
+                                       float *hout);
 pai_status_t b200_launch_step_tail(pai_b200_ctx_t *ctx, uint32_t batch,
                                    int32_t *tok_out, int32_t *tok_in, int32_t *pos);
 pai_status_t b200_launch_synth_normal(pai_b200_ctx_t *ctx, float *dst, uint64_t rows,

@@ -402,6 +402,14 @@ struct pai_b200_session {
   void *graph;
   uint32_t graph_kernels;
   pai_b200_tp_t *tp; /* tensor-parallel communicator, NULL on one GPU */
+  /* prefill scratch (allocated by the first prefill): rows of hidden state,
+   * normed rows, q|k|v, attention output, gate|up, silu*up, o/down output,
+   * token ids, and the GEMV operand of 8 rows */
+  uint32_t pf_rows;
+  float *pf_x, *pf_xn, *pf_qkv, *pf_att, *pf_gu, *pf_h, *pf_tmp;
+  int32_t *pf_tok, *pf_htok;
+  void *pf_xq_buf;
+  b200_xq_t pf_xq;
 };
 
 /* Tensor-parallel hooks (csrc/host/b200_tp.c). */
@@ -590,6 +598,16 @@ pai_status_t pai_b200_session_destroy(pai_b200_session_t *s) {
   pai_b200_free(ctx, s->sin_t);
   pai_b200_free(ctx, s->kc);
   pai_b200_host_free(ctx, s->htok);
+  pai_b200_free(ctx, s->pf_x);
+  pai_b200_free(ctx, s->pf_xn);
+  pai_b200_free(ctx, s->pf_qkv);
+  pai_b200_free(ctx, s->pf_att);
+  pai_b200_free(ctx, s->pf_gu);
+  pai_b200_free(ctx, s->pf_h);
+  pai_b200_free(ctx, s->pf_tmp);
+  pai_b200_free(ctx, s->pf_tok);
+  pai_b200_free(ctx, s->pf_xq_buf);
+  pai_b200_host_free(ctx, s->pf_htok);
   free(s);
   return PAI_OK;
 }
@@ -657,3 +675,120 @@ pai_status_t pai_b200_session_step(pai_b200_session_t *s, const int32_t *tokens,
 }
 
 const float *pai_b200_session_hidden(const pai_b200_session_t *s) { return s ? s->x : NULL; }
+
+/* ---- prompt prefill ------------------------------------------------------------------ */
+
+/* Rows of prompt positions per pass: the prefill scratch holds this many
+ * rows (all sequences); a longer prompt runs in several passes, each
+ * attending over the cache the earlier passes filled. */
+#define PF_MAX_ROWS 2048u
+
+static pai_status_t prefill_alloc(pai_b200_session_t *s) {
+  pai_b200_model_t *m = s->m;
+  pai_b200_ctx_t *ctx = m->ctx;
+  const uint64_t R = PF_MAX_ROWS, E = m->cfg.n_embd;
+  const uint64_t kmax = E > m->k_o ? (E > m->ffl ? E : m->ffl) : (m->k_o > m->ffl ? m->k_o : m->ffl);
+  pai_status_t st = PAI_OK;
+  if (s->pf_x) return PAI_OK;
+  SALLOC(s->pf_x, R * E * 4);
+  SALLOC(s->pf_xn, R * E * 4);
+  SALLOC(s->pf_qkv, R * m->n_qkv * 4);
+  SALLOC(s->pf_att, R * m->k_o * 4);
+  SALLOC(s->pf_gu, R * 2 * m->ffl * 4);
+  SALLOC(s->pf_h, R * m->ffl * 4);
+  SALLOC(s->pf_tmp, R * E * 4);
+  SALLOC(s->pf_tok, R * 4);
+  SALLOC(s->pf_xq_buf, b200_xq_bytes(8, kmax));
+  if (!st) st = pai_b200_host_alloc(ctx, R * 4, (void **)&s->pf_htok);
+  if (!st) s->pf_rows = PF_MAX_ROWS;
+  return st;
+}
+
+/* Y[rows][n] = X[rows][k] . W^T over a packed layer matrix: the tcgen05
+ * GEMM for Q4_0 weights, else the GEMV in groups of 8 rows (epi as in the
+ * decode step; residual adds Y's old value when epi is B200_EPI_RESIDUAL,
+ * SILU_GLU writes n/2 values per row). */
+static pai_status_t rows_matmul(pai_b200_session_t *s, uint32_t type, uint32_t rows, uint64_t n, uint64_t k,
+                                const void *w, const float *x, float *y, int epi) {
+  pai_b200_model_t *m = s->m;
+  pai_b200_ctx_t *ctx = m->ctx;
+  pai_status_t st = PAI_OK;
+  if (type == PAI_B200_Q4_0) {
+    float *dst = epi == B200_EPI_STORE ? y : (epi == B200_EPI_RESIDUAL ? s->pf_tmp : s->pf_gu);
+    st = pai_b200_gemm_q4_0_f32(ctx, rows, n, k, x, w, dst);
+    if (!st && epi == B200_EPI_RESIDUAL) st = pai_b200_vecadd_f32(ctx, y, dst, y, (uint64_t)rows * n);
+    if (!st && epi == B200_EPI_SILU_GLU) st = b200_launch_silu_glu_rows(ctx, rows, (uint32_t)(n / 2), dst, y);
+    return st;
+  }
+  const uint64_t ystride = epi == B200_EPI_SILU_GLU ? n / 2 : n;
+  for (uint32_t r0 = 0; r0 < rows && !st; r0 += 8) {
+    const uint32_t b = rows - r0 < 8 ? rows - r0 : 8;
+    b200_xq_t xq = b200_xq_view(s->pf_xq_buf, b, k);
+    st = b200_launch_xprep(ctx, b, k, x + (uint64_t)r0 * k, &xq);
+    if (!st)
+      st = b200_launch_gemv(ctx, type, b, n, k, w, &xq, epi == B200_EPI_RESIDUAL ? y + (uint64_t)r0 * ystride : NULL,
+                            y + (uint64_t)r0 * ystride, epi, NULL);
+  }
+  return st;
+}
+
+pai_status_t pai_b200_session_prefill(pai_b200_session_t *s, const int32_t *tokens, uint32_t n, int32_t *next) {
+  if (!s || !tokens || !next || n == 0) return b200_fail(PAI_ERR_INVALID_ARG, "session_prefill: NULL or empty");
+  pai_b200_model_t *m = s->m;
+  pai_b200_ctx_t *ctx = m->ctx;
+  const pai_b200_model_cfg_t *c = &m->cfg;
+  const uint32_t B = s->batch, E = c->n_embd, hd = c->head_dim;
+  if (m->tp > 1) return b200_fail(PAI_ERR_UNSUPPORTED, "session_prefill: tensor-parallel sessions step the prompt");
+  if ((uint64_t)s->pos + n > s->max_ctx)
+    return b200_fail(PAI_ERR_INVALID_ARG, "session_prefill: %u positions from %u exceed the %u-position cache", n,
+                     s->pos, s->max_ctx);
+  for (uint64_t i = 0; i < (uint64_t)B * n; i++)
+    if (tokens[i] < 0 || (uint32_t)tokens[i] >= c->vocab)
+      return b200_fail(PAI_ERR_INVALID_ARG, "session_prefill: token %d outside vocab %u", tokens[i], c->vocab);
+  pai_status_t st = prefill_alloc(s);
+  const uint32_t per_pass = PF_MAX_ROWS / B;
+  for (uint32_t done = 0; !st && done < n;) {
+    const uint32_t mc = n - done < per_pass ? n - done : per_pass, rows = B * mc, p0 = s->pos;
+    for (uint32_t b = 0; b < B; b++)
+      memcpy(s->pf_htok + (uint64_t)b * mc, tokens + (uint64_t)b * n + done, (uint64_t)mc * 4);
+    st = pai_b200_memcpy_h2d(ctx, s->pf_tok, s->pf_htok, (uint64_t)rows * 4);
+    if (!st) st = b200_launch_embed(ctx, c->etype, rows, c->vocab, E, m->tok_embd, s->pf_tok, s->pf_x);
+    for (uint32_t l = 0; !st && l < c->n_layer; l++) {
+      uint16_t *kc = s->kc + (uint64_t)l * s->layer_stride, *vc = s->vc + (uint64_t)l * s->layer_stride;
+      st = b200_launch_rmsnorm_xq(ctx, rows, E, s->pf_x, m->attn_norm[l], c->eps, s->pf_xn, NULL);
+      if (!st) st = rows_matmul(s, c->wtype, rows, m->n_qkv, E, m->wqkv[l], s->pf_xn, s->pf_qkv, B200_EPI_STORE);
+      if (!st)
+        st = b200_launch_prefill_rope_append(ctx, rows, mc, p0, m->hl, m->hkl, hd, s->pf_qkv, s->cos_t, s->sin_t, kc,
+                                             vc, s->max_ctx, s->seq_stride);
+      if (!st)
+        st = b200_launch_attn_prefill(ctx, rows, mc, p0, m->hl, m->hkl, hd, s->pf_qkv, kc, vc, s->max_ctx,
+                                      s->seq_stride, s->pf_att);
+      if (!st) st = rows_matmul(s, c->wtype, rows, E, m->k_o, m->wo[l], s->pf_att, s->pf_x, B200_EPI_RESIDUAL);
+      if (!st) st = b200_launch_rmsnorm_xq(ctx, rows, E, s->pf_x, m->ffn_norm[l], c->eps, s->pf_xn, NULL);
+      if (!st)
+        st = rows_matmul(s, c->wtype, rows, 2ull * m->ffl, E, m->wgu[l], s->pf_xn, s->pf_h, B200_EPI_SILU_GLU);
+      if (!st) st = rows_matmul(s, c->wtype, rows, E, m->ffl, m->wdown[l], s->pf_h, s->pf_x, B200_EPI_RESIDUAL);
+    }
+    /* the last position of each sequence becomes the decode state */
+    for (uint32_t b = 0; !st && b < B; b++)
+      st = pai_b200_memcpy_d2d(ctx, s->x + (uint64_t)b * E, s->pf_x + ((uint64_t)b * mc + mc - 1) * E,
+                               (uint64_t)E * 4);
+    if (!st) {
+      s->pos += mc;
+      done += mc;
+    }
+  }
+  /* logits of the last position, greedy token; it is also the next decode
+   * step's input, and the device position follows the prompt */
+  if (!st) st = norm_gemv(s, c->etype, m->vl, m->output, m->output_norm, s->logits, B200_EPI_STORE, NULL);
+  if (!st) st = b200_launch_argmax(ctx, B, m->vl, s->logits, s->tok_out);
+  if (!st) st = pai_b200_memcpy_d2d(ctx, s->tok_in, s->tok_out, (uint64_t)B * 4);
+  if (!st) {
+    int32_t p = (int32_t)s->pos;
+    memcpy(s->htok, &p, 4);
+    st = pai_b200_memcpy_h2d(ctx, s->dpos, s->htok, 4);
+    if (!st) st = pai_b200_sync(ctx);
+  }
+  if (!st) st = pai_b200_session_get_tokens(s, next);
+  return st;
+}

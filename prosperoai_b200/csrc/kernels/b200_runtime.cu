@@ -5,6 +5,7 @@
 // the split-K scratch the kernels share.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
@@ -29,7 +30,22 @@ struct pai_b200_ctx {
   int capturing;
   int pdl;          // launch the decode-step kernels with programmatic dependent launch
   int pdl_allowed;  // PAI_B200_PDL=0 in the environment turns it off
+  // Scratch buffers replaced by larger ones. A CUDA graph captured earlier
+  // (a session's decode step) keeps the old addresses, so they are released
+  // only at shutdown; growth at least doubles, which bounds their number.
+  void *retired[64];
+  uint32_t nretired;
 };
+
+// Retire a scratch buffer (see pai_b200_ctx::retired).
+static void retire(pai_b200_ctx_t *c, void *p) {
+  if (!p) return;
+  if (c->nretired < sizeof(c->retired) / sizeof(c->retired[0])) {
+    c->retired[c->nretired++] = p;
+  } else {  // unreachable with doubling growth; keep correctness over memory
+    cudaStreamSynchronize(c->stream);
+  }
+}
 
 static thread_local char g_err[512];
 
@@ -119,6 +135,7 @@ extern "C" pai_status_t pai_b200_shutdown(pai_b200_ctx_t *c) {
   if (c->partial) cudaFree(c->partial);
   if (c->counters) cudaFree(c->counters);
   if (c->xq) cudaFree(c->xq);
+  for (uint32_t i = 0; i < c->nretired; i++) cudaFree(c->retired[i]);
   if (c->err_host) cudaFreeHost(c->err_host);
   cudaStreamDestroy(c->stream);
   delete c;
@@ -142,13 +159,10 @@ extern "C" uint32_t *b200_ctx_errflag(pai_b200_ctx_t *c) { return c->err_dev; }
 extern "C" pai_status_t b200_ctx_xq(pai_b200_ctx_t *c, uint64_t bytes, void **buf) {
   if (bytes > c->xq_bytes) {
     if (c->capturing) return b200_fail(PAI_ERR_INTERNAL, "activation scratch growth during graph capture");
-    if (c->xq) {
-      cudaStreamSynchronize(c->stream);
-      cudaFree(c->xq);
-      c->xq = nullptr;
-      c->xq_bytes = 0;
-    }
-    const uint64_t want = bytes < (1u << 20) ? (1u << 20) : bytes;
+    const uint64_t want = std::max<uint64_t>(std::max<uint64_t>(bytes, 1u << 20), 2 * c->xq_bytes);
+    retire(c, c->xq);
+    c->xq = nullptr;
+    c->xq_bytes = 0;
     pai_status_t st = b200_cuda(cudaMalloc(&c->xq, want), "activation scratch alloc");
     if (st) return st;
     c->xq_bytes = want;
@@ -187,12 +201,10 @@ extern "C" pai_status_t b200_ctx_scratch(pai_b200_ctx_t *c, uint64_t partial_flo
                                          uint32_t **counter) {
   if (partial_floats > c->partial_floats) {
     if (c->capturing) return b200_fail(PAI_ERR_INTERNAL, "scratch growth during graph capture");
-    if (c->partial) {
-      cudaStreamSynchronize(c->stream);
-      cudaFree(c->partial);
-      c->partial = nullptr;
-    }
-    uint64_t want = partial_floats < (1u << 20) ? (1u << 20) : partial_floats;
+    const uint64_t want =
+        std::max<uint64_t>(std::max<uint64_t>(partial_floats, 1u << 20), 2 * c->partial_floats);
+    retire(c, c->partial);
+    c->partial = nullptr;
     pai_status_t st = b200_cuda(cudaMalloc(&c->partial, want * sizeof(float)), "scratch alloc");
     if (st) {
       c->partial_floats = 0;
@@ -202,12 +214,9 @@ extern "C" pai_status_t b200_ctx_scratch(pai_b200_ctx_t *c, uint64_t partial_flo
   }
   if (counters > c->ncounters) {
     if (c->capturing) return b200_fail(PAI_ERR_INTERNAL, "scratch growth during graph capture");
-    if (c->counters) {
-      cudaStreamSynchronize(c->stream);
-      cudaFree(c->counters);
-      c->counters = nullptr;
-    }
-    uint32_t want = counters < 16384u ? 16384u : counters;
+    const uint32_t want = std::max<uint32_t>(std::max<uint32_t>(counters, 16384u), 2 * c->ncounters);
+    retire(c, c->counters);
+    c->counters = nullptr;
     pai_status_t st = b200_cuda(cudaMalloc(&c->counters, want * sizeof(uint32_t)), "counter alloc");
     if (st) {
       c->ncounters = 0;
