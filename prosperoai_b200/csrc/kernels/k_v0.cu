@@ -31,6 +31,8 @@
 // Shapes the vector path does not take (n not a multiple of 8, unaligned
 // pointers, flat groups that are not a multiple of 8) run an element-wise
 // kernel with the same split and reduction order.
+#include <cuda.h>  // CUtensorMap and its enums (types only; the encoder comes from the runtime)
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -291,6 +293,263 @@ __global__ void __launch_bounds__(kThreads) k_gemm_v0(V0Args p) {
   finish_strip(p);
 }
 
+// TMA path (the default where its alignment rules hold): the CTA's
+// weights arrive by 2-D tensor copies, one box of 32 rows x one 256-byte
+// (int8) or 128-byte (nibble) column strip per ring stage, issued by a
+// producer warp into a 6-stage shared-memory ring (mbarrier completion,
+// bounded waits), so the consumer warps never wait on their own loads.
+// Consumers: warp w takes rows w, w+8, w+16, w+24 of each stage; lane =
+// 8 columns, read from shared memory (8 or 4 bytes, conflict-free); the
+// arithmetic is the vector path's. The tensor map's inner coordinate is
+// the strip's byte offset, a multiple of 128.
+constexpr int kTmaRows = 32;    // rows per box (stage)
+constexpr int kTmaStages = 6;
+constexpr int kTmaThreads = kThreads + 32;  // 8 consumer warps + 1 producer warp
+constexpr uint64_t kTmaWaitLimit = 2000000000ull;  // ns before a wait gives up
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int32_t x, int32_t y, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+template <int BITS, int LAYOUT, int MB>
+__global__ void __launch_bounds__(kTmaThreads) k_gemm_v0_tma(V0Args p, uint32_t *err,
+                                                             const __grid_constant__ CUtensorMap map) {
+  constexpr uint32_t SB = BITS == 8 ? 256 : 128;  // bytes of a row strip
+  constexpr uint32_t STAGE = SB * kTmaRows;
+  using Raw = typename std::conditional<BITS == 8, uint2, uint32_t>::type;
+  extern __shared__ __align__(128) uint8_t dsm[];
+  uint8_t *ring = dsm;                                                   // [kTmaStages][STAGE]
+  float *sa = reinterpret_cast<float *>(dsm + kTmaStages * STAGE);       // [MB][per]
+  float *ss = sa + MB * p.per;                                           // [ngr][kStrip] (kOpScales)
+  __shared__ __align__(16) float red[kWarps][kStrip];
+  __shared__ __align__(8) uint64_t full[kTmaStages], empty[kTmaStages];
+  __shared__ int failed;
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint64_t c0 = (uint64_t)blockIdx.x * kStrip, j0 = c0 + lane * kCols;
+  const uint64_t t0 = (uint64_t)blockIdx.y * p.per, t1 = min(p.k, t0 + p.per);
+  const uint32_t nst = (uint32_t)((t1 - t0 + kTmaRows - 1) / kTmaRows);
+  const float *sf = reinterpret_cast<const float *>(p.s);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kTmaStages; i++) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kWarps);
+    }
+    fence_mbar_init();
+    failed = 0;
+  }
+  __syncthreads();
+  pdl_wait();  // a no-op unless launched as a programmatic dependent
+  uint32_t issued = 0;
+  const bool producer = warp == kWarps;
+  auto issue = [&](uint32_t st) -> bool {  // stage st into slot st % kTmaStages
+    const uint32_t slot = st % kTmaStages;
+    if (st >= (uint32_t)kTmaStages && !mbar_wait_spin(&empty[slot], ((st / kTmaStages) - 1) & 1u, kTmaWaitLimit))
+      return false;
+    mbar_expect_tx(&full[slot], STAGE);
+    tma_load_2d(ring + (size_t)slot * STAGE, &map, (int32_t)(blockIdx.x * SB), (int32_t)(t0 + (uint64_t)st * kTmaRows),
+                &full[slot]);
+    return true;
+  };
+  if (producer && lane == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map)) : "memory");
+    for (; issued < nst && issued < (uint32_t)kTmaStages; issued++) issue(issued);
+  }
+  // activations (and per-(group, column) scales) while the first boxes land
+  uint64_t gnext = 0;
+  uint32_t gl = 0;
+  if (!producer) {
+    for (uint32_t i = threadIdx.x; i < MB * p.per; i += kThreads) {
+      const uint32_t r = i / (uint32_t)p.per, tt = i - r * (uint32_t)p.per;
+      sa[i] = (r < p.m && t0 + tt < t1) ? __ldg(p.a + r * p.k + t0 + tt) : 0.0f;
+    }
+    if (LAYOUT == kOpScales) {
+      const uint64_t gfirst = t0 / p.g, ngr = (t1 - 1) / p.g - gfirst + 1, ngroups = (p.k + p.g - 1) / p.g;
+      for (uint32_t i = threadIdx.x; i < ngr * kStrip; i += kThreads) {
+        const uint64_t gi = gfirst + i / kStrip, col = c0 + i % kStrip;
+        ss[i] = (col < p.n && gi < ngroups) ? __ldg(sf + gi * p.n + col) : 0.0f;
+      }
+      const uint64_t gi = (t0 + warp) / p.g;
+      gl = (uint32_t)(gi - gfirst);
+      gnext = (gi + 1) * p.g;
+    }
+  }
+  __syncthreads();
+
+  if (producer) {
+    if (lane == 0) {
+      bool ok = true;
+      for (; ok && issued < nst; issued++) ok = issue(issued);
+      if (!ok) {
+        // a wait ran out: raise the error and let the boxes in flight land (bounded)
+        atomicExch(err, 1u);
+        failed = 1;
+        for (uint32_t f = issued > (uint32_t)kTmaStages ? issued - kTmaStages : 0; f < issued; f++)
+          mbar_wait(&full[f % kTmaStages], (f / kTmaStages) & 1u, kTmaWaitLimit);
+      }
+    }
+  } else {
+    const bool live = j0 < p.n;
+    float acc[MB][kCols];
+#pragma unroll
+    for (int r = 0; r < MB; r++)
+#pragma unroll
+      for (int e = 0; e < kCols; e++) acc[r][e] = 0.0f;
+    float sc[kCols];
+    if (LAYOUT == kOpScales) {
+      const float4 s0 = *reinterpret_cast<const float4 *>(ss + gl * kStrip + lane * kCols);
+      const float4 s1 = *reinterpret_cast<const float4 *>(ss + gl * kStrip + lane * kCols + 4);
+      sc[0] = s0.x, sc[1] = s0.y, sc[2] = s0.z, sc[3] = s0.w;
+      sc[4] = s1.x, sc[5] = s1.y, sc[6] = s1.z, sc[7] = s1.w;
+    }
+    // kFlatScales: cursor (f / g, f % g) of this lane's first column of the
+    // next row whose scale is loaded (rows advance by kWarps); the scales of
+    // a stage's rows are loaded one stage ahead
+    constexpr int RPW = kTmaRows / kWarps;  // rows per warp per stage
+    uint64_t qg = 0, rg = 0, dq = 0, dr = 0;
+    float rs_next[RPW];
+    auto load_scales = [&](uint32_t st) {
+#pragma unroll
+      for (int u = 0; u < RPW; u++) {
+        const uint64_t t = t0 + (uint64_t)st * kTmaRows + warp + kWarps * u;
+        const bool in = t < t1;
+        rs_next[u] = (live && in) ? __ldg(sf + qg) : 0.0f;
+        if (in) {
+          rg += dr;
+          qg += dq;
+          if (rg >= p.g) {
+            rg -= p.g;
+            qg++;
+          }
+        }
+      }
+    };
+    if (LAYOUT == kFlatScales) {
+      const uint64_t f = (t0 + warp) * p.n + j0, step = (uint64_t)kWarps * p.n;
+      qg = f / p.g;
+      rg = f - qg * p.g;
+      dq = step / p.g;
+      dr = step - dq * p.g;
+      load_scales(0);
+    }
+    for (uint32_t st = 0; st < nst; st++) {
+      const uint32_t slot = st % kTmaStages;
+      if (!mbar_wait(&full[slot], (st / kTmaStages) & 1u, kTmaWaitLimit)) {
+        if (lane == 0) atomicExch(err, 1u);
+        failed = 1;
+        break;
+      }
+      float rs[RPW];
+      if (LAYOUT == kFlatScales) {
+#pragma unroll
+        for (int u = 0; u < RPW; u++) rs[u] = rs_next[u];
+        if (st + 1 < nst) load_scales(st + 1);
+      }
+      const uint8_t *stage = ring + (size_t)slot * STAGE;
+#pragma unroll
+      for (int u = 0; u < RPW; u++) {
+        const uint32_t row = warp + kWarps * u;
+        const uint64_t tu = t0 + (uint64_t)st * kTmaRows + row;
+        if (tu >= t1) break;
+        const Raw raw = *reinterpret_cast<const Raw *>(stage + (size_t)row * SB + lane * sizeof(Raw));
+        float v[kCols];
+        if constexpr (BITS == 8) {
+          const uint32_t x0 = raw.x ^ 0x80808080u, x1 = raw.y ^ 0x80808080u;
+#pragma unroll
+          for (int e = 0; e < 4; e++) {
+            v[e] = biased_byte(x0, e) - 8388736.0f;  // 2^23 + 128
+            v[e + 4] = biased_byte(x1, e) - 8388736.0f;
+          }
+        } else {
+          const uint32_t x = raw ^ 0x88888888u;
+          const uint32_t lo = x & 0x0F0F0F0Fu, hi = (x >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+          for (int e = 0; e < 4; e++) {
+            v[2 * e] = biased_byte(lo, e) - 8388616.0f;  // 2^23 + 8
+            v[2 * e + 1] = biased_byte(hi, e) - 8388616.0f;
+          }
+        }
+        const uint32_t tl = (uint32_t)(tu - t0);
+        if constexpr (LAYOUT == kOpScales) {
+          if (tu >= gnext) {  // uniform across the warp; g >= 8, so one group at most
+            gl++;
+            gnext += p.g;
+            const float4 s0 = *reinterpret_cast<const float4 *>(ss + gl * kStrip + lane * kCols);
+            const float4 s1 = *reinterpret_cast<const float4 *>(ss + gl * kStrip + lane * kCols + 4);
+            sc[0] = s0.x, sc[1] = s0.y, sc[2] = s0.z, sc[3] = s0.w;
+            sc[4] = s1.x, sc[5] = s1.y, sc[6] = s1.z, sc[7] = s1.w;
+          }
+#pragma unroll
+          for (int e = 0; e < kCols; e++) {
+            const float we = v[e] * sc[e];
+#pragma unroll
+            for (int r = 0; r < MB; r++) acc[r][e] = fmaf(sa[r * p.per + tl], we, acc[r][e]);
+          }
+        } else {
+#pragma unroll
+          for (int r = 0; r < MB; r++) {
+            const float as = sa[r * p.per + tl] * rs[u];
+#pragma unroll
+            for (int e = 0; e < kCols; e++) acc[r][e] = fmaf(as, v[e], acc[r][e]);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+    }
+    // reduction of the warps' partial sums, one activation row at a time
+#pragma unroll
+    for (int r = 0; r < MB; r++) {
+      if (r >= (int)p.m) break;
+      float4 *dst = reinterpret_cast<float4 *>(&red[warp][lane * kCols]);
+      dst[0] = make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+      dst[1] = make_float4(acc[r][4], acc[r][5], acc[r][6], acc[r][7]);
+      asm volatile("bar.sync 1, %0;" ::"r"(kThreads) : "memory");  // consumer warps only
+      float s = 0.0f;
+#pragma unroll
+      for (int w = 0; w < kWarps; w++) s += red[w][threadIdx.x];
+      const uint64_t j = c0 + threadIdx.x;
+      if (j < p.n) put_result(p, r, j, s);
+      asm volatile("bar.sync 1, %0;" ::"r"(kThreads) : "memory");
+    }
+  }
+  __syncthreads();
+  if (failed) return;
+  // k-splits: the strip's last CTA adds the partials in split order
+  if (gridDim.y == 1) return;
+  __shared__ uint32_t ticket;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) ticket = atomicAdd(&p.cnt[blockIdx.x], 1u);
+  __syncthreads();
+  if (ticket != gridDim.y - 1) return;
+  __threadfence();
+  if (threadIdx.x < kStrip) {
+    const uint64_t j = c0 + threadIdx.x;
+    if (j < p.n) {
+      const uint64_t ys = p.m * p.n;
+      for (uint64_t r = 0; r < p.m; r++) {
+        const float *src = p.part + r * p.n + j;
+        float v = 0.0f;
+        uint32_t y = 0;
+        for (; y + kSplitLoads <= gridDim.y; y += kSplitLoads) {
+          float b[kSplitLoads];
+#pragma unroll
+          for (int u = 0; u < kSplitLoads; u++) b[u] = __ldcg(src + (uint64_t)(y + u) * ys);
+#pragma unroll
+          for (int u = 0; u < kSplitLoads; u++) v += b[u];
+        }
+        for (; y < gridDim.y; y++) v += __ldcg(src + (uint64_t)y * ys);
+        p.c[r * p.n + j] = v;
+      }
+    }
+  }
+  if (threadIdx.x == 0) p.cnt[blockIdx.x] = 0;
+}
+
 // Element-wise path for every other shape: thread per column, all rows of
 // the split in order.
 template <int BITS, int LAYOUT>
@@ -333,11 +592,59 @@ cudaError_t launch_vec(pai_b200_ctx_t *ctx, dim3 grid, uint32_t mb, const V0Args
   }
 }
 
+// cuTensorMapEncodeTiled from the driver, looked up through the runtime
+// once (no link-time dependency on libcuda); NULL where unavailable.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static bool looked = false;
+  if (!looked) {
+    looked = true;
+    void *f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }
+  return fn;
+}
+
+template <int BITS, int LAYOUT, int MB>
+cudaError_t launch_tma_mb(pai_b200_ctx_t *ctx, dim3 grid, const V0Args &a, const CUtensorMap &map) {
+  constexpr uint32_t SB = BITS == 8 ? 256 : 128;
+  size_t smem = (size_t)kTmaStages * SB * kTmaRows + (size_t)MB * a.per * sizeof(float);
+  if (LAYOUT == kOpScales) smem += split_groups(a.per, a.g) * kStrip * sizeof(float);
+  static size_t opted = 0;  // dynamic shared memory this instantiation is opted in to
+  if (smem > opted) {
+    cudaError_t e = cudaFuncSetAttribute(k_gemm_v0_tma<BITS, LAYOUT, MB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return e;
+    opted = smem;
+  }
+  return b200_launch(ctx, k_gemm_v0_tma<BITS, LAYOUT, MB>, grid, dim3(kTmaThreads), smem, a, b200_ctx_errflag(ctx),
+                     map);
+}
+
+template <int BITS, int LAYOUT>
+cudaError_t launch_tma(pai_b200_ctx_t *ctx, dim3 grid, uint32_t mb, const V0Args &a, const CUtensorMap &map) {
+  switch (mb) {
+    case 1: return launch_tma_mb<BITS, LAYOUT, 1>(ctx, grid, a, map);
+    case 2: return launch_tma_mb<BITS, LAYOUT, 2>(ctx, grid, a, map);
+    case 4: return launch_tma_mb<BITS, LAYOUT, 4>(ctx, grid, a, map);
+    default: return launch_tma_mb<BITS, LAYOUT, 8>(ctx, grid, a, map);
+  }
+}
+
 pai_status_t gemm_v0(pai_b200_ctx_t *ctx, uint32_t bits, int layout, uint64_t m, uint64_t n, uint64_t k,
                      const float *a, const void *w, const void *s, uint64_t g, float *c, const char *what) {
   const uintptr_t wa = (uintptr_t)w, sa = (uintptr_t)s;
   const bool vec = n % kCols == 0 && wa % (bits == 8 ? 8 : 4) == 0 &&
                    (layout == kOpScales ? (sa % 16 == 0 && g >= kCols) : (sa % 4 == 0 && g % kCols == 0));
+  // TMA path: rows of whole 16-byte multiples (the tensor map's stride rule), 16-byte aligned
+  // values, and the vector path's scale rules
+  const uint64_t row_bytes = bits == 8 ? n : n / 2;
+  PFN_cuTensorMapEncodeTiled_v12000 encode = vec ? tensor_map_encoder() : nullptr;
+  const bool tma = encode && (bits == 8 ? n % 16 == 0 : n % 32 == 0) && wa % 16 == 0 && k <= 0x7FFFFFFFull &&
+                   row_bytes >= (bits == 8 ? 256u : 128u) && row_bytes < (1ull << 40);
   const uint64_t strips = (n + kStrip - 1) / kStrip;
   // about kCtasPerSm CTAs per SM, at least 64 rows per split, at most
   // kMaxPer (and, with staged scales, at most kMaxScaleGroups groups)
@@ -348,8 +655,20 @@ pai_status_t gemm_v0(pai_b200_ctx_t *ctx, uint32_t bits, int layout, uint64_t m,
   splits = std::min<uint64_t>(splits, std::max<uint64_t>(1, k / 64));
   splits = std::max<uint64_t>(splits, (k + max_per - 1) / max_per);
   uint64_t per = (k + splits - 1) / splits;
-  per = (per + kWarps - 1) / kWarps * kWarps;
+  const uint64_t quantum = tma ? kTmaRows : kWarps;  // whole boxes per split on the TMA path
+  per = (per + quantum - 1) / quantum * quantum;
   splits = (k + per - 1) / per;
+  CUtensorMap map;
+  if (tma) {
+    const cuuint64_t dims[2] = {row_bytes, k};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {bits == 8 ? 256u : 128u, (cuuint32_t)kTmaRows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = encode(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(w), dims, strides, box, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return b200_fail(PAI_ERR_INTERNAL, "%s: cuTensorMapEncodeTiled error %d", what, (int)r);
+  }
   if (strips > 0xFFFFFFFFull || splits > 65535)
     return b200_fail(PAI_ERR_INVALID_ARG, "%s: n %llu x k %llu is beyond the launch grid", what,
                      (unsigned long long)n, (unsigned long long)k);
@@ -371,7 +690,15 @@ pai_status_t gemm_v0(pai_b200_ctx_t *ctx, uint32_t bits, int layout, uint64_t m,
     }
     const dim3 grid((uint32_t)strips, (uint32_t)splits);
     cudaError_t e;
-    if (vec) {
+    if (tma) {
+      const uint32_t mb = mm == 1 ? 1 : mm == 2 ? 2 : mm <= 4 ? 4 : 8;
+      if (bits == 8)
+        e = layout == kOpScales ? launch_tma<8, kOpScales>(ctx, grid, mb, p, map)
+                                : launch_tma<8, kFlatScales>(ctx, grid, mb, p, map);
+      else
+        e = layout == kOpScales ? launch_tma<4, kOpScales>(ctx, grid, mb, p, map)
+                                : launch_tma<4, kFlatScales>(ctx, grid, mb, p, map);
+    } else if (vec) {
       const uint32_t mb = mm == 1 ? 1 : mm == 2 ? 2 : mm <= 4 ? 4 : 8;
       if (bits == 8)
         e = layout == kOpScales ? launch_vec<8, kOpScales>(ctx, grid, mb, p) : launch_vec<8, kFlatScales>(ctx, grid, mb, p);
@@ -386,7 +713,7 @@ pai_status_t gemm_v0(pai_b200_ctx_t *ctx, uint32_t bits, int layout, uint64_t m,
                                 : b200_launch(ctx, k_gemm_v0_any<4, kFlatScales>, grid, dim3(kThreads), 0, p);
     }
     if (e != cudaSuccess) return b200_cuda(e, what);
-    pai_status_t st = b200_launched(ctx, 1, vec ? "k_gemm_v0" : "k_gemm_v0_any");
+    pai_status_t st = b200_launched(ctx, 1, tma ? "k_gemm_v0_tma" : vec ? "k_gemm_v0" : "k_gemm_v0_any");
     if (st) return st;
   }
   return PAI_OK;
