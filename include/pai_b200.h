@@ -497,8 +497,10 @@ pai_status_t pai_b200_session_run(pai_b200_session_t *s, uint32_t steps);
  * the greedy token after the last position, which is also the input of the
  * next pai_b200_session_run step. Equivalent to stepping the prompt; with
  * Q4_0 layers the bf16 GEMM tiles put the hidden state within about 1e-2
- * (max-abs-rel) of the stepped result. Single GPU: tensor-parallel
- * sessions return PAI_ERR_UNSUPPORTED and step the prompt. */
+ * (max-abs-rel) of the stepped result. Under tensor parallelism every rank
+ * calls it with the same tokens (a collective): the row-parallel o/down
+ * outputs of all prompt rows are summed over ranks by an NCCL all-reduce
+ * before the residual add. */
 pai_status_t pai_b200_session_prefill(pai_b200_session_t *s, const int32_t *tokens, uint32_t n,
                                       int32_t *next);
 pai_status_t pai_b200_session_set_tokens(pai_b200_session_t *s,

@@ -713,6 +713,15 @@ static pai_status_t rows_matmul(pai_b200_session_t *s, uint32_t type, uint32_t r
   pai_b200_model_t *m = s->m;
   pai_b200_ctx_t *ctx = m->ctx;
   pai_status_t st = PAI_OK;
+  if (epi == B200_EPI_RESIDUAL && m->tp > 1) {
+    /* row-parallel under tensor parallelism: this rank's partial rows, the
+     * sum over ranks (NCCL all-reduce, the same bits on every rank), then
+     * the residual add */
+    st = rows_matmul(s, type, rows, n, k, w, x, s->pf_tmp, B200_EPI_STORE);
+    if (!st) st = pai_b200_tp_allreduce_f32(s->tp, s->pf_tmp, (uint64_t)rows * n);
+    if (!st) st = pai_b200_vecadd_f32(ctx, y, s->pf_tmp, y, (uint64_t)rows * n);
+    return st;
+  }
   if (type == PAI_B200_Q4_0) {
     float *dst = epi == B200_EPI_STORE ? y : (epi == B200_EPI_RESIDUAL ? s->pf_tmp : s->pf_gu);
     st = pai_b200_gemm_q4_0_f32(ctx, rows, n, k, x, w, dst);
@@ -738,7 +747,6 @@ pai_status_t pai_b200_session_prefill(pai_b200_session_t *s, const int32_t *toke
   pai_b200_ctx_t *ctx = m->ctx;
   const pai_b200_model_cfg_t *c = &m->cfg;
   const uint32_t B = s->batch, E = c->n_embd, hd = c->head_dim;
-  if (m->tp > 1) return b200_fail(PAI_ERR_UNSUPPORTED, "session_prefill: tensor-parallel sessions step the prompt");
   if ((uint64_t)s->pos + n > s->max_ctx)
     return b200_fail(PAI_ERR_INVALID_ARG, "session_prefill: %u positions from %u exceed the %u-position cache", n,
                      s->pos, s->max_ctx);
@@ -781,7 +789,10 @@ pai_status_t pai_b200_session_prefill(pai_b200_session_t *s, const int32_t *toke
   /* logits of the last position, greedy token; it is also the next decode
    * step's input, and the device position follows the prompt */
   if (!st) st = norm_gemv(s, c->etype, m->vl, m->output, m->output_norm, s->logits, B200_EPI_STORE, NULL);
-  if (!st) st = b200_launch_argmax(ctx, B, m->vl, s->logits, s->tok_out);
+  if (!st) {
+    st = m->tp == 1 ? b200_launch_argmax(ctx, B, m->vl, s->logits, s->tok_out)
+                    : b200_tp_argmax(s->tp, ctx, B, m->vl, m->v0, s->logits, s->tok_out);
+  }
   if (!st) st = pai_b200_memcpy_d2d(ctx, s->tok_in, s->tok_out, (uint64_t)B * 4);
   if (!st) {
     int32_t p = (int32_t)s->pos;

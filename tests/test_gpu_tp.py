@@ -4,7 +4,8 @@
 - a 2-rank tensor-parallel decode (column-parallel q/k/v/gate/up,
   row-parallel o/down with the all-reduce, vocabulary-sharded lm head with
   the cross-rank argmax) gives the same 64 greedy tokens on both ranks as
-  the oracle's unsharded decode of the same synthetic weights.
+  the oracle's unsharded decode of the same synthetic weights;
+- a 2-rank prompt prefill followed by decode gives the oracle's tokens.
 
 Skipped on a box with fewer than 2 GPUs. Children bind one GPU each and
 run with NVLink SHARP (NVLS) off, so no rank binds memory to an NVLink
@@ -75,11 +76,44 @@ def _worker(rank, world, port, cfg, prompt, steps, max_ctx, q):
     q.put(out)
 
 
-def _run_ranks(world, cfg, prompt, steps, max_ctx):
+def _prefill_worker(rank, world, port, cfg, prompt, steps, max_ctx, q):
+    """Prompt prefill under tensor parallelism, then greedy decode steps."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    out = {"rank": rank}
+    try:
+        import torch.distributed as dist
+        from prosperoai_b200.api import Device, Model, Session, TPComm
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60))
+        dev = Device(rank)
+        comm = TPComm.over_group(dev, rank, world)
+        model = Model(dev, cfg, tp_rank=rank, tp_size=world)
+        model.synthesize(SEED)
+        model.set_tp(comm)
+        sess = Session(model, 1, max_ctx)
+        toks = [int(sess.prefill(np.asarray(prompt, np.int32)[None, :])[0])]
+        for _ in range(steps - 1):
+            toks.append(int(sess.step(np.array([toks[-1]], np.int32))[0]))
+        out["tokens"] = toks
+        dist.barrier()
+        sess.close()
+        comm.close()
+        model.close()
+        dev.close()
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:  # reported to the parent, which fails the test
+        out["error"] = repr(e)
+    q.put(out)
+
+
+def _run_ranks(world, cfg, prompt, steps, max_ctx, target=None):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, cfg, prompt, steps, max_ctx, q))
+    procs = [ctx.Process(target=target or _worker, args=(r, world, port, cfg, prompt, steps, max_ctx, q))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -110,4 +144,23 @@ def test_tp2_decode_matches_oracle(dev):
     for r in range(2):
         assert "error" not in res[r], res[r]["error"]
         np.testing.assert_array_equal(res[r]["allreduce"], np.arange(4096, dtype=np.float32) * 3)
+        assert res[r]["tokens"] == [int(t) for t in want], f"rank {r}"
+
+
+def test_tp2_prefill_then_decode_matches_oracle(dev):
+    """Prompt prefill with 2 ranks (Q8_0 layers: the batched GEMV; the
+    row-parallel outputs summed by the NCCL all-reduce), then decode: the
+    tokens equal the oracle's stepped decode."""
+    if _gpu_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from test_gpu_model import oracle_generate, synth_weights
+    cfg = dict(TP_CFG, wtype=po.Q8_0)
+    prompt = list(np.random.default_rng(8).integers(0, cfg["vocab"], 29))
+    steps = 24
+    max_ctx = len(prompt) + steps + 4
+    w = synth_weights(dev, cfg, SEED)
+    want, _ = oracle_generate(cfg, w, prompt, steps, max_ctx)
+    res = _run_ranks(2, cfg, prompt, steps, max_ctx, target=_prefill_worker)
+    for r in range(2):
+        assert "error" not in res[r], res[r]["error"]
         assert res[r]["tokens"] == [int(t) for t in want], f"rank {r}"
