@@ -227,9 +227,10 @@ extern "C" pai_status_t b200_launch_rmsnorm_xq(pai_b200_ctx_t *ctx, uint64_t row
   if (rows > 65535) return b200_fail(PAI_ERR_UNSUPPORTED, "rmsnorm: %llu rows (at most 65535)", (unsigned long long)rows);
   b200_xq_t q{};
   if (xq) q = *xq;
-  // one 32-element block per warp, up to 256 CTAs per row
+  // one 32-element block per warp, up to 256 CTAs per row; with many rows
+  // (a prompt) one CTA per row already fills the GPU and reads each row once
   const uint64_t nblk = xq ? xq->quads * 4 : (n + 31) / 32;
-  const uint64_t nsl = std::max<uint64_t>(1, std::min<uint64_t>(256, (nblk + 3) / 4));
+  const uint64_t nsl = rows >= 64 ? 1 : std::max<uint64_t>(1, std::min<uint64_t>(256, (nblk + 3) / 4));
   const uint32_t bps = (uint32_t)((nblk + nsl - 1) / nsl);
   b200_launch(ctx, k_rmsnorm, dim3((unsigned)nsl, (unsigned)rows), dim3(kNormThreads), 0, (uint32_t)n, bps, a, gamma,
               eps, c, q);

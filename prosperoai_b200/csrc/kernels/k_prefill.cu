@@ -13,6 +13,9 @@
 //                          with a running maximum (the reference's two-pass
 //                          softmax, cpu/reference/ref_ops.c:307-349, to fp32
 //                          rounding).
+//   k_attn_prefill_tiled   the same, with each 32-position K/V tile staged
+//                          once in shared memory for all the (row, head)
+//                          warps of a GQA group and 8/G consecutive rows.
 //   k_silu_glu_rows        silu(gate) * up of the fused gate/up GEMM output,
 //                          whose 16-row tiles hold 8 gate rows then the 8
 //                          matching up rows (ref_ops.c:219-228, 124-133 with
@@ -130,6 +133,99 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attn_prefill(uint32_t nrows
   *reinterpret_cast<float4 *>(out + (size_t)r * h * kHD + (size_t)head * kHD + 4 * lane) = o;
 }
 
+// Two fp16 values packed in a word (low half first) as floats, exactly.
+__device__ __forceinline__ float2 half2_bits_to_float2(uint32_t w) {
+  return make_float2(__half2float(__ushort_as_half((unsigned short)(w & 0xFFFFu))),
+                     __half2float(__ushort_as_half((unsigned short)(w >> 16))));
+}
+
+// Tiled form: CTA per (sequence, kv head, block of 8/G consecutive rows)
+// with one warp per (row, query head of the GQA group), G = h/hk dividing
+// 8. The 32-position K and V tiles are loaded once per CTA into shared
+// memory and read by all its warps (8x less L2 traffic than a tile per
+// warp); the arithmetic per warp is k_attn_prefill's. K rows are padded to
+// 136 halves so that the lanes' 16-byte reads of different rows fall in
+// different banks.
+constexpr int kTile = 32, kKPad = kHD + 8;
+__global__ void __launch_bounds__(256) k_attn_prefill_tiled(uint32_t rows_per_seq, uint32_t p0, uint32_t h, uint32_t hk,
+                                                            const float *__restrict__ qkv,
+                                                            const __half *__restrict__ kc,
+                                                            const __half *__restrict__ vc, uint64_t cap,
+                                                            uint64_t seq_stride, float inv_scale,
+                                                            float *__restrict__ out) {
+  __shared__ __align__(16) __half kt[kTile][kKPad];
+  __shared__ __align__(16) __half vt[kTile][kHD];
+  __shared__ __align__(16) float qs[8][kHD];
+  const uint32_t G = h / hk, RB = 8 / G;
+  const uint32_t lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const uint32_t b = blockIdx.z, kvh = blockIdx.y, i0 = blockIdx.x * RB;
+  const uint32_t g = w % G, i = i0 + w / G, head = kvh * G + g;
+  const bool active = i < rows_per_seq;
+  const uint32_t r = b * rows_per_seq + i;
+  const uint32_t npos = active ? p0 + i + 1 : 0;
+  const uint32_t ilast = min(i0 + RB, rows_per_seq) - 1, nmax = p0 + ilast + 1;  // positions this CTA needs
+  if (active) {
+    const float *q = qkv + (size_t)r * (h + 2 * hk) * kHD + (size_t)head * kHD;
+    for (uint32_t d = lane; d < kHD; d += 32) qs[w][d] = q[d];
+  }
+  const size_t base = (size_t)b * seq_stride + (size_t)kvh * cap * kHD;
+  float m = -INFINITY, l = 0.0f, acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  for (uint32_t j0 = 0; j0 < nmax; j0 += kTile) {
+    __syncthreads();  // the previous tile is consumed (and qs written, first time)
+    // 32 rows x 16 chunks of 16 B for K and for V: 2 + 2 per thread
+    for (uint32_t c = threadIdx.x; c < kTile * (kHD / 8); c += blockDim.x) {
+      const uint32_t row = c / (kHD / 8), col = c % (kHD / 8);
+      uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
+      if (j0 + row < nmax) {
+        kv = __ldg(reinterpret_cast<const uint4 *>(kc + base + (size_t)(j0 + row) * kHD) + col);
+        vv = __ldg(reinterpret_cast<const uint4 *>(vc + base + (size_t)(j0 + row) * kHD) + col);
+      }
+      *reinterpret_cast<uint4 *>(&kt[row][col * 8]) = kv;
+      *reinterpret_cast<uint4 *>(&vt[row][col * 8]) = vv;
+    }
+    __syncthreads();
+    if (!active || j0 >= npos) continue;
+    const uint32_t j = j0 + lane;
+    float s = -INFINITY;
+    if (j < npos) {
+      float dot = 0.0f;
+#pragma unroll 4
+      for (int c = 0; c < kHD / 8; c++) {
+        const uint4 raw = *reinterpret_cast<const uint4 *>(&kt[lane][c * 8]);
+        const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          const float2 f = half2_bits_to_float2(words[e]);
+          dot = fmaf(qs[w][8 * c + 2 * e], f.x, dot);
+          dot = fmaf(qs[w][8 * c + 2 * e + 1], f.y, dot);
+        }
+      }
+      s = __fmul_rn(dot, inv_scale);
+    }
+    const float mt = warp_max(s);
+    const float mn = fmaxf(m, mt);
+    const float corr = m == -INFINITY ? 0.0f : expf(m - mn);
+    const float pj = j < npos ? expf(s - mn) : 0.0f;
+    l = l * corr + warp_sum(pj);
+#pragma unroll
+    for (int e = 0; e < 4; e++) acc[e] *= corr;
+    const uint32_t cnt = min((uint32_t)kTile, npos - j0);
+    for (uint32_t u = 0; u < cnt; u++) {
+      const float pu = __shfl_sync(0xffffffffu, pj, u);
+      const uint2 raw = *reinterpret_cast<const uint2 *>(&vt[u][4 * lane]);
+      const float2 v0 = half2_bits_to_float2(raw.x), v1 = half2_bits_to_float2(raw.y);
+      acc[0] = fmaf(pu, v0.x, acc[0]);
+      acc[1] = fmaf(pu, v0.y, acc[1]);
+      acc[2] = fmaf(pu, v1.x, acc[2]);
+      acc[3] = fmaf(pu, v1.y, acc[3]);
+    }
+    m = mn;
+  }
+  if (!active) return;
+  float4 o = make_float4(acc[0] / l, acc[1] / l, acc[2] / l, acc[3] / l);
+  *reinterpret_cast<float4 *>(out + (size_t)r * h * kHD + (size_t)head * kHD + 4 * lane) = o;
+}
+
 __global__ void k_silu_glu_rows(uint64_t rows, uint32_t ff, const float *__restrict__ gu, float *__restrict__ hout) {
   const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= rows * ff) return;
@@ -165,6 +261,16 @@ extern "C" pai_status_t b200_launch_attn_prefill(pai_b200_ctx_t *ctx, uint32_t r
   if (blocks > 0x7FFFFFFFull) return b200_fail(PAI_ERR_UNSUPPORTED, "attn_prefill: too many rows");
   // 1/sqrtf(hd), the scale of the decode attention
   const float inv_scale = 1.0f / sqrtf((float)hd);
+  const uint32_t G = h / hk;
+  if (G <= 8 && 8 % G == 0 && rows % rows_per_seq == 0) {
+    const uint32_t RB = 8 / G, nseq = rows / rows_per_seq;
+    if (nseq > 65535 || hk > 65535) return b200_fail(PAI_ERR_UNSUPPORTED, "attn_prefill: grid");
+    k_attn_prefill_tiled<<<dim3((rows_per_seq + RB - 1) / RB, hk, nseq), 256, 0,
+                           (cudaStream_t)b200_ctx_stream(ctx)>>>(
+        rows_per_seq, p0, h, hk, qkv, reinterpret_cast<const __half *>(kc), reinterpret_cast<const __half *>(vc),
+        cap, seq_stride, inv_scale, out);
+    return b200_launched(ctx, 1, "k_attn_prefill_tiled");
+  }
   k_attn_prefill<<<(uint32_t)blocks, kAttnWarps * 32, 0, (cudaStream_t)b200_ctx_stream(ctx)>>>(
       rows, rows_per_seq, p0, h, hk, qkv, reinterpret_cast<const __half *>(kc), reinterpret_cast<const __half *>(vc),
       cap, seq_stride, inv_scale, out);
