@@ -509,6 +509,9 @@ def gpu_arm(args):
     if tp:
         # the exchanges are 16 KB per sequence: no NVLink multicast (NVLS) objects
         os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    if world > 1 and os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+        # NCCL's version banner goes to stdout, where rank 0 prints the one JSON line
+        os.environ["NCCL_DEBUG"] = "WARN"
     L = _native.load()
     dev = Device(local)
     cfg = dict(CFG_8B)
