@@ -632,7 +632,7 @@ def gpu_arm(args):
                        "layers": cfg["n_layer"], "hidden": cfg["n_embd"], "vocab": cfg["vocab"],
                        "kv_cache": "fp16",
                        "parallelism": ("single GPU" if world == 1 else
-                                       f"tp{world} (NCCL all-reduce after o/down, vocab-sharded argmax)"
+                                       f"tp{world} (NVLink peer-memory all-reduce after o/down, vocab-sharded argmax)"
                                        if tp else f"{world} independent replicas"),
                        "l2": "no flush: 4.5 GB of weights per step exceed the 126 MB L2"},
             "e2e": {"value": round(jobs * B * K / (t_e2e * 1e-3), 3), "unit": UNIT,
