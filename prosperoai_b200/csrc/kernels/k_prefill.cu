@@ -153,8 +153,8 @@ __global__ void __launch_bounds__(256) k_attn_prefill_tiled(uint32_t rows_per_se
                                                             const __half *__restrict__ vc, uint64_t cap,
                                                             uint64_t seq_stride, float inv_scale,
                                                             float *__restrict__ out) {
-  __shared__ __align__(16) __half kt[kTile][kKPad];
-  __shared__ __align__(16) __half vt[kTile][kHD];
+  __shared__ __align__(16) __half kt[2][kTile][kKPad];  // double-buffered tiles
+  __shared__ __align__(16) __half vt[2][kTile][kHD];
   __shared__ __align__(16) float qs[8][kHD];
   const uint32_t G = h / hk, RB = 8 / G;
   const uint32_t lane = threadIdx.x & 31, w = threadIdx.x >> 5;
@@ -170,56 +170,74 @@ __global__ void __launch_bounds__(256) k_attn_prefill_tiled(uint32_t rows_per_se
   }
   const size_t base = (size_t)b * seq_stride + (size_t)kvh * cap * kHD;
   float m = -INFINITY, l = 0.0f, acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-  for (uint32_t j0 = 0; j0 < nmax; j0 += kTile) {
-    __syncthreads();  // the previous tile is consumed (and qs written, first time)
-    // 32 rows x 16 chunks of 16 B for K and for V: 2 + 2 per thread
+  // tile t of positions [32t, 32t + 32) into buffer t & 1: 32 rows x 16
+  // chunks of 16 B for K and for V, 2 + 2 asynchronous copies per thread;
+  // rows at or beyond nmax are zero-filled (source size 0, no read)
+  auto load_tile = [&](uint32_t t) {
+    const uint32_t buf = t & 1u, j0 = t * kTile;
     for (uint32_t c = threadIdx.x; c < kTile * (kHD / 8); c += blockDim.x) {
       const uint32_t row = c / (kHD / 8), col = c % (kHD / 8);
-      uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-      if (j0 + row < nmax) {
-        kv = __ldg(reinterpret_cast<const uint4 *>(kc + base + (size_t)(j0 + row) * kHD) + col);
-        vv = __ldg(reinterpret_cast<const uint4 *>(vc + base + (size_t)(j0 + row) * kHD) + col);
-      }
-      *reinterpret_cast<uint4 *>(&kt[row][col * 8]) = kv;
-      *reinterpret_cast<uint4 *>(&vt[row][col * 8]) = vv;
+      const bool in = j0 + row < nmax;
+      const size_t off = base + (size_t)(in ? j0 + row : 0) * kHD + col * 8;
+      const uint32_t n = in ? 16u : 0u;
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(&kt[buf][row][col * 8])),
+                   "l"(kc + off), "r"(n)
+                   : "memory");
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(&vt[buf][row][col * 8])),
+                   "l"(vc + off), "r"(n)
+                   : "memory");
     }
-    __syncthreads();
-    if (!active || j0 >= npos) continue;
-    const uint32_t j = j0 + lane;
-    float s = -INFINITY;
-    if (j < npos) {
-      float dot = 0.0f;
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  const uint32_t ntiles = (nmax + kTile - 1) / kTile;
+  load_tile(0);
+  for (uint32_t t = 0; t < ntiles; t++) {
+    const uint32_t j0 = t * kTile, buf = t & 1u;
+    if (t + 1 < ntiles) {
+      load_tile(t + 1);  // its buffer was last read in iteration t - 1, before that iteration's barrier
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
+    __syncthreads();  // tile t is in shared memory for every thread (and qs, the first time)
+    if (active && j0 < npos) {
+      const uint32_t j = j0 + lane;
+      float s = -INFINITY;
+      if (j < npos) {
+        float dot = 0.0f;
 #pragma unroll 4
-      for (int c = 0; c < kHD / 8; c++) {
-        const uint4 raw = *reinterpret_cast<const uint4 *>(&kt[lane][c * 8]);
-        const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
+        for (int c = 0; c < kHD / 8; c++) {
+          const uint4 raw = *reinterpret_cast<const uint4 *>(&kt[buf][lane][c * 8]);
+          const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
-        for (int e = 0; e < 4; e++) {
-          const float2 f = half2_bits_to_float2(words[e]);
-          dot = fmaf(qs[w][8 * c + 2 * e], f.x, dot);
-          dot = fmaf(qs[w][8 * c + 2 * e + 1], f.y, dot);
+          for (int e = 0; e < 4; e++) {
+            const float2 f = half2_bits_to_float2(words[e]);
+            dot = fmaf(qs[w][8 * c + 2 * e], f.x, dot);
+            dot = fmaf(qs[w][8 * c + 2 * e + 1], f.y, dot);
+          }
         }
+        s = __fmul_rn(dot, inv_scale);
       }
-      s = __fmul_rn(dot, inv_scale);
-    }
-    const float mt = warp_max(s);
-    const float mn = fmaxf(m, mt);
-    const float corr = m == -INFINITY ? 0.0f : expf(m - mn);
-    const float pj = j < npos ? expf(s - mn) : 0.0f;
-    l = l * corr + warp_sum(pj);
+      const float mt = warp_max(s);
+      const float mn = fmaxf(m, mt);
+      const float corr = m == -INFINITY ? 0.0f : expf(m - mn);
+      const float pj = j < npos ? expf(s - mn) : 0.0f;
+      l = l * corr + warp_sum(pj);
 #pragma unroll
-    for (int e = 0; e < 4; e++) acc[e] *= corr;
-    const uint32_t cnt = min((uint32_t)kTile, npos - j0);
-    for (uint32_t u = 0; u < cnt; u++) {
-      const float pu = __shfl_sync(0xffffffffu, pj, u);
-      const uint2 raw = *reinterpret_cast<const uint2 *>(&vt[u][4 * lane]);
-      const float2 v0 = half2_bits_to_float2(raw.x), v1 = half2_bits_to_float2(raw.y);
-      acc[0] = fmaf(pu, v0.x, acc[0]);
-      acc[1] = fmaf(pu, v0.y, acc[1]);
-      acc[2] = fmaf(pu, v1.x, acc[2]);
-      acc[3] = fmaf(pu, v1.y, acc[3]);
+      for (int e = 0; e < 4; e++) acc[e] *= corr;
+      const uint32_t cnt = min((uint32_t)kTile, npos - j0);
+      for (uint32_t u = 0; u < cnt; u++) {
+        const float pu = __shfl_sync(0xffffffffu, pj, u);
+        const uint2 raw = *reinterpret_cast<const uint2 *>(&vt[buf][u][4 * lane]);
+        const float2 v0 = half2_bits_to_float2(raw.x), v1 = half2_bits_to_float2(raw.y);
+        acc[0] = fmaf(pu, v0.x, acc[0]);
+        acc[1] = fmaf(pu, v0.y, acc[1]);
+        acc[2] = fmaf(pu, v1.x, acc[2]);
+        acc[3] = fmaf(pu, v1.y, acc[3]);
+      }
+      m = mn;
     }
-    m = mn;
+    __syncthreads();  // every warp is done with buffer t & 1 before tile t + 2 is copied into it
   }
   if (!active) return;
   float4 o = make_float4(acc[0] / l, acc[1] / l, acc[2] / l, acc[3] / l);
