@@ -14,9 +14,8 @@
 //                          softmax, cpu/reference/ref_ops.c:307-349, to fp32
 //                          rounding).
 //   k_attn_prefill_tiled   the same, with each 32-position K/V tile staged
-//                          once in shared memory (as fp32) for all the
-//                          (row, head) warps of a GQA group and 8/G
-//                          consecutive rows.
+//                          once in shared memory for all the (row, head)
+//                          warps of a GQA group and 8/G consecutive rows.
 //   k_silu_glu_rows        silu(gate) * up of the fused gate/up GEMM output,
 //                          whose 16-row tiles hold 8 gate rows then the 8
 //                          matching up rows (ref_ops.c:219-228, 124-133 with
@@ -142,24 +141,21 @@ __device__ __forceinline__ float2 half2_bits_to_float2(uint32_t w) {
 
 // Tiled form: CTA per (sequence, kv head, block of 8/G consecutive rows)
 // with one warp per (row, query head of the GQA group), G = h/hk dividing
-// 8. Each 32-position K/V tile is read from the cache once per CTA,
-// converted to fp32 once as it is stored to shared memory, and used by all
-// the CTA's warps (8x less L2 traffic and conversion work than a tile per
-// warp); the next tile's loads are in flight in registers while the
-// current one is used. The arithmetic per warp is k_attn_prefill's. K rows
-// are padded to 132 floats so that the lanes' 16-byte reads of different
-// rows fall in different banks.
-constexpr int kTile = 32, kKPad = kHD + 4;
+// 8. The 32-position K and V tiles are loaded once per CTA into shared
+// memory and read by all its warps (8x less L2 traffic than a tile per
+// warp); the arithmetic per warp is k_attn_prefill's. K rows are padded to
+// 136 halves so that the lanes' 16-byte reads of different rows fall in
+// different banks.
+constexpr int kTile = 32, kKPad = kHD + 8;
 __global__ void __launch_bounds__(256) k_attn_prefill_tiled(uint32_t rows_per_seq, uint32_t p0, uint32_t h, uint32_t hk,
                                                             const float *__restrict__ qkv,
                                                             const __half *__restrict__ kc,
                                                             const __half *__restrict__ vc, uint64_t cap,
                                                             uint64_t seq_stride, float inv_scale,
                                                             float *__restrict__ out) {
-  __shared__ __align__(16) float kf[kTile][kKPad];
-  __shared__ __align__(16) float vf[kTile][kHD];
+  __shared__ __align__(16) __half kt[2][kTile][kKPad];  // double-buffered tiles
+  __shared__ __align__(16) __half vt[2][kTile][kHD];
   __shared__ __align__(16) float qs[8][kHD];
-  constexpr uint32_t kChunks = kTile * (kHD / 8) / 256;  // 16-byte chunks of K (and of V) per thread: 2
   const uint32_t G = h / hk, RB = 8 / G;
   const uint32_t lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const uint32_t b = blockIdx.z, kvh = blockIdx.y, i0 = blockIdx.x * RB;
@@ -173,73 +169,75 @@ __global__ void __launch_bounds__(256) k_attn_prefill_tiled(uint32_t rows_per_se
     for (uint32_t d = lane; d < kHD; d += 32) qs[w][d] = q[d];
   }
   const size_t base = (size_t)b * seq_stride + (size_t)kvh * cap * kHD;
-  // chunk c = threadIdx.x + 256 x: row c / 16, columns 8 (c % 16) .. + 7
-  uint4 kr[kChunks], vr[kChunks];
-  auto load_tile = [&](uint32_t t) {
-#pragma unroll
-    for (uint32_t x = 0; x < kChunks; x++) {
-      const uint32_t c = threadIdx.x + 256 * x, row = c / (kHD / 8), col = c % (kHD / 8);
-      kr[x] = vr[x] = make_uint4(0, 0, 0, 0);
-      if (t * kTile + row < nmax) {  // rows beyond the CTA's last position stay zero
-        kr[x] = __ldg(reinterpret_cast<const uint4 *>(kc + base + (size_t)(t * kTile + row) * kHD) + col);
-        vr[x] = __ldg(reinterpret_cast<const uint4 *>(vc + base + (size_t)(t * kTile + row) * kHD) + col);
-      }
-    }
-  };
   float m = -INFINITY, l = 0.0f, acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  // tile t of positions [32t, 32t + 32) into buffer t & 1: 32 rows x 16
+  // chunks of 16 B for K and for V, 2 + 2 asynchronous copies per thread;
+  // rows at or beyond nmax are zero-filled (source size 0, no read)
+  auto load_tile = [&](uint32_t t) {
+    const uint32_t buf = t & 1u, j0 = t * kTile;
+    for (uint32_t c = threadIdx.x; c < kTile * (kHD / 8); c += blockDim.x) {
+      const uint32_t row = c / (kHD / 8), col = c % (kHD / 8);
+      const bool in = j0 + row < nmax;
+      const size_t off = base + (size_t)(in ? j0 + row : 0) * kHD + col * 8;
+      const uint32_t n = in ? 16u : 0u;
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(&kt[buf][row][col * 8])),
+                   "l"(kc + off), "r"(n)
+                   : "memory");
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(&vt[buf][row][col * 8])),
+                   "l"(vc + off), "r"(n)
+                   : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
   const uint32_t ntiles = (nmax + kTile - 1) / kTile;
   load_tile(0);
   for (uint32_t t = 0; t < ntiles; t++) {
-    const uint32_t j0 = t * kTile;
-    __syncthreads();  // every warp is done with the previous tile (and qs is written)
+    const uint32_t j0 = t * kTile, buf = t & 1u;
+    if (t + 1 < ntiles) {
+      load_tile(t + 1);  // its buffer was last read in iteration t - 1, before that iteration's barrier
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
+    __syncthreads();  // tile t is in shared memory for every thread (and qs, the first time)
+    if (active && j0 < npos) {
+      const uint32_t j = j0 + lane;
+      float s = -INFINITY;
+      if (j < npos) {
+        float dot = 0.0f;
+#pragma unroll 4
+        for (int c = 0; c < kHD / 8; c++) {
+          const uint4 raw = *reinterpret_cast<const uint4 *>(&kt[buf][lane][c * 8]);
+          const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
-    for (uint32_t x = 0; x < kChunks; x++) {
-      const uint32_t c = threadIdx.x + 256 * x, row = c / (kHD / 8), col = 8 * (c % (kHD / 8));
-      const uint32_t kw[4] = {kr[x].x, kr[x].y, kr[x].z, kr[x].w}, vw[4] = {vr[x].x, vr[x].y, vr[x].z, vr[x].w};
-#pragma unroll
-      for (int e = 0; e < 4; e++) {
-        const float2 kk = half2_bits_to_float2(kw[e]), vv = half2_bits_to_float2(vw[e]);
-        kf[row][col + 2 * e] = kk.x;
-        kf[row][col + 2 * e + 1] = kk.y;
-        vf[row][col + 2 * e] = vv.x;
-        vf[row][col + 2 * e + 1] = vv.y;
+          for (int e = 0; e < 4; e++) {
+            const float2 f = half2_bits_to_float2(words[e]);
+            dot = fmaf(qs[w][8 * c + 2 * e], f.x, dot);
+            dot = fmaf(qs[w][8 * c + 2 * e + 1], f.y, dot);
+          }
+        }
+        s = __fmul_rn(dot, inv_scale);
       }
-    }
-    if (t + 1 < ntiles) load_tile(t + 1);  // in flight while tile t is used
-    __syncthreads();
-    if (!active || j0 >= npos) continue;
-    const uint32_t j = j0 + lane;
-    float s = -INFINITY;
-    if (j < npos) {
-      float dot = 0.0f;
-#pragma unroll 8
-      for (int c = 0; c < kHD / 4; c++) {
-        const float4 kk = *reinterpret_cast<const float4 *>(&kf[lane][4 * c]);
-        const float4 qq = *reinterpret_cast<const float4 *>(&qs[w][4 * c]);
-        dot = fmaf(qq.x, kk.x, dot);
-        dot = fmaf(qq.y, kk.y, dot);
-        dot = fmaf(qq.z, kk.z, dot);
-        dot = fmaf(qq.w, kk.w, dot);
-      }
-      s = __fmul_rn(dot, inv_scale);
-    }
-    const float mt = warp_max(s);
-    const float mn = fmaxf(m, mt);
-    const float corr = m == -INFINITY ? 0.0f : expf(m - mn);
-    const float pj = j < npos ? expf(s - mn) : 0.0f;
-    l = l * corr + warp_sum(pj);
+      const float mt = warp_max(s);
+      const float mn = fmaxf(m, mt);
+      const float corr = m == -INFINITY ? 0.0f : expf(m - mn);
+      const float pj = j < npos ? expf(s - mn) : 0.0f;
+      l = l * corr + warp_sum(pj);
 #pragma unroll
-    for (int e = 0; e < 4; e++) acc[e] *= corr;
-    const uint32_t cnt = min((uint32_t)kTile, npos - j0);
-    for (uint32_t u = 0; u < cnt; u++) {
-      const float pu = __shfl_sync(0xffffffffu, pj, u);
-      const float4 vv = *reinterpret_cast<const float4 *>(&vf[u][4 * lane]);
-      acc[0] = fmaf(pu, vv.x, acc[0]);
-      acc[1] = fmaf(pu, vv.y, acc[1]);
-      acc[2] = fmaf(pu, vv.z, acc[2]);
-      acc[3] = fmaf(pu, vv.w, acc[3]);
+      for (int e = 0; e < 4; e++) acc[e] *= corr;
+      const uint32_t cnt = min((uint32_t)kTile, npos - j0);
+      for (uint32_t u = 0; u < cnt; u++) {
+        const float pu = __shfl_sync(0xffffffffu, pj, u);
+        const uint2 raw = *reinterpret_cast<const uint2 *>(&vt[buf][u][4 * lane]);
+        const float2 v0 = half2_bits_to_float2(raw.x), v1 = half2_bits_to_float2(raw.y);
+        acc[0] = fmaf(pu, v0.x, acc[0]);
+        acc[1] = fmaf(pu, v0.y, acc[1]);
+        acc[2] = fmaf(pu, v1.x, acc[2]);
+        acc[3] = fmaf(pu, v1.y, acc[3]);
+      }
+      m = mn;
     }
-    m = mn;
+    __syncthreads();  // every warp is done with buffer t & 1 before tile t + 2 is copied into it
   }
   if (!active) return;
   float4 o = make_float4(acc[0] / l, acc[1] / l, acc[2] / l, acc[3] / l);
