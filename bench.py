@@ -389,6 +389,50 @@ def v0_sweep(dev, hbm_peak, peak_kind, iters=40):
     return {"peak": hbm_peak, "peak_kind": peak_kind, "unit": "GB/s", "shapes": out}
 
 
+def layer_config4(dev, hbm_peak, peak_kind, steps=30, warmup=5):
+    """Config 4: one Q4_0 decoder layer of the 8B shape, fp16 KV cache with
+    4096 past positions, batch 1, one token appended per step. Built as a
+    one-layer model with a 512-row Q8_0 embedding/lm head; the 4096 past
+    positions are written by a prefill of seeded token ids (the cache
+    values, not their distribution, are what the step reads). Timed with
+    CUDA events over graph-replayed steps; the step also runs the embedding
+    row, the final norm, the 2.2 MB lm head and the argmax."""
+    from prosperoai_b200 import _native
+    from prosperoai_b200.api import Model, Session
+    L = _native.load()
+    cfg = dict(CFG_8B, n_layer=1, vocab=512)
+    past = 4096
+    m = Model(dev, cfg)
+    m.synthesize(SEED + 4)
+    sess = Session(m, 1, past + warmup + steps + 8)
+    sess.prefill(np.random.default_rng(SEED + 4).integers(0, cfg["vocab"], (1, past)).astype(np.int32))
+    sess.run(warmup)
+    dev.sync()
+    e0, e1 = C.c_void_p(), C.c_void_p()
+    L.pai_b200_event_create(dev.ctx, C.byref(e0))
+    L.pai_b200_event_create(dev.ctx, C.byref(e1))
+    pos0 = sess.pos
+    L.pai_b200_event_record(dev.ctx, e0)
+    sess.run(steps)
+    L.pai_b200_event_record(dev.ctx, e1)
+    ms = C.c_float()
+    _native.check(L.pai_b200_event_elapsed(e0, e1, C.byref(ms)), "elapsed")
+    dev.sync()
+    sess.close()
+    m.close()
+    us = ms.value / steps * 1e3
+    E, F, hd, H, HK = cfg["n_embd"], cfg["n_ff"], cfg["head_dim"], cfg["n_head"], cfg["n_head_kv"]
+    weights = ((H + 2 * HK) * hd * E + E * H * hd + 3 * F * E) * 18 // 32  # Q4_0 bytes of the layer
+    kv = HK * (pos0 + steps // 2) * hd * 2 * 2  # K and V read at the middle timed position
+    alg = weights + kv + 4 * (E + F) * 2
+    gbs = alg / (us * 1e-6) / 1e9
+    return {"workload": "config 4: one Q4_0 decoder layer (8B shape), fp16 KV cache, batch 1",
+            "past_positions": past, "positions_timed": [pos0, pos0 + steps - 1], "us_per_step": round(us, 2),
+            "layer_steps_per_s": round(1e6 / us, 1), "algorithmic_bytes": int(alg), "gbs": round(gbs, 1),
+            "frac": round(gbs / hbm_peak, 4), "peak_kind": peak_kind,
+            "note": "the step also runs an embedding row, final norm, a 512-row Q8_0 lm head and argmax"}
+
+
 def prefill_timing(dev, sess, prompts, reps=3, pg=None):
     """Time-to-first-token of the config-5 prompt through
     pai_b200_session_prefill (tokens from host memory, the next token read
@@ -468,16 +512,15 @@ def cpu_baseline_port(dev, steps=3, prompt=24):
 
 def decode_variant(dev, model, batch, prompt, steps=20, warmup=3):
     """Decode tok/s of one more session of the same model: `batch`
-    independent sequences after a `prompt`-token seeded prompt, CUDA-graph
-    steps timed with CUDA events (as the headline line)."""
+    independent sequences after a `prompt`-token seeded prompt (appended by
+    pai_b200_session_prefill), CUDA-graph steps timed with CUDA events (as
+    the headline line)."""
     from prosperoai_b200 import _native
     from prosperoai_b200.api import Session
     L = _native.load()
     sess = Session(model, batch, prompt + warmup + steps + 8)
     ids = np.random.default_rng(SEED + batch).integers(0, CFG_8B["vocab"], (batch, prompt)).astype(np.int32)
-    for p in range(prompt):
-        sess.set_tokens(ids[:, p])
-        sess.run(1)
+    sess.prefill(ids)
     sess.run(warmup)
     dev.sync()
     e0, e1 = C.c_void_p(), C.c_void_p()
@@ -619,6 +662,7 @@ def gpu_arm(args):
         if world == 1 and not args.no_roofline:
             # configs 4-5 also name 8 independent sequences and a 4096-position cache
             variants = [decode_variant(dev, model, 8, P), decode_variant(dev, model, 1, 4096)]
+            variants.append(layer_config4(dev, hbm, kind))
         jobs = 1 if tp else world  # sequences advanced per step: TP ranks share one job
         value = jobs * B * K / (t_dev * 1e-3)
         result = {
