@@ -613,12 +613,15 @@ cudaError_t launch_tma_mb(pai_b200_ctx_t *ctx, dim3 grid, const V0Args &a, const
   constexpr uint32_t SB = BITS == 8 ? 256 : 128;
   size_t smem = (size_t)kTmaStages * SB * kTmaRows + (size_t)MB * a.per * sizeof(float);
   if (LAYOUT == kOpScales) smem += split_groups(a.per, a.g) * kStrip * sizeof(float);
-  static size_t opted = 0;  // dynamic shared memory this instantiation is opted in to
-  if (smem > opted) {
+  // dynamic shared memory this instantiation is opted in to, per device (the attribute is per device)
+  static size_t opted[64];
+  const int dev = b200_ctx_device(ctx);
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (smem > opted[dev]) {
     cudaError_t e = cudaFuncSetAttribute(k_gemm_v0_tma<BITS, LAYOUT, MB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
     if (e != cudaSuccess) return e;
-    opted = smem;
+    opted[dev] = smem;
   }
   return b200_launch(ctx, k_gemm_v0_tma<BITS, LAYOUT, MB>, grid, dim3(kTmaThreads), smem, a, b200_ctx_errflag(ctx),
                      map);
