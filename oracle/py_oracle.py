@@ -135,6 +135,7 @@ def ref():
              C.POINTER(C.POINTER(C.c_float)), C.POINTER(U64))
         _sig(R.pai_quantize_f32, C.c_int32, f32p, U64, C.POINTER(QuantScheme), i8p, f32p,
              C.POINTER(U64))
+        _sig(R.pai_quant_weights_bytes, U64, U64, C.POINTER(QuantScheme))
         _sig(R.pai_dequantize_f32, C.c_int32, i8p, f32p, U64, C.POINTER(QuantScheme), f32p)
         _sig(R.pai_opt_gemm_f32, C.c_int32, U64, U64, U64, f32p, f32p, f32p)
         _sig(R.pai_opt_gemm_w8_f32, C.c_int32, U64, U64, U64, f32p, i8p, f32p, U64,

@@ -129,3 +129,16 @@ int main(void) {
         subprocess.run(["gcc", "-std=c11", inc, f"-DHDR={hdr}", str(src), "-o", str(exe)], check=True)
         outs.append(subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout)
     assert outs[0] == outs[1], outs
+
+
+@pytest.mark.skipif(po.ref() is None, reason="reference build (oracle/_ref) not present")
+def test_v0_blob_bytes_match_reference():
+    """pai_b200_v0_blob_bytes is the reference's pai_quant_weights_bytes
+    (models/quantize.c:53-72): packed values plus one f32 scale per group."""
+    L = _native.load()
+    R = po.ref()
+    for bits in (8, 4):
+        for gs in (0, 1, 7, 32, 4096, 65535):
+            for n in (1, 2, 33, 1000, 4096 * 4096):
+                want = R.pai_quant_weights_bytes(n, C.byref(po.QuantScheme(bits, 1, gs)))
+                assert L.pai_b200_v0_blob_bytes(bits, gs, n) == want, (bits, gs, n)
