@@ -215,3 +215,28 @@ def test_file_above_two_gib_is_mapped(tmp_path):
     assert os.path.getsize(p) > (2 << 30)
     info = gguf_inspect(str(p))
     assert info["cfg"]["n_layer"] == CFG["n_layer"]
+
+
+@pytest.mark.parametrize("version", [1, 2])
+def test_older_container_versions_read_like_the_reference(tmp_path, version):
+    """Versions 1-3 are accepted with one layout (adapters/llama/gguf.c:148-152
+    reads 64-bit counts for all of them); both parsers read the same file."""
+    w = weights(CFG)
+    data = gw.container(gw.llama_kvs(CFG), gw.llama_tensors(CFG, w), version=version)
+    p = tmp_path / "m.gguf"
+    p.write_bytes(data)
+    info = gguf_inspect(str(p))
+    assert info["version"] == version and info["cfg"]["n_layer"] == CFG["n_layer"]
+    if po.ref() is not None:
+        st, f, buf = ref_open(data)
+        assert st == 0 and f.version == version and f.tensor_count == info["tensor_count"]
+        po.ref().pai_gguf_close(C.byref(f))
+
+
+def test_mistral_architecture_is_read(tmp_path):
+    """llama.c:309-313 accepts "llama" and "mistral" (keys prefixed by the name)."""
+    w = weights(CFG)
+    p = tmp_path / "m.gguf"
+    p.write_bytes(gw.container(gw.llama_kvs(CFG, arch="mistral"), gw.llama_tensors(CFG, w)))
+    info = gguf_inspect(str(p))
+    assert info["architecture"] == "mistral" and info["cfg"]["n_embd"] == CFG["n_embd"]
