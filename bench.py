@@ -811,12 +811,13 @@ def reference_arm(args):
               f"cpu/reference elementwise ops, 1 of 32 layers + 1/32 of the lm head per step, "
               f"f32 weights dequantised by the reference's dequant_block, attention over {P + 1} "
               f"cached positions; tok/s = 1/(32 x {dt * 1e3:.1f} ms)")
-    return {"metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": 0,
+    # n_gpus: the launch's N (the reference path runs on the host cores; its GPUs stay idle)
+    return {"metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(32 * dt * 1e3, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32 (weights dequantised from Q4_0/Q8_0)", "data": "synthetic",
             "config": {"workload": "Llama-3-8B-shaped Q4_0 decode (config 5)", "batch": 1,
-                       "prompt": PROMPT},
+                       "prompt": PROMPT, "device": f"host CPU, {threads} threads"},
             "impl": "reference",
             "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": kind,
                              "sample": sample},
