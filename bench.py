@@ -845,6 +845,8 @@ def main():
                     help="time only the config-2 prefill GEMM and print its line")
     ap.add_argument("--gemm-m", type=int, action="append",
                     help="with --gemm-only: token counts to time (repeatable; default 16 128 512 2048)")
+    ap.add_argument("--prefill-only", action="store_true",
+                    help="time only the config-5 prompt prefill (with --nvtx: one prefill inside the range prefill)")
     ap.add_argument("--v0-only", action="store_true",
                     help="time only the v0 grouped-scale GEMMs (w8/w4 ops and .pai blobs)")
     ap.add_argument("--nvtx", action="store_true",
@@ -857,6 +859,30 @@ def main():
         from prosperoai_b200.api import Device
         dev = Device(local)
         print(json.dumps(prefill_gemm(dev, ms=tuple(args.gemm_m or (16, 128, 512, 2048)))), flush=True)
+        dev.close()
+        return
+    if args.prefill_only:
+        # config-5 prompt prefill alone: one untimed prefill, then (inside the
+        # NVTX range "prefill" with --nvtx) the timed ones
+        from prosperoai_b200.api import Device, Model, Session
+        dev = Device(local)
+        model = Model(dev, dict(CFG_8B))
+        model.synthesize(SEED)
+        sess = Session(model, 1, PROMPT + 8)
+        prompts = np.random.default_rng(SEED).integers(0, CFG_8B["vocab"], (1, PROMPT)).astype(np.int32)
+        sess.prefill(prompts)
+        sess.reset()
+        dev.sync()
+        if args.nvtx:
+            import torch.cuda.nvtx as nvtx
+            nvtx.range_push("prefill")
+            sess.prefill(prompts)
+            nvtx.range_pop()
+            sess.reset()
+            dev.sync()
+        print(json.dumps(prefill_timing(dev, sess, prompts)), flush=True)
+        sess.close()
+        model.close()
         dev.close()
         return
     if args.v0_only:
