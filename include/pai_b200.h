@@ -467,14 +467,16 @@ pai_status_t pai_b200_tp_allreduce_f32(pai_b200_tp_t *tp, float *buf, uint64_t n
 pai_status_t pai_b200_model_set_tp(pai_b200_model_t *m, pai_b200_tp_t *tp);
 
 /* A decode session of `batch` independent sequences with an fp16 KV cache
- * of max_ctx positions per sequence ([layer][kv_head][pos][head_dim],
- * split by KV head across tensor-parallel ranks). */
+ * of max_ctx positions per sequence, rounded up to whole 128-position
+ * blocks ([layer][sequence][kv_head][pos][head_dim], split by KV head
+ * across tensor-parallel ranks). */
 pai_status_t pai_b200_session_create(pai_b200_model_t *m, uint32_t batch,
                                      uint32_t max_ctx, pai_b200_session_t **out);
 pai_status_t pai_b200_session_destroy(pai_b200_session_t *s);
 /* Position of the next token (equal for all sequences). */
 uint32_t pai_b200_session_pos(const pai_b200_session_t *s);
-/* Reset to position 0 (the cache contents are left; positions >= pos
+/* Reset to position 0 (pai_kv_cache_reset: the count of positions and
+ * reservations goes to zero; the cache contents are left, positions >= pos
  * are never read). */
 pai_status_t pai_b200_session_reset(pai_b200_session_t *s);
 /* One decode step from host memory: feed tokens[batch], run every layer
@@ -508,6 +510,38 @@ pai_status_t pai_b200_session_set_tokens(pai_b200_session_t *s,
 pai_status_t pai_b200_session_get_tokens(pai_b200_session_t *s, int32_t *tokens);
 /* Hidden state after the last step (device pointer, [batch][n_embd]). */
 const float *pai_b200_session_hidden(const pai_b200_session_t *s);
+
+/* ---- KV-cache position accounting ---------------------------------------------
+ * The session's cache keeps the bookkeeping of the reference's
+ * pai_kv_cache_t (cache/kv_cache.h:29-56): capacity in token positions,
+ * whole blocks of PAI_B200_KV_BLOCK_TOKENS positions (PAI_KV_BLOCK_TOKENS,
+ * kv_cache.h:27; the session's max_ctx is rounded up to whole blocks), a
+ * count of written positions, and reserve/reset with the status codes of
+ * pai_kv_cache_reserve (kv_cache.c:125-152). The blocks own device K/V:
+ * block b of (layer, sequence, kv head) is positions [128 b, 128 b + 128)
+ * of that head's contiguous fp16 rows. Decode steps and prompt prefill
+ * reserve their positions through the same accounting, so a full cache
+ * answers PAI_ERR_NOMEM as the reference's does. */
+#define PAI_B200_KV_BLOCK_TOKENS 128u
+typedef struct pai_b200_kv_info {
+  uint32_t capacity_tokens; /* positions per sequence (whole blocks)            */
+  uint32_t positions;       /* positions written (the next token's position)    */
+  uint32_t block_tokens;    /* PAI_B200_KV_BLOCK_TOKENS                          */
+  uint32_t n_layer, batch, kv_heads, head_dim; /* kv_heads: this rank's share   */
+  uint64_t layer_stride;    /* fp16 elements between layers                     */
+  uint64_t seq_stride;      /* ... between sequences of one layer               */
+  uint64_t head_stride;     /* ... between kv heads of one sequence (capacity x head_dim) */
+  uint64_t stats_blocks;    /* successful reservations (pai_kv_cache_t.stats_blocks) */
+  void *k, *v;              /* device: [layer][sequence][kv head][position][head_dim] fp16 */
+} pai_b200_kv_info_t;
+pai_status_t pai_b200_session_kv_info(const pai_b200_session_t *s, pai_b200_kv_info_t *out);
+/* pai_kv_cache_reserve for all sequences of the session: *out_pos = the
+ * first of `tokens` new positions, which the caller fills through the
+ * pointers of pai_b200_session_kv_info (device memory, e.g. a cache handed
+ * over from elsewhere); the next decode step attends over them and writes
+ * position *out_pos + tokens. PAI_ERR_INVALID_ARG for tokens == 0 or a NULL
+ * pointer; PAI_ERR_NOMEM when the positions do not fit. */
+pai_status_t pai_b200_session_kv_reserve(pai_b200_session_t *s, uint32_t tokens, uint32_t *out_pos);
 
 #ifdef __cplusplus
 }

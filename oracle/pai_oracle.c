@@ -787,6 +787,25 @@ void po_session_destroy(po_session_t *s) {
 
 const float *po_session_hidden(const po_session_t *s) { return s->x; }
 
+/* Cache rows of layer l ([hk][max_ctx][hd] fp16), for tests that start
+ * from a given cache, and the position of the next step (the positions
+ * below it must hold the cache contents to attend over). */
+uint16_t *po_session_kv(po_session_t *s, uint32_t layer, int v) {
+  const uint64_t kd = (uint64_t)s->cfg.n_head_kv * s->cfg.head_dim;
+  if (layer >= s->cfg.n_layer) {
+    return NULL;
+  }
+  return (v ? s->vc : s->kc) + (uint64_t)layer * kd * s->max_ctx;
+}
+
+int po_session_seek(po_session_t *s, uint32_t pos) {
+  if (pos > s->max_ctx) {
+    return -1;
+  }
+  s->pos = pos;
+  return 0;
+}
+
 int64_t po_session_step(po_session_t *s, uint32_t token, float *logits) {
   const po_model_cfg_t *c = &s->cfg;
   uint64_t E = c->n_embd, hd = c->head_dim, r2 = hd / 2;

@@ -172,6 +172,10 @@ void po_session_destroy(po_session_t *s);
 int64_t po_session_step(po_session_t *s, uint32_t token, float *logits);
 /* Hidden state after the last step (n_embd floats). */
 const float *po_session_hidden(const po_session_t *s);
+/* K (v = 0) or V (v = 1) cache of one layer: [hk][max_ctx][hd] fp16. */
+uint16_t *po_session_kv(po_session_t *s, uint32_t layer, int v);
+/* Continue at position pos (0 <= pos <= max_ctx). */
+int po_session_seek(po_session_t *s, uint32_t pos);
 
 #ifdef __cplusplus
 }

@@ -32,6 +32,16 @@ def build() -> None:
     subprocess.run(["make", "-s", "-C", HERE], check=True)
 
 
+def reference_dir() -> str:
+    """Location of the reference checkout: PAI_REFERENCE_DIR, else the
+    default that oracle/Makefile names (its only written copy)."""
+    env = os.environ.get("PAI_REFERENCE_DIR")
+    if env:
+        return env
+    r = subprocess.run(["make", "-s", "-C", HERE, "print-ref"], capture_output=True, text=True)
+    return r.stdout.strip()
+
+
 def _sig(fn, res, *args):
     fn.restype = res
     fn.argtypes = list(args)
@@ -74,6 +84,8 @@ def lib():
         _sig(L.po_session_destroy, None, C.c_void_p)
         _sig(L.po_session_step, C.c_int64, C.c_void_p, C.c_uint32, C.c_void_p)
         _sig(L.po_session_hidden, C.POINTER(C.c_float), C.c_void_p)
+        _sig(L.po_session_kv, C.POINTER(C.c_uint16), C.c_void_p, C.c_uint32, C.c_int)
+        _sig(L.po_session_seek, C.c_int, C.c_void_p, C.c_uint32)
         _lib = L
     return _lib
 
@@ -342,6 +354,7 @@ class Session:
                                          "attn_norm", "ffn_norm")])
         self.vocab = cfg["vocab"]
         self.n_embd = cfg["n_embd"]
+        self.max_ctx = max_ctx
         self.h = lib().po_session_create(C.byref(self.cfg), C.byref(self.w), max_ctx, threads)
         assert self.h, "oracle session allocation failed"
 
@@ -355,6 +368,19 @@ class Session:
     def hidden(self) -> np.ndarray:
         p = lib().po_session_hidden(self.h)
         return np.ctypeslib.as_array(p, (self.n_embd,)).copy()
+
+    def set_kv(self, layer: int, k: np.ndarray, v: np.ndarray) -> None:
+        """Cache rows of one layer, [kv_head][positions][head_dim] fp16 bits
+        (positions <= max_ctx), from position 0."""
+        for which, a in ((0, k), (1, v)):
+            a = np.ascontiguousarray(a, np.uint16)
+            hk, npos, hd = a.shape
+            dst = np.ctypeslib.as_array(lib().po_session_kv(self.h, layer, which),
+                                        (hk, self.max_ctx, hd))
+            dst[:, :npos, :] = a
+
+    def seek(self, pos: int) -> None:
+        assert lib().po_session_seek(self.h, pos) == 0
 
     def close(self):
         if self.h:

@@ -303,6 +303,15 @@ class Model:
             self.h = None
 
 
+class KvInfo(C.Structure):
+    """pai_b200_kv_info_t."""
+    _fields_ = [("capacity_tokens", C.c_uint32), ("positions", C.c_uint32),
+                ("block_tokens", C.c_uint32), ("n_layer", C.c_uint32), ("batch", C.c_uint32),
+                ("kv_heads", C.c_uint32), ("head_dim", C.c_uint32), ("layer_stride", C.c_uint64),
+                ("seq_stride", C.c_uint64), ("head_stride", C.c_uint64),
+                ("stats_blocks", C.c_uint64), ("k", C.c_void_p), ("v", C.c_void_p)]
+
+
 class Session:
     """Greedy decode session (pai_b200_session_*)."""
 
@@ -350,6 +359,34 @@ class Session:
 
     def reset(self):
         check(load().pai_b200_session_reset(self.h), "session_reset")
+
+    def kv_info(self) -> dict:
+        info = KvInfo()
+        check(load().pai_b200_session_kv_info(self.h, C.byref(info)), "session_kv_info")
+        return {f: getattr(info, f) for f, _ in KvInfo._fields_}
+
+    def kv_reserve(self, tokens: int) -> int:
+        """pai_kv_cache_reserve semantics: the first of `tokens` new positions."""
+        pos = C.c_uint32()
+        check(load().pai_b200_session_kv_reserve(self.h, tokens, C.byref(pos)), "session_kv_reserve")
+        return int(pos.value)
+
+    def write_kv(self, layer: int, seq: int, k: np.ndarray, v: np.ndarray, pos0: int = 0) -> None:
+        """Copy host fp16 rows [kv_head][positions][head_dim] into the cache of
+        one layer and sequence at positions pos0.. (this rank's kv heads)."""
+        info = self.kv_info()
+        L = load()
+        for base, a in ((info["k"], k), (info["v"], v)):
+            a = np.ascontiguousarray(a, np.float16)
+            hk, npos, hd = a.shape
+            assert hk == info["kv_heads"] and hd == info["head_dim"]
+            assert pos0 + npos <= info["capacity_tokens"]
+            for h in range(hk):
+                off = (layer * info["layer_stride"] + seq * info["seq_stride"] + h * info["head_stride"]
+                       + pos0 * hd) * 2
+                check(L.pai_b200_memcpy_h2d(self.model.dev.ctx, C.c_void_p(base + off), a[h].ctypes.data,
+                                            a[h].nbytes), "h2d")
+        self.model.dev.sync()
 
     def hidden(self) -> np.ndarray:
         p = load().pai_b200_session_hidden(self.h)

@@ -391,7 +391,8 @@ pai_status_t pai_b200_model_synthesize(pai_b200_model_t *m, uint64_t seed) {
 
 struct pai_b200_session {
   pai_b200_model_t *m;
-  uint32_t batch, max_ctx, pos;
+  uint32_t batch, max_ctx, pos; /* max_ctx: capacity in positions, whole 128-position blocks */
+  uint64_t kv_reservations;     /* pai_kv_cache_t.stats_blocks */
   int32_t *tok_in, *tok_out, *dpos; /* device */
   int32_t *htok;                    /* pinned host staging, 2*batch */
   float *x, *qkv, *att, *ox, *h, *logits, *cos_t, *sin_t;
@@ -504,6 +505,10 @@ pai_status_t pai_b200_session_create(pai_b200_model_t *m, uint32_t batch, uint32
   if (batch != 1 && batch != 2 && batch != 4 && batch != 8)
     return b200_fail(PAI_ERR_UNSUPPORTED, "session_create: batch %u (1, 2, 4 or 8)", batch);
   if (max_ctx == 0) return b200_fail(PAI_ERR_INVALID_ARG, "session_create: max_ctx 0");
+  if (max_ctx > 0x7FFFFFFFu - PAI_B200_KV_BLOCK_TOKENS)
+    return b200_fail(PAI_ERR_UNSUPPORTED, "session_create: max_ctx %u", max_ctx);
+  /* whole cache blocks (PAI_KV_BLOCK_TOKENS positions, cache/kv_cache.h:27) */
+  max_ctx = (max_ctx + PAI_B200_KV_BLOCK_TOKENS - 1) / PAI_B200_KV_BLOCK_TOKENS * PAI_B200_KV_BLOCK_TOKENS;
   if (m->tp > 1 && !m->tp_comm) return b200_fail(PAI_ERR_INIT, "session_create: tensor-parallel model without a communicator");
   ctx = m->ctx;
   c = &m->cfg;
@@ -614,12 +619,66 @@ pai_status_t pai_b200_session_destroy(pai_b200_session_t *s) {
 
 uint32_t pai_b200_session_pos(const pai_b200_session_t *s) { return s ? s->pos : 0; }
 
+/* Position accounting of pai_kv_cache_reserve (cache/kv_cache.c:125-152):
+ * tokens == 0 is an invalid argument, positions beyond the capacity are
+ * PAI_ERR_NOMEM; on success the first new position is returned and the
+ * count advances. Host bookkeeping only: the caller moves the device
+ * position (the decode graph advances it itself). */
+static pai_status_t kv_take(pai_b200_session_t *s, uint32_t tokens, uint32_t *first) {
+  if (tokens == 0) return b200_fail(PAI_ERR_INVALID_ARG, "kv_reserve: 0 tokens");
+  if ((uint64_t)s->pos + tokens > s->max_ctx)
+    return b200_fail(PAI_ERR_NOMEM, "kv_reserve: %u positions from %u exceed the %u-position cache", tokens, s->pos,
+                     s->max_ctx);
+  if (first) *first = s->pos;
+  s->pos += tokens;
+  s->kv_reservations++;
+  return PAI_OK;
+}
+
+static pai_status_t set_device_pos(pai_b200_session_t *s) {
+  int32_t p = (int32_t)s->pos;
+  pai_status_t st = pai_b200_sync(s->m->ctx); /* the staging word may still feed an earlier copy */
+  if (st) return st;
+  memcpy(s->htok, &p, 4);
+  st = pai_b200_memcpy_h2d(s->m->ctx, s->dpos, s->htok, 4);
+  return st ? st : pai_b200_sync(s->m->ctx);
+}
+
 pai_status_t pai_b200_session_reset(pai_b200_session_t *s) {
   pai_status_t st;
   if (!s) return b200_fail(PAI_ERR_INVALID_ARG, "session_reset: NULL");
   st = pai_b200_memset(s->m->ctx, s->dpos, 0, 4);
-  if (!st) s->pos = 0;
+  if (!st) {
+    s->pos = 0;
+    s->kv_reservations = 0;
+  }
   return st;
+}
+
+pai_status_t pai_b200_session_kv_info(const pai_b200_session_t *s, pai_b200_kv_info_t *out) {
+  if (!s || !out) return b200_fail(PAI_ERR_INVALID_ARG, "session_kv_info: NULL");
+  memset(out, 0, sizeof(*out));
+  out->capacity_tokens = s->max_ctx;
+  out->positions = s->pos;
+  out->block_tokens = PAI_B200_KV_BLOCK_TOKENS;
+  out->n_layer = s->m->cfg.n_layer;
+  out->batch = s->batch;
+  out->kv_heads = s->m->hkl;
+  out->head_dim = s->m->cfg.head_dim;
+  out->layer_stride = s->layer_stride;
+  out->seq_stride = s->seq_stride;
+  out->head_stride = (uint64_t)s->max_ctx * s->m->cfg.head_dim;
+  out->stats_blocks = s->kv_reservations;
+  out->k = s->kc;
+  out->v = s->vc;
+  return PAI_OK;
+}
+
+pai_status_t pai_b200_session_kv_reserve(pai_b200_session_t *s, uint32_t tokens, uint32_t *out_pos) {
+  pai_status_t st;
+  if (!s || !out_pos) return b200_fail(PAI_ERR_INVALID_ARG, "session_kv_reserve: NULL");
+  st = kv_take(s, tokens, out_pos);
+  return st ? st : set_device_pos(s);
 }
 
 static pai_status_t check_tokens(const pai_b200_session_t *s, const int32_t *tokens) {
@@ -652,11 +711,12 @@ pai_status_t pai_b200_session_run(pai_b200_session_t *s, uint32_t steps) {
   pai_status_t st = PAI_OK;
   if (!s) return b200_fail(PAI_ERR_INVALID_ARG, "session_run: NULL");
   if ((uint64_t)s->pos + steps > s->max_ctx)
-    return b200_fail(PAI_ERR_INVALID_ARG, "session_run: %u steps from position %u exceed the %u-position cache",
-                     steps, s->pos, s->max_ctx);
+    return b200_fail(PAI_ERR_NOMEM, "session_run: %u steps from position %u exceed the %u-position cache", steps,
+                     s->pos, s->max_ctx);
+  /* one reservation of one position per step, as a stepped decode makes */
   for (uint32_t i = 0; i < steps && !st; i++) {
     st = b200_graph_launch(s->m->ctx, s->graph, s->graph_kernels);
-    if (!st) s->pos++;
+    if (!st) st = kv_take(s, 1, NULL);
   }
   return st;
 }
@@ -748,8 +808,8 @@ pai_status_t pai_b200_session_prefill(pai_b200_session_t *s, const int32_t *toke
   const pai_b200_model_cfg_t *c = &m->cfg;
   const uint32_t B = s->batch, E = c->n_embd, hd = c->head_dim;
   if ((uint64_t)s->pos + n > s->max_ctx)
-    return b200_fail(PAI_ERR_INVALID_ARG, "session_prefill: %u positions from %u exceed the %u-position cache", n,
-                     s->pos, s->max_ctx);
+    return b200_fail(PAI_ERR_NOMEM, "session_prefill: %u positions from %u exceed the %u-position cache", n, s->pos,
+                     s->max_ctx);
   for (uint64_t i = 0; i < (uint64_t)B * n; i++)
     if (tokens[i] < 0 || (uint32_t)tokens[i] >= c->vocab)
       return b200_fail(PAI_ERR_INVALID_ARG, "session_prefill: token %d outside vocab %u", tokens[i], c->vocab);
@@ -781,10 +841,8 @@ pai_status_t pai_b200_session_prefill(pai_b200_session_t *s, const int32_t *toke
     for (uint32_t b = 0; !st && b < B; b++)
       st = pai_b200_memcpy_d2d(ctx, s->x + (uint64_t)b * E, s->pf_x + ((uint64_t)b * mc + mc - 1) * E,
                                (uint64_t)E * 4);
-    if (!st) {
-      s->pos += mc;
-      done += mc;
-    }
+    if (!st) st = kv_take(s, mc, NULL);
+    if (!st) done += mc;
   }
   /* logits of the last position, greedy token; it is also the next decode
    * step's input, and the device position follows the prompt */

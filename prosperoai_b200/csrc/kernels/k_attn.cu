@@ -624,8 +624,10 @@ pai_status_t noalloc_scratch(int device, float **out) {
     if (st) return st;
     void *p = nullptr;
     st = b200_cuda(cudaGetSymbolAddress(&p, g_attn_noalloc_scratch), "cudaGetSymbolAddress");
-    cudaSetDevice(prev);
+    // the calling thread gets its own device back, or an error says it did not
+    const pai_status_t back = b200_cuda(cudaSetDevice(prev), "cudaSetDevice (restoring the caller's device)");
     if (st) return st;
+    if (back) return back;
     addr[device] = (float *)p;
   }
   *out = addr[device];

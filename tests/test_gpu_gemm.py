@@ -53,3 +53,58 @@ def test_gemm_q4_0_config2_shape(dev):
     y = dev.alloc(m * n * 4)
     dev.gemm_q4_0(w, dev.put(x), y, m)
     assert np.array_equal(y.download(np.float32).reshape(m, n).view(np.uint32), got.view(np.uint32))
+
+
+def dense_ref(blocks, n, k, x):
+    """Every row at once: X . W^T in fp32 (numpy) over the oracle's dequantised
+    weights. Used to check ALL rows within the bar; the sampled rows below are
+    checked against the oracle's own GEMV (the reference's product order)."""
+    w = po.dequant(po.Q4_0, blocks, n * k).reshape(n, k)
+    return x @ w.T
+
+
+def check_all_rows(dev, m, n, k, seed, oracle_rows):
+    rng = np.random.default_rng(seed)
+    blocks = quantize(po.Q4_0, (rng.standard_normal(n * k) * 0.02).astype(np.float32))
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    w = PackedMatrix(dev, po.Q4_0, n, k, blocks)
+    y = dev.alloc(m * n * 4)
+    dev.gemm_q4_0(w, dev.put(x), y, m)
+    got = y.download(np.float32).reshape(m, n)
+    ref = dense_ref(blocks, n, k, x)
+    row_err = np.max(np.abs(got - ref), axis=1) / np.max(np.abs(ref), axis=1)
+    assert float(np.max(row_err)) <= TOL, (m, n, k, int(np.argmax(row_err)), float(np.max(row_err)))
+    for r in oracle_rows:
+        o = po.gemv_q(po.Q4_0, n, k, blocks, x[r], threads=8)
+        assert maxrel(got[r], o) <= TOL, (m, n, k, r, maxrel(got[r], o))
+    return got
+
+
+def tile_rows(m, bn=256):
+    """First, middle and last row of every 256-row token tile."""
+    rows = set()
+    for t0 in range(0, m, bn):
+        t1 = min(m, t0 + bn) - 1
+        rows.update({t0, (t0 + t1) // 2, t1})
+    return sorted(rows)
+
+
+@pytest.mark.parametrize("m,n,k", [(2048, 4864, 1024), (512, 19200, 512), (1000, 9472, 768)])
+def test_gemm_persistent_stream_k_branch(dev, m, n, k):
+    """Shapes with at least 148 output tiles (256 features x 256 tokens): the
+    GEMM runs one persistent CTA per SM over the (tile, K unit) stream, so
+    runs end inside tiles and split tiles are summed by their last
+    contributor. Every row is checked (all feature tiles on both sides of
+    every run boundary), and rows of every token tile against the oracle."""
+    ftiles, mtiles = -(-n // 256), -(-m // 256)
+    assert ftiles * mtiles >= 148
+    check_all_rows(dev, m, n, k, seed=m + n + k, oracle_rows=tile_rows(m))
+
+
+@pytest.mark.parametrize("m", [16, 128, 2048])
+def test_gemm_config2_full_shape(dev, m):
+    """Config 2 (W 14336 x 4096 Q4_0, fp32 out) at the M the benchmark times:
+    M=2048 is 448 tiles (the persistent stream-K branch), M=16 and 128 the
+    even split. All rows against the dense product, rows of every token tile
+    against the oracle."""
+    check_all_rows(dev, m, 14336, 4096, seed=40 + m, oracle_rows=tile_rows(m))

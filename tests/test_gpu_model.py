@@ -54,8 +54,8 @@ def synth_weights(dev, cfg, seed):
     return out
 
 
-def oracle_generate(cfg, w, prompt, steps, max_ctx):
-    s = po.Session(cfg, w, max_ctx, threads=8)
+def oracle_generate(cfg, w, prompt, steps, max_ctx, threads=8):
+    s = po.Session(cfg, w, max_ctx, threads=threads)
     tok = None
     for t in prompt:
         tok = s.step(int(t))
@@ -173,10 +173,10 @@ def test_session_bounds(dev):
     with pytest.raises(PaiError) as e:
         s.step(np.array([SMALL["vocab"]], np.int32))
     assert e.value.status == -1
-    for _ in range(4):
+    for _ in range(128):  # max_ctx 4 is rounded up to one 128-position cache block
         s.step(np.array([1], np.int32))
     with pytest.raises(PaiError) as e:
         s.step(np.array([1], np.int32))
-    assert e.value.status == -1
+    assert e.value.status == -2  # PAI_ERR_NOMEM, as pai_kv_cache_reserve (kv_cache.c:135-137)
     s.close()
     m.close()

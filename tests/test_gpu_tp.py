@@ -164,3 +164,69 @@ def test_tp2_prefill_then_decode_matches_oracle(dev):
     for r in range(2):
         assert "error" not in res[r], res[r]["error"]
         assert res[r]["tokens"] == [int(t) for t in want], f"rank {r}"
+
+
+# ---- the benchmark's 8B shape at 2, 4 and 8 ranks ----------------------------------
+
+TP_8B = dict(n_layer=32, n_embd=4096, n_head=32, n_head_kv=8, head_dim=128, n_ff=14336,
+             vocab=128256, eps=1e-5, rope_theta=500000.0, wtype=po.Q4_0, etype=po.Q8_0)
+SEED_8B = 8008
+
+
+@pytest.fixture(scope="module")
+def oracle_8b(dev):
+    """The oracle's greedy tokens for the 8B-shaped model, computed once for
+    every world size (skipped without a second GPU)."""
+    if _gpu_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from test_gpu_model import oracle_generate, synth_weights
+    prompt = [int(t) for t in np.random.default_rng(SEED_8B).integers(0, TP_8B["vocab"], 4)]
+    max_ctx = len(prompt) + STEPS
+    w = synth_weights(dev, TP_8B, SEED_8B)
+    want, _ = oracle_generate(TP_8B, w, prompt, STEPS, max_ctx, threads=max(8, os.cpu_count() or 8))
+    return prompt, max_ctx, [int(t) for t in want]
+
+
+def _worker_8b(rank, world, port, cfg, prompt, steps, max_ctx, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    out = {"rank": rank}
+    try:
+        import torch.distributed as dist
+        from prosperoai_b200.api import Device, Model, Session, TPComm
+        from test_gpu_model import gpu_generate
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=120))
+        dev = Device(rank)
+        comm = TPComm.over_group(dev, rank, world)
+        model = Model(dev, cfg, tp_rank=rank, tp_size=world)
+        model.synthesize(SEED_8B)
+        model.set_tp(comm)
+        sess = Session(model, 1, max_ctx)
+        out["tokens"] = gpu_generate(sess, prompt, steps)
+        dist.barrier()
+        sess.close()
+        comm.close()
+        model.close()
+        dev.close()
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:  # reported to the parent, which fails the test
+        out["error"] = repr(e)
+    q.put(out)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_8b_shape_decode_matches_oracle(oracle_8b, world):
+    """Column-parallel q/k/v/gate/up, row-parallel o/down with the peer-memory
+    exchange, KV cache split by KV head (one per rank at 8), vocabulary-sharded
+    lm head with the cross-rank argmax: 64 greedy tokens on every rank equal
+    the oracle's unsharded decode of the same weights."""
+    if _gpu_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    prompt, max_ctx, want = oracle_8b
+    res = _run_ranks(world, TP_8B, prompt, STEPS, max_ctx, target=_worker_8b)
+    for r in range(world):
+        assert "error" not in res[r], res[r]["error"]
+        assert res[r]["tokens"] == want, f"rank {r} of {world}"

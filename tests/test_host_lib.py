@@ -19,7 +19,7 @@ from prosperoai_b200.api import quantize, rope_tables
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 HEADER = os.path.join(ROOT, "include", "pai_b200.h")
-REF = "/root/reference"
+REF = po.reference_dir()
 
 
 def declared_functions():
