@@ -136,6 +136,13 @@ pai_status_t pai_b200_sync(pai_b200_ctx_t *ctx);
  * No reference counterpart. The environment variable PAI_B200_PDL=0
  * disables it for the process. */
 pai_status_t pai_b200_set_pdl(pai_b200_ctx_t *ctx, int on);
+/* Limit on every bounded wait inside this context's kernels (a bulk copy
+ * landing, a peer rank's stamp, a grid barrier), in nanoseconds; 0 restores
+ * the default of 2 s, the range is 1 ms to 60 s. A wait that runs out ends
+ * its kernel early and the next pai_b200_sync answers PAI_ERR_TIMEOUT: the
+ * counterpart of the reference's pai_gpu_wait_label(..., timeout_ns)
+ * (gpu/hal/hal.h:106-108). */
+pai_status_t pai_b200_set_wait_limit(pai_b200_ctx_t *ctx, uint64_t ns);
 
 /* Stream-ordered timing: event_record places a marker, event_elapsed
  * waits for both markers and returns milliseconds between them. */
@@ -462,6 +469,32 @@ uint32_t pai_b200_tp_rank(const pai_b200_tp_t *tp);
 uint32_t pai_b200_tp_size(const pai_b200_tp_t *tp);
 /* In-place sum over all ranks of n fp32 values, on the context's stream. */
 pai_status_t pai_b200_tp_allreduce_f32(pai_b200_tp_t *tp, float *buf, uint64_t n);
+/* The one-shot exchange the tensor-parallel decode uses, for callers that
+ * run their own ranks: every rank owns an exchange buffer (a header of
+ * arrival stamps and two slots of `cap` floats) in its HBM, maps the other
+ * ranks' buffers with their IPC handles, writes its partial sums into a
+ * slot of its own buffer, then calls pai_b200_tp_allreduce_add_f32, which
+ * stamps its arrival into every rank's header, waits (bounded by the
+ * context's wait limit) for all ranks' stamps, and adds the sum of all
+ * ranks' slots, in rank order, to x. Plain peer loads and stores over
+ * NVLink; no multicast. A rank whose peers never stamp gets
+ * PAI_ERR_TIMEOUT from the next pai_b200_sync; the buffers are then out of
+ * step and must be made again. No reference counterpart (the reference
+ * runs on one device). */
+#define PAI_B200_TP_HANDLE_BYTES 64
+pai_status_t pai_b200_tp_xbuf_create(pai_b200_ctx_t *ctx, uint64_t cap, void **buf,
+                                     uint8_t handle[PAI_B200_TP_HANDLE_BYTES]);
+pai_status_t pai_b200_tp_xbuf_open(pai_b200_ctx_t *ctx, const uint8_t handle[PAI_B200_TP_HANDLE_BYTES],
+                                   void **buf);
+/* Release a buffer: owned = 1 for one made by xbuf_create, 0 for a mapping. */
+pai_status_t pai_b200_tp_xbuf_release(pai_b200_ctx_t *ctx, void *buf, int owned);
+/* Device address of slot 0 or 1 of a buffer made with capacity `cap`. */
+float *pai_b200_tp_xbuf_slot(void *buf, uint32_t slot, uint64_t cap);
+/* x[0..n) += sum over ranks r (in rank order) of slot `slot` of bufs[r]
+ * (bufs[r] = rank r's buffer as mapped on this rank). */
+pai_status_t pai_b200_tp_allreduce_add_f32(pai_b200_ctx_t *ctx, void *const *bufs, uint32_t rank,
+                                           uint32_t nranks, uint32_t slot, uint64_t cap, float *x,
+                                           uint64_t n);
 /* Attach the communicator to a model created for the same rank and size
  * (before pai_b200_session_create; the model does not own it). */
 pai_status_t pai_b200_model_set_tp(pai_b200_model_t *m, pai_b200_tp_t *tp);

@@ -78,6 +78,12 @@ SIGNATURES = {
     "pai_b200_memset": (I32, [P, P, C.c_int, U64]),
     "pai_b200_sync": (I32, [P]),
     "pai_b200_set_pdl": (I32, [P, I32]),
+    "pai_b200_set_wait_limit": (I32, [P, U64]),
+    "pai_b200_tp_xbuf_create": (I32, [P, U64, PP, P]),
+    "pai_b200_tp_xbuf_open": (I32, [P, P, PP]),
+    "pai_b200_tp_xbuf_release": (I32, [P, P, C.c_int]),
+    "pai_b200_tp_xbuf_slot": (P, [P, U32, U64]),
+    "pai_b200_tp_allreduce_add_f32": (I32, [P, P, U32, U32, U32, U64, P, U64]),
     "pai_b200_event_create": (I32, [P, PP]),
     "pai_b200_event_destroy": (I32, [P, P]),
     "pai_b200_event_record": (I32, [P, P]),

@@ -146,6 +146,9 @@ uint32_t *b200_ctx_errflag(pai_b200_ctx_t *ctx);
  * points, whose inputs a preceding kernel may just have written.
  * PAI_B200_PDL=0 in the environment keeps it off. */
 int b200_ctx_pdl(pai_b200_ctx_t *ctx);
+/* Limit in nanoseconds on every bounded device wait of the context's
+ * kernels (pai_b200_set_wait_limit; 2 s by default). */
+uint64_t b200_ctx_wait_ns(pai_b200_ctx_t *ctx);
 void b200_ctx_set_pdl(pai_b200_ctx_t *ctx, int on);
 
 /* CUDA graph capture of everything launched on the context stream. */
@@ -242,6 +245,59 @@ pai_status_t b200_launch_attn_prefill(pai_b200_ctx_t *ctx, uint32_t rows, uint32
                                       const uint16_t *vc, uint64_t cap, uint64_t seq_stride, float *out);
 pai_status_t b200_launch_silu_glu_rows(pai_b200_ctx_t *ctx, uint64_t rows, uint32_t ff, const float *gu,
                                        float *hout);
+/* ---- persistent decode step (kernels/k_decode*.cu) --------------------------------
+ * One cooperative launch runs the layers of a decode step as a list of
+ * phases over one CTA per SM: a weight producer streams every matrix of the
+ * step, in order, into a shared-memory ring (it never waits for activations,
+ * so the next matrix is in flight while the current phase finishes);
+ * consumer warps run the phases in order and meet at a grid barrier between
+ * them. B200_PH_NORM quantises RMSNorm(xf) * gamma into xo (the lm head's
+ * operand); every GEMV phase uses the block type the plan was made for. */
+enum { B200_PH_EMBED = 0, B200_PH_GEMV = 1, B200_PH_ATTN = 2, B200_PH_NORM = 3 };
+enum { B200_X_XQ = 0, B200_X_NORM = 1 };
+typedef struct b200_phase {
+  uint32_t kind, type, epi, xsrc; /* B200_PH_*, block type, B200_EPI_*, B200_X_* */
+  const void *w;                  /* GEMV: packed matrix (256-byte aligned) */
+  uint64_t n, k;                  /* GEMV: rows, columns */
+  const float *xf, *gamma;        /* B200_X_NORM, B200_PH_NORM: fp32 rows [batch][k], RMSNorm gain */
+  b200_xq_t xq;                   /* B200_X_XQ: quantised input */
+  const float *res;               /* EPI_RESIDUAL: residual rows (may be y) */
+  float *y;                       /* output rows */
+  b200_xq_t xo;                   /* EPI_SILU_GLU / B200_PH_NORM: quantised output (limbs NULL: none) */
+  uint32_t layer, reserved;       /* ATTN: cache layer */
+} b200_phase_t;
+
+typedef struct b200_decode_args {
+  uint32_t batch;
+  float eps;                      /* RMSNorm epsilon of every norm phase */
+  /* embedding: x[b] = row tok_in[b] of the packed vocab x n_embd table */
+  uint32_t etype;
+  const void *emb;
+  uint64_t vocab, n_embd;
+  const int32_t *tok_in;
+  float *x;
+  /* attention: q|k|v rows [batch][(h + 2 hk) hd], fp16 cache
+   * [layer][seq][kv head][cap][hd], rotary tables [cap][hd/2] */
+  uint32_t h, hk, hd;
+  int32_t *pos;                   /* device position of the step's token (advanced at the end) */
+  uint64_t cap, seq_stride, layer_stride;
+  uint16_t *kc, *vc;
+  const float *cos_t, *sin_t;
+  const float *qkv;
+  float *att;
+  b200_xq_t xq_att;               /* attention output, quantised for the o projection */
+} b200_decode_args_t;
+
+typedef struct b200_decode_plan b200_decode_plan_t;
+/* Check the phase list against the kernel's limits, size and allocate its
+ * scratch (split-K partials, tickets, attention partials, barrier words)
+ * and upload the phases. PAI_ERR_UNSUPPORTED when a shape does not fit. */
+pai_status_t b200_decode_plan_create(pai_b200_ctx_t *ctx, uint32_t type, const b200_decode_args_t *args,
+                                     const b200_phase_t *phases, uint32_t nphases,
+                                     b200_decode_plan_t **out);
+pai_status_t b200_decode_launch(pai_b200_ctx_t *ctx, b200_decode_plan_t *plan);
+void b200_decode_plan_destroy(b200_decode_plan_t *plan);
+
 pai_status_t b200_launch_step_tail(pai_b200_ctx_t *ctx, uint32_t batch,
                                    int32_t *tok_out, int32_t *tok_in, int32_t *pos);
 pai_status_t b200_launch_synth_normal(pai_b200_ctx_t *ctx, float *dst, uint64_t rows,

@@ -402,6 +402,8 @@ struct pai_b200_session {
   uint64_t seq_stride, layer_stride;
   void *graph;
   uint32_t graph_kernels;
+  b200_decode_plan_t *plan; /* persistent decode kernel of the layers (NULL: one launch per op) */
+  int failed;               /* a bounded device wait ran out: the session refuses further work */
   pai_b200_tp_t *tp; /* tensor-parallel communicator, NULL on one GPU */
   /* prefill scratch (allocated by the first prefill): rows of hidden state,
    * normed rows, q|k|v, attention output, gate|up, silu*up, o/down output,
@@ -414,6 +416,8 @@ struct pai_b200_session {
 };
 
 /* Tensor-parallel hooks (csrc/host/b200_tp.c). */
+void b200_tp_mark_failed(pai_b200_tp_t *tp);
+int b200_tp_failed(const pai_b200_tp_t *tp);
 pai_status_t b200_tp_reserve(pai_b200_tp_t *tp, uint64_t cap);
 float *b200_tp_slot(pai_b200_tp_t *tp, uint32_t slot);
 pai_status_t b200_tp_allreduce_add(pai_b200_tp_t *tp, pai_b200_ctx_t *ctx, uint32_t slot, float *x, uint64_t n);
@@ -434,13 +438,66 @@ static pai_status_t norm_gemv(pai_b200_session_t *s, uint32_t type, uint64_t n, 
   return st;
 }
 
+/* The phase list of the persistent decode kernel: the embedding row, the
+ * five phases of every layer in the op order of llama.c:669-797, and the
+ * final RMSNorm into the lm head's operand. */
+static pai_status_t make_plan(pai_b200_session_t *s) {
+  pai_b200_model_t *m = s->m;
+  const pai_b200_model_cfg_t *c = &m->cfg;
+  const uint32_t E = c->n_embd, nph = 2 + 5 * c->n_layer;
+  b200_phase_t *ph = (b200_phase_t *)calloc(nph, sizeof(*ph));
+  b200_decode_args_t a;
+  uint32_t i = 0;
+  pai_status_t st;
+  if (!ph) return b200_fail(PAI_ERR_NOMEM, "session_create: host allocation");
+  ph[i++].kind = B200_PH_EMBED;
+  for (uint32_t l = 0; l < c->n_layer; l++) {
+    b200_phase_t *q = &ph[i++], *at = &ph[i++], *o = &ph[i++], *gu = &ph[i++], *dn = &ph[i++];
+    q->kind = B200_PH_GEMV, q->type = c->wtype, q->epi = B200_EPI_STORE, q->xsrc = B200_X_NORM;
+    q->w = m->wqkv[l], q->n = m->n_qkv, q->k = E, q->xf = s->x, q->gamma = m->attn_norm[l], q->y = s->qkv;
+    at->kind = B200_PH_ATTN, at->layer = l;
+    o->kind = B200_PH_GEMV, o->type = c->wtype, o->epi = B200_EPI_RESIDUAL, o->xsrc = B200_X_XQ;
+    o->w = m->wo[l], o->n = E, o->k = m->k_o, o->xq = s->xq_o, o->res = s->x, o->y = s->x;
+    gu->kind = B200_PH_GEMV, gu->type = c->wtype, gu->epi = B200_EPI_SILU_GLU, gu->xsrc = B200_X_NORM;
+    gu->w = m->wgu[l], gu->n = 2ull * m->ffl, gu->k = E, gu->xf = s->x, gu->gamma = m->ffn_norm[l];
+    gu->y = s->h, gu->xo = s->xq_h;
+    dn->kind = B200_PH_GEMV, dn->type = c->wtype, dn->epi = B200_EPI_RESIDUAL, dn->xsrc = B200_X_XQ;
+    dn->w = m->wdown[l], dn->n = E, dn->k = m->ffl, dn->xq = s->xq_h, dn->res = s->x, dn->y = s->x;
+  }
+  ph[i].kind = B200_PH_NORM, ph[i].xf = s->x, ph[i].gamma = m->output_norm, ph[i].k = E, ph[i].xo = s->xq_e;
+  i++;
+  memset(&a, 0, sizeof(a));
+  a.batch = s->batch;
+  a.eps = c->eps;
+  a.etype = c->etype, a.emb = m->tok_embd, a.vocab = c->vocab, a.n_embd = E, a.tok_in = s->tok_in, a.x = s->x;
+  a.h = m->hl, a.hk = m->hkl, a.hd = c->head_dim, a.pos = s->dpos;
+  a.cap = s->max_ctx, a.seq_stride = s->seq_stride, a.layer_stride = s->layer_stride;
+  a.kc = s->kc, a.vc = s->vc, a.cos_t = s->cos_t, a.sin_t = s->sin_t;
+  a.qkv = s->qkv, a.att = s->att, a.xq_att = s->xq_o;
+  st = b200_decode_plan_create(m->ctx, c->wtype, &a, ph, i, &s->plan);
+  free(ph);
+  return st;
+}
+
 static pai_status_t enqueue_step(pai_b200_session_t *s) {
   pai_b200_model_t *m = s->m;
   const pai_b200_model_cfg_t *c = &m->cfg;
   pai_b200_ctx_t *ctx = m->ctx;
   const uint32_t B = s->batch, E = c->n_embd, hd = c->head_dim;
+  pai_status_t st;
+  if (s->plan) {
+    /* the layers in one persistent launch, then the lm head, the greedy
+     * pick and the token feedback as separate launches */
+    st = b200_decode_launch(ctx, s->plan);
+    b200_ctx_set_pdl(ctx, 1);
+    if (!st) st = b200_launch_gemv(ctx, c->etype, B, m->vl, E, m->output, &s->xq_e, NULL, s->logits, B200_EPI_STORE, NULL);
+    if (!st) st = b200_launch_argmax(ctx, B, m->vl, s->logits, s->tok_out);
+    if (!st) st = b200_launch_step_tail(ctx, B, s->tok_out, s->tok_in, s->dpos);
+    b200_ctx_set_pdl(ctx, 0);
+    return st;
+  }
   b200_ctx_set_pdl(ctx, 1); /* every kernel of the step waits for its predecessor's writes */
-  pai_status_t st = b200_launch_embed(ctx, c->etype, B, c->vocab, E, m->tok_embd, s->tok_in, s->x);
+  st = b200_launch_embed(ctx, c->etype, B, c->vocab, E, m->tok_embd, s->tok_in, s->x);
   for (uint32_t l = 0; !st && l < c->n_layer; l++) {
     uint16_t *kc = s->kc + (uint64_t)l * s->layer_stride, *vc = s->vc + (uint64_t)l * s->layer_stride;
     st = norm_gemv(s, c->wtype, m->n_qkv, m->wqkv[l], m->attn_norm[l], s->qkv, B200_EPI_STORE, NULL);
@@ -510,6 +567,8 @@ pai_status_t pai_b200_session_create(pai_b200_model_t *m, uint32_t batch, uint32
   /* whole cache blocks (PAI_KV_BLOCK_TOKENS positions, cache/kv_cache.h:27) */
   max_ctx = (max_ctx + PAI_B200_KV_BLOCK_TOKENS - 1) / PAI_B200_KV_BLOCK_TOKENS * PAI_B200_KV_BLOCK_TOKENS;
   if (m->tp > 1 && !m->tp_comm) return b200_fail(PAI_ERR_INIT, "session_create: tensor-parallel model without a communicator");
+  if (m->tp_comm && b200_tp_failed(m->tp_comm))
+    return b200_fail(PAI_ERR_INIT, "session_create: the communicator's exchange timed out earlier; make a new one");
   ctx = m->ctx;
   c = &m->cfg;
   s = (pai_b200_session_t *)calloc(1, sizeof(*s));
@@ -561,6 +620,15 @@ pai_status_t pai_b200_session_create(pai_b200_model_t *m, uint32_t batch, uint32
   if (!st) st = pai_b200_sync(ctx);
   free(tab_c);
   free(tab_s);
+  /* Single GPU: the layers of a step run as one persistent kernel unless
+   * PAI_B200_PERSISTENT=0; shapes it does not take keep one launch per op. */
+  if (!st && m->tp == 1) {
+    const char *e = getenv("PAI_B200_PERSISTENT");
+    if (!(e && e[0] == '0')) {
+      st = make_plan(s);
+      if (st == PAI_ERR_UNSUPPORTED) st = PAI_OK;
+    }
+  }
   /* One eager step sizes the shared scratch and sets kernel attributes,
    * then the step is captured once as a CUDA graph. The eager step wrote
    * only position 0 of the cache, which the first real step overwrites. */
@@ -589,6 +657,7 @@ pai_status_t pai_b200_session_destroy(pai_b200_session_t *s) {
   ctx = s->m->ctx;
   pai_b200_sync(ctx);
   b200_graph_destroy(s->graph);
+  b200_decode_plan_destroy(s->plan);
   pai_b200_free(ctx, s->tok_in);
   pai_b200_free(ctx, s->tok_out);
   pai_b200_free(ctx, s->dpos);
@@ -642,6 +711,26 @@ static pai_status_t set_device_pos(pai_b200_session_t *s) {
   memcpy(s->htok, &p, 4);
   st = pai_b200_memcpy_h2d(s->m->ctx, s->dpos, s->htok, 4);
   return st ? st : pai_b200_sync(s->m->ctx);
+}
+
+/* A wait that ran out inside a step leaves the tensor-parallel exchange
+ * buffers out of step between ranks (a rank that timed out did not advance
+ * its call counters; its peers may have): the session and its communicator
+ * refuse further work until both are made again. On one GPU the session is
+ * marked the same way, since the step's state is unknown. */
+static pai_status_t seen(pai_b200_session_t *s, pai_status_t st) {
+  if (st == PAI_ERR_TIMEOUT) {
+    s->failed = 1;
+    if (s->tp) b200_tp_mark_failed(s->tp);
+  }
+  return st;
+}
+
+static pai_status_t usable(const pai_b200_session_t *s) {
+  if (s->failed)
+    return b200_fail(PAI_ERR_INIT, "session: a device wait ran out in an earlier step; destroy the session%s and "
+                                   "create it again", s->tp ? " and its tensor-parallel communicator" : "");
+  return PAI_OK;
 }
 
 pai_status_t pai_b200_session_reset(pai_b200_session_t *s) {
@@ -702,7 +791,7 @@ pai_status_t pai_b200_session_get_tokens(pai_b200_session_t *s, int32_t *tokens)
   pai_status_t st;
   if (!s || !tokens) return b200_fail(PAI_ERR_INVALID_ARG, "get_tokens: NULL");
   st = pai_b200_memcpy_d2h(s->m->ctx, s->htok + s->batch, s->tok_out, s->batch * 4);
-  if (!st) st = pai_b200_sync(s->m->ctx);
+  if (!st) st = seen(s, pai_b200_sync(s->m->ctx));
   if (!st) memcpy(tokens, s->htok + s->batch, s->batch * 4);
   return st;
 }
@@ -710,6 +799,8 @@ pai_status_t pai_b200_session_get_tokens(pai_b200_session_t *s, int32_t *tokens)
 pai_status_t pai_b200_session_run(pai_b200_session_t *s, uint32_t steps) {
   pai_status_t st = PAI_OK;
   if (!s) return b200_fail(PAI_ERR_INVALID_ARG, "session_run: NULL");
+  st = usable(s);
+  if (st) return st;
   if ((uint64_t)s->pos + steps > s->max_ctx)
     return b200_fail(PAI_ERR_NOMEM, "session_run: %u steps from position %u exceed the %u-position cache", steps,
                      s->pos, s->max_ctx);
@@ -813,7 +904,8 @@ pai_status_t pai_b200_session_prefill(pai_b200_session_t *s, const int32_t *toke
   for (uint64_t i = 0; i < (uint64_t)B * n; i++)
     if (tokens[i] < 0 || (uint32_t)tokens[i] >= c->vocab)
       return b200_fail(PAI_ERR_INVALID_ARG, "session_prefill: token %d outside vocab %u", tokens[i], c->vocab);
-  pai_status_t st = prefill_alloc(s);
+  pai_status_t st = usable(s);
+  if (!st) st = prefill_alloc(s);
   const uint32_t per_pass = PF_MAX_ROWS / B;
   for (uint32_t done = 0; !st && done < n;) {
     const uint32_t mc = n - done < per_pass ? n - done : per_pass, rows = B * mc, p0 = s->pos;
@@ -856,8 +948,8 @@ pai_status_t pai_b200_session_prefill(pai_b200_session_t *s, const int32_t *toke
     int32_t p = (int32_t)s->pos;
     memcpy(s->htok, &p, 4);
     st = pai_b200_memcpy_h2d(ctx, s->dpos, s->htok, 4);
-    if (!st) st = pai_b200_sync(ctx);
+    if (!st) st = seen(s, pai_b200_sync(ctx));
   }
   if (!st) st = pai_b200_session_get_tokens(s, next);
-  return st;
+  return seen(s, st);
 }

@@ -89,7 +89,14 @@ struct pai_b200_tp {
   float *pairs;                     /* argmax exchange: [rank][row][2] for up to 8 rows */
   void *xbuf[B200_TP_MAX_RANKS];    /* exchange buffers: own (allocated), peers (IPC-mapped) */
   uint64_t cap;                     /* floats per exchange slot */
+  int failed;                       /* an exchange timed out: the buffers are out of step */
 };
+
+void b200_tp_mark_failed(pai_b200_tp_t *tp) {
+  if (tp) tp->failed = 1;
+}
+
+int b200_tp_failed(const pai_b200_tp_t *tp) { return tp ? tp->failed : 0; }
 
 static void xbufs_release(pai_b200_tp_t *tp) {
   for (uint32_t r = 0; r < tp->size; r++) {

@@ -14,6 +14,12 @@
 
 #include "../b200_internal.h"
 
+// Bounded device waits (bulk copies landing, peers stamping, grid
+// barriers): the default limit and the range a caller may set.
+constexpr uint64_t kDefaultWaitNs = 2000000000ull;
+constexpr uint64_t kMinWaitNs = 1000000ull;
+constexpr uint64_t kMaxWaitNs = 60000000000ull;
+
 struct pai_b200_ctx {
   int device;
   cudaStream_t stream;
@@ -30,6 +36,7 @@ struct pai_b200_ctx {
   int capturing;
   int pdl;          // launch the decode-step kernels with programmatic dependent launch
   int pdl_allowed;  // PAI_B200_PDL=0 in the environment turns it off
+  uint64_t wait_ns; // limit on every bounded device wait of this context's kernels
   // Scratch buffers replaced by larger ones. A CUDA graph captured earlier
   // (a session's decode step) keeps the old addresses, so they are released
   // only at shutdown; growth at least doubles, which bounds their number.
@@ -106,6 +113,7 @@ extern "C" pai_status_t pai_b200_init(int device, pai_b200_ctx_t **out) {
   pai_b200_ctx *c = new (std::nothrow) pai_b200_ctx();
   if (!c) return b200_fail(PAI_ERR_NOMEM, "init: host allocation");
   c->device = device;
+  c->wait_ns = kDefaultWaitNs;
   {
     const char *e = getenv("PAI_B200_PDL");
     c->pdl_allowed = !(e && e[0] == '0');
@@ -155,6 +163,16 @@ extern "C" pai_status_t pai_b200_set_pdl(pai_b200_ctx_t *c, int on) {
   return PAI_OK;
 }
 extern "C" uint32_t *b200_ctx_errflag(pai_b200_ctx_t *c) { return c->err_dev; }
+extern "C" uint64_t b200_ctx_wait_ns(pai_b200_ctx_t *c) { return c->wait_ns; }
+extern "C" pai_status_t pai_b200_set_wait_limit(pai_b200_ctx_t *c, uint64_t ns) {
+  if (!c) return b200_fail(PAI_ERR_INVALID_ARG, "set_wait_limit: NULL context");
+  if (ns == 0) ns = kDefaultWaitNs;
+  if (ns < kMinWaitNs || ns > kMaxWaitNs)
+    return b200_fail(PAI_ERR_INVALID_ARG, "set_wait_limit: %llu ns outside [%llu, %llu]", (unsigned long long)ns,
+                     (unsigned long long)kMinWaitNs, (unsigned long long)kMaxWaitNs);
+  c->wait_ns = ns;
+  return PAI_OK;
+}
 
 extern "C" pai_status_t b200_ctx_xq(pai_b200_ctx_t *c, uint64_t bytes, void **buf) {
   if (bytes > c->xq_bytes) {

@@ -52,6 +52,7 @@ struct AttnParams {
   __half *kw, *vw;
   uint32_t *cnt;
   uint32_t *err;   // the context's error word (a bounded wait ran out)
+  uint64_t wait_ns;  // the context's limit on every wait
   uint32_t stage;  // positions of K (and of V) staged in shared memory per round
 };
 
@@ -188,7 +189,7 @@ __global__ void __launch_bounds__(128) k_attn_split(AttnParams p) {
       mbar_expect_tx(&kvbar, cnt * HD * 2);
       bulk_g2s(dst, src, cnt * HD * 2, &kvbar);
     }
-    if (!mbar_wait(&kvbar, kv_phase & 1u, 2000000000ull)) kvfail = 1;
+    if (!mbar_wait(&kvbar, kv_phase & 1u, p.wait_ns)) kvfail = 1;
     kv_phase++;
     __syncthreads();
     if (kvfail && t == 0) atomicExch(p.err, 1u);
@@ -201,7 +202,7 @@ __global__ void __launch_bounds__(128) k_attn_split(AttnParams p) {
       bulk_g2s(kst, kb, len * HD * 2, &kvbar);
       bulk_g2s(vst, vb, len * HD * 2, &kvbar);
     }
-    if (!mbar_wait(&kvbar, 0, 2000000000ull)) kvfail = 1;
+    if (!mbar_wait(&kvbar, 0, p.wait_ns)) kvfail = 1;
     kv_phase = 1;
     __syncthreads();
     if (kvfail) {
@@ -496,6 +497,7 @@ pai_status_t attn_setup(pai_b200_ctx_t *ctx, uint32_t batch, uint32_t h, uint32_
   p.inv_scale = 1.0f / sqrtf((float)hd);
   if (xq_out) p.xo = *xq_out;
   p.err = b200_ctx_errflag(ctx);
+  p.wait_ns = b200_ctx_wait_ns(ctx);
   const uint64_t slots = (uint64_t)batch * h * nsplit;
   float *scratch;
   uint32_t *counters;
@@ -685,6 +687,7 @@ extern "C" pai_status_t pai_b200_attn_decode_f16kv_noalloc(pai_b200_ctx_t *ctx, 
   p.opart = scratch;
   p.ml = scratch + h * nsplit * HD;
   p.err = b200_ctx_errflag(ctx);
+  p.wait_ns = b200_ctx_wait_ns(ctx);
   switch (G) {
     case 1: st = launch_split<1>(ctx, p, 1); break;
     case 2: st = launch_split<2>(ctx, p, 1); break;

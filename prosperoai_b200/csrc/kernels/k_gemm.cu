@@ -39,7 +39,6 @@ namespace {
 constexpr int kFT = 256;          // output features per CTA (two M=128 MMAs)
 constexpr int kBK = 64;           // K per stage: one 128-byte row of bf16
 constexpr int kAStage = kFT * kBK * 2;  // 32 KB of bf16 weights per stage
-constexpr uint64_t kGWaitLimit = 2000000000ull;
 
 // Stages are [rows][64] bf16 in the 128-byte swizzle layout: 16-byte chunk c
 // of row r sits at chunk position c ^ (r % 8).
@@ -94,6 +93,7 @@ struct GemmP {
   float *partial;          // split output tiles: [2 slots per CTA][BN][256] fp32
   uint32_t *cnt;           // tickets, one per (output tile, epilogue warp), left at zero
   uint32_t *err;
+  uint64_t wait_ns;  // the context's limit on every wait
   uint32_t m, n, ntiles, nunits;  // tokens, features, weight tiles, K units of 128
   uint32_t mtiles;                // token tiles; output tile t = (feature tile t / mtiles, token tile t % mtiles)
   uint64_t work;                  // output tiles x K units: the stream every CTA takes an equal run of
@@ -267,7 +267,7 @@ __global__ void __launch_bounds__(kGThreadsWS, 1) k_gemm_q4_0(GemmP p) {
       for (uint64_t w = w_begin; w < w_end && ok; w++, i++) {
         const uint32_t nv = min(16u, p.ntiles - tile0);
         const uint32_t rs = i % kRawStages;
-        if (i >= (uint32_t)kRawStages && !mbar_wait_spin(&rempty[rs], ((i / kRawStages) - 1) & 1u, kGWaitLimit)) {
+        if (i >= (uint32_t)kRawStages && !mbar_wait_spin(&rempty[rs], ((i / kRawStages) - 1) & 1u, p.wait_ns)) {
           ok = false;
           break;
         }
@@ -292,7 +292,7 @@ __global__ void __launch_bounds__(kGThreadsWS, 1) k_gemm_q4_0(GemmP p) {
       for (uint64_t w = w_begin; w < w_end && ok; w++) {
         for (uint32_t half = 0; half < 2; half++, j++) {
           const uint32_t s = j % SB;
-          if (j >= (uint32_t)SB && !mbar_wait_spin(&bempty[s], ((j / SB) - 1) & 1u, kGWaitLimit)) {
+          if (j >= (uint32_t)SB && !mbar_wait_spin(&bempty[s], ((j / SB) - 1) & 1u, p.wait_ns)) {
             ok = false;
             break;
           }
@@ -314,7 +314,7 @@ __global__ void __launch_bounds__(kGThreadsWS, 1) k_gemm_q4_0(GemmP p) {
       for (uint64_t w = w_begin; w < w_end && ok; w++, u = (u + 1 == U) ? 0 : u + 1) {
         const bool seg_first = w == w_begin || u == 0, seg_last = w + 1 == w_end || u == U - 1;
         if (seg_first && e > 0) {  // the previous segment's epilogue has read the accumulators
-          if (!mbar_wait_spin(&accempty, (e - 1) & 1u, kGWaitLimit)) {
+          if (!mbar_wait_spin(&accempty, (e - 1) & 1u, p.wait_ns)) {
             ok = false;
             break;
           }
@@ -322,8 +322,8 @@ __global__ void __launch_bounds__(kGThreadsWS, 1) k_gemm_q4_0(GemmP p) {
         }
         for (uint32_t half = 0; half < 2; half++, j++) {
           const uint32_t s = j % SA, sb = j % SB;
-          if (!mbar_wait_spin(&afull[s], (j / SA) & 1u, kGWaitLimit) ||
-              !mbar_wait_spin(&bfull[sb], (j / SB) & 1u, kGWaitLimit)) {
+          if (!mbar_wait_spin(&afull[s], (j / SA) & 1u, p.wait_ns) ||
+              !mbar_wait_spin(&bfull[sb], (j / SB) & 1u, p.wait_ns)) {
             ok = false;
             break;
           }
@@ -368,7 +368,7 @@ __global__ void __launch_bounds__(kGThreadsWS, 1) k_gemm_q4_0(GemmP p) {
     auto stage_half = [&](uint32_t j, auto half_tag) -> bool {
       constexpr int HALF = decltype(half_tag)::value;
       const uint32_t s = j % SA;
-      if (j >= (uint32_t)SA && !mbar_wait_sleep(&aempty[s], ((j / SA) - 1) & 1u, kGWaitLimit)) return false;
+      if (j >= (uint32_t)SA && !mbar_wait_sleep(&aempty[s], ((j / SA) - 1) & 1u, p.wait_ns)) return false;
       if (mine) dequant_half<HALF>(a_st + (size_t)s * kAStage, soff, q, sclp);
       fence_proxy_async();  // each lane's generic-proxy stores -> visible to the tensor core
       __syncwarp();
@@ -386,7 +386,7 @@ __global__ void __launch_bounds__(kGThreadsWS, 1) k_gemm_q4_0(GemmP p) {
     for (uint64_t w = w_begin; w < w_end && ok; w++, i++) {
       mine = (uint32_t)warp < min(16u, p.ntiles - ft * 16);
       const uint32_t rs = i % kRawStages;
-      if (!mbar_wait_sleep(&rfull[rs], (i / kRawStages) & 1u, kGWaitLimit)) {
+      if (!mbar_wait_sleep(&rfull[rs], (i / kRawStages) & 1u, p.wait_ns)) {
         ok = false;
         break;
       }
@@ -414,7 +414,7 @@ __global__ void __launch_bounds__(kGThreadsWS, 1) k_gemm_q4_0(GemmP p) {
       }
 
       // ---- segment end: epilogue of this warp's slice ----
-      if (!mbar_wait_sleep(&accfull, e & 1u, kGWaitLimit)) {
+      if (!mbar_wait_sleep(&accfull, e & 1u, p.wait_ns)) {
         ok = false;
         break;
       }
@@ -589,6 +589,7 @@ pai_status_t gemm_launch(pai_b200_ctx_t *ctx, uint32_t m, uint32_t n, uint32_t k
   p.partial = partial;
   p.cnt = cnt;
   p.err = b200_ctx_errflag(ctx);
+  p.wait_ns = b200_ctx_wait_ns(ctx);
   p.m = m;
   p.n = n;
   p.ntiles = (uint32_t)b200_ntiles(n);

@@ -70,7 +70,6 @@ template <int NT, int CONS>
 constexpr int kThreadsT = (CONS + 1) * 32;
 template <int NT, int CONS>
 constexpr size_t kSmemCap = (NT == 1 && CONS == 8) ? 110 * 1024 : 220 * 1024;  // dynamic shared memory per CTA
-constexpr uint64_t kWaitLimit = 2000000000ull;  // ns before a wait gives up (2 s)
 
 struct GemvP {
   const uint8_t *qs, *sc;
@@ -81,6 +80,7 @@ struct GemvP {
   uint32_t *tile_cnt;    // split-K tickets, one per tile, left at zero
   uint32_t *grp_cnt;     // SILU_GLU re-quantisation tickets, one per 64-row group
   uint32_t *err;         // host-mapped error word (timeouts)
+  uint64_t wait_ns;      // the context's limit on every wait
   b200_xq_t xo;          // SILU_GLU: re-quantised output (limbs == nullptr: none)
   uint32_t n, nout, units, ntiles, ngroups, upc, batch, npad;
   uint32_t resident;     // 1: all of x staged once per CTA (slot 0)
@@ -351,7 +351,7 @@ __global__ void __launch_bounds__(kThreadsT<NT, CONS>, 1) k_gemv(GemvP p) {
     for (int x = 0; x < kXSlots; x++) xuse[x] = 0;
     // x of quads [u0*XPU, u1*XPU) into slot xs, after the consumers released it
     auto stage_x = [&](int xs, uint32_t u0, uint32_t u1) {
-      if (xuse[xs] > 0 && !mbar_wait(&xempty[xs], (xuse[xs] - 1) & 1u, kWaitLimit)) {
+      if (xuse[xs] > 0 && !mbar_wait(&xempty[xs], (xuse[xs] - 1) & 1u, p.wait_ns)) {
         ok = false;
         return;
       }
@@ -379,7 +379,7 @@ __global__ void __launch_bounds__(kThreadsT<NT, CONS>, 1) k_gemv(GemvP p) {
     auto fill_stage = [&]() -> bool {
       if (wpos >= r1) return false;
       const uint32_t ua = wu, ub = min(w.u1, ua + U), slot = fill % kStages;
-      if (fill >= (uint32_t)kStages && !mbar_wait(&empty[slot], ((fill / kStages) - 1) & 1u, kWaitLimit)) {
+      if (fill >= (uint32_t)kStages && !mbar_wait(&empty[slot], ((fill / kStages) - 1) & 1u, p.wait_ns)) {
         ok = false;
         return false;
       }
@@ -427,9 +427,9 @@ __global__ void __launch_bounds__(kThreadsT<NT, CONS>, 1) k_gemv(GemvP p) {
       // (bounded), and stop; the consumers time out on their own waits.
       atomicExch(p.err, 1u);
       for (uint32_t f = fill > (uint32_t)kStages ? fill - kStages : 0; f < fill; f++)
-        mbar_wait(&full[f % kStages], (f / kStages) & 1u, kWaitLimit);
+        mbar_wait(&full[f % kStages], (f / kStages) & 1u, p.wait_ns);
       for (int x = 0; x < kXSlots; x++)
-        if (xuse[x]) mbar_wait(&xfull[x], (xuse[x] - 1) & 1u, kWaitLimit);
+        if (xuse[x]) mbar_wait(&xfull[x], (xuse[x] - 1) & 1u, p.wait_ns);
     }
     return;
   }
@@ -448,14 +448,14 @@ __global__ void __launch_bounds__(kThreadsT<NT, CONS>, 1) k_gemv(GemvP p) {
   Requant pend;
   if (p.xnorm) {
     norm_prologue<NT, CONS>(p, slot_view(0), c, lane, red);
-  } else if (p.resident && !mbar_wait(&xfull[0], 0, kWaitLimit)) {
+  } else if (p.resident && !mbar_wait(&xfull[0], 0, p.wait_ns)) {
     if (lane == 0) atomicExch(p.err, 1u);
     return;
   }
   for (uint64_t pos = r0; pos < r1;) {
     const Sub s = sub_at(p, pos, r0, r1);
     pos += s.u1 - s.u0;
-    if (!p.resident && !mbar_wait(&xfull[xs], (xuse / kXSlots) & 1u, kWaitLimit)) {
+    if (!p.resident && !mbar_wait(&xfull[xs], (xuse / kXSlots) & 1u, p.wait_ns)) {
       if (lane == 0) atomicExch(p.err, 1u);
       return;
     }
@@ -469,7 +469,7 @@ __global__ void __launch_bounds__(kThreadsT<NT, CONS>, 1) k_gemv(GemvP p) {
     }
     for (uint32_t ua = s.u0; ua < s.u1; ua += U) {
       const uint32_t slot = seq % kStages, par = (seq / kStages) & 1u;
-      if (!mbar_wait(&full[slot], par, kWaitLimit)) {
+      if (!mbar_wait(&full[slot], par, p.wait_ns)) {
         if (lane == 0) atomicExch(p.err, 1u);
         return;
       }
@@ -599,6 +599,7 @@ pai_status_t launch_t(pai_b200_ctx_t *ctx, GemvP p) {
   p.tile_cnt = cnt;
   p.grp_cnt = cnt + p.ntiles;
   p.err = b200_ctx_errflag(ctx);
+  p.wait_ns = b200_ctx_wait_ns(ctx);
   b200_launch(ctx, kern, dim3(grid), dim3(kThreadsT<NT, CONS>), smem, p);
   return b200_launched(ctx, 1, "k_gemv");
 }

@@ -35,7 +35,6 @@
 namespace {
 
 constexpr uint32_t kMaxCtas = 64;
-constexpr uint64_t kTpWaitLimit = 2000000000ull;
 constexpr size_t kHeader = 8192;  // counters [kMaxCtas] u64, flags [B200_TP_MAX_RANKS][kMaxCtas] u64
 static_assert(kMaxCtas * 8 + B200_TP_MAX_RANKS * kMaxCtas * 8 <= kHeader, "header");
 
@@ -46,6 +45,7 @@ struct TpArgs {
   float *x;      // residual in, sum out
   uint64_t n;
   uint32_t *err;
+  uint64_t wait_ns;  // the context's limit on the wait for the other ranks
 };
 
 __device__ __forceinline__ uint64_t *counters(uint8_t *b) { return reinterpret_cast<uint64_t *>(b); }
@@ -88,7 +88,7 @@ __global__ void __launch_bounds__(256) k_tp_allreduce_add(TpArgs a) {
           const uint64_t now = globaltimer_ns();
           if (it == 0) {
             t0 = now;
-          } else if (now - t0 > kTpWaitLimit) {
+          } else if (now - t0 > a.wait_ns) {
             ok = false;
             break;
           }
@@ -209,10 +209,52 @@ extern "C" pai_status_t b200_launch_tp_allreduce_add(pai_b200_ctx_t *ctx, void *
   a.x = x;
   a.n = n;
   a.err = b200_ctx_errflag(ctx);
+  a.wait_ns = b200_ctx_wait_ns(ctx);
   // one group of 4 elements per thread when it fits in kMaxCtas CTAs of 256
   const uint32_t ctas = (uint32_t)std::min<uint64_t>(kMaxCtas, std::max<uint64_t>(1, (n + 1023) / 1024));
   if ((uintptr_t)x % 16 || (cap * sizeof(float)) % 16)
     return b200_fail(PAI_ERR_INVALID_ARG, "tp_allreduce_add: x and slots must be 16-byte aligned");
   b200_launch(ctx, k_tp_allreduce_add, dim3(ctas), dim3(256), 0, a);
   return b200_launched(ctx, 1, "k_tp_allreduce_add");
+}
+
+// ---- public form of the exchange ------------------------------------------------------------
+
+extern "C" pai_status_t pai_b200_tp_xbuf_create(pai_b200_ctx_t *ctx, uint64_t cap, void **buf,
+                                                uint8_t handle[PAI_B200_TP_HANDLE_BYTES]) {
+  if (!ctx || !buf || !handle) return b200_fail(PAI_ERR_INVALID_ARG, "tp_xbuf_create: NULL");
+  if (cap == 0 || cap % 4 || cap > (1ull << 32)) return b200_fail(PAI_ERR_INVALID_ARG, "tp_xbuf_create: capacity");
+  static_assert(PAI_B200_TP_HANDLE_BYTES == B200_TP_HANDLE_BYTES, "handle size");
+  return b200_tp_xbuf_alloc(ctx, cap, buf, handle);
+}
+
+extern "C" pai_status_t pai_b200_tp_xbuf_open(pai_b200_ctx_t *ctx, const uint8_t handle[PAI_B200_TP_HANDLE_BYTES],
+                                              void **buf) {
+  if (!ctx || !buf || !handle) return b200_fail(PAI_ERR_INVALID_ARG, "tp_xbuf_open: NULL");
+  return b200_tp_xbuf_open(ctx, handle, buf);
+}
+
+extern "C" pai_status_t pai_b200_tp_xbuf_release(pai_b200_ctx_t *ctx, void *buf, int owned) {
+  if (!ctx) return b200_fail(PAI_ERR_INVALID_ARG, "tp_xbuf_release: NULL");
+  pai_status_t st = b200_ctx_use_device(ctx);
+  if (st) return st;
+  st = b200_cuda(cudaStreamSynchronize((cudaStream_t)b200_ctx_stream(ctx)), "tp_xbuf_release");
+  if (owned)
+    b200_tp_xbuf_free(buf);
+  else
+    b200_tp_xbuf_close(buf);
+  return st;
+}
+
+extern "C" float *pai_b200_tp_xbuf_slot(void *buf, uint32_t slot, uint64_t cap) {
+  return (buf && slot < 2) ? b200_tp_xbuf_slot(buf, slot, cap) : nullptr;
+}
+
+extern "C" pai_status_t pai_b200_tp_allreduce_add_f32(pai_b200_ctx_t *ctx, void *const *bufs, uint32_t rank,
+                                                      uint32_t nranks, uint32_t slot, uint64_t cap, float *x,
+                                                      uint64_t n) {
+  if (!ctx || !bufs || !x) return b200_fail(PAI_ERR_INVALID_ARG, "tp_allreduce_add: NULL");
+  for (uint32_t r = 0; r < nranks && r < B200_TP_MAX_RANKS; r++)
+    if (!bufs[r]) return b200_fail(PAI_ERR_INVALID_ARG, "tp_allreduce_add: buffer of rank %u is NULL", r);
+  return b200_launch_tp_allreduce_add(ctx, bufs, rank, nranks, slot, cap, x, n);
 }

@@ -66,6 +66,7 @@ struct V0Args {
   uint64_t per;       // rows of k per split, a multiple of kWarps
   float *part;        // [split][m][n] when gridDim.y > 1
   uint32_t *cnt;      // [strip] arrival counters, left at zero
+  uint64_t wait_ns;   // the context's limit on every wait (TMA ring)
 };
 
 // Signed value of flat element f (models/quantize.c:165-172).
@@ -305,7 +306,6 @@ __global__ void __launch_bounds__(kThreads) k_gemm_v0(V0Args p) {
 constexpr int kTmaRows = 32;    // rows per box (stage)
 constexpr int kTmaStages = 6;
 constexpr int kTmaThreads = kThreads + 32;  // 8 consumer warps + 1 producer warp
-constexpr uint64_t kTmaWaitLimit = 2000000000ull;  // ns before a wait gives up
 
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int32_t x, int32_t y, uint64_t *bar) {
   asm volatile(
@@ -347,7 +347,7 @@ __global__ void __launch_bounds__(kTmaThreads) k_gemm_v0_tma(V0Args p, uint32_t 
   const bool producer = warp == kWarps;
   auto issue = [&](uint32_t st) -> bool {  // stage st into slot st % kTmaStages
     const uint32_t slot = st % kTmaStages;
-    if (st >= (uint32_t)kTmaStages && !mbar_wait_spin(&empty[slot], ((st / kTmaStages) - 1) & 1u, kTmaWaitLimit))
+    if (st >= (uint32_t)kTmaStages && !mbar_wait_spin(&empty[slot], ((st / kTmaStages) - 1) & 1u, p.wait_ns))
       return false;
     mbar_expect_tx(&full[slot], STAGE);
     tma_load_2d(ring + (size_t)slot * STAGE, &map, (int32_t)(blockIdx.x * SB), (int32_t)(t0 + (uint64_t)st * kTmaRows),
@@ -388,7 +388,7 @@ __global__ void __launch_bounds__(kTmaThreads) k_gemm_v0_tma(V0Args p, uint32_t 
         atomicExch(err, 1u);
         failed = 1;
         for (uint32_t f = issued > (uint32_t)kTmaStages ? issued - kTmaStages : 0; f < issued; f++)
-          mbar_wait(&full[f % kTmaStages], (f / kTmaStages) & 1u, kTmaWaitLimit);
+          mbar_wait(&full[f % kTmaStages], (f / kTmaStages) & 1u, p.wait_ns);
       }
     }
   } else {
@@ -437,7 +437,7 @@ __global__ void __launch_bounds__(kTmaThreads) k_gemm_v0_tma(V0Args p, uint32_t 
     }
     for (uint32_t st = 0; st < nst; st++) {
       const uint32_t slot = st % kTmaStages;
-      if (!mbar_wait(&full[slot], (st / kTmaStages) & 1u, kTmaWaitLimit)) {
+      if (!mbar_wait(&full[slot], (st / kTmaStages) & 1u, p.wait_ns)) {
         if (lane == 0) atomicExch(err, 1u);
         failed = 1;
         break;
@@ -687,6 +687,7 @@ pai_status_t gemm_v0(pai_b200_ctx_t *ctx, uint32_t bits, int layout, uint64_t m,
     p.g = g;
     p.c = c + r0 * n;
     p.per = per;
+    p.wait_ns = b200_ctx_wait_ns(ctx);
     if (splits > 1) {
       pai_status_t st = b200_ctx_scratch(ctx, splits * mm * n, (uint32_t)strips, &p.part, &p.cnt);
       if (st) return st;
