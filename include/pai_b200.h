@@ -543,6 +543,16 @@ pai_status_t pai_b200_session_set_tokens(pai_b200_session_t *s,
 pai_status_t pai_b200_session_get_tokens(pai_b200_session_t *s, int32_t *tokens);
 /* Hidden state after the last step (device pointer, [batch][n_embd]). */
 const float *pai_b200_session_hidden(const pai_b200_session_t *s);
+/* Kernels one decode step launches: 4 when the layers run as the persistent
+ * decode kernel (layers, lm head GEMV, greedy pick, token feedback), else one
+ * launch per op. */
+uint32_t pai_b200_session_step_kernels(const pai_b200_session_t *s);
+/* Launch only the persistent layer kernel of a step, `reps` times, on the
+ * context's stream (asynchronous): for timing that kernel by itself. The
+ * position does not advance, so every launch appends at the same cache
+ * position and reads the same positions. PAI_ERR_UNSUPPORTED when the
+ * session runs one launch per op. */
+pai_status_t pai_b200_session_run_layers(pai_b200_session_t *s, uint32_t reps);
 
 /* ---- KV-cache position accounting ---------------------------------------------
  * The session's cache keeps the bookkeeping of the reference's

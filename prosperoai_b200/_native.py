@@ -152,6 +152,8 @@ SIGNATURES = {
     "pai_b200_session_get_tokens": (I32, [P, P]),
     "pai_b200_session_hidden": (P, [P]),
     "pai_b200_session_kv_info": (I32, [P, P]),
+    "pai_b200_session_step_kernels": (U32, [P]),
+    "pai_b200_session_run_layers": (I32, [P, U32]),
     "pai_b200_session_kv_reserve": (I32, [P, U32, P]),
 }
 

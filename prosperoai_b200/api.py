@@ -360,6 +360,15 @@ class Session:
     def reset(self):
         check(load().pai_b200_session_reset(self.h), "session_reset")
 
+    @property
+    def step_kernels(self) -> int:
+        """Kernels one decode step launches (4 on the persistent path)."""
+        return int(load().pai_b200_session_step_kernels(self.h))
+
+    def run_layers(self, reps: int = 1):
+        """Launch only the persistent layer kernel (timing; the position does not advance)."""
+        check(load().pai_b200_session_run_layers(self.h, reps), "session_run_layers")
+
     def kv_info(self) -> dict:
         info = KvInfo()
         check(load().pai_b200_session_kv_info(self.h, C.byref(info)), "session_kv_info")

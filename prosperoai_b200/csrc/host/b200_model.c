@@ -827,6 +827,17 @@ pai_status_t pai_b200_session_step(pai_b200_session_t *s, const int32_t *tokens,
 
 const float *pai_b200_session_hidden(const pai_b200_session_t *s) { return s ? s->x : NULL; }
 
+uint32_t pai_b200_session_step_kernels(const pai_b200_session_t *s) { return s ? s->graph_kernels : 0; }
+
+pai_status_t pai_b200_session_run_layers(pai_b200_session_t *s, uint32_t reps) {
+  pai_status_t st;
+  if (!s) return b200_fail(PAI_ERR_INVALID_ARG, "session_run_layers: NULL");
+  if (!s->plan) return b200_fail(PAI_ERR_UNSUPPORTED, "session_run_layers: the session runs one launch per op");
+  st = usable(s);
+  for (uint32_t i = 0; i < reps && !st; i++) st = b200_decode_launch(s->m->ctx, s->plan);
+  return st;
+}
+
 /* ---- prompt prefill ------------------------------------------------------------------ */
 
 /* Rows of prompt positions per pass: the prefill scratch holds this many

@@ -180,3 +180,33 @@ def test_session_bounds(dev):
     assert e.value.status == -2  # PAI_ERR_NOMEM, as pai_kv_cache_reserve (kv_cache.c:135-137)
     s.close()
     m.close()
+
+
+@pytest.mark.parametrize("wtype", [po.Q4_0, po.Q4_K, po.Q8_0])
+@pytest.mark.parametrize("batch", [1, 4])
+def test_persistent_kernel_agrees_with_one_launch_per_op(dev, wtype, batch, monkeypatch):
+    """The persistent decode kernel (one cooperative launch for every layer)
+    and the one-launch-per-op step compute the same decode: the same greedy
+    tokens, hidden states within 1e-4 max-abs-rel (the RMSNorm sums and
+    split-K partials are added in different orders)."""
+    cfg = dict(SMALL, wtype=wtype)
+    m = Model(dev, cfg)
+    m.synthesize(31 + wtype)
+    monkeypatch.setenv("PAI_B200_PERSISTENT", "0")
+    s_op = Session(m, batch, 64)
+    monkeypatch.delenv("PAI_B200_PERSISTENT")
+    s_pk = Session(m, batch, 64)
+    assert s_pk.step_kernels == 4 and s_op.step_kernels > 4
+    tok = np.random.default_rng(batch).integers(0, cfg["vocab"], batch).astype(np.int32)
+    t_op, t_pk = tok.copy(), tok.copy()
+    for i in range(24):
+        t_op = s_op.step(t_op)
+        t_pk = s_pk.step(t_pk)
+        assert np.array_equal(t_op, t_pk), i
+        h_op, h_pk = s_op.hidden(), s_pk.hidden()
+        assert np.max(np.abs(h_op - h_pk)) <= 1e-4 * np.max(np.abs(h_op)), i
+    s_pk.run_layers(2)  # timing entry point: launches only the layer kernel
+    dev.sync()
+    s_op.close()
+    s_pk.close()
+    m.close()
