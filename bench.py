@@ -235,9 +235,51 @@ def gemv_roofline(dev, hbm_peak, peak_kind, iters=40):
             "launch_mode": "back-to-back, programmatic dependent launch (as in the decode step)",
             "plain_launch": {"avg_launch_ms": round(per[0], 5),
                              "achieved": round(alg / (per[0] * 1e-3) / 1e9, 1)},
-            # DRAM bytes of one launch of this kernel on this workload, from an ncu
-            # capture (dram__bytes_read.sum + dram__bytes_write.sum = 66.18 MB + 0.67 MB)
-            "traffic": 66847744, "traffic_source": "ncu --set full, one launch"}
+            # DRAM bytes of one launch of this kernel on this workload, from one ncu
+            # capture (profiles/k_gemv_q4_0_gateup.md: dram__bytes_read.sum 66.18 MB
+            # + dram__bytes_write.sum 0.47 MB), not measured by this run
+            "traffic": 66650000, "traffic_source": "one ncu capture (profiles/k_gemv_q4_0_gateup.md)"}
+
+
+def layer_kernel_roofline(dev, model, sess, hbm_peak, peak_kind, reps=20):
+    """The dominant kernel of the step: the persistent layer kernel (every
+    layer of one decode step in one cooperative launch), timed alone with
+    CUDA events on its stream over `reps` back-to-back launches. Algorithmic
+    bytes per launch: every layer's packed weights (read once), the K/V cache
+    rows attended over, one embedding row and the new K/V rows. The position
+    does not advance between these launches (pai_b200_session_run_layers)."""
+    from prosperoai_b200 import _native
+    L = _native.load()
+    c = model.cfg
+    if sess.step_kernels != 4:
+        return None
+    e0, e1 = C.c_void_p(), C.c_void_p()
+    L.pai_b200_event_create(dev.ctx, C.byref(e0))
+    L.pai_b200_event_create(dev.ctx, C.byref(e1))
+    sess.run_layers(3)  # warm-up
+    dev.sync()
+    L.pai_b200_event_record(dev.ctx, e0)
+    sess.run_layers(reps)
+    L.pai_b200_event_record(dev.ctx, e1)
+    ms = C.c_float()
+    _native.check(L.pai_b200_event_elapsed(e0, e1, C.byref(ms)), "elapsed")
+    per_ms = ms.value / reps
+    E, vocab = c["n_embd"], c["vocab"]
+    lm_head = L.pai_b200_block_bytes(c["etype"], vocab * E)
+    emb_row = L.pai_b200_block_bytes(c["etype"], E)
+    layer_w = model.step_weight_bytes() - lm_head - emb_row
+    npos = sess.pos + 1
+    kv = c["n_layer"] * c["n_head_kv"] * c["head_dim"] * 2 * 2 * npos * sess.batch
+    alg = layer_w + kv + emb_row
+    achieved = alg / (per_ms * 1e-3) / 1e9
+    return {"kernel": "k_decode<Q4_0> (persistent: embedding row, 32 layers, final RMSNorm; 148 CTAs, "
+                      "cooperative launch)",
+            "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+            "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind,
+            "algorithmic_bytes_per_launch": int(alg),
+            "bytes_breakdown": {"layer_weights": int(layer_w), "kv_cache": int(kv), "embedding_row": int(emb_row)},
+            "positions_attended": npos, "avg_launch_ms": round(per_ms, 5), "launches_timed": reps,
+            "traffic": None, "traffic_source": "see profiles/k_decode_q4_0_8b.md (ncu capture)"}
 
 
 def gemv_sweep(dev, hbm_peak, peak_kind, iters=30):
@@ -510,15 +552,22 @@ def cpu_baseline_port(dev, steps=3, prompt=24):
                        f"full-model tok/s = 1/(32 x {dt * 1e3:.1f} ms)")}
 
 
-def decode_variant(dev, model, batch, prompt, steps=20, warmup=3):
+def decode_variant(dev, model, batch, prompt, steps=20, warmup=3, per_op=False):
     """Decode tok/s of one more session of the same model: `batch`
     independent sequences after a `prompt`-token seeded prompt (appended by
     pai_b200_session_prefill), CUDA-graph steps timed with CUDA events (as
-    the headline line)."""
+    the headline line). per_op: the step as one launch per op instead of the
+    persistent layer kernel (PAI_B200_PERSISTENT=0), for comparison."""
     from prosperoai_b200 import _native
     from prosperoai_b200.api import Session
     L = _native.load()
-    sess = Session(model, batch, prompt + warmup + steps + 8)
+    if per_op:
+        os.environ["PAI_B200_PERSISTENT"] = "0"
+    try:
+        sess = Session(model, batch, prompt + warmup + steps + 8)
+    finally:
+        os.environ.pop("PAI_B200_PERSISTENT", None)
+    kernels = sess.step_kernels
     ids = np.random.default_rng(SEED + batch).integers(0, CFG_8B["vocab"], (batch, prompt)).astype(np.int32)
     sess.prefill(ids)
     sess.run(warmup)
@@ -535,7 +584,8 @@ def decode_variant(dev, model, batch, prompt, steps=20, warmup=3):
     sess.close()
     return {"batch": batch, "prompt": prompt, "positions_timed": [pos0, pos0 + steps - 1],
             "ms_per_step": round(ms.value / steps, 4), "value": round(batch * steps / (ms.value * 1e-3), 3),
-            "unit": UNIT}
+            "unit": UNIT, "launches_per_step": kernels,
+            "path": "one launch per op" if kernels != 4 else "persistent layer kernel"}
 
 
 def gpu_arm(args):
@@ -652,7 +702,9 @@ def gpu_arm(args):
             gemm["by_m"][str(m)] = {"us": round(float(t[i]), 2), "tflops": round(tf, 1),
                                     "frac": round(tf / (peak_tf * world), 4)}
     if rank == 0:
-        roof = None if args.no_roofline else gemv_roofline(dev, hbm, kind)
+        layer_roof = None if args.no_roofline or tp else layer_kernel_roofline(dev, model, sess, hbm, kind)
+        gemv_roof = None if args.no_roofline else gemv_roofline(dev, hbm, kind)
+        roof = layer_roof or gemv_roof
         if gemm is None and not args.no_roofline:
             gemm = prefill_gemm(dev)
         sweep = None if args.no_roofline else gemv_sweep(dev, hbm, kind)
@@ -661,7 +713,8 @@ def gpu_arm(args):
         variants = None
         if world == 1 and not args.no_roofline:
             # configs 4-5 also name 8 independent sequences and a 4096-position cache
-            variants = [decode_variant(dev, model, 8, P), decode_variant(dev, model, 1, 4096)]
+            variants = [decode_variant(dev, model, 8, P), decode_variant(dev, model, 1, 4096),
+                        decode_variant(dev, model, 1, P, per_op=True)]
             variants.append(layer_config4(dev, hbm, kind))
         jobs = 1 if tp else world  # sequences advanced per step: TP ranks share one job
         value = jobs * B * K / (t_dev * 1e-3)
@@ -682,7 +735,12 @@ def gpu_arm(args):
             "e2e": {"value": round(jobs * B * K / (t_e2e * 1e-3), 3), "unit": UNIT,
                     "h2d_bytes_per_step": 4 * B, "d2h_bytes_per_step": 4 * B},
             "gpu_launches": int(launches),
+            "decode_path": (f"persistent layer kernel + lm head GEMV + argmax + token feedback "
+                            f"({sess.step_kernels} launches per step, one CUDA graph)"
+                            if sess.step_kernels == 4 else
+                            f"one launch per op ({sess.step_kernels} per step, one CUDA graph)"),
             "roofline": roof,
+            "gemv_roofline": gemv_roof if roof is not gemv_roof else None,
             "prefill_gemm": gemm,
             "prompt_prefill": prefill,
             "decode_variants": variants,
