@@ -159,7 +159,7 @@ void b200_graph_destroy(void *exec);
 
 /* ---- kernel launchers (csrc/kernels) ----------------------------------------------- */
 
-enum { B200_EPI_STORE = 0, B200_EPI_RESIDUAL = 1, B200_EPI_SILU_GLU = 2 };
+enum { B200_EPI_STORE = 0, B200_EPI_RESIDUAL = 1, B200_EPI_SILU_GLU = 2, B200_EPI_PUSH = 3 };
 
 /* GEMV over a packed matrix with x given as xq (batch vectors of k).
  * B200_EPI_SILU_GLU: each 16-row tile holds 8 gate rows then the 8 matching
@@ -219,6 +219,13 @@ pai_status_t b200_launch_argmax_pair(pai_b200_ctx_t *ctx, uint64_t rows, uint64_
                                      const float *logits, float *pair);
 pai_status_t b200_launch_argmax_ranks(pai_b200_ctx_t *ctx, uint32_t rows, uint32_t nranks, const float *pairs,
                                       int32_t *out);
+/* Tensor-parallel greedy pick over peer memory: this shard's (maximum,
+ * index + v0) per row is stored into every rank's landing buffer, the last
+ * CTA waits (bounded) for all ranks' pairs, merges them in rank order,
+ * writes tok_out and the next step's tok_in and advances *pos. */
+pai_status_t b200_launch_argmax_peer(pai_b200_ctx_t *ctx, uint64_t rows, uint64_t n, uint32_t v0,
+                                     const float *logits, void *const *land, uint32_t rank, uint32_t nranks,
+                                     int32_t *tok_out, int32_t *tok_in, int32_t *pos);
 
 /* Tensor-parallel exchange over NVLink peer memory (kernels/k_tp.cu). */
 #define B200_TP_MAX_RANKS 8
@@ -227,6 +234,9 @@ pai_status_t b200_launch_argmax_ranks(pai_b200_ctx_t *ctx, uint32_t rows, uint32
  * and its IPC handle for the other ranks. */
 pai_status_t b200_tp_xbuf_alloc(pai_b200_ctx_t *ctx, uint64_t cap, void **buf, uint8_t handle[B200_TP_HANDLE_BYTES]);
 pai_status_t b200_tp_xbuf_open(pai_b200_ctx_t *ctx, const uint8_t handle[B200_TP_HANDLE_BYTES], void **buf);
+/* `bytes` of zeroed device memory and its IPC handle (close with
+ * b200_tp_xbuf_free; peers map it with b200_tp_xbuf_open). */
+pai_status_t b200_ipc_alloc(pai_b200_ctx_t *ctx, uint64_t bytes, void **buf, uint8_t handle[B200_TP_HANDLE_BYTES]);
 void b200_tp_xbuf_close(void *buf);
 void b200_tp_xbuf_free(void *buf);
 float *b200_tp_xbuf_slot(void *buf, uint32_t slot, uint64_t cap);
@@ -253,7 +263,26 @@ pai_status_t b200_launch_silu_glu_rows(pai_b200_ctx_t *ctx, uint64_t rows, uint3
  * consumer warps run the phases in order and meet at a grid barrier between
  * them. B200_PH_NORM quantises RMSNorm(xf) * gamma into xo (the lm head's
  * operand); every GEMV phase uses the block type the plan was made for. */
-enum { B200_PH_EMBED = 0, B200_PH_GEMV = 1, B200_PH_ATTN = 2, B200_PH_NORM = 3 };
+enum { B200_PH_EMBED = 0, B200_PH_GEMV = 1, B200_PH_ATTN = 2, B200_PH_NORM = 3, B200_PH_XCHG = 4 };
+
+/* Landing buffer of the tensor-parallel persistent decode: one per rank in
+ * its HBM, mapped into every other rank with CUDA IPC.
+ *   header (B200_LAND_HDR bytes), u64 words: [0] arrivals of row exchanges
+ *   (every CTA of every rank adds 1 per exchange), [1] row exchanges this
+ *   rank completed, [2] arrivals of greedy pairs (every rank adds 1 per
+ *   step), [3] greedy exchanges this rank completed;
+ *   row slots [2 parities][ranks][rows] fp32 (rows = batch x n_embd): the
+ *   o/down GEMV epilogue of rank r stores its partial rows into slot
+ *   [parity][r] of every rank's buffer (B200_EPI_PUSH);
+ *   pair slots [2 parities][ranks][8][2] fp32: each rank's (maximum, index)
+ *   of its vocabulary shard per sequence. */
+#define B200_LAND_HDR 256u
+static inline B200_HD uint64_t b200_land_bytes(uint32_t nranks, uint64_t rows) {
+  return B200_LAND_HDR + (2ull * nranks * rows + 2ull * nranks * 16u) * 4u;
+}
+static inline B200_HD uint64_t b200_land_pairs_off(uint32_t nranks, uint64_t rows) {
+  return B200_LAND_HDR + 2ull * nranks * rows * 4u;
+}
 enum { B200_X_XQ = 0, B200_X_NORM = 1 };
 typedef struct b200_phase {
   uint32_t kind, type, epi, xsrc; /* B200_PH_*, block type, B200_EPI_*, B200_X_* */
@@ -264,7 +293,8 @@ typedef struct b200_phase {
   const float *res;               /* EPI_RESIDUAL: residual rows (may be y) */
   float *y;                       /* output rows */
   b200_xq_t xo;                   /* EPI_SILU_GLU / B200_PH_NORM: quantised output (limbs NULL: none) */
-  uint32_t layer, reserved;       /* ATTN: cache layer */
+  uint32_t layer;                 /* ATTN: cache layer */
+  uint32_t xi;                    /* EPI_PUSH GEMV and B200_PH_XCHG: index of the row exchange in the step */
 } b200_phase_t;
 
 typedef struct b200_decode_args {
@@ -286,6 +316,10 @@ typedef struct b200_decode_args {
   const float *qkv;
   float *att;
   b200_xq_t xq_att;               /* attention output, quantised for the o projection */
+  /* tensor parallelism: rank of nranks, every rank's landing buffer as
+   * mapped here (nranks = 1: none) */
+  uint32_t rank, nranks;
+  void *land[B200_TP_MAX_RANKS];
 } b200_decode_args_t;
 
 typedef struct b200_decode_plan b200_decode_plan_t;

@@ -89,6 +89,8 @@ struct pai_b200_tp {
   float *pairs;                     /* argmax exchange: [rank][row][2] for up to 8 rows */
   void *xbuf[B200_TP_MAX_RANKS];    /* exchange buffers: own (allocated), peers (IPC-mapped) */
   uint64_t cap;                     /* floats per exchange slot */
+  void *land[B200_TP_MAX_RANKS];    /* landing buffers of the persistent decode: own, peers */
+  uint64_t land_rows;               /* rows per landing slot */
   int failed;                       /* an exchange timed out: the buffers are out of step */
 };
 
@@ -97,6 +99,66 @@ void b200_tp_mark_failed(pai_b200_tp_t *tp) {
 }
 
 int b200_tp_failed(const pai_b200_tp_t *tp) { return tp ? tp->failed : 0; }
+
+static void lands_release(pai_b200_tp_t *tp) {
+  for (uint32_t r = 0; r < tp->size; r++) {
+    if (!tp->land[r]) continue;
+    if (r == tp->rank)
+      b200_tp_xbuf_free(tp->land[r]);
+    else
+      b200_tp_xbuf_close(tp->land[r]);
+    tp->land[r] = NULL;
+  }
+  tp->land_rows = 0;
+}
+
+/* Allocate `bytes` of zeroed device memory on every rank and map every
+ * rank's allocation here (out[r]). Collective: the IPC handles travel by an
+ * NCCL all-gather. */
+static pai_status_t ipc_exchange(pai_b200_tp_t *tp, uint64_t bytes, void **out) {
+  uint8_t *dev_h = NULL, *host_h = NULL, mine[B200_TP_HANDLE_BYTES];
+  pai_status_t st = b200_ipc_alloc(tp->ctx, bytes, &out[tp->rank], mine);
+  if (!st) st = pai_b200_alloc(tp->ctx, (uint64_t)tp->size * B200_TP_HANDLE_BYTES, (void **)&dev_h);
+  if (!st) {
+    host_h = (uint8_t *)malloc((size_t)tp->size * B200_TP_HANDLE_BYTES);
+    if (!host_h) st = b200_fail(PAI_ERR_NOMEM, "tp: host allocation");
+  }
+  if (!st) st = pai_b200_memcpy_h2d(tp->ctx, dev_h + (uint64_t)tp->rank * B200_TP_HANDLE_BYTES, mine, sizeof mine);
+  if (!st)
+    st = nccl_check(g_nccl.all_gather(dev_h + (uint64_t)tp->rank * B200_TP_HANDLE_BYTES, dev_h, B200_TP_HANDLE_BYTES,
+                                      NCCL_UINT8, tp->comm, b200_ctx_stream(tp->ctx)),
+                    "ncclAllGather (exchange handles)");
+  if (!st) st = pai_b200_memcpy_d2h(tp->ctx, host_h, dev_h, (uint64_t)tp->size * B200_TP_HANDLE_BYTES);
+  if (!st) st = pai_b200_sync(tp->ctx);
+  for (uint32_t r = 0; !st && r < tp->size; r++)
+    if (r != tp->rank) st = b200_tp_xbuf_open(tp->ctx, host_h + (uint64_t)r * B200_TP_HANDLE_BYTES, &out[r]);
+  free(host_h);
+  pai_b200_free(tp->ctx, dev_h);
+  return st;
+}
+
+/* Landing buffers of `rows` floats per slot on every rank (the persistent
+ * decode's row exchanges and greedy pairs), mapped here; collective, every
+ * rank with the same rows. They start zeroed, so every rank's counters
+ * begin in step. */
+pai_status_t b200_tp_land(pai_b200_tp_t *tp, uint64_t rows, void **out) {
+  pai_status_t st;
+  if (!tp || !out) return b200_fail(PAI_ERR_INVALID_ARG, "tp_land: NULL");
+  if (tp->failed) return b200_fail(PAI_ERR_INIT, "tp_land: the communicator's exchange timed out earlier");
+  if (rows > tp->land_rows) {
+    st = pai_b200_sync(tp->ctx);
+    if (st) return st;
+    lands_release(tp);
+    st = ipc_exchange(tp, b200_land_bytes(tp->size, rows), tp->land);
+    if (st) {
+      lands_release(tp);
+      return st;
+    }
+    tp->land_rows = rows;
+  }
+  for (uint32_t r = 0; r < tp->size; r++) out[r] = tp->land[r];
+  return PAI_OK;
+}
 
 static void xbufs_release(pai_b200_tp_t *tp) {
   for (uint32_t r = 0; r < tp->size; r++) {
@@ -197,6 +259,7 @@ pai_status_t pai_b200_tp_destroy(pai_b200_tp_t *tp) {
   if (!tp) return PAI_OK;
   pai_b200_sync(tp->ctx);
   xbufs_release(tp);
+  lands_release(tp);
   pai_b200_free(tp->ctx, tp->pairs);
   if (tp->comm) st = nccl_check(g_nccl.comm_destroy(tp->comm), "ncclCommDestroy");
   free(tp);

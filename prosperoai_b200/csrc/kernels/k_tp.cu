@@ -153,10 +153,14 @@ __global__ void __launch_bounds__(256) k_tp_allreduce_add(TpArgs a) {
 
 extern "C" pai_status_t b200_tp_xbuf_alloc(pai_b200_ctx_t *ctx, uint64_t cap, void **buf,
                                            uint8_t handle[B200_TP_HANDLE_BYTES]) {
+  return b200_ipc_alloc(ctx, kHeader + 2 * (size_t)cap * sizeof(float), buf, handle);
+}
+
+extern "C" pai_status_t b200_ipc_alloc(pai_b200_ctx_t *ctx, uint64_t bytes, void **buf,
+                                       uint8_t handle[B200_TP_HANDLE_BYTES]) {
   pai_status_t st = b200_ctx_use_device(ctx);
   if (st) return st;
   void *p = nullptr;
-  const size_t bytes = kHeader + 2 * (size_t)cap * sizeof(float);
   st = b200_cuda(cudaMalloc(&p, bytes), "exchange buffer alloc");
   if (st) return st;
   st = b200_cuda(cudaMemset(p, 0, bytes), "exchange buffer clear");
