@@ -224,8 +224,8 @@ pai_status_t b200_launch_argmax_ranks(pai_b200_ctx_t *ctx, uint32_t rows, uint32
  * CTA waits (bounded) for all ranks' pairs, merges them in rank order,
  * writes tok_out and the next step's tok_in and advances *pos. */
 pai_status_t b200_launch_argmax_peer(pai_b200_ctx_t *ctx, uint64_t rows, uint64_t n, uint32_t v0,
-                                     const float *logits, void *const *land, uint32_t rank, uint32_t nranks,
-                                     int32_t *tok_out, int32_t *tok_in, int32_t *pos);
+                                     const float *logits, void *const *land, uint64_t land_rows, uint32_t rank,
+                                     uint32_t nranks, int32_t *tok_out, int32_t *tok_in, int32_t *pos);
 
 /* Tensor-parallel exchange over NVLink peer memory (kernels/k_tp.cu). */
 #define B200_TP_MAX_RANKS 8

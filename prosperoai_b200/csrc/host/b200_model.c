@@ -403,6 +403,7 @@ struct pai_b200_session {
   void *graph;
   uint32_t graph_kernels;
   b200_decode_plan_t *plan; /* persistent decode kernel of the layers (NULL: one launch per op) */
+  void *land[B200_TP_MAX_RANKS]; /* tensor parallelism: every rank's landing buffer (persistent path) */
   int failed;               /* a bounded device wait ran out: the session refuses further work */
   pai_b200_tp_t *tp; /* tensor-parallel communicator, NULL on one GPU */
   /* prefill scratch (allocated by the first prefill): rows of hidden state,
@@ -417,6 +418,7 @@ struct pai_b200_session {
 
 /* Tensor-parallel hooks (csrc/host/b200_tp.c). */
 void b200_tp_mark_failed(pai_b200_tp_t *tp);
+pai_status_t b200_tp_land(pai_b200_tp_t *tp, uint64_t rows, void **out);
 int b200_tp_failed(const pai_b200_tp_t *tp);
 pai_status_t b200_tp_reserve(pai_b200_tp_t *tp, uint64_t cap);
 float *b200_tp_slot(pai_b200_tp_t *tp, uint32_t slot);
@@ -440,11 +442,14 @@ static pai_status_t norm_gemv(pai_b200_session_t *s, uint32_t type, uint64_t n, 
 
 /* The phase list of the persistent decode kernel: the embedding row, the
  * five phases of every layer in the op order of llama.c:669-797, and the
- * final RMSNorm into the lm head's operand. */
+ * final RMSNorm into the lm head's operand. Under tensor parallelism the
+ * o and down GEMVs push their partial rows to every rank and a row
+ * exchange adds them to the hidden state (seven phases per layer). */
 static pai_status_t make_plan(pai_b200_session_t *s) {
   pai_b200_model_t *m = s->m;
   const pai_b200_model_cfg_t *c = &m->cfg;
-  const uint32_t E = c->n_embd, nph = 2 + 5 * c->n_layer;
+  const int tp = m->tp > 1;
+  const uint32_t E = c->n_embd, nph = 2 + (tp ? 7 : 5) * c->n_layer;
   b200_phase_t *ph = (b200_phase_t *)calloc(nph, sizeof(*ph));
   b200_decode_args_t a;
   uint32_t i = 0;
@@ -452,7 +457,8 @@ static pai_status_t make_plan(pai_b200_session_t *s) {
   if (!ph) return b200_fail(PAI_ERR_NOMEM, "session_create: host allocation");
   ph[i++].kind = B200_PH_EMBED;
   for (uint32_t l = 0; l < c->n_layer; l++) {
-    b200_phase_t *q = &ph[i++], *at = &ph[i++], *o = &ph[i++], *gu = &ph[i++], *dn = &ph[i++];
+    b200_phase_t *q = &ph[i++], *at = &ph[i++], *o = &ph[i++], *xo = tp ? &ph[i++] : NULL, *gu = &ph[i++];
+    b200_phase_t *dn = &ph[i++], *xd = tp ? &ph[i++] : NULL;
     q->kind = B200_PH_GEMV, q->type = c->wtype, q->epi = B200_EPI_STORE, q->xsrc = B200_X_NORM;
     q->w = m->wqkv[l], q->n = m->n_qkv, q->k = E, q->xf = s->x, q->gamma = m->attn_norm[l], q->y = s->qkv;
     at->kind = B200_PH_ATTN, at->layer = l;
@@ -463,6 +469,12 @@ static pai_status_t make_plan(pai_b200_session_t *s) {
     gu->y = s->h, gu->xo = s->xq_h;
     dn->kind = B200_PH_GEMV, dn->type = c->wtype, dn->epi = B200_EPI_RESIDUAL, dn->xsrc = B200_X_XQ;
     dn->w = m->wdown[l], dn->n = E, dn->k = m->ffl, dn->xq = s->xq_h, dn->res = s->x, dn->y = s->x;
+    if (tp) {
+      /* row-parallel o/down: partial rows pushed to every rank, then added */
+      o->epi = dn->epi = B200_EPI_PUSH, o->res = dn->res = NULL, o->y = dn->y = s->x;
+      o->xi = xo->xi = 2 * l, dn->xi = xd->xi = 2 * l + 1;
+      xo->kind = xd->kind = B200_PH_XCHG, xo->n = xd->n = E, xo->y = xd->y = s->x;
+    }
   }
   ph[i].kind = B200_PH_NORM, ph[i].xf = s->x, ph[i].gamma = m->output_norm, ph[i].k = E, ph[i].xo = s->xq_e;
   i++;
@@ -474,7 +486,11 @@ static pai_status_t make_plan(pai_b200_session_t *s) {
   a.cap = s->max_ctx, a.seq_stride = s->seq_stride, a.layer_stride = s->layer_stride;
   a.kc = s->kc, a.vc = s->vc, a.cos_t = s->cos_t, a.sin_t = s->sin_t;
   a.qkv = s->qkv, a.att = s->att, a.xq_att = s->xq_o;
-  st = b200_decode_plan_create(m->ctx, c->wtype, &a, ph, i, &s->plan);
+  a.rank = m->rank, a.nranks = m->tp;
+  st = PAI_OK;
+  if (tp) st = b200_tp_land(s->tp, (uint64_t)s->batch * E, s->land); /* collective */
+  for (uint32_t r = 0; tp && r < m->tp; r++) a.land[r] = s->land[r];
+  if (!st) st = b200_decode_plan_create(m->ctx, c->wtype, &a, ph, i, &s->plan);
   free(ph);
   return st;
 }
@@ -487,12 +503,19 @@ static pai_status_t enqueue_step(pai_b200_session_t *s) {
   pai_status_t st;
   if (s->plan) {
     /* the layers in one persistent launch, then the lm head, the greedy
-     * pick and the token feedback as separate launches */
+     * pick and the token feedback as separate launches; under tensor
+     * parallelism the pick merges the ranks' pairs over peer memory and
+     * feeds the token back itself (no collective library call) */
     st = b200_decode_launch(ctx, s->plan);
     b200_ctx_set_pdl(ctx, 1);
     if (!st) st = b200_launch_gemv(ctx, c->etype, B, m->vl, E, m->output, &s->xq_e, NULL, s->logits, B200_EPI_STORE, NULL);
-    if (!st) st = b200_launch_argmax(ctx, B, m->vl, s->logits, s->tok_out);
-    if (!st) st = b200_launch_step_tail(ctx, B, s->tok_out, s->tok_in, s->dpos);
+    if (m->tp == 1) {
+      if (!st) st = b200_launch_argmax(ctx, B, m->vl, s->logits, s->tok_out);
+      if (!st) st = b200_launch_step_tail(ctx, B, s->tok_out, s->tok_in, s->dpos);
+    } else if (!st) {
+      st = b200_launch_argmax_peer(ctx, B, m->vl, m->v0, s->logits, s->land, (uint64_t)B * E, m->rank, m->tp,
+                                   s->tok_out, s->tok_in, s->dpos);
+    }
     b200_ctx_set_pdl(ctx, 0);
     return st;
   }
@@ -620,9 +643,10 @@ pai_status_t pai_b200_session_create(pai_b200_model_t *m, uint32_t batch, uint32
   if (!st) st = pai_b200_sync(ctx);
   free(tab_c);
   free(tab_s);
-  /* Single GPU: the layers of a step run as one persistent kernel unless
-   * PAI_B200_PERSISTENT=0; shapes it does not take keep one launch per op. */
-  if (!st && m->tp == 1) {
+  /* The layers of a step run as one persistent kernel unless
+   * PAI_B200_PERSISTENT=0 (every rank of a tensor-parallel group must make
+   * the same choice); shapes it does not take keep one launch per op. */
+  if (!st) {
     const char *e = getenv("PAI_B200_PERSISTENT");
     if (!(e && e[0] == '0')) {
       st = make_plan(s);

@@ -85,7 +85,7 @@ struct DPh {
   const float *res;
   float *y;
   b200_xq_t xo;
-  uint32_t layer, pad;
+  uint32_t layer, xi;  // attention: cache layer; EPI_PUSH / XCHG: index of the row exchange in the step
 };
 
 struct KP {
@@ -117,7 +117,22 @@ struct KP {
   uint32_t *bar;       // [0] barrier arrivals, [1] exits, [2] abort
   uint32_t *err;       // the context's host-mapped error word
   uint64_t wait_ns;
+  // tensor parallelism: every rank's landing buffer as mapped here
+  uint8_t *land[B200_TP_MAX_RANKS];
+  uint32_t rank, nranks;
+  uint32_t xrows;  // floats per landing slot (batch x n_embd)
+  uint32_t nx;     // row exchanges per step
 };
+
+__device__ __forceinline__ uint64_t *land_words(uint8_t *b) { return reinterpret_cast<uint64_t *>(b); }
+__device__ __forceinline__ float *land_rows(const KP &p, uint32_t r, uint32_t parity, uint32_t src) {
+  return reinterpret_cast<float *>(p.land[r] + B200_LAND_HDR) + ((size_t)parity * p.nranks + src) * p.xrows;
+}
+__device__ __forceinline__ uint64_t ld_acquire_sys64(const uint64_t *q) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(q) : "memory");
+  return v;
+}
 
 __device__ __forceinline__ void cbar(int nthr) { asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory"); }
 
@@ -405,9 +420,26 @@ struct Requant {
 // 2nt + vsel) through the phase's epilogue.
 template <int NT>
 __device__ void finish_tile(const DPh &ph, const KP &p, uint32_t tile, int lane, const float (&ya)[NT],
-                            const float (&yb)[NT], Requant &pend) {
+                            const float (&yb)[NT], Requant &pend, uint32_t parity) {
   const uint32_t r = lane >> 2, vsel = (lane & 3) >> 1;
   const bool holder = (lane & 1) == 0;
+  if (ph.epi == B200_EPI_PUSH) {
+    // row-parallel partial sums of this rank into slot [parity][rank] of
+    // every rank's landing buffer (plain peer stores over NVLink)
+    if (!holder) return;
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++) {
+      const uint32_t vec = 2 * nt + vsel;
+      if (vec >= p.batch) continue;
+      const uint32_t row = tile * 16 + r;
+      for (uint32_t q = 0; q < p.nranks; q++) {
+        float *dst = land_rows(p, q, parity, p.rank) + (size_t)vec * ph.n;
+        if (row < ph.n) dst[row] = ya[nt];
+        if (row + 8 < ph.n) dst[row + 8] = yb[nt];
+      }
+    }
+    return;
+  }
   if (ph.epi == B200_EPI_SILU_GLU) {
     const uint32_t o = tile * 8 + r;  // rows r (gate) and r+8 (up) of the tile are in the same lane
     if (holder) {
@@ -443,7 +475,7 @@ __device__ void finish_tile(const DPh &ph, const KP &p, uint32_t tile, int lane,
 // tile to arrive adds all parts in CTA order and finishes the tile.
 template <int NT>
 __device__ void settle_splits(const DPh &ph, const KP &p, uint32_t (&tiles)[2], uint32_t (&nsegs)[2], int &n,
-                              int lane, Requant &pend) {
+                              int lane, Requant &pend, uint32_t parity) {
   if (n == 0) return;
   const uint32_t r = lane >> 2, vsel = (lane & 3) >> 1;
   const bool holder = (lane & 1) == 0;
@@ -486,7 +518,7 @@ __device__ void settle_splits(const DPh &ph, const KP &p, uint32_t (&tiles)[2], 
       yb[nt] = b;
     }
     if (lane == 0) p.tile_cnt[tile] = 0;
-    finish_tile<NT>(ph, p, tile, lane, ya, yb, pend);
+    finish_tile<NT>(ph, p, tile, lane, ya, yb, pend, parity);
   }
   n = 0;
 }
@@ -496,7 +528,9 @@ __device__ void settle_splits(const DPh &ph, const KP &p, uint32_t (&tiles)[2], 
 // reaches the same barriers.
 template <uint32_t T, int NT, int CONS>
 __device__ void consume(const KP &p, const DPh &ph, uint8_t *ring, uint64_t *full, uint64_t *empty, uint32_t &seq,
-                        uint8_t *area, double (*red)[8], int c, int lane, int ctid, int nthr, volatile int *failed) {
+                        uint8_t *area, double (*red)[8], int c, int lane, int ctid, int nthr, volatile int *failed,
+                        uint64_t xbase) {
+  const uint32_t parity = (uint32_t)((xbase + ph.xi) & 1u);
   using Un = Unit<T>;
   constexpr int U = Un::U, XPU = Un::XPU;
   constexpr uint32_t GQ = CONS * Un::QB, GS = CONS * Un::SB;
@@ -563,7 +597,7 @@ __device__ void consume(const KP &p, const DPh &ph, uint8_t *ring, uint64_t *ful
       yb[nt] = yr8[nt] + __shfl_xor_sync(0xffffffffu, yr8[nt], 1);
     }
     if (nseg == 1) {
-      finish_tile<NT>(ph, p, tile, lane, ya, yb, pend);
+      finish_tile<NT>(ph, p, tile, lane, ya, yb, pend, parity);
       continue;
     }
     const uint32_t split = blockIdx.x - cta_lo;
@@ -578,12 +612,12 @@ __device__ void consume(const KP &p, const DPh &ph, uint8_t *ring, uint64_t *ful
         }
       }
     }
-    if (nsplit == 2) settle_splits<NT>(ph, p, split_tile, split_n, nsplit, lane, pend);
+    if (nsplit == 2) settle_splits<NT>(ph, p, split_tile, split_n, nsplit, lane, pend, parity);
     split_tile[nsplit] = tile;
     split_n[nsplit++] = nseg;
   }
   if (!bad) {
-    settle_splits<NT>(ph, p, split_tile, split_n, nsplit, lane, pend);
+    settle_splits<NT>(ph, p, split_tile, split_n, nsplit, lane, pend, parity);
     pend.flush(ph, p.batch, p.grp_cnt, lane);
   }
 }
@@ -852,6 +886,69 @@ __device__ void norm_out(const KP &p, const DPh &ph, int c, int lane, int nthr, 
   }
 }
 
+// ---- tensor-parallel row exchange ----------------------------------------------------
+
+// After a row-parallel GEMV phase (B200_EPI_PUSH): every CTA of every rank
+// adds one arrival to every rank's counter once its pushes are out, waits
+// (bounded) until all ranks' CTAs arrived at this exchange, then adds the
+// ranks' partial rows of its slice, in rank order, to x (the residual add of
+// llama.c:747-749, 793-795). Every rank computes the same bits. The arrival
+// takes the place of a grid barrier: it also proves this rank's CTAs are done.
+__device__ inline bool exchange(const KP &p, const DPh &ph, uint64_t xbase, int ctid, int nthr, volatile int *sflag) {
+  cbar(nthr);  // this CTA's pushes are issued
+  const uint64_t e = xbase + ph.xi;
+  if (ctid == 0) {
+    bool ok = true;
+    __threadfence_system();
+    for (uint32_t q = 0; q < p.nranks; q++)
+      atomicAdd_system(reinterpret_cast<unsigned long long *>(land_words(p.land[q])), 1ull);
+    const uint64_t target = (e + 1) * (uint64_t)gridDim.x * p.nranks;
+    const uint64_t *cnt = land_words(p.land[p.rank]);
+    uint64_t t0 = 0;
+    for (uint32_t it = 0;; it++) {
+      if (ld_acquire_sys64(cnt) >= target) break;
+      if ((it & 63u) == 0) {
+        if (*(volatile uint32_t *)(p.bar + 2)) {
+          ok = false;
+          break;
+        }
+        const uint64_t now = globaltimer_ns();
+        if (it == 0) {
+          t0 = now;
+        } else if (now - t0 > p.wait_ns) {
+          raise_abort(p);
+          ok = false;
+          break;
+        }
+      }
+    }
+    *sflag = ok ? 1 : 0;
+  }
+  cbar(nthr);
+  if (!*sflag) return false;
+  const uint32_t parity = (uint32_t)(e & 1u);
+  const uint32_t n4 = p.xrows / 4, per = (n4 + gridDim.x - 1) / gridDim.x;
+  const uint32_t g0 = min(n4, blockIdx.x * per), g1 = min(n4, g0 + per);
+  for (uint32_t g = g0 + ctid; g < g1; g += nthr) {
+    float4 sum = __ldcg(reinterpret_cast<const float4 *>(land_rows(p, p.rank, parity, 0)) + g);
+    for (uint32_t q = 1; q < p.nranks; q++) {  // rank order: the same sum on every rank
+      const float4 v = __ldcg(reinterpret_cast<const float4 *>(land_rows(p, p.rank, parity, q)) + g);
+      sum.x += v.x;
+      sum.y += v.y;
+      sum.z += v.z;
+      sum.w += v.w;
+    }
+    float4 *xp = reinterpret_cast<float4 *>(ph.y) + g;
+    float4 xv = __ldcg(xp);
+    xv.x += sum.x;
+    xv.y += sum.y;
+    xv.z += sum.z;
+    xv.w += sum.w;
+    *xp = xv;
+  }
+  return true;
+}
+
 // ---- the kernel ---------------------------------------------------------------------
 
 template <uint32_t T, int NT, int CONS>
@@ -896,9 +993,16 @@ __global__ void __launch_bounds__((CONS + 1) * 32, 1) k_decode(const __grid_cons
   // ---- consumers ----
   const int c = warp - 1, ctid = threadIdx.x - 32, nthr = CONS * 32;
   uint32_t seq = 0, epoch = 0;
+  // row exchanges this rank completed in earlier steps (written by the
+  // previous launch's last CTA)
+  const uint64_t xbase = p.nranks > 1 ? *(volatile uint64_t *)(land_words(p.land[p.rank]) + 1) : 0;
   bool ok = true;
   for (uint32_t i = 0; i < p.nph && ok; i++) {
     const DPh &ph = p.ph[i];
+    if (ph.kind == B200_PH_XCHG) {  // its arrival counter also serves as the barrier
+      ok = exchange(p, ph, xbase, ctid, nthr, &sflag);
+      continue;
+    }
     if (i > 0 && !grid_sync(p, epoch, ctid, nthr, &sflag)) {
       ok = false;
       break;
@@ -906,7 +1010,7 @@ __global__ void __launch_bounds__((CONS + 1) * 32, 1) k_decode(const __grid_cons
     switch (ph.kind) {
       case B200_PH_EMBED: embed(p, ctid, nthr); break;
       case B200_PH_GEMV:
-        consume<T, NT, CONS>(p, ph, ring, full, empty, seq, area, red, c, lane, ctid, nthr, &sfailed);
+        consume<T, NT, CONS>(p, ph, ring, full, empty, seq, area, red, c, lane, ctid, nthr, &sfailed, xbase);
         cbar(nthr);
         if (sfailed) {
           if (ctid == 0) raise_abort(p);
@@ -933,6 +1037,7 @@ __global__ void __launch_bounds__((CONS + 1) * 32, 1) k_decode(const __grid_cons
     if (out == gridDim.x - 1 && !*(volatile uint32_t *)(p.bar + 2)) {
       p.bar[0] = 0;
       p.bar[1] = 0;
+      if (p.nranks > 1) land_words(p.land[p.rank])[1] = xbase + p.nx;  // read by the next launch
     }
   }
 }

@@ -43,6 +43,11 @@ extern "C" pai_status_t b200_decode_plan_create(pai_b200_ctx_t *ctx, uint32_t ty
     return b200_fail(PAI_ERR_UNSUPPORTED, "decode_plan: %u heads per kv head", G);
   if (!b200_type_ok(a->etype) || a->n_embd == 0 || a->n_embd % b200_blk_elems(a->etype))
     return b200_fail(PAI_ERR_UNSUPPORTED, "decode_plan: embedding shape");
+  if (a->nranks == 0 || a->nranks > B200_TP_MAX_RANKS || a->rank >= a->nranks)
+    return b200_fail(PAI_ERR_INVALID_ARG, "decode_plan: rank %u of %u", a->rank, a->nranks);
+  for (uint32_t r = 0; a->nranks > 1 && r < a->nranks; r++)
+    if (!a->land[r] || ((uintptr_t)a->land[r] & 255))
+      return b200_fail(PAI_ERR_INVALID_ARG, "decode_plan: landing buffer of rank %u", r);
   pai_status_t st = b200_ctx_use_device(ctx);
   if (st) return st;
   b200_decode_plan *plan = new (std::nothrow) b200_decode_plan();
@@ -62,6 +67,7 @@ extern "C" pai_status_t b200_decode_plan_create(pai_b200_ctx_t *ctx, uint32_t ty
     return b200_fail(PAI_ERR_NOMEM, "decode_plan: host allocation");
   }
   uint64_t partial_floats = 0, tiles = 0, groups4 = 0;
+  uint32_t nx = 0;
   size_t area = 0;
   for (uint32_t i = 0; i < nphases && !st; i++) {
     const b200_phase_t &s = phases[i];
@@ -71,6 +77,7 @@ extern "C" pai_status_t b200_decode_plan_create(pai_b200_ctx_t *ctx, uint32_t ty
     d.epi = s.epi;
     d.xsrc = s.xsrc;
     d.layer = s.layer;
+    d.xi = s.xi;
     d.xf = s.xf;
     d.gamma = s.gamma;
     d.xo = s.xo;
@@ -84,6 +91,17 @@ extern "C" pai_status_t b200_decode_plan_create(pai_b200_ctx_t *ctx, uint32_t ty
       continue;
     }
     if (s.kind == B200_PH_EMBED || s.kind == B200_PH_ATTN) continue;
+    if (s.kind == B200_PH_XCHG) {
+      // the exchange adds every rank's rows [batch][n_embd] to y (= the hidden state)
+      if (a->nranks < 2 || !s.y || s.n != a->n_embd || ((uintptr_t)s.y & 15) || s.xi != nx) {
+        st = b200_fail(PAI_ERR_INVALID_ARG, "decode_plan: phase %u (row exchange)", i);
+        break;
+      }
+      d.n = (uint32_t)s.n;
+      d.y = s.y;
+      nx++;
+      continue;
+    }
     if (s.kind != B200_PH_GEMV) {
       st = b200_fail(PAI_ERR_INVALID_ARG, "decode_plan: phase %u kind %u", i, s.kind);
       break;
@@ -96,6 +114,7 @@ extern "C" pai_status_t b200_decode_plan_create(pai_b200_ctx_t *ctx, uint32_t ty
     if ((s.xsrc == B200_X_NORM && (!s.xf || !s.gamma || s.k % 32)) ||
         (s.xsrc == B200_X_XQ && (!s.xq.limbs || s.xq.batch < B || s.xq.k < s.k)) ||
         (s.epi == B200_EPI_RESIDUAL && !s.res) ||
+        (s.epi == B200_EPI_PUSH && (a->nranks < 2 || s.n != a->n_embd || s.xi != nx)) ||
         (s.epi == B200_EPI_SILU_GLU && (s.n % 64 || (s.xo.limbs && (s.xo.batch < B || s.xo.k < s.n / 2))))) {
       st = b200_fail(PAI_ERR_INVALID_ARG, "decode_plan: phase %u operands", i);
       break;
@@ -189,6 +208,11 @@ extern "C" pai_status_t b200_decode_plan_create(pai_b200_ctx_t *ctx, uint32_t ty
   k.bar = (uint32_t *)(((uintptr_t)sp + 255) & ~(uintptr_t)255);
   k.err = b200_ctx_errflag(ctx);
   k.wait_ns = b200_ctx_wait_ns(ctx);
+  k.rank = a->rank;
+  k.nranks = a->nranks;
+  for (uint32_t r = 0; r < a->nranks && a->nranks > 1; r++) k.land[r] = (uint8_t *)a->land[r];
+  k.xrows = (uint32_t)(B * a->n_embd);
+  k.nx = nx;
   *out = plan;
   return PAI_OK;
 }

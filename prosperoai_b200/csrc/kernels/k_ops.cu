@@ -208,6 +208,111 @@ __global__ void k_argmax_ranks(uint32_t rows, uint32_t nranks, const float *__re
   out[row] = (int32_t)bidx;
 }
 
+// Tensor-parallel greedy pick over NVLink peer memory, without a
+// collective library call. CTA (slice, row) scans its slice of this rank's
+// vocabulary shard; the last slice of a row merges the row (first index of
+// the maximum) into a staged pair; the last row to finish then stores every
+// row's (maximum, index + v0) into slot [parity][rank] of every rank's
+// landing buffer, adds one arrival to every rank's greedy counter, waits
+// (bounded) until all ranks arrived, merges the ranks' pairs in rank order
+// (shard r holds the indices [r vl, (r + 1) vl), so on equal values the
+// lower rank's index wins: the first index over the whole vocabulary,
+// models/sampler.c:89-99), writes the tokens, feeds them back as the next
+// step's input and advances the position.
+struct PeerPick {
+  uint8_t *land[B200_TP_MAX_RANKS];
+  uint32_t rank, nranks;
+  uint64_t pairs_off;  // byte offset of the pair slots in a landing buffer
+  int32_t *tok_out, *tok_in, *pos;
+  uint32_t *err;
+  uint64_t wait_ns;
+};
+
+__global__ void __launch_bounds__(256) k_argmax_peer(uint64_t n, uint64_t per, const float *__restrict__ logits,
+                                                     float *__restrict__ part, uint32_t *__restrict__ cnt, uint32_t v0,
+                                                     PeerPick a) {
+  pdl_trigger();
+  pdl_wait();
+  const uint32_t row = blockIdx.y, rows = gridDim.y, slice = blockIdx.x, nsl = gridDim.x;
+  const float *lr = logits + (size_t)row * n;
+  const uint64_t lo = (uint64_t)slice * per, hi = min(n, lo + per);
+  float best = -INFINITY;
+  uint32_t bidx = 0xFFFFFFFFu;
+  for (uint64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+    const float v = lr[i];
+    if (bidx == 0xFFFFFFFFu || v > best) {
+      best = v;
+      bidx = (uint32_t)i;
+    }
+  }
+  amax_block(best, bidx);
+  __shared__ uint32_t ticket;
+  float *staged = part + (size_t)rows * nsl * 2;  // [row][2]: each row's merged pair
+  if (threadIdx.x == 0) {
+    part[((size_t)row * nsl + slice) * 2] = best;
+    part[((size_t)row * nsl + slice) * 2 + 1] = __uint_as_float(bidx);
+    __threadfence();
+    ticket = atomicAdd(&cnt[row], 1u);
+  }
+  __syncthreads();
+  if (ticket != nsl - 1) return;
+  __threadfence();
+  best = -INFINITY;
+  bidx = 0xFFFFFFFFu;
+  for (uint32_t s = threadIdx.x; s < nsl; s += blockDim.x)
+    amax_merge(best, bidx, __ldcg(&part[((size_t)row * nsl + s) * 2]),
+               __float_as_uint(__ldcg(&part[((size_t)row * nsl + s) * 2 + 1])));
+  amax_block(best, bidx);
+  if (threadIdx.x != 0) return;
+  staged[row * 2] = best;
+  staged[row * 2 + 1] = __uint_as_float(bidx == 0xFFFFFFFFu ? bidx : bidx + v0);
+  cnt[row] = 0;
+  __threadfence();
+  if (atomicAdd(&cnt[rows], 1u) != rows - 1) return;
+  // the last row: exchange all rows' pairs with the other ranks
+  __threadfence();
+  cnt[rows] = 0;
+  uint64_t *mine = reinterpret_cast<uint64_t *>(a.land[a.rank]);
+  const uint64_t done = *(volatile uint64_t *)(mine + 3), parity = done & 1u;
+  for (uint32_t q = 0; q < a.nranks; q++) {
+    float *dst = reinterpret_cast<float *>(a.land[q] + a.pairs_off) + ((parity * a.nranks + a.rank) * 8) * 2;
+    for (uint32_t r = 0; r < rows; r++) {
+      dst[r * 2] = __ldcg(&staged[r * 2]);
+      dst[r * 2 + 1] = __ldcg(&staged[r * 2 + 1]);
+    }
+  }
+  __threadfence_system();
+  for (uint32_t q = 0; q < a.nranks; q++)
+    atomicAdd_system(reinterpret_cast<unsigned long long *>(a.land[q]) + 2, 1ull);
+  const uint64_t target = (done + 1) * a.nranks;
+  uint64_t t0 = 0;
+  for (uint32_t it = 0;; it++) {
+    uint64_t v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(mine + 2) : "memory");
+    if (v >= target) break;
+    if ((it & 255u) == 0) {
+      const uint64_t now = globaltimer_ns();
+      if (it == 0) {
+        t0 = now;
+      } else if (now - t0 > a.wait_ns) {
+        atomicExch(a.err, 1u);
+        return;  // the position is not advanced: the step did not complete
+      }
+    }
+  }
+  const float *pairs = reinterpret_cast<const float *>(a.land[a.rank] + a.pairs_off) + (parity * a.nranks * 8) * 2;
+  for (uint32_t r = 0; r < rows; r++) {
+    float b = -INFINITY;
+    uint32_t bi = 0xFFFFFFFFu;
+    for (uint32_t q = 0; q < a.nranks; q++)
+      amax_merge(b, bi, __ldcg(&pairs[(q * 8 + r) * 2]), __float_as_uint(__ldcg(&pairs[(q * 8 + r) * 2 + 1])));
+    a.tok_out[r] = (int32_t)bi;
+    a.tok_in[r] = (int32_t)bi;
+  }
+  *a.pos += 1;
+  mine[3] = done + 1;
+}
+
 // End of a device-resident decode step: advance the position and feed
 // the chosen tokens back as the next step's input.
 __global__ void k_step_tail(uint32_t batch, const int32_t *__restrict__ tok_out, int32_t *__restrict__ tok_in,
@@ -319,6 +424,37 @@ extern "C" pai_status_t pai_b200_argmax_f32(pai_b200_ctx_t *ctx, uint64_t rows, 
   if (rows == 0 || n == 0 || n > 0xFFFFFFFEull) return b200_fail(PAI_ERR_INVALID_ARG, "argmax: shape");
   if (rows > 65535) return b200_fail(PAI_ERR_UNSUPPORTED, "argmax: %llu rows (at most 65535)", (unsigned long long)rows);
   return b200_launch_argmax(ctx, rows, n, logits, out);
+}
+
+extern "C" pai_status_t b200_launch_argmax_peer(pai_b200_ctx_t *ctx, uint64_t rows, uint64_t n, uint32_t v0,
+                                                const float *logits, void *const *land, uint64_t land_rows,
+                                                uint32_t rank, uint32_t nranks, int32_t *tok_out, int32_t *tok_in,
+                                                int32_t *pos) {
+  if (rows == 0 || rows > 8 || nranks == 0 || nranks > B200_TP_MAX_RANKS || rank >= nranks || n == 0 ||
+      n > 0xFFFFFFFEull || !land || !logits)
+    return b200_fail(PAI_ERR_INVALID_ARG, "argmax_peer: rows %llu, rank %u of %u", (unsigned long long)rows, rank,
+                     nranks);
+  const uint64_t nsl = std::min<uint64_t>(148, (n + 2047) / 2048), per = (n + nsl - 1) / nsl;
+  float *part = nullptr;
+  uint32_t *cnt = nullptr;
+  pai_status_t st = b200_ctx_scratch(ctx, rows * nsl * 2 + rows * 2, (uint32_t)rows + 1, &part, &cnt);
+  if (st) return st;
+  PeerPick a{};
+  for (uint32_t r = 0; r < nranks; r++) {
+    if (!land[r]) return b200_fail(PAI_ERR_INVALID_ARG, "argmax_peer: landing buffer of rank %u is NULL", r);
+    a.land[r] = static_cast<uint8_t *>(land[r]);
+  }
+  a.rank = rank;
+  a.nranks = nranks;
+  a.tok_out = tok_out;
+  a.tok_in = tok_in;
+  a.pos = pos;
+  a.err = b200_ctx_errflag(ctx);
+  a.wait_ns = b200_ctx_wait_ns(ctx);
+  // the pair slots follow the row slots of the landing buffers
+  a.pairs_off = b200_land_pairs_off(nranks, land_rows);
+  b200_launch(ctx, k_argmax_peer, dim3((unsigned)nsl, (unsigned)rows), dim3(256), 0, n, per, logits, part, cnt, v0, a);
+  return b200_launched(ctx, 1, "k_argmax_peer");
 }
 
 extern "C" pai_status_t b200_launch_step_tail(pai_b200_ctx_t *ctx, uint32_t batch, int32_t *tok_out,

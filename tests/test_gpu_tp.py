@@ -230,3 +230,67 @@ def test_tp_8b_shape_decode_matches_oracle(oracle_8b, world):
     for r in range(world):
         assert "error" not in res[r], res[r]["error"]
         assert res[r]["tokens"] == want, f"rank {r} of {world}"
+
+
+def _skip_worker(rank, world, port, cfg, prompt, steps, max_ctx, q):
+    """Both ranks decode a few steps; then rank 1 skips a step (it leaves
+    between steps, nothing of it in flight) while rank 0 runs one with a
+    200 ms wait limit. The persistent step's exchanges are bounded peer-memory
+    waits, not collective library calls, so rank 0 gets PAI_ERR_TIMEOUT and
+    its session then refuses further steps."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    out = {"rank": rank}
+    try:
+        import torch.distributed as dist
+        from prosperoai_b200 import PaiError, _native
+        from prosperoai_b200.api import Device, Model, Session, TPComm
+        from test_gpu_model import gpu_generate
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=120))
+        dev = Device(rank)
+        comm = TPComm.over_group(dev, rank, world)
+        model = Model(dev, cfg, tp_rank=rank, tp_size=world)
+        model.synthesize(SEED)
+        model.set_tp(comm)
+        sess = Session(model, 1, max_ctx)
+        out["kernels"] = sess.step_kernels
+        out["tokens"] = gpu_generate(sess, prompt, steps)
+        dist.barrier()
+        if rank == 0:
+            _native.check(_native.load().pai_b200_set_wait_limit(dev.ctx, 200_000_000), "set_wait_limit")
+            try:
+                sess.step(np.array([out["tokens"][-1]], np.int32))
+                out["first"] = 0
+            except PaiError as e:
+                out["first"] = e.status
+            try:
+                sess.step(np.array([out["tokens"][-1]], np.int32))
+                out["second"] = 0
+            except PaiError as e:
+                out["second"] = e.status
+        dist.barrier()  # rank 1 stays idle until rank 0 is done
+        sess.close()
+        comm.close()
+        model.close()
+        dev.close()
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:  # reported to the parent, which fails the test
+        out["error"] = repr(e)
+    q.put(out)
+
+
+def test_tp2_rank_that_skips_a_step_times_out_the_other(dev):
+    if _gpu_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    cfg = dict(TP_CFG)
+    prompt = [3, 1, 4]
+    res = _run_ranks(2, cfg, prompt, 6, 64, target=_skip_worker)
+    for r in range(2):
+        assert "error" not in res[r], res[r]["error"]
+        assert res[r]["kernels"] == 3  # layers, lm head shard, greedy pick over peer memory
+    assert res[0]["tokens"] == res[1]["tokens"]
+    assert res[0]["first"] == -5  # PAI_ERR_TIMEOUT
+    assert res[0]["second"] == -8  # PAI_ERR_INIT: the session refuses further steps
