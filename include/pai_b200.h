@@ -92,6 +92,14 @@ enum {
   PAI_KERNEL_B200_GEMM_V0 = 28
 };
 
+/* Quantized weight operand of a descriptor: pai_op_descriptor_t.reserved[0]
+ * holds its format -- a ggml block type below, or one of these -- and
+ * reserved[1] holds 1 + its input index (0: the op has none). */
+#define PAI_B200_WEIGHT_ANY_GGML 0x100u /* any of the ggml block types below            */
+#define PAI_B200_WEIGHT_W8_COLS 0x101u  /* int8 [k][n], f32 scales per (k group, column) */
+#define PAI_B200_WEIGHT_W4_COLS 0x102u  /* nibbles of the same layout                    */
+#define PAI_B200_WEIGHT_V0_BLOB 0x103u  /* a v0 .pai tensor blob (values, flat-group scales) */
+
 /* ggml block types, numbered as adapters/llama/gguf.h:36-51. */
 #define PAI_B200_Q4_0 2u  /* 32 weights: fp16 d, 16 B of nibbles       (18 B) */
 #define PAI_B200_Q8_0 8u  /* 32 weights: fp16 d, 32 int8                (34 B) */

@@ -9,31 +9,38 @@
  */
 #include "../b200_internal.h"
 
-#define B200_DESC(nm, nin, kid)                                                         \
+/* in/out dtype 0 is PAI_DTYPE_F32 (pai/dtype.h:14): the activation operands
+ * and the outputs are f32. The reference's dtype carries only storage, and
+ * quantization is metadata (pai/dtype.h:1-5), so a descriptor names its
+ * quantized weight operand in reserved[]: reserved[0] = block format
+ * (PAI_B200_WEIGHT_*: a ggml type id, or a v0 .pai grouped format),
+ * reserved[1] = 1 + the index of that operand among the inputs (0: none).
+ * ref_fn is NULL: these ops have no CPU path (pai_op_eval_f32 answers
+ * PAI_ERR_UNSUPPORTED for them, op_registry.c:479-480); their CPU twins are
+ * the builtin ops of the same meaning (gemm_f32, rmsnorm_f32, ...). */
+#define B200_DESC(nm, nin, kid, wfmt, warg)                                              \
   {                                                                                      \
     .name = nm, .version = 1, .num_inputs = nin, .num_outputs = 1, .in_dtype = 0,        \
     .out_dtype = 0, .caps = PAI_OP_CAP_CUDA_B200, .ref_fn = 0, .kernel_id = kid,          \
-    .reserved = {0, 0}                                                                   \
+    .reserved = {wfmt, warg}                                                             \
   }
 
-/* in/out dtype 0 is PAI_DTYPE_F32 (pai/dtype.h:14): activations are f32;
- * the quantized weight operand is described by the op name. */
 static const pai_op_descriptor_t s_ops[] = {
-    B200_DESC("gemv_q8_0_f32", 2, PAI_KERNEL_B200_GEMV_Q8_0),     /* W blocks, x     */
-    B200_DESC("gemv_q4_0_f32", 2, PAI_KERNEL_B200_GEMV_Q4_0),
-    B200_DESC("gemv_q4_k_f32", 2, PAI_KERNEL_B200_GEMV_Q4_K),
-    B200_DESC("gemm_q4_0_f32", 2, PAI_KERNEL_B200_GEMM_Q4_0),     /* X, W blocks     */
-    B200_DESC("rmsnorm_gamma_f32_b200", 2, PAI_KERNEL_B200_RMSNORM), /* a, gamma     */
-    B200_DESC("rope_f32_b200", 3, PAI_KERNEL_B200_ROPE),          /* x, cos, sin     */
-    B200_DESC("attention_decode_f16kv", 3, PAI_KERNEL_B200_ATTN_DECODE), /* q, K, V  */
-    B200_DESC("attention_f32_b200", 3, PAI_KERNEL_B200_ATTENTION), /* q, k, v        */
-    B200_DESC("silu_mul_f32", 2, PAI_KERNEL_B200_SILU_MUL),       /* gate, up        */
-    B200_DESC("vecadd_f32_b200", 2, PAI_KERNEL_B200_VECADD),
-    B200_DESC("dequant_block_f32", 1, PAI_KERNEL_B200_DEQUANT),
-    B200_DESC("argmax_f32", 1, PAI_KERNEL_B200_ARGMAX),
-    B200_DESC("gemm_w8_f32_b200", 3, PAI_KERNEL_B200_GEMM_W8),    /* a, w_q, b_scales */
-    B200_DESC("gemm_w4_f32_b200", 3, PAI_KERNEL_B200_GEMM_W4),    /* a, w_q4, b_scales */
-    B200_DESC("gemm_v0_f32", 2, PAI_KERNEL_B200_GEMM_V0),         /* a, .pai blob    */
+    B200_DESC("gemv_q8_0_f32", 2, PAI_KERNEL_B200_GEMV_Q8_0, PAI_B200_Q8_0, 1), /* W blocks, x */
+    B200_DESC("gemv_q4_0_f32", 2, PAI_KERNEL_B200_GEMV_Q4_0, PAI_B200_Q4_0, 1),
+    B200_DESC("gemv_q4_k_f32", 2, PAI_KERNEL_B200_GEMV_Q4_K, PAI_B200_Q4_K, 1),
+    B200_DESC("gemm_q4_0_f32", 2, PAI_KERNEL_B200_GEMM_Q4_0, PAI_B200_Q4_0, 2), /* X, W blocks */
+    B200_DESC("rmsnorm_gamma_f32_b200", 2, PAI_KERNEL_B200_RMSNORM, 0, 0),     /* a, gamma */
+    B200_DESC("rope_f32_b200", 3, PAI_KERNEL_B200_ROPE, 0, 0),                 /* x, cos, sin */
+    B200_DESC("attention_decode_f16kv", 3, PAI_KERNEL_B200_ATTN_DECODE, 0, 0), /* q, K, V (fp16 cache) */
+    B200_DESC("attention_f32_b200", 3, PAI_KERNEL_B200_ATTENTION, 0, 0),       /* q, k, v */
+    B200_DESC("silu_mul_f32", 2, PAI_KERNEL_B200_SILU_MUL, 0, 0),              /* gate, up */
+    B200_DESC("vecadd_f32_b200", 2, PAI_KERNEL_B200_VECADD, 0, 0),
+    B200_DESC("dequant_block_f32", 1, PAI_KERNEL_B200_DEQUANT, PAI_B200_WEIGHT_ANY_GGML, 1),
+    B200_DESC("argmax_f32", 1, PAI_KERNEL_B200_ARGMAX, 0, 0),
+    B200_DESC("gemm_w8_f32_b200", 3, PAI_KERNEL_B200_GEMM_W8, PAI_B200_WEIGHT_W8_COLS, 2), /* a, w_q, scales */
+    B200_DESC("gemm_w4_f32_b200", 3, PAI_KERNEL_B200_GEMM_W4, PAI_B200_WEIGHT_W4_COLS, 2), /* a, w_q4, scales */
+    B200_DESC("gemm_v0_f32", 2, PAI_KERNEL_B200_GEMM_V0, PAI_B200_WEIGHT_V0_BLOB, 2),      /* a, .pai blob */
 };
 
 #define B200_NOPS (sizeof(s_ops) / sizeof(s_ops[0]))

@@ -142,3 +142,49 @@ def test_v0_blob_bytes_match_reference():
             for n in (1, 2, 33, 1000, 4096 * 4096):
                 want = R.pai_quant_weights_bytes(n, C.byref(po.QuantScheme(bits, 1, gs)))
                 assert L.pai_b200_v0_blob_bytes(bits, gs, n) == want, (bits, gs, n)
+
+
+@pytest.mark.skipif(po.ref() is None, reason="reference build (oracle/_ref) not present")
+def test_ops_register_into_the_reference_registry():
+    """The reference's own registry code (runtime/op_registry.c, compiled in
+    oracle/_ref): pai_op_registry_builtin, then pai_b200_register_ops on the
+    same registry; the reference's lookups then find this backend's ops by
+    name and by kernel id, the builtins are untouched, the capability gate
+    pai_op_supports sees PAI_OP_CAP_CUDA_B200, and the reference's eager
+    CPU path refuses them (no CPU fallback: ref_fn is NULL)."""
+    from prosperoai_b200._native import OpDescriptor, OpRegistry
+    L = _native.load()
+    R = po.ref()
+    DP = C.POINTER(OpDescriptor)
+    R.pai_op_registry_builtin.restype = C.c_int32
+    R.pai_op_registry_lookup.restype = DP
+    R.pai_op_registry_lookup.argtypes = [C.c_void_p, C.c_char_p]
+    R.pai_op_registry_lookup_kernel.restype = DP
+    R.pai_op_registry_lookup_kernel.argtypes = [C.c_void_p, C.c_int32]
+    R.pai_op_supports.restype = C.c_uint32
+    R.pai_op_supports.argtypes = [DP, C.c_uint32]
+    R.pai_op_eval_f32.restype = C.c_int32
+    R.pai_op_eval_f32.argtypes = [C.c_void_p, C.c_char_p, C.c_void_p, C.c_uint32, C.c_void_p,
+                                  C.c_uint32, C.c_void_p, C.c_uint32]
+    reg = OpRegistry()
+    assert R.pai_op_registry_builtin(C.byref(reg)) == 0
+    builtin = reg.count
+    matmul = R.pai_op_registry_lookup(C.byref(reg), b"matmul_f32")
+    assert L.pai_b200_register_ops(C.byref(reg)) == 0
+    assert reg.count == builtin + L.pai_b200_op_count()
+    cuda_b200 = 1 << 3
+    for name, kid, wfmt, warg in ((b"gemv_q4_0_f32", 15, 2, 1), (b"gemv_q8_0_f32", 14, 8, 1),
+                                  (b"gemv_q4_k_f32", 16, 12, 1), (b"gemm_q4_0_f32", 17, 2, 2),
+                                  (b"attention_decode_f16kv", 20, 0, 0)):
+        d = R.pai_op_registry_lookup(C.byref(reg), name)
+        assert d, name
+        assert d.contents.name == name and d.contents.kernel_id == kid
+        assert tuple(d.contents.reserved) == (wfmt, warg)  # the quantized weight operand
+        assert R.pai_op_supports(d, cuda_b200) == 1 and R.pai_op_supports(d, 1) == 0
+        k = R.pai_op_registry_lookup_kernel(C.byref(reg), kid)
+        assert C.addressof(k.contents) == C.addressof(d.contents)
+        # the reference's eager path: a vocabulary-only entry for it
+        assert R.pai_op_eval_f32(C.byref(reg), name, None, d.contents.num_inputs, None,
+                                 d.contents.num_outputs, None, 0) == -3  # PAI_ERR_UNSUPPORTED
+    after = R.pai_op_registry_lookup(C.byref(reg), b"matmul_f32")
+    assert (not matmul and not after) or C.addressof(after.contents) == C.addressof(matmul.contents)
