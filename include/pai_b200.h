@@ -435,6 +435,54 @@ pai_status_t pai_b200_gguf_inspect(const char *path, pai_b200_gguf_info_t *info)
 pai_status_t pai_b200_model_load_gguf(pai_b200_ctx_t *ctx, const char *path, uint32_t tp_rank,
                                       uint32_t tp_size, pai_b200_model_t **out,
                                       pai_b200_gguf_info_t *info);
+/* ---- .pai containers holding ggml blocks ---------------------------------------------
+ * The reference's .pai container (pai/pai.h:1-20) keeps u32 section offsets
+ * and sizes (a 4 GiB file limit) and its IR quantization descriptor
+ * (ir/ir.h:95-103) has no ggml block kind, so its LLaMA import dequantises
+ * every weight to f32 (llama.c:408-457). Version 2 of the container, read
+ * and written here, keeps the magic ("PAIC"), the header and the META
+ * payload of version 1 and changes three things:
+ *   - section table entries are 24 bytes: u32 type, u32 flags, u64 offset,
+ *     u64 size (no 4 GiB limit);
+ *   - a MANIFEST entry appends the tensor's pai_ir_quant_t (8 bytes) to the
+ *     version-1 entry; ggml-blocked tensors use block structure
+ *     PAI_IR_QUANT_BLOCK_GGML with dtype U8 (bytes of blocks, stored as
+ *     in GGUF, [out][in]);
+ *   - an HPARAMS section (type PAI_B200_PAI_SEC_HPARAMS) holds the LLaMA
+ *     configuration: u32 n_layer, n_embd, n_head, n_head_kv, head_dim, n_ff,
+ *     vocab, f32 eps, f32 rope_theta, u32 wtype, u32 etype, u32 n_rot,
+ *     u32 tied_output (52 bytes).
+ * The header CRC-32 (IEEE) covers the header's first 12 bytes, the section
+ * table and every payload except WEIGHTS (weights carry no checksum, as in
+ * GGUF). A version-1 reader rejects version 2 (pai_pai_open checks the
+ * version), so the two never mix. */
+#ifndef PAI_IR_H
+typedef struct pai_ir_quant { /* ir/ir.h:95-103 */
+  uint8_t present, bit_width, scale_repr, zero_point_repr, is_signed, block_structure;
+  uint16_t group_size;
+} pai_ir_quant_t;
+#endif
+/* Block structure after PAI_IR_QUANT_BLOCK_GROUP (ir/ir.h:88-93): ggml
+ * blocks; group_size = weights per block, bit_width = code bits, scale_repr
+ * = F16. Q4_0: 4 bits, 32, signed (codes - 8); Q8_0: 8 bits, 32, signed;
+ * Q4_K: 4 bits, 256, unsigned (with per-sub-block mins). */
+#define PAI_IR_QUANT_BLOCK_GGML 3u
+#define PAI_B200_PAI_VERSION 2u
+#define PAI_B200_PAI_SEC_HPARAMS 0x100u
+pai_status_t pai_b200_ir_quant_ggml(uint32_t ggml_type, pai_ir_quant_t *out);
+/* The ggml type a descriptor names; PAI_ERR_UNSUPPORTED for any other. */
+pai_status_t pai_b200_ir_quant_ggml_type(const pai_ir_quant_t *q, uint32_t *ggml_type);
+/* Convert a LLaMA-family GGUF file into a version-2 .pai container, blocks
+ * copied as stored (no dequantisation, no size limit). */
+pai_status_t pai_b200_pai_from_gguf(const char *gguf_path, const char *pai_path);
+/* Parse and validate a version-2 .pai container without a GPU; info as for
+ * pai_b200_gguf_inspect (version = 2). Status codes as the GGUF reader's. */
+pai_status_t pai_b200_pai_inspect(const char *path, pai_b200_gguf_info_t *info);
+/* Create the model and load its blocks from a version-2 .pai file, as
+ * stored (the file is mapped, not read). */
+pai_status_t pai_b200_model_load_pai(pai_b200_ctx_t *ctx, const char *path, uint32_t tp_rank,
+                                     uint32_t tp_size, pai_b200_model_t **out,
+                                     pai_b200_gguf_info_t *info);
 /* Load one whole (unsharded) tensor from host memory: ggml blocks
  * [out][in] for matrices, fp32 for norms. The model keeps its shard. */
 pai_status_t pai_b200_model_set_tensor(pai_b200_model_t *m, uint32_t kind,

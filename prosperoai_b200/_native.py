@@ -135,6 +135,11 @@ SIGNATURES = {
     "pai_b200_model_destroy": (I32, [P]),
     "pai_b200_gguf_inspect": (I32, [C.c_char_p, C.POINTER(GgufInfo)]),
     "pai_b200_model_load_gguf": (I32, [P, C.c_char_p, U32, U32, PP, C.POINTER(GgufInfo)]),
+    "pai_b200_pai_from_gguf": (I32, [C.c_char_p, C.c_char_p]),
+    "pai_b200_pai_inspect": (I32, [C.c_char_p, C.POINTER(GgufInfo)]),
+    "pai_b200_model_load_pai": (I32, [P, C.c_char_p, U32, U32, PP, C.POINTER(GgufInfo)]),
+    "pai_b200_ir_quant_ggml": (I32, [U32, C.c_void_p]),
+    "pai_b200_ir_quant_ggml_type": (I32, [C.c_void_p, C.POINTER(C.c_uint32)]),
     "pai_b200_model_set_tensor": (I32, [P, U32, U32, P]),
     "pai_b200_model_synthesize": (I32, [P, U64]),
     "pai_b200_tensor_seed": (U64, [U64, U32, U32]),

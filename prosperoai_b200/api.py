@@ -14,7 +14,8 @@ import numpy as np
 from ._native import (Q4_0, Q4_K, Q8_0, GgufInfo, ModelCfg, OpRegistry, PaiError, check, load)
 
 __all__ = ["Device", "Buffer", "PackedMatrix", "Model", "Session", "PaiError",
-           "Q4_0", "Q8_0", "Q4_K", "block_bytes", "quantize", "rope_tables", "gguf_inspect"]
+           "Q4_0", "Q8_0", "Q4_K", "block_bytes", "quantize", "rope_tables", "gguf_inspect",
+           "pai_from_gguf", "pai_inspect"]
 
 BLOCK_ELEMS = {Q4_0: 32, Q8_0: 32, Q4_K: 256}
 
@@ -256,6 +257,19 @@ def gguf_inspect(path: str) -> dict:
     return _info_dict(info)
 
 
+def pai_from_gguf(gguf_path: str, pai_path: str) -> None:
+    """Convert a LLaMA-family GGUF file into a version-2 .pai container that
+    keeps the ggml blocks as stored (pai_b200_pai_from_gguf; no GPU needed)."""
+    check(load().pai_b200_pai_from_gguf(os.fsencode(gguf_path), os.fsencode(pai_path)), "pai_from_gguf")
+
+
+def pai_inspect(path: str) -> dict:
+    """Parse and validate a version-2 .pai container (no GPU needed)."""
+    info = GgufInfo()
+    check(load().pai_b200_pai_inspect(os.fsencode(path), C.byref(info)), "pai_inspect")
+    return _info_dict(info)
+
+
 class Model:
     """LLaMA-shaped decoder resident on one device (one tensor-parallel rank)."""
 
@@ -277,6 +291,19 @@ class Model:
         h = C.c_void_p()
         check(load().pai_b200_model_load_gguf(dev.ctx, os.fsencode(path), tp_rank, tp_size, C.byref(h),
                                               C.byref(info)), "model_load_gguf")
+        self = cls.__new__(cls)
+        self.dev = dev
+        self.cfg = _info_dict(info)["cfg"]
+        self.h = h.value
+        return self
+
+    @classmethod
+    def from_pai(cls, dev: Device, path: str, tp_rank: int = 0, tp_size: int = 1) -> "Model":
+        """Load a version-2 .pai container's blocks as stored (pai_b200_model_load_pai)."""
+        info = GgufInfo()
+        h = C.c_void_p()
+        check(load().pai_b200_model_load_pai(dev.ctx, os.fsencode(path), tp_rank, tp_size, C.byref(h),
+                                             C.byref(info)), "model_load_pai")
         self = cls.__new__(cls)
         self.dev = dev
         self.cfg = _info_dict(info)["cfg"]

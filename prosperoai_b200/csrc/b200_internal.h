@@ -108,6 +108,23 @@ static inline B200_HD b200_xq_t b200_xq_view(void *base, uint32_t batch, uint64_
   return v;
 }
 
+/* ---- model files (csrc/host/b200_gguf.c, b200_pai.c) ------------------------------- */
+
+/* One tensor of a model file, viewed in place: ggml type (0 = f32), ggml
+ * shape rows x cols ([out][in]), bytes. */
+typedef struct b200_named_tensor {
+  char name[128];
+  uint32_t type;
+  uint64_t rows, cols, bytes;
+  const uint8_t *data;
+} b200_named_tensor_t;
+typedef struct b200_gguf_view b200_gguf_view_t;
+/* The tensors a LLaMA GGUF file's model uses (views into the mapped file,
+ * valid until b200_gguf_release); info as pai_b200_gguf_inspect. */
+pai_status_t b200_gguf_llama_tensors(const char *path, pai_b200_gguf_info_t *info, b200_named_tensor_t **out,
+                                     uint32_t *count, b200_gguf_view_t **view);
+void b200_gguf_release(b200_gguf_view_t *view);
+
 /* ---- errors ------------------------------------------------------------------------- */
 
 pai_status_t b200_fail(pai_status_t st, const char *fmt, ...);

@@ -438,6 +438,70 @@ static pai_status_t llama_view(const gg_file *f, pai_b200_gguf_info_t *info, gg_
   return PAI_OK;
 }
 
+/* The tensors a LLaMA model uses, in load order (token_embd, output [unless
+ * tied], output_norm, then blk.L.* per layer), as named views into the
+ * mapped file; b200_gguf_release unmaps it. */
+struct b200_gguf_view {
+  gg_file f;
+};
+
+pai_status_t b200_gguf_llama_tensors(const char *path, pai_b200_gguf_info_t *info, b200_named_tensor_t **out,
+                                     uint32_t *count, b200_gguf_view_t **view) {
+  gg_llama v;
+  b200_gguf_view_t *gv;
+  pai_status_t st;
+  if (!path || !info || !out || !count || !view) return b200_fail(PAI_ERR_INVALID_ARG, "gguf: NULL");
+  *out = NULL;
+  *count = 0;
+  *view = NULL;
+  memset(info, 0, sizeof(*info));
+  gv = (b200_gguf_view_t *)calloc(1, sizeof(*gv));
+  if (!gv) return b200_fail(PAI_ERR_NOMEM, "gguf: host allocation");
+  st = gg_open(path, &gv->f);
+  if (st) {
+    free(gv);
+    return st;
+  }
+  st = llama_view(&gv->f, info, &v);
+  const uint32_t n = 3 + 9 * info->cfg.n_layer;
+  b200_named_tensor_t *t = st ? NULL : (b200_named_tensor_t *)calloc(n, sizeof(*t));
+  if (!st && !t) st = b200_fail(PAI_ERR_NOMEM, "gguf: host allocation");
+  uint32_t k = 0;
+  const uint8_t *data = gv->f.base + gv->f.data_off;
+  const gg_tensor *top[3] = {v.embd, info->tied_output ? NULL : v.out, v.onorm};
+  for (uint32_t i = 0; !st && i < 3 + 9 * info->cfg.n_layer; i++) {
+    const gg_tensor *g = i < 3 ? top[i] : v.layer[i - 3];
+    if (!g) continue;
+    uint64_t b = 0;
+    st = tensor_bytes(&gv->f, g, &b);
+    if (st) break;
+    snprintf(t[k].name, sizeof(t[k].name), "%s", g->name);
+    t[k].type = g->type;
+    t[k].rows = g->n_dims >= 2 ? g->ne[1] : 1;
+    t[k].cols = g->ne[0];
+    t[k].data = data + g->offset;
+    t[k].bytes = b;
+    k++;
+  }
+  free(v.layer);
+  if (st) {
+    free(t);
+    gg_close(&gv->f);
+    free(gv);
+    return st;
+  }
+  *out = t;
+  *count = k;
+  *view = gv;
+  return PAI_OK;
+}
+
+void b200_gguf_release(b200_gguf_view_t *view) {
+  if (!view) return;
+  gg_close(&view->f);
+  free(view);
+}
+
 pai_status_t pai_b200_gguf_inspect(const char *path, pai_b200_gguf_info_t *info) {
   gg_file f;
   gg_llama v;

@@ -2,13 +2,15 @@
 stored, no dequantisation at import) decodes the same 64 greedy tokens as
 the oracle's composed reference decode of the same blocks, with non-unit
 norm gains; an untied and a tied lm head (output.weight absent: the
-embedding, adapters/llama/llama.c:445-470)."""
+embedding, adapters/llama/llama.c:445-470). The same file converted to a
+version-2 .pai container (ggml blocks kept, pai_b200_pai_from_gguf) and
+loaded from it (pai_b200_model_load_pai) decodes the same tokens."""
 import numpy as np
 import pytest
 
 import gguf_writer as gw
 from oracle import py_oracle as po
-from prosperoai_b200.api import Model, Session, gguf_inspect
+from prosperoai_b200.api import Model, Session, gguf_inspect, pai_from_gguf
 from test_gpu_model import SMALL, gpu_generate, oracle_generate, synth_weights
 
 pytestmark = pytest.mark.gpu
@@ -39,3 +41,13 @@ def test_gguf_model_matches_oracle(dev, tmp_path, wtype, etype, tied):
     m.close()
     assert got == want
     assert np.max(np.abs(hidden - want_hidden)) <= 1e-3 * np.max(np.abs(want_hidden))
+    pai = tmp_path / "model.pai"
+    pai_from_gguf(str(path), str(pai))
+    m = Model.from_pai(dev, str(pai))
+    sess = Session(m, 1, 80)
+    got_pai = gpu_generate(sess, prompt, 64)
+    hidden_pai = sess.hidden()
+    sess.close()
+    m.close()
+    assert got_pai == want
+    assert np.array_equal(hidden_pai, hidden)  # the same blocks reach the device
