@@ -4,7 +4,28 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+#include <mutex>
+
 #include "../b200_internal.h"
+
+// Per-device opt-in of a kernel's dynamic shared memory (the attribute is
+// per device and per kernel): raised, never lowered, to at least the bytes a
+// launch needs, once per device; safe when several host threads launch.
+struct SmemOptIn {
+  std::atomic<size_t> bytes[64];
+  std::mutex mu;
+  template <typename F>
+  cudaError_t ensure(int dev, size_t want, F &&set) {
+    if (dev < 0 || dev >= 64) return set(want);
+    if (bytes[dev].load(std::memory_order_acquire) >= want) return cudaSuccess;
+    std::lock_guard<std::mutex> lock(mu);
+    if (bytes[dev].load(std::memory_order_relaxed) >= want) return cudaSuccess;
+    const cudaError_t e = set(want);
+    if (e == cudaSuccess) bytes[dev].store(want, std::memory_order_release);
+    return e;
+  }
+};
 
 // ---- programmatic dependent launch ---------------------------------------------------------
 // pdl_wait blocks the calling thread until the previous kernel in the

@@ -44,14 +44,16 @@ struct pai_b200_ctx {
   uint32_t nretired;
 };
 
-// Retire a scratch buffer (see pai_b200_ctx::retired).
-static void retire(pai_b200_ctx_t *c, void *p) {
-  if (!p) return;
-  if (c->nretired < sizeof(c->retired) / sizeof(c->retired[0])) {
-    c->retired[c->nretired++] = p;
-  } else {  // unreachable with doubling growth; keep correctness over memory
-    cudaStreamSynchronize(c->stream);
-  }
+// Retire a scratch buffer (see pai_b200_ctx::retired). With growth that at
+// least doubles, 64 retirements cannot happen; should the list ever be full,
+// the growth is refused rather than a buffer a captured graph may still use
+// being freed or lost.
+static pai_status_t retire(pai_b200_ctx_t *c, void *p) {
+  if (!p) return PAI_OK;
+  if (c->nretired >= sizeof(c->retired) / sizeof(c->retired[0]))
+    return b200_fail(PAI_ERR_NOMEM, "scratch growth: %u buffers already retired", c->nretired);
+  c->retired[c->nretired++] = p;
+  return PAI_OK;
 }
 
 static thread_local char g_err[512];
@@ -178,7 +180,8 @@ extern "C" pai_status_t b200_ctx_xq(pai_b200_ctx_t *c, uint64_t bytes, void **bu
   if (bytes > c->xq_bytes) {
     if (c->capturing) return b200_fail(PAI_ERR_INTERNAL, "activation scratch growth during graph capture");
     const uint64_t want = std::max<uint64_t>(std::max<uint64_t>(bytes, 1u << 20), 2 * c->xq_bytes);
-    retire(c, c->xq);
+    pai_status_t rs = retire(c, c->xq);
+    if (rs) return rs;
     c->xq = nullptr;
     c->xq_bytes = 0;
     pai_status_t st = b200_cuda(cudaMalloc(&c->xq, want), "activation scratch alloc");
@@ -221,7 +224,8 @@ extern "C" pai_status_t b200_ctx_scratch(pai_b200_ctx_t *c, uint64_t partial_flo
     if (c->capturing) return b200_fail(PAI_ERR_INTERNAL, "scratch growth during graph capture");
     const uint64_t want =
         std::max<uint64_t>(std::max<uint64_t>(partial_floats, 1u << 20), 2 * c->partial_floats);
-    retire(c, c->partial);
+    pai_status_t rs = retire(c, c->partial);
+    if (rs) return rs;
     c->partial = nullptr;
     pai_status_t st = b200_cuda(cudaMalloc(&c->partial, want * sizeof(float)), "scratch alloc");
     if (st) {
@@ -233,7 +237,8 @@ extern "C" pai_status_t b200_ctx_scratch(pai_b200_ctx_t *c, uint64_t partial_flo
   if (counters > c->ncounters) {
     if (c->capturing) return b200_fail(PAI_ERR_INTERNAL, "scratch growth during graph capture");
     const uint32_t want = std::max<uint32_t>(std::max<uint32_t>(counters, 16384u), 2 * c->ncounters);
-    retire(c, c->counters);
+    pai_status_t rs = retire(c, c->counters);
+    if (rs) return rs;
     c->counters = nullptr;
     pai_status_t st = b200_cuda(cudaMalloc(&c->counters, want * sizeof(uint32_t)), "counter alloc");
     if (st) {

@@ -187,10 +187,23 @@ __device__ inline bool grid_sync(const KP &p, uint32_t &epoch, int ctid, int nth
 
 // ---- GEMV phases ------------------------------------------------------------------------
 
+// CTAs a GEMV phase's work is split over: every CTA when the phase has at
+// least one (group, unit) pair per CTA, else one pair each for the first
+// `total` CTAs (the rest idle). No CTA inside the split has an empty range,
+// so the CTAs that meet a row group are consecutive owners of its pairs.
+__device__ __forceinline__ uint32_t work_grid(const DPh &ph) {
+  return (uint32_t)min((uint64_t)gridDim.x, (uint64_t)ph.ngroups * ph.units);
+}
+
 __device__ __forceinline__ void phase_range(const DPh &ph, uint64_t &r0, uint64_t &r1) {
   const uint64_t total = (uint64_t)ph.ngroups * ph.units;
-  r0 = (uint64_t)blockIdx.x * total / gridDim.x;
-  r1 = (uint64_t)(blockIdx.x + 1) * total / gridDim.x;
+  const uint32_t gw = work_grid(ph);
+  if (blockIdx.x >= gw) {
+    r0 = r1 = total;
+    return;
+  }
+  r0 = (uint64_t)blockIdx.x * total / gw;
+  r1 = (uint64_t)(blockIdx.x + 1) * total / gw;
 }
 
 // A piece of a CTA's range inside one row group: units [u0, u1) of group g.
@@ -588,8 +601,9 @@ __device__ void consume(const KP &p, const DPh &ph, uint8_t *ring, uint64_t *ful
     }
     if (!active || bad) continue;
     // ---- this CTA's segment of group g is done ----
-    const uint32_t cta_lo = cta_of((uint64_t)s.g * ph.units, total, gridDim.x);
-    const uint32_t nseg = cta_of((uint64_t)(s.g + 1) * ph.units - 1, total, gridDim.x) - cta_lo + 1;
+    const uint32_t gw = work_grid(ph);
+    const uint32_t cta_lo = cta_of((uint64_t)s.g * ph.units, total, gw);
+    const uint32_t nseg = cta_of((uint64_t)(s.g + 1) * ph.units - 1, total, gw) - cta_lo + 1;
     float ya[NT], yb[NT];
 #pragma unroll
     for (int nt = 0; nt < NT; nt++) {  // lane pairs (c, c^1) hold the two halves of one sum
@@ -635,7 +649,7 @@ template <int G, int CONS>
 __device__ __noinline__ void attention(const KP &p, const DPh &ph, uint8_t *area, int warp, int lane, int ctid, int nthr,
                           volatile uint32_t *sticket) {
   constexpr int W = CONS;
-  const uint32_t nsub = nthr / 64;
+  const uint32_t nsub = nthr / 64;  // whole groups of 64 threads (2 dims each) share the positions
   float *qs = reinterpret_cast<float *>(area);
   float *sc = qs + G * kHD;
   float *red = sc + G * kAttnSub;
@@ -689,6 +703,7 @@ __device__ __noinline__ void attention(const KP &p, const DPh &ph, uint8_t *area
     const __half *kb = p.kc + kvbase + (size_t)start * kHD;
     const __half *vb = p.vc + kvbase + (size_t)start * kHD;
     const uint32_t dp = ctid & 63, sub = ctid >> 6;
+    const bool pv = sub < nsub;  // threads past the last whole group of 64 sit out the V sums
     float acc[G][2];
 #pragma unroll
     for (int g = 0; g < G; g++) acc[g][0] = acc[g][1] = 0.f;
@@ -760,7 +775,7 @@ __device__ __noinline__ void attention(const KP &p, const DPh &ph, uint8_t *area
         acc[g][0] *= al;
         acc[g][1] *= al;
       }
-      for (uint32_t i = sub; i < cnt; i += nsub) {
+      for (uint32_t i = sub; pv && i < cnt; i += nsub) {
         const uint32_t raw = __ldcg(reinterpret_cast<const unsigned int *>(vb + (size_t)(s0 + i) * kHD + 2 * dp));
         const float2 v = __half22float2(*reinterpret_cast<const __half2 *>(&raw));
 #pragma unroll
@@ -772,10 +787,12 @@ __device__ __noinline__ void attention(const KP &p, const DPh &ph, uint8_t *area
       }
       cbar(nthr);  // the scores are rewritten by the next round
     }
+    if (pv) {
 #pragma unroll
-    for (int g = 0; g < G; g++) {
-      red[((size_t)sub * G + g) * kHD + 2 * dp] = acc[g][0];
-      red[((size_t)sub * G + g) * kHD + 2 * dp + 1] = acc[g][1];
+      for (int g = 0; g < G; g++) {
+        red[((size_t)sub * G + g) * kHD + 2 * dp] = acc[g][0];
+        red[((size_t)sub * G + g) * kHD + 2 * dp + 1] = acc[g][1];
+      }
     }
     cbar(nthr);
     for (uint32_t i = ctid; i < G * kHD; i += nthr) {

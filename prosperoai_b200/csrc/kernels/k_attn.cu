@@ -449,9 +449,14 @@ pai_status_t launch_split(pai_b200_ctx_t *ctx, const AttnParams &p0, uint32_t ba
   p.stage = stage;
   const size_t smem = base + stage * row2;
   if (smem + stat > 48 * 1024) {
-    pai_status_t st = b200_cuda(
-        cudaFuncSetAttribute(k_attn_split<G, STEP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-        "k_attn_split smem attribute");
+    static SmemOptIn opt;
+    pai_status_t st = b200_cuda(opt.ensure(b200_ctx_device(ctx), smem,
+                                           [](size_t b) {
+                                             return cudaFuncSetAttribute(k_attn_split<G, STEP>,
+                                                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                                         (int)b);
+                                           }),
+                                "k_attn_split smem attribute");
     if (st) return st;
   }
   b200_launch(ctx, k_attn_split<G, STEP>, dim3(p.hk, p.nsplit, batch), dim3(128), smem, p);

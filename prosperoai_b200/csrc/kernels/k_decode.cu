@@ -130,10 +130,11 @@ extern "C" pai_status_t b200_decode_plan_create(pai_b200_ctx_t *ctx, uint32_t ty
     d.xq = s.xq;
     d.res = s.res;
     d.y = s.y;
-    const uint64_t total = (uint64_t)d.ngroups * d.units;
-    const uint64_t share = std::max<uint64_t>(1, total / pl->grid), max_range = (total + pl->grid - 1) / pl->grid;
-    // most CTAs one group meets: a CTA's share is at least floor(total/grid)
-    d.maxseg = (uint32_t)std::min<uint64_t>(pl->grid, (d.units + share - 1) / share + 1);
+    // the phase's work is split over gw = min(grid, total) CTAs (work_grid)
+    const uint64_t total = (uint64_t)d.ngroups * d.units, gw = std::min<uint64_t>(pl->grid, total);
+    const uint64_t share = total / gw, max_range = (total + gw - 1) / gw;
+    // most CTAs one group meets: a CTA's share is at least floor(total/gw) >= 1
+    d.maxseg = (uint32_t)std::min<uint64_t>(gw, (d.units + share - 1) / share + 1);
     if (d.maxseg > 1) partial_floats = std::max<uint64_t>(partial_floats, (uint64_t)d.maxseg * B * d.npad);
     tiles = std::max<uint64_t>(tiles, d.ntiles);
     groups4 = std::max<uint64_t>(groups4, (d.ntiles + 3) / 4);

@@ -597,14 +597,14 @@ pai_status_t gemm_launch(pai_b200_ctx_t *ctx, uint32_t m, uint32_t n, uint32_t k
   p.mtiles = mtiles;
   p.work = work;
   const size_t smem = gemm_smem_bytes<BN>();
-  static bool attr_set[64];
-  const int dev = b200_ctx_device(ctx);
-  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    st = b200_cuda(cudaFuncSetAttribute(k_gemm_q4_0<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-                   "k_gemm smem attribute");
-    if (st) return st;
-    if (dev >= 0 && dev < 64) attr_set[dev] = true;
-  }
+  static SmemOptIn opt;
+  st = b200_cuda(opt.ensure(b200_ctx_device(ctx), smem,
+                            [](size_t b) {
+                              return cudaFuncSetAttribute(k_gemm_q4_0<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                          (int)b);
+                            }),
+                 "k_gemm smem attribute");
+  if (st) return st;
   k_gemm_q4_0<BN><<<grid, kGThreadsWS, smem, s>>>(p);
   return b200_launched(ctx, 1, "k_gemm_q4_0");
 }

@@ -531,12 +531,15 @@ __global__ void __launch_bounds__(kThreadsT<NT, CONS>, 1) k_gemv(GemvP p) {
 }
 
 int sm_count(pai_b200_ctx_t *ctx) {
-  static int cached[64];
+  static std::atomic<int> cached[64];
   int dev = b200_ctx_device(ctx);
-  if (dev >= 0 && dev < 64 && cached[dev]) return cached[dev];
+  if (dev >= 0 && dev < 64) {
+    const int c = cached[dev].load(std::memory_order_relaxed);
+    if (c) return c;
+  }
   int v = 148;
   cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
-  if (dev >= 0 && dev < 64) cached[dev] = v;
+  if (dev >= 0 && dev < 64) cached[dev].store(v, std::memory_order_relaxed);
   return v;
 }
 
@@ -572,18 +575,18 @@ pai_status_t launch_t(pai_b200_ctx_t *ctx, GemvP p) {
   if (smem > kSmemCap<NT, CONS>) return b200_fail(PAI_ERR_UNSUPPORTED, "gemv: %zu B of shared memory", smem);
   // Function attributes are set once per device (the largest size seen),
   // not per launch: they cost host time on the decode path.
-  static size_t smem_set[64];
-  const int dev = b200_ctx_device(ctx);
-  pai_status_t st = PAI_OK;
-  if (dev < 0 || dev >= 64 || smem > smem_set[dev]) {
-    st = b200_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-                   "k_gemv smem attribute");
-    if (!st)
-      st = b200_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100),
-                     "k_gemv carveout attribute");
-    if (st) return st;
-    if (dev >= 0 && dev < 64) smem_set[dev] = smem;
-  }
+  static SmemOptIn opt;
+  pai_status_t st = b200_cuda(opt.ensure(b200_ctx_device(ctx), smem,
+                                         [&](size_t b) {
+                                           cudaError_t e = cudaFuncSetAttribute(
+                                               kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)b);
+                                           if (e == cudaSuccess)
+                                             e = cudaFuncSetAttribute(
+                                                 kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+                                           return e;
+                                         }),
+                              "k_gemv smem attribute");
+  if (st) return st;
   // Most segments a group can be cut into: a CTA's share is at least
   // floor(total / grid) units, so a group of `units` meets at most
   // ceil(units / share) + 1 CTAs.

@@ -596,15 +596,14 @@ cudaError_t launch_vec(pai_b200_ctx_t *ctx, dim3 grid, uint32_t mb, const V0Args
 // once (no link-time dependency on libcuda); NULL where unavailable.
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static bool looked = false;
-  if (!looked) {
-    looked = true;
+  static std::once_flag once;
+  std::call_once(once, [] {
     void *f = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
       fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
-  }
+  });
   return fn;
 }
 
@@ -614,15 +613,11 @@ cudaError_t launch_tma_mb(pai_b200_ctx_t *ctx, dim3 grid, const V0Args &a, const
   size_t smem = (size_t)kTmaStages * SB * kTmaRows + (size_t)MB * a.per * sizeof(float);
   if (LAYOUT == kOpScales) smem += split_groups(a.per, a.g) * kStrip * sizeof(float);
   // dynamic shared memory this instantiation is opted in to, per device (the attribute is per device)
-  static size_t opted[64];
-  const int dev = b200_ctx_device(ctx);
-  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (smem > opted[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(k_gemm_v0_tma<BITS, LAYOUT, MB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
-    if (e != cudaSuccess) return e;
-    opted[dev] = smem;
-  }
+  static SmemOptIn opt;
+  const cudaError_t e = opt.ensure(b200_ctx_device(ctx), smem, [](size_t b) {
+    return cudaFuncSetAttribute(k_gemm_v0_tma<BITS, LAYOUT, MB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)b);
+  });
+  if (e != cudaSuccess) return e;
   return b200_launch(ctx, k_gemm_v0_tma<BITS, LAYOUT, MB>, grid, dim3(kTmaThreads), smem, a, b200_ctx_errflag(ctx),
                      map);
 }
