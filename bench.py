@@ -909,6 +909,10 @@ def main():
                     help="time only the v0 grouped-scale GEMMs (w8/w4 ops and .pai blobs)")
     ap.add_argument("--nvtx", action="store_true",
                     help="wrap the timed decode steps in the NVTX range decode_timed")
+    ap.add_argument("--profile-layers", type=int, default=0,
+                    help="profiling only: the persistent layer kernel of an N-layer model with the 8B layer "
+                         "shapes (a few GB on the device), launched --steps times after --warmup; prints "
+                         "its CUDA-event time per launch, not a bench line")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -939,6 +943,34 @@ def main():
             sess.reset()
             dev.sync()
         print(json.dumps(prefill_timing(dev, sess, prompts)), flush=True)
+        sess.close()
+        model.close()
+        dev.close()
+        return
+    if args.profile_layers:
+        # a small-memory stand-in for ncu captures of k_decode: N layers of the
+        # config-5 shape after a 512-token prefill
+        from prosperoai_b200.api import Device, Model, Session
+        dev = Device(local)
+        cfg = dict(CFG_8B, n_layer=args.profile_layers)
+        model = Model(dev, cfg)
+        model.synthesize(SEED)
+        sess = Session(model, args.batch, PROMPT + args.warmup + 8)
+        prompts = np.random.default_rng(SEED).integers(0, cfg["vocab"], (args.batch, PROMPT)).astype(np.int32)
+        sess.prefill(prompts)
+        sess.run(args.warmup)
+        dev.sync()
+        L = __import__("prosperoai_b200._native", fromlist=["load"]).load()
+        e0, e1 = C.c_void_p(), C.c_void_p()
+        L.pai_b200_event_create(dev.ctx, C.byref(e0))
+        L.pai_b200_event_create(dev.ctx, C.byref(e1))
+        L.pai_b200_event_record(dev.ctx, e0)
+        sess.run_layers(args.steps)
+        L.pai_b200_event_record(dev.ctx, e1)
+        ms = C.c_float()
+        L.pai_b200_event_elapsed(e0, e1, C.byref(ms))
+        print(json.dumps({"profile": "k_decode", "layers": args.profile_layers, "batch": args.batch,
+                          "launches": args.steps, "ms_per_launch": round(ms.value / args.steps, 4)}), flush=True)
         sess.close()
         model.close()
         dev.close()
