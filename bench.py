@@ -552,21 +552,30 @@ def cpu_baseline_port(dev, steps=3, prompt=24):
                        f"full-model tok/s = 1/(32 x {dt * 1e3:.1f} ms)")}
 
 
-def decode_variant(dev, model, batch, prompt, steps=20, warmup=3, per_op=False):
+def path_session(model, batch, max_ctx, persistent):
+    """A session whose step runs the layers as the persistent kernel
+    (PAI_B200_PERSISTENT=1) or as one launch per op."""
+    from prosperoai_b200.api import Session
+    os.environ["PAI_B200_PERSISTENT"] = "1" if persistent else "0"
+    try:
+        return Session(model, batch, max_ctx)
+    finally:
+        os.environ.pop("PAI_B200_PERSISTENT", None)
+
+
+def decode_variant(dev, model, batch, prompt, steps=20, warmup=3, persistent=None):
     """Decode tok/s of one more session of the same model: `batch`
     independent sequences after a `prompt`-token seeded prompt (appended by
     pai_b200_session_prefill), CUDA-graph steps timed with CUDA events (as
-    the headline line). per_op: the step as one launch per op instead of the
-    persistent layer kernel (PAI_B200_PERSISTENT=0), for comparison."""
+    the headline line). persistent: True/False picks the step's path
+    (persistent layer kernel or one launch per op), None the default."""
     from prosperoai_b200 import _native
     from prosperoai_b200.api import Session
     L = _native.load()
-    if per_op:
-        os.environ["PAI_B200_PERSISTENT"] = "0"
-    try:
+    if persistent is None:
         sess = Session(model, batch, prompt + warmup + steps + 8)
-    finally:
-        os.environ.pop("PAI_B200_PERSISTENT", None)
+    else:
+        sess = path_session(model, batch, prompt + warmup + steps + 8, persistent)
     kernels = sess.step_kernels
     ids = np.random.default_rng(SEED + batch).integers(0, CFG_8B["vocab"], (batch, prompt)).astype(np.int32)
     sess.prefill(ids)
@@ -702,9 +711,18 @@ def gpu_arm(args):
             gemm["by_m"][str(m)] = {"us": round(float(t[i]), 2), "tflops": round(tf, 1),
                                     "frac": round(tf / (peak_tf * world), 4)}
     if rank == 0:
-        layer_roof = None if args.no_roofline or tp else layer_kernel_roofline(dev, model, sess, hbm, kind)
+        layer_roof = None
+        if not args.no_roofline and not tp:
+            # the persistent layer kernel timed alone, from a session on that path
+            psess = sess if sess.step_kernels == 4 else path_session(model, B, max_ctx, True)
+            if psess is not sess:
+                psess.prefill(prompts)
+            layer_roof = layer_kernel_roofline(dev, model, psess, hbm, kind)
+            if psess is not sess:
+                psess.close()
         gemv_roof = None if args.no_roofline else gemv_roofline(dev, hbm, kind)
-        roof = layer_roof or gemv_roof
+        # the dominant kernel of the step the headline measures
+        roof = layer_roof if sess.step_kernels == 4 else gemv_roof
         if gemm is None and not args.no_roofline:
             gemm = prefill_gemm(dev)
         sweep = None if args.no_roofline else gemv_sweep(dev, hbm, kind)
@@ -714,7 +732,7 @@ def gpu_arm(args):
         if world == 1 and not args.no_roofline:
             # configs 4-5 also name 8 independent sequences and a 4096-position cache
             variants = [decode_variant(dev, model, 8, P), decode_variant(dev, model, 1, 4096),
-                        decode_variant(dev, model, 1, P, per_op=True)]
+                        decode_variant(dev, model, 1, P, persistent=sess.step_kernels != 4)]
             variants.append(layer_config4(dev, hbm, kind))
         jobs = 1 if tp else world  # sequences advanced per step: TP ranks share one job
         value = jobs * B * K / (t_dev * 1e-3)
@@ -741,6 +759,7 @@ def gpu_arm(args):
                             f"one launch per op ({sess.step_kernels} per step, one CUDA graph)"),
             "roofline": roof,
             "gemv_roofline": gemv_roof if roof is not gemv_roof else None,
+            "layer_kernel_roofline": layer_roof if roof is not layer_roof else None,
             "prefill_gemm": gemm,
             "prompt_prefill": prefill,
             "decode_variants": variants,

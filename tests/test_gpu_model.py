@@ -194,7 +194,7 @@ def test_persistent_kernel_agrees_with_one_launch_per_op(dev, wtype, batch, monk
     m.synthesize(31 + wtype)
     monkeypatch.setenv("PAI_B200_PERSISTENT", "0")
     s_op = Session(m, batch, 64)
-    monkeypatch.delenv("PAI_B200_PERSISTENT")
+    monkeypatch.setenv("PAI_B200_PERSISTENT", "1")
     s_pk = Session(m, batch, 64)
     assert s_pk.step_kernels == 4 and s_op.step_kernels > 4
     tok = np.random.default_rng(batch).integers(0, cfg["vocab"], batch).astype(np.int32)

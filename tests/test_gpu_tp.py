@@ -187,10 +187,11 @@ def oracle_8b(dev):
     return prompt, max_ctx, [int(t) for t in want]
 
 
-def _worker_8b(rank, world, port, cfg, prompt, steps, max_ctx, q):
+def _worker_8b(rank, world, port, cfg, prompt, steps, max_ctx, q, persistent="0"):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
+    os.environ["PAI_B200_PERSISTENT"] = persistent
     out = {"rank": rank}
     try:
         import torch.distributed as dist
@@ -204,6 +205,7 @@ def _worker_8b(rank, world, port, cfg, prompt, steps, max_ctx, q):
         model.synthesize(SEED_8B)
         model.set_tp(comm)
         sess = Session(model, 1, max_ctx)
+        out["kernels"] = sess.step_kernels
         out["tokens"] = gpu_generate(sess, prompt, steps)
         dist.barrier()
         sess.close()
@@ -217,8 +219,13 @@ def _worker_8b(rank, world, port, cfg, prompt, steps, max_ctx, q):
     q.put(out)
 
 
+def _worker_8b_persistent(rank, world, port, cfg, prompt, steps, max_ctx, q):
+    _worker_8b(rank, world, port, cfg, prompt, steps, max_ctx, q, persistent="1")
+
+
+@pytest.mark.parametrize("persistent", [False, True])
 @pytest.mark.parametrize("world", [2, 4, 8])
-def test_tp_8b_shape_decode_matches_oracle(oracle_8b, world):
+def test_tp_8b_shape_decode_matches_oracle(oracle_8b, world, persistent):
     """Column-parallel q/k/v/gate/up, row-parallel o/down with the peer-memory
     exchange, KV cache split by KV head (one per rank at 8), vocabulary-sharded
     lm head with the cross-rank argmax: 64 greedy tokens on every rank equal
@@ -226,9 +233,11 @@ def test_tp_8b_shape_decode_matches_oracle(oracle_8b, world):
     if _gpu_count() < world:
         pytest.skip(f"needs {world} GPUs")
     prompt, max_ctx, want = oracle_8b
-    res = _run_ranks(world, TP_8B, prompt, STEPS, max_ctx, target=_worker_8b)
+    res = _run_ranks(world, TP_8B, prompt, STEPS, max_ctx,
+                     target=_worker_8b_persistent if persistent else _worker_8b)
     for r in range(world):
         assert "error" not in res[r], res[r]["error"]
+        assert (res[r]["kernels"] == 3) == persistent  # 3: layers, lm head shard, greedy pick over peer memory
         assert res[r]["tokens"] == want, f"rank {r} of {world}"
 
 
@@ -241,6 +250,7 @@ def _skip_worker(rank, world, port, cfg, prompt, steps, max_ctx, q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
+    os.environ["PAI_B200_PERSISTENT"] = "1"  # the step holds no collective library call
     out = {"rank": rank}
     try:
         import torch.distributed as dist
