@@ -176,7 +176,7 @@ void b200_graph_destroy(void *exec);
 
 /* ---- kernel launchers (csrc/kernels) ----------------------------------------------- */
 
-enum { B200_EPI_STORE = 0, B200_EPI_RESIDUAL = 1, B200_EPI_SILU_GLU = 2, B200_EPI_PUSH = 3 };
+enum { B200_EPI_STORE = 0, B200_EPI_RESIDUAL = 1, B200_EPI_SILU_GLU = 2 };
 
 /* GEMV over a packed matrix with x given as xq (batch vectors of k).
  * B200_EPI_SILU_GLU: each 16-row tile holds 8 gate rows then the 8 matching
@@ -273,66 +273,61 @@ pai_status_t b200_launch_attn_prefill(pai_b200_ctx_t *ctx, uint32_t rows, uint32
 pai_status_t b200_launch_silu_glu_rows(pai_b200_ctx_t *ctx, uint64_t rows, uint32_t ff, const float *gu,
                                        float *hout);
 /* ---- persistent decode step (kernels/k_decode*.cu) --------------------------------
- * One cooperative launch runs the layers of a decode step as a list of
- * phases over one CTA per SM: a weight producer streams every matrix of the
- * step, in order, into a shared-memory ring (it never waits for activations,
- * so the next matrix is in flight while the current phase finishes);
- * consumer warps run the phases in order and meet at a grid barrier between
- * them. B200_PH_NORM quantises RMSNorm(xf) * gamma into xo (the lm head's
- * operand); every GEMV phase uses the block type the plan was made for. */
-enum { B200_PH_EMBED = 0, B200_PH_GEMV = 1, B200_PH_ATTN = 2, B200_PH_NORM = 3, B200_PH_XCHG = 4 };
+ * One cooperative launch runs the layers of a decode step over one CTA per
+ * SM: a weight producer streams every matrix of the step, in order, into a
+ * shared-memory ring (it never waits for activations, so the next matrix is
+ * in flight while the current phase finishes); consumer warps run the
+ * phases of each layer in order and meet at a grid barrier between them. */
 
 /* Landing buffer of the tensor-parallel persistent decode: one per rank in
  * its HBM, mapped into every other rank with CUDA IPC.
- *   header (B200_LAND_HDR bytes), u64 words: [0] arrivals of row exchanges
- *   (every CTA of every rank adds 1 per exchange), [1] row exchanges this
- *   rank completed, [2] arrivals of greedy pairs (every rank adds 1 per
- *   step), [3] greedy exchanges this rank completed;
+ *   header (B200_LAND_HDR bytes): u64 words [1] row exchanges this rank
+ *   completed, [2] arrivals of greedy pairs (every rank adds 1 per step),
+ *   [3] greedy exchanges this rank completed; from byte B200_LAND_FLAGS,
+ *   u64 arrival stamps [rank][cta] of the row exchanges;
  *   row slots [2 parities][ranks][rows] fp32 (rows = batch x n_embd): the
- *   o/down GEMV epilogue of rank r stores its partial rows into slot
- *   [parity][r] of every rank's buffer (B200_EPI_PUSH);
+ *   rows a rank reduced from its o/down partial sums, stored by that rank
+ *   into slot [parity][rank] of every rank's buffer;
  *   pair slots [2 parities][ranks][8][2] fp32: each rank's (maximum, index)
  *   of its vocabulary shard per sequence. */
-#define B200_LAND_HDR 256u
+#define B200_LAND_HDR 16384u
+#define B200_LAND_FLAGS 1024u
+#define B200_LAND_MAX_CTAS 192u
 static inline B200_HD uint64_t b200_land_bytes(uint32_t nranks, uint64_t rows) {
   return B200_LAND_HDR + (2ull * nranks * rows + 2ull * nranks * 16u) * 4u;
 }
 static inline B200_HD uint64_t b200_land_pairs_off(uint32_t nranks, uint64_t rows) {
   return B200_LAND_HDR + 2ull * nranks * rows * 4u;
 }
-enum { B200_X_XQ = 0, B200_X_NORM = 1 };
-typedef struct b200_phase {
-  uint32_t kind, type, epi, xsrc; /* B200_PH_*, block type, B200_EPI_*, B200_X_* */
-  const void *w;                  /* GEMV: packed matrix (256-byte aligned) */
-  uint64_t n, k;                  /* GEMV: rows, columns */
-  const float *xf, *gamma;        /* B200_X_NORM, B200_PH_NORM: fp32 rows [batch][k], RMSNorm gain */
-  b200_xq_t xq;                   /* B200_X_XQ: quantised input */
-  const float *res;               /* EPI_RESIDUAL: residual rows (may be y) */
-  float *y;                       /* output rows */
-  b200_xq_t xo;                   /* EPI_SILU_GLU / B200_PH_NORM: quantised output (limbs NULL: none) */
-  uint32_t layer;                 /* ATTN: cache layer */
-  uint32_t xi;                    /* EPI_PUSH GEMV and B200_PH_XCHG: index of the row exchange in the step */
-} b200_phase_t;
+
+/* The matrices and norm gains of one layer (packed, this rank's shard). */
+typedef struct b200_decode_layer {
+  const void *wqkv, *wo, *wgu, *wdown;
+  const float *attn_norm, *ffn_norm;
+} b200_decode_layer_t;
 
 typedef struct b200_decode_args {
-  uint32_t batch;
-  float eps;                      /* RMSNorm epsilon of every norm phase */
+  uint32_t type;                  /* block type of the layer matrices */
+  uint32_t batch, n_layer;
+  float eps;                      /* RMSNorm epsilon */
   /* embedding: x[b] = row tok_in[b] of the packed vocab x n_embd table */
   uint32_t etype;
   const void *emb;
   uint64_t vocab, n_embd;
   const int32_t *tok_in;
-  float *x;
-  /* attention: q|k|v rows [batch][(h + 2 hk) hd], fp16 cache
-   * [layer][seq][kv head][cap][hd], rotary tables [cap][hd/2] */
+  /* this rank's shapes: q|k|v rows, o input columns, ffn rows per gate/up half */
+  uint64_t n_qkv, k_o, ffl;
+  /* attention: fp16 cache [layer][seq][kv head][cap][hd], rotary tables [cap][hd/2] */
   uint32_t h, hk, hd;
-  int32_t *pos;                   /* device position of the step's token (advanced at the end) */
+  int32_t *pos;                   /* device position of the step's token */
   uint64_t cap, seq_stride, layer_stride;
   uint16_t *kc, *vc;
   const float *cos_t, *sin_t;
-  const float *qkv;
-  float *att;
-  b200_xq_t xq_att;               /* attention output, quantised for the o projection */
+  /* outputs: the hidden state after the last layer and RMSNorm(x) * out_norm
+   * quantised for the lm head */
+  const float *out_norm;
+  float *x;
+  b200_xq_t xq_out;
   /* tensor parallelism: rank of nranks, every rank's landing buffer as
    * mapped here (nranks = 1: none) */
   uint32_t rank, nranks;
@@ -340,12 +335,12 @@ typedef struct b200_decode_args {
 } b200_decode_args_t;
 
 typedef struct b200_decode_plan b200_decode_plan_t;
-/* Check the phase list against the kernel's limits, size and allocate its
- * scratch (split-K partials, tickets, attention partials, barrier words)
- * and upload the phases. PAI_ERR_UNSUPPORTED when a shape does not fit. */
-pai_status_t b200_decode_plan_create(pai_b200_ctx_t *ctx, uint32_t type, const b200_decode_args_t *args,
-                                     const b200_phase_t *phases, uint32_t nphases,
-                                     b200_decode_plan_t **out);
+/* Check the shapes against the kernel's limits, size and allocate its
+ * scratch (split-K partials, attention partials, the normed operand, block
+ * sums of squares, barrier words) and upload the layer table.
+ * PAI_ERR_UNSUPPORTED when a shape does not fit. */
+pai_status_t b200_decode_plan_create(pai_b200_ctx_t *ctx, const b200_decode_args_t *args,
+                                     const b200_decode_layer_t *layers, b200_decode_plan_t **out);
 pai_status_t b200_decode_launch(pai_b200_ctx_t *ctx, b200_decode_plan_t *plan);
 void b200_decode_plan_destroy(b200_decode_plan_t *plan);
 

@@ -440,58 +440,33 @@ static pai_status_t norm_gemv(pai_b200_session_t *s, uint32_t type, uint64_t n, 
   return st;
 }
 
-/* The phase list of the persistent decode kernel: the embedding row, the
- * five phases of every layer in the op order of llama.c:669-797, and the
- * final RMSNorm into the lm head's operand. Under tensor parallelism the
- * o and down GEMVs push their partial rows to every rank and a row
- * exchange adds them to the hidden state (seven phases per layer). */
+/* The persistent decode kernel of the session: the layer table, the shapes
+ * of this rank's shard, the cache and the lm head's operand (xq_e). Under
+ * tensor parallelism it also maps every rank's landing buffer (collective). */
 static pai_status_t make_plan(pai_b200_session_t *s) {
   pai_b200_model_t *m = s->m;
   const pai_b200_model_cfg_t *c = &m->cfg;
-  const int tp = m->tp > 1;
-  const uint32_t E = c->n_embd, nph = 2 + (tp ? 7 : 5) * c->n_layer;
-  b200_phase_t *ph = (b200_phase_t *)calloc(nph, sizeof(*ph));
+  b200_decode_layer_t *layers = (b200_decode_layer_t *)calloc(c->n_layer, sizeof(*layers));
   b200_decode_args_t a;
-  uint32_t i = 0;
-  pai_status_t st;
-  if (!ph) return b200_fail(PAI_ERR_NOMEM, "session_create: host allocation");
-  ph[i++].kind = B200_PH_EMBED;
+  pai_status_t st = PAI_OK;
+  if (!layers) return b200_fail(PAI_ERR_NOMEM, "session_create: host allocation");
   for (uint32_t l = 0; l < c->n_layer; l++) {
-    b200_phase_t *q = &ph[i++], *at = &ph[i++], *o = &ph[i++], *xo = tp ? &ph[i++] : NULL, *gu = &ph[i++];
-    b200_phase_t *dn = &ph[i++], *xd = tp ? &ph[i++] : NULL;
-    q->kind = B200_PH_GEMV, q->type = c->wtype, q->epi = B200_EPI_STORE, q->xsrc = B200_X_NORM;
-    q->w = m->wqkv[l], q->n = m->n_qkv, q->k = E, q->xf = s->x, q->gamma = m->attn_norm[l], q->y = s->qkv;
-    at->kind = B200_PH_ATTN, at->layer = l;
-    o->kind = B200_PH_GEMV, o->type = c->wtype, o->epi = B200_EPI_RESIDUAL, o->xsrc = B200_X_XQ;
-    o->w = m->wo[l], o->n = E, o->k = m->k_o, o->xq = s->xq_o, o->res = s->x, o->y = s->x;
-    gu->kind = B200_PH_GEMV, gu->type = c->wtype, gu->epi = B200_EPI_SILU_GLU, gu->xsrc = B200_X_NORM;
-    gu->w = m->wgu[l], gu->n = 2ull * m->ffl, gu->k = E, gu->xf = s->x, gu->gamma = m->ffn_norm[l];
-    gu->y = s->h, gu->xo = s->xq_h;
-    dn->kind = B200_PH_GEMV, dn->type = c->wtype, dn->epi = B200_EPI_RESIDUAL, dn->xsrc = B200_X_XQ;
-    dn->w = m->wdown[l], dn->n = E, dn->k = m->ffl, dn->xq = s->xq_h, dn->res = s->x, dn->y = s->x;
-    if (tp) {
-      /* row-parallel o/down: partial rows pushed to every rank, then added */
-      o->epi = dn->epi = B200_EPI_PUSH, o->res = dn->res = NULL, o->y = dn->y = s->x;
-      o->xi = xo->xi = 2 * l, dn->xi = xd->xi = 2 * l + 1;
-      xo->kind = xd->kind = B200_PH_XCHG, xo->n = xd->n = E, xo->y = xd->y = s->x;
-    }
+    layers[l].wqkv = m->wqkv[l], layers[l].wo = m->wo[l], layers[l].wgu = m->wgu[l], layers[l].wdown = m->wdown[l];
+    layers[l].attn_norm = m->attn_norm[l], layers[l].ffn_norm = m->ffn_norm[l];
   }
-  ph[i].kind = B200_PH_NORM, ph[i].xf = s->x, ph[i].gamma = m->output_norm, ph[i].k = E, ph[i].xo = s->xq_e;
-  i++;
   memset(&a, 0, sizeof(a));
-  a.batch = s->batch;
-  a.eps = c->eps;
-  a.etype = c->etype, a.emb = m->tok_embd, a.vocab = c->vocab, a.n_embd = E, a.tok_in = s->tok_in, a.x = s->x;
+  a.type = c->wtype, a.batch = s->batch, a.n_layer = c->n_layer, a.eps = c->eps;
+  a.etype = c->etype, a.emb = m->tok_embd, a.vocab = c->vocab, a.n_embd = c->n_embd, a.tok_in = s->tok_in;
+  a.n_qkv = m->n_qkv, a.k_o = m->k_o, a.ffl = m->ffl;
   a.h = m->hl, a.hk = m->hkl, a.hd = c->head_dim, a.pos = s->dpos;
   a.cap = s->max_ctx, a.seq_stride = s->seq_stride, a.layer_stride = s->layer_stride;
   a.kc = s->kc, a.vc = s->vc, a.cos_t = s->cos_t, a.sin_t = s->sin_t;
-  a.qkv = s->qkv, a.att = s->att, a.xq_att = s->xq_o;
+  a.out_norm = m->output_norm, a.x = s->x, a.xq_out = s->xq_e;
   a.rank = m->rank, a.nranks = m->tp;
-  st = PAI_OK;
-  if (tp) st = b200_tp_land(s->tp, (uint64_t)s->batch * E, s->land); /* collective */
-  for (uint32_t r = 0; tp && r < m->tp; r++) a.land[r] = s->land[r];
-  if (!st) st = b200_decode_plan_create(m->ctx, c->wtype, &a, ph, i, &s->plan);
-  free(ph);
+  if (m->tp > 1) st = b200_tp_land(s->tp, (uint64_t)s->batch * c->n_embd, s->land); /* collective */
+  for (uint32_t r = 0; m->tp > 1 && r < m->tp; r++) a.land[r] = s->land[r];
+  if (!st) st = b200_decode_plan_create(m->ctx, &a, layers, &s->plan);
+  free(layers);
   return st;
 }
 

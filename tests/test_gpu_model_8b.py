@@ -36,7 +36,10 @@ def top2_gap(logits):
     return float(logits[i] - np.max(rest))
 
 
-def test_8b_shape_greedy_tokens_match_reference_for_64_steps(dev):
+@pytest.fixture(scope="module")
+def oracle_8b_run(dev):
+    """The oracle's 64 greedy tokens, top-1/top-2 gaps and final hidden state
+    for the 8B-shaped model (computed once for both step paths)."""
     cfg, seed, steps = CFG_8B, 88, 64
     prompt = [int(t) for t in np.random.default_rng(seed).integers(0, cfg["vocab"], 8)]
     max_ctx = len(prompt) + steps
@@ -54,21 +57,31 @@ def test_8b_shape_greedy_tokens_match_reference_for_64_steps(dev):
         gaps.append(top2_gap(logits))
     ref_hidden = ref.hidden()
     ref.close()
-    del w
     print(f"oracle top-1/top-2 logit gaps: min {min(gaps):.3e}, median {np.median(gaps):.3e}")
-    m = Model(dev, cfg)
-    m.synthesize(seed)
-    s = Session(m, 1, max_ctx)
-    got = gpu_generate(s, prompt, steps)
+    return dict(cfg=cfg, seed=seed, prompt=prompt, max_ctx=max_ctx, want=want, gaps=gaps, hidden=ref_hidden)
+
+
+@pytest.mark.parametrize("persistent", [False, True])
+def test_8b_shape_greedy_tokens_match_reference_for_64_steps(dev, oracle_8b_run, persistent, monkeypatch):
+    o = oracle_8b_run
+    monkeypatch.setenv("PAI_B200_PERSISTENT", "1" if persistent else "0")
+    m = Model(dev, o["cfg"])
+    m.synthesize(o["seed"])
+    s = Session(m, 1, o["max_ctx"])
+    assert (s.step_kernels == 4) == persistent
+    got = gpu_generate(s, o["prompt"], 64)
     hidden = s.hidden()
     s.close()
     m.close()
+    want, gaps = o["want"], o["gaps"]
     first_bad = next((i for i, (a, b) in enumerate(zip(got, want)) if a != b), None)
     assert got == want, f"first mismatch at step {first_bad}, oracle gap there {gaps[first_bad]:.3e}"
-    assert np.max(np.abs(hidden - ref_hidden)) <= 1e-3 * np.max(np.abs(ref_hidden))
+    assert np.max(np.abs(hidden - o["hidden"])) <= 1e-3 * np.max(np.abs(o["hidden"]))
 
 
-def test_config4_layer_over_4096_position_cache(dev):
+@pytest.mark.parametrize("persistent", [False, True])
+def test_config4_layer_over_4096_position_cache(dev, persistent, monkeypatch):
+    monkeypatch.setenv("PAI_B200_PERSISTENT", "1" if persistent else "0")
     cfg = dict(CFG_8B, n_layer=1, vocab=2048)
     seed, past, steps = 404, 4096, 8
     max_ctx = past + 128
