@@ -896,6 +896,16 @@ def reference_arm(args):
             "config": {"workload": "Llama-3-8B-shaped Q4_0 decode (config 5)", "batch": 1,
                        "prompt": PROMPT, "device": f"host CPU, {threads} threads"},
             "impl": "reference",
+            "caveats": [
+                "a bounded sample: 1 of 32 layers and 1/32 of the lm-head rows per token, scaled x32",
+                "the reference's fastest GEMV (cpu/optimized pai_opt_gemv_f32) rather than the "
+                "pai_ref_gemm_f32 its executor calls, and split over all host threads by this harness "
+                "(the reference executor runs a step on one thread): the reference's best case",
+                "weights held as f32 after dequantisation, as the reference session keeps them "
+                "(models/model.c:246-290): 4x-8x the bytes of the quantised blocks",
+                "RoPE at one position and the last-row decode attention are the oracle's restatements "
+                "(the reference offers only the full-sequence forms); all other ops are the reference's",
+            ],
             "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": kind,
                              "sample": sample},
             "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,

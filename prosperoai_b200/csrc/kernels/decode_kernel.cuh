@@ -82,13 +82,21 @@ constexpr int kStages = 4;
 template <int CONS>
 constexpr uint32_t kStageBytes = CONS * 2304u;
 constexpr uint32_t kHD = 128;
+constexpr uint32_t kAS = kHD + 4;  // attention partial: o[kHD], max, sum, 2 pad (16-byte rows)
 enum { M_QKV = 0, M_O = 1, M_GU = 2, M_DOWN = 3 };
 
 // Shape and work split of one layer-matrix kind (the same for every layer).
 struct Shape {
   uint32_t n, k, units, ntiles, ngroups, npad, gw, maxseg, cons;
+  uint32_t tab;     // first entry of this shape's groups in the split-count table
   uint64_t sc_off;  // byte offset of the header plane in the packed matrix
 };
+
+// Split counts (CTAs per row group) of the four shapes' groups, filled by
+// every CTA at the start of the launch: readers of partial sums look the
+// count up instead of recomputing the split.
+constexpr uint32_t kTab = 2048;
+static __shared__ uint8_t s_nseg[kTab];
 
 struct Layer {
   const uint8_t *w[4];  // packed q|k|v, o, gate|up, down
@@ -119,14 +127,22 @@ struct KP {
   b200_xq_t xq_out;  // RMSNorm(x) * out_norm for the lm head
   const float *out_norm;
   float *part[2];  // split-K partials: q|k|v and gate|up in [0], o and down in [1]
-  float *apart;    // attention CTA partials [batch][h][per_head][kHD + 2]
+  float *apart;    // attention CTA partials [batch][h][per_head][kAS]
   uint32_t *bar;   // [0] barrier arrivals, [1] exits, [2] abort
   uint32_t *err;   // the context's host-mapped error word
+  uint32_t scratch_off;  // per-warp staging scratch: byte offset in the staging area
   uint64_t wait_ns;
   // tensor parallelism: every rank's landing buffer as mapped here
   uint8_t *land[B200_TP_MAX_RANKS];
   uint32_t rank, nranks;
 };
+
+// The launch's parameters and position count, copied into shared memory
+// at the start: the phases compiled out of line reach them through a
+// reference, and a reference to a __grid_constant__ parameter reads through
+// the memory system, one dependent round trip per first access.
+static __shared__ KP s_kp;
+static __shared__ uint32_t s_npos;  // positions of the cache including this step's
 
 __device__ __forceinline__ void cbar(int nthr) { asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory"); }
 
@@ -214,16 +230,51 @@ __device__ __forceinline__ void group_split(const Shape &sh, uint32_t g, uint32_
   nseg = cta_of((uint64_t)(g + 1) * sh.units - 1, total, sh.gw) - lo + 1;
 }
 
-// Row `row` of vector b: the group's partial sums added in split order.
+// Row `row` of vector b is the sum of its group's partials in split order.
+// row_load issues the loads of the first CH parts (predicated, no branch: the
+// loads of several rows go out together); row_finish adds them in order and
+// loads any further parts.
+struct RowRef {
+  const float *q;
+  uint32_t nseg;
+};
+template <int CH, int CONS>
+__device__ __forceinline__ RowRef row_load(const float *part, const Shape &sh, uint32_t batch, uint32_t b,
+                                           uint32_t row, float (&v)[CH]) {
+  RowRef r;
+  r.nseg = s_nseg[sh.tab + row / (16u * CONS)];
+  r.q = part + (size_t)b * sh.npad + row;
+  const size_t stride = (size_t)batch * sh.npad;
+#pragma unroll
+  for (int i = 0; i < CH; i++) v[i] = (uint32_t)i < r.nseg ? __ldcg(r.q + i * stride) : 0.0f;
+  return r;
+}
+template <int CH>
+__device__ __forceinline__ float row_finish(const RowRef &r, const float (&v)[CH], uint32_t batch, uint32_t npad) {
+  float s = v[0];
+#pragma unroll
+  for (int i = 1; i < CH; i++)
+    if ((uint32_t)i < r.nseg) s += v[i];
+  for (uint32_t i = CH; i < r.nseg; i++) s += __ldcg(r.q + (size_t)i * batch * npad);
+  return s;
+}
+template <int CH, int CONS>
 __device__ __forceinline__ float row_sum(const float *part, const Shape &sh, uint32_t batch, uint32_t b,
                                          uint32_t row) {
-  uint32_t lo, nseg;
-  group_split(sh, row / 16 / sh.cons, lo, nseg);
-  const float *q = part + (size_t)b * sh.npad + row;
-  const size_t stride = (size_t)batch * sh.npad;
-  float s = __ldcg(q);
-  for (uint32_t i = 1; i < nseg; i++) s += __ldcg(q + i * stride);
-  return s;
+  float v[CH];
+  const RowRef r = row_load<CH, CONS>(part, sh, batch, b, row, v);
+  return row_finish<CH>(r, v, batch, sh.npad);
+}
+
+// Fill s_nseg (consumer threads; a named barrier follows before any use).
+__device__ inline void fill_split_table(const KP &p, int ctid, int nthr) {
+#pragma unroll
+  for (int k = 0; k < 4; k++)
+    for (uint32_t g = ctid; g < p.sh[k].ngroups; g += nthr) {
+      uint32_t lo, nseg;
+      group_split(p.sh[k], g, lo, nseg);
+      s_nseg[p.sh[k].tab + g] = (uint8_t)nseg;
+    }
 }
 
 // A piece of a CTA's range inside one row group: units [u0, u1) of group g.
@@ -282,6 +333,7 @@ __device__ bool produce(const KP &p, const Shape &sh, const uint8_t *w, uint8_t 
 struct XArea {
   XS xs;
   uint32_t nent;
+  uint32_t u0;  // unit of entry 0
   bool resident;
 };
 
@@ -291,6 +343,7 @@ __device__ __forceinline__ XArea x_area(const KP &p, const Shape &sh, uint8_t *a
   const uint64_t L = r1 - r0;
   a.resident = L >= sh.units;
   a.nent = a.resident ? sh.units : (uint32_t)L;
+  a.u0 = a.resident ? 0u : (uint32_t)(r0 % sh.units);
   const uint32_t nq = a.nent * XPU;
   a.xs.limbs = area;
   a.xs.sb = reinterpret_cast<const float *>(area + (size_t)NT * nq * 1024);
@@ -305,8 +358,11 @@ __host__ __device__ constexpr size_t x_area_bytes(uint32_t nt, uint32_t batch, u
   return (size_t)nt * nent * xpu * 1024 + 2 * (size_t)batch * nent * xpu * 16;
 }
 
+// Unit of entry e: a range shorter than a group spans at most two groups, so
+// the units run u0, u0 + 1, ... and wrap once.
 __device__ __forceinline__ uint32_t entry_unit(const Shape &sh, const XArea &a, uint64_t r0, uint32_t e) {
-  return a.resident ? e : (uint32_t)((r0 + e) % sh.units);
+  const uint32_t u = a.u0 + e;
+  return u >= sh.units ? u - sh.units : u;
 }
 
 __device__ __forceinline__ b200_xq_t slot_view(const KP &p, const XArea &a, uint32_t k) {
@@ -327,105 +383,119 @@ __device__ __forceinline__ float norm_scale(const KP &p, uint32_t b, int lane) {
   const uint32_t nb = p.n_embd / 32;
   const double *s = p.ssq + (size_t)b * nb;
   double acc = 0.0;
-  for (uint32_t i = lane; i < nb; i += 32) acc = __dadd_rn(acc, __ldcg(s + i));
+  for (uint32_t i0 = lane; i0 < nb; i0 += 8 * 32) {
+    double v[8];
+#pragma unroll
+    for (int m = 0; m < 8; m++) v[m] = i0 + 32 * m < nb ? __ldcg(s + i0 + 32 * m) : 0.0;
+#pragma unroll
+    for (int m = 0; m < 8; m++)
+      if (i0 + 32 * m < nb) acc = __dadd_rn(acc, v[m]);
+  }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) acc = __dadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
   const float ms = (float)__ddiv_rn(acc, (double)p.n_embd);
   return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, p.eps)));
 }
 
+// 16-byte asynchronous global -> shared copy (L2 only, no registers held).
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n cp.async.wait_all;" ::: "memory");
+}
+
 // Normed input: the unscaled quantised x * gamma (xqn) of the entries' units
-// with their block scales multiplied by the norm scale.
+// with their block scales multiplied by the norm scale. The digits and the
+// scales go to shared memory by asynchronous copies while warp b adds vector
+// b's block sums of squares; the scales are then multiplied in place.
 template <int NT, int XPU, int CONS>
-__device__ void stage_normq(const KP &p, const Shape &sh, const XArea &a, uint64_t r0, int c, int lane, int ctid,
-                            int nthr, float *scales) {
-  if (c == 0)
-    for (uint32_t b = 0; b < p.batch; b++) {
-      const float s = norm_scale(p, b, lane);
-      if (lane == 0) scales[b] = s;
-    }
+__device__ __noinline__ void stage_normq(const KP &p, const Shape &sh, const XArea &a, uint64_t r0, int c, int lane,
+                                         int ctid, int nthr, float *scales) {
   const uint32_t nq = a.nent * XPU, per = NT * XPU * 64;  // uint4 per entry (digits)
   uint4 *dl = reinterpret_cast<uint4 *>(const_cast<uint8_t *>(a.xs.limbs));
   const uint4 *sl = reinterpret_cast<const uint4 *>(p.xqn.limbs);
   for (uint32_t i = ctid; i < a.nent * per; i += nthr) {
     const uint32_t e = i / per, r = i % per, nt = r / (XPU * 64), o = r % (XPU * 64);
-    const uint32_t u = entry_unit(sh, a, r0, e);
-    dl[(((size_t)nt * nq + (size_t)e * XPU) * 1024) / 16 + o] =
-        __ldcg(sl + (((size_t)nt * p.xqn.quads + (size_t)u * XPU) * 1024) / 16 + o);
+    cp_async16(dl + (((size_t)nt * nq + (size_t)e * XPU) * 1024) / 16 + o,
+               sl + (((size_t)nt * p.xqn.quads + (size_t)entry_unit(sh, a, r0, e) * XPU) * 1024) / 16 + o);
   }
-  cbar(nthr);  // the scales are in shared memory
   float4 *db = reinterpret_cast<float4 *>(const_cast<float *>(a.xs.sb));
   float4 *dx = reinterpret_cast<float4 *>(const_cast<float *>(a.xs.sx));
   const float4 *sb = reinterpret_cast<const float4 *>(p.xqn.sb);
   const float4 *sx = reinterpret_cast<const float4 *>(p.xqn.sx);
-  for (uint32_t i = ctid; i < a.nent * p.batch * XPU; i += nthr) {
+  const uint32_t nsc = a.nent * p.batch * XPU;
+  for (uint32_t i = ctid; i < nsc; i += nthr) {
     const uint32_t e = i / (p.batch * XPU), r = i % (p.batch * XPU), vec = r / XPU, q = r % XPU;
-    const uint32_t u = entry_unit(sh, a, r0, e);
-    const size_t s = (size_t)vec * p.xqn.quads + (size_t)u * XPU + q, d = (size_t)vec * nq + (size_t)e * XPU + q;
+    const size_t src = (size_t)vec * p.xqn.quads + (size_t)entry_unit(sh, a, r0, e) * XPU + q;
+    const size_t d = (size_t)vec * nq + (size_t)e * XPU + q;
+    cp_async16(db + d, sb + src);
+    cp_async16(dx + d, sx + src);
+  }
+  for (uint32_t b = c; b < p.batch; b += CONS) {  // warp b: vector b's scale
+    const float sc = norm_scale(p, b, lane);
+    if (lane == 0) scales[b] = sc;
+  }
+  cp_async_wait_all();
+  cbar(nthr);  // the copies and the norm scales are in shared memory
+  for (uint32_t i = ctid; i < nsc; i += nthr) {
+    const uint32_t e = i / (p.batch * XPU), r = i % (p.batch * XPU), vec = r / XPU, q = r % XPU;
+    const size_t d = (size_t)vec * nq + (size_t)e * XPU + q;
     const float f = scales[vec];
-    float4 b4 = __ldcg(sb + s), x4 = __ldcg(sx + s);
-    b4.x = __fmul_rn(b4.x, f), b4.y = __fmul_rn(b4.y, f), b4.z = __fmul_rn(b4.z, f), b4.w = __fmul_rn(b4.w, f);
-    x4.x = __fmul_rn(x4.x, f), x4.y = __fmul_rn(x4.y, f), x4.z = __fmul_rn(x4.z, f), x4.w = __fmul_rn(x4.w, f);
-    db[d] = b4;
-    dx[d] = x4;
+    float4 bv = db[d], xv = dx[d];
+    bv.x = __fmul_rn(bv.x, f), bv.y = __fmul_rn(bv.y, f), bv.z = __fmul_rn(bv.z, f), bv.w = __fmul_rn(bv.w, f);
+    xv.x = __fmul_rn(xv.x, f), xv.y = __fmul_rn(xv.y, f), xv.z = __fmul_rn(xv.z, f), xv.w = __fmul_rn(xv.w, f);
+    db[d] = bv;
+    dx[d] = xv;
   }
 }
 
 // o's input: the attention output of the heads in the entries' units,
-// merged from the attention CTAs' partials (fixed order) and quantised.
-// One warp per (vector, head): lane l holds dims 4l..4l+3; the 128 values
-// go through the warp's shared scratch to quantise lane = element.
+// merged from the attention CTAs' partials (slot order) and quantised. One
+// warp per (vector, head); the slots go in chunks of 16 with every load of
+// a chunk in flight at once (lane s < 16 holds slot s's statistics, lane l
+// the dims 4l..4l+3 of every slot), combined with running-max rescaling
+// across chunks. The 128 values go through the warp's shared scratch to
+// quantise with lane = element.
 template <int NT, int XPU, int CONS>
-__device__ void stage_att(const KP &p, const Shape &sh, const XArea &a, uint64_t r0, int c, int lane,
-                          float *scratch) {
+__device__ __noinline__ void stage_att(const KP &p, const Shape &sh, const XArea &a, uint64_t r0, int c, int lane,
+                                       float *scratch) {
   b200_xq_t v = slot_view(p, a, sh.k);
   float *ws = scratch + c * kHD;
   const uint32_t heads = a.nent * XPU, ph = p.per_head;
+  constexpr uint32_t CH = 16;
   for (uint32_t j = c; j < heads * p.batch; j += CONS) {
     const uint32_t b = j / heads, eh = j % heads, e = eh / XPU;
     const uint32_t hh = entry_unit(sh, a, r0, e) * XPU + eh % XPU;  // head of this rank
-    const float *base = p.apart + (((size_t)b * p.h + hh) * ph) * (kHD + 2);
-    float M = -INFINITY;
-    for (uint32_t s0 = 0; s0 < ph; s0 += 8) {
-      float mv[8], lv[8];
+    const float *base = p.apart + (((size_t)b * p.h + hh) * ph) * kAS;
+    float M = -INFINITY, L = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
+    for (uint32_t s0 = 0; s0 < ph; s0 += CH) {
+      const uint32_t cnt = min(CH, ph - s0);
+      float2 ml = make_float2(-INFINITY, 0.0f);
+      if ((uint32_t)lane < cnt) ml = __ldcg(reinterpret_cast<const float2 *>(base + (size_t)(s0 + lane) * kAS + kHD));
+      float4 ov[CH];
 #pragma unroll
-      for (int m = 0; m < 8; m++) {
-        mv[m] = s0 + m < ph ? __ldcg(base + (size_t)(s0 + m) * (kHD + 2) + kHD) : -INFINITY;
-        lv[m] = s0 + m < ph ? __ldcg(base + (size_t)(s0 + m) * (kHD + 2) + kHD + 1) : 0.0f;
+      for (uint32_t m = 0; m < CH; m++)
+        ov[m] = m < cnt ? __ldcg(reinterpret_cast<const float4 *>(base + (size_t)(s0 + m) * kAS) + lane)
+                        : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float mc = warp_max(ml.y > 0.0f ? ml.x : -INFINITY);
+      const float m_new = fmaxf(M, mc);
+      const float alpha = M == -INFINITY ? 0.0f : expf(M - m_new);
+      const float w = ml.y > 0.0f ? expf(ml.x - m_new) : 0.0f;
+      L = fmaf(L, alpha, warp_sum(ml.y * w));
+#pragma unroll
+      for (int q = 0; q < 4; q++) o[q] *= alpha;
+#pragma unroll
+      for (uint32_t m = 0; m < CH; m++) {
+        const float wm = __shfl_sync(0xffffffffu, w, m);
+        o[0] = fmaf(ov[m].x, wm, o[0]), o[1] = fmaf(ov[m].y, wm, o[1]);
+        o[2] = fmaf(ov[m].z, wm, o[2]), o[3] = fmaf(ov[m].w, wm, o[3]);
       }
-#pragma unroll
-      for (int m = 0; m < 8; m++)
-        if (lv[m] > 0.0f) M = fmaxf(M, mv[m]);
-    }
-    float L = 0.f, o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
-    for (uint32_t s0 = 0; s0 < ph; s0 += 8) {
-      float mv[8], lv[8];
-      float4 ov[8];
-#pragma unroll
-      for (int m = 0; m < 8; m++) {
-        const float *sl = base + (size_t)(s0 + m) * (kHD + 2);
-        const bool in = s0 + m < ph;
-        mv[m] = in ? __ldcg(sl + kHD) : -INFINITY;
-        lv[m] = in ? __ldcg(sl + kHD + 1) : 0.0f;
-        if (in) {
-          ov[m].x = __ldcg(sl + 4 * lane), ov[m].y = __ldcg(sl + 4 * lane + 1);
-          ov[m].z = __ldcg(sl + 4 * lane + 2), ov[m].w = __ldcg(sl + 4 * lane + 3);
-        } else {
-          ov[m] = make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-      }
-#pragma unroll
-      for (int m = 0; m < 8; m++) {
-        if (lv[m] > 0.0f) {
-          const float w = expf(mv[m] - M);
-          L = fmaf(lv[m], w, L);
-          o0 = fmaf(ov[m].x, w, o0), o1 = fmaf(ov[m].y, w, o1);
-          o2 = fmaf(ov[m].z, w, o2), o3 = fmaf(ov[m].w, w, o3);
-        }
-      }
+      M = m_new;
     }
     __syncwarp();
-    ws[4 * lane] = o0 / L, ws[4 * lane + 1] = o1 / L, ws[4 * lane + 2] = o2 / L, ws[4 * lane + 3] = o3 / L;
+#pragma unroll
+    for (int q = 0; q < 4; q++) ws[4 * lane + q] = o[q] / L;
     __syncwarp();
     // head hh is x blocks 4 hh .. 4 hh + 3; in the entry they are blocks
     // 4 (e XPU + eh % XPU) .. of the slot
@@ -437,23 +507,61 @@ __device__ void stage_att(const KP &p, const Shape &sh, const XArea &a, uint64_t
 
 // down's input: h = silu(gate) * up for the entries' units, from the
 // gate|up partial sums (gate|up tile t holds gate rows 8t.. then the
-// matching up rows), quantised. One warp per (vector, 32-element block).
+// matching up rows), quantised. One warp per (vector, 128 outputs): lane l
+// takes outputs 4l..4l+3 -- 4 consecutive gate rows and the 4 up rows 8
+// further, one 16-byte load each per split, all splits' loads in flight --
+// and the values go through the warp's shared scratch to quantise with
+// lane = element.
 template <int NT, int XPU, int CONS>
-__device__ void stage_silu(const KP &p, const Shape &sh, const XArea &a, uint64_t r0, int c, int lane) {
+__device__ __noinline__ void stage_silu(const KP &p, const Shape &sh, const XArea &a, uint64_t r0, int c, int lane,
+                                        float *scratch) {
   b200_xq_t v = slot_view(p, a, sh.k);
+  float *ws = scratch + c * kHD;
   const Shape &gu = p.sh[M_GU];
   const float *part = p.part[0];
-  const uint32_t bpe = XPU * 4, nb = a.nent * bpe;
-  for (uint32_t j = c; j < nb * p.batch; j += CONS) {
-    const uint32_t b = j / nb, jb = j % nb, e = jb / bpe;
-    const uint32_t o = (entry_unit(sh, a, r0, e) * bpe + jb % bpe) * 32 + lane;  // output of the gate/up pair
-    float h = 0.0f;
-    if (o < sh.k) {
+  const uint32_t nch = a.nent * XPU, ni = nch * p.batch;  // 128-output chunks
+  const size_t stride = (size_t)p.batch * gu.npad;
+  constexpr int CH = 4;
+  for (uint32_t it = c; it < ni; it += CONS) {
+    const uint32_t b = it / nch, ch = it % nch, e = ch / XPU;
+    const uint32_t o = (entry_unit(sh, a, r0, e) * XPU + ch % XPU) * 128 + 4 * lane;
+    float4 h4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (o < sh.k) {  // k % 32 == 0: the lane's 4 outputs are all in or all out
       const uint32_t grow = (o / 8) * 16 + o % 8;
-      const float gate = row_sum(part, gu, p.batch, b, grow), up = row_sum(part, gu, p.batch, b, grow + 8);
-      h = __fmul_rn(__fdiv_rn(gate, __fadd_rn(1.0f, expf(-gate))), up);  // llama.c:774-781
+      const uint32_t nseg = s_nseg[gu.tab + grow / (16u * CONS)];
+      const float4 *q = reinterpret_cast<const float4 *>(part + (size_t)b * gu.npad + grow);
+      const size_t st4 = stride / 4;
+      float4 gs = make_float4(0.f, 0.f, 0.f, 0.f), us = gs;
+      for (uint32_t i0 = 0; i0 < nseg; i0 += CH) {
+        float4 gv[CH], uv[CH];
+#pragma unroll
+        for (int i = 0; i < CH; i++) {
+          const bool in = i0 + i < nseg;
+          gv[i] = in ? __ldcg(q + (i0 + i) * st4) : make_float4(0.f, 0.f, 0.f, 0.f);
+          uv[i] = in ? __ldcg(q + (i0 + i) * st4 + 2) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int i = 0; i < CH; i++)
+          if (i0 + i < nseg) {
+            if (i0 + i == 0) {
+              gs = gv[i], us = uv[i];
+            } else {
+              gs.x += gv[i].x, gs.y += gv[i].y, gs.z += gv[i].z, gs.w += gv[i].w;
+              us.x += uv[i].x, us.y += uv[i].y, us.z += uv[i].z, us.w += uv[i].w;
+            }
+          }
+      }
+      // llama.c:774-781
+      h4.x = __fmul_rn(__fdiv_rn(gs.x, __fadd_rn(1.0f, expf(-gs.x))), us.x);
+      h4.y = __fmul_rn(__fdiv_rn(gs.y, __fadd_rn(1.0f, expf(-gs.y))), us.y);
+      h4.z = __fmul_rn(__fdiv_rn(gs.z, __fadd_rn(1.0f, expf(-gs.z))), us.z);
+      h4.w = __fmul_rn(__fdiv_rn(gs.w, __fadd_rn(1.0f, expf(-gs.w))), us.w);
     }
-    xq_store_block(v, b, jb, h);
+    __syncwarp();
+    *reinterpret_cast<float4 *>(ws + 4 * lane) = h4;
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < 4; q++) xq_store_block(v, b, ch * 4 + q, ws[32 * q + lane]);
   }
 }
 
@@ -466,22 +574,23 @@ enum { X_NORMQ = 0, X_ATT = 1, X_SILU = 2 };
 // wait that ran out; the loop structure is the same either way, so every
 // thread reaches the same barriers.
 template <uint32_t T, int NT, int CONS>
-__device__ void consume(const KP &p, const Shape &sh, int xsrc, float *part, uint8_t *ring, uint64_t *full,
+__device__ void consume(const KP &p, int k, int xsrc, float *part, uint8_t *ring, uint64_t *full,
                         uint64_t *empty, uint32_t &seq, uint8_t *area, float *scratch, float *scales, int c,
                         int lane, int ctid, int nthr, volatile int *failed) {
   using Un = Unit<T>;
   constexpr int U = Un::U, XPU = Un::XPU;
   constexpr uint32_t GQ = CONS * Un::QB, GS = CONS * Un::SB;
+  const Shape &sh = p.sh[k];
   uint64_t r0, r1;
   phase_range(sh, r0, r1);
   if (r0 >= r1) return;
   const XArea a = x_area<NT, XPU>(p, sh, area, r0, r1);
   if (xsrc == X_NORMQ)
-    stage_normq<NT, XPU, CONS>(p, sh, a, r0, c, lane, ctid, nthr, scales);
+    stage_normq<NT, XPU, CONS>(s_kp, s_kp.sh[k], a, r0, c, lane, ctid, nthr, scales);
   else if (xsrc == X_ATT)
-    stage_att<NT, XPU, CONS>(p, sh, a, r0, c, lane, scratch);
+    stage_att<NT, XPU, CONS>(s_kp, s_kp.sh[k], a, r0, c, lane, scratch);
   else
-    stage_silu<NT, XPU, CONS>(p, sh, a, r0, c, lane);
+    stage_silu<NT, XPU, CONS>(s_kp, s_kp.sh[k], a, r0, c, lane, scratch);
   cbar(nthr);
   const uint64_t total = (uint64_t)sh.ngroups * sh.units;
   const uint32_t r = lane >> 2, vsel = (lane & 3) >> 1;
@@ -561,12 +670,14 @@ __device__ __forceinline__ void finish_block(const KP &p, uint32_t b, uint32_t b
 // One GPU: x += the o or down GEMV's row sums (the residual adds of
 // llama.c:747-749, 793-795); warp per 32-row block.
 template <int CONS>
-__device__ void reduce_rows(const KP &p, const Shape &sh, const float *gamma, int c, int lane) {
+__device__ __noinline__ void reduce_rows(const KP &p, const Shape &sh, const float *gamma, int c, int lane) {
   const uint32_t nb = p.n_embd / 32;
   for (uint32_t wb = blockIdx.x * CONS + c; wb < p.batch * nb; wb += gridDim.x * CONS) {
     const uint32_t b = wb / nb, blk = wb % nb, row = blk * 32 + lane;
-    const float v = __fadd_rn(__ldcg(p.x + (size_t)b * p.n_embd + row), row_sum(p.part[1], sh, p.batch, b, row));
-    finish_block(p, b, blk, v, gamma, lane);
+    float pv[16];
+    const RowRef rr = row_load<16, CONS>(p.part[1], sh, p.batch, b, row, pv);
+    const float xv = __ldcg(p.x + (size_t)b * p.n_embd + row);
+    finish_block(p, b, blk, __fadd_rn(xv, row_finish<16>(rr, pv, p.batch, sh.npad)), gamma, lane);
   }
 }
 
@@ -582,12 +693,12 @@ __device__ __forceinline__ float *land_rows(const KP &p, uint32_t r, uint32_t pa
 // CTA index of every rank handled the same blocks), and adds the ranks' rows
 // in rank order to x.
 template <int CONS>
-__device__ bool exchange_rows(const KP &p, const Shape &sh, const float *gamma, uint64_t e, int c, int lane, int ctid,
+__device__ __noinline__ bool exchange_rows(const KP &p, const Shape &sh, const float *gamma, uint64_t e, int c, int lane, int ctid,
                               int nthr, volatile int *sflag) {
   const uint32_t nb = p.n_embd / 32, parity = (uint32_t)(e & 1u);
   for (uint32_t wb = blockIdx.x * CONS + c; wb < p.batch * nb; wb += gridDim.x * CONS) {
     const uint32_t b = wb / nb, blk = wb % nb, row = blk * 32 + lane;
-    const float v = row_sum(p.part[1], sh, p.batch, b, row);
+    const float v = row_sum<16, CONS>(p.part[1], sh, p.batch, b, row);
     for (uint32_t q = 0; q < p.nranks; q++) land_rows(p, q, parity, p.rank)[(size_t)b * p.n_embd + row] = v;
   }
   cbar(nthr);  // this CTA's stores are issued
@@ -635,44 +746,107 @@ __device__ bool exchange_rows(const KP &p, const Shape &sh, const float *gamma, 
 
 // ---- attention ---------------------------------------------------------------------------
 
-// RoPE (pai_ref_rope_f32's pairs (i, i + 64)) of the 4 dims 4l..4l+3 a lane
-// holds: its partner dims sit in lane l ^ 16.
-__device__ __forceinline__ void rope4(float (&x)[4], const KP &p, uint32_t pos, int lane) {
-  float y[4];
-#pragma unroll
-  for (int e = 0; e < 4; e++) y[e] = __shfl_xor_sync(0xffffffffu, x[e], 16);
-  const uint32_t r2 = kHD / 2;
-#pragma unroll
-  for (int e = 0; e < 4; e++) {
-    const uint32_t i = (4 * lane + e) % r2;
-    const float c = __ldg(p.cos_t + (size_t)pos * r2 + i), s = __ldg(p.sin_t + (size_t)pos * r2 + i);
-    float o0, o1;
-    if (lane < 16) {
-      rope_pair(x[e], y[e], c, s, o0, o1);
-      x[e] = o0;
-    } else {
-      rope_pair(y[e], x[e], c, s, o0, o1);
-      x[e] = o1;
-    }
-  }
-}
-
 // Attention over layer `layer`'s cache (the last row of pai_ref_attention_f32,
 // cpu/reference/ref_ops.c:307-349, on the cache contents: scores scaled by
 // 1/sqrtf(hd) after the dot, softmax with the maximum subtracted, sum of
-// p_i v_i). Not inlined: its arrays keep their own register allocation.
+// p_i v_i), after RoPE (pai_ref_rope_f32's pairs (i, i + 64)) of q and k and
+// the fp16 append of k and v at the position (llama.c:700-731).
+//
+// Work item (sequence b, kv head, slot j): positions [j cpos, (j+1) cpos),
+// slots = per_head CTAs per (sequence, kv head). The CTA first adds the
+// q|k|v partial sums of its G + 2 heads' rows into shared memory (all loads
+// in flight), rotates q and k there, and -- the CTA whose range holds the
+// position -- appends k and v to the cache. Warp w takes the 8-position
+// groups p0 + 8 w + 8 CONS t: lane 4i + r dots quarter r (32 dims) of
+// position i's K row with the G q heads and two shuffles add the quarters;
+// softmax statistics over the 8 positions take three shuffles; the V rows of
+// the 8 positions are loaded at once with lane l on dims 4l..4l+3. The warps
+// are merged in shared memory into one partial (o, max, sum) per head and
+// slot. Not inlined: its arrays keep their own register allocation.
+constexpr uint32_t kQP = 36;  // shared-memory q: quarter rows of 32 dims padded to 36 (banks)
 template <int G, int CONS>
 __device__ __noinline__ void attention(const KP &p, uint32_t layer, int warp, int lane, int ctid, int nthr,
                                        float *sm) {
   const Shape &sq = p.sh[M_QKV];
   const float *part = p.part[0];
-  const uint32_t npos = (uint32_t)__ldcg(p.pos) + 1u, pos = npos - 1, ph = p.per_head;
-  const uint32_t cpos = max(32u, ((npos + ph - 1) / ph + 31u) / 32u * 32u);  // positions per CTA
+  const uint32_t npos = s_npos, pos = npos - 1, ph = p.per_head;
+  const uint32_t cpos = ((npos + ph - 1) / ph + 7u) / 8u * 8u;  // positions per slot
   const uint32_t nitems = p.batch * p.hk * ph;
   const size_t lofs = (size_t)layer * p.layer_stride;
+  constexpr uint32_t R = (G + 2) * kHD;  // rows of q (G heads), k, v
+  // shared memory: q [G][4][kQP] | k, v [2][kHD] | the warps' partials [CONS][G][kAS]
+  float *qs = sm, *kvs = sm + G * 4 * kQP, *wpart = kvs + 2 * kHD;
+  const int r4 = lane & 3, i8 = lane >> 2;  // quarter, position in the group of 8
   for (uint32_t item = blockIdx.x; item < nitems; item += gridDim.x) {
     const uint32_t b = item / (p.hk * ph), kvh = (item / ph) % p.hk, j = item % ph, h0 = kvh * G;
     const uint32_t p0 = j * cpos, p1 = min(npos, p0 + cpos);
+    if (p0 >= p1) {  // no positions (CTA-uniform): the slot says so
+      for (uint32_t i = ctid; i < G * kAS; i += nthr) {
+        const uint32_t g = i / kAS, d = i % kAS;
+        p.apart[(((size_t)b * p.h + h0 + g) * p.per_head + j) * kAS + d] = d == kHD ? -INFINITY : 0.0f;
+      }
+      continue;
+    }
+    const uint32_t nw = min((uint32_t)CONS, (p1 - p0 + 7) / 8);  // warps with positions
+    // RoPE table entries of the first pair this thread rotates below (loaded with the rows)
+    constexpr uint32_t NP = (G + 1) * (kHD / 2);  // pairs of the G q heads and k
+    float rc = 0.f, rs = 0.f;
+    if ((uint32_t)ctid < NP) {
+      const uint32_t d = (uint32_t)ctid % (kHD / 2);
+      rc = __ldg(p.cos_t + (size_t)pos * (kHD / 2) + d), rs = __ldg(p.sin_t + (size_t)pos * (kHD / 2) + d);
+    }
+    // q | k | v rows of this kv head from the q|k|v partial sums
+    for (uint32_t i0 = ctid; i0 < R; i0 += 2 * nthr) {
+      float va[8], vb[8];
+      const uint32_t i1 = min(i0 + nthr, R - 1);
+      const uint32_t rowa = i0 < G * kHD ? h0 * kHD + i0
+                                         : (i0 < (G + 1) * kHD ? (p.h + kvh) * kHD + i0 - G * kHD
+                                                               : (p.h + p.hk + kvh) * kHD + i0 - (G + 1) * kHD);
+      const uint32_t rowb = i1 < G * kHD ? h0 * kHD + i1
+                                         : (i1 < (G + 1) * kHD ? (p.h + kvh) * kHD + i1 - G * kHD
+                                                               : (p.h + p.hk + kvh) * kHD + i1 - (G + 1) * kHD);
+      const RowRef ra = row_load<8, CONS>(part, sq, p.batch, b, rowa, va);
+      const RowRef rb = row_load<8, CONS>(part, sq, p.batch, b, rowb, vb);
+      const float xa = row_finish<8>(ra, va, p.batch, sq.npad);
+      const float xb = row_finish<8>(rb, vb, p.batch, sq.npad);
+      // q rows go to the padded quarter layout, k and v rows after them
+      if (i0 < G * kHD) qs[(i0 / kHD) * 4 * kQP + ((i0 % kHD) / 32) * kQP + i0 % 32] = xa;
+      else kvs[i0 - G * kHD] = xa;
+      if (i0 + nthr < R) {
+        if (i1 < G * kHD) qs[(i1 / kHD) * 4 * kQP + ((i1 % kHD) / 32) * kQP + i1 % 32] = xb;
+        else kvs[i1 - G * kHD] = xb;
+      }
+    }
+    cbar(nthr);
+    // RoPE of the G q heads and k at the position: pair (d, d + 64)
+    for (uint32_t i = ctid; i < NP; i += nthr) {
+      const uint32_t hh = i / (kHD / 2), d = i % (kHD / 2);
+      float c = rc, sn = rs;
+      if (i != (uint32_t)ctid)
+        c = __ldg(p.cos_t + (size_t)pos * (kHD / 2) + d), sn = __ldg(p.sin_t + (size_t)pos * (kHD / 2) + d);
+      float *lo, *hi;
+      if (hh < (uint32_t)G) {
+        lo = qs + hh * 4 * kQP + (d / 32) * kQP + d % 32;
+        hi = qs + hh * 4 * kQP + ((d + 64) / 32) * kQP + d % 32;
+      } else {
+        lo = kvs + d;
+        hi = kvs + d + 64;
+      }
+      float o0, o1;
+      rope_pair(*lo, *hi, c, sn, o0, o1);
+      *lo = o0;
+      *hi = o1;
+    }
+    cbar(nthr);
+    const size_t kvbase = lofs + (size_t)b * p.seq_stride + (size_t)kvh * p.cap * kHD;
+    if (p0 <= pos && pos < p1) {  // CTA-uniform: append k and v (fp16) at the position
+      for (uint32_t i = ctid; i < kHD; i += nthr) {
+        const uint32_t kv = i / (kHD / 2), d = 2 * (i % (kHD / 2));
+        *reinterpret_cast<__half2 *>((kv ? p.vc : p.kc) + kvbase + (size_t)pos * kHD + d) =
+            __floats2half2_rn(kvs[kv * kHD + d], kvs[kv * kHD + d + 1]);
+      }
+      cbar(nthr);  // the appended row is read back below (from L2, by other threads)
+    }
     float m[G], l[G], o[G][4];
 #pragma unroll
     for (int g = 0; g < G; g++) {
@@ -680,128 +854,97 @@ __device__ __noinline__ void attention(const KP &p, uint32_t layer, int warp, in
 #pragma unroll
       for (int e = 0; e < 4; e++) o[g][e] = 0.f;
     }
-    if (p0 + 32 * warp < p1) {
-      // q of the G heads (the partial sums of their rows), rotated at the position
-      float q[G][4];
+    for (uint32_t c0 = p0 + 8 * warp; c0 < p1; c0 += 8 * CONS) {
+      const uint32_t cnt = min(8u, p1 - c0);
+      const bool mine = (uint32_t)i8 < cnt;
+      // quarter r4 of position c0 + i8's K row (32 fp16 = 4 x 16 B)
+      const uint4 *kr =
+          reinterpret_cast<const uint4 *>(p.kc + kvbase + (size_t)(c0 + (mine ? i8 : 0)) * kHD + 32 * r4);
+      uint4 kw[4];
 #pragma unroll
-      for (int g = 0; g < G; g++) {
+      for (int t = 0; t < 4; t++) kw[t] = __ldcg(kr + t);
+      // the V rows of the 8 positions, lane l on dims 4l..4l+3 (loaded now, used below)
+      const uint2 *vr = reinterpret_cast<const uint2 *>(p.vc + kvbase + (size_t)c0 * kHD) + lane;
+      uint2 vw[8];
 #pragma unroll
-        for (int e = 0; e < 4; e++) q[g][e] = row_sum(part, sq, p.batch, b, (h0 + g) * kHD + 4 * lane + e);
-        rope4(q[g], p, pos, lane);
-      }
-      const size_t kvbase = lofs + (size_t)b * p.seq_stride + (size_t)kvh * p.cap * kHD;
-      for (uint32_t c0 = p0 + 32 * warp; c0 < p1; c0 += 32 * CONS) {
-        const uint32_t cnt = min(32u, p1 - c0);
-        if (c0 <= pos && pos < c0 + cnt) {
-          // this chunk holds the position: append the rotated k and v (fp16);
-          // lane l writes dims 4l..4l+3, the words it reads back below
-          float kk[4], vv[4];
+      for (int t = 0; t < 8; t++) vw[t] = (uint32_t)t < cnt ? __ldcg(vr + (size_t)t * (kHD / 4)) : make_uint2(0u, 0u);
+      float sc[G];
 #pragma unroll
-          for (int e = 0; e < 4; e++) {
-            kk[e] = row_sum(part, sq, p.batch, b, (p.h + kvh) * kHD + 4 * lane + e);
-            vv[e] = row_sum(part, sq, p.batch, b, (p.h + p.hk + kvh) * kHD + 4 * lane + e);
-          }
-          rope4(kk, p, pos, lane);
-          const size_t at = kvbase + (size_t)pos * kHD + 4 * lane;
-          __half2 k01 = __floats2half2_rn(kk[0], kk[1]), k23 = __floats2half2_rn(kk[2], kk[3]);
-          __half2 v01 = __floats2half2_rn(vv[0], vv[1]), v23 = __floats2half2_rn(vv[2], vv[3]);
-          uint2 kw, vw;
-          kw.x = *reinterpret_cast<uint32_t *>(&k01), kw.y = *reinterpret_cast<uint32_t *>(&k23);
-          vw.x = *reinterpret_cast<uint32_t *>(&v01), vw.y = *reinterpret_cast<uint32_t *>(&v23);
-          *reinterpret_cast<uint2 *>(p.kc + at) = kw;
-          *reinterpret_cast<uint2 *>(p.vc + at) = vw;
-        }
-        // scores of the chunk: lane i keeps position c0 + i
-        float s_mine[G];
+      for (int g = 0; g < G; g++) sc[g] = 0.f;
 #pragma unroll
-        for (int g = 0; g < G; g++) s_mine[g] = -INFINITY;
-        for (uint32_t i0 = 0; i0 < cnt; i0 += 4) {
-          float d[4][G];
-#pragma unroll
-          for (int u = 0; u < 4; u++) {
-            float2 k01 = make_float2(0.f, 0.f), k23 = k01;
-            if (i0 + u < cnt) {
-              const uint2 raw =
-                  __ldcg(reinterpret_cast<const uint2 *>(p.kc + kvbase + (size_t)(c0 + i0 + u) * kHD + 4 * lane));
-              k01 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
-              k23 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
-            }
-#pragma unroll
-            for (int g = 0; g < G; g++) {
-              float sv = q[g][0] * k01.x;
-              sv = fmaf(q[g][1], k01.y, sv);
-              sv = fmaf(q[g][2], k23.x, sv);
-              sv = fmaf(q[g][3], k23.y, sv);
-              d[u][g] = sv;
-            }
-          }
-#pragma unroll
-          for (int off = 16; off > 0; off >>= 1)
-#pragma unroll
-            for (int u = 0; u < 4; u++)
-#pragma unroll
-              for (int g = 0; g < G; g++) d[u][g] += __shfl_xor_sync(0xffffffffu, d[u][g], off);
-#pragma unroll
-          for (int u = 0; u < 4; u++)
-            if ((uint32_t)lane == i0 + u && i0 + u < cnt) {
-#pragma unroll
-              for (int g = 0; g < G; g++) s_mine[g] = d[u][g] * p.inv_scale;
-            }
-        }
-        // running softmax statistics
-        float e_mine[G];
+      for (int t = 0; t < 4; t++) {
+        const float2 k0 = __half22float2(*reinterpret_cast<const __half2 *>(&kw[t].x));
+        const float2 k1 = __half22float2(*reinterpret_cast<const __half2 *>(&kw[t].y));
+        const float2 k2 = __half22float2(*reinterpret_cast<const __half2 *>(&kw[t].z));
+        const float2 k3 = __half22float2(*reinterpret_cast<const __half2 *>(&kw[t].w));
 #pragma unroll
         for (int g = 0; g < G; g++) {
-          const float m_new = fmaxf(m[g], warp_max(s_mine[g]));
-          const float alpha = m[g] == -INFINITY ? 0.0f : expf(m[g] - m_new);
-          e_mine[g] = (uint32_t)lane < cnt ? expf(s_mine[g] - m_new) : 0.0f;
-          l[g] = fmaf(l[g], alpha, warp_sum(e_mine[g]));
-          m[g] = m_new;
-#pragma unroll
-          for (int e = 0; e < 4; e++) o[g][e] *= alpha;
+          const float *qq = qs + g * 4 * kQP + r4 * kQP + 8 * t;
+          const float4 qa = *reinterpret_cast<const float4 *>(qq), qb = *reinterpret_cast<const float4 *>(qq + 4);
+          float a = sc[g];
+          a = fmaf(qa.x, k0.x, a), a = fmaf(qa.y, k0.y, a), a = fmaf(qa.z, k1.x, a), a = fmaf(qa.w, k1.y, a);
+          a = fmaf(qb.x, k2.x, a), a = fmaf(qb.y, k2.y, a), a = fmaf(qb.z, k3.x, a), a = fmaf(qb.w, k3.y, a);
+          sc[g] = a;
         }
-        // exp-weighted V: position i's weight broadcast from lane i
-        for (uint32_t i = 0; i < cnt; i++) {
-          const uint2 raw = __ldcg(reinterpret_cast<const uint2 *>(p.vc + kvbase + (size_t)(c0 + i) * kHD + 4 * lane));
-          const float2 v01 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
-          const float2 v23 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
+      }
+      // quarters added (lanes 4i..4i+3), then softmax over the 8 positions
+      float ew[G];
 #pragma unroll
-          for (int g = 0; g < G; g++) {
-            const float w = __shfl_sync(0xffffffffu, e_mine[g], i);
-            o[g][0] = fmaf(w, v01.x, o[g][0]);
-            o[g][1] = fmaf(w, v01.y, o[g][1]);
-            o[g][2] = fmaf(w, v23.x, o[g][2]);
-            o[g][3] = fmaf(w, v23.y, o[g][3]);
-          }
+      for (int g = 0; g < G; g++) {
+        float sv = sc[g] + __shfl_xor_sync(0xffffffffu, sc[g], 1);
+        sv += __shfl_xor_sync(0xffffffffu, sv, 2);
+        sv = mine ? sv * p.inv_scale : -INFINITY;
+        float mx = fmaxf(sv, __shfl_xor_sync(0xffffffffu, sv, 4));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+        const float m_new = fmaxf(m[g], mx);
+        const float alpha = m[g] == -INFINITY ? 0.0f : expf(m[g] - m_new);
+        ew[g] = mine ? expf(sv - m_new) : 0.0f;
+        float es = ew[g] + __shfl_xor_sync(0xffffffffu, ew[g], 4);
+        es += __shfl_xor_sync(0xffffffffu, es, 8);
+        es += __shfl_xor_sync(0xffffffffu, es, 16);
+        l[g] = fmaf(l[g], alpha, es);
+        m[g] = m_new;
+#pragma unroll
+        for (int e = 0; e < 4; e++) o[g][e] *= alpha;
+      }
+      // exp-weighted V: position t's weight broadcast from lane 4t
+#pragma unroll
+      for (int t = 0; t < 8; t++) {
+        const float2 v01 = __half22float2(*reinterpret_cast<const __half2 *>(&vw[t].x));
+        const float2 v23 = __half22float2(*reinterpret_cast<const __half2 *>(&vw[t].y));
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+          const float w = __shfl_sync(0xffffffffu, ew[g], 4 * t);
+          o[g][0] = fmaf(w, v01.x, o[g][0]);
+          o[g][1] = fmaf(w, v01.y, o[g][1]);
+          o[g][2] = fmaf(w, v23.x, o[g][2]);
+          o[g][3] = fmaf(w, v23.y, o[g][3]);
         }
       }
     }
-    // the CTA's warps merged in shared memory: sm[warp][g][kHD + 2]
+    // the warps with positions merged in shared memory
+    if ((uint32_t)warp < nw) {
 #pragma unroll
-    for (int g = 0; g < G; g++) {
-      float *w = sm + ((size_t)warp * G + g) * (kHD + 2);
-#pragma unroll
-      for (int e = 0; e < 4; e++) w[4 * lane + e] = o[g][e];
-      if (lane == 0) w[kHD] = m[g], w[kHD + 1] = l[g];
+      for (int g = 0; g < G; g++) {
+        float *w = wpart + ((size_t)warp * G + g) * kAS;
+        *reinterpret_cast<float4 *>(w + 4 * lane) = make_float4(o[g][0], o[g][1], o[g][2], o[g][3]);
+        if (lane == 0) w[kHD] = m[g], w[kHD + 1] = l[g];
+      }
     }
     cbar(nthr);
     for (uint32_t i = ctid; i < G * kHD; i += nthr) {
       const uint32_t g = i / kHD, dd = i % kHD;
       float M = -INFINITY;
-      for (int w = 0; w < CONS; w++) {
-        const float *ws = sm + ((size_t)w * G + g) * (kHD + 2);
-        if (ws[kHD + 1] > 0.0f) M = fmaxf(M, ws[kHD]);
-      }
+      for (uint32_t w = 0; w < nw; w++) M = fmaxf(M, wpart[((size_t)w * G + g) * kAS + kHD]);
       float L = 0.f, od = 0.f;
-      for (int w = 0; w < CONS; w++) {
-        const float *ws = sm + ((size_t)w * G + g) * (kHD + 2);
-        if (ws[kHD + 1] > 0.0f) {
-          const float wt = expf(ws[kHD] - M);
-          L = fmaf(ws[kHD + 1], wt, L);
-          od = fmaf(ws[dd], wt, od);
-        }
+      for (uint32_t w = 0; w < nw; w++) {
+        const float *ws = wpart + ((size_t)w * G + g) * kAS;
+        const float wt = expf(ws[kHD] - M);
+        L = fmaf(ws[kHD + 1], wt, L);
+        od = fmaf(ws[dd], wt, od);
       }
-      float *dst = p.apart + (((size_t)b * p.h + h0 + g) * ph + j) * (kHD + 2);
+      float *dst = p.apart + (((size_t)b * p.h + h0 + g) * p.per_head + j) * kAS;
       dst[dd] = od;
       if (dd == 0) dst[kHD] = M, dst[kHD + 1] = L;
     }
@@ -847,11 +990,10 @@ __device__ void embed(const KP &p, int c, int lane) {
 // reduce phase) with its block scales multiplied by the norm scale.
 template <int CONS>
 __device__ void final_norm(const KP &p, int c, int lane, int ctid, int nthr, float *scales) {
-  if (c == 0)
-    for (uint32_t b = 0; b < p.batch; b++) {
-      const float s = norm_scale(p, b, lane);
-      if (lane == 0) scales[b] = s;
-    }
+  for (uint32_t b = c; b < p.batch; b += CONS) {
+    const float s = norm_scale(p, b, lane);
+    if (lane == 0) scales[b] = s;
+  }
   cbar(nthr);
   const uint32_t quads = (uint32_t)p.xqn.quads;
   const uint32_t limb16 = (uint32_t)(b200_xq_limb_bytes(p.batch, p.n_embd) / 16);
@@ -882,7 +1024,11 @@ __global__ void __launch_bounds__((CONS + 1) * 32, 1) k_decode(const __grid_cons
     }
     fence_mbar_init();
     sfailed = 0;
+    s_npos = (uint32_t)__ldcg(p.pos) + 1u;
   }
+  static_assert(sizeof(KP) % 4 == 0, "KP copied as words");
+  for (uint32_t i = threadIdx.x; i < sizeof(KP) / 4; i += blockDim.x)
+    reinterpret_cast<uint32_t *>(&s_kp)[i] = reinterpret_cast<const uint32_t *>(&p)[i];
   __syncthreads();
 
   if (warp == 0) {
@@ -905,15 +1051,15 @@ __global__ void __launch_bounds__((CONS + 1) * 32, 1) k_decode(const __grid_cons
   // ---- consumers ----
   const int c = warp - 1, ctid = threadIdx.x - 32, nthr = CONS * 32;
   // the x staging area comes first; per-warp scratch (128 floats) after it
-  float *scratch = reinterpret_cast<float *>(area + ((x_area_bytes(NT, p.batch, Unit<T>::XPU, p.sh[M_O].units) + 127) &
-                                                     ~(size_t)127));
+  float *scratch = reinterpret_cast<float *>(area + p.scratch_off);
   uint32_t seq = 0, epoch = 0;
   // row exchanges this rank completed in earlier steps (written by the
   // previous launch's last CTA)
   const uint64_t xbase = p.nranks > 1 ? *(volatile uint64_t *)(land_words(p.land[p.rank]) + 1) : 0;
   bool ok = true;
+  fill_split_table(p, ctid, nthr);  // the first grid barrier's named barrier publishes it
   auto gemv = [&](int k, int xsrc, int pi) {
-    consume<T, NT, CONS>(p, p.sh[k], xsrc, p.part[pi], ring, full, empty, seq, area, scratch, scales, c, lane, ctid,
+    consume<T, NT, CONS>(p, k, xsrc, p.part[pi], ring, full, empty, seq, area, scratch, scales, c, lane, ctid,
                          nthr, &sfailed);
     cbar(nthr);
     if (sfailed) {
@@ -933,27 +1079,27 @@ __global__ void __launch_bounds__((CONS + 1) * 32, 1) k_decode(const __grid_cons
     gemv(M_QKV, X_NORMQ, 0);
     if (!sync()) break;
     switch (p.h / p.hk) {
-      case 1: attention<1, CONS>(p, l, c, lane, ctid, nthr, reinterpret_cast<float *>(area)); break;
-      case 2: attention<2, CONS>(p, l, c, lane, ctid, nthr, reinterpret_cast<float *>(area)); break;
-      case 4: attention<4, CONS>(p, l, c, lane, ctid, nthr, reinterpret_cast<float *>(area)); break;
-      default: attention<8, CONS>(p, l, c, lane, ctid, nthr, reinterpret_cast<float *>(area)); break;
+      case 1: attention<1, CONS>(s_kp, l, c, lane, ctid, nthr, reinterpret_cast<float *>(area)); break;
+      case 2: attention<2, CONS>(s_kp, l, c, lane, ctid, nthr, reinterpret_cast<float *>(area)); break;
+      case 4: attention<4, CONS>(s_kp, l, c, lane, ctid, nthr, reinterpret_cast<float *>(area)); break;
+      default: attention<8, CONS>(s_kp, l, c, lane, ctid, nthr, reinterpret_cast<float *>(area)); break;
     }
     if (!sync()) break;
     gemv(M_O, X_ATT, 1);
     if (!sync()) break;
     if (p.nranks > 1)
-      ok = exchange_rows<CONS>(p, p.sh[M_O], L.ffn_norm, xbase + 2ull * l, c, lane, ctid, nthr, &sflag);
+      ok = exchange_rows<CONS>(s_kp, s_kp.sh[M_O], L.ffn_norm, xbase + 2ull * l, c, lane, ctid, nthr, &sflag);
     else
-      reduce_rows<CONS>(p, p.sh[M_O], L.ffn_norm, c, lane);
+      reduce_rows<CONS>(s_kp, s_kp.sh[M_O], L.ffn_norm, c, lane);
     if (!sync()) break;
     gemv(M_GU, X_NORMQ, 0);
     if (!sync()) break;
     gemv(M_DOWN, X_SILU, 1);
     if (!sync()) break;
     if (p.nranks > 1)
-      ok = exchange_rows<CONS>(p, p.sh[M_DOWN], g_next, xbase + 2ull * l + 1, c, lane, ctid, nthr, &sflag);
+      ok = exchange_rows<CONS>(s_kp, s_kp.sh[M_DOWN], g_next, xbase + 2ull * l + 1, c, lane, ctid, nthr, &sflag);
     else
-      reduce_rows<CONS>(p, p.sh[M_DOWN], g_next, c, lane);
+      reduce_rows<CONS>(s_kp, s_kp.sh[M_DOWN], g_next, c, lane);
   }
   if (ok && sync()) final_norm<CONS>(p, c, lane, ctid, nthr, scales);
   // Leave: the last CTA out resets the barrier words for the next launch

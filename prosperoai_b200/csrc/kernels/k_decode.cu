@@ -94,17 +94,25 @@ extern "C" pai_status_t b200_decode_plan_create(pai_b200_ctx_t *ctx, const b200_
   const uint64_t dims[4][2] = {{a->n_qkv, E}, {E, a->k_o}, {2 * a->ffl, E}, {E, a->ffl}};
   uint64_t part_floats[2] = {0, 0};
   size_t area = 0;
+  uint32_t tab = 0;
   for (int i = 0; i < 4; i++) {
     uint64_t max_range = 0;
     k.sh[i] = make_shape(T, dims[i][0], dims[i][1], cons, pl->grid, max_range);
+    k.sh[i].tab = tab;
+    tab += k.sh[i].ngroups;
     part_floats[i & 1] = std::max<uint64_t>(part_floats[i & 1], (uint64_t)k.sh[i].maxseg * B * k.sh[i].npad);
-    size_t bytes = b200dec::x_area_bytes(pl->nt, B, xpu, std::min<uint64_t>(k.sh[i].units, max_range));
-    if (i == b200dec::M_O)  // the attention merge's per-warp scratch follows o's staged operand
-      bytes = ((b200dec::x_area_bytes(pl->nt, B, xpu, k.sh[i].units) + 127) & ~(size_t)127) +
-              (size_t)cons * kHD * sizeof(float);
-    area = std::max(area, bytes);
+    // a staged operand holds at most min(units, longest range) entries
+    area = std::max(area, b200dec::x_area_bytes(pl->nt, B, xpu, std::min<uint64_t>(k.sh[i].units, max_range)));
   }
-  area = std::max(area, (size_t)cons * G * (kHD + 2) * sizeof(float));  // attention: the warps' partials
+  if (tab > b200dec::kTab) {
+    delete plan;
+    return b200_fail(PAI_ERR_UNSUPPORTED, "decode_plan: %u row groups exceed the split table", tab);
+  }
+  // the stagings' per-warp scratch (128 floats) follows the largest staged operand
+  k.scratch_off = (uint32_t)((area + 127) & ~(size_t)127);
+  area = k.scratch_off + (size_t)cons * kHD * sizeof(float);
+  // attention: q (padded quarter rows), k and v of one kv head, then the warps' partials
+  area = std::max(area, ((size_t)G * 4 * b200dec::kQP + 2 * kHD + (size_t)cons * G * b200dec::kAS) * sizeof(float));
   area = (area + 127) & ~(size_t)127;
   pl->smem = (size_t)kStages * cons * 2304u + area;  // ring (kStageBytes) + staging area
   if (pl->smem > 220 * 1024) {
@@ -113,7 +121,7 @@ extern "C" pai_status_t b200_decode_plan_create(pai_b200_ctx_t *ctx, const b200_
   }
   const uint32_t per_head = std::max<uint32_t>(1, pl->grid / (a->hk * B));
   // scratch: partials [2] | attention partials | ssq (doubles) | xqn | barrier words
-  const uint64_t attn_floats = (uint64_t)B * a->h * per_head * (kHD + 2);
+  const uint64_t attn_floats = (uint64_t)B * a->h * per_head * b200dec::kAS;
   const uint64_t ssq_bytes = (uint64_t)B * (E / 32) * 8;
   const uint64_t xqn_bytes = b200_xq_bytes(B, E);
   const uint64_t off_p1 = b200_align256(part_floats[0] * 4), off_at = off_p1 + b200_align256(part_floats[1] * 4);
