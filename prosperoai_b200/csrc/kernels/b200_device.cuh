@@ -177,7 +177,8 @@ __device__ __forceinline__ void rope_pair(float x0, float x1, float c, float s, 
 // its two scales, so a buffer reused with another layout needs no clearing.
 __device__ __forceinline__ void xq_store_block(const b200_xq_t &xq, uint32_t vec, uint32_t b, float v) {
   const uint32_t lane = threadIdx.x & 31;
-  const float amax = warp_max(fabsf(v));
+  // |v| bit patterns order as unsigned integers: one warp reduction gives the maximum
+  const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v))));
   const float s = __fdiv_rn(amax, (float)B200_XQ_MAX);
   int X = 0;
   if (s > 0.0f) {
@@ -188,7 +189,7 @@ __device__ __forceinline__ void xq_store_block(const b200_xq_t &xq, uint32_t vec
   const int t1 = (X - L0) >> 8;
   const int L1 = ((t1 + 128) & 255) - 128;
   const int L2 = (t1 - L1) >> 8;
-  const int sum = warp_sum_i(X);
+  const int sum = __reduce_add_sync(0xffffffffu, X);
   const uint32_t part = lane >> 4, c = (lane & 15) >> 2, q = b >> 2, i = b & 3;
   const uint32_t pair = vec >> 1, vs = vec & 1;
   uint8_t *base = xq.limbs + (((uint64_t)pair * xq.quads + q) * 2 + part) * 512 + i * 4 + (lane & 3);

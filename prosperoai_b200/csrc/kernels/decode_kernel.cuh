@@ -83,6 +83,7 @@ template <int CONS>
 constexpr uint32_t kStageBytes = CONS * 2304u;
 constexpr uint32_t kHD = 128;
 constexpr uint32_t kAS = kHD + 4;  // attention partial: o[kHD], max, sum, 2 pad (16-byte rows)
+constexpr uint32_t kMaxSlots = 16;  // attention CTAs per (sequence, kv head) at most
 enum { M_QKV = 0, M_O = 1, M_GU = 2, M_DOWN = 3 };
 
 // Shape and work split of one layer-matrix kind (the same for every layer).
@@ -123,6 +124,7 @@ struct KP {
   // state
   float *x;          // hidden state [batch][n_embd]
   b200_xq_t xqn;     // x * gamma of the next RMSNorm, quantised unscaled
+  b200_xq_t xqa, xqh;  // batches of 3+: attention output and silu(gate) * up, quantised once
   double *ssq;       // [batch][n_embd / 32] sums of squares of x per block
   b200_xq_t xq_out;  // RMSNorm(x) * out_norm for the lm head
   const float *out_norm;
@@ -266,6 +268,27 @@ __device__ __forceinline__ float row_sum(const float *part, const Shape &sh, uin
   return row_finish<CH>(r, v, batch, sh.npad);
 }
 
+// This CTA's (group, unit) range [r0, r1) of one shape, the group of r0 and
+// the CTA's split index in that group (it is split 0 of every later group
+// it touches), computed once per launch (64-bit arithmetic).
+struct Range {
+  uint32_t r0, r1, g0, split0;
+};
+static __shared__ Range s_rng[4];
+
+__device__ inline Range make_range(const Shape &sh) {
+  uint64_t r0, r1;
+  phase_range(sh, r0, r1);
+  Range r;
+  r.r0 = (uint32_t)r0;
+  r.r1 = (uint32_t)r1;
+  r.g0 = r0 < r1 ? (uint32_t)(r0 / sh.units) : 0u;
+  uint32_t lo = blockIdx.x, nseg;
+  if (r0 < r1) group_split(sh, r.g0, lo, nseg);
+  r.split0 = blockIdx.x - lo;
+  return r;
+}
+
 // Fill s_nseg (consumer threads; a named barrier follows before any use).
 __device__ inline void fill_split_table(const KP &p, int ctid, int nthr) {
 #pragma unroll
@@ -282,12 +305,11 @@ struct Sub {
   uint32_t g, u0, u1;
 };
 
-__device__ __forceinline__ Sub sub_at(const Shape &sh, uint64_t pos, uint64_t r1) {
+__device__ __forceinline__ Sub sub_at(const Shape &sh, uint32_t pos, uint32_t r1) {
   Sub s;
-  s.g = (uint32_t)(pos / sh.units);
-  s.u0 = (uint32_t)(pos - (uint64_t)s.g * sh.units);
-  const uint64_t seg_end = min(r1, (uint64_t)(s.g + 1) * sh.units);
-  s.u1 = (uint32_t)(seg_end - (uint64_t)s.g * sh.units);
+  s.g = pos / sh.units;
+  s.u0 = pos - s.g * sh.units;
+  s.u1 = min(r1, (s.g + 1) * sh.units) - s.g * sh.units;
   return s;
 }
 
@@ -295,15 +317,15 @@ __device__ __forceinline__ Sub sub_at(const Shape &sh, uint64_t pos, uint64_t r1
 // ring, one stage per U units of a sub-item. Returns false when a wait for
 // a free stage ran out.
 template <uint32_t T, int CONS>
-__device__ bool produce(const KP &p, const Shape &sh, const uint8_t *w, uint8_t *ring, uint64_t *full,
-                        uint64_t *empty, uint32_t &fill) {
+__device__ bool produce(const KP &p, int k, const uint8_t *w, uint8_t *ring, uint64_t *full, uint64_t *empty,
+                        uint32_t &fill) {
   using Un = Unit<T>;
   constexpr int U = Un::U;
   constexpr uint32_t GQ = CONS * Un::QB, GS = CONS * Un::SB;
+  const Shape &sh = p.sh[k];
   const uint8_t *qs = w, *sc = w + sh.sc_off;
-  uint64_t r0, r1;
-  phase_range(sh, r0, r1);
-  for (uint64_t pos = r0; pos < r1;) {
+  const uint32_t r0 = s_rng[k].r0, r1 = s_rng[k].r1;
+  for (uint32_t pos = r0; pos < r1;) {
     const Sub s = sub_at(sh, pos, r1);
     pos += s.u1 - s.u0;
     const uint32_t nv = min((uint32_t)CONS, sh.ntiles - s.g * CONS);  // tiles present in the group
@@ -338,12 +360,12 @@ struct XArea {
 };
 
 template <int NT, int XPU>
-__device__ __forceinline__ XArea x_area(const KP &p, const Shape &sh, uint8_t *area, uint64_t r0, uint64_t r1) {
+__device__ __forceinline__ XArea x_area(const KP &p, const Shape &sh, uint8_t *area, uint32_t r0, uint32_t r1) {
   XArea a;
-  const uint64_t L = r1 - r0;
+  const uint32_t L = r1 - r0;
   a.resident = L >= sh.units;
-  a.nent = a.resident ? sh.units : (uint32_t)L;
-  a.u0 = a.resident ? 0u : (uint32_t)(r0 % sh.units);
+  a.nent = a.resident ? sh.units : L;
+  a.u0 = a.resident ? 0u : r0 % sh.units;
   const uint32_t nq = a.nent * XPU;
   a.xs.limbs = area;
   a.xs.sb = reinterpret_cast<const float *>(area + (size_t)NT * nq * 1024);
@@ -360,7 +382,7 @@ __host__ __device__ constexpr size_t x_area_bytes(uint32_t nt, uint32_t batch, u
 
 // Unit of entry e: a range shorter than a group spans at most two groups, so
 // the units run u0, u0 + 1, ... and wrap once.
-__device__ __forceinline__ uint32_t entry_unit(const Shape &sh, const XArea &a, uint64_t r0, uint32_t e) {
+__device__ __forceinline__ uint32_t entry_unit(const Shape &sh, const XArea &a, uint32_t e) {
   const uint32_t u = a.u0 + e;
   return u >= sh.units ? u - sh.units : u;
 }
@@ -405,169 +427,189 @@ __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.commit_group;\n cp.async.wait_all;" ::: "memory");
 }
 
-// Normed input: the unscaled quantised x * gamma (xqn) of the entries' units
-// with their block scales multiplied by the norm scale. The digits and the
-// scales go to shared memory by asynchronous copies while warp b adds vector
-// b's block sums of squares; the scales are then multiplied in place.
-template <int NT, int XPU, int CONS>
-__device__ __noinline__ void stage_normq(const KP &p, const Shape &sh, const XArea &a, uint64_t r0, int c, int lane,
-                                         int ctid, int nthr, float *scales) {
+// A GEMV operand quantised once in global memory (src), the entries' units
+// of it staged by asynchronous copies. NORM: src is the unscaled x * gamma
+// of an RMSNorm (xqn), and the block scales are multiplied by the norm
+// scale, which warp b computes for vector b from the block sums of squares
+// while the copies land.
+template <int NT, int XPU, int CONS, bool NORM>
+__device__ __noinline__ void stage_copy(const KP &p, const Shape &sh, const XArea &a, const b200_xq_t &src, int c,
+                                        int lane, int ctid, int nthr, float *scales) {
   const uint32_t nq = a.nent * XPU, per = NT * XPU * 64;  // uint4 per entry (digits)
   uint4 *dl = reinterpret_cast<uint4 *>(const_cast<uint8_t *>(a.xs.limbs));
-  const uint4 *sl = reinterpret_cast<const uint4 *>(p.xqn.limbs);
+  const uint4 *sl = reinterpret_cast<const uint4 *>(src.limbs);
   for (uint32_t i = ctid; i < a.nent * per; i += nthr) {
     const uint32_t e = i / per, r = i % per, nt = r / (XPU * 64), o = r % (XPU * 64);
     cp_async16(dl + (((size_t)nt * nq + (size_t)e * XPU) * 1024) / 16 + o,
-               sl + (((size_t)nt * p.xqn.quads + (size_t)entry_unit(sh, a, r0, e) * XPU) * 1024) / 16 + o);
+               sl + (((size_t)nt * src.quads + (size_t)entry_unit(sh, a, e) * XPU) * 1024) / 16 + o);
   }
   float4 *db = reinterpret_cast<float4 *>(const_cast<float *>(a.xs.sb));
   float4 *dx = reinterpret_cast<float4 *>(const_cast<float *>(a.xs.sx));
-  const float4 *sb = reinterpret_cast<const float4 *>(p.xqn.sb);
-  const float4 *sx = reinterpret_cast<const float4 *>(p.xqn.sx);
+  const float4 *sb = reinterpret_cast<const float4 *>(src.sb);
+  const float4 *sx = reinterpret_cast<const float4 *>(src.sx);
   const uint32_t nsc = a.nent * p.batch * XPU;
   for (uint32_t i = ctid; i < nsc; i += nthr) {
     const uint32_t e = i / (p.batch * XPU), r = i % (p.batch * XPU), vec = r / XPU, q = r % XPU;
-    const size_t src = (size_t)vec * p.xqn.quads + (size_t)entry_unit(sh, a, r0, e) * XPU + q;
+    const size_t from = (size_t)vec * src.quads + (size_t)entry_unit(sh, a, e) * XPU + q;
     const size_t d = (size_t)vec * nq + (size_t)e * XPU + q;
-    cp_async16(db + d, sb + src);
-    cp_async16(dx + d, sx + src);
+    cp_async16(db + d, sb + from);
+    cp_async16(dx + d, sx + from);
   }
-  for (uint32_t b = c; b < p.batch; b += CONS) {  // warp b: vector b's scale
-    const float sc = norm_scale(p, b, lane);
-    if (lane == 0) scales[b] = sc;
-  }
+  if (NORM)
+    for (uint32_t b = c; b < p.batch; b += CONS) {  // warp b: vector b's scale
+      const float sc = norm_scale(p, b, lane);
+      if (lane == 0) scales[b] = sc;
+    }
   cp_async_wait_all();
   cbar(nthr);  // the copies and the norm scales are in shared memory
-  for (uint32_t i = ctid; i < nsc; i += nthr) {
-    const uint32_t e = i / (p.batch * XPU), r = i % (p.batch * XPU), vec = r / XPU, q = r % XPU;
-    const size_t d = (size_t)vec * nq + (size_t)e * XPU + q;
-    const float f = scales[vec];
-    float4 bv = db[d], xv = dx[d];
-    bv.x = __fmul_rn(bv.x, f), bv.y = __fmul_rn(bv.y, f), bv.z = __fmul_rn(bv.z, f), bv.w = __fmul_rn(bv.w, f);
-    xv.x = __fmul_rn(xv.x, f), xv.y = __fmul_rn(xv.y, f), xv.z = __fmul_rn(xv.z, f), xv.w = __fmul_rn(xv.w, f);
-    db[d] = bv;
-    dx[d] = xv;
-  }
-}
-
-// o's input: the attention output of the heads in the entries' units,
-// merged from the attention CTAs' partials (slot order) and quantised. One
-// warp per (vector, head); the slots go in chunks of 16 with every load of
-// a chunk in flight at once (lane s < 16 holds slot s's statistics, lane l
-// the dims 4l..4l+3 of every slot), combined with running-max rescaling
-// across chunks. The 128 values go through the warp's shared scratch to
-// quantise with lane = element.
-template <int NT, int XPU, int CONS>
-__device__ __noinline__ void stage_att(const KP &p, const Shape &sh, const XArea &a, uint64_t r0, int c, int lane,
-                                       float *scratch) {
-  b200_xq_t v = slot_view(p, a, sh.k);
-  float *ws = scratch + c * kHD;
-  const uint32_t heads = a.nent * XPU, ph = p.per_head;
-  constexpr uint32_t CH = 16;
-  for (uint32_t j = c; j < heads * p.batch; j += CONS) {
-    const uint32_t b = j / heads, eh = j % heads, e = eh / XPU;
-    const uint32_t hh = entry_unit(sh, a, r0, e) * XPU + eh % XPU;  // head of this rank
-    const float *base = p.apart + (((size_t)b * p.h + hh) * ph) * kAS;
-    float M = -INFINITY, L = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
-    for (uint32_t s0 = 0; s0 < ph; s0 += CH) {
-      const uint32_t cnt = min(CH, ph - s0);
-      float2 ml = make_float2(-INFINITY, 0.0f);
-      if ((uint32_t)lane < cnt) ml = __ldcg(reinterpret_cast<const float2 *>(base + (size_t)(s0 + lane) * kAS + kHD));
-      float4 ov[CH];
-#pragma unroll
-      for (uint32_t m = 0; m < CH; m++)
-        ov[m] = m < cnt ? __ldcg(reinterpret_cast<const float4 *>(base + (size_t)(s0 + m) * kAS) + lane)
-                        : make_float4(0.f, 0.f, 0.f, 0.f);
-      const float mc = warp_max(ml.y > 0.0f ? ml.x : -INFINITY);
-      const float m_new = fmaxf(M, mc);
-      const float alpha = M == -INFINITY ? 0.0f : expf(M - m_new);
-      const float w = ml.y > 0.0f ? expf(ml.x - m_new) : 0.0f;
-      L = fmaf(L, alpha, warp_sum(ml.y * w));
-#pragma unroll
-      for (int q = 0; q < 4; q++) o[q] *= alpha;
-#pragma unroll
-      for (uint32_t m = 0; m < CH; m++) {
-        const float wm = __shfl_sync(0xffffffffu, w, m);
-        o[0] = fmaf(ov[m].x, wm, o[0]), o[1] = fmaf(ov[m].y, wm, o[1]);
-        o[2] = fmaf(ov[m].z, wm, o[2]), o[3] = fmaf(ov[m].w, wm, o[3]);
-      }
-      M = m_new;
+  if (NORM)
+    for (uint32_t i = ctid; i < nsc; i += nthr) {
+      const uint32_t e = i / (p.batch * XPU), r = i % (p.batch * XPU), vec = r / XPU, q = r % XPU;
+      const size_t d = (size_t)vec * nq + (size_t)e * XPU + q;
+      const float f = scales[vec];
+      float4 bv = db[d], xv = dx[d];
+      bv.x = __fmul_rn(bv.x, f), bv.y = __fmul_rn(bv.y, f), bv.z = __fmul_rn(bv.z, f), bv.w = __fmul_rn(bv.w, f);
+      xv.x = __fmul_rn(xv.x, f), xv.y = __fmul_rn(xv.y, f), xv.z = __fmul_rn(xv.z, f), xv.w = __fmul_rn(xv.w, f);
+      db[d] = bv;
+      dx[d] = xv;
     }
-    __syncwarp();
+}
+
+// Attention output of head hh of vector b: the attention CTAs' partials of
+// its slots merged (slot order; one round of loads -- lane s holds slot s's
+// statistics, lane l the dims 4l..4l+3 of every slot) and quantised into
+// blocks blk0 .. blk0 + 3 of vector b of `dst` (through the warp's shared
+// scratch ws, lane = element). One warp.
+__device__ __forceinline__ void merge_head(const KP &p, uint32_t b, uint32_t hh, int lane, float *ws,
+                                           const b200_xq_t &dst, uint32_t blk0) {
+  const uint32_t ph = p.per_head;
+  const float *base = p.apart + (((size_t)b * p.h + hh) * ph) * kAS;
+  const float2 ml = (uint32_t)lane < ph ? __ldcg(reinterpret_cast<const float2 *>(base + (size_t)lane * kAS + kHD))
+                                        : make_float2(-INFINITY, 0.0f);
+  float4 ov[kMaxSlots];
 #pragma unroll
-    for (int q = 0; q < 4; q++) ws[4 * lane + q] = o[q] / L;
-    __syncwarp();
-    // head hh is x blocks 4 hh .. 4 hh + 3; in the entry they are blocks
-    // 4 (e XPU + eh % XPU) .. of the slot
-    const uint32_t blk0 = (e * XPU + eh % XPU) * 4;
+  for (uint32_t m = 0; m < kMaxSlots; m++)
+    ov[m] = m < ph ? __ldcg(reinterpret_cast<const float4 *>(base + (size_t)m * kAS) + lane)
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
+  const float M = warp_max(ml.y > 0.0f ? ml.x : -INFINITY);
+  const float w = ml.y > 0.0f ? expf(ml.x - M) : 0.0f;
+  const float L = warp_sum(ml.y * w);
+  float o[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int q = 0; q < 4; q++) xq_store_block(v, b, blk0 + q, ws[32 * q + lane]);
+  for (uint32_t m = 0; m < kMaxSlots; m++) {
+    const float wm = __shfl_sync(0xffffffffu, w, m);
+    o[0] = fmaf(ov[m].x, wm, o[0]), o[1] = fmaf(ov[m].y, wm, o[1]);
+    o[2] = fmaf(ov[m].z, wm, o[2]), o[3] = fmaf(ov[m].w, wm, o[3]);
+  }
+  __syncwarp();
+  *reinterpret_cast<float4 *>(ws + 4 * lane) = make_float4(o[0] / L, o[1] / L, o[2] / L, o[3] / L);
+  __syncwarp();
+#pragma unroll
+  for (int q = 0; q < 4; q++) xq_store_block(dst, b, blk0 + q, ws[32 * q + lane]);
+  __syncwarp();
+}
+
+// o's input at batches of 1-2: the heads in the entries' units merged by this
+// CTA (one warp per (vector, head)).
+template <int NT, int XPU, int CONS>
+__device__ __noinline__ void stage_att(const KP &p, const Shape &sh, const XArea &a, int c, int lane, float *scratch) {
+  const b200_xq_t v = slot_view(p, a, sh.k);
+  const uint32_t heads = a.nent * XPU, nj = heads * p.batch;
+  for (uint32_t j = c; j < nj; j += CONS) {
+    const uint32_t b = j / heads, eh = j % heads, e = eh / XPU;
+    // head (unit e XPU + eh % XPU) is x blocks 4 hh .. 4 hh + 3; in the entry
+    // they are blocks 4 (e XPU + eh % XPU) .. of the slot
+    merge_head(p, b, entry_unit(sh, a, e) * XPU + eh % XPU, lane, scratch + c * kHD, v, (e * XPU + eh % XPU) * 4);
   }
 }
 
-// down's input: h = silu(gate) * up for the entries' units, from the
+// Batches of 3+: every (vector, head) merged once into xqa, one warp each
+// over the grid (o then stages xqa by copies).
+template <int CONS>
+__device__ __noinline__ void merge_phase(const KP &p, int c, int lane, float *scratch) {
+  const uint32_t nj = p.batch * p.h;
+  for (uint32_t j = blockIdx.x * CONS + c; j < nj; j += gridDim.x * CONS)
+    merge_head(p, j / p.h, j % p.h, lane, scratch + c * kHD, p.xqa, 4 * (j % p.h));
+}
+
+// h = silu(gate) * up for outputs o0 .. o0 + 127 of vector b from the
 // gate|up partial sums (gate|up tile t holds gate rows 8t.. then the
-// matching up rows), quantised. One warp per (vector, 128 outputs): lane l
-// takes outputs 4l..4l+3 -- 4 consecutive gate rows and the 4 up rows 8
-// further, one 16-byte load each per split, all splits' loads in flight --
-// and the values go through the warp's shared scratch to quantise with
-// lane = element.
-template <int NT, int XPU, int CONS>
-__device__ __noinline__ void stage_silu(const KP &p, const Shape &sh, const XArea &a, uint64_t r0, int c, int lane,
-                                        float *scratch) {
-  b200_xq_t v = slot_view(p, a, sh.k);
-  float *ws = scratch + c * kHD;
+// matching up rows), quantised into blocks blk0 .. blk0 + 3 of vector b of
+// `dst`. One warp: lane l takes outputs 4l..4l+3 -- 4 consecutive gate rows
+// and the 4 up rows 8 further, one 16-byte load each per split, all splits'
+// loads in flight -- and the values go through the warp's shared scratch to
+// quantise with lane = element.
+template <int CONS>
+__device__ __forceinline__ void silu_chunk(const KP &p, uint32_t b, uint32_t o0, uint32_t k, int lane, float *ws,
+                                           const b200_xq_t &dst, uint32_t blk0) {
   const Shape &gu = p.sh[M_GU];
-  const float *part = p.part[0];
+  const size_t st4 = (size_t)p.batch * gu.npad / 4;
+  constexpr int CH = 4;  // splits loaded at once (a gate|up group spans few CTAs)
+  const uint32_t o = o0 + 4 * lane, oc = min(o, k - 4);
+  const uint32_t grow = (oc / 8) * 16 + oc % 8;
+  const uint32_t nseg = s_nseg[gu.tab + grow / (16u * CONS)];
+  const float4 *q = reinterpret_cast<const float4 *>(p.part[0] + (size_t)b * gu.npad + grow);
+  float4 gv[CH], uv[CH];
+#pragma unroll
+  for (int m = 0; m < CH; m++) {
+    const bool in = (uint32_t)m < nseg;
+    gv[m] = in ? __ldcg(q + m * st4) : make_float4(0.f, 0.f, 0.f, 0.f);
+    uv[m] = in ? __ldcg(q + m * st4 + 2) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  float4 gs = gv[0], us = uv[0];
+#pragma unroll
+  for (int m = 1; m < CH; m++)
+    if ((uint32_t)m < nseg) {
+      gs.x += gv[m].x, gs.y += gv[m].y, gs.z += gv[m].z, gs.w += gv[m].w;
+      us.x += uv[m].x, us.y += uv[m].y, us.z += uv[m].z, us.w += uv[m].w;
+    }
+  for (uint32_t m = CH; m < nseg; m++) {
+    const float4 g4 = __ldcg(q + m * st4), u4 = __ldcg(q + m * st4 + 2);
+    gs.x += g4.x, gs.y += g4.y, gs.z += g4.z, gs.w += g4.w;
+    us.x += u4.x, us.y += u4.y, us.z += u4.z, us.w += u4.w;
+  }
+  float4 h4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (o < k) {  // k % 32 == 0: the lane's 4 outputs are all in or all out
+    // llama.c:774-781
+    h4.x = __fmul_rn(__fdiv_rn(gs.x, __fadd_rn(1.0f, expf(-gs.x))), us.x);
+    h4.y = __fmul_rn(__fdiv_rn(gs.y, __fadd_rn(1.0f, expf(-gs.y))), us.y);
+    h4.z = __fmul_rn(__fdiv_rn(gs.z, __fadd_rn(1.0f, expf(-gs.z))), us.z);
+    h4.w = __fmul_rn(__fdiv_rn(gs.w, __fadd_rn(1.0f, expf(-gs.w))), us.w);
+  }
+  __syncwarp();
+  *reinterpret_cast<float4 *>(ws + 4 * lane) = h4;
+  __syncwarp();
+#pragma unroll
+  for (int qq = 0; qq < 4; qq++) xq_store_block(dst, b, blk0 + qq, ws[32 * qq + lane]);
+  __syncwarp();
+}
+
+// down's input at batches of 1-2: the entries' units computed by this CTA,
+// one warp per (vector, 128 outputs).
+template <int NT, int XPU, int CONS>
+__device__ __noinline__ void stage_silu(const KP &p, const Shape &sh, const XArea &a, int c, int lane,
+                                        float *scratch) {
+  const b200_xq_t v = slot_view(p, a, sh.k);
   const uint32_t nch = a.nent * XPU, ni = nch * p.batch;  // 128-output chunks
-  const size_t stride = (size_t)p.batch * gu.npad;
-  constexpr int CH = 4;
   for (uint32_t it = c; it < ni; it += CONS) {
     const uint32_t b = it / nch, ch = it % nch, e = ch / XPU;
-    const uint32_t o = (entry_unit(sh, a, r0, e) * XPU + ch % XPU) * 128 + 4 * lane;
-    float4 h4 = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (o < sh.k) {  // k % 32 == 0: the lane's 4 outputs are all in or all out
-      const uint32_t grow = (o / 8) * 16 + o % 8;
-      const uint32_t nseg = s_nseg[gu.tab + grow / (16u * CONS)];
-      const float4 *q = reinterpret_cast<const float4 *>(part + (size_t)b * gu.npad + grow);
-      const size_t st4 = stride / 4;
-      float4 gs = make_float4(0.f, 0.f, 0.f, 0.f), us = gs;
-      for (uint32_t i0 = 0; i0 < nseg; i0 += CH) {
-        float4 gv[CH], uv[CH];
-#pragma unroll
-        for (int i = 0; i < CH; i++) {
-          const bool in = i0 + i < nseg;
-          gv[i] = in ? __ldcg(q + (i0 + i) * st4) : make_float4(0.f, 0.f, 0.f, 0.f);
-          uv[i] = in ? __ldcg(q + (i0 + i) * st4 + 2) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-#pragma unroll
-        for (int i = 0; i < CH; i++)
-          if (i0 + i < nseg) {
-            if (i0 + i == 0) {
-              gs = gv[i], us = uv[i];
-            } else {
-              gs.x += gv[i].x, gs.y += gv[i].y, gs.z += gv[i].z, gs.w += gv[i].w;
-              us.x += uv[i].x, us.y += uv[i].y, us.z += uv[i].z, us.w += uv[i].w;
-            }
-          }
-      }
-      // llama.c:774-781
-      h4.x = __fmul_rn(__fdiv_rn(gs.x, __fadd_rn(1.0f, expf(-gs.x))), us.x);
-      h4.y = __fmul_rn(__fdiv_rn(gs.y, __fadd_rn(1.0f, expf(-gs.y))), us.y);
-      h4.z = __fmul_rn(__fdiv_rn(gs.z, __fadd_rn(1.0f, expf(-gs.z))), us.z);
-      h4.w = __fmul_rn(__fdiv_rn(gs.w, __fadd_rn(1.0f, expf(-gs.w))), us.w);
-    }
-    __syncwarp();
-    *reinterpret_cast<float4 *>(ws + 4 * lane) = h4;
-    __syncwarp();
-#pragma unroll
-    for (int q = 0; q < 4; q++) xq_store_block(v, b, ch * 4 + q, ws[32 * q + lane]);
+    silu_chunk<CONS>(p, b, (entry_unit(sh, a, e) * XPU + ch % XPU) * 128, sh.k, lane, scratch + c * kHD, v,
+                     ch * 4);
   }
+}
+
+// Batches of 3+: h computed once into xqh, one warp per (vector, 128
+// outputs) over the grid (down then stages xqh by copies).
+template <int CONS>
+__device__ __noinline__ void silu_phase(const KP &p, int c, int lane, float *scratch) {
+  const uint32_t k = p.sh[M_DOWN].k, nch = (k + 127) / 128, ni = nch * p.batch;
+  for (uint32_t it = blockIdx.x * CONS + c; it < ni; it += gridDim.x * CONS)
+    silu_chunk<CONS>(p, it / nch, (it % nch) * 128, k, lane, scratch + c * kHD, p.xqh, (it % nch) * 4);
 }
 
 // ---- GEMV phases ------------------------------------------------------------------------
 
-enum { X_NORMQ = 0, X_ATT = 1, X_SILU = 2 };
+enum { X_NORMQ = 0, X_ATT = 1, X_SILU = 2, X_COPY_A = 3, X_COPY_H = 4 };
 
 // Consumer side of one GEMV phase: stage the operand, run the ring, write
 // the CTA's segments as partial row sums. `failed` (shared) records a ring
@@ -581,25 +623,27 @@ __device__ void consume(const KP &p, int k, int xsrc, float *part, uint8_t *ring
   constexpr int U = Un::U, XPU = Un::XPU;
   constexpr uint32_t GQ = CONS * Un::QB, GS = CONS * Un::SB;
   const Shape &sh = p.sh[k];
-  uint64_t r0, r1;
-  phase_range(sh, r0, r1);
+  const uint32_t r0 = s_rng[k].r0, r1 = s_rng[k].r1, g0 = s_rng[k].g0, split0 = s_rng[k].split0;
   if (r0 >= r1) return;
   const XArea a = x_area<NT, XPU>(p, sh, area, r0, r1);
   if (xsrc == X_NORMQ)
-    stage_normq<NT, XPU, CONS>(s_kp, s_kp.sh[k], a, r0, c, lane, ctid, nthr, scales);
+    stage_copy<NT, XPU, CONS, true>(s_kp, s_kp.sh[k], a, s_kp.xqn, c, lane, ctid, nthr, scales);
+  else if (xsrc == X_COPY_A)
+    stage_copy<NT, XPU, CONS, false>(s_kp, s_kp.sh[k], a, s_kp.xqa, c, lane, ctid, nthr, scales);
+  else if (xsrc == X_COPY_H)
+    stage_copy<NT, XPU, CONS, false>(s_kp, s_kp.sh[k], a, s_kp.xqh, c, lane, ctid, nthr, scales);
   else if (xsrc == X_ATT)
-    stage_att<NT, XPU, CONS>(s_kp, s_kp.sh[k], a, r0, c, lane, scratch);
+    stage_att<NT, XPU, CONS>(s_kp, s_kp.sh[k], a, c, lane, scratch);
   else
-    stage_silu<NT, XPU, CONS>(s_kp, s_kp.sh[k], a, r0, c, lane, scratch);
+    stage_silu<NT, XPU, CONS>(s_kp, s_kp.sh[k], a, c, lane, scratch);
   cbar(nthr);
-  const uint64_t total = (uint64_t)sh.ngroups * sh.units;
   const uint32_t r = lane >> 2, vsel = (lane & 3) >> 1;
   const bool holder = (lane & 1) == 0;
   float yr[NT], yr8[NT];
   bool bad = false;
-  for (uint64_t pos = r0; pos < r1;) {
+  for (uint32_t pos = r0; pos < r1;) {
     const Sub s = sub_at(sh, pos, r1);
-    const uint32_t eoff = (uint32_t)(pos - r0);  // entry of unit s.u0 when not resident
+    const uint32_t eoff = pos - r0;  // entry of unit s.u0 when not resident
     pos += s.u1 - s.u0;
     const uint32_t tile = s.g * CONS + c;
     const bool active = tile < sh.ntiles;
@@ -634,10 +678,7 @@ __device__ void consume(const KP &p, int k, int xsrc, float *part, uint8_t *ring
     }
     if (!active || bad) continue;
     // this CTA's segment of group g: its partial row sums
-    uint32_t lo, nseg;
-    group_split(sh, s.g, lo, nseg);
-    (void)total;
-    const uint32_t split = blockIdx.x - lo;
+    const uint32_t split = s.g == g0 ? split0 : 0u;
 #pragma unroll
     for (int nt = 0; nt < NT; nt++) {  // lane pairs (c, c^1) hold the two halves of one sum
       const float ya = yr[nt] + __shfl_xor_sync(0xffffffffu, yr[nt], 1);
@@ -764,6 +805,7 @@ __device__ __noinline__ bool exchange_rows(const KP &p, const Shape &sh, const f
 // are merged in shared memory into one partial (o, max, sum) per head and
 // slot. Not inlined: its arrays keep their own register allocation.
 constexpr uint32_t kQP = 36;  // shared-memory q: quarter rows of 32 dims padded to 36 (banks)
+
 template <int G, int CONS>
 __device__ __noinline__ void attention(const KP &p, uint32_t layer, int warp, int lane, int ctid, int nthr,
                                        float *sm) {
@@ -1026,6 +1068,7 @@ __global__ void __launch_bounds__((CONS + 1) * 32, 1) k_decode(const __grid_cons
     sfailed = 0;
     s_npos = (uint32_t)__ldcg(p.pos) + 1u;
   }
+  if (threadIdx.x < 4) s_rng[threadIdx.x] = make_range(p.sh[threadIdx.x]);
   static_assert(sizeof(KP) % 4 == 0, "KP copied as words");
   for (uint32_t i = threadIdx.x; i < sizeof(KP) / 4; i += blockDim.x)
     reinterpret_cast<uint32_t *>(&s_kp)[i] = reinterpret_cast<const uint32_t *>(&p)[i];
@@ -1037,7 +1080,7 @@ __global__ void __launch_bounds__((CONS + 1) * 32, 1) k_decode(const __grid_cons
     uint32_t fill = 0;
     bool ok = true;
     for (uint32_t l = 0; l < p.n_layer && ok; l++)
-      for (int k = 0; k < 4 && ok; k++) ok = produce<T, CONS>(p, p.sh[k], p.layers[l].w[k], ring, full, empty, fill);
+      for (int k = 0; k < 4 && ok; k++) ok = produce<T, CONS>(p, k, p.layers[l].w[k], ring, full, empty, fill);
     if (!ok) {
       // a wait for a free stage ran out: raise the error and let the copies
       // already issued land (bounded) before this thread leaves
@@ -1085,7 +1128,13 @@ __global__ void __launch_bounds__((CONS + 1) * 32, 1) k_decode(const __grid_cons
       default: attention<8, CONS>(s_kp, l, c, lane, ctid, nthr, reinterpret_cast<float *>(area)); break;
     }
     if (!sync()) break;
-    gemv(M_O, X_ATT, 1);
+    if (NT > 1) {  // batches of 3+: merge once, then stage by copies
+      merge_phase<CONS>(s_kp, c, lane, scratch);
+      if (!sync()) break;
+      gemv(M_O, X_COPY_A, 1);
+    } else {
+      gemv(M_O, X_ATT, 1);
+    }
     if (!sync()) break;
     if (p.nranks > 1)
       ok = exchange_rows<CONS>(s_kp, s_kp.sh[M_O], L.ffn_norm, xbase + 2ull * l, c, lane, ctid, nthr, &sflag);
@@ -1094,7 +1143,13 @@ __global__ void __launch_bounds__((CONS + 1) * 32, 1) k_decode(const __grid_cons
     if (!sync()) break;
     gemv(M_GU, X_NORMQ, 0);
     if (!sync()) break;
-    gemv(M_DOWN, X_SILU, 1);
+    if (NT > 1) {
+      silu_phase<CONS>(s_kp, c, lane, scratch);
+      if (!sync()) break;
+      gemv(M_DOWN, X_COPY_H, 1);
+    } else {
+      gemv(M_DOWN, X_SILU, 1);
+    }
     if (!sync()) break;
     if (p.nranks > 1)
       ok = exchange_rows<CONS>(s_kp, s_kp.sh[M_DOWN], g_next, xbase + 2ull * l + 1, c, lane, ctid, nthr, &sflag);

@@ -104,6 +104,11 @@ extern "C" pai_status_t b200_decode_plan_create(pai_b200_ctx_t *ctx, const b200_
     // a staged operand holds at most min(units, longest range) entries
     area = std::max(area, b200dec::x_area_bytes(pl->nt, B, xpu, std::min<uint64_t>(k.sh[i].units, max_range)));
   }
+  for (int i = 0; i < 4; i++)
+    if ((uint64_t)k.sh[i].ngroups * k.sh[i].units >= (1ull << 31)) {
+      delete plan;
+      return b200_fail(PAI_ERR_UNSUPPORTED, "decode_plan: matrix %d has too many (group, unit) pairs", i);
+    }
   if (tab > b200dec::kTab) {
     delete plan;
     return b200_fail(PAI_ERR_UNSUPPORTED, "decode_plan: %u row groups exceed the split table", tab);
@@ -119,14 +124,19 @@ extern "C" pai_status_t b200_decode_plan_create(pai_b200_ctx_t *ctx, const b200_
     delete plan;
     return b200_fail(PAI_ERR_UNSUPPORTED, "decode_plan: %zu B of shared memory per CTA", pl->smem);
   }
-  const uint32_t per_head = std::max<uint32_t>(1, pl->grid / (a->hk * B));
-  // scratch: partials [2] | attention partials | ssq (doubles) | xqn | barrier words
+  // attention CTAs per (sequence, kv head): at most 16, the slots the o
+  // GEMV's staging merges in one round of loads
+  const uint32_t per_head = std::min<uint32_t>(b200dec::kMaxSlots, std::max<uint32_t>(1, pl->grid / (a->hk * B)));
+  // scratch: partials [2] | attention partials | ssq (doubles) | xqn | xqa | xqh | barrier words
+  // (xqa, xqh: the once-quantised o and down operands of batches of 3+)
   const uint64_t attn_floats = (uint64_t)B * a->h * per_head * b200dec::kAS;
   const uint64_t ssq_bytes = (uint64_t)B * (E / 32) * 8;
   const uint64_t xqn_bytes = b200_xq_bytes(B, E);
   const uint64_t off_p1 = b200_align256(part_floats[0] * 4), off_at = off_p1 + b200_align256(part_floats[1] * 4);
   const uint64_t off_ssq = off_at + b200_align256(attn_floats * 4), off_xqn = off_ssq + b200_align256(ssq_bytes);
-  const uint64_t off_bar = off_xqn + b200_align256(xqn_bytes), bytes = off_bar + 256;
+  const uint64_t xqa_bytes = pl->nt > 1 ? b200_xq_bytes(B, a->k_o) : 0, xqh_bytes = pl->nt > 1 ? b200_xq_bytes(B, a->ffl) : 0;
+  const uint64_t off_xqa = off_xqn + b200_align256(xqn_bytes), off_xqh = off_xqa + b200_align256(xqa_bytes);
+  const uint64_t off_bar = off_xqh + b200_align256(xqh_bytes), bytes = off_bar + 256;
   st = b200_cuda(cudaMalloc(&pl->scratch, bytes), "decode scratch");
   if (!st) st = b200_cuda(cudaMemset(pl->scratch, 0, bytes), "decode scratch clear");
   b200dec::Layer *hl = st ? nullptr : (b200dec::Layer *)calloc(a->n_layer, sizeof(b200dec::Layer));
@@ -180,6 +190,10 @@ extern "C" pai_status_t b200_decode_plan_create(pai_b200_ctx_t *ctx, const b200_
   k.inv_scale = 1.0f / sqrtf((float)kHD);
   k.x = a->x;
   k.xqn = b200_xq_view(sp + off_xqn, B, E);
+  if (pl->nt > 1) {
+    k.xqa = b200_xq_view(sp + off_xqa, B, a->k_o);
+    k.xqh = b200_xq_view(sp + off_xqh, B, a->ffl);
+  }
   k.ssq = (double *)(sp + off_ssq);
   k.xq_out = a->xq_out;
   k.out_norm = a->out_norm;
