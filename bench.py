@@ -35,6 +35,10 @@ CFG_8B = dict(n_layer=32, n_embd=4096, n_head=32, n_head_kv=8, head_dim=128, n_f
               vocab=128256, eps=1e-5, rope_theta=500000.0, wtype=2, etype=8)
 PROMPT = 512
 SEED = 20261201
+# DRAM bytes per launch of the 32-layer persistent layer kernel, batch 1: ncu's
+# dram__bytes_read.sum + dram__bytes_write.sum of a 4-layer launch x 8
+# (profiles/k_decode_q4_0_8b.md)
+K_DECODE_TRAFFIC = 4166 * 10 ** 6
 METRIC = "Q4_0 8B-shape decode tok/s"
 UNIT = "tokens/s"
 
@@ -279,7 +283,10 @@ def layer_kernel_roofline(dev, model, sess, hbm_peak, peak_kind, reps=20):
             "algorithmic_bytes_per_launch": int(alg),
             "bytes_breakdown": {"layer_weights": int(layer_w), "kv_cache": int(kv), "embedding_row": int(emb_row)},
             "positions_attended": npos, "avg_launch_ms": round(per_ms, 5), "launches_timed": reps,
-            "traffic": None, "traffic_source": "see profiles/k_decode_q4_0_8b.md (ncu capture)"}
+            # ncu dram__bytes_read.sum + dram__bytes_write.sum of a 4-layer launch of the same
+            # kernel (profiles/k_decode_q4_0_8b.md), scaled to 32 layers (batch 1 only)
+            "traffic": K_DECODE_TRAFFIC if sess.batch == 1 and c["n_layer"] == 32 else None,
+            "traffic_source": "profiles/k_decode_q4_0_8b.md: ncu DRAM bytes of a 4-layer launch x 32/4"}
 
 
 def gemv_sweep(dev, hbm_peak, peak_kind, iters=30):
@@ -460,6 +467,15 @@ def layer_config4(dev, hbm_peak, peak_kind, steps=30, warmup=5):
     ms = C.c_float()
     _native.check(L.pai_b200_event_elapsed(e0, e1, C.byref(ms)), "elapsed")
     dev.sync()
+    kern_us = None
+    if sess.step_kernels == 4:  # the persistent layer kernel of this one-layer model, timed alone
+        sess.run_layers(3)
+        L.pai_b200_event_record(dev.ctx, e0)
+        sess.run_layers(steps)
+        L.pai_b200_event_record(dev.ctx, e1)
+        ms_k = C.c_float()
+        _native.check(L.pai_b200_event_elapsed(e0, e1, C.byref(ms_k)), "elapsed")
+        kern_us = ms_k.value / steps * 1e3
     sess.close()
     m.close()
     us = ms.value / steps * 1e3
@@ -468,11 +484,18 @@ def layer_config4(dev, hbm_peak, peak_kind, steps=30, warmup=5):
     kv = HK * (pos0 + steps // 2) * hd * 2 * 2  # K and V read at the middle timed position
     alg = weights + kv + 4 * (E + F) * 2
     gbs = alg / (us * 1e-6) / 1e9
-    return {"workload": "config 4: one Q4_0 decoder layer (8B shape), fp16 KV cache, batch 1",
-            "past_positions": past, "positions_timed": [pos0, pos0 + steps - 1], "us_per_step": round(us, 2),
-            "layer_steps_per_s": round(1e6 / us, 1), "algorithmic_bytes": int(alg), "gbs": round(gbs, 1),
-            "frac": round(gbs / hbm_peak, 4), "peak_kind": peak_kind,
-            "note": "the step also runs an embedding row, final norm, a 512-row Q8_0 lm head and argmax"}
+    out = {"workload": "config 4: one Q4_0 decoder layer (8B shape), fp16 KV cache, batch 1",
+           "past_positions": past, "positions_timed": [pos0, pos0 + steps - 1], "us_per_step": round(us, 2),
+           "layer_steps_per_s": round(1e6 / us, 1), "algorithmic_bytes": int(alg), "gbs": round(gbs, 1),
+           "frac": round(gbs / hbm_peak, 4), "peak_kind": peak_kind,
+           "note": "the step also runs an embedding row, final norm, a 512-row Q8_0 lm head and argmax"}
+    if kern_us is not None:
+        kg = alg / (kern_us * 1e-6) / 1e9
+        out["layer_kernel"] = {"us_per_launch": round(kern_us, 2), "gbs": round(kg, 1),
+                               "frac": round(kg / hbm_peak, 4),
+                               "what": "the persistent layer kernel alone (embedding row, the layer, final "
+                                       "norm; one cooperative launch each, position not advanced)"}
+    return out
 
 
 def prefill_timing(dev, sess, prompts, reps=3, pg=None):
@@ -590,11 +613,29 @@ def decode_variant(dev, model, batch, prompt, steps=20, warmup=3, persistent=Non
     L.pai_b200_event_record(dev.ctx, e1)
     ms = C.c_float()
     _native.check(L.pai_b200_event_elapsed(e0, e1, C.byref(ms)), "elapsed")
+    out = {"batch": batch, "prompt": prompt, "positions_timed": [pos0, pos0 + steps - 1],
+           "ms_per_step": round(ms.value / steps, 4), "value": round(batch * steps / (ms.value * 1e-3), 3),
+           "unit": UNIT, "launches_per_step": kernels,
+           "path": "one launch per op" if kernels != 4 else "persistent layer kernel"}
+    if kernels == 4:
+        # the layer kernel alone: per-layer time and bytes inside the 32-layer launch
+        sess.run_layers(2)
+        L.pai_b200_event_record(dev.ctx, e0)
+        sess.run_layers(10)
+        L.pai_b200_event_record(dev.ctx, e1)
+        _native.check(L.pai_b200_event_elapsed(e0, e1, C.byref(ms)), "elapsed")
+        c = model.cfg
+        per_layer_us = ms.value / 10 * 1e3 / c["n_layer"]
+        E, F, hd, H, HK = c["n_embd"], c["n_ff"], c["head_dim"], c["n_head"], c["n_head_kv"]
+        lw = ((H + 2 * HK) * hd * E + E * H * hd + 3 * F * E) * 18 // 32  # Q4_0 bytes of one layer
+        kv = HK * (sess.pos + 1) * hd * 2 * 2 * batch
+        gbs = (lw + kv) / (per_layer_us * 1e-6) / 1e9
+        hbm, kind = peaks()
+        out["layer_in_model"] = {"us_per_layer": round(per_layer_us, 2), "bytes_per_layer": int(lw + kv),
+                                 "gbs": round(gbs, 1), "frac": round(gbs / hbm, 4), "peak_kind": kind,
+                                 "what": "persistent layer kernel timed alone / layers"}
     sess.close()
-    return {"batch": batch, "prompt": prompt, "positions_timed": [pos0, pos0 + steps - 1],
-            "ms_per_step": round(ms.value / steps, 4), "value": round(batch * steps / (ms.value * 1e-3), 3),
-            "unit": UNIT, "launches_per_step": kernels,
-            "path": "one launch per op" if kernels != 4 else "persistent layer kernel"}
+    return out
 
 
 def gpu_arm(args):
@@ -619,8 +660,9 @@ def gpu_arm(args):
     cfg = dict(CFG_8B)
     B, K, W = args.batch, args.steps, args.warmup
     # tensor parallel: rank r holds 1/world of every matrix (column-parallel
-    # q/k/v/gate/up, row-parallel o/down, vocab-sharded lm head) and the
-    # exchange steps run on an NCCL communicator inside the step's graph
+    # q/k/v/gate/up, row-parallel o/down, vocab-sharded lm head); the row
+    # exchanges after o/down and the argmax merge go over NVLink peer memory
+    # (IPC-mapped buffers whose handles NCCL exchanges once at setup)
     model = Model(dev, cfg, tp_rank=rank if tp else 0, tp_size=world if tp else 1)
     model.synthesize(SEED)
     comm = None
@@ -747,7 +789,12 @@ def gpu_arm(args):
                        "layers": cfg["n_layer"], "hidden": cfg["n_embd"], "vocab": cfg["vocab"],
                        "kv_cache": "fp16",
                        "parallelism": ("single GPU" if world == 1 else
-                                       f"tp{world} (NVLink peer-memory all-reduce after o/down, vocab-sharded argmax)"
+                                       (f"tp{world}: rows exchanged over NVLink peer memory inside the "
+                                        f"persistent layer kernel after o and down, vocab-sharded lm head, "
+                                        f"argmax merged over peer memory (no collective library call per step)"
+                                        if sess.step_kernels == 3 else
+                                        f"tp{world}: peer-memory exchange kernel after o/down, NCCL all-gather "
+                                        f"for the argmax")
                                        if tp else f"{world} independent replicas"),
                        "l2": "no flush: 4.5 GB of weights per step exceed the 126 MB L2"},
             "e2e": {"value": round(jobs * B * K / (t_e2e * 1e-3), 3), "unit": UNIT,

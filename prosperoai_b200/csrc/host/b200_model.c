@@ -618,13 +618,13 @@ pai_status_t pai_b200_session_create(pai_b200_model_t *m, uint32_t batch, uint32
   if (!st) st = pai_b200_sync(ctx);
   free(tab_c);
   free(tab_s);
-  /* The layers of a step run as one persistent kernel when
-   * PAI_B200_PERSISTENT=1 (every rank of a tensor-parallel group must make
-   * the same choice); otherwise, and for shapes it does not take, one
+  /* The layers of a step run as one persistent kernel unless
+   * PAI_B200_PERSISTENT=0 (every rank of a tensor-parallel group must make
+   * the same choice); with it, and for shapes the kernel does not take, one
    * launch per op. */
   if (!st) {
     const char *e = getenv("PAI_B200_PERSISTENT");
-    if (e && e[0] == '1') {
+    if (!(e && e[0] == '0')) {
       st = make_plan(s);
       if (st == PAI_ERR_UNSUPPORTED) st = PAI_OK;
     }
