@@ -802,7 +802,7 @@ def gpu_arm(args):
             "gpu_launches": int(launches),
             "decode_path": (f"persistent layer kernel + lm head GEMV + argmax + token feedback "
                             f"({sess.step_kernels} launches per step, one CUDA graph)"
-                            if sess.step_kernels == 4 else
+                            if sess.step_kernels <= 4 else
                             f"one launch per op ({sess.step_kernels} per step, one CUDA graph)"),
             "roofline": roof,
             "gemv_roofline": gemv_roof if roof is not gemv_roof else None,

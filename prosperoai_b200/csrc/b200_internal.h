@@ -283,21 +283,19 @@ pai_status_t b200_launch_silu_glu_rows(pai_b200_ctx_t *ctx, uint64_t rows, uint3
  * its HBM, mapped into every other rank with CUDA IPC.
  *   header (B200_LAND_HDR bytes): u64 words [1] row exchanges this rank
  *   completed, [2] arrivals of greedy pairs (every rank adds 1 per step),
- *   [3] greedy exchanges this rank completed; from byte B200_LAND_FLAGS,
- *   u64 arrival stamps [rank][cta] of the row exchanges;
- *   row slots [2 parities][ranks][rows] fp32 (rows = batch x n_embd): the
- *   rows a rank reduced from its o/down partial sums, stored by that rank
- *   into slot [parity][rank] of every rank's buffer;
+ *   [3] greedy exchanges this rank completed;
+ *   row slots [2 parities][ranks][rows] u64 (rows = batch x n_embd): the
+ *   rows a rank reduced from its o/down partial sums, each an fp32 value in
+ *   the low word and the exchange's tag in the high word, stored by that
+ *   rank into slot [parity][rank] of every rank's buffer;
  *   pair slots [2 parities][ranks][8][2] fp32: each rank's (maximum, index)
  *   of its vocabulary shard per sequence. */
 #define B200_LAND_HDR 16384u
-#define B200_LAND_FLAGS 1024u
-#define B200_LAND_MAX_CTAS 192u
 static inline B200_HD uint64_t b200_land_bytes(uint32_t nranks, uint64_t rows) {
-  return B200_LAND_HDR + (2ull * nranks * rows + 2ull * nranks * 16u) * 4u;
+  return B200_LAND_HDR + 2ull * nranks * rows * 8u + 2ull * nranks * 16u * 4u;
 }
 static inline B200_HD uint64_t b200_land_pairs_off(uint32_t nranks, uint64_t rows) {
-  return B200_LAND_HDR + 2ull * nranks * rows * 4u;
+  return B200_LAND_HDR + 2ull * nranks * rows * 8u;
 }
 
 /* The matrices and norm gains of one layer (packed, this rank's shard). */

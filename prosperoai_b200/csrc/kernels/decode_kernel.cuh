@@ -153,15 +153,6 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t *p) {
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ uint64_t ld_acquire_sys64(const uint64_t *q) {
-  uint64_t v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(q) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_release_sys64(uint64_t *q, uint64_t v) {
-  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(q), "l"(v) : "memory");
-}
-
 __device__ __forceinline__ void raise_abort(const KP &p) {
   atomicExch(p.bar + 2, 1u);
   atomicExch(p.err, 1u);
@@ -723,41 +714,56 @@ __device__ __noinline__ void reduce_rows(const KP &p, const Shape &sh, const flo
 }
 
 __device__ __forceinline__ uint64_t *land_words(uint8_t *b) { return reinterpret_cast<uint64_t *>(b); }
-__device__ __forceinline__ float *land_rows(const KP &p, uint32_t r, uint32_t parity, uint32_t src) {
-  return reinterpret_cast<float *>(p.land[r] + B200_LAND_HDR) + ((size_t)parity * p.nranks + src) * p.batch * p.n_embd;
+// Row slot [parity][src] of rank r's landing buffer: batch x n_embd tagged words.
+__device__ __forceinline__ uint64_t *land_rows(const KP &p, uint32_t r, uint32_t parity, uint32_t src) {
+  return reinterpret_cast<uint64_t *>(p.land[r] + B200_LAND_HDR) + ((size_t)parity * p.nranks + src) * p.batch * p.n_embd;
+}
+__device__ __forceinline__ void st_relaxed_sys64(uint64_t *q, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(q), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_relaxed_sys64(const uint64_t *q) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(q) : "memory");
+  return v;
 }
 
-// Tensor parallelism: the same as reduce_rows with the sum over ranks. This
-// CTA's blocks of this rank's row sums go into slot [parity][rank] of every
-// rank's landing buffer; then the CTA stamps epoch e into flag [rank][cta] of
-// every rank, waits (bounded) for flag [r][cta] >= e of every rank (the same
-// CTA index of every rank handled the same blocks), and adds the ranks' rows
-// in rank order to x.
+// Tensor parallelism: the same as reduce_rows with the sum over ranks, by a
+// low-latency protocol. Every row value of this rank travels as one 8-byte
+// word (tag << 32 | value bits; tag = low 32 bits of the exchange count + 1,
+// so a word of an older exchange or the zeroed buffer never matches) stored
+// into slot [parity][this rank] of every rank's landing buffer (plain peer
+// stores over NVLink; an aligned 8-byte store arrives whole). The warp that
+// owns a 32-row block -- the same block -> warp map on every rank -- then
+// polls its own buffer for each rank's word of its rows (bounded, ends early
+// when another CTA raised the abort word) and adds the ranks' values in rank
+// order, so every rank holds the same bits. No fence, no flag round, no
+// barrier inside the exchange. A slot is reused two exchanges later, which
+// no rank reaches before every rank has read it: exchange e+1 needs every
+// rank's rows of e+1, which a rank writes only after its grid barrier that
+// follows its reading of e. Returns false (the same answer to every consumer
+// thread of the CTA) when a wait ran out or the launch was aborted.
 template <int CONS>
-__device__ __noinline__ bool exchange_rows(const KP &p, const Shape &sh, const float *gamma, uint64_t e, int c, int lane, int ctid,
-                              int nthr, volatile int *sflag) {
-  const uint32_t nb = p.n_embd / 32, parity = (uint32_t)(e & 1u);
-  for (uint32_t wb = blockIdx.x * CONS + c; wb < p.batch * nb; wb += gridDim.x * CONS) {
+__device__ __noinline__ bool exchange_rows(const KP &p, const Shape &sh, const float *gamma, uint64_t e, int c,
+                                           int lane, int ctid, int nthr, volatile int *sflag) {
+  const uint32_t nb = p.n_embd / 32, parity = (uint32_t)(e & 1u), tag = (uint32_t)(e + 1);
+  bool ok = true;
+  for (uint32_t wb = blockIdx.x * CONS + c; wb < p.batch * nb && ok; wb += gridDim.x * CONS) {
     const uint32_t b = wb / nb, blk = wb % nb, row = blk * 32 + lane;
+    const size_t at = (size_t)b * p.n_embd + row;
     const float v = row_sum<16, CONS>(p.part[1], sh, p.batch, b, row);
-    for (uint32_t q = 0; q < p.nranks; q++) land_rows(p, q, parity, p.rank)[(size_t)b * p.n_embd + row] = v;
-  }
-  cbar(nthr);  // this CTA's stores are issued
-  if (ctid == 0) {
-    bool ok = true;
-    __threadfence_system();
-    for (uint32_t q = 0; q < p.nranks; q++)
-      st_release_sys64(reinterpret_cast<uint64_t *>(p.land[q] + B200_LAND_FLAGS) +
-                           (size_t)p.rank * B200_LAND_MAX_CTAS + blockIdx.x,
-                       e + 1);
-    const uint64_t *fl = reinterpret_cast<const uint64_t *>(p.land[p.rank] + B200_LAND_FLAGS);
-    for (uint32_t q = 0; q < p.nranks && ok; q++) {
+    const uint64_t word = ((uint64_t)tag << 32) | __float_as_uint(v);
+    for (uint32_t q = 0; q < p.nranks; q++) st_relaxed_sys64(land_rows(p, q, parity, p.rank) + at, word);
+    const float xv = __ldcg(p.x + at);
+    float sum = 0.0f;
+    bool mine = true;
+    for (uint32_t q = 0; q < p.nranks && mine; q++) {  // rank order
+      const uint64_t *src = land_rows(p, p.rank, parity, q) + at;
+      uint64_t w = ld_relaxed_sys64(src);
       uint64_t t0 = 0;
-      for (uint32_t it = 0;; it++) {
-        if (ld_acquire_sys64(fl + (size_t)q * B200_LAND_MAX_CTAS + blockIdx.x) >= e + 1) break;
+      for (uint32_t it = 0; (uint32_t)(w >> 32) != tag; it++) {
         if ((it & 63u) == 0) {
           if (*(volatile uint32_t *)(p.bar + 2)) {
-            ok = false;
+            mine = false;
             break;
           }
           const uint64_t now = globaltimer_ns();
@@ -765,24 +771,22 @@ __device__ __noinline__ bool exchange_rows(const KP &p, const Shape &sh, const f
             t0 = now;
           } else if (now - t0 > p.wait_ns) {
             raise_abort(p);
-            ok = false;
+            mine = false;
             break;
           }
         }
+        w = ld_relaxed_sys64(src);
       }
+      const float vq = __uint_as_float((uint32_t)w);
+      sum = q == 0 ? vq : sum + vq;
     }
-    *sflag = ok ? 1 : 0;
+    ok = __all_sync(0xffffffffu, mine);
+    if (ok) finish_block(p, b, blk, __fadd_rn(xv, sum), gamma, lane);
   }
   cbar(nthr);
-  if (!*sflag) return false;
-  for (uint32_t wb = blockIdx.x * CONS + c; wb < p.batch * nb; wb += gridDim.x * CONS) {
-    const uint32_t b = wb / nb, blk = wb % nb, row = blk * 32 + lane;
-    const size_t at = (size_t)b * p.n_embd + row;
-    float s = __ldcg(land_rows(p, p.rank, parity, 0) + at);
-    for (uint32_t q = 1; q < p.nranks; q++) s += __ldcg(land_rows(p, p.rank, parity, q) + at);  // rank order
-    finish_block(p, b, blk, __fadd_rn(__ldcg(p.x + at), s), gamma, lane);
-  }
-  return true;
+  if (ctid == 0) *sflag = *(volatile uint32_t *)(p.bar + 2) ? 0 : 1;
+  cbar(nthr);
+  return *sflag != 0;
 }
 
 // ---- attention ---------------------------------------------------------------------------

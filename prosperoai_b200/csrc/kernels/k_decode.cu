@@ -85,10 +85,6 @@ extern "C" pai_status_t b200_decode_plan_create(pai_b200_ctx_t *ctx, const b200_
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, pl->device);
   pl->grid = (uint32_t)sms;
-  if (a->nranks > 1 && pl->grid > B200_LAND_MAX_CTAS) {
-    delete plan;
-    return b200_fail(PAI_ERR_UNSUPPORTED, "decode_plan: %u SMs exceed the landing flags", pl->grid);
-  }
   const uint32_t cons = (uint32_t)pl->cons, xpu = T == PAI_B200_Q4_K ? 2 : 1;
   b200dec::KP &k = pl->kp;
   const uint64_t dims[4][2] = {{a->n_qkv, E}, {E, a->k_o}, {2 * a->ffl, E}, {E, a->ffl}};
