@@ -168,8 +168,9 @@ __device__ inline bool grid_sync(const KP &p, uint32_t &epoch, int ctid, int nth
   if (ctid == 0) {
     epoch++;
     bool ok = true;
-    __threadfence();
-    atomicAdd(p.bar, 1u);
+    // publish the CTA's writes (ordered before this thread by the named
+    // barrier) at GPU scope, then arrive without waiting for a reply
+    asm volatile("fence.acq_rel.gpu;\n red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(p.bar) : "memory");
     const uint32_t target = epoch * gridDim.x;
     uint64_t t0 = 0;
     for (uint32_t it = 0;; it++) {
@@ -189,8 +190,7 @@ __device__ inline bool grid_sync(const KP &p, uint32_t &epoch, int ctid, int nth
         }
       }
     }
-    __threadfence();
-    *sflag = ok ? 1 : 0;
+    *sflag = ok ? 1 : 0;  // the acquire load that saw the count orders the reads after it
   }
   cbar(nthr);
   return *sflag != 0;
