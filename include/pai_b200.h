@@ -271,6 +271,12 @@ pai_status_t pai_b200_gemv_rmsnorm_f32(pai_b200_ctx_t *ctx, uint32_t type, uint6
  * relative (the benchmark's bar is max-abs-rel 2e-2). */
 pai_status_t pai_b200_gemm_q4_0_f32(pai_b200_ctx_t *ctx, uint64_t m, uint64_t n, uint64_t k,
                                     const float *x, const void *w, float *y);
+/* The same GEMM for any packed layer block type: PAI_B200_Q4_0, PAI_B200_Q8_0
+ * or PAI_B200_Q4_K (k a whole number of blocks: 32, 32, 256). Each weight is
+ * the reference's fp32 dequantised value (gguf.c's arithmetic) rounded once
+ * to bf16; same bar as the Q4_0 form. PAI_ERR_UNSUPPORTED for other types. */
+pai_status_t pai_b200_gemm_f32(pai_b200_ctx_t *ctx, uint32_t type, uint64_t m, uint64_t n, uint64_t k,
+                               const float *x, const void *w, float *y);
 
 /* v0 grouped-scale integer weights (models/quantize.h), read in place.
  * The weight is a [k][n] GEMM B operand (n contiguous), c[m][n] = a[m][k] x W.

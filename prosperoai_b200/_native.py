@@ -108,6 +108,7 @@ SIGNATURES = {
     "pai_b200_gemv_prepared_f32": (I32, [P, U32, U64, U64, U64, P, P, P, P]),
     "pai_b200_gemv_rmsnorm_f32": (I32, [P, U32, U64, U64, U64, P, P, P, F32, P, P]),
     "pai_b200_gemm_q4_0_f32": (I32, [P, U64, U64, U64, P, P, P]),
+    "pai_b200_gemm_f32": (I32, [P, U32, U64, U64, U64, P, P, P]),
     "pai_b200_gemm_w8_f32": (I32, [P, U64, U64, U64, P, P, P, U64, P]),
     "pai_b200_gemm_w4_f32": (I32, [P, U64, U64, U64, P, P, P, U64, P]),
     "pai_b200_gemm_v0_f32": (I32, [P, U32, U32, U64, U64, U64, P, P, P]),

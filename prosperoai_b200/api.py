@@ -148,6 +148,10 @@ class Device:
         """Y[m][n] = X[m][k] . W^T on the tensor cores (bf16 tiles, fp32 accumulate)."""
         check(load().pai_b200_gemm_q4_0_f32(self.ctx, m, w.n, w.k, x.ptr, w.ptr, y.ptr), "gemm_q4_0")
 
+    def gemm(self, w: PackedMatrix, x: Buffer, y: Buffer, m: int):
+        """The same GEMM for a packed Q4_0, Q8_0 or Q4_K matrix."""
+        check(load().pai_b200_gemm_f32(self.ctx, w.wtype, m, w.n, w.k, x.ptr, w.ptr, y.ptr), "gemm")
+
     def gemm_wq(self, bits: int, m: int, n: int, k: int, a: Buffer, w_q: Buffer, scales: Buffer,
                 group_size: int, c: Buffer):
         """pai_ref_gemm_w8_f32 / _w4_f32 semantics on the GPU ([k][n] int8 or nibbles)."""

@@ -15,11 +15,14 @@
  *     x   = x + h.Wdown              (residual fused)    :782-795
  *   logits = rmsnorm(x, output_norm).Wout; token = argmax :884-895
  *
- * Kernels per layer: each norm quantises x for the GEMV that consumes it;
- * RoPE, the cache append, attention and the chunk merge are one kernel
- * that also writes the o projection's quantised input; the gate/up GEMV
- * applies SiLU*up and quantises h for the down projection. So a layer is
- * 7 kernels: norm, qkv, attention, o (+x), norm, gate/up, down (+x).
+ * The decode step runs every layer in one persistent cooperative kernel
+ * (kernels/decode_kernel.cuh), then the lm head, the argmax and the token
+ * feedback. With PAI_B200_PERSISTENT=0 (or a shape that kernel does not
+ * take) a layer is 7 launches instead: each norm quantises x for the GEMV
+ * that consumes it; RoPE, the cache append, attention and the chunk merge
+ * are one kernel that also writes the o projection's quantised input; the
+ * gate/up GEMV applies SiLU*up and quantises h for the down projection:
+ * norm, qkv, attention, o (+x), norm, gate/up, down (+x).
  *
  * Host code only: every device step is a launcher from csrc/kernels.
  */
@@ -405,6 +408,7 @@ struct pai_b200_session {
   b200_decode_plan_t *plan; /* persistent decode kernel of the layers (NULL: one launch per op) */
   void *land[B200_TP_MAX_RANKS]; /* tensor parallelism: every rank's landing buffer (persistent path) */
   int failed;               /* a bounded device wait ran out: the session refuses further work */
+  int pf_gemm;              /* prefill layer matrices on the tensor-core GEMM (else the batched GEMV) */
   pai_b200_tp_t *tp; /* tensor-parallel communicator, NULL on one GPU */
   /* prefill scratch (allocated by the first prefill): rows of hidden state,
    * normed rows, q|k|v, attention output, gate|up, silu*up, o/down output,
@@ -618,6 +622,13 @@ pai_status_t pai_b200_session_create(pai_b200_model_t *m, uint32_t batch, uint32
   if (!st) st = pai_b200_sync(ctx);
   free(tab_c);
   free(tab_s);
+  /* Prefill layer matrices run on the tensor-core GEMM (bf16 tiles) unless
+   * PAI_B200_PREFILL_GEMM=0, which keeps the batched GEMV's per-row
+   * arithmetic (the decode step's). */
+  {
+    const char *e = getenv("PAI_B200_PREFILL_GEMM");
+    s->pf_gemm = !(e && e[0] == '0');
+  }
   /* The layers of a step run as one persistent kernel unless
    * PAI_B200_PERSISTENT=0 (every rank of a tensor-parallel group must make
    * the same choice); with it, and for shapes the kernel does not take, one
@@ -867,7 +878,8 @@ static pai_status_t prefill_alloc(pai_b200_session_t *s) {
 }
 
 /* Y[rows][n] = X[rows][k] . W^T over a packed layer matrix: the tcgen05
- * GEMM for Q4_0 weights, else the GEMV in groups of 8 rows (epi as in the
+ * GEMM (Q4_0, Q8_0, Q4_K), or with PAI_B200_PREFILL_GEMM=0 the GEMV in
+ * groups of 8 rows (epi as in the
  * decode step; residual adds Y's old value when epi is B200_EPI_RESIDUAL,
  * SILU_GLU writes n/2 values per row). */
 static pai_status_t rows_matmul(pai_b200_session_t *s, uint32_t type, uint32_t rows, uint64_t n, uint64_t k,
@@ -884,9 +896,9 @@ static pai_status_t rows_matmul(pai_b200_session_t *s, uint32_t type, uint32_t r
     if (!st) st = pai_b200_vecadd_f32(ctx, y, s->pf_tmp, y, (uint64_t)rows * n);
     return st;
   }
-  if (type == PAI_B200_Q4_0) {
+  if (s->pf_gemm) {
     float *dst = epi == B200_EPI_STORE ? y : (epi == B200_EPI_RESIDUAL ? s->pf_tmp : s->pf_gu);
-    st = pai_b200_gemm_q4_0_f32(ctx, rows, n, k, x, w, dst);
+    st = pai_b200_gemm_f32(ctx, type, rows, n, k, x, w, dst);
     if (!st && epi == B200_EPI_RESIDUAL) st = pai_b200_vecadd_f32(ctx, y, dst, y, (uint64_t)rows * n);
     if (!st && epi == B200_EPI_SILU_GLU) st = b200_launch_silu_glu_rows(ctx, rows, (uint32_t)(n / 2), dst, y);
     return st;

@@ -33,6 +33,7 @@
 
 #include "../b200_internal.h"
 #include "b200_device.cuh"
+#include "gemv_unit.cuh"
 
 namespace {
 
@@ -192,27 +193,124 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&v)[N]) {
   }
 }
 
+// Q8_0 and Q4_K: K order inside each 64-wide stage. 16-byte chunk 2c + b
+// (b = which of the stage's two 32-weight (sub-)blocks) holds elements
+// 4c..4c+3 and 16+4c..16+4c+3 of (sub-)block b, in that order: the bytes a
+// lane finds in chunks (row, 0) and (row, 1) of the packed piece (k_gemv.cu's
+// Q8_0 / Q4_K layouts), so no nibble or byte is moved between lanes.
+__host__ __device__ constexpr uint32_t kperm_nat(uint32_t c, uint32_t j) { return (j < 4 ? 0u : 16u) + 4u * c + (j & 3u); }
+
+// Per block type: bytes of one tile's codes (QB) and headers (SB) per K unit,
+// 64-wide stages per unit, raw-unit stages in flight.
+template <uint32_t T>
+struct GT;
+template <>
+struct GT<PAI_B200_Q4_0> {
+  static constexpr uint32_t QB = 1024, SB = 128;
+  static constexpr int SPU = 2, RAW = 3;
+};
+template <>
+struct GT<PAI_B200_Q8_0> {
+  static constexpr uint32_t QB = 2048, SB = 128;
+  static constexpr int SPU = 2, RAW = 2;
+};
+template <>
+struct GT<PAI_B200_Q4_K> {
+  static constexpr uint32_t QB = 2048, SB = 256;
+  static constexpr int SPU = 4, RAW = 2;  // one 256-weight super-block per unit
+};
+
 constexpr int kWorkers = 16;                      // dequantising warps, one weight tile each
 constexpr int kGThreadsWS = (kWorkers + 3) * 32;  // + raw-W producer, X producer, MMA issuer
-constexpr int kRawStages = 3;                     // packed-weight units in flight
-constexpr uint32_t kRawStage = 16 * 1024 + 16 * 128;  // one unit of the CTA's 16 tiles: codes, then headers
-constexpr uint32_t kSclBytes = kWorkers * 16 * 4 * 8;  // split scales of the current unit, per warp
-template <int BN>
-constexpr int kAStages = BN == 256 ? 2 : (BN == 128 ? 3 : 4);  // bf16 weight stages (shared memory bound)
-template <int BN>
-constexpr int kBStages = BN == 256 ? 3 : 4;  // bf16 activation stages
-template <int BN>
+template <uint32_t T>
+constexpr uint32_t kRawStage = 16 * (GT<T>::QB + GT<T>::SB);  // one unit of the CTA's 16 tiles: codes, then headers
+template <uint32_t T>
+constexpr uint32_t kSclBytes = T == PAI_B200_Q4_0 ? kWorkers * 16 * 4 * 8 : 0;  // Q4_0's split scales, per warp
+// bf16 weight / activation stages (shared memory bound; the 2-byte-code types
+// have raw units twice as large)
+template <uint32_t T, int BN>
+constexpr int kAStages = T == PAI_B200_Q4_0 ? (BN == 256 ? 2 : (BN == 128 ? 3 : 4)) : (BN >= 128 ? 2 : (BN == 64 ? 3 : 4));
+template <uint32_t T, int BN>
+constexpr int kBStages = T == PAI_B200_Q4_0 ? (BN == 256 ? 3 : 4) : (BN == 256 ? 2 : 4);
+template <uint32_t T, int BN>
 constexpr size_t gemm_smem_bytes() {
-  return 1024 + (size_t)kAStages<BN> * kAStage + (size_t)kBStages<BN> * BN * 128 + (size_t)kRawStages * kRawStage +
-         kSclBytes;
+  return 1024 + (size_t)kAStages<T, BN> * kAStage + (size_t)kBStages<T, BN> * BN * 128 +
+         (size_t)GT<T>::RAW * kRawStage<T> + kSclBytes<T>;
 }
 
-template <int BN>
-__global__ void __launch_bounds__(kGThreadsWS, 1) k_gemm_q4_0(GemmP p) {
+// Eight fp32 values -> one 16-byte chunk of bf16, each rounded once (RN).
+__device__ __forceinline__ uint4 bf16x8(const float (&v)[8]) {
+  uint4 o;
+  __nv_bfloat162 b0 = __floats2bfloat162_rn(v[0], v[1]), b1 = __floats2bfloat162_rn(v[2], v[3]);
+  __nv_bfloat162 b2 = __floats2bfloat162_rn(v[4], v[5]), b3 = __floats2bfloat162_rn(v[6], v[7]);
+  o.x = *reinterpret_cast<uint32_t *>(&b0);
+  o.y = *reinterpret_cast<uint32_t *>(&b1);
+  o.z = *reinterpret_cast<uint32_t *>(&b2);
+  o.w = *reinterpret_cast<uint32_t *>(&b3);
+  return o;
+}
+
+__device__ __forceinline__ uint32_t word_of(const uint4 &v, int i) {
+  return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
+}
+
+// A dequantising lane's part of one K unit of its tile, Q8_0 or Q4_K: the
+// packed chunks (row rl + 8h, bytes 16p..) j = 2h + p, and the headers of
+// rows rl and rl + 8.
+struct RawLane {
+  uint4 c[4];
+  uint4 hd[2];  // Q4_K: the 16-byte header; Q8_0: .x, .y = the 4 fp16 block scales
+};
+
+// Stage s of the unit into the swizzled bf16 stage: for each row (h) and
+// (sub-)block b of the stage, the lane's 8 weights, each the reference's
+// fp32 dequantised value (gguf.c's arithmetic, explicitly rounded) rounded
+// once to bf16.
+//   Q8_0 (gguf.c:680-693 form y = q * d; exact in fp32): stage s holds
+//   blocks 2s, 2s + 1.
+//   Q4_K (y = d*sc * q - dmin*m, gguf.c:750-761): stage s is 64-group s,
+//   sub-block 2s + b in the low (b = 0) or high (b = 1) nibbles.
+template <uint32_t T>
+__device__ __forceinline__ void dequant_stage_nat(uint8_t *stage, const uint32_t (&soff)[2][2], const RawLane &r,
+                                                  int s) {
+#pragma unroll
+  for (int h = 0; h < 2; h++)
+#pragma unroll
+    for (int b = 0; b < 2; b++) {
+      float v[8];
+      if constexpr (T == PAI_B200_Q8_0) {
+        const int i = 2 * s + b;
+        const uint32_t w0 = word_of(r.c[2 * h], i), w1 = word_of(r.c[2 * h + 1], i);
+        const uint32_t dw = i < 2 ? r.hd[h].x : r.hd[h].y;
+        const float d = __half2float(__ushort_as_half((uint16_t)((i & 1) ? (dw >> 16) : (dw & 0xFFFFu))));
+#pragma unroll
+        for (int t = 0; t < 4; t++) {
+          v[t] = __fmul_rn((float)(int8_t)(w0 >> (8 * t)), d);
+          v[4 + t] = __fmul_rn((float)(int8_t)(w1 >> (8 * t)), d);
+        }
+      } else {
+        float dsc, dmm;
+        gemv::Unit<PAI_B200_Q4_K>::scale_min(r.hd[h], 2 * s + b, dsc, dmm);
+        const uint32_t w0 = word_of(r.c[2 * h], s), w1 = word_of(r.c[2 * h + 1], s);
+#pragma unroll
+        for (int t = 0; t < 4; t++) {
+          v[t] = __fsub_rn(__fmul_rn(dsc, (float)((w0 >> (8 * t + 4 * b)) & 15u)), dmm);
+          v[4 + t] = __fsub_rn(__fmul_rn(dsc, (float)((w1 >> (8 * t + 4 * b)) & 15u)), dmm);
+        }
+      }
+      *reinterpret_cast<uint4 *>(stage + soff[h][b]) = bf16x8(v);
+    }
+}
+
+template <uint32_t T, int BN>
+__global__ void __launch_bounds__(kGThreadsWS, 1) k_gemm(GemmP p) {
   constexpr uint32_t kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;  // power of two for BN in {16, 64, 128, 256}
   constexpr uint32_t kBStage = BN * 128;
   constexpr uint32_t kIdesc = idesc_bf16(BN);
-  constexpr int SA = kAStages<BN>, SB = kBStages<BN>;
+  constexpr int SA = kAStages<T, BN>, SB = kBStages<T, BN>;
+  constexpr int kRawStages = GT<T>::RAW, SPU = GT<T>::SPU;
+  constexpr uint32_t QB = GT<T>::QB, HB = GT<T>::SB, kRaw = kRawStage<T>;
+  static_assert(gemm_smem_bytes<T, BN>() <= 227 * 1024, "shared memory of one CTA");
   constexpr uint32_t kECols = BN / 2;                      // epilogue columns (tokens) per warp
   constexpr uint32_t kEChunk = kECols < 16 ? kECols : 16;  // columns per TMEM load round
   constexpr uint32_t kFChunk = kECols < 16 ? kECols : 16;  // columns per round of the split-tile sum
@@ -221,8 +319,8 @@ __global__ void __launch_bounds__(kGThreadsWS, 1) k_gemm_q4_0(GemmP p) {
   uint8_t *gsm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~(uintptr_t)1023);
   uint8_t *a_st = gsm;                                // [SA][2 acc][128 rows][128 B]
   uint8_t *b_st = a_st + (size_t)SA * kAStage;        // [SB][BN rows][128 B]
-  uint8_t *r_st = b_st + (size_t)SB * kBStage;        // [kRawStages][16 KB codes | 2 KB headers]
-  uint4 *scl_all = reinterpret_cast<uint4 *>(r_st + (size_t)kRawStages * kRawStage);
+  uint8_t *r_st = b_st + (size_t)SB * kBStage;        // [kRawStages][16 tiles' codes | 16 tiles' headers]
+  uint4 *scl_all = reinterpret_cast<uint4 *>(r_st + (size_t)kRawStages * kRaw);
   __shared__ __align__(8) uint64_t rfull[kRawStages], rempty[kRawStages];
   __shared__ __align__(8) uint64_t afull[SA], aempty[SA], bfull[SB], bempty[SB];
   __shared__ __align__(8) uint64_t accfull, accempty;
@@ -271,11 +369,11 @@ __global__ void __launch_bounds__(kGThreadsWS, 1) k_gemm_q4_0(GemmP p) {
           ok = false;
           break;
         }
-        uint8_t *dst = r_st + (size_t)rs * kRawStage;
+        uint8_t *dst = r_st + (size_t)rs * kRaw;
         const size_t piece = (size_t)u * p.ntiles + tile0;
-        mbar_expect_tx(&rfull[rs], nv * (1024 + 128));
-        bulk_g2s(dst, p.qs + piece * 1024, nv * 1024, &rfull[rs]);
-        bulk_g2s(dst + 16 * 1024, p.sc + piece * 128, nv * 128, &rfull[rs]);
+        mbar_expect_tx(&rfull[rs], nv * (QB + HB));
+        bulk_g2s(dst, p.qs + piece * QB, nv * QB, &rfull[rs]);
+        bulk_g2s(dst + 16 * QB, p.sc + piece * HB, nv * HB, &rfull[rs]);
         if (++u == U) {  // next output tile: token tile fastest
           u = 0;
           if (++mt == p.mtiles) {
@@ -290,14 +388,14 @@ __global__ void __launch_bounds__(kGThreadsWS, 1) k_gemm_q4_0(GemmP p) {
     if (lane == 0) {
       uint32_t j = 0, u = (uint32_t)(w_begin % U), mt = first_tile % p.mtiles;
       for (uint64_t w = w_begin; w < w_end && ok; w++) {
-        for (uint32_t half = 0; half < 2; half++, j++) {
+        for (uint32_t hs = 0; hs < (uint32_t)SPU; hs++, j++) {
           const uint32_t s = j % SB;
           if (j >= (uint32_t)SB && !mbar_wait_spin(&bempty[s], ((j / SB) - 1) & 1u, p.wait_ns)) {
             ok = false;
             break;
           }
           mbar_expect_tx(&bfull[s], kBStage);
-          bulk_g2s(b_st + (size_t)s * kBStage, p.xp + ((size_t)mt * (2 * U) + 2 * u + half) * kBStage, kBStage,
+          bulk_g2s(b_st + (size_t)s * kBStage, p.xp + ((size_t)mt * (SPU * U) + SPU * u + hs) * kBStage, kBStage,
                    &bfull[s]);
         }
         if (++u == U) {
@@ -320,7 +418,7 @@ __global__ void __launch_bounds__(kGThreadsWS, 1) k_gemm_q4_0(GemmP p) {
           }
           tc_fence_after();
         }
-        for (uint32_t half = 0; half < 2; half++, j++) {
+        for (uint32_t hs = 0; hs < (uint32_t)SPU; hs++, j++) {
           const uint32_t s = j % SA, sb = j % SB;
           if (!mbar_wait_spin(&afull[s], (j / SA) & 1u, p.wait_ns) ||
               !mbar_wait_spin(&bfull[sb], (j / SB) & 1u, p.wait_ns)) {
@@ -332,7 +430,7 @@ __global__ void __launch_bounds__(kGThreadsWS, 1) k_gemm_q4_0(GemmP p) {
           // build the stage's two once, then step 32 bytes per K slice and 16 KB
           // to the second accumulator's rows
           const uint64_t ad = a_desc0 + (uint64_t)(s * (kAStage >> 4)), bd = b_desc0 + (uint64_t)(sb * (kBStage >> 4));
-          const bool fresh = seg_first && half == 0;
+          const bool fresh = seg_first && hs == 0;
           // alternate the two accumulators so consecutive MMAs are independent
 #pragma unroll
           for (int k = 0; k < kBK / 16; k++)
@@ -375,6 +473,16 @@ __global__ void __launch_bounds__(kGThreadsWS, 1) k_gemm_q4_0(GemmP p) {
       if (lane == 0) mbar_arrive(&afull[s]);  // one arrival per warp
       return true;
     };
+    // Q8_0 / Q4_K: stage hs of the unit, the same publication protocol
+    auto stage_nat = [&](uint32_t j, int hs, const RawLane &rl) -> bool {
+      const uint32_t s = j % SA;
+      if (j >= (uint32_t)SA && !mbar_wait_sleep(&aempty[s], ((j / SA) - 1) & 1u, p.wait_ns)) return false;
+      if (mine) dequant_stage_nat<T>(a_st + (size_t)s * kAStage, soff, rl, hs);
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&afull[s]);
+      return true;
+    };
     // epilogue slice of this warp: TMEM lanes 32 (w % 4).. of accumulator (w / 4) % 2 (features),
     // columns [w / 8 * BN / 2, + BN / 2) (tokens)
     const uint32_t g = warp & 3, acc = (warp >> 2) & 1, cbase = (warp >> 3) * kECols;
@@ -390,8 +498,27 @@ __global__ void __launch_bounds__(kGThreadsWS, 1) k_gemm_q4_0(GemmP p) {
         ok = false;
         break;
       }
-      const uint8_t *raw = r_st + (size_t)rs * kRawStage;
-      if (mine) {
+      const uint8_t *raw = r_st + (size_t)rs * kRaw;
+      if constexpr (T != PAI_B200_Q4_0) {
+        RawLane rl{};
+        if (mine) {
+#pragma unroll
+          for (int j = 0; j < 4; j++) rl.c[j] = *reinterpret_cast<const uint4 *>(raw + warp * QB + j * 512 + lane * 16);
+          const uint8_t *hp = raw + 16 * QB + warp * HB;
+          if constexpr (T == PAI_B200_Q8_0) {
+            const uint2 a = *reinterpret_cast<const uint2 *>(hp + (lane >> 2) * 8);
+            const uint2 b = *reinterpret_cast<const uint2 *>(hp + 64 + (lane >> 2) * 8);
+            rl.hd[0] = make_uint4(a.x, a.y, 0u, 0u);
+            rl.hd[1] = make_uint4(b.x, b.y, 0u, 0u);
+          } else {
+            rl.hd[0] = *reinterpret_cast<const uint4 *>(hp + (lane >> 2) * 16);
+            rl.hd[1] = *reinterpret_cast<const uint4 *>(hp + 128 + (lane >> 2) * 16);
+          }
+        }
+#pragma unroll
+        for (int hs = 0; hs < SPU; hs++)
+          if (ok) ok = stage_nat(SPU * i + hs, hs, rl);
+      } else if (mine) {
         // split the tile's 64 block scales once: lane l takes row l / 2, blocks 2 (l % 2) + {0, 1}
         const uint32_t dd = *reinterpret_cast<const uint32_t *>(raw + 16 * 1024 + warp * 128 + lane * 4);
         uint4 sp;
@@ -404,7 +531,9 @@ __global__ void __launch_bounds__(kGThreadsWS, 1) k_gemm_q4_0(GemmP p) {
         q[0] = *reinterpret_cast<const uint4 *>(pq);
         q[1] = *reinterpret_cast<const uint4 *>(pq + 512);
       }
-      ok = stage_half(2 * i, std::integral_constant<int, 0>{}) && stage_half(2 * i + 1, std::integral_constant<int, 1>{});
+      if constexpr (T == PAI_B200_Q4_0)
+        ok = stage_half(2 * i, std::integral_constant<int, 0>{}) &&
+             stage_half(2 * i + 1, std::integral_constant<int, 1>{});
       __syncwarp();
       if (lane == 0) mbar_arrive(&rempty[rs]);
       if (!ok) break;
@@ -524,7 +653,8 @@ __global__ void __launch_bounds__(kGThreadsWS, 1) k_gemm_q4_0(GemmP p) {
 
 // X fp32 [M][K] -> bf16 in the GEMM's operand layout: [token tile][K chunk of
 // 64][BN rows][128 B swizzled]; rows beyond M and columns beyond K are zero.
-template <int BN>
+// NAT: the K order of the Q8_0 / Q4_K stages (kperm_nat), else Q4_0's.
+template <int BN, bool NAT>
 __global__ void __launch_bounds__(256) k_gemm_xprep(const float *__restrict__ x, uint32_t m, uint32_t k,
                                                     uint32_t nkc, uint8_t *__restrict__ xp) {
   const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;  // one 8-element chunk
@@ -534,30 +664,24 @@ __global__ void __launch_bounds__(256) k_gemm_xprep(const float *__restrict__ x,
   const uint32_t mtiles = (m + BN - 1) / BN;
   if (row >= (uint64_t)mtiles * BN) return;
   const uint32_t kt = ch / 8, c = ch % 8;
-  // chunk c of the stage: block c & 1, packed word c >> 1, in kperm order
+  // chunk c of the stage: (sub-)block c & 1, packed word c >> 1, in the weights' K order
   const uint32_t kb = kt * 64 + (c & 1u) * 32;
   float v[8];
 #pragma unroll
   for (int j = 0; j < 8; j++) {
-    const uint32_t kk = kb + kperm(c >> 1, j);
+    const uint32_t kk = kb + (NAT ? kperm_nat(c >> 1, j) : kperm(c >> 1, j));
     v[j] = (row < m && kk < k) ? x[row * k + kk] : 0.0f;
   }
-  uint4 o;
-  __nv_bfloat162 b0 = __floats2bfloat162_rn(v[0], v[1]), b1 = __floats2bfloat162_rn(v[2], v[3]);
-  __nv_bfloat162 b2 = __floats2bfloat162_rn(v[4], v[5]), b3 = __floats2bfloat162_rn(v[6], v[7]);
-  o.x = *reinterpret_cast<uint32_t *>(&b0);
-  o.y = *reinterpret_cast<uint32_t *>(&b1);
-  o.z = *reinterpret_cast<uint32_t *>(&b2);
-  o.w = *reinterpret_cast<uint32_t *>(&b3);
+  const uint4 o = bf16x8(v);
   const uint32_t tt = (uint32_t)(row / BN), r = (uint32_t)(row % BN);
   uint8_t *dst = xp + ((size_t)tt * nkc + kt) * (BN * 128) + r * 128 + (((c ^ r) & 7u) << 4);
   *reinterpret_cast<uint4 *>(dst) = o;
 }
 
-template <int BN>
+template <uint32_t T, int BN>
 pai_status_t gemm_launch(pai_b200_ctx_t *ctx, uint32_t m, uint32_t n, uint32_t k, const float *x, const void *w,
                          float *y) {
-  const uint32_t nunits = (uint32_t)b200_units(PAI_B200_Q4_0, k), nkc = 2 * nunits;  // K chunks of 64
+  const uint32_t nunits = (uint32_t)b200_units(T, k), nkc = GT<T>::SPU * nunits;  // K chunks of 64
   const uint32_t mtiles = (m + BN - 1) / BN, ftiles = (n + kFT - 1) / kFT;
   const uint64_t tiles = (uint64_t)ftiles * mtiles, work = tiles * nunits;
   int sms = 148;
@@ -578,12 +702,12 @@ pai_status_t gemm_launch(pai_b200_ctx_t *ctx, uint32_t m, uint32_t n, uint32_t k
   if (st) return st;
   cudaStream_t s = (cudaStream_t)b200_ctx_stream(ctx);
   const uint64_t nchunks = (uint64_t)mtiles * BN * nkc * 8;
-  k_gemm_xprep<BN><<<(unsigned)((nchunks + 255) / 256), 256, 0, s>>>(x, m, k, nkc, (uint8_t *)xp);
+  k_gemm_xprep<BN, T != PAI_B200_Q4_0><<<(unsigned)((nchunks + 255) / 256), 256, 0, s>>>(x, m, k, nkc, (uint8_t *)xp);
   st = b200_launched(ctx, 1, "k_gemm_xprep");
   if (st) return st;
   GemmP p{};
   p.qs = (const uint8_t *)w;
-  p.sc = p.qs + b200_sc_offset(PAI_B200_Q4_0, n, k);
+  p.sc = p.qs + b200_sc_offset(T, n, k);
   p.xp = (const uint8_t *)xp;
   p.y = y;
   p.partial = partial;
@@ -596,32 +720,49 @@ pai_status_t gemm_launch(pai_b200_ctx_t *ctx, uint32_t m, uint32_t n, uint32_t k
   p.nunits = nunits;
   p.mtiles = mtiles;
   p.work = work;
-  const size_t smem = gemm_smem_bytes<BN>();
+  const size_t smem = gemm_smem_bytes<T, BN>();
   static SmemOptIn opt;
   st = b200_cuda(opt.ensure(b200_ctx_device(ctx), smem,
                             [](size_t b) {
-                              return cudaFuncSetAttribute(k_gemm_q4_0<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              return cudaFuncSetAttribute(k_gemm<T, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                           (int)b);
                             }),
                  "k_gemm smem attribute");
   if (st) return st;
-  k_gemm_q4_0<BN><<<grid, kGThreadsWS, smem, s>>>(p);
-  return b200_launched(ctx, 1, "k_gemm_q4_0");
+  k_gemm<T, BN><<<grid, kGThreadsWS, smem, s>>>(p);
+  return b200_launched(ctx, 1, "k_gemm");
+}
+
+template <uint32_t T>
+pai_status_t gemm_typed(pai_b200_ctx_t *ctx, uint32_t m, uint32_t n, uint32_t k, const float *x, const void *w,
+                        float *y) {
+  if (m <= 16) return gemm_launch<T, 16>(ctx, m, n, k, x, w, y);
+  if (m <= 64) return gemm_launch<T, 64>(ctx, m, n, k, x, w, y);
+  if (m <= 128) return gemm_launch<T, 128>(ctx, m, n, k, x, w, y);
+  return gemm_launch<T, 256>(ctx, m, n, k, x, w, y);
 }
 
 }  // namespace
 
-extern "C" pai_status_t pai_b200_gemm_q4_0_f32(pai_b200_ctx_t *ctx, uint64_t m, uint64_t n, uint64_t k,
-                                               const float *x, const void *w, float *y) {
+extern "C" pai_status_t pai_b200_gemm_f32(pai_b200_ctx_t *ctx, uint32_t type, uint64_t m, uint64_t n, uint64_t k,
+                                          const float *x, const void *w, float *y) {
   if (!ctx || !x || !w || !y) return b200_fail(PAI_ERR_INVALID_ARG, "gemm: NULL pointer");
-  if (m == 0 || n == 0 || k == 0 || k % 32)
-    return b200_fail(PAI_ERR_MISMATCH, "gemm: k=%llu is not a whole number of Q4_0 blocks", (unsigned long long)k);
+  if (type != PAI_B200_Q4_0 && type != PAI_B200_Q8_0 && type != PAI_B200_Q4_K)
+    return b200_fail(PAI_ERR_UNSUPPORTED, "gemm: block type %u", type);
+  if (m == 0 || n == 0 || k == 0 || k % b200_blk_elems(type))
+    return b200_fail(PAI_ERR_MISMATCH, "gemm: k=%llu is not a whole number of blocks", (unsigned long long)k);
   if (m > 0x7FFFFFFFull || n > 0x7FFFFFF0ull || k > 0x7FFFFFFFull || (n + kFT - 1) / kFT > 0x7FFFFFFFull ||
       (m + 15) / 16 > 65535 || m * n > (1ull << 40))
     return b200_fail(PAI_ERR_UNSUPPORTED, "gemm: shape too large");
   if ((uintptr_t)w & 255) return b200_fail(PAI_ERR_INVALID_ARG, "gemm: weights not 256-byte aligned");
-  if (m <= 16) return gemm_launch<16>(ctx, (uint32_t)m, (uint32_t)n, (uint32_t)k, x, w, y);
-  if (m <= 64) return gemm_launch<64>(ctx, (uint32_t)m, (uint32_t)n, (uint32_t)k, x, w, y);
-  if (m <= 128) return gemm_launch<128>(ctx, (uint32_t)m, (uint32_t)n, (uint32_t)k, x, w, y);
-  return gemm_launch<256>(ctx, (uint32_t)m, (uint32_t)n, (uint32_t)k, x, w, y);
+  switch (type) {
+    case PAI_B200_Q4_0: return gemm_typed<PAI_B200_Q4_0>(ctx, (uint32_t)m, (uint32_t)n, (uint32_t)k, x, w, y);
+    case PAI_B200_Q8_0: return gemm_typed<PAI_B200_Q8_0>(ctx, (uint32_t)m, (uint32_t)n, (uint32_t)k, x, w, y);
+    default: return gemm_typed<PAI_B200_Q4_K>(ctx, (uint32_t)m, (uint32_t)n, (uint32_t)k, x, w, y);
+  }
+}
+
+extern "C" pai_status_t pai_b200_gemm_q4_0_f32(pai_b200_ctx_t *ctx, uint64_t m, uint64_t n, uint64_t k,
+                                               const float *x, const void *w, float *y) {
+  return pai_b200_gemm_f32(ctx, PAI_B200_Q4_0, m, n, k, x, w, y);
 }

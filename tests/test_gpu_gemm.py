@@ -1,5 +1,5 @@
-"""GPU parity of the tcgen05 prefill GEMM (Q4_0 weights, bf16 tiles) against
-the oracle: every row of Y is the oracle's fp32 GEMV of the same dequantised
+"""GPU parity of the tcgen05 prefill GEMM (Q4_0, Q8_0 and Q4_K weights, bf16
+tiles) against the oracle: every row of Y is the oracle's fp32 GEMV of the same dequantised
 weights with that row of X (the reference GEMM's products in the same
 order). Bar: max-abs-rel <= 2e-2 per row, the benchmark's bar for bf16 prefill
 tiles; the bf16 rounding of X and of the weights puts the actual error near
@@ -55,27 +55,30 @@ def test_gemm_q4_0_config2_shape(dev):
     assert np.array_equal(y.download(np.float32).reshape(m, n).view(np.uint32), got.view(np.uint32))
 
 
-def dense_ref(blocks, n, k, x):
+def dense_ref(blocks, n, k, x, wtype=po.Q4_0):
     """Every row at once: X . W^T in fp32 (numpy) over the oracle's dequantised
     weights. Used to check ALL rows within the bar; the sampled rows below are
     checked against the oracle's own GEMV (the reference's product order)."""
-    w = po.dequant(po.Q4_0, blocks, n * k).reshape(n, k)
+    w = po.dequant(wtype, blocks, n * k).reshape(n, k)
     return x @ w.T
 
 
-def check_all_rows(dev, m, n, k, seed, oracle_rows):
+def check_all_rows(dev, m, n, k, seed, oracle_rows, wtype=po.Q4_0):
     rng = np.random.default_rng(seed)
-    blocks = quantize(po.Q4_0, (rng.standard_normal(n * k) * 0.02).astype(np.float32))
+    blocks = quantize(wtype, (rng.standard_normal(n * k) * 0.02).astype(np.float32))
     x = rng.standard_normal((m, k)).astype(np.float32)
-    w = PackedMatrix(dev, po.Q4_0, n, k, blocks)
+    w = PackedMatrix(dev, wtype, n, k, blocks)
     y = dev.alloc(m * n * 4)
-    dev.gemm_q4_0(w, dev.put(x), y, m)
+    if wtype == po.Q4_0:
+        dev.gemm_q4_0(w, dev.put(x), y, m)
+    else:
+        dev.gemm(w, dev.put(x), y, m)
     got = y.download(np.float32).reshape(m, n)
-    ref = dense_ref(blocks, n, k, x)
+    ref = dense_ref(blocks, n, k, x, wtype)
     row_err = np.max(np.abs(got - ref), axis=1) / np.max(np.abs(ref), axis=1)
     assert float(np.max(row_err)) <= TOL, (m, n, k, int(np.argmax(row_err)), float(np.max(row_err)))
     for r in oracle_rows:
-        o = po.gemv_q(po.Q4_0, n, k, blocks, x[r], threads=8)
+        o = po.gemv_q(wtype, n, k, blocks, x[r], threads=8)
         assert maxrel(got[r], o) <= TOL, (m, n, k, r, maxrel(got[r], o))
     return got
 
@@ -108,3 +111,45 @@ def test_gemm_config2_full_shape(dev, m):
     even split. All rows against the dense product, rows of every token tile
     against the oracle."""
     check_all_rows(dev, m, 14336, 4096, seed=40 + m, oracle_rows=tile_rows(m))
+
+
+SHAPES_Q8_Q4K = [(1, 256, 256), (16, 256, 4096), (5, 300, 512), (64, 1024, 1024), (100, 512, 768),
+                 (128, 2048, 4096), (300, 1000, 1280)]
+
+
+@pytest.mark.parametrize("wtype,m,n,k", [(t,) + sh for t in (po.Q8_0, po.Q4_K) for sh in SHAPES_Q8_Q4K] +
+                         [(po.Q8_0, 40, 272, 1312)])
+def test_gemm_q8_0_q4_k_against_oracle(dev, wtype, m, n, k):
+    """The same GEMM for Q8_0 (32-weight blocks, int8 codes) and Q4_K
+    (256-weight super-blocks, 6-bit sub-block scales and minimums): every row
+    against the dense product over the oracle's dequantised weights, rows of
+    every token tile against the oracle's GEMV. Shapes cover ragged M and N,
+    all four token-tile widths, and for Q8_0 a K that ends inside a 128-weight
+    unit (1312 = 41 blocks)."""
+    check_all_rows(dev, m, n, k, seed=m * 7 + n + k + wtype, oracle_rows=tile_rows(m), wtype=wtype)
+
+
+@pytest.mark.parametrize("wtype", [po.Q8_0, po.Q4_K])
+@pytest.mark.parametrize("m", [16, 512, 2048])
+def test_gemm_q8_0_q4_k_config2_shape(dev, wtype, m):
+    """Config 2's weight shape (14336 x 4096) with Q8_0 and Q4_K blocks; M =
+    2048 runs the persistent stream-K branch. All rows against the dense
+    product, rows of every token tile against the oracle; a second call
+    reproduces the first bit for bit."""
+    got = check_all_rows(dev, m, 14336, 4096, seed=60 + m + wtype, oracle_rows=tile_rows(m), wtype=wtype)
+    rng = np.random.default_rng(60 + m + wtype)
+    blocks = quantize(wtype, (rng.standard_normal(14336 * 4096) * 0.02).astype(np.float32))
+    x = rng.standard_normal((m, 4096)).astype(np.float32)
+    w = PackedMatrix(dev, wtype, 14336, 4096, blocks)
+    y = dev.alloc(m * 14336 * 4)
+    dev.gemm(w, dev.put(x), y, m)
+    assert np.array_equal(y.download(np.float32).reshape(m, 14336).view(np.uint32), got.view(np.uint32))
+
+
+def test_gemm_rejects_other_block_types_and_partial_super_blocks(dev):
+    from prosperoai_b200 import _native
+    L = _native.load()
+    x, y = dev.alloc(4 * 256), dev.alloc(4 * 256)
+    w = dev.alloc(1 << 16)
+    assert L.pai_b200_gemm_f32(dev.ctx, 6, 1, 256, 256, x.ptr, w.ptr, y.ptr) == -3  # PAI_ERR_UNSUPPORTED: a type it does not run
+    assert L.pai_b200_gemm_f32(dev.ctx, po.Q4_K, 1, 256, 128, x.ptr, w.ptr, y.ptr) == -6  # PAI_ERR_MISMATCH: k not whole super-blocks

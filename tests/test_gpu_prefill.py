@@ -2,16 +2,18 @@
 pass per layer (GEMMs over all rows, RoPE + fp16 K/V append for every
 position, causal attention over the cache) is equivalent to stepping it.
 
-- Q8_0 / Q4_K layers run the batched GEMV, whose per-row arithmetic is the
-  decode step's: the token after the prompt and 24 greedy decode steps after
-  it equal the oracle's stepped decode, for 1 and 2 sequences;
+- with the layer matrices on the batched GEMV (PAI_B200_PREFILL_GEMM=0),
+  whose per-row arithmetic is the decode step's: the token after the prompt
+  and 24 greedy decode steps after it equal the oracle's stepped decode, for
+  1 and 2 sequences (Q8_0, Q4_K layers);
 - a prompt prefilled in two calls, and one longer than a pass (several
   passes attending over the cache earlier passes filled), give the tokens
-  of the oracle;
-- Q4_0 layers run the tcgen05 GEMM with bf16 tiles: the hidden state after
-  the prompt is within 2e-2 (max-abs-rel) of the oracle's, and the next
-  token is the oracle's wherever the oracle's top-two logit gap exceeds the
-  error bound.
+  of the oracle (the same GEMV path: these check the prefill's positions,
+  cache layout and passes);
+- the default path, the tcgen05 GEMM with bf16 tiles, for Q4_0, Q8_0 and
+  Q4_K layers: the hidden state after the prompt is within 2e-2
+  (max-abs-rel) of the oracle's, and the next token is the oracle's
+  wherever the oracle's top-two logit gap exceeds the error bound.
 """
 import numpy as np
 import pytest
@@ -47,7 +49,8 @@ def gpu_decode(sess, first, steps):
 
 
 @pytest.mark.parametrize("wtype,batch", [(po.Q8_0, 1), (po.Q4_K, 2)])
-def test_prefill_then_decode_matches_stepped_oracle(dev, wtype, batch):
+def test_prefill_then_decode_matches_stepped_oracle(dev, wtype, batch, monkeypatch):
+    monkeypatch.setenv("PAI_B200_PREFILL_GEMM", "0")
     cfg = dict(SMALL, wtype=wtype)
     seed = 5100 + wtype
     w = synth_weights(dev, cfg, seed)
@@ -67,7 +70,8 @@ def test_prefill_then_decode_matches_stepped_oracle(dev, wtype, batch):
         assert [t[b] for t in got] == want, f"sequence {b}"
 
 
-def test_prefill_in_parts_and_in_several_passes(dev):
+def test_prefill_in_parts_and_in_several_passes(dev, monkeypatch):
+    monkeypatch.setenv("PAI_B200_PREFILL_GEMM", "0")
     cfg = dict(SMALL, wtype=po.Q8_0)
     seed = 5200
     w = synth_weights(dev, cfg, seed)
@@ -94,9 +98,10 @@ def test_prefill_in_parts_and_in_several_passes(dev):
         assert first[b] == want[0], f"sequence {b}"
 
 
-def test_prefill_q4_0_gemm_within_bf16_bound(dev):
-    cfg = dict(SMALL, wtype=po.Q4_0)
-    seed = 5300
+@pytest.mark.parametrize("wtype", [po.Q4_0, po.Q8_0, po.Q4_K])
+def test_prefill_gemm_within_bf16_bound(dev, wtype):
+    cfg = dict(SMALL, wtype=wtype)
+    seed = 5300 + wtype
     w = synth_weights(dev, cfg, seed)
     rng = np.random.default_rng(seed)
     P, max_ctx = 96, 128
