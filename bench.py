@@ -61,7 +61,7 @@ def tensor_peak():
         return 1590.0, "fallback"
 
 
-def prefill_gemm(dev, iters=12, ms=(16, 128, 512, 2048), shards=1):
+def prefill_gemm(dev, iters=12, ms=(16, 128, 512, 2048), shards=1, t=2):
     """Config 2: the Q4_0 prefill GEMM Y[M,14336] = X[M,4096] . W^T on the
     tcgen05 tensor cores (X f32 -> bf16 tiles, W dequantised to bf16 in
     shared memory, fp32 accumulate in TMEM), for M in 16/128/512/2048.
@@ -72,8 +72,10 @@ def prefill_gemm(dev, iters=12, ms=(16, 128, 512, 2048), shards=1):
     from prosperoai_b200 import _native
     from prosperoai_b200.api import Buffer
     L = _native.load()
-    # with shards > 1 this rank holds a column shard (N / shards output rows)
-    n, k, t = CFG_8B["n_ff"] // shards, CFG_8B["n_embd"], 2
+    # with shards > 1 this rank holds a column shard (N / shards output rows);
+    # t: the weights' block type (Q4_0 is config 2's; Q8_0 and Q4_K run the same GEMM)
+    n, k = CFG_8B["n_ff"] // shards, CFG_8B["n_embd"]
+    tname = {2: "Q4_0", 8: "Q8_0", 12: "Q4_K"}[t]
     rb = L.pai_b200_block_bytes(t, k)
     copies = 4 * shards
     tmp = dev.alloc(n * k * 4)
@@ -89,9 +91,9 @@ def prefill_gemm(dev, iters=12, ms=(16, 128, 512, 2048), shards=1):
     tmp.free()
     blk.free()
     peak, kind = tensor_peak()
-    out = {"workload": f"Q4_0 GEMM N={n} K=4096 (config 2{', column shard' if shards > 1 else ''}), "
+    out = {"workload": f"{tname} GEMM N={n} K=4096 (config 2{', column shard' if shards > 1 else ''}), "
                        "bf16 tiles, fp32 accumulate",
-           "kernel": "k_gemm (tcgen05.mma kind::f16, TMEM accumulators) + k_gemm_xprep",
+           "kernel": f"k_gemm<{tname}> (tcgen05.mma kind::f16, TMEM accumulators) + k_gemm_xprep",
            "peak_tflops": peak, "peak_kind": kind,
            "l2": f"{copies} rotating weight copies ({copies * n * rb / 1e6:.0f} MB)",
            "by_m": {}}
@@ -102,12 +104,11 @@ def prefill_gemm(dev, iters=12, ms=(16, 128, 512, 2048), shards=1):
         x = dev.put(np.random.default_rng(m).standard_normal((m, k)).astype(np.float32))
         y = dev.alloc(m * n * 4)
         for i in range(4):
-            _native.check(L.pai_b200_gemm_q4_0_f32(dev.ctx, m, n, k, x.ptr, mats[i % copies].ptr,
-                                                   y.ptr), "gemm")
+            _native.check(L.pai_b200_gemm_f32(dev.ctx, t, m, n, k, x.ptr, mats[i % copies].ptr, y.ptr), "gemm")
         dev.sync()
         L.pai_b200_event_record(dev.ctx, e0)
         for i in range(iters):
-            L.pai_b200_gemm_q4_0_f32(dev.ctx, m, n, k, x.ptr, mats[i % copies].ptr, y.ptr)
+            L.pai_b200_gemm_f32(dev.ctx, t, m, n, k, x.ptr, mats[i % copies].ptr, y.ptr)
         L.pai_b200_event_record(dev.ctx, e1)
         ms = C.c_float()
         _native.check(L.pai_b200_event_elapsed(e0, e1, C.byref(ms)), "elapsed")
@@ -767,6 +768,8 @@ def gpu_arm(args):
         roof = layer_roof if sess.step_kernels == 4 else gemv_roof
         if gemm is None and not args.no_roofline:
             gemm = prefill_gemm(dev)
+            # the same GEMM with the other layer block types (prefill of Q8_0 / Q4_K models)
+            gemm["other_types"] = [prefill_gemm(dev, ms=(128, 512, 2048), t=t) for t in (8, 12)]
         sweep = None if args.no_roofline else gemv_sweep(dev, hbm, kind)
         v0 = None if args.no_roofline else v0_sweep(dev, hbm, kind)
         cpu = None if args.no_cpu_baseline else cpu_baseline_port(dev)
