@@ -77,8 +77,20 @@ namespace b200dec {
 using namespace gemv;
 
 constexpr int kStages = 4;
-// bytes of one ring stage: the largest of U units x CONS tiles x (codes +
-// headers) over the block types (Q4_0: 2 x 1152, Q8_0: 2176, Q4_K: 2304)
+// Tiles per consumer warp and K units per ring stage: with two or more
+// vector pairs, Q4_0 gives each warp two tiles (one unit per stage), so a
+// warp reads a stage's activations -- four times the weights' bytes at
+// batch 8 -- once for both (measured: 8 % off the batch-8 step). At batch
+// 1-2 the larger row groups would double the splits the residual phases add
+// up, which costs more than it saves; Q8_0 and Q4_K keep one tile (a
+// two-tile stage would not fit the ring).
+template <uint32_t T, int NT>
+constexpr int kTPW = (T == PAI_B200_Q4_0 && NT > 1) ? 2 : 1;
+template <uint32_t T, int NT>
+constexpr int kUPS = kTPW<T, NT> == 2 ? 1 : gemv::Unit<T>::U;
+// bytes of one ring stage: the largest of units x tiles x (codes + headers)
+// over the block types (Q4_0: 1 x 2 CONS x 1152, Q8_0: CONS x 2176, Q4_K:
+// CONS x 2304)
 template <int CONS>
 constexpr uint32_t kStageBytes = CONS * 2304u;
 constexpr uint32_t kHD = 128;
@@ -88,7 +100,8 @@ enum { M_QKV = 0, M_O = 1, M_GU = 2, M_DOWN = 3 };
 
 // Shape and work split of one layer-matrix kind (the same for every layer).
 struct Shape {
-  uint32_t n, k, units, ntiles, ngroups, npad, gw, maxseg, cons;
+  uint32_t n, k, units, ntiles, ngroups, npad, gw, maxseg;
+  uint32_t gt;      // 16-row tiles per row group (consumer warps x tiles per warp)
   uint32_t tab;     // first entry of this shape's groups in the split-count table
   uint64_t sc_off;  // byte offset of the header plane in the packed matrix
 };
@@ -235,7 +248,7 @@ template <int CH, int CONS>
 __device__ __forceinline__ RowRef row_load(const float *part, const Shape &sh, uint32_t batch, uint32_t b,
                                            uint32_t row, float (&v)[CH]) {
   RowRef r;
-  r.nseg = s_nseg[sh.tab + row / (16u * CONS)];
+  r.nseg = s_nseg[sh.tab + row / (16u * sh.gt)];
   r.q = part + (size_t)b * sh.npad + row;
   const size_t stride = (size_t)batch * sh.npad;
 #pragma unroll
@@ -304,23 +317,70 @@ __device__ __forceinline__ Sub sub_at(const Shape &sh, uint32_t pos, uint32_t r1
   return s;
 }
 
+// Q4_0, two consecutive 16-row tiles of one K unit (codes at qs and
+// qs + 1024, headers at sc and sc + 128; the layout of gemv_unit.cuh's
+// Unit<Q4_0>): the activation digits and their scale products are loaded and
+// formed once and used for both tiles. Per tile the arithmetic is
+// Unit<Q4_0>::compute's, in the same order.
+template <int NT>
+__device__ __forceinline__ void q4_0_two_tiles(const uint8_t *qs, const uint8_t *sc, const XS &xs, uint32_t qq,
+                                               int lane, float (&yr)[2][NT], float (&yr8)[2][NT]) {
+  XOp x[NT];
+#pragma unroll
+  for (int nt = 0; nt < NT; nt++) load_x(xs, nt, qq, lane, x[nt]);
+  uint4 a0[2], a1[2];
+  uint2 d0[2], d1[2];
+#pragma unroll
+  for (int t = 0; t < 2; t++) {
+    a0[t] = *reinterpret_cast<const uint4 *>(qs + t * 1024 + lane * 16);
+    a1[t] = *reinterpret_cast<const uint4 *>(qs + t * 1024 + 512 + lane * 16);
+    d0[t] = *reinterpret_cast<const uint2 *>(sc + t * 128 + (lane >> 2) * 8);
+    d1[t] = *reinterpret_cast<const uint2 *>(sc + t * 128 + 64 + (lane >> 2) * 8);
+  }
+  const float lscale = (lane & 1) ? (1.0f / 256.0f) : 256.0f;
+  const float cmul = (lane & 1) ? 0.0f : 8.0f;  // the -8 offset of Q4_0 codes, once per lane pair
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    float sl[NT], cr[NT];
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++) {
+      sl[nt] = comp(x[nt].sb, i) * lscale;
+      cr[nt] = comp(x[nt].sx, i) * cmul;
+    }
+#pragma unroll
+    for (int t = 0; t < 2; t++) {
+      const uint32_t wr = comp(a0[t], i), wr8 = comp(a1[t], i);
+      const uint32_t A0 = wr & M4, A1 = wr8 & M4, A2 = (wr >> 4) & M4, A3 = (wr8 >> 4) & M4;
+      const float dr = half_at(d0[t], i), dr8 = half_at(d1[t], i);
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++) {
+        int acc[4];
+        mma_u8s8(acc, A0, A1, A2, A3, comp(x[nt].lo, i), comp(x[nt].hi, i));
+        yr[t][nt] = fmaf(dr, fmaf(sl[nt], fold(acc[0], acc[1]), -cr[nt]), yr[t][nt]);
+        yr8[t][nt] = fmaf(dr8, fmaf(sl[nt], fold(acc[2], acc[3]), -cr[nt]), yr8[t][nt]);
+      }
+    }
+  }
+}
+
 // Producer: stream the weights of the CTA's range of one GEMV phase into the
 // ring, one stage per U units of a sub-item. Returns false when a wait for
 // a free stage ran out.
-template <uint32_t T, int CONS>
+template <uint32_t T, int NT, int CONS>
 __device__ bool produce(const KP &p, int k, const uint8_t *w, uint8_t *ring, uint64_t *full, uint64_t *empty,
                         uint32_t &fill) {
   using Un = Unit<T>;
-  constexpr int U = Un::U;
-  constexpr uint32_t GQ = CONS * Un::QB, GS = CONS * Un::SB;
+  constexpr int U = kUPS<T, NT>, GT = CONS * kTPW<T, NT>;
+  constexpr uint32_t GQ = GT * Un::QB, GS = GT * Un::SB;
+  static_assert(U * (GQ + GS) <= kStageBytes<CONS>, "ring stage");
   const Shape &sh = p.sh[k];
   const uint8_t *qs = w, *sc = w + sh.sc_off;
   const uint32_t r0 = s_rng[k].r0, r1 = s_rng[k].r1;
   for (uint32_t pos = r0; pos < r1;) {
     const Sub s = sub_at(sh, pos, r1);
     pos += s.u1 - s.u0;
-    const uint32_t nv = min((uint32_t)CONS, sh.ntiles - s.g * CONS);  // tiles present in the group
-    const size_t tile0 = (size_t)s.g * CONS;
+    const uint32_t nv = min((uint32_t)GT, sh.ntiles - s.g * GT);  // tiles present in the group
+    const size_t tile0 = (size_t)s.g * GT;
     for (uint32_t ua = s.u0; ua < s.u1; ua += U) {
       const uint32_t ub = min(s.u1, ua + U), slot = fill % kStages;
       if (fill >= (uint32_t)kStages && !mbar_wait(&empty[slot], ((fill / kStages) - 1) & 1u, p.wait_ns)) return false;
@@ -538,7 +598,7 @@ __device__ __forceinline__ void silu_chunk(const KP &p, uint32_t b, uint32_t o0,
   constexpr int CH = 4;  // splits loaded at once (a gate|up group spans few CTAs)
   const uint32_t o = o0 + 4 * lane, oc = min(o, k - 4);
   const uint32_t grow = (oc / 8) * 16 + oc % 8;
-  const uint32_t nseg = s_nseg[gu.tab + grow / (16u * CONS)];
+  const uint32_t nseg = s_nseg[gu.tab + grow / (16u * gu.gt)];
   const float4 *q = reinterpret_cast<const float4 *>(p.part[0] + (size_t)b * gu.npad + grow);
   float4 gv[CH], uv[CH];
 #pragma unroll
@@ -611,8 +671,8 @@ __device__ void consume(const KP &p, int k, int xsrc, float *part, uint8_t *ring
                         uint64_t *empty, uint32_t &seq, uint8_t *area, float *scratch, float *scales, int c,
                         int lane, int ctid, int nthr, volatile int *failed) {
   using Un = Unit<T>;
-  constexpr int U = Un::U, XPU = Un::XPU;
-  constexpr uint32_t GQ = CONS * Un::QB, GS = CONS * Un::SB;
+  constexpr int U = kUPS<T, NT>, XPU = Un::XPU, TPW = kTPW<T, NT>, GT = CONS * TPW;
+  constexpr uint32_t GQ = GT * Un::QB, GS = GT * Un::SB;
   const Shape &sh = p.sh[k];
   const uint32_t r0 = s_rng[k].r0, r1 = s_rng[k].r1, g0 = s_rng[k].g0, split0 = s_rng[k].split0;
   if (r0 >= r1) return;
@@ -630,16 +690,18 @@ __device__ void consume(const KP &p, int k, int xsrc, float *part, uint8_t *ring
   cbar(nthr);
   const uint32_t r = lane >> 2, vsel = (lane & 3) >> 1;
   const bool holder = (lane & 1) == 0;
-  float yr[NT], yr8[NT];
+  float yr[TPW][NT], yr8[TPW][NT];
   bool bad = false;
   for (uint32_t pos = r0; pos < r1;) {
     const Sub s = sub_at(sh, pos, r1);
     const uint32_t eoff = pos - r0;  // entry of unit s.u0 when not resident
     pos += s.u1 - s.u0;
-    const uint32_t tile = s.g * CONS + c;
-    const bool active = tile < sh.ntiles;
+    const uint32_t tile0 = s.g * GT + c * TPW;  // the warp's first tile of the group
+    const bool active = tile0 < sh.ntiles;
 #pragma unroll
-    for (int nt = 0; nt < NT; nt++) yr[nt] = yr8[nt] = 0.f;
+    for (int t = 0; t < TPW; t++)
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++) yr[t][nt] = yr8[t][nt] = 0.f;
     for (uint32_t ua = s.u0; ua < s.u1; ua += U) {
       const uint32_t slot = seq % kStages, par = (seq / kStages) & 1u;
       if (!bad) {
@@ -658,8 +720,11 @@ __device__ void consume(const KP &p, int k, int xsrc, float *part, uint8_t *ring
           const uint32_t u = ua + uu;
           if (u < s.u1) {
             const uint32_t e = a.resident ? u : eoff + (u - s.u0);
-            Un::template compute<NT>(st + uu * GQ + c * Un::QB, st + U * GQ + uu * GS + c * Un::SB, a.xs, e * XPU,
-                                     lane, yr, yr8);
+            const uint8_t *q = st + uu * GQ + c * TPW * Un::QB, *h = st + U * GQ + uu * GS + c * TPW * Un::SB;
+            if constexpr (TPW == 2)
+              q4_0_two_tiles<NT>(q, h, a.xs, e * XPU, lane, yr, yr8);
+            else
+              Un::template compute<NT>(q, h, a.xs, e * XPU, lane, yr[0], yr8[0]);
           }
         }
       }
@@ -671,14 +736,18 @@ __device__ void consume(const KP &p, int k, int xsrc, float *part, uint8_t *ring
     // this CTA's segment of group g: its partial row sums
     const uint32_t split = s.g == g0 ? split0 : 0u;
 #pragma unroll
-    for (int nt = 0; nt < NT; nt++) {  // lane pairs (c, c^1) hold the two halves of one sum
-      const float ya = yr[nt] + __shfl_xor_sync(0xffffffffu, yr[nt], 1);
-      const float yb = yr8[nt] + __shfl_xor_sync(0xffffffffu, yr8[nt], 1);
-      const uint32_t vec = 2 * nt + vsel;
-      if (holder && vec < p.batch) {
-        float *pp = part + ((size_t)split * p.batch + vec) * sh.npad + (size_t)tile * 16 + r;
-        pp[0] = ya;
-        pp[8] = yb;
+    for (int t = 0; t < TPW; t++) {
+      const uint32_t tile = tile0 + t;
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++) {  // lane pairs (c, c^1) hold the two halves of one sum
+        const float ya = yr[t][nt] + __shfl_xor_sync(0xffffffffu, yr[t][nt], 1);
+        const float yb = yr8[t][nt] + __shfl_xor_sync(0xffffffffu, yr8[t][nt], 1);
+        const uint32_t vec = 2 * nt + vsel;
+        if (holder && vec < p.batch && tile < sh.ntiles) {
+          float *pp = part + ((size_t)split * p.batch + vec) * sh.npad + (size_t)tile * 16 + r;
+          pp[0] = ya;
+          pp[8] = yb;
+        }
       }
     }
   }
@@ -706,10 +775,10 @@ __device__ __noinline__ void reduce_rows(const KP &p, const Shape &sh, const flo
   const uint32_t nb = p.n_embd / 32;
   for (uint32_t wb = blockIdx.x * CONS + c; wb < p.batch * nb; wb += gridDim.x * CONS) {
     const uint32_t b = wb / nb, blk = wb % nb, row = blk * 32 + lane;
-    float pv[16];
-    const RowRef rr = row_load<16, CONS>(p.part[1], sh, p.batch, b, row, pv);
+    float pv[32];
+    const RowRef rr = row_load<32, CONS>(p.part[1], sh, p.batch, b, row, pv);
     const float xv = __ldcg(p.x + (size_t)b * p.n_embd + row);
-    finish_block(p, b, blk, __fadd_rn(xv, row_finish<16>(rr, pv, p.batch, sh.npad)), gamma, lane);
+    finish_block(p, b, blk, __fadd_rn(xv, row_finish<32>(rr, pv, p.batch, sh.npad)), gamma, lane);
   }
 }
 
@@ -750,7 +819,7 @@ __device__ __noinline__ bool exchange_rows(const KP &p, const Shape &sh, const f
   for (uint32_t wb = blockIdx.x * CONS + c; wb < p.batch * nb && ok; wb += gridDim.x * CONS) {
     const uint32_t b = wb / nb, blk = wb % nb, row = blk * 32 + lane;
     const size_t at = (size_t)b * p.n_embd + row;
-    const float v = row_sum<16, CONS>(p.part[1], sh, p.batch, b, row);
+    const float v = row_sum<32, CONS>(p.part[1], sh, p.batch, b, row);
     const uint64_t word = ((uint64_t)tag << 32) | __float_as_uint(v);
     for (uint32_t q = 0; q < p.nranks; q++) st_relaxed_sys64(land_rows(p, q, parity, p.rank) + at, word);
     const float xv = __ldcg(p.x + at);
@@ -843,7 +912,7 @@ __device__ __noinline__ void attention(const KP &p, uint32_t layer, int warp, in
     }
     // q | k | v rows of this kv head from the q|k|v partial sums
     for (uint32_t i0 = ctid; i0 < R; i0 += 2 * nthr) {
-      float va[8], vb[8];
+      float va[16], vb[16];
       const uint32_t i1 = min(i0 + nthr, R - 1);
       const uint32_t rowa = i0 < G * kHD ? h0 * kHD + i0
                                          : (i0 < (G + 1) * kHD ? (p.h + kvh) * kHD + i0 - G * kHD
@@ -851,10 +920,10 @@ __device__ __noinline__ void attention(const KP &p, uint32_t layer, int warp, in
       const uint32_t rowb = i1 < G * kHD ? h0 * kHD + i1
                                          : (i1 < (G + 1) * kHD ? (p.h + kvh) * kHD + i1 - G * kHD
                                                                : (p.h + p.hk + kvh) * kHD + i1 - (G + 1) * kHD);
-      const RowRef ra = row_load<8, CONS>(part, sq, p.batch, b, rowa, va);
-      const RowRef rb = row_load<8, CONS>(part, sq, p.batch, b, rowb, vb);
-      const float xa = row_finish<8>(ra, va, p.batch, sq.npad);
-      const float xb = row_finish<8>(rb, vb, p.batch, sq.npad);
+      const RowRef ra = row_load<16, CONS>(part, sq, p.batch, b, rowa, va);
+      const RowRef rb = row_load<16, CONS>(part, sq, p.batch, b, rowb, vb);
+      const float xa = row_finish<16>(ra, va, p.batch, sq.npad);
+      const float xb = row_finish<16>(rb, vb, p.batch, sq.npad);
       // q rows go to the padded quarter layout, k and v rows after them
       if (i0 < G * kHD) qs[(i0 / kHD) * 4 * kQP + ((i0 % kHD) / 32) * kQP + i0 % 32] = xa;
       else kvs[i0 - G * kHD] = xa;
@@ -1084,7 +1153,7 @@ __global__ void __launch_bounds__((CONS + 1) * 32, 1) k_decode(const __grid_cons
     uint32_t fill = 0;
     bool ok = true;
     for (uint32_t l = 0; l < p.n_layer && ok; l++)
-      for (int k = 0; k < 4 && ok; k++) ok = produce<T, CONS>(p, k, p.layers[l].w[k], ring, full, empty, fill);
+      for (int k = 0; k < 4 && ok; k++) ok = produce<T, NT, CONS>(p, k, p.layers[l].w[k], ring, full, empty, fill);
     if (!ok) {
       // a wait for a free stage ran out: raise the error and let the copies
       // already issued land (bounded) before this thread leaves

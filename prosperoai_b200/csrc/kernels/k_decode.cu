@@ -20,17 +20,17 @@ using b200dec::kHD;
 using b200dec::kStages;
 using b200dec::Shape;
 
-// Work split of an n x k matrix of type t over `grid` CTAs of `cons` tiles per
+// Work split of an n x k matrix of type t over `grid` CTAs of `gt` tiles per
 // row group (decode_kernel.cuh: phase_range, group_split).
-Shape make_shape(uint32_t t, uint64_t n, uint64_t k, uint32_t cons, uint32_t grid, uint64_t &max_range) {
+Shape make_shape(uint32_t t, uint64_t n, uint64_t k, uint32_t gt, uint32_t grid, uint64_t &max_range) {
   Shape s{};
   s.n = (uint32_t)n;
   s.k = (uint32_t)k;
   s.units = (uint32_t)b200_units(t, k);
   s.ntiles = (uint32_t)b200_ntiles(n);
-  s.ngroups = (s.ntiles + cons - 1) / cons;
+  s.ngroups = (s.ntiles + gt - 1) / gt;
   s.npad = s.ntiles * 16;
-  s.cons = cons;
+  s.gt = gt;
   s.sc_off = b200_sc_offset(t, n, k);
   const uint64_t total = (uint64_t)s.ngroups * s.units;
   s.gw = (uint32_t)std::min<uint64_t>(grid, total);
@@ -93,7 +93,9 @@ extern "C" pai_status_t b200_decode_plan_create(pai_b200_ctx_t *ctx, const b200_
   uint32_t tab = 0;
   for (int i = 0; i < 4; i++) {
     uint64_t max_range = 0;
-    k.sh[i] = make_shape(T, dims[i][0], dims[i][1], cons, pl->grid, max_range);
+    // tiles per consumer warp: decode_kernel.cuh's kTPW<T, NT>
+    const uint32_t tpw = (T == PAI_B200_Q4_0 && pl->nt > 1) ? 2u : 1u;
+    k.sh[i] = make_shape(T, dims[i][0], dims[i][1], cons * tpw, pl->grid, max_range);
     k.sh[i].tab = tab;
     tab += k.sh[i].ngroups;
     part_floats[i & 1] = std::max<uint64_t>(part_floats[i & 1], (uint64_t)k.sh[i].maxseg * B * k.sh[i].npad);
