@@ -712,6 +712,11 @@ def gpu_arm(args):
     # e2e: the same steps through the host-buffer C ABI call
     tok = sess.tokens()
     dev.sync()
+    if pg:
+        # every rank starts the e2e loop together: the clock sampler's exit above
+        # takes a variable fraction of a second per rank, and under tensor
+        # parallelism a rank's first step waits for the last rank to begin
+        pg.barrier()
     L.pai_b200_event_record(dev.ctx, e0)
     w0 = time.perf_counter()
     for _ in range(K):
