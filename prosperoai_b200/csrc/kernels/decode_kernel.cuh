@@ -756,16 +756,16 @@ __device__ void consume(const KP &p, int k, int xsrc, float *part, uint8_t *ring
 // ---- reduce phases: residual add, block sums of squares, the next norm's operand -----------
 
 // x block (32 rows) of vector b: v = x + sum; writes x, the block's sum of
-// squares (fixed shuffle order) and v * gamma quantised (unscaled). One warp.
-__device__ __forceinline__ void finish_block(const KP &p, uint32_t b, uint32_t blk, float v, const float *gamma,
-                                             int lane) {
+// squares (fixed shuffle order) and v * gamma quantised (unscaled); g is the
+// lane's gain, loaded by the caller with its other operands. One warp.
+__device__ __forceinline__ void finish_block(const KP &p, uint32_t b, uint32_t blk, float v, float g, int lane) {
   const uint32_t row = blk * 32 + lane;
   p.x[(size_t)b * p.n_embd + row] = v;
   double sq = __dmul_rn((double)v, (double)v);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) sq = __dadd_rn(sq, __shfl_xor_sync(0xffffffffu, sq, o));
   if (lane == 0) p.ssq[(size_t)b * (p.n_embd / 32) + blk] = sq;
-  xq_store_block(p.xqn, b, blk, __fmul_rn(v, __ldg(gamma + row)));
+  xq_store_block(p.xqn, b, blk, __fmul_rn(v, g));
 }
 
 // One GPU: x += the o or down GEMV's row sums (the residual adds of
@@ -777,8 +777,8 @@ __device__ __noinline__ void reduce_rows(const KP &p, const Shape &sh, const flo
     const uint32_t b = wb / nb, blk = wb % nb, row = blk * 32 + lane;
     float pv[32];
     const RowRef rr = row_load<32, CONS>(p.part[1], sh, p.batch, b, row, pv);
-    const float xv = __ldcg(p.x + (size_t)b * p.n_embd + row);
-    finish_block(p, b, blk, __fadd_rn(xv, row_finish<32>(rr, pv, p.batch, sh.npad)), gamma, lane);
+    const float xv = __ldcg(p.x + (size_t)b * p.n_embd + row), g = __ldg(gamma + row);  // same round
+    finish_block(p, b, blk, __fadd_rn(xv, row_finish<32>(rr, pv, p.batch, sh.npad)), g, lane);
   }
 }
 
@@ -822,7 +822,7 @@ __device__ __noinline__ bool exchange_rows(const KP &p, const Shape &sh, const f
     const float v = row_sum<32, CONS>(p.part[1], sh, p.batch, b, row);
     const uint64_t word = ((uint64_t)tag << 32) | __float_as_uint(v);
     for (uint32_t q = 0; q < p.nranks; q++) st_relaxed_sys64(land_rows(p, q, parity, p.rank) + at, word);
-    const float xv = __ldcg(p.x + at);
+    const float xv = __ldcg(p.x + at), g = __ldg(gamma + row);
     float sum = 0.0f;
     bool mine = true;
     for (uint32_t q = 0; q < p.nranks && mine; q++) {  // rank order
@@ -850,7 +850,7 @@ __device__ __noinline__ bool exchange_rows(const KP &p, const Shape &sh, const f
       sum = q == 0 ? vq : sum + vq;
     }
     ok = __all_sync(0xffffffffu, mine);
-    if (ok) finish_block(p, b, blk, __fadd_rn(xv, sum), gamma, lane);
+    if (ok) finish_block(p, b, blk, __fadd_rn(xv, sum), g, lane);
   }
   cbar(nthr);
   if (ctid == 0) *sflag = *(volatile uint32_t *)(p.bar + 2) ? 0 : 1;
@@ -1097,7 +1097,7 @@ __device__ void embed(const KP &p, int c, int lane) {
   for (uint32_t wb = blockIdx.x * CONS + c; wb < p.batch * nb; wb += gridDim.x * CONS) {
     const uint32_t b = wb / nb, blk = wb % nb;
     const uint64_t r = (uint32_t)__ldcg(p.tok_in + b);
-    finish_block(p, b, blk, emb_elem(p, r, blk * 32 + lane), gamma, lane);
+    finish_block(p, b, blk, emb_elem(p, r, blk * 32 + lane), __ldg(gamma + blk * 32 + lane), lane);
   }
 }
 
