@@ -89,7 +89,9 @@ enum {
   PAI_KERNEL_B200_ARGMAX = 25,
   PAI_KERNEL_B200_GEMM_W8 = 26,
   PAI_KERNEL_B200_GEMM_W4 = 27,
-  PAI_KERNEL_B200_GEMM_V0 = 28
+  PAI_KERNEL_B200_GEMM_V0 = 28,
+  PAI_KERNEL_B200_GEMM_Q8_0 = 29,
+  PAI_KERNEL_B200_GEMM_Q4_K = 30
 };
 
 /* Quantized weight operand of a descriptor: pai_op_descriptor_t.reserved[0]

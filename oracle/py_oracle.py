@@ -155,8 +155,41 @@ def ref():
         _sig(R.pai_opt_backend_name, C.c_char_p)
         _sig(R.pai_sampler_sample_logits, C.c_int32, C.c_void_p, f32p, C.c_uint32,
              C.POINTER(C.c_uint32))
+        _sig(R.refdisp_run, C.c_int32, C.c_char_p, C.c_int32, C.c_uint32, U64, U64, U64, u8p,
+             f32p, f32p, f32p, f32p, f32p, C.POINTER(DispatchReport))
         _ref = R
     return _ref
+
+
+class DispatchReport(C.Structure):
+    """refdisp_report_t (oracle/ref_dispatch.c)."""
+    _fields_ = [("gate_cpu_ref", C.c_int32), ("gate_b200_ref_map", C.c_int32),
+                ("gate_b200", C.c_int32), ("cpu_status", C.c_int32), ("gpu_status", C.c_int32),
+                ("num_steps", C.c_uint32), ("gpu_steps", C.c_uint32),
+                ("kernel_ids", C.c_int32 * 4), ("devices", C.c_uint8 * 4),
+                ("error", C.c_char * 256)]
+
+
+def dispatch_slice(backend_so: str, run_gpu: bool, wtype: int, m: int, n: int, k: int,
+                   blocks: np.ndarray, x: np.ndarray, gamma: np.ndarray, res: np.ndarray):
+    """The decoder slice rmsnorm -> projection -> residual add, built with the
+    reference's graph builder, planned by its scheduler and run by its executor
+    on the host; with run_gpu, also through the executor's cuda-b200 branch
+    (oracle/ref_dispatch.c), which loads backend_so. Returns
+    (report, out_cpu [m][n], out_gpu [m][n])."""
+    R = ref()
+    assert R is not None, "oracle/_ref/libpai_ref.so is not built"
+    rep = DispatchReport()
+    out_cpu = np.zeros(m * n, np.float32)
+    out_gpu = np.zeros(m * n, np.float32)
+    rc = R.refdisp_run(backend_so.encode(), int(run_gpu), wtype, m, n, k,
+                       np.ascontiguousarray(blocks, np.uint8).ravel(),
+                       np.ascontiguousarray(x, np.float32).ravel(),
+                       np.ascontiguousarray(gamma, np.float32).ravel(),
+                       np.ascontiguousarray(res, np.float32).ravel(), out_cpu, out_gpu,
+                       C.byref(rep))
+    assert rc == 0, rep.error.decode()
+    return rep, out_cpu.reshape(m, n), out_gpu.reshape(m, n)
 
 
 # ---- convenience wrappers (numpy in, numpy out) ---------------------------------

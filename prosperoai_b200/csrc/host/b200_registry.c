@@ -30,6 +30,8 @@ static const pai_op_descriptor_t s_ops[] = {
     B200_DESC("gemv_q4_0_f32", 2, PAI_KERNEL_B200_GEMV_Q4_0, PAI_B200_Q4_0, 1),
     B200_DESC("gemv_q4_k_f32", 2, PAI_KERNEL_B200_GEMV_Q4_K, PAI_B200_Q4_K, 1),
     B200_DESC("gemm_q4_0_f32", 2, PAI_KERNEL_B200_GEMM_Q4_0, PAI_B200_Q4_0, 2), /* X, W blocks */
+    B200_DESC("gemm_q8_0_f32", 2, PAI_KERNEL_B200_GEMM_Q8_0, PAI_B200_Q8_0, 2),
+    B200_DESC("gemm_q4_k_f32", 2, PAI_KERNEL_B200_GEMM_Q4_K, PAI_B200_Q4_K, 2),
     B200_DESC("rmsnorm_gamma_f32_b200", 2, PAI_KERNEL_B200_RMSNORM, 0, 0),     /* a, gamma */
     B200_DESC("rope_f32_b200", 3, PAI_KERNEL_B200_ROPE, 0, 0),                 /* x, cos, sin */
     B200_DESC("attention_decode_f16kv", 3, PAI_KERNEL_B200_ATTN_DECODE, 0, 0), /* q, K, V (fp16 cache) */

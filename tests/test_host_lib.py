@@ -36,6 +36,16 @@ def test_library_loads_and_exports_every_declared_symbol():
     assert b"sm_100a" in L.pai_b200_version()
 
 
+def test_library_exports_only_the_declared_abi():
+    """Dynamic symbol table of libpai_b200.so: the declared pai_b200_* entry
+    points and nothing else (internal helpers, kernel templates and the
+    statically linked CUDA runtime stay local)."""
+    out = subprocess.run(["nm", "-D", "--defined-only", _native.LIB_PATH], check=True,
+                         capture_output=True, text=True).stdout
+    exported = {ln.split()[-1] for ln in out.splitlines() if ln.strip()}
+    assert exported == set(declared_functions()), sorted(exported ^ set(declared_functions()))
+
+
 def test_host_quantiser_matches_restated_formulas():
     rng = np.random.default_rng(11)
     for t in (po.Q4_0, po.Q8_0, po.Q4_K):
@@ -87,7 +97,7 @@ def test_registry_registration():
     assert {"gemv_q4_0_f32", "gemv_q8_0_f32", "gemv_q4_k_f32", "attention_decode_f16kv"} <= names
     for i in range(n):
         d = reg.ops[28 + i].contents
-        assert d.caps == 1 << 3 and 14 <= d.kernel_id <= 28
+        assert d.caps == 1 << 3 and 14 <= d.kernel_id <= 30
     full = _native.OpRegistry()
     full.count = 60
     assert L.pai_b200_register_ops(C.byref(full)) == -2  # PAI_ERR_NOMEM: 64-op cap
@@ -175,6 +185,7 @@ def test_ops_register_into_the_reference_registry():
     cuda_b200 = 1 << 3
     for name, kid, wfmt, warg in ((b"gemv_q4_0_f32", 15, 2, 1), (b"gemv_q8_0_f32", 14, 8, 1),
                                   (b"gemv_q4_k_f32", 16, 12, 1), (b"gemm_q4_0_f32", 17, 2, 2),
+                                  (b"gemm_q8_0_f32", 29, 8, 2), (b"gemm_q4_k_f32", 30, 12, 2),
                                   (b"attention_decode_f16kv", 20, 0, 0)):
         d = R.pai_op_registry_lookup(C.byref(reg), name)
         assert d, name
@@ -188,3 +199,59 @@ def test_ops_register_into_the_reference_registry():
                                  d.contents.num_outputs, None, 0) == -3  # PAI_ERR_UNSUPPORTED
     after = R.pai_op_registry_lookup(C.byref(reg), b"matmul_f32")
     assert (not matmul and not after) or C.addressof(after.contents) == C.addressof(matmul.contents)
+
+
+def slice_inputs(wtype, m, n, k, seed):
+    rng = np.random.default_rng(seed)
+    blocks = quantize(wtype, (rng.standard_normal(n * k) * 0.05).astype(np.float32))
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    gamma = (1.0 + 0.1 * rng.standard_normal(k)).astype(np.float32)
+    res = rng.standard_normal((m, n)).astype(np.float32)
+    return blocks, x, gamma, res
+
+
+@pytest.mark.parametrize("wtype,m,k", [(po.Q4_0, 1, 256), (po.Q8_0, 1, 256), (po.Q4_K, 1, 512),
+                                       (po.Q4_0, 8, 256), (po.Q4_K, 4, 256)])
+def test_reference_scheduler_plans_gates_and_runs_the_slice(wtype, m, k):
+    """The reference's graph builder, memory planner, scheduler, registry and
+    executor (graph.c, planner.c, scheduler.c, op_registry.c compiled from its
+    sources into oracle/_ref) over rmsnorm -> projection -> residual add, each
+    op hinted to the GPU. The reference's own gate pai_kernel_plan_check passes
+    for PAI_OP_CAP_CPU_REF and refuses PAI_OP_CAP_CUDA_B200 (its name map,
+    scheduler.c:647-682, picks the f32 builtins); the gate over the name map
+    extended with the quantized names passes once this backend is registered.
+    The executor's host result is rmsnorm, the dense product with the
+    reference-dequantised weights, and the add."""
+    R = po.ref()
+    if R is None:
+        pytest.skip("reference checkout not built into oracle/_ref")
+    n = 96
+    blocks, x, gamma, res = slice_inputs(wtype, m, n, k, seed=m * 7 + k + wtype)
+    rep, cpu, _ = po.dispatch_slice(_native.LIB_PATH, False, wtype, m, n, k, blocks, x, gamma, res)
+    assert rep.num_steps == 3 and rep.gpu_steps == 3, rep.error
+    assert list(rep.devices[:3]) == [2, 2, 2]  # PAI_SCHED_DEV_GPU
+    assert rep.gate_cpu_ref == 0
+    assert rep.gate_b200_ref_map == -3  # PAI_ERR_UNSUPPORTED
+    assert rep.gate_b200 == 0
+    assert rep.cpu_status == 0 and rep.gpu_status == 1  # the GPU branch did not run
+    w = po.dequant(wtype, blocks, n * k).reshape(n, k).astype(np.float64)
+    want = po.rmsnorm_gamma(x, gamma).astype(np.float64) @ w.T + res
+    assert np.max(np.abs(cpu - want)) <= 1e-4 * max(1.0, float(np.max(np.abs(want))))
+
+
+def test_b200_gate_refuses_a_block_type_without_a_kernel():
+    """Q5_0 weights (ggml type 6): the reference executor still runs the slice
+    on the host, and the cuda-b200 gate refuses the plan (no descriptor)."""
+    R = po.ref()
+    if R is None:
+        pytest.skip("reference checkout not built into oracle/_ref")
+    m, n, k = 1, 64, 128
+    rng = np.random.default_rng(5)
+    blocks = rng.integers(0, 256, n * k // 32 * 22, dtype=np.uint8)
+    blocks.reshape(-1, 22)[:, 0:2] = np.frombuffer(np.float16(0.01).tobytes(), np.uint8)
+    x = rng.standard_normal(k).astype(np.float32)
+    rep, cpu, _ = po.dispatch_slice(_native.LIB_PATH, False, 6, m, n, k, blocks, x,
+                                    np.ones(k, np.float32), np.zeros(n, np.float32))
+    assert rep.gate_cpu_ref == 0 and rep.cpu_status == 0
+    assert rep.gate_b200 == -3 and rep.gate_b200_ref_map == -3
+    assert np.all(np.isfinite(cpu))
