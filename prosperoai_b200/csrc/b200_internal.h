@@ -130,6 +130,9 @@ void b200_gguf_release(b200_gguf_view_t *view);
 pai_status_t b200_fail(pai_status_t st, const char *fmt, ...);
 /* Map a CUDA runtime error code to a status (PAI_OK for 0). */
 pai_status_t b200_cuda(int err, const char *what);
+/* The driver's cuTensorMapEncodeTiled, looked up once through the runtime
+ * (no link-time dependency on libcuda); NULL where unavailable. */
+void *b200_tensor_map_encoder(void);
 
 /* ---- context ------------------------------------------------------------------------ */
 

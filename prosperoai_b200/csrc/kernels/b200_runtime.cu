@@ -10,6 +10,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <new>
 
 #include "../b200_internal.h"
@@ -72,6 +73,19 @@ extern "C" pai_status_t b200_cuda(int err, const char *what) {
   if (e == cudaErrorMemoryAllocation)
     return b200_fail(PAI_ERR_NOMEM, "%s: %s", what, cudaGetErrorString(e));
   return b200_fail(PAI_ERR_INTERNAL, "%s: %s", what, cudaGetErrorString(e));
+}
+
+extern "C" void *b200_tensor_map_encoder(void) {
+  static void *fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = f;
+  });
+  return fn;
 }
 
 extern "C" const char *pai_b200_last_error(void) { return g_err; }

@@ -592,21 +592,6 @@ cudaError_t launch_vec(pai_b200_ctx_t *ctx, dim3 grid, uint32_t mb, const V0Args
   }
 }
 
-// cuTensorMapEncodeTiled from the driver, looked up through the runtime
-// once (no link-time dependency on libcuda); NULL where unavailable.
-PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void *f = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
-  });
-  return fn;
-}
-
 template <int BITS, int LAYOUT, int MB>
 cudaError_t launch_tma_mb(pai_b200_ctx_t *ctx, dim3 grid, const V0Args &a, const CUtensorMap &map) {
   constexpr uint32_t SB = BITS == 8 ? 256 : 128;
@@ -640,7 +625,8 @@ pai_status_t gemm_v0(pai_b200_ctx_t *ctx, uint32_t bits, int layout, uint64_t m,
   // TMA path: rows of whole 16-byte multiples (the tensor map's stride rule), 16-byte aligned
   // values, and the vector path's scale rules
   const uint64_t row_bytes = bits == 8 ? n : n / 2;
-  PFN_cuTensorMapEncodeTiled_v12000 encode = vec ? tensor_map_encoder() : nullptr;
+  PFN_cuTensorMapEncodeTiled_v12000 encode =
+      vec ? reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(b200_tensor_map_encoder()) : nullptr;
   const bool tma = encode && (bits == 8 ? n % 16 == 0 : n % 32 == 0) && wa % 16 == 0 && k <= 0x7FFFFFFFull &&
                    row_bytes >= (bits == 8 ? 256u : 128u) && row_bytes < (1ull << 40);
   const uint64_t strips = (n + kStrip - 1) / kStrip;
