@@ -228,14 +228,25 @@ template <uint32_t T>
 constexpr uint32_t kSclBytes = T == PAI_B200_Q4_0 ? kWorkers * 16 * 4 * 8 : 0;  // Q4_0's split scales, per warp
 // bf16 weight / activation stages (shared memory bound; the 2-byte-code types
 // have raw units twice as large)
+// With few tokens (BN 16, 64) an MMA drains its stage at once, so the bf16
+// ring stays short and the rest of shared memory holds raw weight units in
+// flight: the copies' latency, not the tensor core, bounds those tiles.
 template <uint32_t T, int BN>
-constexpr int kAStages = T == PAI_B200_Q4_0 ? (BN == 256 ? 2 : (BN == 128 ? 3 : 4)) : (BN >= 128 ? 2 : (BN == 64 ? 3 : 4));
+constexpr int kAStages = BN == 16 ? 2 : (T == PAI_B200_Q4_0 ? (BN == 256 ? 2 : 3) : (BN >= 128 ? 2 : 3));
 template <uint32_t T, int BN>
 constexpr int kBStages = T == PAI_B200_Q4_0 ? (BN == 256 ? 3 : 4) : (BN == 256 ? 2 : 4);
 template <uint32_t T, int BN>
+constexpr size_t gemm_fixed_bytes() {
+  return 1024 + (size_t)kAStages<T, BN> * kAStage + (size_t)kBStages<T, BN> * BN * 128 + kSclBytes<T>;
+}
+// raw units in flight: as many as fit beside the rest (at most 8; 1 KB of the
+// 227 KB left for the static mbarriers), at least the type's minimum
+template <uint32_t T, int BN>
+constexpr int kRawStages = std::max<int>(GT<T>::RAW, std::min<int>(8, (int)((226 * 1024 - gemm_fixed_bytes<T, BN>()) /
+                                                                              kRawStage<T>)));
+template <uint32_t T, int BN>
 constexpr size_t gemm_smem_bytes() {
-  return 1024 + (size_t)kAStages<T, BN> * kAStage + (size_t)kBStages<T, BN> * BN * 128 +
-         (size_t)GT<T>::RAW * kRawStage<T> + kSclBytes<T>;
+  return gemm_fixed_bytes<T, BN>() + (size_t)kRawStages<T, BN> * kRawStage<T>;
 }
 
 // Eight fp32 values -> one 16-byte chunk of bf16, each rounded once (RN).
@@ -308,9 +319,9 @@ __global__ void __launch_bounds__(kGThreadsWS, 1) k_gemm(GemmP p) {
   constexpr uint32_t kBStage = BN * 128;
   constexpr uint32_t kIdesc = idesc_bf16(BN);
   constexpr int SA = kAStages<T, BN>, SB = kBStages<T, BN>;
-  constexpr int kRawStages = GT<T>::RAW, SPU = GT<T>::SPU;
+  constexpr int RS = kRawStages<T, BN>, SPU = GT<T>::SPU;
   constexpr uint32_t QB = GT<T>::QB, HB = GT<T>::SB, kRaw = kRawStage<T>;
-  static_assert(gemm_smem_bytes<T, BN>() <= 227 * 1024, "shared memory of one CTA");
+  static_assert(gemm_smem_bytes<T, BN>() <= 226 * 1024, "shared memory of one CTA");
   constexpr uint32_t kECols = BN / 2;                      // epilogue columns (tokens) per warp
   constexpr uint32_t kEChunk = kECols < 16 ? kECols : 16;  // columns per TMEM load round
   constexpr uint32_t kFChunk = kECols < 16 ? kECols : 16;  // columns per round of the split-tile sum
@@ -319,9 +330,9 @@ __global__ void __launch_bounds__(kGThreadsWS, 1) k_gemm(GemmP p) {
   uint8_t *gsm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~(uintptr_t)1023);
   uint8_t *a_st = gsm;                                // [SA][2 acc][128 rows][128 B]
   uint8_t *b_st = a_st + (size_t)SA * kAStage;        // [SB][BN rows][128 B]
-  uint8_t *r_st = b_st + (size_t)SB * kBStage;        // [kRawStages][16 tiles' codes | 16 tiles' headers]
-  uint4 *scl_all = reinterpret_cast<uint4 *>(r_st + (size_t)kRawStages * kRaw);
-  __shared__ __align__(8) uint64_t rfull[kRawStages], rempty[kRawStages];
+  uint8_t *r_st = b_st + (size_t)SB * kBStage;        // [RS][16 tiles' codes | 16 tiles' headers]
+  uint4 *scl_all = reinterpret_cast<uint4 *>(r_st + (size_t)RS * kRaw);
+  __shared__ __align__(8) uint64_t rfull[RS], rempty[RS];
   __shared__ __align__(8) uint64_t afull[SA], aempty[SA], bfull[SB], bempty[SB];
   __shared__ __align__(8) uint64_t accfull, accempty;
   __shared__ uint32_t tmem_base_s;
@@ -331,7 +342,7 @@ __global__ void __launch_bounds__(kGThreadsWS, 1) k_gemm(GemmP p) {
   const uint64_t w_begin = sk_begin(cta, p.work, G), w_end = sk_begin(cta + 1, p.work, G);
   const uint32_t first_tile = (uint32_t)(w_begin / U);
   if (tid == 0) {
-    for (int s = 0; s < kRawStages; s++) {
+    for (int s = 0; s < RS; s++) {
       mbar_init(&rfull[s], 1);
       mbar_init(&rempty[s], kWorkers);
     }
@@ -364,8 +375,8 @@ __global__ void __launch_bounds__(kGThreadsWS, 1) k_gemm(GemmP p) {
       uint32_t i = 0, u = (uint32_t)(w_begin % U), tile0 = (first_tile / p.mtiles) * 16, mt = first_tile % p.mtiles;
       for (uint64_t w = w_begin; w < w_end && ok; w++, i++) {
         const uint32_t nv = min(16u, p.ntiles - tile0);
-        const uint32_t rs = i % kRawStages;
-        if (i >= (uint32_t)kRawStages && !mbar_wait_spin(&rempty[rs], ((i / kRawStages) - 1) & 1u, p.wait_ns)) {
+        const uint32_t rs = i % RS;
+        if (i >= (uint32_t)RS && !mbar_wait(&rempty[rs], ((i / RS) - 1) & 1u, p.wait_ns)) {
           ok = false;
           break;
         }
@@ -390,7 +401,7 @@ __global__ void __launch_bounds__(kGThreadsWS, 1) k_gemm(GemmP p) {
       for (uint64_t w = w_begin; w < w_end && ok; w++) {
         for (uint32_t hs = 0; hs < (uint32_t)SPU; hs++, j++) {
           const uint32_t s = j % SB;
-          if (j >= (uint32_t)SB && !mbar_wait_spin(&bempty[s], ((j / SB) - 1) & 1u, p.wait_ns)) {
+          if (j >= (uint32_t)SB && !mbar_wait(&bempty[s], ((j / SB) - 1) & 1u, p.wait_ns)) {
             ok = false;
             break;
           }
@@ -412,7 +423,7 @@ __global__ void __launch_bounds__(kGThreadsWS, 1) k_gemm(GemmP p) {
       for (uint64_t w = w_begin; w < w_end && ok; w++, u = (u + 1 == U) ? 0 : u + 1) {
         const bool seg_first = w == w_begin || u == 0, seg_last = w + 1 == w_end || u == U - 1;
         if (seg_first && e > 0) {  // the previous segment's epilogue has read the accumulators
-          if (!mbar_wait_spin(&accempty, (e - 1) & 1u, p.wait_ns)) {
+          if (!mbar_wait(&accempty, (e - 1) & 1u, p.wait_ns)) {
             ok = false;
             break;
           }
@@ -420,8 +431,7 @@ __global__ void __launch_bounds__(kGThreadsWS, 1) k_gemm(GemmP p) {
         }
         for (uint32_t hs = 0; hs < (uint32_t)SPU; hs++, j++) {
           const uint32_t s = j % SA, sb = j % SB;
-          if (!mbar_wait_spin(&afull[s], (j / SA) & 1u, p.wait_ns) ||
-              !mbar_wait_spin(&bfull[sb], (j / SB) & 1u, p.wait_ns)) {
+          if (!mbar_wait(&afull[s], (j / SA) & 1u, p.wait_ns) || !mbar_wait(&bfull[sb], (j / SB) & 1u, p.wait_ns)) {
             ok = false;
             break;
           }
@@ -493,8 +503,8 @@ __global__ void __launch_bounds__(kGThreadsWS, 1) k_gemm(GemmP p) {
     bool seg_full_start = u == 0;  // the current segment starts at the tile's first K unit
     for (uint64_t w = w_begin; w < w_end && ok; w++, i++) {
       mine = (uint32_t)warp < min(16u, p.ntiles - ft * 16);
-      const uint32_t rs = i % kRawStages;
-      if (!mbar_wait_sleep(&rfull[rs], (i / kRawStages) & 1u, p.wait_ns)) {
+      const uint32_t rs = i % RS;
+      if (!mbar_wait_sleep(&rfull[rs], (i / RS) & 1u, p.wait_ns)) {
         ok = false;
         break;
       }
@@ -689,7 +699,9 @@ pai_status_t gemm_launch(pai_b200_ctx_t *ctx, uint32_t m, uint32_t n, uint32_t k
   // Grid: with at least as many output tiles as SMs, one persistent CTA per
   // SM over the whole stream (tiles split only where runs meet). With fewer,
   // each tile is split evenly over floor(SMs / tiles) CTAs, so no tile has
-  // more contributors than it needs. Runs are at least 4 K units long.
+  // more contributors than it needs (measured: stream-K over 112 tiles on
+  // 148 CTAs is 23 % slower at M = 512, the split tiles' sums costing more
+  // than the extra SMs give). Runs are at least 4 K units long.
   const uint64_t g_want = tiles >= (uint64_t)sms ? (uint64_t)sms : tiles * ((uint64_t)sms / tiles);
   const uint32_t grid = (uint32_t)std::max<uint64_t>(1, std::min<uint64_t>(g_want, work / 4));
   const uint64_t xp_bytes = (uint64_t)mtiles * nkc * BN * 128;
