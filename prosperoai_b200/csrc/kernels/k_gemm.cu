@@ -234,7 +234,7 @@ constexpr uint32_t kSclBytes = T == PAI_B200_Q4_0 ? kWorkers * 16 * 4 * 8 : 0;  
 template <uint32_t T, int BN>
 constexpr int kAStages = BN == 16 ? 2 : (T == PAI_B200_Q4_0 ? (BN == 256 ? 2 : 3) : (BN >= 128 ? 2 : 3));
 template <uint32_t T, int BN>
-constexpr int kBStages = T == PAI_B200_Q4_0 ? (BN == 256 ? 3 : 4) : (BN == 256 ? 2 : 4);
+constexpr int kBStages = BN == 16 ? 16 : (T == PAI_B200_Q4_0 ? (BN == 256 ? 3 : 4) : (BN == 256 ? 2 : 4));
 template <uint32_t T, int BN>
 constexpr size_t gemm_fixed_bytes() {
   return 1024 + (size_t)kAStages<T, BN> * kAStage + (size_t)kBStages<T, BN> * BN * 128 + kSclBytes<T>;
