@@ -910,26 +910,29 @@ __device__ __noinline__ void attention(const KP &p, uint32_t layer, int warp, in
       const uint32_t d = (uint32_t)ctid % (kHD / 2);
       rc = __ldg(p.cos_t + (size_t)pos * (kHD / 2) + d), rs = __ldg(p.sin_t + (size_t)pos * (kHD / 2) + d);
     }
-    // q | k | v rows of this kv head from the q|k|v partial sums
-    for (uint32_t i0 = ctid; i0 < R; i0 += 2 * nthr) {
-      float va[16], vb[16];
-      const uint32_t i1 = min(i0 + nthr, R - 1);
-      const uint32_t rowa = i0 < G * kHD ? h0 * kHD + i0
-                                         : (i0 < (G + 1) * kHD ? (p.h + kvh) * kHD + i0 - G * kHD
-                                                               : (p.h + p.hk + kvh) * kHD + i0 - (G + 1) * kHD);
-      const uint32_t rowb = i1 < G * kHD ? h0 * kHD + i1
-                                         : (i1 < (G + 1) * kHD ? (p.h + kvh) * kHD + i1 - G * kHD
-                                                               : (p.h + p.hk + kvh) * kHD + i1 - (G + 1) * kHD);
-      const RowRef ra = row_load<16, CONS>(part, sq, p.batch, b, rowa, va);
-      const RowRef rb = row_load<16, CONS>(part, sq, p.batch, b, rowb, vb);
-      const float xa = row_finish<16>(ra, va, p.batch, sq.npad);
-      const float xb = row_finish<16>(rb, vb, p.batch, sq.npad);
-      // q rows go to the padded quarter layout, k and v rows after them
-      if (i0 < G * kHD) qs[(i0 / kHD) * 4 * kQP + ((i0 % kHD) / 32) * kQP + i0 % 32] = xa;
-      else kvs[i0 - G * kHD] = xa;
-      if (i0 + nthr < R) {
-        if (i1 < G * kHD) qs[(i1 / kHD) * 4 * kQP + ((i1 % kHD) / 32) * kQP + i1 % 32] = xb;
-        else kvs[i1 - G * kHD] = xb;
+    // q | k | v rows of this kv head from the q|k|v partial sums: every
+    // thread's rows (RPT of them) with the first 8 parts of each loaded in
+    // one round -- a q|k|v row group is split over at most 8 CTAs at the
+    // shapes this kernel serves, and row_finish loads any further parts
+    constexpr uint32_t RPT = (R + CONS * 32 - 1) / (CONS * 32);
+    {
+      float v[RPT][8];
+      RowRef rr[RPT];
+#pragma unroll
+      for (uint32_t t = 0; t < RPT; t++) {
+        const uint32_t i = min((uint32_t)ctid + t * nthr, R - 1);
+        const uint32_t row = i < G * kHD ? h0 * kHD + i
+                                         : (i < (G + 1) * kHD ? (p.h + kvh) * kHD + i - G * kHD
+                                                              : (p.h + p.hk + kvh) * kHD + i - (G + 1) * kHD);
+        rr[t] = row_load<8, CONS>(part, sq, p.batch, b, row, v[t]);
+      }
+#pragma unroll
+      for (uint32_t t = 0; t < RPT; t++) {
+        const uint32_t i = ctid + t * nthr;
+        const float x = row_finish<8>(rr[t], v[t], p.batch, sq.npad);
+        // q rows go to the padded quarter layout, k and v rows after them
+        if (i < G * kHD) qs[(i / kHD) * 4 * kQP + ((i % kHD) / 32) * kQP + i % 32] = x;
+        else if (i < R) kvs[i - G * kHD] = x;
       }
     }
     cbar(nthr);
