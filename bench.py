@@ -38,7 +38,7 @@ SEED = 20261201
 # DRAM bytes per launch of the 32-layer persistent layer kernel, batch 1: ncu's
 # dram__bytes_read.sum + dram__bytes_write.sum of a 4-layer launch x 8
 # (profiles/k_decode_q4_0_8b.md)
-K_DECODE_TRAFFIC = 4166 * 10 ** 6
+K_DECODE_TRAFFIC = 4176 * 10 ** 6
 METRIC = "Q4_0 8B-shape decode tok/s"
 UNIT = "tokens/s"
 
