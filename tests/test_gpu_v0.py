@@ -73,7 +73,9 @@ def random_wq(rng, bits, n, k, gs):
 
 
 @pytest.mark.parametrize("bits,m,n,k,gs", [
-    (8, 1, 4096, 4096, 32),    # config-1 shape, vector path, many k-splits
+    (8, 1, 4096, 4096, 32),    # config-1 shape: wide strips, 74 k-splits per strip
+    (8, 2, 2560, 1000, 32),    # wide: a partial second strip, ragged last split
+    (4, 8, 4096, 512, 16),     # wide, nibbles, 8 rows, split length one box
     (4, 3, 1024, 2048, 64),
     (8, 11, 512, 256, 0),      # two row passes (8 + 3), one group over k
     (4, 8, 264, 1000, 100),    # ragged strip and split ends
@@ -124,13 +126,15 @@ def test_v0_argument_errors(dev):
     assert _native.load().pai_b200_v0_blob_bytes(2, 0, 64) == 0
 
 
-def test_graph_capture_replays_the_op(dev):
+@pytest.mark.parametrize("n", [1024, 4096])
+def test_graph_capture_replays_the_op(dev, n):
     """pai_b200_graph_begin/end/launch: two ops captured once, replayed,
-    give the bits of the direct calls."""
+    give the bits of the direct calls (n = 4096: the wide-strip form, a
+    cooperative launch whose strips share their k-split reduction)."""
     import ctypes as C
     L = _native.load()
     rng = np.random.default_rng(9)
-    m, n, k = 2, 1024, 512
+    m, k = 2, 512
     a = dev.put(rng.standard_normal((m, k)).astype(np.float32))
     wq, sc = random_wq(rng, 8, n, k, 32)
     w, s = dev.put(wq), dev.put(sc)
